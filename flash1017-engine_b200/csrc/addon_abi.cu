@@ -1,0 +1,537 @@
+// addon_abi.cu -- the reference's plugin ABI (include/merkaba_hw_addon.h) on B200.
+//
+// The Rust host (crates/flash-core/src/hardware_addon.rs, "HA") calls these
+// functions with HOST pointers and reads `out` right after they return.  B200
+// memory is discrete, so this layer
+//   * keeps one HBM copy per weight range: ranges registered through
+//     gx10_rust_register_host_range are copied eagerly; any other weight
+//     pointer (inside gx10_rust_register_shard_bounds ranges or not) is copied
+//     the first time a kernel needs it, as exactly the bytes that call reads.
+//     Weights are immutable for the process lifetime in the reference (mmap'd
+//     read-only safetensors), which is what makes the cache valid;
+//   * stages x / out through device buffers on one internal stream;
+//   * runs the same kernels as the device-resident ABI (ffn_b200.h).
+// Calls are serialised by a mutex (the reference calls from one thread at a
+// time, CLI:1833-1846).  There is no CPU compute path here: every result comes
+// from a CUDA kernel, and failures are reported, not recomputed.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <vector>
+
+#include "ffn_internal.h"
+#include "merkaba_hw_addon.h"
+
+namespace ffn {
+namespace {
+
+struct DevBuf {
+  void *p = nullptr;
+  size_t n = 0;
+  int ensure(size_t bytes) {
+    if (bytes <= n) return 0;
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+    const size_t want = std::max<size_t>(bytes, 1 << 20);
+    cudaError_t e = cudaMalloc(&p, want);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(staging)");
+    n = want;
+    return 0;
+  }
+};
+
+struct Range {
+  uintptr_t h;
+  size_t n;
+  char *d;
+};
+
+struct Ctx {
+  std::mutex mu;
+  bool init = false;
+  int device = -1;
+  cudaStream_t st = nullptr;
+  DevBuf x, out, ws, tmp;
+  std::map<uintptr_t, std::vector<Range>> ranges;  // by start address
+  size_t cached = 0;
+  std::vector<std::pair<uintptr_t, size_t>> shard_bounds;
+  // pending accumulation of gx10_rust_*_mlp_accum / _mlp_batch
+  float *pend_host = nullptr;
+  size_t pend_n = 0;
+  // batched-layer input x_all (ffn_b200_set_batch_input)
+  const float *xall_host = nullptr;
+  size_t xall_tok = 0, xall_hidden = 0;
+  bool xall_dev_valid = false;
+  DevBuf xall;
+};
+
+Ctx &ctx() {
+  static Ctx *c = new Ctx();  // never destroyed: the vtable outlives static teardown
+  return *c;
+}
+
+int ensure_init(Ctx &c) {
+  if (c.init) {
+    int dev = -1;
+    cudaGetDevice(&dev);
+    if (dev == c.device) return 0;
+    return fail(FFN_B200_EUNSUP, "reference ABI: called on a different device than the first call");
+  }
+  FFN_CUDA_TRY(cudaGetDevice(&c.device));
+  FFN_CUDA_TRY(cudaStreamCreateWithFlags(&c.st, cudaStreamNonBlocking));
+  c.init = true;
+  return 0;
+}
+
+// Device address of host bytes [h, h+n): an existing copy containing them, or
+// a new copy of exactly those bytes.
+int dev_ptr(Ctx &c, const void *hp, size_t n, const void **out) {
+  if (!hp) return fail(FFN_B200_EINVAL, "reference ABI: null weight pointer");
+  const uintptr_t h = (uintptr_t)hp;
+  auto it = c.ranges.upper_bound(h);
+  while (it != c.ranges.begin()) {
+    --it;
+    for (const Range &r : it->second)
+      if (r.h <= h && h + n <= r.h + r.n) {
+        *out = r.d + (h - r.h);
+        return 0;
+      }
+    if (it->first + (1ull << 40) < h) break;  // ranges are tensors, far smaller than 1 TiB
+  }
+  char *d = nullptr;
+  FFN_CUDA_TRY(cudaMalloc(&d, n));
+  cudaError_t e = cudaMemcpy(d, hp, n, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return cuda_fail(e, "cudaMemcpy(weight upload)");
+  }
+  c.ranges[h].push_back(Range{h, n, d});
+  c.cached += n;
+  *out = d;
+  return 0;
+}
+
+int flush_pending(Ctx &c) {
+  if (!c.pend_host) return 0;
+  cudaError_t e = cudaMemcpyAsync(c.pend_host, c.out.p, c.pend_n * sizeof(float),
+                                  cudaMemcpyDeviceToHost, c.st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c.st);
+  c.pend_host = nullptr;
+  c.pend_n = 0;
+  if (e != cudaSuccess) return cuda_fail(e, "pending out download");
+  return 0;
+}
+
+void fill_nan(float *out, size_t n) {
+  if (!out) return;
+  const float q = std::nanf("");
+  for (size_t i = 0; i < n; ++i) out[i] = q;
+}
+
+// Stage x, run `body(ctx, dx, dout)`, copy out back, synchronise.  void-returning
+// ABI: on failure `out` is NaN-filled and the error is recorded.
+template <class F>
+void run_sync(size_t x_n, const float *x, size_t out_n, float *out, F body) {
+  Ctx &c = ctx();
+  std::lock_guard<std::mutex> lk(c.mu);
+  int rc = ensure_init(c);
+  if (!rc) rc = flush_pending(c);
+  if (!rc && (!x || !out)) rc = fail(FFN_B200_EINVAL, "reference ABI: null x/out");
+  if (!rc) rc = c.x.ensure(x_n * sizeof(float));
+  if (!rc) rc = c.out.ensure(out_n * sizeof(float));
+  if (!rc) {
+    cudaError_t e = cudaMemcpyAsync(c.x.p, x, x_n * sizeof(float), cudaMemcpyHostToDevice, c.st);
+    if (e != cudaSuccess) rc = cuda_fail(e, "x upload");
+  }
+  if (!rc) rc = body(c, (const float *)c.x.p, (float *)c.out.p);
+  if (!rc) {
+    cudaError_t e = cudaMemcpyAsync(out, c.out.p, out_n * sizeof(float), cudaMemcpyDeviceToHost, c.st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c.st);
+    if (e != cudaSuccess) rc = cuda_fail(e, "out download");
+  }
+  if (rc) {
+    std::fprintf(stderr, "[ffn_b200] %s\n", ffn_b200_last_error());
+    fill_nan(out, out_n);
+  }
+}
+
+// ------------------------------------------------------------- V1 dots
+float dot_common(int mode, const void *a, size_t a_bytes, const void *aux, size_t aux_bytes,
+                 const float *x, size_t x_n) {
+  Ctx &c = ctx();
+  std::lock_guard<std::mutex> lk(c.mu);
+  float r = std::nanf("");
+  int rc = ensure_init(c);
+  if (!rc) rc = flush_pending(c);
+  if (!rc && (!a || !x)) rc = fail(FFN_B200_EINVAL, "dot: null pointer");
+  if (!rc) rc = c.tmp.ensure(a_bytes + aux_bytes + x_n * 4 + 1024);
+  if (!rc) {
+    char *base = (char *)c.tmp.p;
+    char *da = base, *daux = base + ((a_bytes + 255) & ~(size_t)255);
+    char *dx = daux + ((aux_bytes + 255) & ~(size_t)255);
+    float *dr = (float *)(dx + ((x_n * 4 + 255) & ~(size_t)255));
+    cudaError_t e = cudaMemcpyAsync(da, a, a_bytes, cudaMemcpyHostToDevice, c.st);
+    if (e == cudaSuccess && aux_bytes) e = cudaMemcpyAsync(daux, aux, aux_bytes, cudaMemcpyHostToDevice, c.st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dx, x, x_n * 4, cudaMemcpyHostToDevice, c.st);
+    if (e != cudaSuccess) rc = cuda_fail(e, "dot upload");
+    if (!rc) rc = launch_dot(mode, da, daux, (const float *)dx, x_n, dr, c.st);
+    if (!rc) {
+      e = cudaMemcpyAsync(&r, dr, 4, cudaMemcpyDeviceToHost, c.st);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(c.st);
+      if (e != cudaSuccess) rc = cuda_fail(e, "dot download");
+    }
+  }
+  if (rc) std::fprintf(stderr, "[ffn_b200] %s\n", ffn_b200_last_error());
+  return r;
+}
+
+float v1_dot_f32(const float *a, const float *b, size_t len) {
+  return dot_common(0, a, len * 4, nullptr, 0, b, len);
+}
+float v1_dot_i8_f32(const int8_t *w, const float *x, size_t len) {
+  return dot_common(1, w, len, nullptr, 0, x, len);
+}
+float v1_dot_q4_g32_f32(const uint8_t *nib, const uint16_t *sc, const float *x, size_t cols) {
+  return dot_common(2, nib, cols / 2, sc, (cols / 32) * 2, x, cols);
+}
+float v1_dot_ternary_2bit_f32(const uint8_t *p, const float *x, size_t cols) {
+  return dot_common(3, p, cols / 4, nullptr, 0, x, cols);
+}
+
+// ------------------------------------------------------------ V2/V3 matvecs
+void v3_matbatch_bf16(size_t rows, size_t cols, size_t seq, const uint16_t *w, const float *xb,
+                      float *ob) {
+  run_sync(seq * cols, xb, seq * rows, ob, [&](Ctx &c, const float *dx, float *dout) {
+    if (!w || rows == 0 || cols == 0) return fail(FFN_B200_EINVAL, "matbatch_bf16: bad arguments");
+    const void *dw;
+    int rc = dev_ptr(c, w, rows * cols * 2, &dw);
+    if (rc) return rc;
+    // exact sequential sum per row (flash1017.rs:2212-2226)
+    return launch_exact_matvec(nullptr, (const uint16_t *)dw, dx, (int)seq, (int)rows, (int)cols,
+                               dout, c.st);
+  });
+}
+void v2_matvec_bf16(size_t rows, size_t cols, const uint16_t *w, const float *x, float *out) {
+  v3_matbatch_bf16(rows, cols, 1, w, x, out);
+}
+
+void v3_matbatch_nvfp4(size_t rows, size_t cols, size_t seq, const uint8_t *w, const uint8_t *s,
+                       float gs, const float *xb, float *ob) {
+  run_sync(seq * cols, xb, seq * rows, ob, [&](Ctx &c, const float *dx, float *dout) {
+    if (!w || !s || cols % 16) return fail(FFN_B200_EINVAL, "matbatch_nvfp4: bad arguments");
+    ffn_b200_nvfp4_mat m{};
+    const void *dw, *ds;
+    int rc = dev_ptr(c, w, rows * cols / 2, &dw);
+    if (!rc) rc = dev_ptr(c, s, rows * cols / 16, &ds);
+    if (rc) return rc;
+    m.w = (const uint8_t *)dw;
+    m.s = (const uint8_t *)ds;
+    m.gs = gs;
+    if ((rc = c.ws.ensure(ffn_b200_matvec_ws_bytes(seq, cols)))) return rc;
+    return ffn_b200_nvfp4_matvec(rows, cols, seq, &m, dx, dout, c.ws.p, c.ws.n, c.st);
+  });
+}
+void v3_matvec_nvfp4(size_t rows, size_t cols, const uint8_t *w, const uint8_t *s, float gs,
+                     const float *x, float *out) {
+  v3_matbatch_nvfp4(rows, cols, 1, w, s, gs, x, out);
+}
+
+void v3_matbatch_ternary(size_t rows, size_t cols, size_t seq, const uint8_t *p, const float *rs,
+                         const float *xb, float *ob) {
+  run_sync(seq * cols, xb, seq * rows, ob, [&](Ctx &c, const float *dx, float *dout) {
+    if (!p || !rs || cols % 4) return fail(FFN_B200_EINVAL, "matbatch_ternary_158: bad arguments");
+    ffn_b200_ternary_mat m{};
+    const void *dp, *drs;
+    int rc = dev_ptr(c, p, rows * cols / 4, &dp);
+    if (!rc) rc = dev_ptr(c, rs, rows * 4, &drs);
+    if (rc) return rc;
+    m.p = (const uint8_t *)dp;
+    m.rs = (const float *)drs;
+    if ((rc = c.ws.ensure(ffn_b200_matvec_ws_bytes(seq, cols)))) return rc;
+    return ffn_b200_ternary_matvec(rows, cols, seq, &m, dx, dout, c.ws.p, c.ws.n, c.st);
+  });
+}
+void v3_matvec_ternary(size_t rows, size_t cols, const uint8_t *p, const float *rs,
+                       const float *x, float *out) {
+  v3_matbatch_ternary(rows, cols, 1, p, rs, x, out);
+}
+
+const char kId[] = "addon_b200_ffn";
+const char kDesc[] =
+    "B200 (sm_100a) quantized expert-FFN backend: NVFP4 + 1.58-bit ternary (+rank-16 Q8) "
+    "tensor-core GEMV/GEMM, routed SwiGLU MoE";
+
+HardwareAddonVTable make_vtable() {
+  HardwareAddonVTable v;
+  std::memset(&v, 0, sizeof(v));
+  v.abi_version = MERKABA_HW_ABI_V3;
+  v.addon_id_ptr = (const uint8_t *)kId;
+  v.addon_id_len = sizeof(kId) - 1;
+  v.addon_desc_ptr = (const uint8_t *)kDesc;
+  v.addon_desc_len = sizeof(kDesc) - 1;
+  v.dot_f32 = v1_dot_f32;
+  v.dot_i8_f32 = v1_dot_i8_f32;
+  v.dot_q4_g32_f32 = v1_dot_q4_g32_f32;
+  v.dot_ternary_2bit_f32 = v1_dot_ternary_2bit_f32;
+  v.matvec_bf16 = v2_matvec_bf16;
+  v.matbatch_bf16 = v3_matbatch_bf16;
+  v.matvec_nvfp4 = v3_matvec_nvfp4;
+  v.matbatch_nvfp4 = v3_matbatch_nvfp4;
+  v.matvec_ternary_158 = v3_matvec_ternary;
+  v.matbatch_ternary_158 = v3_matbatch_ternary;
+  return v;
+}
+
+// ---------------------------------------------------------- fused experts
+int resolve_expert(Ctx &c, ffn_b200_expert &e, size_t inter, size_t hidden) {
+  for (int i = 0; i < 3; ++i) {
+    const size_t r = i == 2 ? hidden : inter, k = i == 2 ? inter : hidden;
+    const void *a, *b;
+    int rc;
+    if (e.format == FFN_B200_FMT_NVFP4) {
+      if ((rc = dev_ptr(c, e.nv[i].w, r * k / 2, &a))) return rc;
+      if ((rc = dev_ptr(c, e.nv[i].s, r * k / 16, &b))) return rc;
+      e.nv[i].w = (const uint8_t *)a;
+      e.nv[i].s = (const uint8_t *)b;
+    } else {
+      if ((rc = dev_ptr(c, e.tn[i].p, r * k / 4, &a))) return rc;
+      if ((rc = dev_ptr(c, e.tn[i].rs, r * 4, &b))) return rc;
+      e.tn[i].p = (const uint8_t *)a;
+      e.tn[i].rs = (const float *)b;
+    }
+  }
+  return 0;
+}
+
+// Shared by the *_mlp_accum entry points: x is one token, out [hidden].
+bool mlp_accum(const ffn_b200_expert &he, size_t inter, size_t hidden, const float *x, float *out,
+               float w, bool accumulate, bool sync_now) {
+  Ctx &c = ctx();
+  std::lock_guard<std::mutex> lk(c.mu);
+  int rc = ensure_init(c);
+  if (!rc && (!x || !out)) rc = fail(FFN_B200_EINVAL, "mlp_accum: null x/out");
+  // A new target flushes the previous pending one.
+  if (!rc && c.pend_host && (c.pend_host != out || c.pend_n != hidden)) rc = flush_pending(c);
+  if (!rc) rc = c.x.ensure(hidden * 4);
+  if (!rc) rc = c.out.ensure(hidden * 4);
+  if (!rc) rc = c.ws.ensure(ffn_b200_expert_ws_bytes(inter, hidden, 1));
+  ffn_b200_expert e = he;
+  if (!rc) rc = resolve_expert(c, e, inter, hidden);
+  if (!rc && accumulate && !c.pend_host) {
+    // accumulate onto the host's current contents
+    cudaError_t er = cudaMemcpyAsync(c.out.p, out, hidden * 4, cudaMemcpyHostToDevice, c.st);
+    if (er != cudaSuccess) rc = cuda_fail(er, "out upload");
+  }
+  if (!rc) {
+    cudaError_t er = cudaMemcpyAsync(c.x.p, x, hidden * 4, cudaMemcpyHostToDevice, c.st);
+    if (er != cudaSuccess) rc = cuda_fail(er, "x upload");
+  }
+  if (!rc)
+    rc = ffn_b200_expert_forward(inter, hidden, 1, &e, (const float *)c.x.p, (float *)c.out.p, w,
+                                 accumulate ? 1 : 0, c.ws.p, c.ws.n, c.st);
+  if (!rc) {
+    c.pend_host = out;
+    c.pend_n = hidden;
+    if (sync_now) rc = flush_pending(c);
+  }
+  if (rc) {
+    std::fprintf(stderr, "[ffn_b200] %s\n", ffn_b200_last_error());
+    c.pend_host = nullptr;
+    c.pend_n = 0;
+    return false;
+  }
+  return true;
+}
+
+bool mlp_batch(const ffn_b200_expert &he, size_t inter, size_t hidden, size_t m, size_t x_off,
+               const size_t *dst, const float *dw, size_t b_len, float *out, bool sync_now) {
+  Ctx &c = ctx();
+  std::lock_guard<std::mutex> lk(c.mu);
+  int rc = ensure_init(c);
+  if (!rc && (!dst || !dw || !out)) rc = fail(FFN_B200_EINVAL, "mlp_batch: null pointer");
+  if (!rc && (!c.xall_host || c.xall_hidden != hidden || x_off + m > c.xall_tok))
+    rc = fail(FFN_B200_EINVAL, "mlp_batch: x rows outside the ffn_b200_set_batch_input buffer");
+  if (!rc && (m == 0 || m > 8)) rc = fail(FFN_B200_EINVAL, "mlp_batch: 1..8 tokens per call");
+  for (size_t k = 0; !rc && k < m; ++k)
+    if (dst[k] >= b_len) rc = fail(FFN_B200_EINVAL, "mlp_batch: destination token out of range");
+  if (!rc && c.pend_host && (c.pend_host != out || c.pend_n != b_len * hidden)) rc = flush_pending(c);
+  const size_t ews = ffn_b200_expert_ws_bytes(inter, hidden, m);
+  if (!rc) rc = c.out.ensure(b_len * hidden * 4);
+  if (!rc) rc = c.ws.ensure(ews + 256 + m * hidden * 4);
+  if (!rc) rc = c.tmp.ensure(1024);
+  if (!rc && !c.xall_dev_valid) {
+    rc = c.xall.ensure(c.xall_tok * hidden * 4);
+    if (!rc) {
+      cudaError_t er = cudaMemcpyAsync(c.xall.p, c.xall_host, c.xall_tok * hidden * 4,
+                                       cudaMemcpyHostToDevice, c.st);
+      if (er != cudaSuccess) rc = cuda_fail(er, "x_all upload");
+      else c.xall_dev_valid = true;
+    }
+  }
+  ffn_b200_expert e = he;
+  if (!rc) rc = resolve_expert(c, e, inter, hidden);
+  if (!rc && !c.pend_host) {
+    cudaError_t er = cudaMemcpyAsync(c.out.p, out, b_len * hidden * 4, cudaMemcpyHostToDevice, c.st);
+    if (er != cudaSuccess) rc = cuda_fail(er, "out_batch upload");
+  }
+  // expert outputs y [m, hidden] land after the expert workspace
+  float *y = (float *)((char *)c.ws.p + ((ews + 255) & ~(size_t)255));
+  if (!rc) {
+    int64_t d64[8];
+    float w8[8];
+    for (size_t k = 0; k < m; ++k) { d64[k] = (int64_t)dst[k]; w8[k] = dw[k]; }
+    cudaError_t er = cudaMemcpyAsync(c.tmp.p, d64, m * 8, cudaMemcpyHostToDevice, c.st);
+    if (er == cudaSuccess)
+      er = cudaMemcpyAsync((char *)c.tmp.p + 512, w8, m * 4, cudaMemcpyHostToDevice, c.st);
+    // the copies read these stack arrays: wait for them before they go out of scope
+    if (er == cudaSuccess) er = cudaStreamSynchronize(c.st);
+    if (er != cudaSuccess) rc = cuda_fail(er, "dst upload");
+  }
+  if (!rc)
+    rc = ffn_b200_expert_forward(inter, hidden, m, &e, (const float *)c.xall.p + x_off * hidden, y,
+                                 1.0f, 0, c.ws.p, ews, c.st);
+  if (!rc)
+    rc = launch_scatter_axpy(y, (const int64_t *)c.tmp.p, (const float *)((char *)c.tmp.p + 512),
+                             (int)m, (int)hidden, (float *)c.out.p, c.st);
+  if (!rc) {
+    c.pend_host = out;
+    c.pend_n = b_len * hidden;
+    if (sync_now) rc = flush_pending(c);
+  }
+  if (rc) {
+    std::fprintf(stderr, "[ffn_b200] %s\n", ffn_b200_last_error());
+    c.pend_host = nullptr;
+    c.pend_n = 0;
+    return false;
+  }
+  return true;
+}
+
+ffn_b200_expert nvfp4_expert(const uint8_t *w1, const uint8_t *s1, float g1, const uint8_t *w3,
+                             const uint8_t *s3, float g3, const uint8_t *w2, const uint8_t *s2,
+                             float g2) {
+  ffn_b200_expert e{};
+  e.format = FFN_B200_FMT_NVFP4;
+  e.proj_scale = 1.0f;
+  e.nv[0] = {w1, s1, g1, 0};
+  e.nv[1] = {w3, s3, g3, 0};
+  e.nv[2] = {w2, s2, g2, 0};
+  return e;
+}
+
+ffn_b200_expert ternary_expert(const uint8_t *p1, const float *r1, const uint8_t *p3,
+                               const float *r3, const uint8_t *p2, const float *r2, float sc) {
+  ffn_b200_expert e{};
+  e.format = FFN_B200_FMT_TERNARY;
+  e.proj_scale = sc;
+  e.tn[0].p = p1; e.tn[0].rs = r1;
+  e.tn[1].p = p3; e.tn[1].rs = r3;
+  e.tn[2].p = p2; e.tn[2].rs = r2;
+  return e;
+}
+
+}  // namespace
+}  // namespace ffn
+
+using namespace ffn;
+
+extern "C" {
+
+const HardwareAddonVTable *merkaba_hardware_addon_v1(void) {
+  static const HardwareAddonVTable vt = make_vtable();
+  return &vt;
+}
+
+bool gx10_rust_nvfp4_mlp_accum(size_t inter_rows, size_t hidden_cols, const uint8_t *w1_fp4,
+                               const uint8_t *w1_s, float w1_sc2, const uint8_t *w3_fp4,
+                               const uint8_t *w3_s, float w3_sc2, const uint8_t *w2_fp4,
+                               const uint8_t *w2_s, float w2_sc2, const float *x, float *out,
+                               float accum_weight, bool accumulate, bool sync_now) {
+  const ffn_b200_expert e =
+      nvfp4_expert(w1_fp4, w1_s, w1_sc2, w3_fp4, w3_s, w3_sc2, w2_fp4, w2_s, w2_sc2);
+  return mlp_accum(e, inter_rows, hidden_cols, x, out, accum_weight, accumulate, sync_now);
+}
+
+bool gx10_rust_ternary_158_mlp_accum(size_t inter_rows, size_t hidden_cols, const uint8_t *w1_p,
+                                     const float *w1_s, const uint8_t *w3_p, const float *w3_s,
+                                     const uint8_t *w2_p, const float *w2_s, float proj_scale,
+                                     const float *x, float *out, float accum_weight,
+                                     bool accumulate, bool sync_now) {
+  const ffn_b200_expert e = ternary_expert(w1_p, w1_s, w3_p, w3_s, w2_p, w2_s, proj_scale);
+  return mlp_accum(e, inter_rows, hidden_cols, x, out, accum_weight, accumulate, sync_now);
+}
+
+bool gx10_rust_nvfp4_mlp_batch(size_t inter_rows, size_t hidden_cols, size_t seq_len,
+                               const uint8_t *w1_fp4, const uint8_t *w1_s, float w1_sc2,
+                               const uint8_t *w3_fp4, const uint8_t *w3_s, float w3_sc2,
+                               const uint8_t *w2_fp4, const uint8_t *w2_s, float w2_sc2,
+                               size_t x_tok_offset, const size_t *dst_tok_indices,
+                               const float *dst_weights, size_t b_len, float *out_batch,
+                               bool sync_now) {
+  const ffn_b200_expert e =
+      nvfp4_expert(w1_fp4, w1_s, w1_sc2, w3_fp4, w3_s, w3_sc2, w2_fp4, w2_s, w2_sc2);
+  return mlp_batch(e, inter_rows, hidden_cols, seq_len, x_tok_offset, dst_tok_indices,
+                   dst_weights, b_len, out_batch, sync_now);
+}
+
+bool gx10_rust_ternary_158_mlp_batch(size_t inter_rows, size_t hidden_cols, size_t seq_len,
+                                     const uint8_t *w1_p, const float *w1_s, const uint8_t *w3_p,
+                                     const float *w3_s, const uint8_t *w2_p, const float *w2_s,
+                                     float proj_scale, size_t x_tok_offset,
+                                     const size_t *dst_tok_indices, const float *dst_weights,
+                                     size_t b_len, float *out_batch, bool sync_now) {
+  const ffn_b200_expert e = ternary_expert(w1_p, w1_s, w3_p, w3_s, w2_p, w2_s, proj_scale);
+  return mlp_batch(e, inter_rows, hidden_cols, seq_len, x_tok_offset, dst_tok_indices,
+                   dst_weights, b_len, out_batch, sync_now);
+}
+
+void gx10_rust_register_host_range(const void *ptr, size_t bytes) {
+  if (!ptr || !bytes) return;
+  Ctx &c = ctx();
+  std::lock_guard<std::mutex> lk(c.mu);
+  const void *d;
+  if (ensure_init(c) || dev_ptr(c, ptr, bytes, &d))
+    std::fprintf(stderr, "[ffn_b200] register_host_range: %s\n", ffn_b200_last_error());
+}
+
+void gx10_rust_register_shard_bounds(const void *ptr, size_t bytes) {
+  if (!ptr || !bytes) return;
+  Ctx &c = ctx();
+  std::lock_guard<std::mutex> lk(c.mu);
+  // Shards are many GB; their tensors are copied on first use (dev_ptr).
+  c.shard_bounds.emplace_back((uintptr_t)ptr, bytes);
+}
+
+int ffn_b200_set_batch_input(const float *x_all_host, size_t x_total_tokens, size_t hidden) {
+  Ctx &c = ctx();
+  std::lock_guard<std::mutex> lk(c.mu);
+  c.xall_host = x_all_host;
+  c.xall_tok = x_total_tokens;
+  c.xall_hidden = hidden;
+  c.xall_dev_valid = false;
+  return 0;
+}
+
+int ffn_b200_release_host_ranges(void) {
+  Ctx &c = ctx();
+  std::lock_guard<std::mutex> lk(c.mu);
+  int rc = flush_pending(c);
+  if (c.init) cudaStreamSynchronize(c.st);
+  for (auto &kv : c.ranges)
+    for (Range &r : kv.second) cudaFree(r.d);
+  c.ranges.clear();
+  c.cached = 0;
+  return rc;
+}
+
+size_t ffn_b200_host_cache_bytes(void) {
+  Ctx &c = ctx();
+  std::lock_guard<std::mutex> lk(c.mu);
+  return c.cached;
+}
+
+}  // extern "C"

@@ -1,0 +1,504 @@
+// ffn_api.cu -- the device-resident extension ABI (include/ffn_b200.h).
+#include <algorithm>
+#include <atomic>
+#include <string>
+
+#include "ffn_internal.h"
+
+namespace ffn {
+
+// ------------------------------------------------------------------ status
+static thread_local std::string t_last_error;
+static std::atomic<uint64_t> g_launches{0};
+
+void set_error(const std::string &msg) { t_last_error = msg; }
+int fail(int code, const std::string &msg) {
+  t_last_error = msg;
+  return code;
+}
+int cuda_fail(cudaError_t e, const char *what) {
+  return fail(FFN_B200_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+void note_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+static int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+// Persistent grid: two CTAs per SM (the phase kernels' occupancy target).
+static int phase_grid(long long tiles) {
+  const long long cap = 2LL * sm_count();
+  return (int)std::max<long long>(1, std::min<long long>(tiles, cap));
+}
+
+// ---------------------------------------------------------- workspace carving
+// A bump allocator over the caller's buffer; with base == nullptr it only sizes.
+struct Carve {
+  char *base;
+  size_t off = 0;
+  explicit Carve(void *b) : base((char *)b) {}
+  template <class T>
+  T *take(size_t n) {
+    off = (off + 255) & ~(size_t)255;
+    T *p = base ? reinterpret_cast<T *>(base + off) : nullptr;
+    off += n * sizeof(T);
+    return p;
+  }
+};
+
+static bool aligned(const void *p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+static int check_mat_shape(int fmt, size_t rows, size_t cols, const char *what) {
+  if (rows == 0 || cols == 0)
+    return fail(FFN_B200_EINVAL, std::string(what) + ": rows and cols must be positive");
+  if (rows > (1u << 30) || cols > (1u << 24))
+    return fail(FFN_B200_EINVAL, std::string(what) + ": shape too large");
+  const size_t q = fmt == FFN_B200_FMT_NVFP4 ? 32 : 64;
+  if (cols % q)
+    return fail(FFN_B200_EUNSUP, std::string(what) + ": cols must be a multiple of " +
+                                     std::to_string(q) + " for this format");
+  return 0;
+}
+
+static int check_nvfp4(const ffn_b200_nvfp4_mat &m, const char *what) {
+  if (!m.w || !m.s) return fail(FFN_B200_EINVAL, std::string(what) + ": null NVFP4 pointer");
+  if (!aligned(m.w, 16) || !aligned(m.s, 2))
+    return fail(FFN_B200_EINVAL, std::string(what) + ": NVFP4 w must be 16-byte and s 2-byte aligned");
+  return 0;
+}
+
+static int check_ternary(const ffn_b200_ternary_mat &m, const char *what) {
+  if (!m.p || !m.rs) return fail(FFN_B200_EINVAL, std::string(what) + ": null ternary pointer");
+  if (!aligned(m.p, 16) || !aligned(m.rs, 4))
+    return fail(FFN_B200_EINVAL, std::string(what) + ": ternary p must be 16-byte and rs 4-byte aligned");
+  if (m.core_a && (!m.core_b || !m.core_a_sc || !m.core_b_sc || !aligned(m.core_b, 16)))
+    return fail(FFN_B200_EINVAL, std::string(what) + ": incomplete or misaligned rank-16 core");
+  return 0;
+}
+
+// Workspace of one dense activation block: x16 hi/lo + exponents + core z.
+struct ActWs {
+  __half *xh, *xl;
+  int *xe;
+  float *z;
+};
+static ActWs carve_act(Carve &c, size_t n_rows, size_t K) {
+  ActWs w;
+  w.xh = c.take<__half>(n_rows * K);
+  w.xl = c.take<__half>(n_rows * K);
+  w.xe = c.take<int>(n_rows);
+  w.z = c.take<float>(n_rows * 3 * 16);
+  return w;
+}
+
+}  // namespace ffn
+
+using namespace ffn;
+
+extern "C" {
+
+const char *ffn_b200_version(void) { return "ffn_b200 0.1 (sm_100a)"; }
+const char *ffn_b200_last_error(void) { return t_last_error.c_str(); }
+uint64_t ffn_b200_launch_count(void) { return g_launches.load(); }
+
+int ffn_b200_set_device(int device) {
+  FFN_CUDA_TRY(cudaSetDevice(device));
+  return 0;
+}
+
+uint64_t ffn_b200_key(uint64_t parent, uint64_t v) {
+  uint64_t z = parent + 0x9E3779B97F4A7C15ULL * (v + 1);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+
+// ------------------------------------------------------------ single matrix
+size_t ffn_b200_matvec_ws_bytes(size_t seq, size_t cols) {
+  Carve c(nullptr);
+  carve_act(c, seq, cols);
+  return c.off + 256;
+}
+
+static int matvec_common(int fmt, size_t rows, size_t cols, size_t seq, const ffn_b200_expert &E,
+                         const float *x, float *out, void *ws, size_t ws_bytes, void *stream) {
+  if (seq == 0) return 0;
+  if (!x || !out) return fail(FFN_B200_EINVAL, "matvec: null x/out");
+  if (seq > (1u << 24)) return fail(FFN_B200_EINVAL, "matvec: seq too large");
+  if (!ws || ws_bytes < ffn_b200_matvec_ws_bytes(seq, cols))
+    return fail(FFN_B200_ENOSPC, "matvec: workspace too small (see ffn_b200_matvec_ws_bytes)");
+  cudaStream_t st = (cudaStream_t)stream;
+  Carve c(ws);
+  ActWs a = carve_act(c, seq, cols);
+  const bool tern = fmt == FFN_B200_FMT_TERNARY;
+  int rc = launch_xprep(x, (int)cols, (int)seq, (int)cols, tern ? nullptr : a.xh,
+                        tern ? nullptr : a.xl, tern ? a.xh : nullptr, tern ? a.xl : nullptr,
+                        (int)cols, a.xe, st);
+  if (rc) return rc;
+  if (tern && E.tn[0].core_a) {
+    CoreZArgs z{};
+    z.direct = E;
+    z.n_tok_direct = (int)seq;
+    z.K = (int)cols;
+    z.mat0 = 0;
+    z.nmat = 1;
+    z.xf = x;
+    z.ld_xf = (int)cols;
+    z.z = a.z;
+    if ((rc = launch_corez(z, (int)((seq + kNTok - 1) / kNTok), st))) return rc;
+  }
+  PhaseArgs p{};
+  p.direct = E;
+  p.n_tok_direct = (int)seq;
+  p.rows = (int)rows;
+  p.K = (int)cols;
+  p.blocks = (int)((rows + rows_per_tile(0) - 1) / rows_per_tile(0));
+  p.xh = a.xh;
+  p.xl = a.xl;
+  p.xe = a.xe;
+  p.ld_x = (int)cols;
+  p.z = a.z;
+  p.y = out;
+  p.ld_y = (int)rows;
+  p.out_w = 1.0f;
+  p.mat = 0;
+  const long long tiles = (long long)((seq + kNTok - 1) / kNTok) * p.blocks;
+  return launch_phase(fmt, 0, p, phase_grid(tiles), st);
+}
+
+int ffn_b200_nvfp4_matvec(size_t rows, size_t cols, size_t seq, const ffn_b200_nvfp4_mat *m,
+                          const float *x, float *out, void *ws, size_t ws_bytes, void *stream) {
+  if (!m) return fail(FFN_B200_EINVAL, "nvfp4_matvec: null matrix");
+  int rc = check_mat_shape(FFN_B200_FMT_NVFP4, rows, cols, "nvfp4_matvec");
+  if (!rc) rc = check_nvfp4(*m, "nvfp4_matvec");
+  if (rc) return rc;
+  ffn_b200_expert E{};
+  E.format = FFN_B200_FMT_NVFP4;
+  E.proj_scale = 1.0f;
+  E.nv[0] = *m;
+  return matvec_common(FFN_B200_FMT_NVFP4, rows, cols, seq, E, x, out, ws, ws_bytes, stream);
+}
+
+int ffn_b200_ternary_matvec(size_t rows, size_t cols, size_t seq, const ffn_b200_ternary_mat *m,
+                            const float *x, float *out, void *ws, size_t ws_bytes, void *stream) {
+  if (!m) return fail(FFN_B200_EINVAL, "ternary_matvec: null matrix");
+  int rc = check_mat_shape(FFN_B200_FMT_TERNARY, rows, cols, "ternary_matvec");
+  if (!rc) rc = check_ternary(*m, "ternary_matvec");
+  if (rc) return rc;
+  ffn_b200_expert E{};
+  E.format = FFN_B200_FMT_TERNARY;
+  E.proj_scale = 1.0f;
+  E.tn[0] = *m;
+  return matvec_common(FFN_B200_FMT_TERNARY, rows, cols, seq, E, x, out, ws, ws_bytes, stream);
+}
+
+// --------------------------------------------------------------- one expert
+size_t ffn_b200_expert_ws_bytes(size_t inter, size_t hidden, size_t seq) {
+  Carve c(nullptr);
+  carve_act(c, seq, hidden);
+  c.take<__half>(seq * inter);
+  c.take<__half>(seq * inter);
+  return c.off + 256;
+}
+
+static int check_expert(const ffn_b200_expert &e, size_t inter, size_t hidden, const char *what) {
+  int rc;
+  if (e.format != FFN_B200_FMT_NVFP4 && e.format != FFN_B200_FMT_TERNARY)
+    return fail(FFN_B200_EINVAL, std::string(what) + ": unknown expert format");
+  if ((rc = check_mat_shape(e.format, inter, hidden, what))) return rc;
+  if ((rc = check_mat_shape(e.format, hidden, inter, what))) return rc;
+  for (int i = 0; i < 3; ++i) {
+    rc = e.format == FFN_B200_FMT_NVFP4 ? check_nvfp4(e.nv[i], what) : check_ternary(e.tn[i], what);
+    if (rc) return rc;
+  }
+  return 0;
+}
+
+int ffn_b200_expert_forward(size_t inter, size_t hidden, size_t seq, const ffn_b200_expert *e,
+                            const float *x, float *out, float accum_weight, int accumulate,
+                            void *ws, size_t ws_bytes, void *stream) {
+  if (!e) return fail(FFN_B200_EINVAL, "expert_forward: null expert");
+  int rc = check_expert(*e, inter, hidden, "expert_forward");
+  if (rc) return rc;
+  if (seq == 0) return 0;
+  if (!x || !out) return fail(FFN_B200_EINVAL, "expert_forward: null x/out");
+  if (seq > (1u << 24)) return fail(FFN_B200_EINVAL, "expert_forward: seq too large");
+  if (!ws || ws_bytes < ffn_b200_expert_ws_bytes(inter, hidden, seq))
+    return fail(FFN_B200_ENOSPC, "expert_forward: workspace too small (see ffn_b200_expert_ws_bytes)");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int fmt = e->format;
+  const bool tern = fmt == FFN_B200_FMT_TERNARY;
+  Carve c(ws);
+  ActWs a = carve_act(c, seq, hidden);
+  __half *hh = c.take<__half>(seq * inter), *hl = c.take<__half>(seq * inter);
+  const int nv = (int)((seq + kNTok - 1) / kNTok);
+  if ((rc = launch_xprep(x, (int)hidden, (int)seq, (int)hidden, tern ? nullptr : a.xh,
+                         tern ? nullptr : a.xl, tern ? a.xh : nullptr, tern ? a.xl : nullptr,
+                         (int)hidden, a.xe, st)))
+    return rc;
+  const bool cores = tern && (e->tn[0].core_a || e->tn[1].core_a || e->tn[2].core_a);
+  if (cores) {
+    CoreZArgs z{};
+    z.direct = *e;
+    z.n_tok_direct = (int)seq;
+    z.K = (int)hidden;
+    z.mat0 = 0;
+    z.nmat = 2;
+    z.xf = x;
+    z.ld_xf = (int)hidden;
+    z.z = a.z;
+    if ((rc = launch_corez(z, nv, st))) return rc;
+  }
+  PhaseArgs p{};
+  p.direct = *e;
+  p.n_tok_direct = (int)seq;
+  p.rows = (int)inter;
+  p.K = (int)hidden;
+  p.blocks = (int)((inter + rows_per_tile(1) - 1) / rows_per_tile(1));
+  p.xh = a.xh;
+  p.xl = a.xl;
+  p.xe = a.xe;
+  p.ld_x = (int)hidden;
+  p.z = a.z;
+  p.hh = hh;
+  p.hl = hl;
+  p.ld_h = (int)inter;
+  if ((rc = launch_phase(fmt, 1, p, phase_grid((long long)nv * p.blocks), st))) return rc;
+  if (cores) {
+    CoreZArgs z{};
+    z.direct = *e;
+    z.n_tok_direct = (int)seq;
+    z.K = (int)inter;
+    z.mat0 = 2;
+    z.nmat = 1;
+    z.hh = hh;
+    z.hl = hl;
+    z.ld_h = (int)inter;
+    z.z = a.z;
+    if ((rc = launch_corez(z, nv, st))) return rc;
+  }
+  // h is written unscaled (|h| <= 100 by the clamps), so phase 2 takes no exponent.
+  PhaseArgs q{};
+  q.direct = *e;
+  q.n_tok_direct = (int)seq;
+  q.rows = (int)hidden;
+  q.K = (int)inter;
+  q.blocks = (int)((hidden + rows_per_tile(2) - 1) / rows_per_tile(2));
+  q.xh = hh;
+  q.xl = hl;
+  q.xe = nullptr;
+  q.ld_x = (int)inter;
+  q.z = a.z;
+  q.y = out;
+  q.ld_y = (int)hidden;
+  q.out_w = accum_weight;
+  q.accumulate = accumulate ? 1 : 0;
+  return launch_phase(fmt, 2, q, phase_grid((long long)nv * q.blocks), st);
+}
+
+// ---------------------------------------------------------------- MoE layer
+struct MoeWs {
+  __half *xh, *xl, *th, *tl;
+  int *xe;
+  float *logits;
+  int32_t *idx, *inv, *pair_tok;
+  float *wt;
+  int *ints;
+  VExp *vexp_nv, *vexp_tn;
+  int *n_vexp;
+  __half *hh, *hl;
+  float *z, *y;
+};
+
+static MoeWs carve_moe(Carve &c, const ffn_b200_moe_desc &d, size_t T) {
+  MoeWs w{};
+  const size_t H = d.hidden, I = d.inter, E = d.n_experts, k = d.top_k, P = T * k;
+  if (d.has_nvfp4) { w.xh = c.take<__half>(T * H); w.xl = c.take<__half>(T * H); }
+  if (d.has_ternary) { w.th = c.take<__half>(T * H); w.tl = c.take<__half>(T * H); }
+  w.xe = c.take<int>(T);
+  w.logits = c.take<float>(T * E);
+  w.idx = c.take<int32_t>(P);
+  w.wt = c.take<float>(P);
+  w.inv = c.take<int32_t>(P);
+  w.pair_tok = c.take<int32_t>(P);
+  w.ints = c.take<int>(4 * E);
+  w.vexp_nv = c.take<VExp>(P + E);
+  w.vexp_tn = c.take<VExp>(P + E);
+  w.n_vexp = c.take<int>(4);
+  w.hh = c.take<__half>(P * I);
+  w.hl = c.take<__half>(P * I);
+  w.z = d.has_ternary ? c.take<float>(P * 3 * 16) : nullptr;
+  w.y = c.take<float>(P * H);
+  return w;
+}
+
+size_t ffn_b200_moe_ws_bytes(const ffn_b200_moe_desc *d, size_t max_tokens) {
+  if (!d) return 0;
+  Carve c(nullptr);
+  carve_moe(c, *d, max_tokens);
+  return c.off + 256;
+}
+
+int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
+                       const float *residual, float *out, int32_t *topk_idx, float *topk_w,
+                       void *ws, size_t ws_bytes, void *stream) {
+  if (!d) return fail(FFN_B200_EINVAL, "moe_layer: null descriptor");
+  const size_t H = d->hidden, I = d->inter, E = d->n_experts, k = d->top_k;
+  if (!d->experts || !d->router_w) return fail(FFN_B200_EINVAL, "moe_layer: null experts/router");
+  if (E == 0 || E > 4096) return fail(FFN_B200_EINVAL, "moe_layer: n_experts must be in 1..4096");
+  if (k == 0 || k > (size_t)kTopKMax || k > E)
+    return fail(FFN_B200_EINVAL, "moe_layer: top_k must be in 1..min(16, n_experts)");
+  if (!d->has_nvfp4 && !d->has_ternary)
+    return fail(FFN_B200_EINVAL, "moe_layer: has_nvfp4/has_ternary both zero");
+  if (H % 64 || I % 64 || H == 0 || I == 0 || H > (1u << 20) || I > (1u << 20))
+    return fail(FFN_B200_EUNSUP, "moe_layer: hidden and inter must be multiples of 64");
+  if (d->expert_begin < 0 || d->expert_end > (int)E || d->expert_begin > d->expert_end)
+    return fail(FFN_B200_EINVAL, "moe_layer: bad expert range");
+  if (d->score_fn != FFN_B200_SCORE_REF_SQRTSOFTPLUS && d->score_fn != FFN_B200_SCORE_SIGMOID)
+    return fail(FFN_B200_EINVAL, "moe_layer: unknown score_fn");
+  if (d->router_mode != FFN_B200_ROUTER_EXACT)
+    return fail(FFN_B200_EUNSUP, "moe_layer: only FFN_B200_ROUTER_EXACT is implemented");
+  if (n_tok == 0) return 0;
+  if (!x || !out) return fail(FFN_B200_EINVAL, "moe_layer: null x/out");
+  if (n_tok * k > (1u << 24)) return fail(FFN_B200_EINVAL, "moe_layer: too many tokens");
+  if (!ws || ws_bytes < ffn_b200_moe_ws_bytes(d, n_tok))
+    return fail(FFN_B200_ENOSPC, "moe_layer: workspace too small (see ffn_b200_moe_ws_bytes)");
+  cudaStream_t st = (cudaStream_t)stream;
+  Carve c(ws);
+  MoeWs w = carve_moe(c, *d, n_tok);
+  const int T = (int)n_tok, P = (int)(n_tok * k);
+  int rc;
+  if ((rc = launch_xprep(x, (int)H, T, (int)H, w.xh, w.xl, w.th, w.tl, (int)H, w.xe, st)))
+    return rc;
+  if ((rc = launch_router(d->router_w, d->router_bias, x, T, (int)E, (int)H, (int)k, d->score_fn,
+                          w.logits, w.idx, w.wt, st)))
+    return rc;
+  if ((rc = launch_group(w.idx, T, (int)k, (int)E, d->expert_begin, d->expert_end, d->experts,
+                         w.ints, w.pair_tok, w.inv, w.vexp_nv, w.vexp_tn, w.n_vexp, st)))
+    return rc;
+  // Upper bound of slices per format (the device count is <= this).
+  const int e_local = d->expert_end - d->expert_begin;
+  const long long max_vexp = std::min<long long>((long long)P, (long long)P / kNTok + e_local);
+  for (int f = 0; f < 2; ++f) {
+    const int fmt = f == 0 ? FFN_B200_FMT_NVFP4 : FFN_B200_FMT_TERNARY;
+    if ((fmt == FFN_B200_FMT_NVFP4 && !d->has_nvfp4) || (fmt == FFN_B200_FMT_TERNARY && !d->has_ternary))
+      continue;
+    const VExp *vl = f == 0 ? w.vexp_nv : w.vexp_tn;
+    const int *nvd = w.n_vexp + f;
+    const bool tern = fmt == FFN_B200_FMT_TERNARY;
+    if (tern) {
+      CoreZArgs z{};
+      z.experts = d->experts;
+      z.vexp = vl;
+      z.n_vexp_dev = nvd;
+      z.K = (int)H;
+      z.mat0 = 0;
+      z.nmat = 2;
+      z.xf = x;
+      z.ld_xf = (int)H;
+      z.pair_tok = w.pair_tok;
+      z.z = w.z;
+      if ((rc = launch_corez(z, (int)max_vexp, st))) return rc;
+    }
+    PhaseArgs p{};
+    p.experts = d->experts;
+    p.vexp = vl;
+    p.n_vexp_dev = nvd;
+    p.rows = (int)I;
+    p.K = (int)H;
+    p.blocks = (int)((I + rows_per_tile(1) - 1) / rows_per_tile(1));
+    p.xh = tern ? w.th : w.xh;
+    p.xl = tern ? w.tl : w.xl;
+    p.xe = w.xe;
+    p.ld_x = (int)H;
+    p.pair_tok = w.pair_tok;
+    p.z = w.z;
+    p.hh = w.hh;
+    p.hl = w.hl;
+    p.ld_h = (int)I;
+    if ((rc = launch_phase(fmt, 1, p, phase_grid(max_vexp * p.blocks), st))) return rc;
+    if (tern) {
+      CoreZArgs z{};
+      z.experts = d->experts;
+      z.vexp = vl;
+      z.n_vexp_dev = nvd;
+      z.K = (int)I;
+      z.mat0 = 2;
+      z.nmat = 1;
+      z.hh = w.hh;
+      z.hl = w.hl;
+      z.ld_h = (int)I;
+      z.z = w.z;
+      if ((rc = launch_corez(z, (int)max_vexp, st))) return rc;
+    }
+    PhaseArgs q{};
+    q.experts = d->experts;
+    q.vexp = vl;
+    q.n_vexp_dev = nvd;
+    q.rows = (int)H;
+    q.K = (int)I;
+    q.blocks = (int)((H + rows_per_tile(2) - 1) / rows_per_tile(2));
+    q.xh = w.hh;
+    q.xl = w.hl;
+    q.xe = nullptr;
+    q.ld_x = (int)I;
+    q.z = w.z;
+    q.y = w.y;
+    q.ld_y = (int)H;
+    if ((rc = launch_phase(fmt, 2, q, phase_grid(max_vexp * q.blocks), st))) return rc;
+  }
+  if ((rc = launch_combine(w.y, (int)H, w.idx, w.wt, w.inv, T, (int)k, d->experts, residual, out,
+                           (int)H, st)))
+    return rc;
+  if (topk_idx)
+    FFN_CUDA_TRY(cudaMemcpyAsync(topk_idx, w.idx, P * sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
+  if (topk_w)
+    FFN_CUDA_TRY(cudaMemcpyAsync(topk_w, w.wt, P * sizeof(float), cudaMemcpyDeviceToDevice, st));
+  return 0;
+}
+
+// -------------------------------------------------------------- generators
+int ffn_b200_gen_nvfp4(uint64_t key, size_t rows, size_t cols, uint8_t *w, uint8_t *s,
+                       void *stream) {
+  if (!w || !s || cols % 16) return fail(FFN_B200_EINVAL, "gen_nvfp4: bad arguments");
+  return launch_gen_nvfp4(ffn_b200_key(key, 1), ffn_b200_key(key, 2), rows, cols, w, s,
+                          (cudaStream_t)stream);
+}
+int ffn_b200_gen_ternary(uint64_t key, size_t rows, size_t cols, uint8_t *p, float *rs,
+                         void *stream) {
+  if (!p || !rs || cols % 4) return fail(FFN_B200_EINVAL, "gen_ternary: bad arguments");
+  return launch_gen_ternary(ffn_b200_key(key, 3), ffn_b200_key(key, 4), rows, cols, p, rs,
+                            (cudaStream_t)stream);
+}
+int ffn_b200_gen_core(uint64_t key, size_t rows, size_t cols, int8_t *a, float *a_sc, int8_t *b,
+                      float *b_sc, void *stream) {
+  if (!a || !a_sc || !b || !b_sc) return fail(FFN_B200_EINVAL, "gen_core: bad arguments");
+  return launch_gen_core(ffn_b200_key(key, 5), ffn_b200_key(key, 6), ffn_b200_key(key, 7),
+                         ffn_b200_key(key, 8), rows, cols, a, a_sc, b, b_sc, (cudaStream_t)stream);
+}
+int ffn_b200_gen_normal(uint64_t key, size_t n, float stdev, float *out, void *stream) {
+  if (!out) return fail(FFN_B200_EINVAL, "gen_normal: null out");
+  return launch_gen_normal(key, n, stdev, out, (cudaStream_t)stream);
+}
+
+int ffn_b200_dequant_nvfp4(size_t rows, size_t cols, const uint8_t *w, const uint8_t *s,
+                           float *out, void *stream) {
+  if (!w || !s || !out || cols % 16) return fail(FFN_B200_EINVAL, "dequant_nvfp4: bad arguments");
+  return launch_dequant_nvfp4(rows, cols, w, s, out, (cudaStream_t)stream);
+}
+int ffn_b200_dequant_ternary(size_t rows, size_t cols, const uint8_t *p, float *out,
+                             void *stream) {
+  if (!p || !out || cols % 4) return fail(FFN_B200_EINVAL, "dequant_ternary: bad arguments");
+  return launch_dequant_ternary(rows, cols, p, out, (cudaStream_t)stream);
+}
+
+}  // extern "C"

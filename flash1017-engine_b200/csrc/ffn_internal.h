@@ -1,0 +1,82 @@
+// ffn_internal.h -- declarations shared by the CUDA launchers and the C-ABI layers.
+#pragma once
+
+#include "common.cuh"
+
+namespace ffn {
+
+// Arguments of the grouped expert GEMV phases (see phase_kernel in ffn_kernels.cu).
+struct PhaseArgs {
+  const ffn_b200_expert *experts;  // device table (list mode)
+  ffn_b200_expert direct;          // the expert of direct mode
+  const VExp *vexp;                // list mode: slices; nullptr = direct mode
+  const int *n_vexp_dev;           // list mode: number of slices
+  int n_tok_direct;                // direct mode: tokens (slices of 8)
+  int rows, K, blocks;             // output rows, reduction length, row blocks per slice
+  // input activations (rows indexed by pair, or by pair_tok[pair] when set)
+  const __half *xh, *xl;
+  const int *xe;                   // per-row power-of-two exponent, or nullptr (0)
+  int ld_x;
+  const int *pair_tok;
+  // rank-16 core terms z[pair][3][16] (ternary experts with cores)
+  const float *z;
+  // outputs
+  __half *hh, *hl;  // phase 1: h [pair][rows]
+  int ld_h;
+  float *y;         // phase 2 list mode: y [pair][rows]; phase 0/2 direct: out [tok][rows]
+  int ld_y;
+  float out_w;      // direct mode epilogue weight
+  int accumulate;   // direct mode: out += w*y (1) or out = w*y (0)
+  int mat;          // phase 0: matrix index of `direct` used
+};
+
+// Arguments of the rank-16 core z kernel.
+struct CoreZArgs {
+  const ffn_b200_expert *experts;
+  ffn_b200_expert direct;
+  const VExp *vexp;
+  const int *n_vexp_dev;
+  int n_tok_direct;
+  int K;
+  int mat0, nmat;            // matrices [mat0, mat0 + nmat)
+  const float *xf;           // f32 input rows (gate/up cores), or nullptr
+  int ld_xf;
+  const int *pair_tok;
+  const __half *hh, *hl;     // pair-order f16 input rows (down core)
+  int ld_h;
+  float *z;                  // [pair][3][16]
+};
+
+int rows_per_tile(int phase);
+int launch_xprep(const float *x, int ld_x, int rows, int K, __half *nh, __half *nl, __half *th,
+                 __half *tl, int ld_o, int *xe, cudaStream_t st);
+int launch_phase(int fmt, int phase, const PhaseArgs &a, int grid, cudaStream_t st);
+int launch_corez(const CoreZArgs &a, int max_vexp, cudaStream_t st);
+int launch_exact_matvec(const float *w32, const uint16_t *w16, const float *x, int n_tok,
+                        int rows, int H, float *out, cudaStream_t st);
+int launch_router(const float *w, const float *bias, const float *x, int n_tok, int n_exp,
+                  int H, int top_k, int score_fn, float *logits, int32_t *idx, float *wt,
+                  cudaStream_t st);
+int launch_group(const int32_t *idx, int n_tok, int top_k, int n_exp, int e_begin, int e_end,
+                 const ffn_b200_expert *experts, int *ws_int, int32_t *pair_tok, int32_t *inv,
+                 VExp *vexp_nv, VExp *vexp_tn, int *n_vexp, cudaStream_t st);
+int launch_combine(const float *y, int ld_y, const int32_t *idx, const float *wt,
+                   const int32_t *inv, int n_tok, int top_k, const ffn_b200_expert *experts,
+                   const float *residual, float *out, int H, cudaStream_t st);
+int launch_scatter_axpy(const float *y, const int64_t *dst, const float *w, int m, int H,
+                        float *out, cudaStream_t st);
+int launch_dot(int mode, const void *a, const void *aux, const float *x, size_t len, float *out,
+               cudaStream_t st);
+int launch_gen_nvfp4(uint64_t kw, uint64_t ks, size_t rows, size_t cols, uint8_t *w, uint8_t *s,
+                     cudaStream_t st);
+int launch_gen_ternary(uint64_t kp, uint64_t kr, size_t rows, size_t cols, uint8_t *p, float *rs,
+                       cudaStream_t st);
+int launch_gen_core(uint64_t ka, uint64_t kb, uint64_t kas, uint64_t kbs, size_t rows,
+                    size_t cols, int8_t *a, float *a_sc, int8_t *b, float *b_sc, cudaStream_t st);
+int launch_gen_normal(uint64_t key, size_t n, float stdev, float *out, cudaStream_t st);
+int launch_dequant_nvfp4(size_t rows, size_t cols, const uint8_t *w, const uint8_t *s, float *out,
+                         cudaStream_t st);
+int launch_dequant_ternary(size_t rows, size_t cols, const uint8_t *p, float *out,
+                           cudaStream_t st);
+
+}  // namespace ffn

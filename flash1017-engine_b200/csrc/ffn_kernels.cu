@@ -1,0 +1,764 @@
+// ffn_kernels.cu -- CUDA kernels of the quantized expert-FFN path (sm_100a)
+// and their host-side launchers.
+//
+// Reference (terox27/Flash1017-Engine, crates/flash-core/src/flash1017.rs):
+//   NVFP4 matvec              :2331-2357     ternary matvec            :2602-2621
+//   rank-16 Q8 core           :2446-2472     SwiGLU expert             :7537-7561
+//   router + top-6            :7277-7376     batched grouping/combine  :8088-8099, 8267-8326
+#include <algorithm>
+
+#include "ffn_internal.h"
+#include "gemv_tile.cuh"
+
+namespace ffn {
+
+// ============================================================ activations
+// One CTA per row: x (f32) -> hi/lo f16 of x * 2^-e, e = floor(log2 max|x|) - 14,
+// in natural column order (NVFP4 consumers) and/or pair order (ternary).
+__global__ void __launch_bounds__(256) xprep_kernel(const float *__restrict__ x, int ld_x, int K,
+                                                    __half *nh, __half *nl, __half *th,
+                                                    __half *tl, int ld_o, int *xe) {
+  const int row = blockIdx.x;
+  const float *xr = x + (size_t)row * ld_x;
+  __shared__ float red[32];
+  float amax = 0.f;
+  for (int c = threadIdx.x; c < K; c += blockDim.x) amax = fmaxf(amax, fabsf(xr[c]));
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  amax = red[0];
+  int e = 0;
+  if (amax > 0.f && isfinite(amax)) {
+    int ex;
+    frexpf(amax, &ex);  // amax = m 2^ex, m in [0.5, 1)
+    e = max(-100, min(100, ex - 15));
+  }
+  const float sc = pow2f(-e);
+  const size_t o = (size_t)row * ld_o;
+  for (int c = threadIdx.x; c < K; c += blockDim.x) {
+    __half hi, lo;
+    split_f16(xr[c] * sc, hi, lo);
+    if (nh) { nh[o + c] = hi; nl[o + c] = lo; }
+    if (th) { const int p = tern_pos(c); th[o + p] = hi; tl[o + p] = lo; }
+  }
+  if (threadIdx.x == 0) xe[row] = e;
+}
+
+int launch_xprep(const float *x, int ld_x, int rows, int K, __half *nh, __half *nl, __half *th,
+                 __half *tl, int ld_o, int *xe, cudaStream_t st) {
+  if (rows <= 0) return 0;
+  xprep_kernel<<<rows, 256, 0, st>>>(x, ld_x, K, nh, nl, th, tl, ld_o, xe);
+  FFN_LAUNCH_CHECK("xprep_kernel");
+  return 0;
+}
+
+// ============================================================ phase kernels
+__device__ __forceinline__ float silu_clamped(float g) {
+  return fminf(g / (1.0f + expf(-g)), 10.0f);  // flash1017.rs:7539
+}
+__device__ __forceinline__ float clamp10(float u) {  // Rust f32::clamp(-10, 10)
+  if (u < -10.f) u = -10.f;
+  if (u > 10.f) u = 10.f;
+  return u;
+}
+
+// Rank-16 core term sum_r B[row][r] * z[r] (flash1017.rs:2465-2471).
+__device__ __forceinline__ float core_term(const int8_t *b, int row, const float *z) {
+  const int4 v = __ldg(reinterpret_cast<const int4 *>(b + (size_t)row * 16));
+  const int8_t *bb = reinterpret_cast<const int8_t *>(&v);
+  float acc = 0.f;
+#pragma unroll
+  for (int r = 0; r < 16; ++r) acc += (float)bb[r] * z[r];
+  return acc;
+}
+
+// What a tile needs of one matrix of its expert.
+struct MatInfo {
+  const uint8_t *w, *s;     // weights / NVFP4 block scales
+  float gs;                 // NVFP4 per-tensor scale
+  const float *rs;          // ternary row scales
+  const int8_t *core_b;     // ternary rank-16 B, or nullptr
+};
+
+template <int FMT>
+__device__ __forceinline__ MatInfo mat_info(const ffn_b200_expert &E, int mm) {
+  MatInfo r;
+  if (FMT == FFN_B200_FMT_NVFP4) {
+    r.w = E.nv[mm].w; r.s = E.nv[mm].s; r.gs = E.nv[mm].gs; r.rs = nullptr; r.core_b = nullptr;
+  } else {
+    r.w = E.tn[mm].p; r.s = nullptr; r.gs = 1.0f; r.rs = E.tn[mm].rs;
+    r.core_b = E.tn[mm].core_a ? E.tn[mm].core_b : nullptr;
+  }
+  return r;
+}
+
+// PHASE 1: gate+up -> h.  PHASE 2: down -> y / out.  PHASE 0: one matrix -> out.
+// Persistent CTAs walk tiles (slice, row block) with a grid stride.
+template <int FMT, int PHASE, int R>
+__global__ void __launch_bounds__(kThreads, 2) phase_kernel(const PhaseArgs a) {
+  constexpr int NMAT = PHASE == 1 ? 2 : 1;
+  using TE = TileEngine<FMT, NMAT, R>;
+  __shared__ float red[TE::RED_FLOATS];
+  const int n_vexp = a.vexp ? *a.n_vexp_dev : (a.n_tok_direct + kNTok - 1) / kNTok;
+  const int n_tiles = n_vexp * a.blocks;
+  for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    const int v = tile / a.blocks, blk = tile - v * a.blocks;
+    VExp ve;
+    if (a.vexp) {
+      ve = a.vexp[v];
+    } else {
+      ve.expert = -1;
+      ve.offset = v * kNTok;
+      ve.count = min(kNTok, a.n_tok_direct - v * kNTok);
+    }
+    int midx[NMAT];
+    if (PHASE == 1) { midx[0] = 0; midx[NMAT - 1] = 1; }
+    else midx[0] = PHASE == 2 ? 2 : a.mat;
+    MatInfo mi_[NMAT];
+    float proj;
+    if (ve.expert >= 0) {
+      const ffn_b200_expert &E = a.experts[ve.expert];
+#pragma unroll
+      for (int mi = 0; mi < NMAT; ++mi) mi_[mi] = mat_info<FMT>(E, midx[mi]);
+      proj = E.proj_scale;
+    } else {
+#pragma unroll
+      for (int mi = 0; mi < NMAT; ++mi) mi_[mi] = mat_info<FMT>(a.direct, midx[mi]);
+      proj = a.direct.proj_scale;
+    }
+    MatRef m[NMAT];
+#pragma unroll
+    for (int mi = 0; mi < NMAT; ++mi) { m[mi].w = mi_[mi].w; m[mi].s = mi_[mi].s; }
+
+    const int g = (threadIdx.x & 31) >> 2;
+    const bool has_tok = g < ve.count;
+    const int xrow = a.pair_tok ? __ldg(a.pair_tok + ve.offset + min(g, ve.count - 1))
+                                : ve.offset + min(g, ve.count - 1);
+    const int row0 = blk * TE::ROWS;
+    float acc[NMAT][R][4];
+    TE::run(m, a.rows, a.K, row0, has_tok, a.xh + (size_t)xrow * a.ld_x,
+            a.xl + (size_t)xrow * a.ld_x, acc);
+    TE::stash(red, acc);
+    __syncthreads();
+
+    // Epilogue: one (row, token) per thread iteration.
+    for (int e = threadIdx.x; e < TE::ROWS * kNTok; e += kThreads) {
+      const int rl = e % TE::ROWS, n = e / TE::ROWS;
+      const int row = row0 + rl;
+      if (n >= ve.count || row >= a.rows) continue;
+      const int p = ve.offset + n;
+      const int xr = a.pair_tok ? __ldg(a.pair_tok + p) : p;
+      const float xsc = a.xe ? pow2f(__ldg(a.xe + xr)) : 1.0f;
+      float val[NMAT];
+#pragma unroll
+      for (int mi = 0; mi < NMAT; ++mi) {
+        float s = TE::total(red, mi, rl, n);
+        if (FMT == FFN_B200_FMT_NVFP4) {
+          s = s * xsc * mi_[mi].gs;
+        } else {
+          s = (s * 0.5f) * xsc * __ldg(mi_[mi].rs + row);
+          if (mi_[mi].core_b)
+            s += core_term(mi_[mi].core_b, row, a.z + ((size_t)p * 3 + midx[mi]) * 16);
+        }
+        val[mi] = s;
+      }
+      if (PHASE == 1) {
+        float gv = val[0], uv = val[NMAT - 1];
+        if (FMT == FFN_B200_FMT_TERNARY) { gv *= proj; uv *= proj; }
+        const float h = silu_clamped(gv) * clamp10(uv);
+        __half hi, lo;
+        split_f16(h, hi, lo);
+        const int col = FMT == FFN_B200_FMT_NVFP4 ? row : tern_pos(row);
+        a.hh[(size_t)p * a.ld_h + col] = hi;
+        a.hl[(size_t)p * a.ld_h + col] = lo;
+      } else {
+        float *dst = a.y + (size_t)p * a.ld_y + row;
+        if (a.vexp || PHASE == 0) {
+          *dst = val[0];
+        } else {
+          const float wy = a.out_w * val[0];  // flash1017.rs:4900-4905 (dst += scale * src)
+          *dst = a.accumulate ? *dst + wy : wy;
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+template <int FMT, int PHASE, int R>
+static int launch_phase_t(const PhaseArgs &a, int grid, cudaStream_t st) {
+  phase_kernel<FMT, PHASE, R><<<grid, kThreads, 0, st>>>(a);
+  FFN_LAUNCH_CHECK("phase_kernel");
+  return 0;
+}
+
+// Rows per CTA tile.  Gate/up tiles carry two matrices, so R=2 (32 rows);
+// single-matrix tiles use R=4 (64 rows) to keep the per-tile work balanced.
+constexpr int kRGateUp = 2;
+constexpr int kRSingle = 4;
+
+int rows_per_tile(int phase) { return 16 * (phase == 1 ? kRGateUp : kRSingle); }
+
+int launch_phase(int fmt, int phase, const PhaseArgs &a, int grid, cudaStream_t st) {
+  if (fmt == FFN_B200_FMT_NVFP4) {
+    if (phase == 1) return launch_phase_t<FFN_B200_FMT_NVFP4, 1, kRGateUp>(a, grid, st);
+    if (phase == 2) return launch_phase_t<FFN_B200_FMT_NVFP4, 2, kRSingle>(a, grid, st);
+    return launch_phase_t<FFN_B200_FMT_NVFP4, 0, kRSingle>(a, grid, st);
+  }
+  if (phase == 1) return launch_phase_t<FFN_B200_FMT_TERNARY, 1, kRGateUp>(a, grid, st);
+  if (phase == 2) return launch_phase_t<FFN_B200_FMT_TERNARY, 2, kRSingle>(a, grid, st);
+  return launch_phase_t<FFN_B200_FMT_TERNARY, 0, kRSingle>(a, grid, st);
+}
+
+// ============================================================ rank-16 core z
+// z[pair][mat][r] = (sum_c A[r][c] * x[c]) * a_sc[r] * b_sc[r]   (flash1017.rs:2452-2463)
+// One CTA per (slice, matrix): 256 threads = 16 core rows x 16 column lanes.
+__global__ void __launch_bounds__(256) corez_kernel(const CoreZArgs a) {
+  const int n_vexp = a.vexp ? *a.n_vexp_dev : (a.n_tok_direct + kNTok - 1) / kNTok;
+  const int item = blockIdx.x;
+  const int v = item / a.nmat, mm = a.mat0 + item % a.nmat;
+  if (v >= n_vexp) return;
+  VExp ve;
+  if (a.vexp) ve = a.vexp[v];
+  else { ve.expert = -1; ve.offset = v * kNTok; ve.count = min(kNTok, a.n_tok_direct - v * kNTok); }
+  int fmt;
+  const int8_t *A;
+  const float *asc, *bsc;
+  if (ve.expert >= 0) {
+    const ffn_b200_expert &E = a.experts[ve.expert];
+    fmt = E.format; A = E.tn[mm].core_a; asc = E.tn[mm].core_a_sc; bsc = E.tn[mm].core_b_sc;
+  } else {
+    fmt = a.direct.format; A = a.direct.tn[mm].core_a;
+    asc = a.direct.tn[mm].core_a_sc; bsc = a.direct.tn[mm].core_b_sc;
+  }
+  if (fmt != FFN_B200_FMT_TERNARY || A == nullptr) return;  // uniform per CTA
+  const int r = threadIdx.x >> 4, l = threadIdx.x & 15;
+  __shared__ float part[kNTok][16][17];
+  for (int n = 0; n < ve.count; ++n) {
+    const int p = ve.offset + n;
+    float acc = 0.f;
+    if (a.xf) {
+      const int xr = a.pair_tok ? a.pair_tok[p] : p;
+      const float *x = a.xf + (size_t)xr * a.ld_xf;
+      for (int c = l; c < a.K; c += 16) acc += (float)A[(size_t)r * a.K + c] * x[c];
+    } else {
+      const __half *xh = a.hh + (size_t)p * a.ld_h, *xl = a.hl + (size_t)p * a.ld_h;
+      for (int c = l; c < a.K; c += 16) {
+        const int q = tern_pos(c);
+        acc += (float)A[(size_t)r * a.K + c] * (__half2float(xh[q]) + __half2float(xl[q]));
+      }
+    }
+    part[n][r][l] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x < 16 * kNTok) {
+    const int n = threadIdx.x >> 4, rr = threadIdx.x & 15;
+    if (n < ve.count) {
+      float s = 0.f;
+      for (int k = 0; k < 16; ++k) s += part[n][rr][k];
+      const int p = ve.offset + n;
+      a.z[((size_t)p * 3 + mm) * 16 + rr] = s * asc[rr] * bsc[rr];
+    }
+  }
+}
+
+int launch_corez(const CoreZArgs &a, int max_vexp, cudaStream_t st) {
+  if (max_vexp <= 0) return 0;
+  corez_kernel<<<max_vexp * a.nmat, 256, 0, st>>>(a);
+  FFN_LAUNCH_CHECK("corez_kernel");
+  return 0;
+}
+
+// ============================================================ router
+// EXACT: logits[t][e] = sum_c w[e][c] * x[t][c], summed sequentially in column
+// order with separate multiply and add (the CPU loop, flash1017.rs:2216-2222),
+// so the logits are bit-identical to the oracle's.  CTA = 32 experts x 8 tokens.
+__device__ __forceinline__ float wload(const float *w, size_t i) { return w[i]; }
+__device__ __forceinline__ float wload(const uint16_t *w, size_t i) {
+  return __uint_as_float((uint32_t)w[i] << 16);  // bf16 -> f32 (flash1017.rs:2220)
+}
+
+template <typename WT>
+__global__ void __launch_bounds__(256) router_exact_kernel(const WT *__restrict__ w,
+                                                           const float *__restrict__ x, int n_tok,
+                                                           int n_exp, int H,
+                                                           float *__restrict__ logits) {
+  __shared__ float ws[32][65];
+  __shared__ float xs[8][64];
+  const int el = threadIdx.x & 31, tl = threadIdx.x >> 5;
+  const int e0 = blockIdx.x * 32, t0 = blockIdx.y * 8;
+  float acc = 0.f;
+  for (int c0 = 0; c0 < H; c0 += 64) {
+    for (int i = threadIdx.x; i < 32 * 64; i += 256) {
+      const int er = i >> 6, cc = i & 63;
+      const int e = e0 + er, c = c0 + cc;
+      ws[er][cc] = (e < n_exp && c < H) ? wload(w, (size_t)e * H + c) : 0.f;
+    }
+    for (int i = threadIdx.x; i < 8 * 64; i += 256) {
+      const int tr = i >> 6, cc = i & 63;
+      const int t = t0 + tr, c = c0 + cc;
+      xs[tr][cc] = (t < n_tok && c < H) ? x[(size_t)t * H + c] : 0.f;
+    }
+    __syncthreads();
+    const int lim = min(64, H - c0);
+    for (int cc = 0; cc < lim; ++cc) acc = __fadd_rn(acc, __fmul_rn(ws[el][cc], xs[tl][cc]));
+    __syncthreads();
+  }
+  const int e = e0 + el, t = t0 + tl;
+  if (e < n_exp && t < n_tok) logits[(size_t)t * n_exp + e] = acc;
+}
+
+// logits [n_tok, rows] with the exact sequential sum over f32 or bf16 weights.
+int launch_exact_matvec(const float *w32, const uint16_t *w16, const float *x, int n_tok,
+                        int rows, int H, float *out, cudaStream_t st) {
+  if (n_tok <= 0 || rows <= 0) return 0;
+  dim3 g1((rows + 31) / 32, (n_tok + 7) / 8);
+  if (g1.y > 65535) return fail(FFN_B200_EINVAL, "exact matvec: too many tokens");
+  if (w32) router_exact_kernel<float><<<g1, 256, 0, st>>>(w32, x, n_tok, rows, H, out);
+  else router_exact_kernel<uint16_t><<<g1, 256, 0, st>>>(w16, x, n_tok, rows, H, out);
+  FFN_LAUNCH_CHECK("router_exact_kernel");
+  return 0;
+}
+
+// Top-k per token, one warp per token (flash1017.rs:7280-7376).  Ties in the
+// biased score are broken by the lower expert index.
+__device__ __forceinline__ float score_of(float l, int fn) {
+  if (fn == FFN_B200_SCORE_REF_SQRTSOFTPLUS) {
+    const float sp = l > 20.0f ? l : (l < -20.0f ? expf(l) : logf(1.0f + expf(l)));
+    return sqrtf(fmaxf(sp, 0.0f));
+  }
+  return 1.0f / (1.0f + expf(-l));
+}
+
+__global__ void __launch_bounds__(256) topk_kernel(const float *__restrict__ logits,
+                                                   const float *__restrict__ bias, int n_tok,
+                                                   int n_exp, int top_k, int score_fn,
+                                                   int32_t *idx, float *wt) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= n_tok) return;
+  const float *lg = logits + (size_t)warp * n_exp;
+  float sel_score[kTopKMax];
+  int sel_idx[kTopKMax];
+  float prev_b = INFINITY;
+  int prev_i = -1;
+  for (int k = 0; k < top_k; ++k) {
+    // best candidate strictly after (prev_b, prev_i) in (biased desc, index asc) order
+    float bb = -INFINITY, bs = 0.f;
+    int bi = 0x7fffffff;
+    for (int e = lane; e < n_exp; e += 32) {
+      const float s = score_of(lg[e], score_fn);
+      const float b = s + (bias ? bias[e] : 0.0f);
+      const bool after = b < prev_b || (b == prev_b && e > prev_i);
+      const bool better = b > bb || (b == bb && e < bi);
+      if (after && better) { bb = b; bs = s; bi = e; }
+    }
+    for (int o = 16; o; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, bb, o);
+      const float os = __shfl_xor_sync(0xffffffffu, bs, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > bb || (ob == bb && oi < bi)) { bb = ob; bs = os; bi = oi; }
+    }
+    sel_score[k] = bs;
+    sel_idx[k] = bi;
+    prev_b = bb;
+    prev_i = bi;
+  }
+  if (lane == 0) {
+    float sum = 0.f;
+    for (int k = 0; k < top_k; ++k) sum += sel_score[k];  // selection order, flash1017.rs:7370
+    const float num = score_fn == FFN_B200_SCORE_REF_SQRTSOFTPLUS ? 1.5f : 1.0f;
+    const float scale = sum > 1e-12f ? num / sum : 0.0f;
+    for (int k = 0; k < top_k; ++k) {
+      idx[(size_t)warp * top_k + k] = sel_idx[k];
+      wt[(size_t)warp * top_k + k] = sel_score[k] * scale;
+    }
+  }
+}
+
+int launch_router(const float *w, const float *bias, const float *x, int n_tok, int n_exp,
+                  int H, int top_k, int score_fn, float *logits, int32_t *idx, float *wt,
+                  cudaStream_t st) {
+  int rc = launch_exact_matvec(w, nullptr, x, n_tok, n_exp, H, logits, st);
+  if (rc) return rc;
+  topk_kernel<<<(n_tok + 7) / 8, 256, 0, st>>>(logits, bias, n_tok, n_exp, top_k, score_fn, idx,
+                                               wt);
+  FFN_LAUNCH_CHECK("topk_kernel");
+  return 0;
+}
+
+// ============================================================ grouping
+// Token->expert groups (flash1017.rs:8088-8099 builds the same groups by a
+// linear scan).  Single CTA: counts per local expert, exclusive scans, pair
+// placement, and slices of <= 8 tokens per expert, listed per weight format.
+__global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__ idx, int n_pairs,
+                                                     int top_k, int n_exp, int e_begin, int e_end,
+                                                     const ffn_b200_expert *__restrict__ experts,
+                                                     int *counts, int *offsets, int *cursor,
+                                                     int *vbase, int32_t *pair_tok, int32_t *inv,
+                                                     VExp *vexp_nv, VExp *vexp_tn, int *n_vexp) {
+  __shared__ int s_tot[2];
+  __shared__ int ws_p[32], ws_n[32], ws_t[32];
+  const int tid = threadIdx.x;
+  for (int e = tid; e < n_exp; e += blockDim.x) { counts[e] = 0; cursor[e] = 0; }
+  __syncthreads();
+  for (int q = tid; q < n_pairs; q += blockDim.x) {
+    const int e = idx[q];
+    if (e >= e_begin && e < e_end) atomicAdd(&counts[e], 1);
+  }
+  __syncthreads();
+  // each thread owns a contiguous run of `per` experts
+  const int per = (n_exp + blockDim.x - 1) / blockDim.x;
+  int loc_pairs = 0, loc_nv = 0, loc_tn = 0;
+  for (int i = 0; i < per; ++i) {
+    const int e = tid * per + i;
+    if (e < n_exp) {
+      const int c = counts[e], s = (c + kNTok - 1) / kNTok;
+      loc_pairs += c;
+      if (experts[e].format == FFN_B200_FMT_NVFP4) loc_nv += s; else loc_tn += s;
+    }
+  }
+  // block-wide exclusive scans of the three per-thread totals
+  int inc_p = loc_pairs, inc_n = loc_nv, inc_t = loc_tn;
+  const int lane = tid & 31, wid = tid >> 5;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int a = __shfl_up_sync(0xffffffffu, inc_p, o);
+    const int b = __shfl_up_sync(0xffffffffu, inc_n, o);
+    const int c = __shfl_up_sync(0xffffffffu, inc_t, o);
+    if (lane >= o) { inc_p += a; inc_n += b; inc_t += c; }
+  }
+  if (lane == 31) { ws_p[wid] = inc_p; ws_n[wid] = inc_n; ws_t[wid] = inc_t; }
+  __syncthreads();
+  if (wid == 0) {
+    const int nw = blockDim.x >> 5;
+    int a = lane < nw ? ws_p[lane] : 0;
+    int b = lane < nw ? ws_n[lane] : 0;
+    int c = lane < nw ? ws_t[lane] : 0;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int x1 = __shfl_up_sync(0xffffffffu, a, o);
+      const int x2 = __shfl_up_sync(0xffffffffu, b, o);
+      const int x3 = __shfl_up_sync(0xffffffffu, c, o);
+      if (lane >= o) { a += x1; b += x2; c += x3; }
+    }
+    ws_p[lane] = a; ws_n[lane] = b; ws_t[lane] = c;
+    if (lane == 31) { s_tot[0] = b; s_tot[1] = c; }
+  }
+  __syncthreads();
+  int base_p = (wid ? ws_p[wid - 1] : 0) + inc_p - loc_pairs;
+  int base_n = (wid ? ws_n[wid - 1] : 0) + inc_n - loc_nv;
+  int base_t = (wid ? ws_t[wid - 1] : 0) + inc_t - loc_tn;
+  for (int i = 0; i < per; ++i) {
+    const int e = tid * per + i;
+    if (e < n_exp) {
+      const int c = counts[e], s = (c + kNTok - 1) / kNTok;
+      offsets[e] = base_p;
+      base_p += c;
+      if (experts[e].format == FFN_B200_FMT_NVFP4) { vbase[e] = base_n; base_n += s; }
+      else { vbase[e] = base_t; base_t += s; }
+    }
+  }
+  __syncthreads();
+  // Pair placement.  The order of tokens inside an expert group does not change
+  // any result: each MMA output column depends only on its own token.
+  for (int q = tid; q < n_pairs; q += blockDim.x) {
+    const int e = idx[q];
+    if (e >= e_begin && e < e_end) {
+      const int pos = offsets[e] + atomicAdd(&cursor[e], 1);
+      pair_tok[pos] = q / top_k;
+      inv[q] = pos;
+    } else {
+      inv[q] = -1;
+    }
+  }
+  __syncthreads();
+  for (int e = tid; e < n_exp; e += blockDim.x) {
+    const int c = counts[e];
+    VExp *dst = experts[e].format == FFN_B200_FMT_NVFP4 ? vexp_nv : vexp_tn;
+    for (int j = 0; j * kNTok < c; ++j) {
+      VExp v;
+      v.expert = e;
+      v.offset = offsets[e] + j * kNTok;
+      v.count = min(kNTok, c - j * kNTok);
+      v.pad = 0;
+      dst[vbase[e] + j] = v;
+    }
+  }
+  if (tid == 0) { n_vexp[0] = s_tot[0]; n_vexp[1] = s_tot[1]; }
+}
+
+int launch_group(const int32_t *idx, int n_tok, int top_k, int n_exp, int e_begin, int e_end,
+                 const ffn_b200_expert *experts, int *ws_int, int32_t *pair_tok, int32_t *inv,
+                 VExp *vexp_nv, VExp *vexp_tn, int *n_vexp, cudaStream_t st) {
+  group_kernel<<<1, 1024, 0, st>>>(idx, n_tok * top_k, top_k, n_exp, e_begin, e_end, experts,
+                                   ws_int, ws_int + n_exp, ws_int + 2 * n_exp,
+                                   ws_int + 3 * n_exp, pair_tok, inv, vexp_nv, vexp_tn, n_vexp);
+  FFN_LAUNCH_CHECK("group_kernel");
+  return 0;
+}
+
+// ============================================================ combine
+// out[t] = residual[t] + sum_k w[t][k] * y[pair(t,k)], the terms added in
+// selection order starting from zero with separate multiply and add, as
+// flash1017_axpy_f32 does (flash1017.rs:4900-4905, 7546-7547).  Ternary
+// experts weigh by w * proj_scale (flash1017.rs:7561).
+__global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ y, int ld_y,
+                                                      const int32_t *__restrict__ idx,
+                                                      const float *__restrict__ wt,
+                                                      const int32_t *__restrict__ inv, int top_k,
+                                                      const ffn_b200_expert *__restrict__ experts,
+                                                      const float *residual, float *out, int H) {
+  const int t = blockIdx.x;
+  __shared__ float wk[kTopKMax];
+  __shared__ int pk[kTopKMax];
+  if (threadIdx.x < top_k) {
+    const int q = t * top_k + threadIdx.x;
+    const int e = idx[q];
+    float w = wt[q];
+    if (experts[e].format == FFN_B200_FMT_TERNARY) w = w * experts[e].proj_scale;
+    wk[threadIdx.x] = w;
+    pk[threadIdx.x] = inv[q];
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < H; c += blockDim.x) {
+    float acc = 0.f;
+    for (int k = 0; k < top_k; ++k) {
+      const int p = pk[k];
+      if (p >= 0) acc = __fadd_rn(acc, __fmul_rn(wk[k], __ldg(y + (size_t)p * ld_y + c)));
+    }
+    if (residual) acc = __fadd_rn(residual[(size_t)t * H + c], acc);
+    out[(size_t)t * H + c] = acc;
+  }
+}
+
+int launch_combine(const float *y, int ld_y, const int32_t *idx, const float *wt,
+                   const int32_t *inv, int n_tok, int top_k, const ffn_b200_expert *experts,
+                   const float *residual, float *out, int H, cudaStream_t st) {
+  if (n_tok <= 0) return 0;
+  combine_kernel<<<n_tok, 256, 0, st>>>(y, ld_y, idx, wt, inv, top_k, experts, residual, out, H);
+  FFN_LAUNCH_CHECK("combine_kernel");
+  return 0;
+}
+
+// ============================================================ reference-ABI helpers
+// out[dst[k]] += w[k] * y[k] for k < m, in k order (flash1017.rs:8297-8303).
+__global__ void scatter_axpy_kernel(const float *__restrict__ y, const int64_t *__restrict__ dst,
+                                    const float *__restrict__ w, int m, int H, float *out) {
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < H; c += gridDim.x * blockDim.x)
+    for (int k = 0; k < m; ++k) {
+      float *o = out + (size_t)dst[k] * H + c;
+      *o = __fadd_rn(*o, __fmul_rn(w[k], y[(size_t)k * H + c]));
+    }
+}
+int launch_scatter_axpy(const float *y, const int64_t *dst, const float *w, int m, int H,
+                        float *out, cudaStream_t st) {
+  if (m <= 0) return 0;
+  scatter_axpy_kernel<<<(H + 255) / 256, 256, 0, st>>>(y, dst, w, m, H, out);
+  FFN_LAUNCH_CHECK("scatter_axpy_kernel");
+  return 0;
+}
+
+// Single-row dots of the V1 vtable slots (HA:150-159).  mode 0: f32 . f32,
+// 1: i8 . f32, 2: Q4_G32 (int4 - 8, bf16 scale per 32; twin HA:1159-1179),
+// 3: ternary 2-bit codes (no scale).  One CTA, fixed-order tree reduction.
+__global__ void __launch_bounds__(256) dot_kernel(int mode, const void *a, const void *aux,
+                                                  const float *x, size_t len, float *out) {
+  float acc = 0.f;
+  if (mode == 0) {
+    const float *v = (const float *)a;
+    for (size_t i = threadIdx.x; i < len; i += 256) acc += v[i] * x[i];
+  } else if (mode == 1) {
+    const int8_t *v = (const int8_t *)a;
+    for (size_t i = threadIdx.x; i < len; i += 256) acc += (float)v[i] * x[i];
+  } else if (mode == 2) {
+    const uint8_t *nib = (const uint8_t *)a;
+    const uint16_t *sc = (const uint16_t *)aux;
+    for (size_t g = threadIdx.x; g < len / 32; g += 256) {
+      float gs = 0.f;
+      for (int k = 0; k < 16; ++k) {
+        const uint32_t b = nib[g * 16 + k];
+        gs += (float)((int)(b & 15u) - 8) * x[g * 32 + 2 * k] +
+              (float)((int)(b >> 4) - 8) * x[g * 32 + 2 * k + 1];
+      }
+      acc += gs * __uint_as_float((uint32_t)sc[g] << 16);
+    }
+  } else {
+    const uint8_t *p = (const uint8_t *)a;
+    for (size_t i = threadIdx.x; i < len / 4; i += 256) {
+      const uint32_t b = p[i];
+      for (int j = 0; j < 4; ++j) acc += tern_to_f32((b >> (2 * j)) & 3u) * x[4 * i + j];
+    }
+  }
+  __shared__ float red[256];
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int o = 128; o; o >>= 1) {
+    if ((int)threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *out = red[0];
+}
+int launch_dot(int mode, const void *a, const void *aux, const float *x, size_t len, float *out,
+               cudaStream_t st) {
+  dot_kernel<<<1, 256, 0, st>>>(mode, a, aux, x, len, out);
+  FFN_LAUNCH_CHECK("dot_kernel");
+  return 0;
+}
+
+// ============================================================ generators
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+__device__ __forceinline__ uint64_t rnd(uint64_t key, uint64_t i) {
+  return mix64(key + 0x9E3779B97F4A7C15ULL * (i + 1));
+}
+__device__ __forceinline__ float normal_at(uint64_t key, uint64_t i) {
+  long long s = 0;
+  for (int d = 0; d < 3; ++d) {
+    const uint64_t r = rnd(key, 3 * i + d);
+    s += (long long)(r & 0xFFFF) + (long long)((r >> 16) & 0xFFFF) +
+         (long long)((r >> 32) & 0xFFFF) + (long long)(r >> 48);
+  }
+  return __fmul_rn((float)(s - 393210), 1.0f / 65536.0f);
+}
+__device__ __forceinline__ float unit_at(uint64_t key, uint64_t i) {
+  return __fmul_rn((float)(uint32_t)(rnd(key, i) >> 40), 1.0f / 16777216.0f);
+}
+// f32 -> E4M3, round to nearest even, saturating at 448 (integer arithmetic).
+__device__ __forceinline__ uint8_t f32_to_e4m3(float f) {
+  const uint32_t u = __float_as_uint(f);
+  const uint32_t sign = (u >> 24) & 0x80u, a = u & 0x7FFFFFFFu;
+  if (a > 0x7F800000u) return (uint8_t)(sign | 0x7Fu);
+  if (a >= 0x43E00000u) return (uint8_t)(sign | 0x7Eu);
+  const int e = (int)(a >> 23) - 127;
+  if (e < -6) {
+    if (e < -40 || (a >> 23) == 0) return (uint8_t)sign;  // rounds to zero
+    const uint32_t M = (a & 0x7FFFFFu) | 0x800000u;     // value = M * 2^(e-23)
+    const int sh = 14 - e;                               // value*2^9 = M >> sh
+    const uint32_t q = M >> sh, rem = M & ((1u << sh) - 1u), half = 1u << (sh - 1);
+    const uint32_t r = q + ((rem > half || (rem == half && (q & 1u))) ? 1u : 0u);
+    return (uint8_t)(sign | r);
+  }
+  const uint32_t mant = a & 0x7FFFFFu, keep = mant >> 20, rest = mant & 0xFFFFFu;
+  uint32_t enc = ((uint32_t)(e + 7) << 3) | keep;
+  if (rest > 0x80000u || (rest == 0x80000u && (keep & 1u))) enc++;
+  if (enc > 0x7Eu) enc = 0x7Eu;
+  return (uint8_t)(sign | enc);
+}
+
+__global__ void gen_nvfp4_kernel(uint64_t kw, uint64_t ks, size_t nb, size_t ns, uint8_t *w,
+                                 uint8_t *s) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nb; i += stride)
+    w[i] = (uint8_t)(rnd(kw, i) & 0xFF);
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < ns; i += stride)
+    s[i] = f32_to_e4m3(__fdiv_rn(fabsf(normal_at(ks, i)), 6.0f));
+}
+
+__global__ void gen_ternary_kernel(uint64_t kp, uint64_t kr, size_t nbytes, size_t rows,
+                                   uint8_t *p, float *rs) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x; b < nbytes; b += stride) {
+    uint32_t byte = 0;
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t u = (uint32_t)(rnd(kp, 4 * b + i) >> 32);
+      const uint32_t code = u < 1288490189u ? 0u : (u < 3006477107u ? 1u : 2u);
+      byte |= code << (2 * i);
+    }
+    p[b] = (uint8_t)byte;
+  }
+  for (size_t r = (size_t)blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += stride)
+    rs[r] = __fadd_rn(0.01f, __fmul_rn(0.04f, unit_at(kr, r)));
+}
+
+__global__ void gen_core_kernel(uint64_t ka, uint64_t kb, uint64_t kas, uint64_t kbs, size_t na,
+                                size_t nb, int8_t *a, float *a_sc, int8_t *b, float *b_sc) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  const size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (size_t i = i0; i < na; i += stride) a[i] = (int8_t)((int)(rnd(ka, i) % 255u) - 127);
+  for (size_t i = i0; i < nb; i += stride) b[i] = (int8_t)((int)(rnd(kb, i) % 255u) - 127);
+  if (i0 < 16) {
+    a_sc[i0] = __fadd_rn(0.0001f, __fmul_rn(0.0009f, unit_at(kas, i0)));
+    b_sc[i0] = __fadd_rn(0.0001f, __fmul_rn(0.0009f, unit_at(kbs, i0)));
+  }
+}
+
+__global__ void gen_normal_kernel(uint64_t key, size_t n, float stdev, float *out) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    out[i] = __fmul_rn(normal_at(key, i), stdev);
+}
+
+static int gen_grid(size_t n) {
+  const size_t b = (n + 255) / 256;
+  return (int)std::max<size_t>(1, std::min<size_t>(b, 148 * 16));
+}
+
+int launch_gen_nvfp4(uint64_t kw, uint64_t ks, size_t rows, size_t cols, uint8_t *w, uint8_t *s,
+                     cudaStream_t st) {
+  const size_t nb = rows * cols / 2, ns = rows * cols / 16;
+  gen_nvfp4_kernel<<<gen_grid(nb), 256, 0, st>>>(kw, ks, nb, ns, w, s);
+  FFN_LAUNCH_CHECK("gen_nvfp4_kernel");
+  return 0;
+}
+int launch_gen_ternary(uint64_t kp, uint64_t kr, size_t rows, size_t cols, uint8_t *p, float *rs,
+                       cudaStream_t st) {
+  const size_t nb = rows * cols / 4;
+  gen_ternary_kernel<<<gen_grid(nb), 256, 0, st>>>(kp, kr, nb, rows, p, rs);
+  FFN_LAUNCH_CHECK("gen_ternary_kernel");
+  return 0;
+}
+int launch_gen_core(uint64_t ka, uint64_t kb, uint64_t kas, uint64_t kbs, size_t rows,
+                    size_t cols, int8_t *a, float *a_sc, int8_t *b, float *b_sc,
+                    cudaStream_t st) {
+  const size_t na = 16 * cols, nb = rows * 16;
+  gen_core_kernel<<<gen_grid(std::max(na, nb)), 256, 0, st>>>(ka, kb, kas, kbs, na, nb, a, a_sc,
+                                                              b, b_sc);
+  FFN_LAUNCH_CHECK("gen_core_kernel");
+  return 0;
+}
+int launch_gen_normal(uint64_t key, size_t n, float stdev, float *out, cudaStream_t st) {
+  gen_normal_kernel<<<gen_grid(n), 256, 0, st>>>(key, n, stdev, out);
+  FFN_LAUNCH_CHECK("gen_normal_kernel");
+  return 0;
+}
+
+// ============================================================ decode checks
+__global__ void dequant_nvfp4_kernel(size_t rows, size_t cols, const uint8_t *w, const uint8_t *s,
+                                     float *out) {
+  const size_t n = rows * cols, stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const size_t r = i / cols, c = i % cols;
+    const uint32_t b = w[r * (cols / 2) + c / 2];
+    const float v = e2m1_to_f32((c & 1) ? (b >> 4) : (b & 15u));
+    out[i] = v * e4m3_to_f32(s[r * (cols / 16) + c / 16]);
+  }
+}
+__global__ void dequant_ternary_kernel(size_t rows, size_t cols, const uint8_t *p, float *out) {
+  const size_t n = rows * cols, stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const size_t r = i / cols, c = i % cols;
+    const uint32_t b = p[r * (cols / 4) + c / 4];
+    out[i] = tern_to_f32((b >> (2 * (c & 3))) & 3u);
+  }
+}
+int launch_dequant_nvfp4(size_t rows, size_t cols, const uint8_t *w, const uint8_t *s, float *out,
+                         cudaStream_t st) {
+  dequant_nvfp4_kernel<<<gen_grid(rows * cols), 256, 0, st>>>(rows, cols, w, s, out);
+  FFN_LAUNCH_CHECK("dequant_nvfp4_kernel");
+  return 0;
+}
+int launch_dequant_ternary(size_t rows, size_t cols, const uint8_t *p, float *out,
+                           cudaStream_t st) {
+  dequant_ternary_kernel<<<gen_grid(rows * cols), 256, 0, st>>>(rows, cols, p, out);
+  FFN_LAUNCH_CHECK("dequant_ternary_kernel");
+  return 0;
+}
+
+}  // namespace ffn

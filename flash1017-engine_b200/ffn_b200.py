@@ -1,0 +1,387 @@
+"""ctypes binding of libffn_b200.so for Python callers (tests, bench, smoke).
+
+The library's C-ABI (include/ffn_b200.h, include/merkaba_hw_addon.h) is the
+product; this module only marshals torch CUDA tensors into it.  PyTorch here
+is plumbing: device memory, streams and torch.distributed.  There is no Python
+or CPU compute path: every function below runs a CUDA kernel of the library,
+and using it without the built library raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "libffn_b200.so")
+
+FMT_NVFP4, FMT_TERNARY = 0, 1
+SCORE_REF, SCORE_SIGMOID = 0, 1
+ROUTER_EXACT, ROUTER_TENSOR = 0, 1
+ERRORS = {0: "OK", -1: "EINVAL", -2: "ECUDA", -3: "ENOSPC", -4: "ENCCL", -5: "EUNSUP"}
+
+# Symbols the public headers declare (checked by the CPU test suite).
+EXPORTS = [
+    "merkaba_hardware_addon_v1",
+    "gx10_rust_nvfp4_mlp_accum", "gx10_rust_ternary_158_mlp_accum",
+    "gx10_rust_nvfp4_mlp_batch", "gx10_rust_ternary_158_mlp_batch",
+    "gx10_rust_register_shard_bounds", "gx10_rust_register_host_range",
+    "ffn_b200_version", "ffn_b200_last_error", "ffn_b200_launch_count", "ffn_b200_set_device",
+    "ffn_b200_matvec_ws_bytes", "ffn_b200_nvfp4_matvec", "ffn_b200_ternary_matvec",
+    "ffn_b200_expert_ws_bytes", "ffn_b200_expert_forward",
+    "ffn_b200_moe_ws_bytes", "ffn_b200_moe_layer",
+    "ffn_b200_key", "ffn_b200_gen_nvfp4", "ffn_b200_gen_ternary", "ffn_b200_gen_core",
+    "ffn_b200_gen_normal", "ffn_b200_dequant_nvfp4", "ffn_b200_dequant_ternary",
+    "ffn_b200_set_batch_input", "ffn_b200_release_host_ranges", "ffn_b200_host_cache_bytes",
+]
+
+
+def build() -> str:
+    subprocess.run(["make", "-s", "-C", HERE, "-j8"], check=True)
+    return LIB_PATH
+
+
+class FfnError(RuntimeError):
+    pass
+
+
+# ------------------------------------------------------------ C structs
+class NvMat(C.Structure):
+    _fields_ = [("w", C.c_void_p), ("s", C.c_void_p), ("gs", C.c_float),
+                ("reserved", C.c_uint32)]
+
+
+class TnMat(C.Structure):
+    _fields_ = [("p", C.c_void_p), ("rs", C.c_void_p), ("core_a", C.c_void_p),
+                ("core_a_sc", C.c_void_p), ("core_b", C.c_void_p), ("core_b_sc", C.c_void_p)]
+
+
+class Expert(C.Structure):
+    _fields_ = [("format", C.c_int32), ("proj_scale", C.c_float), ("nv", NvMat * 3),
+                ("tn", TnMat * 3)]
+
+
+class MoeDesc(C.Structure):
+    _fields_ = [("hidden", C.c_size_t), ("inter", C.c_size_t), ("n_experts", C.c_size_t),
+                ("top_k", C.c_size_t), ("experts", C.c_void_p), ("router_w", C.c_void_p),
+                ("router_bias", C.c_void_p), ("score_fn", C.c_int32),
+                ("router_mode", C.c_int32), ("expert_begin", C.c_int32),
+                ("expert_end", C.c_int32), ("has_nvfp4", C.c_int32),
+                ("has_ternary", C.c_int32)]
+
+
+assert C.sizeof(Expert) == 224, C.sizeof(Expert)
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """The loaded library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FfnError(f"{LIB_PATH} is missing: build it with `make -C {HERE}` "
+                           "(or __graft_entry__.build())")
+        L = C.CDLL(LIB_PATH)
+        sz, vp, f32, i32, u64 = C.c_size_t, C.c_void_p, C.c_float, C.c_int, C.c_uint64
+        L.ffn_b200_version.restype = C.c_char_p
+        L.ffn_b200_last_error.restype = C.c_char_p
+        L.ffn_b200_launch_count.restype = u64
+        L.ffn_b200_set_device.argtypes = [i32]
+        L.ffn_b200_matvec_ws_bytes.restype = sz
+        L.ffn_b200_matvec_ws_bytes.argtypes = [sz, sz]
+        L.ffn_b200_nvfp4_matvec.argtypes = [sz, sz, sz, C.POINTER(NvMat), vp, vp, vp, sz, vp]
+        L.ffn_b200_ternary_matvec.argtypes = [sz, sz, sz, C.POINTER(TnMat), vp, vp, vp, sz, vp]
+        L.ffn_b200_expert_ws_bytes.restype = sz
+        L.ffn_b200_expert_ws_bytes.argtypes = [sz, sz, sz]
+        L.ffn_b200_expert_forward.argtypes = [sz, sz, sz, C.POINTER(Expert), vp, vp, f32, i32,
+                                              vp, sz, vp]
+        L.ffn_b200_moe_ws_bytes.restype = sz
+        L.ffn_b200_moe_ws_bytes.argtypes = [C.POINTER(MoeDesc), sz]
+        L.ffn_b200_moe_layer.argtypes = [C.POINTER(MoeDesc), sz, vp, vp, vp, vp, vp, vp, sz, vp]
+        L.ffn_b200_key.restype = u64
+        L.ffn_b200_key.argtypes = [u64, u64]
+        L.ffn_b200_gen_nvfp4.argtypes = [u64, sz, sz, vp, vp, vp]
+        L.ffn_b200_gen_ternary.argtypes = [u64, sz, sz, vp, vp, vp]
+        L.ffn_b200_gen_core.argtypes = [u64, sz, sz, vp, vp, vp, vp, vp]
+        L.ffn_b200_gen_normal.argtypes = [u64, sz, f32, vp, vp]
+        L.ffn_b200_dequant_nvfp4.argtypes = [sz, sz, vp, vp, vp, vp]
+        L.ffn_b200_dequant_ternary.argtypes = [sz, sz, vp, vp, vp]
+        L.ffn_b200_set_batch_input.argtypes = [vp, sz, sz]
+        L.ffn_b200_host_cache_bytes.restype = sz
+        L.merkaba_hardware_addon_v1.restype = vp
+        _lib = L
+    return _lib
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != 0:
+        msg = lib().ffn_b200_last_error().decode(errors="replace")
+        raise FfnError(f"{what}: {ERRORS.get(rc, rc)}: {msg}")
+
+
+def launch_count() -> int:
+    return int(lib().ffn_b200_launch_count())
+
+
+def key(parent: int, v: int) -> int:
+    return int(lib().ffn_b200_key(parent & (2**64 - 1), v))
+
+
+def path_key(*path: int) -> int:
+    """Same key path as the oracle's generator: derive(derive(ROOT, a), b)..."""
+    k = 0x464C415348313031
+    for v in path:
+        k = key(k, int(v))
+    return k
+
+
+# ----------------------------------------------------------- torch glue
+def _torch():
+    import torch
+    return torch
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream=None):
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+class Workspace:
+    """Grow-only device scratch buffer handed to the library's ws arguments."""
+
+    def __init__(self, device=None):
+        self.buf = None
+        self.device = device
+
+    def get(self, nbytes: int):
+        torch = _torch()
+        if self.buf is None or self.buf.numel() < nbytes:
+            self.buf = None
+            self.buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8,
+                                   device=self.device or "cuda")
+        return self.buf
+
+
+_ws = {}
+
+
+def _default_ws(device) -> Workspace:
+    d = str(device)
+    if d not in _ws:
+        _ws[d] = Workspace(device)
+    return _ws[d]
+
+
+# ----------------------------------------------------------- matrices
+class Nvfp4Matrix:
+    """NVFP4 matrix on the device: w [rows, cols/2] u8, s [rows, cols/16] u8, gs."""
+
+    def __init__(self, w, s, gs: float, rows: int, cols: int):
+        self.w, self.s, self.gs, self.rows, self.cols = w, s, float(gs), rows, cols
+
+    def cstruct(self) -> NvMat:
+        return NvMat(_ptr(self.w), _ptr(self.s), self.gs, 0)
+
+    @classmethod
+    def generate(cls, k: int, rows: int, cols: int, gs: float = 1.0, device="cuda", stream=None):
+        torch = _torch()
+        w = torch.empty(rows * cols // 2, dtype=torch.uint8, device=device)
+        s = torch.empty(rows * cols // 16, dtype=torch.uint8, device=device)
+        check(lib().ffn_b200_gen_nvfp4(k, rows, cols, _ptr(w), _ptr(s), _stream(stream)),
+              "gen_nvfp4")
+        return cls(w, s, gs, rows, cols)
+
+    def matvec(self, x, out=None, stream=None):
+        """out [seq, rows] = x [seq, cols] W^T (x float32 CUDA)."""
+        torch = _torch()
+        x = x.contiguous()
+        seq = x.numel() // self.cols
+        if out is None:
+            out = torch.empty(seq, self.rows, dtype=torch.float32, device=x.device)
+        ws = _default_ws(x.device).get(lib().ffn_b200_matvec_ws_bytes(seq, self.cols))
+        m = self.cstruct()
+        check(lib().ffn_b200_nvfp4_matvec(self.rows, self.cols, seq, C.byref(m), _ptr(x),
+                                          _ptr(out), _ptr(ws), ws.numel(), _stream(stream)),
+              "nvfp4_matvec")
+        return out
+
+    def dequant(self, stream=None):
+        torch = _torch()
+        out = torch.empty(self.rows, self.cols, dtype=torch.float32, device=self.w.device)
+        check(lib().ffn_b200_dequant_nvfp4(self.rows, self.cols, _ptr(self.w), _ptr(self.s),
+                                           _ptr(out), _stream(stream)), "dequant_nvfp4")
+        return out
+
+    def nbytes(self) -> int:
+        return self.w.numel() + self.s.numel()
+
+
+class TernaryMatrix:
+    """Packed ternary matrix p [rows, cols/4] u8 + rs [rows] f32 (+ optional
+    rank-16 core a [16, cols] i8, a_sc [16], b [rows, 16] i8, b_sc [16])."""
+
+    def __init__(self, p, rs, rows, cols, core=None):
+        self.p, self.rs, self.rows, self.cols, self.core = p, rs, rows, cols, core
+
+    def cstruct(self) -> TnMat:
+        c = self.core
+        return TnMat(_ptr(self.p), _ptr(self.rs), _ptr(c[0]) if c else None,
+                     _ptr(c[1]) if c else None, _ptr(c[2]) if c else None,
+                     _ptr(c[3]) if c else None)
+
+    @classmethod
+    def generate(cls, k: int, rows: int, cols: int, with_core: bool = True, device="cuda",
+                 stream=None):
+        torch = _torch()
+        p = torch.empty(rows * cols // 4, dtype=torch.uint8, device=device)
+        rs = torch.empty(rows, dtype=torch.float32, device=device)
+        check(lib().ffn_b200_gen_ternary(k, rows, cols, _ptr(p), _ptr(rs), _stream(stream)),
+              "gen_ternary")
+        core = None
+        if with_core:
+            a = torch.empty(16 * cols, dtype=torch.int8, device=device)
+            a_sc = torch.empty(16, dtype=torch.float32, device=device)
+            b = torch.empty(rows * 16, dtype=torch.int8, device=device)
+            b_sc = torch.empty(16, dtype=torch.float32, device=device)
+            check(lib().ffn_b200_gen_core(k, rows, cols, _ptr(a), _ptr(a_sc), _ptr(b), _ptr(b_sc),
+                                          _stream(stream)), "gen_core")
+            core = (a, a_sc, b, b_sc)
+        return cls(p, rs, rows, cols, core)
+
+    def matvec(self, x, out=None, stream=None):
+        torch = _torch()
+        x = x.contiguous()
+        seq = x.numel() // self.cols
+        if out is None:
+            out = torch.empty(seq, self.rows, dtype=torch.float32, device=x.device)
+        ws = _default_ws(x.device).get(lib().ffn_b200_matvec_ws_bytes(seq, self.cols))
+        m = self.cstruct()
+        check(lib().ffn_b200_ternary_matvec(self.rows, self.cols, seq, C.byref(m), _ptr(x),
+                                            _ptr(out), _ptr(ws), ws.numel(), _stream(stream)),
+              "ternary_matvec")
+        return out
+
+    def dequant(self, stream=None):
+        torch = _torch()
+        out = torch.empty(self.rows, self.cols, dtype=torch.float32, device=self.p.device)
+        check(lib().ffn_b200_dequant_ternary(self.rows, self.cols, _ptr(self.p), _ptr(out),
+                                             _stream(stream)), "dequant_ternary")
+        return out
+
+    def nbytes(self) -> int:
+        n = self.p.numel() + 4 * self.rs.numel()
+        if self.core:
+            n += self.core[0].numel() + self.core[2].numel() + 128
+        return n
+
+
+# Tensor tags of the generator key paths (same values as the oracle's).
+TAG_W1, TAG_W3, TAG_W2, TAG_ROUTER, TAG_X, TAG_BIAS = 1, 3, 2, 10, 11, 12
+
+
+class SwigluExpert:
+    """gate (w1), up (w3), down (w2) of one SwiGLU expert on the device."""
+
+    def __init__(self, fmt, mats, inter, hidden, proj_scale=1.0):
+        self.fmt, self.mats, self.inter, self.hidden = fmt, mats, inter, hidden
+        self.proj_scale = float(proj_scale)
+
+    def cstruct(self) -> Expert:
+        e = Expert()
+        e.format = self.fmt
+        e.proj_scale = self.proj_scale
+        for i, m in enumerate(self.mats):
+            if self.fmt == FMT_NVFP4:
+                e.nv[i] = m.cstruct()
+            else:
+                e.tn[i] = m.cstruct()
+        return e
+
+    @classmethod
+    def generate(cls, fmt, seed, layer, expert, inter, hidden, gs=1.0, with_core=True,
+                 proj_scale=1.0, device="cuda", stream=None):
+        tags = (TAG_W1, TAG_W3, TAG_W2)
+        shapes = ((inter, hidden), (inter, hidden), (hidden, inter))
+        mats = []
+        for tag, (r, c) in zip(tags, shapes):
+            k = path_key(seed, layer, expert, tag)
+            if fmt == FMT_NVFP4:
+                mats.append(Nvfp4Matrix.generate(k, r, c, gs, device, stream))
+            else:
+                mats.append(TernaryMatrix.generate(k, r, c, with_core, device, stream))
+        return cls(fmt, mats, inter, hidden, proj_scale)
+
+    def forward(self, x, out=None, weight=1.0, accumulate=False, stream=None):
+        torch = _torch()
+        x = x.contiguous()
+        seq = x.numel() // self.hidden
+        if out is None:
+            out = torch.zeros(seq, self.hidden, dtype=torch.float32, device=x.device)
+        ws = _default_ws(x.device).get(lib().ffn_b200_expert_ws_bytes(self.inter, self.hidden, seq))
+        e = self.cstruct()
+        check(lib().ffn_b200_expert_forward(self.inter, self.hidden, seq, C.byref(e), _ptr(x),
+                                            _ptr(out), float(weight), int(accumulate), _ptr(ws),
+                                            ws.numel(), _stream(stream)), "expert_forward")
+        return out
+
+    def nbytes(self) -> int:
+        return sum(m.nbytes() for m in self.mats)
+
+
+def gen_normal(k: int, n: int, stdev: float = 1.0, device="cuda", stream=None):
+    torch = _torch()
+    out = torch.empty(n, dtype=torch.float32, device=device)
+    check(lib().ffn_b200_gen_normal(k, n, float(stdev), _ptr(out), _stream(stream)),
+          "gen_normal")
+    return out
+
+
+def expert_table(experts, device="cuda"):
+    """Device array of ffn_b200_expert structs (None entries: placeholders)."""
+    torch = _torch()
+    table = (Expert * len(experts))()
+    fmts = set()
+    for i, e in enumerate(experts):
+        if e is not None:
+            table[i] = e.cstruct()
+            fmts.add(e.fmt)
+    return torch.frombuffer(bytearray(bytes(table)), dtype=torch.uint8).to(device), fmts
+
+
+class MoeLayer:
+    """Routed SwiGLU MoE layer over device-resident experts."""
+
+    def __init__(self, experts, router_w, hidden, inter, top_k=6, score_fn=SCORE_SIGMOID,
+                 router_bias=None, router_mode=ROUTER_EXACT, expert_range=None, device="cuda"):
+        self.experts = experts  # SwigluExpert list (None allowed outside expert_range)
+        self.router_w = router_w
+        self.router_bias = router_bias
+        self.hidden, self.inter, self.top_k = hidden, inter, top_k
+        n = len(experts)
+        self.table, fmts = expert_table(experts, device)
+        lo, hi = expert_range if expert_range else (0, n)
+        self.desc = MoeDesc(hidden, inter, n, top_k, _ptr(self.table), _ptr(router_w),
+                            _ptr(router_bias), score_fn, router_mode, lo, hi,
+                            int(FMT_NVFP4 in fmts or not fmts), int(FMT_TERNARY in fmts))
+        self.ws = Workspace(device)
+
+    def ws_bytes(self, n_tok: int) -> int:
+        return int(lib().ffn_b200_moe_ws_bytes(C.byref(self.desc), n_tok))
+
+    def forward(self, x, out=None, residual=None, topk_idx=None, topk_w=None, stream=None):
+        torch = _torch()
+        x = x.contiguous()
+        n_tok = x.numel() // self.hidden
+        if out is None:
+            out = torch.empty(n_tok, self.hidden, dtype=torch.float32, device=x.device)
+        ws = self.ws.get(self.ws_bytes(n_tok))
+        check(lib().ffn_b200_moe_layer(C.byref(self.desc), n_tok, _ptr(x), _ptr(residual),
+                                       _ptr(out), _ptr(topk_idx), _ptr(topk_w), _ptr(ws),
+                                       ws.numel(), _stream(stream)), "moe_layer")
+        return out

@@ -1,0 +1,188 @@
+/*
+ * ffn_b200.h -- B200 extension ABI of libffn_b200.so.
+ *
+ * The reference's plugin ABI (merkaba_hw_addon.h) passes host pointers and
+ * synchronises on every call.  These entry points are the device-resident
+ * fast path the same kernels run on: all tensor pointers are CUDA device
+ * pointers on the current device, work is enqueued on `stream` (a
+ * cudaStream_t, NULL = legacy default stream) and nothing synchronises.  A
+ * Rust host that does not know these symbols keeps working through the
+ * reference ABI.
+ *
+ * Every function returns 0 on success or a negative FFN_B200_E* code;
+ * ffn_b200_last_error() returns the message of the last failure on the calling
+ * thread.  No function here allocates device memory unless its comment says
+ * so: scratch is the caller's `ws` buffer, sized by the matching *_ws_bytes.
+ *
+ * Weight layouts are the reference's on-disk layouts, byte for byte:
+ *   NVFP4   w [rows, cols/2] E2M1 nibbles (low nibble = even column),
+ *           s [rows, cols/16] E4M3 block scales, gs f32 per-tensor scale
+ *           (flash1017.rs:2282-2391).
+ *   ternary p [rows, cols/4] 2-bit codes (element 4j+i at bits 2i..2i+1 of
+ *           byte j; 0->-1, 1->0, 2->+1, 3->0), rs [rows] f32 row scales;
+ *           optional rank-16 Q8 core a [16, cols] i8 (= V^T), a_sc [16],
+ *           b [rows, 16] i8 (= U), b_sc [16]  (flash1017.rs:2393-2672).
+ */
+#ifndef FFN_B200_H
+#define FFN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifndef FFN_B200_EXPORT
+#if defined(__GNUC__)
+#define FFN_B200_EXPORT __attribute__((visibility("default")))
+#else
+#define FFN_B200_EXPORT
+#endif
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FFN_B200_OK 0
+#define FFN_B200_EINVAL (-1)   /* bad shape, pointer or alignment */
+#define FFN_B200_ECUDA (-2)    /* CUDA runtime error */
+#define FFN_B200_ENOSPC (-3)   /* workspace too small */
+#define FFN_B200_ENCCL (-4)    /* NCCL error */
+#define FFN_B200_EUNSUP (-5)   /* valid but unsupported configuration */
+
+#define FFN_B200_FMT_NVFP4 0
+#define FFN_B200_FMT_TERNARY 1
+
+/* Router score functions.  REF: sqrt(softplus(l)) + bias, weights
+ * score * 1.5 / sum (flash1017.rs:7280-7376).  SIGMOID: sigmoid(l) + bias,
+ * weights score / sum (renormalised). */
+#define FFN_B200_SCORE_REF_SQRTSOFTPLUS 0
+#define FFN_B200_SCORE_SIGMOID 1
+
+/* Router arithmetic.  EXACT sums each logit sequentially in column order
+ * without FMA, the CPU loop's order, so logits are bit-identical to the
+ * reference's; TENSOR uses split-f16 tensor-core products (about fp32
+ * accurate, different summation order: selections can differ on near-ties). */
+#define FFN_B200_ROUTER_EXACT 0
+#define FFN_B200_ROUTER_TENSOR 1
+
+typedef struct ffn_b200_nvfp4_mat {
+    const uint8_t *w;  /* [rows, cols/2] */
+    const uint8_t *s;  /* [rows, cols/16] */
+    float gs;
+    uint32_t reserved;
+} ffn_b200_nvfp4_mat;
+
+typedef struct ffn_b200_ternary_mat {
+    const uint8_t *p;        /* [rows, cols/4] */
+    const float *rs;         /* [rows] */
+    const int8_t *core_a;    /* [16, cols] or NULL (no rank-16 core) */
+    const float *core_a_sc;  /* [16] */
+    const int8_t *core_b;    /* [rows, 16] */
+    const float *core_b_sc;  /* [16] */
+} ffn_b200_ternary_mat;
+
+/* One SwiGLU expert: matrix 0 = gate (w1), 1 = up (w3), 2 = down (w2). */
+typedef struct ffn_b200_expert {
+    int32_t format;     /* FFN_B200_FMT_* */
+    float proj_scale;   /* ternary tier_b_proj_scale (flash1017.rs:7551-7561); 1 for NVFP4 */
+    ffn_b200_nvfp4_mat nv[3];
+    ffn_b200_ternary_mat tn[3];
+} ffn_b200_expert;
+
+/* ---------------------------------------------------------------- library */
+FFN_B200_EXPORT const char *ffn_b200_version(void);
+FFN_B200_EXPORT const char *ffn_b200_last_error(void);
+/* Number of kernels this library has launched in this process. */
+FFN_B200_EXPORT uint64_t ffn_b200_launch_count(void);
+/* Selects the device for later calls on this thread (cudaSetDevice). */
+FFN_B200_EXPORT int ffn_b200_set_device(int device);
+
+/* ------------------------------------------------------------ single matrices
+ * out [seq, rows] = x [seq, cols] * W^T.  Same results as the reference's
+ * CachedNvfp4Mat::matbatch / CachedTernary158Mat::matbatch (flash1017.rs:
+ * 2361-2391, 2631-2668) within the parity tolerance.  ws: see *_ws_bytes. */
+FFN_B200_EXPORT size_t ffn_b200_matvec_ws_bytes(size_t seq, size_t cols);
+FFN_B200_EXPORT int ffn_b200_nvfp4_matvec(size_t rows, size_t cols, size_t seq,
+                                          const ffn_b200_nvfp4_mat *m, const float *x,
+                                          float *out, void *ws, size_t ws_bytes, void *stream);
+/* Ternary rows, then y += B (diag(a_sc b_sc) A x) when m->core_a != NULL
+ * (flash1017.rs:2538-2627, rank-16 core :2446-2472). */
+FFN_B200_EXPORT int ffn_b200_ternary_matvec(size_t rows, size_t cols, size_t seq,
+                                            const ffn_b200_ternary_mat *m, const float *x,
+                                            float *out, void *ws, size_t ws_bytes,
+                                            void *stream);
+
+/* ------------------------------------------------------------- one expert
+ * out[t] (=|+=) accum_weight * expert(x[t]) for t < seq, the fused expert of
+ * gx10_rust_nvfp4_mlp_accum / gx10_rust_ternary_158_mlp_accum (HA:323-357)
+ * plus the rank-16 cores the reference's fused path lacks (the reference
+ * recomputes such experts on its CPU, flash1017.rs:7483-7486).  For ternary
+ * experts the caller passes accum_weight = weight * proj_scale, as the
+ * reference does.  `e` is a host struct holding device pointers. */
+FFN_B200_EXPORT size_t ffn_b200_expert_ws_bytes(size_t inter, size_t hidden, size_t seq);
+FFN_B200_EXPORT int ffn_b200_expert_forward(size_t inter, size_t hidden, size_t seq,
+                                            const ffn_b200_expert *e, const float *x,
+                                            float *out, float accum_weight, int accumulate,
+                                            void *ws, size_t ws_bytes, void *stream);
+
+/* -------------------------------------------------------------- MoE layer
+ * Routed SwiGLU MoE layer (flash1017.rs:7259-7567 decode, 7972-8326 batched):
+ * router logits -> scores -> top_k -> per-expert token groups -> fused expert
+ * GEMV/GEMM -> weighted combine in selection order.  Only experts in
+ * [expert_begin, expert_end) are computed (expert parallelism); the others'
+ * contributions are left out of `out`, so summing `out` over the ranks that
+ * own disjoint ranges gives the full layer. */
+typedef struct ffn_b200_moe_desc {
+    size_t hidden, inter, n_experts, top_k;
+    const ffn_b200_expert *experts;  /* DEVICE array [n_experts] */
+    const float *router_w;           /* DEVICE [n_experts, hidden] f32 */
+    const float *router_bias;        /* DEVICE [n_experts] or NULL */
+    int32_t score_fn;                /* FFN_B200_SCORE_* */
+    int32_t router_mode;             /* FFN_B200_ROUTER_* */
+    int32_t expert_begin, expert_end;
+    int32_t has_nvfp4, has_ternary;  /* which formats occur in experts[] */
+} ffn_b200_moe_desc;
+
+FFN_B200_EXPORT size_t ffn_b200_moe_ws_bytes(const ffn_b200_moe_desc *d, size_t max_tokens);
+/* x [n_tok, hidden] f32; out [n_tok, hidden] = residual + moe(x) when
+ * residual != NULL, else moe(x) (residual may alias x or out).  topk_idx /
+ * topk_w [n_tok, top_k] receive the routing when non-NULL. */
+FFN_B200_EXPORT int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok,
+                                       const float *x, const float *residual, float *out,
+                                       int32_t *topk_idx, float *topk_w, void *ws,
+                                       size_t ws_bytes, void *stream);
+
+/* ----------------------------------------------- seeded synthetic weights
+ * Counter-based generators (SplitMix64 finaliser + Irwin-Hall normals +
+ * round-to-nearest-even E4M3), byte-identical to the CPU oracle's. */
+FFN_B200_EXPORT uint64_t ffn_b200_key(uint64_t parent, uint64_t v);
+FFN_B200_EXPORT int ffn_b200_gen_nvfp4(uint64_t key, size_t rows, size_t cols, uint8_t *w,
+                                       uint8_t *s, void *stream);
+FFN_B200_EXPORT int ffn_b200_gen_ternary(uint64_t key, size_t rows, size_t cols, uint8_t *p,
+                                         float *rs, void *stream);
+FFN_B200_EXPORT int ffn_b200_gen_core(uint64_t key, size_t rows, size_t cols, int8_t *a,
+                                      float *a_sc, int8_t *b, float *b_sc, void *stream);
+FFN_B200_EXPORT int ffn_b200_gen_normal(uint64_t key, size_t n, float stdev, float *out,
+                                        void *stream);
+
+/* --------------------------------------------------------- decode checks
+ * The kernels' own weight decoders written out as f32: NVFP4 e2m1 * e4m3
+ * (without the per-tensor scale) and ternary codes {-1,0,+1}. */
+FFN_B200_EXPORT int ffn_b200_dequant_nvfp4(size_t rows, size_t cols, const uint8_t *w,
+                                           const uint8_t *s, float *out, void *stream);
+FFN_B200_EXPORT int ffn_b200_dequant_ternary(size_t rows, size_t cols, const uint8_t *p,
+                                             float *out, void *stream);
+
+/* -------------------------------------------- reference-ABI support hooks
+ * Host-side x_all buffer for gx10_rust_*_mlp_batch (the reference stages it
+ * through the shared-expert call, flash1017.rs:8170-8186). */
+FFN_B200_EXPORT int ffn_b200_set_batch_input(const float *x_all_host, size_t x_total_tokens,
+                                             size_t hidden);
+/* Drops every HBM weight copy made for host pointers. */
+FFN_B200_EXPORT int ffn_b200_release_host_ranges(void);
+/* Bytes of HBM currently held for host-pointer weight copies. */
+FFN_B200_EXPORT size_t ffn_b200_host_cache_bytes(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FFN_B200_H */

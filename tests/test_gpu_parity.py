@@ -1,0 +1,272 @@
+"""GPU parity tests: the CUDA library (through its C-ABI) against the CPU oracle.
+
+Tolerance: decoded weights and top-k indices bit-exact
+(ties excepted), fp32-accumulated outputs max|y-ref|/max|ref| <= 1e-3 and
+cosine >= 0.99999 (oracle.assert_close).
+"""
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def bench_x(n):
+    return np.array([np.float32(math.sin(i * 0.013) * 0.5) for i in range(n)], dtype=np.float32)
+
+
+def host(t):
+    return np.ascontiguousarray(t.detach().cpu().numpy())
+
+
+def dev(a, cuda):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+
+
+def oracle_nvfp4_expert(oracle, e):
+    return oracle.Nvfp4Expert(e.inter, e.hidden, tuple(host(m.w) for m in e.mats),
+                              tuple(host(m.s) for m in e.mats), tuple(m.gs for m in e.mats))
+
+
+def oracle_core(oracle, m):
+    if m.core is None:
+        return None
+    a, a_sc, b, b_sc = (host(t) for t in m.core)
+    return oracle.Core(a, a_sc, b, b_sc)
+
+
+def oracle_ternary_expert(oracle, e):
+    cores = None
+    if e.mats[0].core is not None:
+        cores = tuple(oracle_core(oracle, m) for m in e.mats)
+    return oracle.TernaryExpert(e.inter, e.hidden, tuple(host(m.p) for m in e.mats),
+                                tuple(host(m.rs) for m in e.mats), cores, e.proj_scale)
+
+
+# ---------------------------------------------------------------- generators
+def test_generators_match_oracle_bytes(oracle, ffn, cuda):
+    rows, cols = 64, 4096
+    k = ffn.path_key(0, 0, 0, ffn.TAG_W1)
+    assert k == oracle.key(0, 0, 0, oracle.TAG_W1)
+    m = ffn.Nvfp4Matrix.generate(k, rows, cols)
+    w, s = oracle.gen_nvfp4(k, rows, cols)
+    assert np.array_equal(host(m.w), w) and np.array_equal(host(m.s), s)
+    kt = ffn.path_key(1, 0, 0, ffn.TAG_W1)
+    t = ffn.TernaryMatrix.generate(kt, rows, cols, with_core=True)
+    p, rs = oracle.gen_ternary(kt, rows, cols)
+    c = oracle.gen_core(kt, rows, cols)
+    assert np.array_equal(host(t.p), p) and np.array_equal(host(t.rs), rs)
+    a, a_sc, b, b_sc = (host(x) for x in t.core)
+    assert np.array_equal(a, c.a) and np.array_equal(b, c.b)
+    assert np.array_equal(a_sc, c.a_sc) and np.array_equal(b_sc, c.b_sc)
+    kx = ffn.path_key(2, 0, 0, ffn.TAG_X)
+    assert np.array_equal(host(ffn.gen_normal(kx, 100000)), oracle.gen_normal(kx, 100000))
+
+
+# ------------------------------------------------------------- decode checks
+def test_dequant_bit_exact(oracle, ffn, cuda):
+    """Decoded weight values e2m1*e4m3 and ternary codes: bit-exact."""
+    m = ffn.Nvfp4Matrix.generate(ffn.path_key(3, 0, 0, 1), 128, 512)
+    got = host(m.dequant())
+    want = oracle.dequant_nvfp4(host(m.w), host(m.s), 1.0, 128, 512)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    # every E4M3 scale code x every E2M1 code (NaN codes compared as NaN)
+    w = np.array([(i * 37 + 11) & 0xFF for i in range(256 * 8)], dtype=np.uint8)
+    s = np.arange(256, dtype=np.uint8)
+    m2 = ffn.Nvfp4Matrix(dev(w, cuda), dev(s, cuda), 1.0, 256, 16)
+    got2, want2 = host(m2.dequant()), oracle.dequant_nvfp4(w, s, 1.0, 256, 16)
+    nan = np.isnan(want2)
+    assert np.array_equal(np.isnan(got2), nan)
+    assert np.array_equal(got2[~nan].view(np.uint32), want2[~nan].view(np.uint32))
+    t = ffn.TernaryMatrix.generate(ffn.path_key(3, 0, 1, 1), 64, 256, with_core=False)
+    assert np.array_equal(host(t.dequant()), oracle.dequant_ternary(host(t.p), 64, 256))
+
+
+# ------------------------------------------------------------ single matrices
+NV_SHAPES = [(64, 128), (2048, 4096), (4096, 2048), (100, 96), (2304, 5120), (5120, 2304)]
+
+
+@pytest.mark.parametrize("rows,cols", NV_SHAPES)
+@pytest.mark.parametrize("seq", [1, 3, 8, 9, 17])
+def test_nvfp4_matvec(oracle, ffn, cuda, rows, cols, seq):
+    if rows * cols > 2048 * 4096 and seq > 3:
+        pytest.skip("large shape covered at seq <= 3")
+    m = ffn.Nvfp4Matrix.generate(ffn.path_key(4, rows, cols, 1), rows, cols, gs=0.75)
+    x = ffn.gen_normal(ffn.path_key(4, seq, cols, ffn.TAG_X), seq * cols).view(seq, cols)
+    y = host(m.matvec(x))
+    ref = oracle.nvfp4_matbatch(host(m.w), host(m.s), 0.75, host(x), rows, cols, seq)
+    oracle.assert_close(y, ref, what=f"nvfp4 {rows}x{cols} seq {seq}")
+
+
+def test_nvfp4_reference_fixtures(oracle, ffn, cuda):
+    ka = json.load(open(os.path.join(GOLD, "known_answers.json")))
+    f = ka["nvfp4_scales"]
+    m = ffn.Nvfp4Matrix(dev(np.array(f["w"], dtype=np.uint8), cuda),
+                        dev(np.array(f["s"], dtype=np.uint8), cuda), f["gs"], f["rows"], f["cols"])
+    y = host(m.matvec(dev(bench_x(f["cols"]), cuda)))[0]
+    oracle.assert_close(y, np.array(f["y"], dtype=np.float32), what="nvfp4 all-codes fixture")
+    f = ka["nvfp4_fixture"]
+    rows, cols = f["rows"], f["cols"]
+    w = np.array([((i * 7 + 3) % 16) | (((i * 13 + 5) % 16) << 4) for i in range(rows * cols // 2)],
+                 dtype=np.uint8)
+    s = np.array([0x38 if i % 2 == 0 else 0x3C for i in range(rows * cols // 16)], dtype=np.uint8)
+    m = ffn.Nvfp4Matrix(dev(w, cuda), dev(s, cuda), f["gs"], rows, cols)
+    y = host(m.matvec(dev(bench_x(cols), cuda)))[0]
+    oracle.assert_close(y, np.array(f["y"], dtype=np.float32), what="reference NVFP4 fixture")
+
+
+@pytest.mark.parametrize("rows,cols", [(32, 256), (2048, 4096), (4096, 2048), (70, 192)])
+@pytest.mark.parametrize("seq", [1, 5, 8, 11])
+@pytest.mark.parametrize("with_core", [False, True])
+def test_ternary_matvec(oracle, ffn, cuda, rows, cols, seq, with_core):
+    m = ffn.TernaryMatrix.generate(ffn.path_key(5, rows, cols, 1), rows, cols, with_core)
+    x = ffn.gen_normal(ffn.path_key(5, seq, cols, ffn.TAG_X), seq * cols).view(seq, cols)
+    y = host(m.matvec(x))
+    ref = oracle.ternary_matbatch(host(m.p), host(m.rs), host(x), rows, cols, seq,
+                                  core=oracle_core(oracle, m))
+    oracle.assert_close(y, ref, what=f"ternary {rows}x{cols} seq {seq} core {with_core}")
+
+
+def test_ternary_known_answer_fixture(oracle, ffn, cuda):
+    f = json.load(open(os.path.join(GOLD, "known_answers.json")))["ternary"]
+    m = ffn.TernaryMatrix(dev(np.array(f["p"], dtype=np.uint8), cuda),
+                          dev(np.array(f["rs"], dtype=np.float32), cuda), f["rows"], f["cols"])
+    y = host(m.matvec(dev(bench_x(f["cols"]), cuda)))[0]
+    oracle.assert_close(y, np.array(f["y"], dtype=np.float32), what="ternary fixture")
+
+
+# ----------------------------------------------------------------- experts
+@pytest.mark.parametrize("seq", [1, 4, 8, 13])
+def test_nvfp4_expert_config0(oracle, ffn, cuda, seq):
+    """BASELINE config 0 shapes (H 4096, I 2048), seed 0."""
+    H, I = 4096, 2048
+    e = ffn.SwigluExpert.generate(ffn.FMT_NVFP4, 0, 0, 0, I, H)
+    x = ffn.gen_normal(ffn.path_key(0, 0, 0, ffn.TAG_X), seq * H).view(seq, H)
+    y = host(e.forward(x))
+    oe = oracle_nvfp4_expert(oracle, e)
+    xs = host(x)
+    ref = np.stack([oe.forward(np.ascontiguousarray(xs[t])) for t in range(seq)])
+    oracle.assert_close(y, ref, what=f"nvfp4 expert seq {seq}")
+
+
+@pytest.mark.parametrize("seq", [1, 6])
+@pytest.mark.parametrize("with_core", [True, False])
+def test_ternary_expert_config1(oracle, ffn, cuda, seq, with_core):
+    """BASELINE config 1 shapes, seed 1, rank-16 Q8 cores on all three matrices."""
+    H, I = 4096, 2048
+    e = ffn.SwigluExpert.generate(ffn.FMT_TERNARY, 1, 0, 0, I, H, with_core=with_core,
+                                  proj_scale=1.0)
+    x = ffn.gen_normal(ffn.path_key(1, 0, 0, ffn.TAG_X), seq * H).view(seq, H)
+    y = host(e.forward(x))
+    oe = oracle_ternary_expert(oracle, e)
+    xs = host(x)
+    ref = np.stack([oe.forward(np.ascontiguousarray(xs[t])) for t in range(seq)])
+    oracle.assert_close(y, ref, what=f"ternary expert seq {seq} core {with_core}")
+
+
+def test_ternary_expert_proj_scale(oracle, ffn, cuda):
+    H, I = 512, 256
+    e = ffn.SwigluExpert.generate(ffn.FMT_TERNARY, 6, 0, 0, I, H, with_core=True, proj_scale=3.5)
+    x = ffn.gen_normal(ffn.path_key(6, 0, 0, ffn.TAG_X), 3 * H).view(3, H)
+    y = host(e.forward(x))
+    oe = oracle_ternary_expert(oracle, e)
+    xs = host(x)
+    ref = np.stack([oe.forward(np.ascontiguousarray(xs[t])) for t in range(3)])
+    oracle.assert_close(y, ref, what="ternary expert proj_scale 3.5")
+
+
+def test_expert_accumulate_modes(oracle, ffn, cuda):
+    import torch
+    H, I = 256, 128
+    e = ffn.SwigluExpert.generate(ffn.FMT_NVFP4, 9, 0, 0, I, H)
+    x = ffn.gen_normal(ffn.path_key(9, 0, 0, ffn.TAG_X), 2 * H).view(2, H)
+    base = torch.full((2, H), 0.25, device=cuda)
+    y1 = e.forward(x, out=base.clone(), weight=0.5, accumulate=True)
+    y0 = e.forward(x, out=base.clone(), weight=0.5, accumulate=False)
+    np.testing.assert_allclose(host(y1), host(y0) + 0.25, rtol=1e-6, atol=1e-6)
+
+
+# --------------------------------------------------------------- MoE layer
+def _moe_small(ffn, fmt, E, H, I, seed, with_core=True):
+    experts = [ffn.SwigluExpert.generate(fmt, seed, 0, e, I, H, with_core=with_core)
+               for e in range(E)]
+    wr = ffn.gen_normal(ffn.path_key(seed, 0, 0, ffn.TAG_ROUTER), E * H, 0.02).view(E, H)
+    return experts, wr
+
+
+@pytest.mark.parametrize("score_fn", [0, 1])
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_moe_layer_small(oracle, ffn, cuda, score_fn, fmt):
+    import torch
+    E, H, I, T, K = 16, 256, 128, 11, 6
+    experts, wr = _moe_small(ffn, fmt, E, H, I, seed=20 + fmt)
+    layer = ffn.MoeLayer(experts, wr, H, I, top_k=K, score_fn=score_fn)
+    x = ffn.gen_normal(ffn.path_key(20, 0, 0, ffn.TAG_X), T * H).view(T, H)
+    idx = torch.empty(T, K, dtype=torch.int32, device=cuda)
+    wt = torch.empty(T, K, dtype=torch.float32, device=cuda)
+    out = host(layer.forward(x, topk_idx=idx, topk_w=wt))
+    oe = [oracle_nvfp4_expert(oracle, e) if fmt == 0 else oracle_ternary_expert(oracle, e)
+          for e in experts]
+    ref, ridx, rwt = oracle.moe_layer(oe, host(wr), host(x), top_k=K, score_fn=score_fn)
+    assert np.array_equal(host(idx), ridx)  # exact router: logits bit-identical
+    np.testing.assert_allclose(host(wt), rwt, rtol=2e-6)
+    oracle.assert_close(out, ref, what=f"moe small fmt {fmt} score {score_fn}")
+
+
+def test_moe_layer_mixed_formats(oracle, ffn, cuda):
+    """A layer whose experts alternate NVFP4 / ternary+core (tier A / tier B)."""
+    E, H, I, T, K = 10, 256, 128, 9, 4
+    experts = [ffn.SwigluExpert.generate(e % 2, 40, 0, e, I, H, with_core=True)
+               for e in range(E)]
+    wr = ffn.gen_normal(ffn.path_key(40, 0, 0, ffn.TAG_ROUTER), E * H, 0.02).view(E, H)
+    x = ffn.gen_normal(ffn.path_key(40, 0, 0, ffn.TAG_X), T * H).view(T, H)
+    out = host(ffn.MoeLayer(experts, wr, H, I, top_k=K, score_fn=0).forward(x))
+    oe = [oracle_nvfp4_expert(oracle, e) if e.fmt == 0 else oracle_ternary_expert(oracle, e)
+          for e in experts]
+    ref, _, _ = oracle.moe_layer(oe, host(wr), host(x), top_k=K, score_fn=0)
+    oracle.assert_close(out, ref, what="moe mixed formats")
+
+
+def test_moe_layer_residual_and_expert_range(oracle, ffn, cuda):
+    """EP slices: the sum over disjoint expert ranges equals the full layer."""
+    E, H, I, T = 12, 128, 64, 7
+    experts, wr = _moe_small(ffn, 0, E, H, I, seed=31)
+    x = ffn.gen_normal(ffn.path_key(31, 0, 0, ffn.TAG_X), T * H).view(T, H)
+    full = host(ffn.MoeLayer(experts, wr, H, I).forward(x))
+    parts = sum(host(ffn.MoeLayer(experts, wr, H, I, expert_range=(a, b)).forward(x))
+                for a, b in ((0, 5), (5, 9), (9, 12)))
+    oracle.assert_close(parts, full, rel=1e-5, cos=0.999999, what="EP partition sum")
+    res = host(ffn.MoeLayer(experts, wr, H, I).forward(x, residual=x))
+    oracle.assert_close(res, full + host(x), rel=1e-6, cos=0.9999999, what="residual")
+
+
+def test_moe_config2_sampled(oracle, ffn, cuda):
+    """384 NVFP4 experts (H 4096, I 2048), 64 tokens, router
+    fp32 N(0, 0.02), sigmoid top-6, seed 2.  All 64 tokens' top-6 indices are
+    compared with the oracle router; outputs of a sample of tokens with the
+    oracle experts they hit."""
+    import torch
+    E, H, I, T, K, seed = 384, 4096, 2048, 64, 6, 2
+    experts = [ffn.SwigluExpert.generate(ffn.FMT_NVFP4, seed, 0, e, I, H) for e in range(E)]
+    wr = ffn.gen_normal(ffn.path_key(seed, 0, 0, ffn.TAG_ROUTER), E * H, 0.02).view(E, H)
+    layer = ffn.MoeLayer(experts, wr, H, I, top_k=K, score_fn=ffn.SCORE_SIGMOID)
+    x = ffn.gen_normal(ffn.path_key(seed, 0, 0, ffn.TAG_X), T * H).view(T, H)
+    idx = torch.empty(T, K, dtype=torch.int32, device=cuda)
+    wt = torch.empty(T, K, dtype=torch.float32, device=cuda)
+    out = host(layer.forward(x, topk_idx=idx, topk_w=wt))
+    xs = host(x)
+    logits = oracle.router_logits(host(wr), xs)
+    ridx, rwt, _, _ = oracle.route(logits, K, None, 1)
+    assert np.array_equal(host(idx), ridx)
+    for t in (0, 17, 63):
+        ref = np.zeros(H, dtype=np.float32)
+        for k in range(K):
+            y = oracle_nvfp4_expert(oracle, experts[ridx[t, k]]).forward(np.ascontiguousarray(xs[t]))
+            oracle.axpy(ref, rwt[t, k], y)
+        oracle.assert_close(out[t], ref, what=f"config2 token {t}")

@@ -23,8 +23,17 @@ void note_launch(uint64_t n = 1);
     if (_e != cudaSuccess) return ::ffn::cuda_fail(_e, #expr); \
   } while (0)
 
-#define FFN_LAUNCH_CHECK(name)                                      \
+// Event-pair timing of one launch (no-ops unless ffn_b200_profile_enable(1)).
+void prof_begin(int kind, cudaStream_t st);
+void prof_end(int kind, cudaStream_t st);
+
+// Launch the kernel<<<...>>> expression given as the trailing arguments on
+// stream `st`, timed under `kind`, and return the launch error if any.
+#define FFN_LAUNCH(kind, st, name, ...)                             \
   do {                                                              \
+    ::ffn::prof_begin(kind, st);                                    \
+    __VA_ARGS__;                                                    \
+    ::ffn::prof_end(kind, st);                                      \
     ::ffn::note_launch();                                           \
     cudaError_t _e = cudaGetLastError();                            \
     if (_e != cudaSuccess) return ::ffn::cuda_fail(_e, name);       \

@@ -1,7 +1,9 @@
 // ffn_api.cu -- the device-resident extension ABI (include/ffn_b200.h).
 #include <algorithm>
 #include <atomic>
+#include <mutex>
 #include <string>
+#include <vector>
 
 #include "ffn_internal.h"
 
@@ -20,6 +22,64 @@ int cuda_fail(cudaError_t e, const char *what) {
   return fail(FFN_B200_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 void note_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+// ------------------------------------------------------------- profiling
+// A fixed pool of event pairs, created when profiling is enabled; launches
+// beyond the pool are not timed (counted in `dropped`).
+namespace {
+struct Prof {
+  std::mutex mu;
+  bool on = false;
+  std::vector<cudaEvent_t> ev;  // 2 per record
+  std::vector<int> kind;        // per record
+  size_t used = 0;              // records in use
+  int open_kind = -1;
+  double total_ms[FFN_B200_K_COUNT] = {0};
+  uint64_t count[FFN_B200_K_COUNT] = {0};
+  uint64_t dropped = 0;
+};
+Prof &prof() {
+  static Prof *p = new Prof();
+  return *p;
+}
+constexpr size_t kProfRecords = 16384;
+}  // namespace
+
+void prof_begin(int kind, cudaStream_t st) {
+  Prof &p = prof();
+  if (!p.on) return;
+  std::lock_guard<std::mutex> lk(p.mu);
+  if (p.used >= p.kind.size()) { ++p.dropped; p.open_kind = -1; return; }
+  cudaEventRecord(p.ev[2 * p.used], st);
+  p.kind[p.used] = kind;
+  p.open_kind = kind;
+}
+
+void prof_end(int kind, cudaStream_t st) {
+  Prof &p = prof();
+  if (!p.on) return;
+  std::lock_guard<std::mutex> lk(p.mu);
+  if (p.open_kind != kind || p.used >= p.kind.size()) return;
+  cudaEventRecord(p.ev[2 * p.used + 1], st);
+  ++p.used;
+  p.open_kind = -1;
+}
+
+// Folds the completed records into the totals (waits for the recorded events).
+static int prof_collect(Prof &p) {
+  for (size_t i = 0; i < p.used; ++i) {
+    cudaError_t e = cudaEventSynchronize(p.ev[2 * i + 1]);
+    if (e != cudaSuccess) return cuda_fail(e, "profile: cudaEventSynchronize");
+    float ms = 0.f;
+    e = cudaEventElapsedTime(&ms, p.ev[2 * i], p.ev[2 * i + 1]);
+    if (e != cudaSuccess) return cuda_fail(e, "profile: cudaEventElapsedTime");
+    const int k = p.kind[i] >= 0 && p.kind[i] < FFN_B200_K_COUNT ? p.kind[i] : FFN_B200_K_OTHER;
+    p.total_ms[k] += ms;
+    p.count[k] += 1;
+  }
+  p.used = 0;
+  return 0;
+}
 
 static int sm_count() {
   static int cache[64] = {0};
@@ -112,6 +172,35 @@ uint64_t ffn_b200_launch_count(void) { return g_launches.load(); }
 
 int ffn_b200_set_device(int device) {
   FFN_CUDA_TRY(cudaSetDevice(device));
+  return 0;
+}
+
+int ffn_b200_profile_enable(int enable) {
+  Prof &p = prof();
+  std::lock_guard<std::mutex> lk(p.mu);
+  if (enable && p.ev.empty()) {
+    p.ev.resize(2 * kProfRecords);
+    for (auto &e : p.ev) FFN_CUDA_TRY(cudaEventCreate(&e));
+    p.kind.assign(kProfRecords, -1);
+  }
+  if (enable) {  // a fresh window
+    int rc = prof_collect(p);
+    if (rc) return rc;
+    for (int k = 0; k < FFN_B200_K_COUNT; ++k) { p.total_ms[k] = 0; p.count[k] = 0; }
+    p.dropped = 0;
+  }
+  p.on = enable != 0;
+  return 0;
+}
+
+int ffn_b200_profile_read(int kind, double *total_ms, uint64_t *launches) {
+  if (kind < 0 || kind >= FFN_B200_K_COUNT) return fail(FFN_B200_EINVAL, "profile_read: bad kind");
+  Prof &p = prof();
+  std::lock_guard<std::mutex> lk(p.mu);
+  int rc = prof_collect(p);
+  if (rc) return rc;
+  if (total_ms) *total_ms = p.total_ms[kind];
+  if (launches) *launches = p.count[kind];
   return 0;
 }
 

@@ -53,8 +53,7 @@ __global__ void __launch_bounds__(256) xprep_kernel(const float *__restrict__ x,
 int launch_xprep(const float *x, int ld_x, int rows, int K, __half *nh, __half *nl, __half *th,
                  __half *tl, int ld_o, int *xe, cudaStream_t st) {
   if (rows <= 0) return 0;
-  xprep_kernel<<<rows, 256, 0, st>>>(x, ld_x, K, nh, nl, th, tl, ld_o, xe);
-  FFN_LAUNCH_CHECK("xprep_kernel");
+  FFN_LAUNCH(FFN_B200_K_XPREP, st, "xprep_kernel", xprep_kernel<<<rows, 256, 0, st>>>(x, ld_x, K, nh, nl, th, tl, ld_o, xe));
   return 0;
 }
 
@@ -191,10 +190,16 @@ __global__ void __launch_bounds__(kThreads, 2) phase_kernel(const PhaseArgs a) {
   }
 }
 
+constexpr int phase_kind(int fmt, int phase) {
+  return phase == 0 ? FFN_B200_K_MATVEC
+                    : (fmt == FFN_B200_FMT_NVFP4 ? (phase == 1 ? FFN_B200_K_GATEUP_NVFP4 : FFN_B200_K_DOWN_NVFP4)
+                                                 : (phase == 1 ? FFN_B200_K_GATEUP_TERNARY : FFN_B200_K_DOWN_TERNARY));
+}
+
 template <int FMT, int PHASE, int R>
 static int launch_phase_t(const PhaseArgs &a, int grid, cudaStream_t st) {
-  phase_kernel<FMT, PHASE, R><<<grid, kThreads, 0, st>>>(a);
-  FFN_LAUNCH_CHECK("phase_kernel");
+  FFN_LAUNCH(phase_kind(FMT, PHASE), st, "phase_kernel",
+             (phase_kernel<FMT, PHASE, R><<<grid, kThreads, 0, st>>>(a)));
   return 0;
 }
 
@@ -270,8 +275,7 @@ __global__ void __launch_bounds__(256) corez_kernel(const CoreZArgs a) {
 
 int launch_corez(const CoreZArgs &a, int max_vexp, cudaStream_t st) {
   if (max_vexp <= 0) return 0;
-  corez_kernel<<<max_vexp * a.nmat, 256, 0, st>>>(a);
-  FFN_LAUNCH_CHECK("corez_kernel");
+  FFN_LAUNCH(FFN_B200_K_COREZ, st, "corez_kernel", corez_kernel<<<max_vexp * a.nmat, 256, 0, st>>>(a));
   return 0;
 }
 
@@ -320,9 +324,12 @@ int launch_exact_matvec(const float *w32, const uint16_t *w16, const float *x, i
   if (n_tok <= 0 || rows <= 0) return 0;
   dim3 g1((rows + 31) / 32, (n_tok + 7) / 8);
   if (g1.y > 65535) return fail(FFN_B200_EINVAL, "exact matvec: too many tokens");
-  if (w32) router_exact_kernel<float><<<g1, 256, 0, st>>>(w32, x, n_tok, rows, H, out);
-  else router_exact_kernel<uint16_t><<<g1, 256, 0, st>>>(w16, x, n_tok, rows, H, out);
-  FFN_LAUNCH_CHECK("router_exact_kernel");
+  if (w32)
+    FFN_LAUNCH(FFN_B200_K_ROUTER, st, "router_exact_kernel",
+               (router_exact_kernel<float><<<g1, 256, 0, st>>>(w32, x, n_tok, rows, H, out)));
+  else
+    FFN_LAUNCH(FFN_B200_K_ROUTER, st, "router_exact_kernel",
+               (router_exact_kernel<uint16_t><<<g1, 256, 0, st>>>(w16, x, n_tok, rows, H, out)));
   return 0;
 }
 
@@ -386,9 +393,8 @@ int launch_router(const float *w, const float *bias, const float *x, int n_tok, 
                   cudaStream_t st) {
   int rc = launch_exact_matvec(w, nullptr, x, n_tok, n_exp, H, logits, st);
   if (rc) return rc;
-  topk_kernel<<<(n_tok + 7) / 8, 256, 0, st>>>(logits, bias, n_tok, n_exp, top_k, score_fn, idx,
-                                               wt);
-  FFN_LAUNCH_CHECK("topk_kernel");
+  FFN_LAUNCH(FFN_B200_K_TOPK, st, "topk_kernel", topk_kernel<<<(n_tok + 7) / 8, 256, 0, st>>>(logits, bias, n_tok, n_exp, top_k, score_fn, idx,
+                                               wt));
   return 0;
 }
 
@@ -494,10 +500,9 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__
 int launch_group(const int32_t *idx, int n_tok, int top_k, int n_exp, int e_begin, int e_end,
                  const ffn_b200_expert *experts, int *ws_int, int32_t *pair_tok, int32_t *inv,
                  VExp *vexp_nv, VExp *vexp_tn, int *n_vexp, cudaStream_t st) {
-  group_kernel<<<1, 1024, 0, st>>>(idx, n_tok * top_k, top_k, n_exp, e_begin, e_end, experts,
+  FFN_LAUNCH(FFN_B200_K_GROUP, st, "group_kernel", group_kernel<<<1, 1024, 0, st>>>(idx, n_tok * top_k, top_k, n_exp, e_begin, e_end, experts,
                                    ws_int, ws_int + n_exp, ws_int + 2 * n_exp,
-                                   ws_int + 3 * n_exp, pair_tok, inv, vexp_nv, vexp_tn, n_vexp);
-  FFN_LAUNCH_CHECK("group_kernel");
+                                   ws_int + 3 * n_exp, pair_tok, inv, vexp_nv, vexp_tn, n_vexp));
   return 0;
 }
 
@@ -539,8 +544,7 @@ int launch_combine(const float *y, int ld_y, const int32_t *idx, const float *wt
                    const int32_t *inv, int n_tok, int top_k, const ffn_b200_expert *experts,
                    const float *residual, float *out, int H, cudaStream_t st) {
   if (n_tok <= 0) return 0;
-  combine_kernel<<<n_tok, 256, 0, st>>>(y, ld_y, idx, wt, inv, top_k, experts, residual, out, H);
-  FFN_LAUNCH_CHECK("combine_kernel");
+  FFN_LAUNCH(FFN_B200_K_COMBINE, st, "combine_kernel", combine_kernel<<<n_tok, 256, 0, st>>>(y, ld_y, idx, wt, inv, top_k, experts, residual, out, H));
   return 0;
 }
 
@@ -557,8 +561,7 @@ __global__ void scatter_axpy_kernel(const float *__restrict__ y, const int64_t *
 int launch_scatter_axpy(const float *y, const int64_t *dst, const float *w, int m, int H,
                         float *out, cudaStream_t st) {
   if (m <= 0) return 0;
-  scatter_axpy_kernel<<<(H + 255) / 256, 256, 0, st>>>(y, dst, w, m, H, out);
-  FFN_LAUNCH_CHECK("scatter_axpy_kernel");
+  FFN_LAUNCH(FFN_B200_K_OTHER, st, "scatter_axpy_kernel", scatter_axpy_kernel<<<(H + 255) / 256, 256, 0, st>>>(y, dst, w, m, H, out));
   return 0;
 }
 
@@ -604,8 +607,7 @@ __global__ void __launch_bounds__(256) dot_kernel(int mode, const void *a, const
 }
 int launch_dot(int mode, const void *a, const void *aux, const float *x, size_t len, float *out,
                cudaStream_t st) {
-  dot_kernel<<<1, 256, 0, st>>>(mode, a, aux, x, len, out);
-  FFN_LAUNCH_CHECK("dot_kernel");
+  FFN_LAUNCH(FFN_B200_K_OTHER, st, "dot_kernel", dot_kernel<<<1, 256, 0, st>>>(mode, a, aux, x, len, out));
   return 0;
 }
 
@@ -703,29 +705,25 @@ static int gen_grid(size_t n) {
 int launch_gen_nvfp4(uint64_t kw, uint64_t ks, size_t rows, size_t cols, uint8_t *w, uint8_t *s,
                      cudaStream_t st) {
   const size_t nb = rows * cols / 2, ns = rows * cols / 16;
-  gen_nvfp4_kernel<<<gen_grid(nb), 256, 0, st>>>(kw, ks, nb, ns, w, s);
-  FFN_LAUNCH_CHECK("gen_nvfp4_kernel");
+  FFN_LAUNCH(FFN_B200_K_OTHER, st, "gen_nvfp4_kernel", gen_nvfp4_kernel<<<gen_grid(nb), 256, 0, st>>>(kw, ks, nb, ns, w, s));
   return 0;
 }
 int launch_gen_ternary(uint64_t kp, uint64_t kr, size_t rows, size_t cols, uint8_t *p, float *rs,
                        cudaStream_t st) {
   const size_t nb = rows * cols / 4;
-  gen_ternary_kernel<<<gen_grid(nb), 256, 0, st>>>(kp, kr, nb, rows, p, rs);
-  FFN_LAUNCH_CHECK("gen_ternary_kernel");
+  FFN_LAUNCH(FFN_B200_K_OTHER, st, "gen_ternary_kernel", gen_ternary_kernel<<<gen_grid(nb), 256, 0, st>>>(kp, kr, nb, rows, p, rs));
   return 0;
 }
 int launch_gen_core(uint64_t ka, uint64_t kb, uint64_t kas, uint64_t kbs, size_t rows,
                     size_t cols, int8_t *a, float *a_sc, int8_t *b, float *b_sc,
                     cudaStream_t st) {
   const size_t na = 16 * cols, nb = rows * 16;
-  gen_core_kernel<<<gen_grid(std::max(na, nb)), 256, 0, st>>>(ka, kb, kas, kbs, na, nb, a, a_sc,
-                                                              b, b_sc);
-  FFN_LAUNCH_CHECK("gen_core_kernel");
+  FFN_LAUNCH(FFN_B200_K_OTHER, st, "gen_core_kernel", gen_core_kernel<<<gen_grid(std::max(na, nb)), 256, 0, st>>>(ka, kb, kas, kbs, na, nb, a, a_sc,
+                                                              b, b_sc));
   return 0;
 }
 int launch_gen_normal(uint64_t key, size_t n, float stdev, float *out, cudaStream_t st) {
-  gen_normal_kernel<<<gen_grid(n), 256, 0, st>>>(key, n, stdev, out);
-  FFN_LAUNCH_CHECK("gen_normal_kernel");
+  FFN_LAUNCH(FFN_B200_K_OTHER, st, "gen_normal_kernel", gen_normal_kernel<<<gen_grid(n), 256, 0, st>>>(key, n, stdev, out));
   return 0;
 }
 
@@ -750,14 +748,12 @@ __global__ void dequant_ternary_kernel(size_t rows, size_t cols, const uint8_t *
 }
 int launch_dequant_nvfp4(size_t rows, size_t cols, const uint8_t *w, const uint8_t *s, float *out,
                          cudaStream_t st) {
-  dequant_nvfp4_kernel<<<gen_grid(rows * cols), 256, 0, st>>>(rows, cols, w, s, out);
-  FFN_LAUNCH_CHECK("dequant_nvfp4_kernel");
+  FFN_LAUNCH(FFN_B200_K_OTHER, st, "dequant_nvfp4_kernel", dequant_nvfp4_kernel<<<gen_grid(rows * cols), 256, 0, st>>>(rows, cols, w, s, out));
   return 0;
 }
 int launch_dequant_ternary(size_t rows, size_t cols, const uint8_t *p, float *out,
                            cudaStream_t st) {
-  dequant_ternary_kernel<<<gen_grid(rows * cols), 256, 0, st>>>(rows, cols, p, out);
-  FFN_LAUNCH_CHECK("dequant_ternary_kernel");
+  FFN_LAUNCH(FFN_B200_K_OTHER, st, "dequant_ternary_kernel", dequant_ternary_kernel<<<gen_grid(rows * cols), 256, 0, st>>>(rows, cols, p, out));
   return 0;
 }
 

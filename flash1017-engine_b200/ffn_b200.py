@@ -33,7 +33,14 @@ EXPORTS = [
     "ffn_b200_key", "ffn_b200_gen_nvfp4", "ffn_b200_gen_ternary", "ffn_b200_gen_core",
     "ffn_b200_gen_normal", "ffn_b200_dequant_nvfp4", "ffn_b200_dequant_ternary",
     "ffn_b200_set_batch_input", "ffn_b200_release_host_ranges", "ffn_b200_host_cache_bytes",
+    "ffn_b200_profile_enable", "ffn_b200_profile_read",
 ]
+
+# Kernel kinds of ffn_b200_profile_read (FFN_B200_K_*).
+K_XPREP, K_ROUTER, K_TOPK, K_GROUP, K_GATEUP_NVFP4, K_DOWN_NVFP4 = 0, 1, 2, 3, 4, 5
+K_GATEUP_TERNARY, K_DOWN_TERNARY, K_COREZ, K_COMBINE, K_MATVEC, K_OTHER = 6, 7, 8, 9, 10, 11
+K_NAMES = ["xprep", "router", "topk", "group", "gateup_nvfp4", "down_nvfp4", "gateup_ternary",
+           "down_ternary", "corez", "combine", "matvec", "other"]
 
 
 def build() -> str:
@@ -110,6 +117,8 @@ def lib() -> C.CDLL:
         L.ffn_b200_set_batch_input.argtypes = [vp, sz, sz]
         L.ffn_b200_host_cache_bytes.restype = sz
         L.merkaba_hardware_addon_v1.restype = vp
+        L.ffn_b200_profile_enable.argtypes = [i32]
+        L.ffn_b200_profile_read.argtypes = [i32, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]
         _lib = L
     return _lib
 
@@ -122,6 +131,22 @@ def check(rc: int, what: str = "") -> None:
 
 def launch_count() -> int:
     return int(lib().ffn_b200_launch_count())
+
+
+def profile_enable(on: bool) -> None:
+    """Start (True: clears the totals) or stop per-kernel event timing."""
+    check(lib().ffn_b200_profile_enable(int(on)), "profile_enable")
+
+
+def profile_read() -> dict:
+    """{kernel kind name: (total device ms, launches)} since profile_enable(True)."""
+    out = {}
+    for k, name in enumerate(K_NAMES):
+        ms, n = C.c_double(), C.c_uint64()
+        check(lib().ffn_b200_profile_read(k, C.byref(ms), C.byref(n)), "profile_read")
+        if n.value:
+            out[name] = (ms.value, int(n.value))
+    return out
 
 
 def key(parent: int, v: int) -> int:

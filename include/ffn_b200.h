@@ -172,6 +172,28 @@ FFN_B200_EXPORT int ffn_b200_dequant_nvfp4(size_t rows, size_t cols, const uint8
 FFN_B200_EXPORT int ffn_b200_dequant_ternary(size_t rows, size_t cols, const uint8_t *p,
                                              float *out, void *stream);
 
+/* ------------------------------------------------------ kernel timing
+ * Measurement hooks.  While enabled, the library records a CUDA event pair
+ * around every kernel it launches, on the stream the kernel is launched on,
+ * and ffn_b200_profile_read() sums the device time per kernel kind (it
+ * synchronises the recorded events).  Enabling creates the events; no work is
+ * skipped or reordered.  Off by default. */
+#define FFN_B200_K_XPREP 0
+#define FFN_B200_K_ROUTER 1
+#define FFN_B200_K_TOPK 2
+#define FFN_B200_K_GROUP 3
+#define FFN_B200_K_GATEUP_NVFP4 4
+#define FFN_B200_K_DOWN_NVFP4 5
+#define FFN_B200_K_GATEUP_TERNARY 6
+#define FFN_B200_K_DOWN_TERNARY 7
+#define FFN_B200_K_COREZ 8
+#define FFN_B200_K_COMBINE 9
+#define FFN_B200_K_MATVEC 10
+#define FFN_B200_K_OTHER 11
+#define FFN_B200_K_COUNT 12
+FFN_B200_EXPORT int ffn_b200_profile_enable(int enable);
+FFN_B200_EXPORT int ffn_b200_profile_read(int kind, double *total_ms, uint64_t *launches);
+
 /* -------------------------------------------- reference-ABI support hooks
  * Host-side x_all buffer for gx10_rust_*_mlp_batch (the reference stages it
  * through the shared-expert call, flash1017.rs:8170-8186). */

@@ -1,0 +1,458 @@
+#!/usr/bin/env python
+"""bench.py -- MoE expert-FFN tokens/s on 1/2/4/8 B200.
+
+Workload: a 40-layer NVFP4 MoE-FFN stack (hidden 4096, intermediate 2048, 384
+routed SwiGLU experts per layer, fp32 router N(0, 0.02), sigmoid top-6 with
+renormalised weights, residual add between layers), one decode step of 256
+tokens, seed 4, random-init weights from the library's seeded generator.
+Experts are sharded expert-parallel: rank r of N owns experts
+[r*384/N, (r+1)*384/N) of every layer; every rank routes all tokens (the
+routing is replicated, so no count exchange is needed) and the per-layer
+partial outputs are summed with one NCCL all-reduce.  A "step" is the full
+40-layer pass over the 256 tokens; `value` is tokens/s for the whole job.
+
+The stack holds 15,360 experts (~217 GB): on one GPU only the layers that fit
+are resident and layer-step l streams the weights of resident layer
+l % resident_layers.  Every layer's weights (>= 2.6 GB per rank) are far
+larger than L2, so every layer-step reads its expert bytes from HBM, as the
+full stack does; config.resident_layers records the number.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+(N > 1 under torchrun, one rank per GPU).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "flash1017-engine_b200")
+ORACLE = os.path.join(ROOT, "oracle")
+for _p in (PKG, ORACLE):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "MoE expert-FFN tokens/s (40-layer NVFP4 top-6/384 decode stack)"
+UNIT = "tokens/s"
+EXPERT_BYTES = lambda H, I: 3 * (I * H // 2 + I * H // 16)  # noqa: E731
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=256)
+    ap.add_argument("--layers", type=int, default=40)
+    ap.add_argument("--experts", type=int, default=384)
+    ap.add_argument("--hidden", type=int, default=4096)
+    ap.add_argument("--inter", type=int, default=2048)
+    ap.add_argument("--top-k", type=int, default=6)
+    ap.add_argument("--seed", type=int, default=4)
+    ap.add_argument("--max-resident", type=int, default=0,
+                    help="cap on resident layers (0: as many as fit)")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="CPU-baseline sample length")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def base_config(a, world, resident):
+    return {
+        "workload": "config4: 40-layer NVFP4 MoE-FFN stack, 256-token decode, top-6 of 384, "
+                    "expert-parallel",
+        "hidden": a.hidden, "inter": a.inter, "experts": a.experts, "top_k": a.top_k,
+        "layers": a.layers, "tokens": a.tokens, "seed": a.seed, "router": "fp32 exact, sigmoid",
+        "resident_layers": resident, "parallelism": f"ep{world}",
+        "l2": "no flush: every layer-step streams >= 2.6 GB of expert weights (> 126 MB L2)",
+    }
+
+
+# --------------------------------------------------------------- CPU legs
+class CpuSample:
+    """The oracle (C restatement of the reference's Rayon CPU path) on a
+    bounded sample of the workload: the first 4 tokens through the first 2
+    layers (router + top-6 + six SwiGLU experts + weighted combine per token,
+    as the reference runs a decode step).  The experts the sample routes to
+    are generated once, outside any timing."""
+
+    N_TOK, N_LAY = 4, 2
+
+    def __init__(self, a, threads: int):
+        import oracle as O
+
+        self.O, self.a, self.threads = O, a, threads
+        O.set_threads(threads)
+        H, I, E, K = a.hidden, a.inter, a.experts, a.top_k
+        self.x = O.gen_hidden(a.seed, self.N_TOK, H)
+        self.routers, self.experts = [], {}
+        for layer in range(self.N_LAY):
+            wr = O.gen_router(a.seed, layer, E, H)
+            idx, _, _, _ = O.route(O.router_logits(wr, self.x), K, None, 1)
+            self.routers.append(wr)
+            for e in set(idx.ravel().tolist()):
+                self.experts[(layer, e)] = O.gen_nvfp4_expert(a.seed, layer, e, I, H)
+
+    def run_once(self) -> int:
+        """One pass over the sample; returns the token-layers computed."""
+        import numpy as np
+        O, a = self.O, self.a
+        for layer in range(self.N_LAY):
+            wr = self.routers[layer]
+            for t in range(self.N_TOK):
+                xt = np.ascontiguousarray(self.x[t])
+                idx, wt, _, _ = O.route(O.router_logits(wr, xt), a.top_k, None, 1)
+                out = np.zeros(a.hidden, dtype=np.float32)
+                for k in range(a.top_k):
+                    O.axpy(out, wt[0, k], self.experts[(layer, int(idx[0, k]))].forward(xt))
+        return self.N_LAY * self.N_TOK
+
+    def measure(self, seconds: float):
+        """(tokens/s of the full stack, seconds, token-layers) over repeated passes."""
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            n += self.run_once()
+            if time.perf_counter() - t0 >= seconds:
+                break
+        dt = time.perf_counter() - t0
+        return 1.0 / (self.a.layers * dt / n), dt, n
+
+    def describe(self, dt, n):
+        return (f"oracle C restatement of the reference CPU path, {self.threads} threads: "
+                f"{n} token-layers ({self.N_TOK} tokens x {self.N_LAY} layers, repeated) in "
+                f"{dt:.1f} s, scaled to the {self.a.layers}-layer stack")
+
+
+def run_reference(a):
+    """--impl reference: the reference's CPU algorithm (the oracle port; the
+    Rust reference cannot be built here) timed on this host's cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    sample = CpuSample(a, threads)
+    vals, tot_dt, tot_n = [], 0.0, 0
+    for i in range(a.warmup + a.steps):
+        v, dt, n = sample.measure(0.0)  # one pass over the sample per step
+        if i >= a.warmup:
+            vals.append(v)
+            tot_dt += dt
+            tot_n += n
+    value = statistics.median(vals)
+    desc = sample.describe(tot_dt, tot_n)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": a.tokens / value * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": base_config(a, a.gpus, a.layers),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock/throttle samples of one GPU while running."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id: str):
+        self.bus_id = bus_id
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", self.bus_id], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                smax = float(f[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------- GPU arm
+def run_ours(a):
+    import torch
+
+    import ffn_b200 as F
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    H, I, E, K, T, L = a.hidden, a.inter, a.experts, a.top_k, a.tokens, a.layers
+    assert E % world == 0, "experts must divide evenly over the ranks"
+    e_loc = E // world
+    e_lo = rank * e_loc
+    ebytes = EXPERT_BYTES(H, I)
+    layer_bytes = e_loc * ebytes
+    free, _ = torch.cuda.mem_get_info(dev)
+    reserve = 4 << 30
+    resident = max(1, min(L, (free - reserve - L * E * H * 4) // layer_bytes))
+    if a.max_resident:
+        resident = min(resident, a.max_resident)
+    if world > 1:  # every rank streams the same layer schedule
+        t = torch.tensor([resident], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        resident = int(t.item())
+
+    # ---- weights: one buffer per resident layer, carved per matrix
+    n1, n1s = I * H // 2, I * H // 16
+    tables = []
+    buffers = []
+    for lay in range(resident):
+        buf = torch.empty(layer_bytes, dtype=torch.uint8, device=dev)
+        buffers.append(buf)
+        experts = [None] * E
+        off = 0
+        for j in range(e_loc):
+            e = e_lo + j
+            mats = []
+            for tag, (r, c) in zip((F.TAG_W1, F.TAG_W3, F.TAG_W2), ((I, H), (I, H), (H, I))):
+                w = buf.narrow(0, off, n1)
+                s = buf.narrow(0, off + n1, n1s)
+                off += n1 + n1s
+                F.check(F.lib().ffn_b200_gen_nvfp4(F.path_key(a.seed, lay, e, tag), r, c,
+                                                   w.data_ptr(), s.data_ptr(), F._stream()),
+                        "gen_nvfp4")
+                mats.append(F.Nvfp4Matrix(w, s, 1.0, r, c))
+            experts[e] = F.SwigluExpert(F.FMT_NVFP4, mats, I, H)
+        tables.append((experts, F.expert_table(experts, dev)))
+    routers = [F.gen_normal(F.path_key(a.seed, lay, 0, F.TAG_ROUTER), E * H, 0.02).view(E, H)
+               for lay in range(L)]
+    ws = F.Workspace(dev)
+    layers = [F.MoeLayer(tables[lay % resident][0], routers[lay], H, I, top_k=K,
+                         score_fn=F.SCORE_SIGMOID, expert_range=(e_lo, e_lo + e_loc),
+                         table=tables[lay % resident][1], ws=ws) for lay in range(L)]
+    x0 = F.gen_normal(F.path_key(a.seed, 0, 0, F.TAG_X), T * H).view(T, H)
+    xa = torch.empty_like(x0)
+    xb = torch.empty_like(x0)
+    topk = [torch.empty(T, K, dtype=torch.int32, device=dev) for _ in range(L)]
+    torch.cuda.synchronize()
+
+    def stack(x_in, capture=False):
+        cur, nxt = x_in, xb if x_in is not xb else xa
+        for lay in range(L):
+            layers[lay].forward(cur, out=nxt, residual=cur if rank == 0 else None,
+                                topk_idx=topk[lay] if capture else None)
+            if world > 1:
+                dist.all_reduce(nxt)
+            cur, nxt = nxt, cur
+        return cur
+
+    def step():
+        xa.copy_(x0)
+        return stack(xa)
+
+    # routing of the (deterministic) step -> experts hit per layer on this rank
+    xa.copy_(x0)
+    stack(xa, capture=True)
+    torch.cuda.synchronize()
+    u_loc = []
+    for lay in range(L):
+        ids = torch.unique(topk[lay])
+        u_loc.append(int(((ids >= e_lo) & (ids < e_lo + e_loc)).sum().item()))
+    gateup_bytes_step = sum(u * 2 * (n1 + n1s) for u in u_loc)
+    weight_bytes_step = sum(u * ebytes for u in u_loc)
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(_bus_id(dev, local))
+    if rank == 0:
+        clocks.start()
+        time.sleep(0.3)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    F.profile_enable(True)
+    n0 = F.launch_count()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for _ in range(a.steps):
+        step()
+    t_end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    launches = F.launch_count() - n0
+    F.profile_enable(False)
+    prof = F.profile_read()
+    clk = clocks.stop() if rank == 0 else None
+    ms = t_start.elapsed_time(t_end)
+    tt = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = float(tt.item())
+    ms_step = ms / a.steps
+    value = T * a.steps / (ms * 1e-3)
+
+    # ---- end to end through the public API with host buffers
+    x_host = x0.cpu().pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    for i in range(a.warmup + a.steps):
+        if i == a.warmup:
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            e_start = torch.cuda.Event(enable_timing=True)
+            e_end = torch.cuda.Event(enable_timing=True)
+            e_start.record()
+        xa.copy_(x_host, non_blocking=True)
+        y = stack(xa)
+        if rank == 0:
+            out_host.copy_(y, non_blocking=True)
+    e_end.record()
+    torch.cuda.synchronize()
+    e_ms = e_start.elapsed_time(e_end)
+    te = torch.tensor([e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e = T * a.steps / (float(te.item()) * 1e-3)
+
+    # ---- roofline of the dominant kernel (gate/up NVFP4 GEMV), live event timing
+    gu_ms, gu_n = prof.get("gateup_nvfp4", (0.0, 0))
+    peaks = _peaks()
+    achieved = gateup_bytes_step * a.steps / (gu_ms * 1e-3) / 1e9 if gu_ms else None
+    traffic = _traffic_per_launch(gateup_bytes_step / L)
+    roof = {"bound": "hbm", "kernel": "phase_kernel<NVFP4, gate+up>",
+            "achieved": achieved, "peak": peaks[0], "unit": "GB/s",
+            "frac": achieved / peaks[0] if achieved else None, "traffic": traffic,
+            "peak_source": peaks[1],
+            "algorithmic_bytes_per_launch": gateup_bytes_step / L,
+            "launches": gu_n, "avg_launch_us": gu_ms * 1e3 / gu_n if gu_n else None}
+    kernels = {k: {"ms": round(v[0], 3), "launches": v[1]} for k, v in prof.items()}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        sample = CpuSample(a, threads)
+        cv, dt, n = sample.measure(a.cpu_seconds)
+        cpu = {"value": cv, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": sample.describe(dt, n)}
+
+    if rank == 0:
+        cfg = base_config(a, world, resident)
+        cfg["experts_hit_per_layer_rank0"] = u_loc
+        cfg["weight_bytes_per_step_rank0"] = weight_bytes_step
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "nvfp4 weights x f16x2 split activations, f32 accumulate",
+            "data": "synthetic (seeded random-init weights and N(0,1) hidden states)",
+            "config": cfg,
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": T * H * 4,
+                    "d2h_bytes_per_step": T * H * 4},
+            "gpu_launches": launches,
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+            "kernels": kernels,
+            "hbm_weight_gbs_rank0": weight_bytes_step / (ms_step * 1e-3) / 1e9,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def _bus_id(dev, local):
+    """nvidia-smi -i selector of this rank's GPU (its UUID when torch knows it)."""
+    import torch
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        if uuid:
+            return uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    except Exception:
+        pass
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        return vis.split(",")[local]
+    return str(local)
+
+
+def _peaks():
+    try:
+        d = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback (6.65 TB/s)"
+
+
+def _traffic_per_launch(alg_bytes_per_launch):
+    """DRAM bytes per launch of the gate/up kernel from the committed ncu
+    summary (profiles/gateup_nvfp4.json: measured traffic / algorithmic bytes
+    of the captured launch), scaled to this launch's algorithmic bytes."""
+    try:
+        d = json.load(open(os.path.join(ROOT, "profiles", "gateup_nvfp4.json")))
+        return alg_bytes_per_launch * float(d["traffic_over_algorithmic"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+def main():
+    a = parse_args()
+    if a.impl == "reference":
+        return run_reference(a)
+    return run_ours(a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

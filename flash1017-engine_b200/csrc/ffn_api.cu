@@ -559,6 +559,7 @@ int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
 int ffn_b200_gen_nvfp4(uint64_t key, size_t rows, size_t cols, uint8_t *w, uint8_t *s,
                        void *stream) {
   if (!w || !s || cols % 16) return fail(FFN_B200_EINVAL, "gen_nvfp4: bad arguments");
+  if ((uintptr_t)w % 8) return fail(FFN_B200_EINVAL, "gen_nvfp4: w must be 8-byte aligned");
   return launch_gen_nvfp4(ffn_b200_key(key, 1), ffn_b200_key(key, 2), rows, cols, w, s,
                           (cudaStream_t)stream);
 }

@@ -629,6 +629,14 @@ __device__ __forceinline__ float normal_at(uint64_t key, uint64_t i) {
   }
   return __fmul_rn((float)(s - 393210), 1.0f / 65536.0f);
 }
+// |N(0,1)| stand-in for block scales: Irwin-Hall sum of the four 16-bit
+// uniforms of one draw, scaled to unit variance (same arithmetic as the oracle).
+__device__ __forceinline__ float normal4_at(uint64_t key, uint64_t i) {
+  const uint64_t r = rnd(key, i);
+  const long long s = (long long)(r & 0xFFFF) + (long long)((r >> 16) & 0xFFFF) +
+                      (long long)((r >> 32) & 0xFFFF) + (long long)(r >> 48);
+  return __fmul_rn((float)(s - 131070), 1.0f / 37837.227f);
+}
 __device__ __forceinline__ float unit_at(uint64_t key, uint64_t i) {
   return __fmul_rn((float)(uint32_t)(rnd(key, i) >> 40), 1.0f / 16777216.0f);
 }
@@ -654,13 +662,17 @@ __device__ __forceinline__ uint8_t f32_to_e4m3(float f) {
   return (uint8_t)(sign | enc);
 }
 
+// One 64-bit draw per 8 weight bytes (little-endian), one per scale byte.
 __global__ void gen_nvfp4_kernel(uint64_t kw, uint64_t ks, size_t nb, size_t ns, uint8_t *w,
                                  uint8_t *s) {
   const size_t stride = (size_t)gridDim.x * blockDim.x;
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nb; i += stride)
-    w[i] = (uint8_t)(rnd(kw, i) & 0xFF);
+  const size_t n8 = nb / 8;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += stride)
+    reinterpret_cast<uint64_t *>(w)[i] = rnd(kw, i);
+  for (size_t i = n8 * 8 + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nb; i += stride)
+    w[i] = (uint8_t)(rnd(kw, i >> 3) >> (8 * (i & 7)));
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < ns; i += stride)
-    s[i] = f32_to_e4m3(__fdiv_rn(fabsf(normal_at(ks, i)), 6.0f));
+    s[i] = f32_to_e4m3(__fdiv_rn(fabsf(normal4_at(ks, i)), 6.0f));
 }
 
 __global__ void gen_ternary_kernel(uint64_t kp, uint64_t kr, size_t nbytes, size_t rows,

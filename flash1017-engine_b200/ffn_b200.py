@@ -383,18 +383,22 @@ class MoeLayer:
     """Routed SwiGLU MoE layer over device-resident experts."""
 
     def __init__(self, experts, router_w, hidden, inter, top_k=6, score_fn=SCORE_SIGMOID,
-                 router_bias=None, router_mode=ROUTER_EXACT, expert_range=None, device="cuda"):
+                 router_bias=None, router_mode=ROUTER_EXACT, expert_range=None, device="cuda",
+                 table=None, ws=None):
         self.experts = experts  # SwigluExpert list (None allowed outside expert_range)
         self.router_w = router_w
         self.router_bias = router_bias
         self.hidden, self.inter, self.top_k = hidden, inter, top_k
         n = len(experts)
-        self.table, fmts = expert_table(experts, device)
+        if table is None:
+            self.table, fmts = expert_table(experts, device)
+        else:  # a shared (table, formats) pair
+            self.table, fmts = table
         lo, hi = expert_range if expert_range else (0, n)
         self.desc = MoeDesc(hidden, inter, n, top_k, _ptr(self.table), _ptr(router_w),
                             _ptr(router_bias), score_fn, router_mode, lo, hi,
                             int(FMT_NVFP4 in fmts or not fmts), int(FMT_TERNARY in fmts))
-        self.ws = Workspace(device)
+        self.ws = ws if ws is not None else Workspace(device)
 
     def ws_bytes(self, n_tok: int) -> int:
         return int(lib().ffn_b200_moe_ws_bytes(C.byref(self.desc), n_tok))

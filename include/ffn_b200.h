@@ -153,7 +153,8 @@ FFN_B200_EXPORT int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok,
 
 /* ----------------------------------------------- seeded synthetic weights
  * Counter-based generators (SplitMix64 finaliser + Irwin-Hall normals +
- * round-to-nearest-even E4M3), byte-identical to the CPU oracle's. */
+ * round-to-nearest-even E4M3), byte-identical to the CPU oracle's.  NVFP4 w
+ * must be 8-byte aligned. */
 FFN_B200_EXPORT uint64_t ffn_b200_key(uint64_t parent, uint64_t v);
 FFN_B200_EXPORT int ffn_b200_gen_nvfp4(uint64_t key, size_t rows, size_t cols, uint8_t *w,
                                        uint8_t *s, void *stream);

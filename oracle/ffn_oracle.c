@@ -459,13 +459,23 @@ ORC_API uint8_t orc_f32_to_e4m3(float f) {
     return (uint8_t)(sign | enc);
 }
 
-/* NVFP4 matrix [rows, cols]: E2M1 codes uniform over all 16 values (two per
- * byte, one 64-bit draw per byte), E4M3 scales RNE(|N(0,1)|/6). */
+/* |N(0,1)| stand-in for block scales: Irwin-Hall sum of the four 16-bit
+ * uniforms of one 64-bit draw, centred and scaled to unit variance by one
+ * exactly rounded multiplication. */
+static inline float normal4_at(uint64_t key, uint64_t i) {
+    uint64_t r = rnd(key, i);
+    int64_t s = (int64_t)(r & 0xFFFF) + (int64_t)((r >> 16) & 0xFFFF) +
+                (int64_t)((r >> 32) & 0xFFFF) + (int64_t)(r >> 48);
+    return (float)(s - 131070) * (1.0f / 37837.227f);
+}
+
+/* NVFP4 matrix [rows, cols]: E2M1 codes uniform over all 16 values (one 64-bit
+ * draw gives 8 packed bytes, little-endian), E4M3 scales RNE(|N(0,1)|/6). */
 ORC_API void orc_gen_nvfp4(uint64_t key, size_t rows, size_t cols, uint8_t *w, uint8_t *s) {
     uint64_t kw = orc_derive(key, 1), ks = orc_derive(key, 2);
     size_t nb = rows * cols / 2, ns = rows * cols / 16;
-    for (size_t i = 0; i < nb; ++i) w[i] = (uint8_t)(rnd(kw, i) & 0xFF);
-    for (size_t i = 0; i < ns; ++i) s[i] = orc_f32_to_e4m3(fabsf(normal_at(ks, i)) / 6.0f);
+    for (size_t i = 0; i < nb; ++i) w[i] = (uint8_t)(rnd(kw, i >> 3) >> (8 * (i & 7)));
+    for (size_t i = 0; i < ns; ++i) s[i] = orc_f32_to_e4m3(fabsf(normal4_at(ks, i)) / 6.0f);
 }
 
 /* Ternary matrix [rows, cols]: codes P(-1,0,+1) = (.3,.4,.3), four per byte in

@@ -2,8 +2,10 @@
 """bench.py -- MoE expert-FFN tokens/s on 1/2/4/8 B200.
 
 Workload: a 40-layer NVFP4 MoE-FFN stack (hidden 4096, intermediate 2048, 384
-routed SwiGLU experts per layer, fp32 router N(0, 0.02), sigmoid top-6 with
-renormalised weights, residual add between layers), one decode step of 256
+routed SwiGLU experts per layer, the reference's ffn_norm RMSNorm on the layer
+input (weights 1, eps 1e-20, flash1017.rs:7637), fp32 router N(0, 0.02) on the
+tensor cores, sigmoid top-6 with renormalised weights, residual add between
+layers), one decode step of 256
 tokens, seed 4, random-init weights from the library's seeded generator.
 Experts are sharded expert-parallel: rank r of N owns experts
 [r*384/N, (r+1)*384/N) of every layer; every rank routes all tokens (the
@@ -70,7 +72,9 @@ def base_config(a, world, resident):
         "workload": "config4: 40-layer NVFP4 MoE-FFN stack, 256-token decode, top-6 of 384, "
                     "expert-parallel",
         "hidden": a.hidden, "inter": a.inter, "experts": a.experts, "top_k": a.top_k,
-        "layers": a.layers, "tokens": a.tokens, "seed": a.seed, "router": "fp32 exact, sigmoid",
+        "layers": a.layers, "tokens": a.tokens, "seed": a.seed,
+        "router": "fp32 weights, tensor-core split-f16 (about fp32 accurate), sigmoid top-k",
+        "ffn_norm": "RMSNorm, weight 1, eps 1e-20",
         "resident_layers": resident, "parallelism": f"ep{world}",
         "l2": "no flush: every layer-step streams >= 2.6 GB of expert weights (> 126 MB L2)",
     }
@@ -80,23 +84,27 @@ def base_config(a, world, resident):
 class CpuSample:
     """The oracle (C restatement of the reference's Rayon CPU path) on a
     bounded sample of the workload: the first 4 tokens through the first 2
-    layers (router + top-6 + six SwiGLU experts + weighted combine per token,
-    as the reference runs a decode step).  The experts the sample routes to
+    layers (ffn_norm + router + top-6 + six SwiGLU experts + weighted combine
+    per token, as the reference runs a decode step).  The experts the sample routes to
     are generated once, outside any timing."""
 
     N_TOK, N_LAY = 4, 2
 
     def __init__(self, a, threads: int):
+        import numpy as np
+
         import oracle as O
 
         self.O, self.a, self.threads = O, a, threads
         O.set_threads(threads)
         H, I, E, K = a.hidden, a.inter, a.experts, a.top_k
         self.x = O.gen_hidden(a.seed, self.N_TOK, H)
+        self.norm_w = np.ones(H, dtype=np.float32)
         self.routers, self.experts = [], {}
+        xn = O.rms_norm(self.x, self.norm_w)
         for layer in range(self.N_LAY):
             wr = O.gen_router(a.seed, layer, E, H)
-            idx, _, _, _ = O.route(O.router_logits(wr, self.x), K, None, 1)
+            idx, _, _, _ = O.route(O.router_logits(wr, xn), K, None, 1)
             self.routers.append(wr)
             for e in set(idx.ravel().tolist()):
                 self.experts[(layer, e)] = O.gen_nvfp4_expert(a.seed, layer, e, I, H)
@@ -108,7 +116,7 @@ class CpuSample:
         for layer in range(self.N_LAY):
             wr = self.routers[layer]
             for t in range(self.N_TOK):
-                xt = np.ascontiguousarray(self.x[t])
+                xt = O.rms_norm(np.ascontiguousarray(self.x[t])[None, :], self.norm_w)[0]
                 idx, wt, _, _ = O.route(O.router_logits(wr, xt), a.top_k, None, 1)
                 out = np.zeros(a.hidden, dtype=np.float32)
                 for k in range(a.top_k):
@@ -273,9 +281,11 @@ def run_ours(a):
     routers = [F.gen_normal(F.path_key(a.seed, lay, 0, F.TAG_ROUTER), E * H, 0.02).view(E, H)
                for lay in range(L)]
     ws = F.Workspace(dev)
+    norm_w = torch.ones(H, dtype=torch.float32, device=dev)
     layers = [F.MoeLayer(tables[lay % resident][0], routers[lay], H, I, top_k=K,
                          score_fn=F.SCORE_SIGMOID, expert_range=(e_lo, e_lo + e_loc),
-                         table=tables[lay % resident][1], ws=ws) for lay in range(L)]
+                         table=tables[lay % resident][1], ws=ws, norm_w=norm_w,
+                         norm_eps=1e-20, router_mode=F.ROUTER_TENSOR) for lay in range(L)]
     x0 = F.gen_normal(F.path_key(a.seed, 0, 0, F.TAG_X), T * H).view(T, H)
     xa = torch.empty_like(x0)
     xb = torch.empty_like(x0)

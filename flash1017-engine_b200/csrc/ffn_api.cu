@@ -397,6 +397,7 @@ int ffn_b200_expert_forward(size_t inter, size_t hidden, size_t seq, const ffn_b
 // ---------------------------------------------------------------- MoE layer
 struct MoeWs {
   __half *xh, *xl, *th, *tl;
+  float *xn;
   int *xe;
   float *logits;
   int32_t *idx, *inv, *pair_tok;
@@ -411,8 +412,10 @@ struct MoeWs {
 static MoeWs carve_moe(Carve &c, const ffn_b200_moe_desc &d, size_t T) {
   MoeWs w{};
   const size_t H = d.hidden, I = d.inter, E = d.n_experts, k = d.top_k, P = T * k;
-  if (d.has_nvfp4) { w.xh = c.take<__half>(T * H); w.xl = c.take<__half>(T * H); }
+  w.xh = c.take<__half>(T * H);  // natural order: NVFP4 experts and the tensor router
+  w.xl = c.take<__half>(T * H);
   if (d.has_ternary) { w.th = c.take<__half>(T * H); w.tl = c.take<__half>(T * H); }
+  w.xn = d.norm_w ? c.take<float>(T * H) : nullptr;
   w.xe = c.take<int>(T);
   w.logits = c.take<float>(T * E);
   w.idx = c.take<int32_t>(P);
@@ -454,8 +457,8 @@ int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
     return fail(FFN_B200_EINVAL, "moe_layer: bad expert range");
   if (d->score_fn != FFN_B200_SCORE_REF_SQRTSOFTPLUS && d->score_fn != FFN_B200_SCORE_SIGMOID)
     return fail(FFN_B200_EINVAL, "moe_layer: unknown score_fn");
-  if (d->router_mode != FFN_B200_ROUTER_EXACT)
-    return fail(FFN_B200_EUNSUP, "moe_layer: only FFN_B200_ROUTER_EXACT is implemented");
+  if (d->router_mode != FFN_B200_ROUTER_EXACT && d->router_mode != FFN_B200_ROUTER_TENSOR)
+    return fail(FFN_B200_EINVAL, "moe_layer: unknown router_mode");
   if (n_tok == 0) return 0;
   if (!x || !out) return fail(FFN_B200_EINVAL, "moe_layer: null x/out");
   if (n_tok * k > (1u << 24)) return fail(FFN_B200_EINVAL, "moe_layer: too many tokens");
@@ -466,10 +469,13 @@ int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
   MoeWs w = carve_moe(c, *d, n_tok);
   const int T = (int)n_tok, P = (int)(n_tok * k);
   int rc;
-  if ((rc = launch_xprep(x, (int)H, T, (int)H, w.xh, w.xl, w.th, w.tl, (int)H, w.xe, st)))
+  const bool exact = d->router_mode == FFN_B200_ROUTER_EXACT;
+  if ((rc = launch_xprep(x, (int)H, T, (int)H, w.xh, w.xl, w.th, w.tl, (int)H, w.xe, st,
+                         d->norm_w, d->norm_eps, exact ? 1 : 0, w.xn)))
     return rc;
-  if ((rc = launch_router(d->router_w, d->router_bias, x, T, (int)E, (int)H, (int)k, d->score_fn,
-                          w.logits, w.idx, w.wt, st)))
+  const float *xin = d->norm_w ? w.xn : x;  // what the router and the experts see
+  if ((rc = launch_router(d->router_w, d->router_bias, xin, w.xh, w.xl, w.xe, d->router_mode, T,
+                          (int)E, (int)H, (int)k, d->score_fn, w.logits, w.idx, w.wt, st)))
     return rc;
   if ((rc = launch_group(w.idx, T, (int)k, (int)E, d->expert_begin, d->expert_end, d->experts,
                          w.ints, w.pair_tok, w.inv, w.vexp_nv, w.vexp_tn, w.n_vexp, st)))
@@ -492,7 +498,7 @@ int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
       z.K = (int)H;
       z.mat0 = 0;
       z.nmat = 2;
-      z.xf = x;
+      z.xf = xin;
       z.ld_xf = (int)H;
       z.pair_tok = w.pair_tok;
       z.z = w.z;

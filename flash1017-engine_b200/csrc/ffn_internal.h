@@ -49,13 +49,15 @@ struct CoreZArgs {
 
 int rows_per_tile(int phase);
 int launch_xprep(const float *x, int ld_x, int rows, int K, __half *nh, __half *nl, __half *th,
-                 __half *tl, int ld_o, int *xe, cudaStream_t st);
+                 __half *tl, int ld_o, int *xe, cudaStream_t st, const float *norm_w = nullptr,
+                 float norm_eps = 0.f, int seq_norm = 0, float *xn = nullptr);
 int launch_phase(int fmt, int phase, const PhaseArgs &a, int grid, cudaStream_t st);
 int launch_corez(const CoreZArgs &a, int max_vexp, cudaStream_t st);
 int launch_exact_matvec(const float *w32, const uint16_t *w16, const float *x, int n_tok,
                         int rows, int H, float *out, cudaStream_t st);
-int launch_router(const float *w, const float *bias, const float *x, int n_tok, int n_exp,
-                  int H, int top_k, int score_fn, float *logits, int32_t *idx, float *wt,
+int launch_router(const float *w, const float *bias, const float *x, const __half *xh,
+                  const __half *xl, const int *xe, int mode, int n_tok, int n_exp, int H,
+                  int top_k, int score_fn, float *logits, int32_t *idx, float *wt,
                   cudaStream_t st);
 int launch_group(const int32_t *idx, int n_tok, int top_k, int n_exp, int e_begin, int e_end,
                  const ffn_b200_expert *experts, int *ws_int, int32_t *pair_tok, int32_t *inv,

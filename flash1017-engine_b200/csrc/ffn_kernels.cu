@@ -13,17 +13,56 @@
 namespace ffn {
 
 // ============================================================ activations
-// One CTA per row: x (f32) -> hi/lo f16 of x * 2^-e, e = floor(log2 max|x|) - 14,
-// in natural column order (NVFP4 consumers) and/or pair order (ternary).
+// One CTA per row.  Optionally RMS-normalises the row first (flash1017.rs:
+// 4880-4891: inv = 1 / sqrt(sum(x^2) / n + eps), xn = x * inv * w; with
+// seq_norm the sum of squares is taken sequentially in column order, the
+// reference's order, so xn is bit-identical to the CPU's), writes xn (f32) when
+// asked, then splits x (or xn) into hi/lo f16 of x * 2^-e with
+// e = floor(log2 max|x|) - 14, in natural column order (NVFP4 consumers)
+// and/or pair order (ternary consumers).
 __global__ void __launch_bounds__(256) xprep_kernel(const float *__restrict__ x, int ld_x, int K,
                                                     __half *nh, __half *nl, __half *th,
-                                                    __half *tl, int ld_o, int *xe) {
+                                                    __half *tl, int ld_o, int *xe,
+                                                    const float *__restrict__ norm_w,
+                                                    float norm_eps, int seq_norm, float *xn) {
   const int row = blockIdx.x;
   const float *xr = x + (size_t)row * ld_x;
   __shared__ float red[32];
+  __shared__ float s_inv;
+  float inv = 1.0f;
+  if (norm_w) {
+    if (seq_norm) {
+      if (threadIdx.x == 0) {
+        float ss = 0.f;
+        for (int c = 0; c < K; ++c) ss = __fadd_rn(ss, __fmul_rn(xr[c], xr[c]));
+        s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), norm_eps)));
+      }
+    } else {
+      float ss = 0.f;
+      for (int c = threadIdx.x; c < K; c += blockDim.x) ss = fmaf(xr[c], xr[c], ss);
+      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+        s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), norm_eps)));
+      }
+    }
+    __syncthreads();
+    inv = s_inv;
+  }
   float amax = 0.f;
-  for (int c = threadIdx.x; c < K; c += blockDim.x) amax = fmaxf(amax, fabsf(xr[c]));
+  for (int c = threadIdx.x; c < K; c += blockDim.x) {
+    float v = xr[c];
+    if (norm_w) {
+      v = __fmul_rn(__fmul_rn(v, inv), norm_w[c]);
+      if (xn) xn[(size_t)row * K + c] = v;
+    }
+    amax = fmaxf(amax, fabsf(v));
+  }
   for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  __syncthreads();
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
   __syncthreads();
   if (threadIdx.x < 32) {
@@ -42,8 +81,10 @@ __global__ void __launch_bounds__(256) xprep_kernel(const float *__restrict__ x,
   const float sc = pow2f(-e);
   const size_t o = (size_t)row * ld_o;
   for (int c = threadIdx.x; c < K; c += blockDim.x) {
+    float v = xr[c];
+    if (norm_w) v = __fmul_rn(__fmul_rn(v, inv), norm_w[c]);
     __half hi, lo;
-    split_f16(xr[c] * sc, hi, lo);
+    split_f16(v * sc, hi, lo);
     if (nh) { nh[o + c] = hi; nl[o + c] = lo; }
     if (th) { const int p = tern_pos(c); th[o + p] = hi; tl[o + p] = lo; }
   }
@@ -51,9 +92,12 @@ __global__ void __launch_bounds__(256) xprep_kernel(const float *__restrict__ x,
 }
 
 int launch_xprep(const float *x, int ld_x, int rows, int K, __half *nh, __half *nl, __half *th,
-                 __half *tl, int ld_o, int *xe, cudaStream_t st) {
+                 __half *tl, int ld_o, int *xe, cudaStream_t st, const float *norm_w,
+                 float norm_eps, int seq_norm, float *xn) {
   if (rows <= 0) return 0;
-  FFN_LAUNCH(FFN_B200_K_XPREP, st, "xprep_kernel", xprep_kernel<<<rows, 256, 0, st>>>(x, ld_x, K, nh, nl, th, tl, ld_o, xe));
+  FFN_LAUNCH(FFN_B200_K_XPREP, st, "xprep_kernel",
+             xprep_kernel<<<rows, 256, 0, st>>>(x, ld_x, K, nh, nl, th, tl, ld_o, xe, norm_w,
+                                                norm_eps, seq_norm, xn));
   return 0;
 }
 
@@ -333,6 +377,101 @@ int launch_exact_matvec(const float *w32, const uint16_t *w16, const float *x, i
   return 0;
 }
 
+// TENSOR: logits[t][e] = sum_c w[e][c] x[t][c] on the tensor cores.  The f32
+// router weights are split into f16 hi/lo pairs as they are loaded; x enters
+// as the hi/lo halves of the per-token normalised row (xprep); three MMAs per
+// k-step (wh*xh + wh*xl + wl*xh) leave an error of about 2^-22 relative.  The
+// summation order differs from the CPU loop, so selections can differ from the
+// reference's only where two biased scores are within that error.
+// CTA = 32 experts x 32 tokens; the 8 warps split K; shared-memory reduction.
+__global__ void __launch_bounds__(256) router_tc_kernel(const float *__restrict__ w,
+                                                        const __half *__restrict__ xh,
+                                                        const __half *__restrict__ xl,
+                                                        const int *__restrict__ xe, int n_tok,
+                                                        int n_exp, int H,
+                                                        float *__restrict__ logits) {
+  __shared__ float red[kWarps][32][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int e0 = blockIdx.x * 32, t0 = blockIdx.y * 32;
+  float acc[2][4][4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[i][j][q] = 0.f;
+  const float *wa[2], *wb[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    wa[i] = w + (size_t)min(e0 + 16 * i + g, n_exp - 1) * H;
+    wb[i] = w + (size_t)min(e0 + 16 * i + g + 8, n_exp - 1) * H;
+  }
+  const __half *ph[4], *pl[4];
+  bool tv[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int tok = t0 + 8 * j + g;
+    tv[j] = tok < n_tok;
+    ph[j] = xh + (size_t)min(tok, n_tok - 1) * H;
+    pl[j] = xl + (size_t)min(tok, n_tok - 1) * H;
+  }
+  for (int ks = warp; ks < H / 16; ks += kWarps) {
+    const int c = ks * 16 + 4 * t;
+    uint32_t ah[2][4], al[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float4 va = __ldg(reinterpret_cast<const float4 *>(wa[i] + c));
+      const float4 vb = __ldg(reinterpret_cast<const float4 *>(wb[i] + c));
+      __half h[8], l[8];
+      const float v[8] = {va.x, va.y, vb.x, vb.y, va.z, va.w, vb.z, vb.w};
+#pragma unroll
+      for (int q = 0; q < 8; ++q) split_f16(v[q], h[q], l[q]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        __half2 hh = __halves2half2(h[2 * q], h[2 * q + 1]);
+        __half2 ll = __halves2half2(l[2 * q], l[2 * q + 1]);
+        ah[i][q] = *reinterpret_cast<uint32_t *>(&hh);
+        al[i][q] = *reinterpret_cast<uint32_t *>(&ll);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint2 bh = make_uint2(0, 0), bl = make_uint2(0, 0);
+      if (tv[j]) {
+        bh = __ldg(reinterpret_cast<const uint2 *>(ph[j] + c));
+        bl = __ldg(reinterpret_cast<const uint2 *>(pl[j] + c));
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        mma_f16(acc[i][j], ah[i][0], ah[i][1], ah[i][2], ah[i][3], bh.x, bh.y);
+        mma_f16(acc[i][j], ah[i][0], ah[i][1], ah[i][2], ah[i][3], bl.x, bl.y);
+        mma_f16(acc[i][j], al[i][0], al[i][1], al[i][2], al[i][3], bh.x, bh.y);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r0 = 16 * i + g, c0 = 8 * j + 2 * t;
+      red[warp][r0][c0] = acc[i][j][0];
+      red[warp][r0][c0 + 1] = acc[i][j][1];
+      red[warp][r0 + 8][c0] = acc[i][j][2];
+      red[warp][r0 + 8][c0 + 1] = acc[i][j][3];
+    }
+  __syncthreads();
+  for (int q = threadIdx.x; q < 32 * 32; q += blockDim.x) {
+    const int el = q & 31, tl = q >> 5;
+    const int e = e0 + el, tok = t0 + tl;
+    if (e >= n_exp || tok >= n_tok) continue;
+    float s = 0.f;
+#pragma unroll
+    for (int wv = 0; wv < kWarps; ++wv) s += red[wv][el][tl];
+    logits[(size_t)tok * n_exp + e] = s * pow2f(xe[tok]);
+  }
+}
+
 // Top-k per token, one warp per token (flash1017.rs:7280-7376).  Ties in the
 // biased score are broken by the lower expert index.
 __device__ __forceinline__ float score_of(float l, int fn) {
@@ -388,11 +527,19 @@ __global__ void __launch_bounds__(256) topk_kernel(const float *__restrict__ log
   }
 }
 
-int launch_router(const float *w, const float *bias, const float *x, int n_tok, int n_exp,
-                  int H, int top_k, int score_fn, float *logits, int32_t *idx, float *wt,
+int launch_router(const float *w, const float *bias, const float *x, const __half *xh,
+                  const __half *xl, const int *xe, int mode, int n_tok, int n_exp, int H,
+                  int top_k, int score_fn, float *logits, int32_t *idx, float *wt,
                   cudaStream_t st) {
-  int rc = launch_exact_matvec(w, nullptr, x, n_tok, n_exp, H, logits, st);
-  if (rc) return rc;
+  if (mode == FFN_B200_ROUTER_EXACT) {
+    int rc = launch_exact_matvec(w, nullptr, x, n_tok, n_exp, H, logits, st);
+    if (rc) return rc;
+  } else {
+    dim3 g1((n_exp + 31) / 32, (n_tok + 31) / 32);
+    if (g1.y > 65535) return fail(FFN_B200_EINVAL, "router: too many tokens");
+    FFN_LAUNCH(FFN_B200_K_ROUTER, st, "router_tc_kernel",
+               router_tc_kernel<<<g1, 256, 0, st>>>(w, xh, xl, xe, n_tok, n_exp, H, logits));
+  }
   FFN_LAUNCH(FFN_B200_K_TOPK, st, "topk_kernel", topk_kernel<<<(n_tok + 7) / 8, 256, 0, st>>>(logits, bias, n_tok, n_exp, top_k, score_fn, idx,
                                                wt));
   return 0;

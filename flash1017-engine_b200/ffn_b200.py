@@ -74,7 +74,8 @@ class MoeDesc(C.Structure):
                 ("router_bias", C.c_void_p), ("score_fn", C.c_int32),
                 ("router_mode", C.c_int32), ("expert_begin", C.c_int32),
                 ("expert_end", C.c_int32), ("has_nvfp4", C.c_int32),
-                ("has_ternary", C.c_int32)]
+                ("has_ternary", C.c_int32), ("norm_w", C.c_void_p), ("norm_eps", C.c_float),
+                ("reserved", C.c_int32)]
 
 
 assert C.sizeof(Expert) == 224, C.sizeof(Expert)
@@ -384,10 +385,11 @@ class MoeLayer:
 
     def __init__(self, experts, router_w, hidden, inter, top_k=6, score_fn=SCORE_SIGMOID,
                  router_bias=None, router_mode=ROUTER_EXACT, expert_range=None, device="cuda",
-                 table=None, ws=None):
+                 table=None, ws=None, norm_w=None, norm_eps=1e-20):
         self.experts = experts  # SwigluExpert list (None allowed outside expert_range)
         self.router_w = router_w
         self.router_bias = router_bias
+        self.norm_w = norm_w
         self.hidden, self.inter, self.top_k = hidden, inter, top_k
         n = len(experts)
         if table is None:
@@ -397,7 +399,8 @@ class MoeLayer:
         lo, hi = expert_range if expert_range else (0, n)
         self.desc = MoeDesc(hidden, inter, n, top_k, _ptr(self.table), _ptr(router_w),
                             _ptr(router_bias), score_fn, router_mode, lo, hi,
-                            int(FMT_NVFP4 in fmts or not fmts), int(FMT_TERNARY in fmts))
+                            int(FMT_NVFP4 in fmts or not fmts), int(FMT_TERNARY in fmts),
+                            _ptr(norm_w), float(norm_eps), 0)
         self.ws = ws if ws is not None else Workspace(device)
 
     def ws_bytes(self, n_tok: int) -> int:

@@ -140,11 +140,18 @@ typedef struct ffn_b200_moe_desc {
     int32_t router_mode;             /* FFN_B200_ROUTER_* */
     int32_t expert_begin, expert_end;
     int32_t has_nvfp4, has_ternary;  /* which formats occur in experts[] */
+    /* Optional RMSNorm of the layer input before routing and the experts, the
+     * reference's ffn_norm (flash1017.rs:7637, 4880-4891): xn = x / sqrt(mean(x^2)
+     * + norm_eps) * norm_w.  NULL: the experts see x itself. */
+    const float *norm_w;             /* DEVICE [hidden] or NULL */
+    float norm_eps;
+    int32_t reserved;
 } ffn_b200_moe_desc;
 
 FFN_B200_EXPORT size_t ffn_b200_moe_ws_bytes(const ffn_b200_moe_desc *d, size_t max_tokens);
-/* x [n_tok, hidden] f32; out [n_tok, hidden] = residual + moe(x) when
- * residual != NULL, else moe(x) (residual may alias x or out).  topk_idx /
+/* x [n_tok, hidden] f32; out [n_tok, hidden] = residual + moe(xn) when
+ * residual != NULL, else moe(xn), with xn = x or its RMSNorm (norm_w); residual
+ * may alias x or out.  topk_idx /
  * topk_w [n_tok, top_k] receive the routing when non-NULL. */
 FFN_B200_EXPORT int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok,
                                        const float *x, const float *residual, float *out,

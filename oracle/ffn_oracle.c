@@ -283,6 +283,14 @@ ORC_API void orc_f32_matvec(size_t rows, size_t cols, const float *w, const floa
     }
 }
 
+/* F:4880-4891 flash1017_rms_norm: out = x * (1/sqrt(sum(x^2)/n + eps)) * w. */
+ORC_API void orc_rms_norm(size_t n, const float *x, const float *w, float eps, float *out) {
+    float sum_sq = 0.0f;
+    for (size_t i = 0; i < n; ++i) sum_sq += x[i] * x[i];
+    float inv_rms = 1.0f / sqrtf(sum_sq / (float)n + eps);
+    for (size_t i = 0; i < n; ++i) out[i] = x[i] * inv_rms * w[i];
+}
+
 /* ------------------------------------------------------------------------- */
 /* SwiGLU expert (F:7537-7547 NVFP4, F:7551-7561 ternary)                     */
 /* ------------------------------------------------------------------------- */

@@ -58,6 +58,7 @@ def lib() -> C.CDLL:
         L.orc_f32_matvec.argtypes = [sz, sz, vp, vp, vp]
         L.orc_swiglu.argtypes = [sz, vp, vp, f32, i32, vp]
         L.orc_axpy.argtypes = [sz, f32, vp, vp]
+        L.orc_rms_norm.argtypes = [sz, vp, vp, f32, vp]
         L.orc_nvfp4_expert.argtypes = [sz, sz, vp, vp, vp, vp, vp, vp]
         L.orc_ternary_expert.argtypes = [sz, sz, vp, vp, vp, f32, vp, vp, vp]
         L.orc_route.argtypes = [sz, sz, sz, vp, vp, i32, vp, vp, vp, vp]
@@ -194,6 +195,19 @@ def swiglu(g, u, proj_scale=1.0, scaled=False) -> np.ndarray:
     h = np.zeros_like(g, dtype=np.float32)
     lib().orc_swiglu(g.size, _p(g), _p(u), float(proj_scale), int(scaled), _p(h))
     return h
+
+
+def rms_norm(x, w, eps=1e-20) -> np.ndarray:
+    """flash1017.rs:4880-4891, row by row for 2-D x."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    out = np.empty_like(x)
+    for r in range(x.shape[0] if x.ndim == 2 else 1):
+        xr = x[r] if x.ndim == 2 else x
+        orow = out[r] if x.ndim == 2 else out
+        lib().orc_rms_norm(xr.size, _p(np.ascontiguousarray(xr)), _p(w), float(eps),
+                           orow.ctypes.data)
+    return out
 
 
 def axpy(dst, scale, src) -> None:
@@ -346,6 +360,25 @@ def route(logits: np.ndarray, top_k: int = 6, bias=None, score_fn: int = 1):
     return idx, wt, sc, bi
 
 
+def topk_agrees(idx, ref_idx, ref_biased_sorted, tol=1e-5):
+    """True per token when the selected set equals the reference's, or the
+    reference's k-th and (k+1)-th biased scores are within `tol` (a near-tie,
+    where a different summation order may legitimately pick either)."""
+    ok = []
+    for t in range(idx.shape[0]):
+        same = set(idx[t].tolist()) == set(ref_idx[t].tolist())
+        k = idx.shape[1]
+        tie = abs(ref_biased_sorted[t, k - 1] - ref_biased_sorted[t, k]) <= tol
+        ok.append(same or tie)
+    return np.array(ok)
+
+
+def biased_sorted(logits, k, bias=None, score_fn=1):
+    """The k+1 largest biased scores per token (for topk_agrees)."""
+    _, _, _, bi = route(logits, k + 1, bias, score_fn)
+    return bi
+
+
 def router_logits(wr: np.ndarray, x: np.ndarray) -> np.ndarray:
     n_exp, hidden = wr.shape
     xs = np.atleast_2d(x)
@@ -355,10 +388,12 @@ def router_logits(wr: np.ndarray, x: np.ndarray) -> np.ndarray:
     return out
 
 
-def moe_layer(experts, wr, x, top_k=6, bias=None, score_fn=1):
-    """Decode MoE layer, reference order (F:7277-7376 routing, F:7521-7566
-    combine, no shared expert).  experts: list of expert objects with
-    .forward(x).  Returns (out [n_tok, hidden], idx, wt)."""
+def moe_layer(experts, wr, x, top_k=6, bias=None, score_fn=1, norm_w=None, norm_eps=1e-20):
+    """Decode MoE layer, reference order (F:7637 ffn_norm when norm_w is given,
+    F:7277-7376 routing, F:7521-7566 combine, no shared expert).  experts: list
+    of expert objects with .forward(x).  Returns (out [n_tok, hidden], idx, wt)."""
+    if norm_w is not None:
+        x = rms_norm(x, norm_w, norm_eps)
     logits = router_logits(wr, x)
     idx, wt, _, _ = route(logits, top_k, bias, score_fn)
     n_tok, hidden = x.shape

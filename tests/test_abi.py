@@ -89,20 +89,22 @@ def test_argument_validation_without_gpu(ffn):
     assert L.ffn_b200_nvfp4_matvec(16, 64, 1, C.byref(m), None, None, None, 0, None) == -1
     t = ffn.TnMat(16, 4, None, None, None, None)
     assert L.ffn_b200_ternary_matvec(16, 96, 1, C.byref(t), None, None, None, 0, None) == -5
-    d = ffn.MoeDesc(4096, 2048, 384, 7, None, None, None, 1, 0, 0, 384, 1, 0)
+    d = ffn.MoeDesc(4096, 2048, 384, 7, None, None, None, 1, 0, 0, 384, 1, 0, None, 0.0, 0)
     assert L.ffn_b200_moe_layer(C.byref(d), 4, None, None, None, None, None, None, 0, None) == -1
-    d = ffn.MoeDesc(4096, 2048, 384, 6, 64, 64, None, 1, 0, 0, 385, 1, 0)
+    d = ffn.MoeDesc(4096, 2048, 384, 6, 64, 64, None, 1, 0, 0, 385, 1, 0, None, 0.0, 0)
     assert L.ffn_b200_moe_layer(C.byref(d), 4, None, None, None, None, None, None, 0, None) == -1
-    d = ffn.MoeDesc(4096, 2048, 384, 6, 64, 64, None, 7, 0, 0, 384, 1, 0)
+    d = ffn.MoeDesc(4096, 2048, 384, 6, 64, 64, None, 7, 0, 0, 384, 1, 0, None, 0.0, 0)
     assert L.ffn_b200_moe_layer(C.byref(d), 4, None, None, None, None, None, None, 0, None) == -1
-    d = ffn.MoeDesc(4096, 2048, 384, 6, 64, 64, None, 1, 0, 0, 384, 1, 0)
+    d = ffn.MoeDesc(4096, 2048, 384, 6, 64, 64, None, 1, 9, 0, 384, 1, 0, None, 0.0, 0)
+    assert L.ffn_b200_moe_layer(C.byref(d), 4, None, None, None, None, None, None, 0, None) == -1
+    d = ffn.MoeDesc(4096, 2048, 384, 6, 64, 64, None, 1, 0, 0, 384, 1, 0, None, 0.0, 0)
     rc = L.ffn_b200_moe_layer(C.byref(d), 4, 64, None, 64, None, None, 64, 16, None)
     assert rc == -3  # workspace too small
 
 
 def test_workspace_sizes_scale(ffn):
     L = ffn.lib()
-    d = ffn.MoeDesc(4096, 2048, 384, 6, None, None, None, 1, 0, 0, 384, 1, 0)
+    d = ffn.MoeDesc(4096, 2048, 384, 6, None, None, None, 1, 0, 0, 384, 1, 0, None, 0.0, 0)
     a, b = L.ffn_b200_moe_ws_bytes(C.byref(d), 64), L.ffn_b200_moe_ws_bytes(C.byref(d), 256)
     assert 0 < a < b
     assert b >= 256 * 6 * 4096 * 4  # y [P, H] f32 dominates

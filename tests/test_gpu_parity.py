@@ -270,3 +270,46 @@ def test_moe_config2_sampled(oracle, ffn, cuda):
             y = oracle_nvfp4_expert(oracle, experts[ridx[t, k]]).forward(np.ascontiguousarray(xs[t]))
             oracle.axpy(ref, rwt[t, k], y)
         oracle.assert_close(out[t], ref, what=f"config2 token {t}")
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_moe_layer_rmsnorm_and_router_modes(oracle, ffn, cuda, mode):
+    """ffn_norm before routing (flash1017.rs:7637).  EXACT router: top-k indices
+    bit-exact; TENSOR router: the selected set equal except at near-ties."""
+    import torch
+    E, H, I, T, K = 32, 512, 256, 24, 6
+    experts, wr = _moe_small(ffn, 0, E, H, I, seed=50)
+    x = ffn.gen_normal(ffn.path_key(50, 0, 0, ffn.TAG_X), T * H).view(T, H) * 37.0
+    nw = torch.linspace(0.5, 1.5, H, device=cuda)
+    idx = torch.empty(T, K, dtype=torch.int32, device=cuda)
+    layer = ffn.MoeLayer(experts, wr, H, I, top_k=K, router_mode=mode, norm_w=nw, norm_eps=1e-20)
+    out = host(layer.forward(x, topk_idx=idx, residual=x))
+    oe = [oracle_nvfp4_expert(oracle, e) for e in experts]
+    xs = host(x)
+    ref, ridx, _ = oracle.moe_layer(oe, host(wr), xs, top_k=K, score_fn=1, norm_w=host(nw))
+    if mode == 0:
+        assert np.array_equal(host(idx), ridx)
+    else:
+        xn = oracle.rms_norm(xs, host(nw))
+        bs = oracle.biased_sorted(oracle.router_logits(host(wr), xn), K)
+        assert oracle.topk_agrees(host(idx), ridx, bs).all()
+        if not np.array_equal(np.sort(host(idx), 1), np.sort(ridx, 1)):
+            pytest.skip("near-tie selection differs; outputs not comparable token by token")
+    oracle.assert_close(out, ref + xs, what=f"moe rmsnorm router {mode}")
+
+
+def test_tensor_router_config2_selection(oracle, ffn, cuda):
+    """TENSOR router on config-2 shapes (384 x 4096 fp32 router, 64 tokens)."""
+    import torch
+    E, H, T, K = 384, 4096, 64, 6
+    wr = ffn.gen_normal(ffn.path_key(2, 0, 0, ffn.TAG_ROUTER), E * H, 0.02).view(E, H)
+    experts = [ffn.SwigluExpert.generate(ffn.FMT_NVFP4, 60, 0, e, 128, H) for e in range(E)]
+    x = ffn.gen_normal(ffn.path_key(2, 0, 0, ffn.TAG_X), T * H).view(T, H)
+    idx = torch.empty(T, K, dtype=torch.int32, device=cuda)
+    ffn.MoeLayer(experts, wr, H, 128, top_k=K, router_mode=ffn.ROUTER_TENSOR).forward(
+        x, topk_idx=idx)
+    logits = oracle.router_logits(host(wr), host(x))
+    ridx, _, _, _ = oracle.route(logits, K, None, 1)
+    bs = oracle.biased_sorted(logits, K)
+    agree = oracle.topk_agrees(host(idx), ridx, bs)
+    assert agree.all(), np.where(~agree)

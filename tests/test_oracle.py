@@ -218,3 +218,15 @@ def test_tolerance_metrics(oracle):
     assert oracle.max_rel_err(b, a) == pytest.approx(1e-3)
     with pytest.raises(AssertionError):
         oracle.assert_close(a + np.array([0, 0, 0.01]), a)
+
+
+def test_rms_norm_matches_restatement(oracle):
+    """flash1017.rs:4880-4891 restated: sequential f32 sum of squares."""
+    x = oracle.gen_normal(oracle.key(9, 0, 0, 11), 256) * np.float32(3.0)
+    w = np.linspace(0.5, 1.5, 256).astype(np.float32)
+    ss = np.float32(0)
+    for v in x:
+        ss = np.float32(ss + np.float32(v * v))
+    inv = np.float32(1.0) / np.float32(np.sqrt(np.float32(ss / np.float32(256) + np.float32(1e-20))))
+    want = np.array([np.float32(np.float32(x[i] * inv) * w[i]) for i in range(256)], dtype=np.float32)
+    assert np.array_equal(oracle.rms_norm(x[None, :], w)[0], want)

@@ -28,7 +28,7 @@ EXPORTS = [
     "gx10_rust_register_shard_bounds", "gx10_rust_register_host_range",
     "ffn_b200_version", "ffn_b200_last_error", "ffn_b200_launch_count", "ffn_b200_set_device",
     "ffn_b200_matvec_ws_bytes", "ffn_b200_nvfp4_matvec", "ffn_b200_ternary_matvec",
-    "ffn_b200_expert_ws_bytes", "ffn_b200_expert_forward",
+    "ffn_b200_expert_ws_bytes", "ffn_b200_expert_forward", "ffn_b200_expert_forward_noalloc",
     "ffn_b200_moe_ws_bytes", "ffn_b200_moe_layer",
     "ffn_b200_key", "ffn_b200_gen_nvfp4", "ffn_b200_gen_ternary", "ffn_b200_gen_core",
     "ffn_b200_gen_normal", "ffn_b200_dequant_nvfp4", "ffn_b200_dequant_ternary",
@@ -104,6 +104,8 @@ def lib() -> C.CDLL:
         L.ffn_b200_expert_ws_bytes.argtypes = [sz, sz, sz]
         L.ffn_b200_expert_forward.argtypes = [sz, sz, sz, C.POINTER(Expert), vp, vp, f32, i32,
                                               vp, sz, vp]
+        L.ffn_b200_expert_forward_noalloc.argtypes = [sz, sz, sz, C.POINTER(Expert), vp, vp, f32,
+                                                      i32, vp]
         L.ffn_b200_moe_ws_bytes.restype = sz
         L.ffn_b200_moe_ws_bytes.argtypes = [C.POINTER(MoeDesc), sz]
         L.ffn_b200_moe_layer.argtypes = [C.POINTER(MoeDesc), sz, vp, vp, vp, vp, vp, vp, sz, vp]

@@ -124,6 +124,22 @@ FFN_B200_EXPORT int ffn_b200_expert_forward(size_t inter, size_t hidden, size_t 
                                             float *out, float accum_weight, int accumulate,
                                             void *ws, size_t ws_bytes, void *stream);
 
+/* The same expert forward for callers that cannot allocate device memory or
+ * hand over scratch: a plugin host that owns the memory budget, code running
+ * during CUDA stream capture, decode loops that must not allocate.  This entry
+ * point has no counterpart in the reference.  It uses a fixed 1 MiB scratch
+ * array that the library keeps on every GPU that loads it until the process
+ * exits, and calls no allocator.  Shapes that need more scratch than 1 MiB
+ * (ffn_b200_expert_ws_bytes) are rejected with FFN_B200_EINVAL.  The first
+ * call on a device looks up the array's device address, so make that first
+ * call before any stream capture.  All calls share the one array: calls whose
+ * work overlaps on the GPU (different streams, or different host threads)
+ * race on it and must be serialised by the caller. */
+FFN_B200_EXPORT int ffn_b200_expert_forward_noalloc(size_t inter, size_t hidden, size_t seq,
+                                                    const ffn_b200_expert *e, const float *x,
+                                                    float *out, float accum_weight,
+                                                    int accumulate, void *stream);
+
 /* -------------------------------------------------------------- MoE layer
  * Routed SwiGLU MoE layer (flash1017.rs:7259-7567 decode, 7972-8326 batched):
  * router logits -> scores -> top_k -> per-expert token groups -> fused expert

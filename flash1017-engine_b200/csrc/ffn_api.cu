@@ -81,10 +81,9 @@ static int prof_collect(Prof &p) {
   return 0;
 }
 
-static int sm_count() {
+int sm_count_of(int dev) {
   static int cache[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (dev < 0 || dev >= 64) return 148;
   if (!cache[dev]) {
     int n = 0;
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
@@ -94,11 +93,6 @@ static int sm_count() {
   return cache[dev];
 }
 
-// Persistent grid: two CTAs per SM (the phase kernels' occupancy target).
-static int phase_grid(long long tiles) {
-  const long long cap = 2LL * sm_count();
-  return (int)std::max<long long>(1, std::min<long long>(tiles, cap));
-}
 
 // ---------------------------------------------------------- workspace carving
 // A bump allocator over the caller's buffer; with base == nullptr it only sizes.
@@ -122,7 +116,7 @@ static int check_mat_shape(int fmt, size_t rows, size_t cols, const char *what) 
     return fail(FFN_B200_EINVAL, std::string(what) + ": rows and cols must be positive");
   if (rows > (1u << 30) || cols > (1u << 24))
     return fail(FFN_B200_EINVAL, std::string(what) + ": shape too large");
-  const size_t q = fmt == FFN_B200_FMT_NVFP4 ? 32 : 64;
+  const size_t q = 64;  // a lane's 16-byte column slice, and 4-byte scale copies
   if (cols % q)
     return fail(FFN_B200_EUNSUP, std::string(what) + ": cols must be a multiple of " +
                                      std::to_string(q) + " for this format");
@@ -131,8 +125,8 @@ static int check_mat_shape(int fmt, size_t rows, size_t cols, const char *what) 
 
 static int check_nvfp4(const ffn_b200_nvfp4_mat &m, const char *what) {
   if (!m.w || !m.s) return fail(FFN_B200_EINVAL, std::string(what) + ": null NVFP4 pointer");
-  if (!aligned(m.w, 16) || !aligned(m.s, 2))
-    return fail(FFN_B200_EINVAL, std::string(what) + ": NVFP4 w must be 16-byte and s 2-byte aligned");
+  if (!aligned(m.w, 16) || !aligned(m.s, 4))
+    return fail(FFN_B200_EINVAL, std::string(what) + ": NVFP4 w must be 16-byte and s 4-byte aligned");
   return 0;
 }
 
@@ -261,7 +255,7 @@ static int matvec_common(int fmt, size_t rows, size_t cols, size_t seq, const ff
   p.out_w = 1.0f;
   p.mat = 0;
   const long long tiles = (long long)((seq + kNTok - 1) / kNTok) * p.blocks;
-  return launch_phase(fmt, 0, p, phase_grid(tiles), st);
+  return launch_phase(fmt, 0, p, tiles, st);
 }
 
 int ffn_b200_nvfp4_matvec(size_t rows, size_t cols, size_t seq, const ffn_b200_nvfp4_mat *m,
@@ -361,7 +355,7 @@ int ffn_b200_expert_forward(size_t inter, size_t hidden, size_t seq, const ffn_b
   p.hh = hh;
   p.hl = hl;
   p.ld_h = (int)inter;
-  if ((rc = launch_phase(fmt, 1, p, phase_grid((long long)nv * p.blocks), st))) return rc;
+  if ((rc = launch_phase(fmt, 1, p, (long long)nv * p.blocks, st))) return rc;
   if (cores) {
     CoreZArgs z{};
     z.direct = *e;
@@ -391,7 +385,7 @@ int ffn_b200_expert_forward(size_t inter, size_t hidden, size_t seq, const ffn_b
   q.ld_y = (int)hidden;
   q.out_w = accum_weight;
   q.accumulate = accumulate ? 1 : 0;
-  return launch_phase(fmt, 2, q, phase_grid((long long)nv * q.blocks), st);
+  return launch_phase(fmt, 2, q, (long long)nv * q.blocks, st);
 }
 
 // ---------------------------------------------------------------- MoE layer
@@ -520,7 +514,7 @@ int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
     p.hh = w.hh;
     p.hl = w.hl;
     p.ld_h = (int)I;
-    if ((rc = launch_phase(fmt, 1, p, phase_grid(max_vexp * p.blocks), st))) return rc;
+    if ((rc = launch_phase(fmt, 1, p, max_vexp * p.blocks, st))) return rc;
     if (tern) {
       CoreZArgs z{};
       z.experts = d->experts;
@@ -549,7 +543,7 @@ int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
     q.z = w.z;
     q.y = w.y;
     q.ld_y = (int)H;
-    if ((rc = launch_phase(fmt, 2, q, phase_grid(max_vexp * q.blocks), st))) return rc;
+    if ((rc = launch_phase(fmt, 2, q, max_vexp * q.blocks, st))) return rc;
   }
   if ((rc = launch_combine(w.y, (int)H, w.idx, w.wt, w.inv, T, (int)k, d->experts, residual, out,
                            (int)H, st)))

@@ -48,10 +48,11 @@ struct CoreZArgs {
 };
 
 int rows_per_tile(int phase);
+int sm_count_of(int dev);  // multiprocessors of device `dev` (cached)
 int launch_xprep(const float *x, int ld_x, int rows, int K, __half *nh, __half *nl, __half *th,
                  __half *tl, int ld_o, int *xe, cudaStream_t st, const float *norm_w = nullptr,
                  float norm_eps = 0.f, int seq_norm = 0, float *xn = nullptr);
-int launch_phase(int fmt, int phase, const PhaseArgs &a, int grid, cudaStream_t st);
+int launch_phase(int fmt, int phase, const PhaseArgs &a, long long tasks, cudaStream_t st);
 int launch_corez(const CoreZArgs &a, int max_vexp, cudaStream_t st);
 int launch_exact_matvec(const float *w32, const uint16_t *w16, const float *x, int n_tok,
                         int rows, int H, float *out, cudaStream_t st);

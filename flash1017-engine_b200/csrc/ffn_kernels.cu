@@ -141,97 +141,190 @@ __device__ __forceinline__ MatInfo mat_info(const ffn_b200_expert &E, int mm) {
   return r;
 }
 
+// Stages of each warp's cp.async ring (units in flight = STAGES - 1).
+#ifndef FFN_STAGES
+#define FFN_STAGES 4
+#endif
+constexpr int kStages = FFN_STAGES;
+
+// Rows of one warp task: gate+up tasks carry two matrices, so R = 1 (16 rows);
+// single-matrix tasks use R = 2 (32 rows), giving both the same unit size.
+#ifndef FFN_R_GATEUP
+#define FFN_R_GATEUP 1
+#endif
+#ifndef FFN_R_SINGLE
+#define FFN_R_SINGLE 2
+#endif
+template <int PHASE>
+__host__ __device__ constexpr int task_r() { return PHASE == 1 ? FFN_R_GATEUP : FFN_R_SINGLE; }
+
+int rows_per_tile(int phase) { return 16 * (phase == 1 ? task_r<1>() : task_r<2>()); }
+
+// A task's slice and first row.
+__device__ __forceinline__ VExp task_slice(const PhaseArgs &a, int task, int rows_per_task, int &row0) {
+  const int v = task / a.blocks, blk = task - v * a.blocks;
+  row0 = blk * rows_per_task;
+  if (a.vexp) return a.vexp[v];
+  VExp ve;
+  ve.expert = -1;
+  ve.offset = v * kNTok;
+  ve.count = min(kNTok, a.n_tok_direct - v * kNTok);
+  ve.pad = 0;
+  return ve;
+}
+
+// Matrix mi (of NMAT) of a task on expert `expert` (-1: the direct expert).
+template <int FMT, int PHASE, int NMAT>
+__device__ __forceinline__ int task_mat(const PhaseArgs &a, int mi) {
+  return PHASE == 1 ? (mi == 0 ? 0 : 1) : (PHASE == 2 ? 2 : a.mat);
+}
+template <int FMT, int PHASE, int NMAT>
+__device__ __forceinline__ MatInfo task_info(const PhaseArgs &a, int expert, int mi) {
+  return mat_info<FMT>(expert >= 0 ? a.experts[expert] : a.direct, task_mat<FMT, PHASE, NMAT>(a, mi));
+}
+
 // PHASE 1: gate+up -> h.  PHASE 2: down -> y / out.  PHASE 0: one matrix -> out.
-// Persistent CTAs walk tiles (slice, row block) with a grid stride.
-template <int FMT, int PHASE, int R>
-__global__ void __launch_bounds__(kThreads, 2) phase_kernel(const PhaseArgs a) {
+// Every warp walks its own tasks (slice, row block) with a grid-wide stride and
+// streams each task's K-chunks through its cp.async ring; warps never wait for
+// one another.  Consecutive warps take consecutive row blocks of one slice, so
+// the slice's activation rows are shared in L1.
+template <int FMT, int PHASE, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a) {
   constexpr int NMAT = PHASE == 1 ? 2 : 1;
-  using TE = TileEngine<FMT, NMAT, R>;
-  __shared__ float red[TE::RED_FLOATS];
+  constexpr int R = task_r<PHASE>();
+  using WE = WarpEngine<FMT, NMAT, R, kStages>;
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
+  uint8_t *ring = smem + warp * WE::RING;
   const int n_vexp = a.vexp ? *a.n_vexp_dev : (a.n_tok_direct + kNTok - 1) / kNTok;
-  const int n_tiles = n_vexp * a.blocks;
-  for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-    const int v = tile / a.blocks, blk = tile - v * a.blocks;
-    VExp ve;
-    if (a.vexp) {
-      ve = a.vexp[v];
-    } else {
-      ve.expert = -1;
-      ve.offset = v * kNTok;
-      ve.count = min(kNTok, a.n_tok_direct - v * kNTok);
-    }
-    int midx[NMAT];
-    if (PHASE == 1) { midx[0] = 0; midx[NMAT - 1] = 1; }
-    else midx[0] = PHASE == 2 ? 2 : a.mat;
-    MatInfo mi_[NMAT];
-    float proj;
-    if (ve.expert >= 0) {
-      const ffn_b200_expert &E = a.experts[ve.expert];
-#pragma unroll
-      for (int mi = 0; mi < NMAT; ++mi) mi_[mi] = mat_info<FMT>(E, midx[mi]);
-      proj = E.proj_scale;
-    } else {
-#pragma unroll
-      for (int mi = 0; mi < NMAT; ++mi) mi_[mi] = mat_info<FMT>(a.direct, midx[mi]);
-      proj = a.direct.proj_scale;
-    }
-    MatRef m[NMAT];
-#pragma unroll
-    for (int mi = 0; mi < NMAT; ++mi) { m[mi].w = mi_[mi].w; m[mi].s = mi_[mi].s; }
+  const int n_tasks = n_vexp * a.blocks;
+  const int nch = WE::nchunks(a.K);
+  const int gw = (int)blockIdx.x * kWarps + warp, nw = (int)gridDim.x * kWarps;
+  const int n_mine = n_tasks > gw ? (n_tasks - gw + nw - 1) / nw : 0;
 
-    const int g = (threadIdx.x & 31) >> 2;
-    const bool has_tok = g < ve.count;
-    const int xrow = a.pair_tok ? __ldg(a.pair_tok + ve.offset + min(g, ve.count - 1))
-                                : ve.offset + min(g, ve.count - 1);
-    const int row0 = blk * TE::ROWS;
+  // producer: issues the units of this warp's tasks in order (task p_k,
+  // chunk p_c), STAGES - 1 units ahead of the consumer
+  int p_k = 0, p_c = 0, p_slot = 0, p_row0 = 0;
+  MatRef pm[NMAT];
+  auto issue_next = [&]() {
+    if (p_k < n_mine) {
+      if (p_c == 0) {
+        const VExp ve = task_slice(a, gw + p_k * nw, WE::ROWS, p_row0);
+#pragma unroll
+        for (int mi = 0; mi < NMAT; ++mi) {
+          const MatInfo m = task_info<FMT, PHASE, NMAT>(a, ve.expert, mi);
+          pm[mi].w = m.w;
+          pm[mi].s = m.s;
+        }
+      }
+      WE::issue(ring + p_slot * WE::UNIT, pm, a.rows, a.K, p_row0, p_c);
+      if (++p_c == nch) { p_c = 0; ++p_k; }
+    }
+    cp_async_commit();
+    p_slot = p_slot + 1 == kStages ? 0 : p_slot + 1;
+  };
+#pragma unroll
+  for (int s = 0; s < kStages - 1; ++s) issue_next();
+
+  int c_slot = 0;
+  for (int k = 0; k < n_mine; ++k) {
+    int row0;
+    const VExp ve = task_slice(a, gw + k * nw, WE::ROWS, row0);
+    const bool packed = ve.count <= 4;
+    // this lane's MMA column: packed: token g&3, hi terms in columns 0-3 and
+    // lo terms in 4-7; otherwise token g with separate hi / lo MMAs
+    const int tok = packed ? (g & 3) : g;
+    const __half *xa = nullptr, *xb = nullptr;
+    if (tok < ve.count) {
+      const int p = ve.offset + tok;
+      const int xr = a.pair_tok ? __ldg(a.pair_tok + p) : p;
+      const __half *hrow = a.xh + (size_t)xr * a.ld_x, *lrow = a.xl + (size_t)xr * a.ld_x;
+      if (packed) xa = g < 4 ? hrow : lrow;
+      else { xa = hrow; xb = lrow; }
+    }
     float acc[NMAT][R][4];
-    TE::run(m, a.rows, a.K, row0, has_tok, a.xh + (size_t)xrow * a.ld_x,
-            a.xl + (size_t)xrow * a.ld_x, acc);
-    TE::stash(red, acc);
-    __syncthreads();
+#pragma unroll
+    for (int mi = 0; mi < NMAT; ++mi)
+#pragma unroll
+      for (int i = 0; i < R; ++i)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[mi][i][q] = 0.f;
+    for (int c = 0; c < nch; ++c) {
+      issue_next();
+      cp_async_wait<kStages - 1>();
+      __syncwarp();
+      const uint8_t *slot = ring + c_slot * WE::UNIT;
+      c_slot = c_slot + 1 == kStages ? 0 : c_slot + 1;
+      if (packed) WE::template compute<true>(slot, a.K, c, xa, xb, acc);
+      else WE::template compute<false>(slot, a.K, c, xa, xb, acc);
+      __syncwarp();
+    }
 
-    // Epilogue: one (row, token) per thread iteration.
-    for (int e = threadIdx.x; e < TE::ROWS * kNTok; e += kThreads) {
-      const int rl = e % TE::ROWS, n = e / TE::ROWS;
-      const int row = row0 + rl;
-      if (n >= ve.count || row >= a.rows) continue;
+    // Epilogue from the accumulators: lane (g, t) holds rows 16i+g and 16i+g+8,
+    // columns 2t and 2t+1.  Packed: token n = column n + column n+4, so lanes
+    // t < 2 add their partner lane t+2 and own tokens 2t, 2t+1.
+    if (packed) {
+#pragma unroll
+      for (int mi = 0; mi < NMAT; ++mi)
+#pragma unroll
+        for (int i = 0; i < R; ++i)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) acc[mi][i][q] += __shfl_xor_sync(0xffffffffu, acc[mi][i][q], 2);
+    }
+    if (packed && t >= 2) continue;
+    MatInfo mat[NMAT];
+#pragma unroll
+    for (int mi = 0; mi < NMAT; ++mi) mat[mi] = task_info<FMT, PHASE, NMAT>(a, ve.expert, mi);
+    const float proj = ve.expert >= 0 ? a.experts[ve.expert].proj_scale : a.direct.proj_scale;
+#pragma unroll
+    for (int jn = 0; jn < 2; ++jn) {
+      const int n = 2 * t + jn;
+      if (n >= ve.count) continue;
       const int p = ve.offset + n;
       const int xr = a.pair_tok ? __ldg(a.pair_tok + p) : p;
       const float xsc = a.xe ? pow2f(__ldg(a.xe + xr)) : 1.0f;
-      float val[NMAT];
 #pragma unroll
-      for (int mi = 0; mi < NMAT; ++mi) {
-        float s = TE::total(red, mi, rl, n);
-        if (FMT == FFN_B200_FMT_NVFP4) {
-          s = s * xsc * mi_[mi].gs;
-        } else {
-          s = (s * 0.5f) * xsc * __ldg(mi_[mi].rs + row);
-          if (mi_[mi].core_b)
-            s += core_term(mi_[mi].core_b, row, a.z + ((size_t)p * 3 + midx[mi]) * 16);
+      for (int i = 0; i < R; ++i)
+#pragma unroll
+        for (int jr = 0; jr < 2; ++jr) {
+          const int row = row0 + 16 * i + g + 8 * jr;
+          if (row >= a.rows) continue;
+          float val[NMAT];
+#pragma unroll
+          for (int mi = 0; mi < NMAT; ++mi) {
+            float s = acc[mi][i][2 * jr + jn];
+            if (FMT == FFN_B200_FMT_NVFP4) {
+              s = s * xsc * mat[mi].gs;
+            } else {
+              const int mm = task_mat<FMT, PHASE, NMAT>(a, mi);
+              s = (s * 0.5f) * xsc * __ldg(mat[mi].rs + row);
+              if (mat[mi].core_b)
+                s += core_term(mat[mi].core_b, row, a.z + ((size_t)p * 3 + mm) * 16);
+            }
+            val[mi] = s;
+          }
+          if (PHASE == 1) {
+            float gv = val[0], uv = val[NMAT - 1];
+            if (FMT == FFN_B200_FMT_TERNARY) { gv *= proj; uv *= proj; }
+            const float h = silu_clamped(gv) * clamp10(uv);
+            __half hi, lo;
+            split_f16(h, hi, lo);
+            const int col = FMT == FFN_B200_FMT_NVFP4 ? row : tern_pos(row);
+            a.hh[(size_t)p * a.ld_h + col] = hi;
+            a.hl[(size_t)p * a.ld_h + col] = lo;
+          } else {
+            float *dst = a.y + (size_t)p * a.ld_y + row;
+            if (a.vexp || PHASE == 0) {
+              *dst = val[0];
+            } else {
+              const float wy = a.out_w * val[0];  // flash1017.rs:4900-4905 (dst += scale * src)
+              *dst = a.accumulate ? *dst + wy : wy;
+            }
+          }
         }
-        val[mi] = s;
-      }
-      if (PHASE == 1) {
-        float gv = val[0], uv = val[NMAT - 1];
-        if (FMT == FFN_B200_FMT_TERNARY) { gv *= proj; uv *= proj; }
-        const float h = silu_clamped(gv) * clamp10(uv);
-        __half hi, lo;
-        split_f16(h, hi, lo);
-        const int col = FMT == FFN_B200_FMT_NVFP4 ? row : tern_pos(row);
-        a.hh[(size_t)p * a.ld_h + col] = hi;
-        a.hl[(size_t)p * a.ld_h + col] = lo;
-      } else {
-        float *dst = a.y + (size_t)p * a.ld_y + row;
-        if (a.vexp || PHASE == 0) {
-          *dst = val[0];
-        } else {
-          const float wy = a.out_w * val[0];  // flash1017.rs:4900-4905 (dst += scale * src)
-          *dst = a.accumulate ? *dst + wy : wy;
-        }
-      }
     }
-    __syncthreads();
   }
+  cp_async_wait<0>();
 }
 
 constexpr int phase_kind(int fmt, int phase) {
@@ -240,29 +333,48 @@ constexpr int phase_kind(int fmt, int phase) {
                                                  : (phase == 1 ? FFN_B200_K_GATEUP_TERNARY : FFN_B200_K_DOWN_TERNARY));
 }
 
-template <int FMT, int PHASE, int R>
-static int launch_phase_t(const PhaseArgs &a, int grid, cudaStream_t st) {
+// CTAs per SM: what the rings' shared memory allows, at most 2 (128 registers
+// per thread; at 3 CTAs the 80-register cap makes the engine spill).
+#ifndef FFN_MAX_CTAS
+#define FFN_MAX_CTAS 2
+#endif
+template <int FMT, int PHASE>
+constexpr int phase_min_blocks() {
+  constexpr size_t smem = WarpEngine<FMT, PHASE == 1 ? 2 : 1, task_r<PHASE>(), kStages>::SMEM;
+  constexpr int by_smem = smem * 3 <= 225 * 1024 ? 3 : (smem * 2 <= 225 * 1024 ? 2 : 1);
+  return by_smem < FFN_MAX_CTAS ? by_smem : FFN_MAX_CTAS;
+}
+
+template <int FMT, int PHASE>
+static int launch_phase_t(const PhaseArgs &a, long long tasks, cudaStream_t st) {
+  constexpr int MINB = phase_min_blocks<FMT, PHASE>();
+  constexpr size_t smem = WarpEngine<FMT, PHASE == 1 ? 2 : 1, task_r<PHASE>(), kStages>::SMEM;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  FFN_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(FFN_B200_EUNSUP, "phase_kernel: device index >= 64");
+  if (!attr_set[dev]) {
+    FFN_CUDA_TRY(cudaFuncSetAttribute(phase_kernel<FMT, PHASE, MINB>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_set[dev] = true;
+  }
+  const long long want = (tasks + kWarps - 1) / kWarps;
+  const int grid = (int)std::max<long long>(1, std::min<long long>(want, (long long)MINB * sm_count_of(dev)));
   FFN_LAUNCH(phase_kind(FMT, PHASE), st, "phase_kernel",
-             (phase_kernel<FMT, PHASE, R><<<grid, kThreads, 0, st>>>(a)));
+             (phase_kernel<FMT, PHASE, MINB><<<grid, kThreads, smem, st>>>(a)));
   return 0;
 }
 
-// Rows per CTA tile.  Gate/up tiles carry two matrices, so R=2 (32 rows);
-// single-matrix tiles use R=4 (64 rows) to keep the per-tile work balanced.
-constexpr int kRGateUp = 2;
-constexpr int kRSingle = 4;
-
-int rows_per_tile(int phase) { return 16 * (phase == 1 ? kRGateUp : kRSingle); }
-
-int launch_phase(int fmt, int phase, const PhaseArgs &a, int grid, cudaStream_t st) {
+// `tasks` is an upper bound of the warp tasks (slices x row blocks).
+int launch_phase(int fmt, int phase, const PhaseArgs &a, long long tasks, cudaStream_t st) {
   if (fmt == FFN_B200_FMT_NVFP4) {
-    if (phase == 1) return launch_phase_t<FFN_B200_FMT_NVFP4, 1, kRGateUp>(a, grid, st);
-    if (phase == 2) return launch_phase_t<FFN_B200_FMT_NVFP4, 2, kRSingle>(a, grid, st);
-    return launch_phase_t<FFN_B200_FMT_NVFP4, 0, kRSingle>(a, grid, st);
+    if (phase == 1) return launch_phase_t<FFN_B200_FMT_NVFP4, 1>(a, tasks, st);
+    if (phase == 2) return launch_phase_t<FFN_B200_FMT_NVFP4, 2>(a, tasks, st);
+    return launch_phase_t<FFN_B200_FMT_NVFP4, 0>(a, tasks, st);
   }
-  if (phase == 1) return launch_phase_t<FFN_B200_FMT_TERNARY, 1, kRGateUp>(a, grid, st);
-  if (phase == 2) return launch_phase_t<FFN_B200_FMT_TERNARY, 2, kRSingle>(a, grid, st);
-  return launch_phase_t<FFN_B200_FMT_TERNARY, 0, kRSingle>(a, grid, st);
+  if (phase == 1) return launch_phase_t<FFN_B200_FMT_TERNARY, 1>(a, tasks, st);
+  if (phase == 2) return launch_phase_t<FFN_B200_FMT_TERNARY, 2>(a, tasks, st);
+  return launch_phase_t<FFN_B200_FMT_TERNARY, 0>(a, tasks, st);
 }
 
 // ============================================================ rank-16 core z

@@ -99,7 +99,9 @@ FFN_B200_EXPORT int ffn_b200_set_device(int device);
 /* ------------------------------------------------------------ single matrices
  * out [seq, rows] = x [seq, cols] * W^T.  Same results as the reference's
  * CachedNvfp4Mat::matbatch / CachedTernary158Mat::matbatch (flash1017.rs:
- * 2361-2391, 2631-2668) within the parity tolerance.  ws: see *_ws_bytes. */
+ * 2361-2391, 2631-2668) within the parity tolerance.  ws: see *_ws_bytes.
+ * cols must be a multiple of 64; NVFP4 w 16-byte and s 4-byte aligned,
+ * ternary p 16-byte aligned. */
 FFN_B200_EXPORT size_t ffn_b200_matvec_ws_bytes(size_t seq, size_t cols);
 FFN_B200_EXPORT int ffn_b200_nvfp4_matvec(size_t rows, size_t cols, size_t seq,
                                           const ffn_b200_nvfp4_mat *m, const float *x,

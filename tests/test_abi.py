@@ -80,11 +80,11 @@ def test_argument_validation_without_gpu(ffn):
     """Bad shapes and pointers are rejected before any CUDA call."""
     L = ffn.lib()
     m = ffn.NvMat(None, None, 1.0, 0)
-    rc = L.ffn_b200_nvfp4_matvec(16, 32, 1, C.byref(m), None, None, None, 0, None)
+    rc = L.ffn_b200_nvfp4_matvec(16, 64, 1, C.byref(m), None, None, None, 0, None)
     assert rc == -1 and b"null" in L.ffn_b200_last_error()
     m = ffn.NvMat(16, 16, 1.0, 0)
     rc = L.ffn_b200_nvfp4_matvec(16, 48, 1, C.byref(m), None, None, None, 0, None)
-    assert rc == -5 and b"multiple of 32" in L.ffn_b200_last_error()
+    assert rc == -5 and b"multiple of 64" in L.ffn_b200_last_error()
     m = ffn.NvMat(24, 16, 1.0, 0)  # misaligned weights
     assert L.ffn_b200_nvfp4_matvec(16, 64, 1, C.byref(m), None, None, None, 0, None) == -1
     t = ffn.TnMat(16, 4, None, None, None, None)

@@ -89,7 +89,7 @@ def test_dequant_bit_exact(oracle, ffn, cuda):
 
 
 # ------------------------------------------------------------ single matrices
-NV_SHAPES = [(64, 128), (2048, 4096), (4096, 2048), (100, 96), (2304, 5120), (5120, 2304)]
+NV_SHAPES = [(64, 128), (2048, 4096), (4096, 2048), (100, 192), (2304, 5120), (5120, 2304)]
 
 
 @pytest.mark.parametrize("rows,cols", NV_SHAPES)

@@ -141,19 +141,26 @@ __device__ __forceinline__ MatInfo mat_info(const ffn_b200_expert &E, int mm) {
   return r;
 }
 
-// Stages of each warp's cp.async ring (units in flight = STAGES - 1).
+// Stages of each warp's cp.async ring (units in flight = STAGES - 1) and
+// sub-chunks per unit (2: 256 NVFP4 columns, so a row's block scales for one
+// unit are one 16-byte copy).
 #ifndef FFN_STAGES
-#define FFN_STAGES 4
+#define FFN_STAGES 2
+#endif
+#ifndef FFN_SUB
+#define FFN_SUB 2
 #endif
 constexpr int kStages = FFN_STAGES;
+constexpr int kSub = FFN_SUB;  // sub-chunks per ring unit
 
-// Rows of one warp task: gate+up tasks carry two matrices, so R = 1 (16 rows);
-// single-matrix tasks use R = 2 (32 rows), giving both the same unit size.
+// Rows of one warp task: gate+up tasks carry two matrices, so R = 2 (32 rows);
+// single-matrix tasks use R = 4 (64 rows): both have four m-tiles, so every
+// activation fragment a lane loads feeds four MMAs per term.
 #ifndef FFN_R_GATEUP
-#define FFN_R_GATEUP 1
+#define FFN_R_GATEUP 2
 #endif
 #ifndef FFN_R_SINGLE
-#define FFN_R_SINGLE 2
+#define FFN_R_SINGLE 4
 #endif
 template <int PHASE>
 __host__ __device__ constexpr int task_r() { return PHASE == 1 ? FFN_R_GATEUP : FFN_R_SINGLE; }
@@ -192,7 +199,7 @@ template <int FMT, int PHASE, int MINB>
 __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a) {
   constexpr int NMAT = PHASE == 1 ? 2 : 1;
   constexpr int R = task_r<PHASE>();
-  using WE = WarpEngine<FMT, NMAT, R, kStages>;
+  using WE = WarpEngine<FMT, NMAT, R, kStages, kSub>;
   extern __shared__ __align__(16) uint8_t smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
   uint8_t *ring = smem + warp * WE::RING;
@@ -205,19 +212,22 @@ __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a
   // producer: issues the units of this warp's tasks in order (task p_k,
   // chunk p_c), STAGES - 1 units ahead of the consumer
   int p_k = 0, p_c = 0, p_slot = 0, p_row0 = 0;
+  bool p_s16 = false;  // scale rows aligned for one SR-byte copy each
   MatRef pm[NMAT];
   auto issue_next = [&]() {
     if (p_k < n_mine) {
       if (p_c == 0) {
         const VExp ve = task_slice(a, gw + p_k * nw, WE::ROWS, p_row0);
+        p_s16 = (a.K / 16) % WE::SR == 0;
 #pragma unroll
         for (int mi = 0; mi < NMAT; ++mi) {
           const MatInfo m = task_info<FMT, PHASE, NMAT>(a, ve.expert, mi);
           pm[mi].w = m.w;
           pm[mi].s = m.s;
+          p_s16 = p_s16 && ((reinterpret_cast<uintptr_t>(m.s) & (WE::SR - 1)) == 0);
         }
       }
-      WE::issue(ring + p_slot * WE::UNIT, pm, a.rows, a.K, p_row0, p_c);
+      WE::issue(ring + p_slot * WE::UNIT, pm, a.rows, a.K, p_row0, p_c, p_s16);
       if (++p_c == nch) { p_c = 0; ++p_k; }
     }
     cp_async_commit();
@@ -333,14 +343,15 @@ constexpr int phase_kind(int fmt, int phase) {
                                                  : (phase == 1 ? FFN_B200_K_GATEUP_TERNARY : FFN_B200_K_DOWN_TERNARY));
 }
 
-// CTAs per SM: what the rings' shared memory allows, at most 2 (128 registers
-// per thread; at 3 CTAs the 80-register cap makes the engine spill).
+// CTAs per SM: what the rings' shared memory allows, capped so that 16 warps
+// share an SM (4-warp CTAs: 3 fit the shared memory, at up to 168 registers
+// per thread; a lower register cap makes the engine spill).
 #ifndef FFN_MAX_CTAS
-#define FFN_MAX_CTAS 2
+#define FFN_MAX_CTAS (16 / FFN_WARPS)
 #endif
 template <int FMT, int PHASE>
 constexpr int phase_min_blocks() {
-  constexpr size_t smem = WarpEngine<FMT, PHASE == 1 ? 2 : 1, task_r<PHASE>(), kStages>::SMEM;
+  constexpr size_t smem = WarpEngine<FMT, PHASE == 1 ? 2 : 1, task_r<PHASE>(), kStages, kSub>::SMEM;
   constexpr int by_smem = smem * 3 <= 225 * 1024 ? 3 : (smem * 2 <= 225 * 1024 ? 2 : 1);
   return by_smem < FFN_MAX_CTAS ? by_smem : FFN_MAX_CTAS;
 }
@@ -348,7 +359,7 @@ constexpr int phase_min_blocks() {
 template <int FMT, int PHASE>
 static int launch_phase_t(const PhaseArgs &a, long long tasks, cudaStream_t st) {
   constexpr int MINB = phase_min_blocks<FMT, PHASE>();
-  constexpr size_t smem = WarpEngine<FMT, PHASE == 1 ? 2 : 1, task_r<PHASE>(), kStages>::SMEM;
+  constexpr size_t smem = WarpEngine<FMT, PHASE == 1 ? 2 : 1, task_r<PHASE>(), kStages, kSub>::SMEM;
   static bool attr_set[64] = {false};
   int dev = 0;
   FFN_CUDA_TRY(cudaGetDevice(&dev));
@@ -496,13 +507,14 @@ int launch_exact_matvec(const float *w32, const uint16_t *w16, const float *x, i
 // summation order differs from the CPU loop, so selections can differ from the
 // reference's only where two biased scores are within that error.
 // CTA = 32 experts x 32 tokens; the 8 warps split K; shared-memory reduction.
+constexpr int kRouterWarps = 8;  // router_tc_kernel runs 256 threads
 __global__ void __launch_bounds__(256) router_tc_kernel(const float *__restrict__ w,
                                                         const __half *__restrict__ xh,
                                                         const __half *__restrict__ xl,
                                                         const int *__restrict__ xe, int n_tok,
                                                         int n_exp, int H,
                                                         float *__restrict__ logits) {
-  __shared__ float red[kWarps][32][33];
+  __shared__ float red[kRouterWarps][32][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int e0 = blockIdx.x * 32, t0 = blockIdx.y * 32;
@@ -528,7 +540,7 @@ __global__ void __launch_bounds__(256) router_tc_kernel(const float *__restrict_
     ph[j] = xh + (size_t)min(tok, n_tok - 1) * H;
     pl[j] = xl + (size_t)min(tok, n_tok - 1) * H;
   }
-  for (int ks = warp; ks < H / 16; ks += kWarps) {
+  for (int ks = warp; ks < H / 16; ks += kRouterWarps) {
     const int c = ks * 16 + 4 * t;
     uint32_t ah[2][4], al[2][4];
 #pragma unroll
@@ -579,7 +591,7 @@ __global__ void __launch_bounds__(256) router_tc_kernel(const float *__restrict_
     if (e >= n_exp || tok >= n_tok) continue;
     float s = 0.f;
 #pragma unroll
-    for (int wv = 0; wv < kWarps; ++wv) s += red[wv][el][tl];
+    for (int wv = 0; wv < kRouterWarps; ++wv) s += red[wv][el][tl];
     logits[(size_t)tok * n_exp + e] = s * pow2f(xe[tok]);
   }
 }

@@ -46,7 +46,10 @@
 
 namespace ffn {
 
-constexpr int kWarps = 8;
+#ifndef FFN_WARPS
+#define FFN_WARPS 4
+#endif
+constexpr int kWarps = FFN_WARPS;
 constexpr int kThreads = kWarps * 32;
 
 // ------------------------------------------------------------ cp.async
@@ -59,6 +62,14 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
 __device__ __forceinline__ void cp_async4(void *dst, const void *src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src));
 }
+template <int N>
+__device__ __forceinline__ void cp_async_n(void *dst, const void *src) {
+  static_assert(N == 4 || N == 8 || N == 16, "cp.async copies 4, 8 or 16 bytes");
+  if constexpr (N == 16)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src));
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(smem_u32(dst)), "l"(src), "n"(N));
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N)); }
@@ -68,70 +79,99 @@ struct MatRef {          // one weight matrix as the tile engine sees it
   const uint8_t *s;      // NVFP4 block scales (unused for ternary)
 };
 
-template <int FMT, int NMAT, int R, int STAGES>
+template <int FMT, int NMAT, int R, int STAGES, int SUB = 1>
 struct WarpEngine {
   static constexpr int ROWS = 16 * R;
   static constexpr int MT = NMAT * R;                                   // m-tiles per unit
-  static constexpr int CHUNK = FMT == FFN_B200_FMT_NVFP4 ? 128 : 256;  // columns per unit
-  static constexpr int UNIT_W = MT * 2 * 32 * 16;                       // weight bytes per unit
-  static constexpr int UNIT_S = FMT == FFN_B200_FMT_NVFP4 ? MT * 16 * 8 : 0;  // scale bytes
-  static constexpr int UNIT = UNIT_W + UNIT_S;
+  static constexpr int CHUNK = FMT == FFN_B200_FMT_NVFP4 ? 128 : 256;  // columns per sub-chunk
+  static constexpr int SUB_W = MT * 2 * 32 * 16;                        // weight bytes per sub-chunk
+  static constexpr int UNIT_W = SUB * SUB_W;
+  static constexpr int SR = 8 * SUB;                                    // scale bytes per row per unit
+  static constexpr int UNIT_S = FMT == FFN_B200_FMT_NVFP4 ? MT * 16 * SR : 0;
+  static constexpr int UNIT = UNIT_W + UNIT_S;                          // [SUB weight blocks][scales]
   static constexpr int RING = STAGES * UNIT;                            // per warp
   static constexpr size_t SMEM = (size_t)kWarps * RING;
 
-  static __device__ __forceinline__ int nchunks(int K) { return (K + CHUNK - 1) / CHUNK; }
+  static __device__ __forceinline__ int nchunks(int K) { return (K + CHUNK * SUB - 1) / (CHUNK * SUB); }
 
-  // Issue the copies of one unit (chunk c of the task whose rows start at row0)
-  // into `slot`.  Lanes whose 16-byte column slice lies past K copy nothing;
-  // the compute step treats their weights as zero.
-  __device__ static void issue(uint8_t *slot, const MatRef (&m)[NMAT], int rows, int K, int row0,
-                               int c) {
+  // Issue the copies of unit c (columns [c*CHUNK*SUB, +CHUNK*SUB)) of the task
+  // whose rows start at row0 into `slot`.  Weights: per sub-chunk and m-tile,
+  // lane (g, t) copies 16 bytes of rows g and g+8; lanes whose 16-byte column
+  // slice lies past K copy nothing (the compute step treats their weights as
+  // zero).  NVFP4 scales: SR bytes of each of the unit's 16*MT rows, one
+  // SR-byte copy per row when every scale row is SR-byte aligned (s_al),
+  // otherwise 4-byte copies.
+  __device__ static void issue(uint8_t *slot, const MatRef (&m)[NMAT], int rows, int K, int row0, int c,
+                               bool s_al) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    constexpr int LB = FMT == FFN_B200_FMT_NVFP4 ? 32 : 64;  // columns per lane per sub-chunk
+    const size_t wld = (size_t)K / (FMT == FFN_B200_FMT_NVFP4 ? 2 : 4);
+#pragma unroll
+    for (int sb = 0; sb < SUB; ++sb) {
+      const int col0 = (c * SUB + sb) * CHUNK + LB * t;
+      if (col0 < K) {
+        const size_t boff = (size_t)col0 / (FMT == FFN_B200_FMT_NVFP4 ? 2 : 4);
+#pragma unroll
+        for (int mi = 0; mi < NMAT; ++mi)
+#pragma unroll
+          for (int i = 0; i < R; ++i) {
+            const int mt = mi * R + i;
+            const int ra = min(row0 + 16 * i + g, rows - 1), rb = min(row0 + 16 * i + g + 8, rows - 1);
+            uint8_t *d = slot + sb * SUB_W + mt * 1024 + lane * 16;
+            cp_async16(d, m[mi].w + ra * wld + boff);
+            cp_async16(d + 512, m[mi].w + rb * wld + boff);
+          }
+      }
+    }
     if constexpr (FMT == FFN_B200_FMT_NVFP4) {
-      const int col0 = c * CHUNK + 32 * t;
-      const size_t wld = (size_t)K / 2, sld = (size_t)K / 16;
+      const int sld = K / 16;
+      uint8_t *sbase = slot + UNIT_W;
+      constexpr int NROW = MT * 16;
+      if (s_al) {
+        // one SR-byte copy per row
 #pragma unroll
-      for (int mi = 0; mi < NMAT; ++mi)
-#pragma unroll
-        for (int i = 0; i < R; ++i) {
-          const int mt = mi * R + i;
-          if (col0 < K) {
-            const int ra = min(row0 + 16 * i + g, rows - 1), rb = min(row0 + 16 * i + g + 8, rows - 1);
-            cp_async16(slot + (mt * 2 + 0) * 512 + lane * 16, m[mi].w + ra * wld + col0 / 2);
-            cp_async16(slot + (mt * 2 + 1) * 512 + lane * 16, m[mi].w + rb * wld + col0 / 2);
-          }
-          // scales: lane L copies 4 bytes (groups c*8 + 4(L&1) ..) of tile row L/2
-          const int sr = min(row0 + 16 * i + (lane >> 1), rows - 1);
-          const int sc = c * 8 + 4 * (lane & 1);
-          if (sc < (int)sld)
-            cp_async4(slot + UNIT_W + mt * 128 + lane * 4, m[mi].s + sr * sld + sc);
-        }
-    } else {
-      const int col0 = c * CHUNK + 64 * t;
-      const size_t wld = (size_t)K / 4;
-#pragma unroll
-      for (int mi = 0; mi < NMAT; ++mi)
-#pragma unroll
-        for (int i = 0; i < R; ++i) {
-          const int mt = mi * R + i;
-          if (col0 < K) {
-            const int ra = min(row0 + 16 * i + g, rows - 1), rb = min(row0 + 16 * i + g + 8, rows - 1);
-            cp_async16(slot + (mt * 2 + 0) * 512 + lane * 16, m[mi].w + ra * wld + col0 / 4);
-            cp_async16(slot + (mt * 2 + 1) * 512 + lane * 16, m[mi].w + rb * wld + col0 / 4);
+        for (int j = 0; j < (NROW + 31) / 32; ++j) {
+          const int rr = lane + 32 * j;
+          if (rr < NROW && c * SR < sld) {
+            const int mt = rr >> 4, mi = mt / R, i = mt % R;
+            const int sr = min(row0 + 16 * i + (rr & 15), rows - 1);
+            cp_async_n<SR>(sbase + rr * SR, m[mi].s + (size_t)sr * sld + c * SR);
           }
         }
+      } else {
+        constexpr int PIECES = NROW * SR / 4;  // 4-byte pieces per unit
+#pragma unroll
+        for (int j = 0; j < (PIECES + 31) / 32; ++j) {
+          const int p = lane + 32 * j;
+          if (p < PIECES) {
+            const int rr = p / (SR / 4), q = p % (SR / 4);
+            const int mt = rr >> 4, mi = mt / R, i = mt % R;
+            const int sr = min(row0 + 16 * i + (rr & 15), rows - 1);
+            const int sc = c * SR + 4 * q;
+            if (sc < sld) cp_async4(sbase + rr * SR + 4 * q, m[mi].s + (size_t)sr * sld + sc);
+          }
+        }
+      }
     }
   }
 
-  // Accumulate one unit (chunk c) from `slot` into acc.  xa/xb: this lane's
+  template <bool PACKED>
+  __device__ static __forceinline__ void compute(const uint8_t *slot, int K, int c, const __half *xa,
+                                                 const __half *xb, float (&acc)[NMAT][R][4]) {
+#pragma unroll
+    for (int sb = 0; sb < SUB; ++sb) compute_sub<PACKED>(slot, sb, K, c * SUB + sb, xa, xb, acc);
+  }
+
+  // Accumulate one sub-chunk c from `slot` into acc.  xa/xb: this lane's
   // B-column source rows (packed: xa = a token's hi or lo halves, xb unused;
   // otherwise xa = hi, xb = lo), or xa == nullptr for an empty column.  The
   // unit's shared-memory weight words are read first; activation words are
   // read from global memory (L1-resident: the warps of a slice share them)
   // next to the k-steps that use them.
   template <bool PACKED>
-  __device__ static void compute(const uint8_t *slot, int K, int c, const __half *xa,
-                                 const __half *xb, float (&acc)[NMAT][R][4]) {
+  __device__ static void compute_sub(const uint8_t *unit, int sb, int K, int c, const __half *xa,
+                                     const __half *xb, float (&acc)[NMAT][R][4]) {
+    const uint8_t *slot = unit + sb * SUB_W;
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int col0 = c * CHUNK + (FMT == FFN_B200_FMT_NVFP4 ? 32 : 64) * t;
     const bool valid = col0 < K;
@@ -149,7 +189,7 @@ struct WarpEngine {
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
       for (int h = 0; h < 2; ++h)
-        wq[mt][h] = valid ? *reinterpret_cast<const uint4 *>(slot + (mt * 2 + h) * 512 + lane * 16)
+        wq[mt][h] = valid ? *reinterpret_cast<const uint4 *>(slot + mt * 1024 + h * 512 + lane * 16)
                           : zero;  // code 1 (ternary) / E2M1 0 (NVFP4) decode to zero
     if constexpr (FMT == FFN_B200_FMT_NVFP4) {
       uint32_t sfa[MT], sfb[MT];
@@ -157,9 +197,9 @@ struct WarpEngine {
       for (int mt = 0; mt < MT; ++mt) {
         // lanes past K read no scale bytes (they may be stale: an E4M3 NaN there
         // would turn the zero weights into NaN)
-        const uint8_t *sp = slot + UNIT_W + mt * 128;
-        sfa[mt] = valid ? e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t *>(sp + g * 8 + 2 * t)) : 0u;
-        sfb[mt] = valid ? e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t *>(sp + (g + 8) * 8 + 2 * t)) : 0u;
+        const uint8_t *sp = unit + UNIT_W + mt * 16 * SR + 8 * sb + 2 * t;
+        sfa[mt] = valid ? e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t *>(sp + g * SR)) : 0u;
+        sfb[mt] = valid ? e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t *>(sp + (g + 8) * SR)) : 0u;
       }
 #pragma unroll
       for (int wd = 0; wd < 4; ++wd) {

@@ -134,7 +134,8 @@ static int check_ternary(const ffn_b200_ternary_mat &m, const char *what) {
   if (!m.p || !m.rs) return fail(FFN_B200_EINVAL, std::string(what) + ": null ternary pointer");
   if (!aligned(m.p, 16) || !aligned(m.rs, 4))
     return fail(FFN_B200_EINVAL, std::string(what) + ": ternary p must be 16-byte and rs 4-byte aligned");
-  if (m.core_a && (!m.core_b || !m.core_a_sc || !m.core_b_sc || !aligned(m.core_b, 16)))
+  if (m.core_a && (!m.core_b || !m.core_a_sc || !m.core_b_sc || !aligned(m.core_a, 16) ||
+                   !aligned(m.core_b, 16)))
     return fail(FFN_B200_EINVAL, std::string(what) + ": incomplete or misaligned rank-16 core");
   return 0;
 }
@@ -152,6 +153,59 @@ static ActWs carve_act(Carve &c, size_t n_rows, size_t K) {
   w.xe = c.take<int>(n_rows);
   w.z = c.take<float>(n_rows * 3 * 16);
   return w;
+}
+
+// K-splits of a direct-mode phase launch (one expert or one matrix, few
+// tokens): as many work items as one wave of resident warps holds (148 SMs x
+// 12 warps on B200), at most one split per ring unit, partial sums within
+// kSplitBytes.  A function of the shape only, so the workspace size does not
+// depend on the device.
+constexpr long long kSplitItems = 148 * 12;
+constexpr size_t kSplitBytes = 512u << 10;
+
+struct SplitPlan {
+  int splits = 1, pt = 0;
+  long long tasks = 0;
+  size_t part_bytes = 0;  // partial sums (0 when splits == 1)
+};
+
+static SplitPlan plan_splits(int fmt, int phase, size_t rows, size_t K, size_t seq) {
+  SplitPlan sp;
+  const long long nv = (long long)((seq + kNTok - 1) / kNTok);
+  sp.tasks = nv * (long long)((rows + rows_per_tile(phase) - 1) / rows_per_tile(phase));
+  sp.pt = (int)std::min<size_t>(seq, kNTok);
+  const long long nch = (long long)((K + chunk_cols(fmt) - 1) / chunk_cols(fmt));
+  const size_t per = (size_t)sp.pt * rows_per_tile(phase) * (phase == 1 ? 2 : 1) * sizeof(float);
+  long long s = std::min<long long>(kSplitItems / sp.tasks, nch);
+  s = std::min<long long>(s, (long long)(kSplitBytes / ((size_t)sp.tasks * per)));
+  sp.splits = (int)std::max<long long>(1, s);
+  sp.part_bytes = sp.splits > 1 ? (size_t)sp.tasks * sp.splits * per : 0;
+  return sp;
+}
+
+// Partial sums and arrival counters of up to two split launches.
+struct SplitWs {
+  float *part = nullptr;
+  int *cnt = nullptr;  // [tasks of launch 0][tasks of launch 1]
+};
+static SplitWs carve_split(Carve &c, const SplitPlan &a, const SplitPlan &b) {
+  SplitWs w;
+  const size_t part = std::max(a.part_bytes, b.part_bytes);
+  if (part) w.part = c.take<float>(part / sizeof(float));
+  const size_t n = (a.splits > 1 ? a.tasks : 0) + (b.splits > 1 ? b.tasks : 0);
+  if (n) w.cnt = c.take<int>(n);
+  return w;
+}
+static int zero_counters(const SplitWs &w, const SplitPlan &a, const SplitPlan &b, cudaStream_t st) {
+  const size_t n = (a.splits > 1 ? a.tasks : 0) + (b.splits > 1 ? b.tasks : 0);
+  if (n) FFN_CUDA_TRY(cudaMemsetAsync(w.cnt, 0, n * sizeof(int), st));
+  return 0;
+}
+static void apply_split(PhaseArgs &p, const SplitPlan &sp, const SplitWs &w, int *cnt) {
+  p.splits = sp.splits;
+  p.pt = sp.pt;
+  p.part = sp.splits > 1 ? w.part : nullptr;
+  p.cnt = sp.splits > 1 ? cnt : nullptr;
 }
 
 }  // namespace ffn
@@ -206,9 +260,23 @@ uint64_t ffn_b200_key(uint64_t parent, uint64_t v) {
 }
 
 // ------------------------------------------------------------ single matrix
+// (rows, format) enter through the split plan; the public size function keeps
+// its (seq, cols) signature and sizes for the largest plan over rows/format.
+static size_t matvec_ws(int fmt, size_t rows, size_t seq, size_t cols) {
+  Carve c(nullptr);
+  carve_act(c, seq, cols);
+  const SplitPlan sp = plan_splits(fmt, 0, rows, cols, seq);
+  carve_split(c, sp, SplitPlan{});
+  return c.off + 256;
+}
+
 size_t ffn_b200_matvec_ws_bytes(size_t seq, size_t cols) {
   Carve c(nullptr);
   carve_act(c, seq, cols);
+  // splits only when tasks * splits <= kSplitItems-ish; partials <= kSplitBytes,
+  // counters <= kSplitItems
+  c.take<float>(kSplitBytes / sizeof(float));
+  c.take<int>(kSplitItems);
   return c.off + 256;
 }
 
@@ -217,11 +285,13 @@ static int matvec_common(int fmt, size_t rows, size_t cols, size_t seq, const ff
   if (seq == 0) return 0;
   if (!x || !out) return fail(FFN_B200_EINVAL, "matvec: null x/out");
   if (seq > (1u << 24)) return fail(FFN_B200_EINVAL, "matvec: seq too large");
-  if (!ws || ws_bytes < ffn_b200_matvec_ws_bytes(seq, cols))
+  if (!ws || ws_bytes < matvec_ws(fmt, rows, seq, cols))
     return fail(FFN_B200_ENOSPC, "matvec: workspace too small (see ffn_b200_matvec_ws_bytes)");
   cudaStream_t st = (cudaStream_t)stream;
   Carve c(ws);
   ActWs a = carve_act(c, seq, cols);
+  const SplitPlan sp = plan_splits(fmt, 0, rows, cols, seq);
+  const SplitWs sw = carve_split(c, sp, SplitPlan{});
   const bool tern = fmt == FFN_B200_FMT_TERNARY;
   int rc = launch_xprep(x, (int)cols, (int)seq, (int)cols, tern ? nullptr : a.xh,
                         tern ? nullptr : a.xl, tern ? a.xh : nullptr, tern ? a.xl : nullptr,
@@ -254,8 +324,9 @@ static int matvec_common(int fmt, size_t rows, size_t cols, size_t seq, const ff
   p.ld_y = (int)rows;
   p.out_w = 1.0f;
   p.mat = 0;
-  const long long tiles = (long long)((seq + kNTok - 1) / kNTok) * p.blocks;
-  return launch_phase(fmt, 0, p, tiles, st);
+  apply_split(p, sp, sw, sw.cnt);
+  if ((rc = zero_counters(sw, sp, SplitPlan{}, st))) return rc;
+  return launch_phase(fmt, 0, p, sp.tasks * sp.splits, st);
 }
 
 int ffn_b200_nvfp4_matvec(size_t rows, size_t cols, size_t seq, const ffn_b200_nvfp4_mat *m,
@@ -285,12 +356,32 @@ int ffn_b200_ternary_matvec(size_t rows, size_t cols, size_t seq, const ffn_b200
 }
 
 // --------------------------------------------------------------- one expert
+// Both formats plan the same way up to the unit width; size for the larger.
+static void expert_plans(int fmt, size_t inter, size_t hidden, size_t seq, SplitPlan &s1, SplitPlan &s2) {
+  s1 = plan_splits(fmt, 1, inter, hidden, seq);
+  s2 = plan_splits(fmt, 2, hidden, inter, seq);
+}
+static void carve_expert(Carve &c, int fmt, size_t inter, size_t hidden, size_t seq, ActWs *a,
+                         __half **hh, __half **hl, SplitWs *sw) {
+  ActWs aw = carve_act(c, seq, hidden);
+  __half *h0 = c.take<__half>(seq * inter), *h1 = c.take<__half>(seq * inter);
+  SplitPlan s1, s2;
+  expert_plans(fmt, inter, hidden, seq, s1, s2);
+  SplitWs w = carve_split(c, s1, s2);
+  if (a) *a = aw;
+  if (hh) *hh = h0;
+  if (hl) *hl = h1;
+  if (sw) *sw = w;
+}
+
 size_t ffn_b200_expert_ws_bytes(size_t inter, size_t hidden, size_t seq) {
-  Carve c(nullptr);
-  carve_act(c, seq, hidden);
-  c.take<__half>(seq * inter);
-  c.take<__half>(seq * inter);
-  return c.off + 256;
+  size_t need = 0;
+  for (int fmt : {FFN_B200_FMT_NVFP4, FFN_B200_FMT_TERNARY}) {
+    Carve c(nullptr);
+    carve_expert(c, fmt, inter, hidden, seq, nullptr, nullptr, nullptr, nullptr);
+    need = std::max(need, c.off + 256);
+  }
+  return need;
 }
 
 static int check_expert(const ffn_b200_expert &e, size_t inter, size_t hidden, const char *what) {
@@ -321,8 +412,13 @@ int ffn_b200_expert_forward(size_t inter, size_t hidden, size_t seq, const ffn_b
   const int fmt = e->format;
   const bool tern = fmt == FFN_B200_FMT_TERNARY;
   Carve c(ws);
-  ActWs a = carve_act(c, seq, hidden);
-  __half *hh = c.take<__half>(seq * inter), *hl = c.take<__half>(seq * inter);
+  ActWs a;
+  __half *hh, *hl;
+  SplitWs sw;
+  carve_expert(c, fmt, inter, hidden, seq, &a, &hh, &hl, &sw);
+  SplitPlan s1, s2;
+  expert_plans(fmt, inter, hidden, seq, s1, s2);
+  if ((rc = zero_counters(sw, s1, s2, st))) return rc;
   const int nv = (int)((seq + kNTok - 1) / kNTok);
   if ((rc = launch_xprep(x, (int)hidden, (int)seq, (int)hidden, tern ? nullptr : a.xh,
                          tern ? nullptr : a.xl, tern ? a.xh : nullptr, tern ? a.xl : nullptr,
@@ -355,7 +451,8 @@ int ffn_b200_expert_forward(size_t inter, size_t hidden, size_t seq, const ffn_b
   p.hh = hh;
   p.hl = hl;
   p.ld_h = (int)inter;
-  if ((rc = launch_phase(fmt, 1, p, (long long)nv * p.blocks, st))) return rc;
+  apply_split(p, s1, sw, sw.cnt);
+  if ((rc = launch_phase(fmt, 1, p, s1.tasks * s1.splits, st))) return rc;
   if (cores) {
     CoreZArgs z{};
     z.direct = *e;
@@ -385,7 +482,8 @@ int ffn_b200_expert_forward(size_t inter, size_t hidden, size_t seq, const ffn_b
   q.ld_y = (int)hidden;
   q.out_w = accum_weight;
   q.accumulate = accumulate ? 1 : 0;
-  return launch_phase(fmt, 2, q, (long long)nv * q.blocks, st);
+  apply_split(q, s2, sw, sw.cnt ? sw.cnt + (s1.splits > 1 ? s1.tasks : 0) : nullptr);
+  return launch_phase(fmt, 2, q, s2.tasks * s2.splits, st);
 }
 
 // ---------------------------------------------------------------- MoE layer

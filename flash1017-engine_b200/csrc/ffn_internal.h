@@ -28,6 +28,14 @@ struct PhaseArgs {
   float out_w;      // direct mode epilogue weight
   int accumulate;   // direct mode: out += w*y (1) or out = w*y (0)
   int mat;          // phase 0: matrix index of `direct` used
+  // K-splits (direct mode): each task's K-chunks are divided among `splits`
+  // warps; they leave partial sums in part[task][split][NMAT][pt][ROWS] and
+  // the last to arrive (cnt[task], zeroed before the launch) adds them up in
+  // split order and runs the epilogue.  splits = 1: no partials.
+  int splits = 1;
+  int pt = 0;       // tokens per slice held in part (min(8, tokens))
+  float *part;
+  int *cnt;
 };
 
 // Arguments of the rank-16 core z kernel.
@@ -48,6 +56,7 @@ struct CoreZArgs {
 };
 
 int rows_per_tile(int phase);
+int chunk_cols(int fmt);  // K columns per ring unit
 int sm_count_of(int dev);  // multiprocessors of device `dev` (cached)
 int launch_xprep(const float *x, int ld_x, int rows, int K, __half *nh, __half *nl, __half *th,
                  __half *tl, int ld_o, int *xe, cudaStream_t st, const float *norm_w = nullptr,

@@ -20,7 +20,7 @@ namespace ffn {
 // asked, then splits x (or xn) into hi/lo f16 of x * 2^-e with
 // e = floor(log2 max|x|) - 14, in natural column order (NVFP4 consumers)
 // and/or pair order (ternary consumers).
-__global__ void __launch_bounds__(256) xprep_kernel(const float *__restrict__ x, int ld_x, int K,
+__global__ void __launch_bounds__(256) xprep_loop_kernel(const float *__restrict__ x, int ld_x, int K,
                                                     __half *nh, __half *nl, __half *th,
                                                     __half *tl, int ld_o, int *xe,
                                                     const float *__restrict__ norm_w,
@@ -39,6 +39,7 @@ __global__ void __launch_bounds__(256) xprep_kernel(const float *__restrict__ x,
       }
     } else {
       float ss = 0.f;
+#pragma unroll 8
       for (int c = threadIdx.x; c < K; c += blockDim.x) ss = fmaf(xr[c], xr[c], ss);
       for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
@@ -53,6 +54,7 @@ __global__ void __launch_bounds__(256) xprep_kernel(const float *__restrict__ x,
     inv = s_inv;
   }
   float amax = 0.f;
+#pragma unroll 8
   for (int c = threadIdx.x; c < K; c += blockDim.x) {
     float v = xr[c];
     if (norm_w) {
@@ -80,6 +82,7 @@ __global__ void __launch_bounds__(256) xprep_kernel(const float *__restrict__ x,
   }
   const float sc = pow2f(-e);
   const size_t o = (size_t)row * ld_o;
+#pragma unroll 8
   for (int c = threadIdx.x; c < K; c += blockDim.x) {
     float v = xr[c];
     if (norm_w) v = __fmul_rn(__fmul_rn(v, inv), norm_w[c]);
@@ -91,13 +94,125 @@ __global__ void __launch_bounds__(256) xprep_kernel(const float *__restrict__ x,
   if (threadIdx.x == 0) xe[row] = e;
 }
 
+// Rows of up to kXprepV * 1024 columns with 16-byte aligned x (and norm
+// weight) rows: each thread holds its 4-column groups in registers, so the row
+// is read from memory once and every pass runs on registers.
+constexpr int kXprepV = 8;
+__global__ void __launch_bounds__(256) xprep_reg_kernel(const float *__restrict__ x, int ld_x, int K,
+                                                        __half *nh, __half *nl, __half *th,
+                                                        __half *tl, int ld_o, int *xe,
+                                                        const float *__restrict__ norm_w,
+                                                        float norm_eps, int seq_norm, float *xn) {
+  const int row = blockIdx.x;
+  const float *xr = x + (size_t)row * ld_x;
+  __shared__ float red[32];
+  __shared__ float s_inv;
+  float4 v[kXprepV];
+#pragma unroll
+  for (int j = 0; j < kXprepV; ++j) {
+    const int c = 4 * (threadIdx.x + 256 * j);
+    v[j] = c < K ? __ldg(reinterpret_cast<const float4 *>(xr + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (norm_w) {
+    if (seq_norm) {
+      if (threadIdx.x == 0) {
+        float ss = 0.f;
+        for (int c = 0; c < K; ++c) ss = __fadd_rn(ss, __fmul_rn(xr[c], xr[c]));
+        s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), norm_eps)));
+      }
+    } else {
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < kXprepV; ++j)
+        ss = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, ss))));
+      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int w = 0; w < 8; ++w) t += red[w];
+        s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), norm_eps)));
+      }
+    }
+    __syncthreads();
+    const float inv = s_inv;
+#pragma unroll
+    for (int j = 0; j < kXprepV; ++j) {
+      const int c = 4 * (threadIdx.x + 256 * j);
+      if (c < K) {
+        const float4 w = __ldg(reinterpret_cast<const float4 *>(norm_w + c));
+        v[j].x = __fmul_rn(__fmul_rn(v[j].x, inv), w.x);
+        v[j].y = __fmul_rn(__fmul_rn(v[j].y, inv), w.y);
+        v[j].z = __fmul_rn(__fmul_rn(v[j].z, inv), w.z);
+        v[j].w = __fmul_rn(__fmul_rn(v[j].w, inv), w.w);
+        if (xn) *reinterpret_cast<float4 *>(xn + (size_t)row * K + c) = v[j];
+      }
+    }
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < kXprepV; ++j)
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float m = threadIdx.x < 8 ? red[threadIdx.x] : 0.f;
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (threadIdx.x == 0) red[0] = m;
+  }
+  __syncthreads();
+  amax = red[0];
+  int e = 0;
+  if (amax > 0.f && isfinite(amax)) {
+    int ex;
+    frexpf(amax, &ex);  // amax = m 2^ex, m in [0.5, 1)
+    e = max(-100, min(100, ex - 15));
+  }
+  const float sc = pow2f(-e);
+  const size_t o = (size_t)row * ld_o;
+#pragma unroll
+  for (int j = 0; j < kXprepV; ++j) {
+    const int c = 4 * (threadIdx.x + 256 * j);
+    if (c >= K) continue;
+    const float f[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+    __half hi[4], lo[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) split_f16(f[q] * sc, hi[q], lo[q]);
+    if (nh) {
+      *reinterpret_cast<__half2 *>(nh + o + c) = __halves2half2(hi[0], hi[1]);
+      *reinterpret_cast<__half2 *>(nh + o + c + 2) = __halves2half2(hi[2], hi[3]);
+      *reinterpret_cast<__half2 *>(nl + o + c) = __halves2half2(lo[0], lo[1]);
+      *reinterpret_cast<__half2 *>(nl + o + c + 2) = __halves2half2(lo[2], lo[3]);
+    }
+    if (th) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int p = tern_pos(c + q);
+        th[o + p] = hi[q];
+        tl[o + p] = lo[q];
+      }
+    }
+  }
+  if (threadIdx.x == 0) xe[row] = e;
+}
+
 int launch_xprep(const float *x, int ld_x, int rows, int K, __half *nh, __half *nl, __half *th,
                  __half *tl, int ld_o, int *xe, cudaStream_t st, const float *norm_w,
                  float norm_eps, int seq_norm, float *xn) {
   if (rows <= 0) return 0;
-  FFN_LAUNCH(FFN_B200_K_XPREP, st, "xprep_kernel",
-             xprep_kernel<<<rows, 256, 0, st>>>(x, ld_x, K, nh, nl, th, tl, ld_o, xe, norm_w,
-                                                norm_eps, seq_norm, xn));
+  const bool reg = K <= kXprepV * 1024 && ld_x % 4 == 0 && ld_o % 2 == 0 &&
+                   (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(norm_w) & 15) == 0;
+  if (reg)
+    FFN_LAUNCH(FFN_B200_K_XPREP, st, "xprep_reg_kernel",
+               xprep_reg_kernel<<<rows, 256, 0, st>>>(x, ld_x, K, nh, nl, th, tl, ld_o, xe, norm_w,
+                                                      norm_eps, seq_norm, xn));
+  else
+    FFN_LAUNCH(FFN_B200_K_XPREP, st, "xprep_loop_kernel",
+               xprep_loop_kernel<<<rows, 256, 0, st>>>(x, ld_x, K, nh, nl, th, tl, ld_o, xe, norm_w,
+                                                       norm_eps, seq_norm, xn));
   return 0;
 }
 
@@ -166,6 +281,7 @@ template <int PHASE>
 __host__ __device__ constexpr int task_r() { return PHASE == 1 ? FFN_R_GATEUP : FFN_R_SINGLE; }
 
 int rows_per_tile(int phase) { return 16 * (phase == 1 ? task_r<1>() : task_r<2>()); }
+int chunk_cols(int fmt) { return (fmt == FFN_B200_FMT_NVFP4 ? 128 : 256) * kSub; }
 
 // A task's slice and first row.
 __device__ __forceinline__ VExp task_slice(const PhaseArgs &a, int task, int rows_per_task, int &row0) {
@@ -191,10 +307,10 @@ __device__ __forceinline__ MatInfo task_info(const PhaseArgs &a, int expert, int
 }
 
 // PHASE 1: gate+up -> h.  PHASE 2: down -> y / out.  PHASE 0: one matrix -> out.
-// Every warp walks its own tasks (slice, row block) with a grid-wide stride and
-// streams each task's K-chunks through its cp.async ring; warps never wait for
-// one another.  Consecutive warps take consecutive row blocks of one slice, so
-// the slice's activation rows are shared in L1.
+// Every warp walks its own work items (slice, row block, K-split) with a
+// grid-wide stride and streams each item's K-chunks through its cp.async ring;
+// warps never wait for one another.  Consecutive warps take consecutive items
+// of one slice, so the slice's activation rows are shared in L1.
 template <int FMT, int PHASE, int MINB>
 __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a) {
   constexpr int NMAT = PHASE == 1 ? 2 : 1;
@@ -204,31 +320,38 @@ __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
   uint8_t *ring = smem + warp * WE::RING;
   const int n_vexp = a.vexp ? *a.n_vexp_dev : (a.n_tok_direct + kNTok - 1) / kNTok;
-  const int n_tasks = n_vexp * a.blocks;
+  const int S = a.splits;
+  const int n_items = n_vexp * a.blocks * S;
   const int nch = WE::nchunks(a.K);
   const int gw = (int)blockIdx.x * kWarps + warp, nw = (int)gridDim.x * kWarps;
-  const int n_mine = n_tasks > gw ? (n_tasks - gw + nw - 1) / nw : 0;
+  const int n_mine = n_items > gw ? (n_items - gw + nw - 1) / nw : 0;
+  // chunks of split s: [s*nch/S, (s+1)*nch/S)
+  auto chunk_lo = [&](int item) { return (int)((long)(item % S) * nch / S); };
+  auto chunk_hi = [&](int item) { return (int)((long)(item % S + 1) * nch / S); };
 
-  // producer: issues the units of this warp's tasks in order (task p_k,
+  // producer: issues the units of this warp's items in order (item p_k,
   // chunk p_c), STAGES - 1 units ahead of the consumer
-  int p_k = 0, p_c = 0, p_slot = 0, p_row0 = 0;
-  bool p_s16 = false;  // scale rows aligned for one SR-byte copy each
+  int p_k = 0, p_c = -1, p_cend = 0, p_slot = 0, p_row0 = 0;
+  bool p_sal = false;  // scale rows aligned for one SR-byte copy each
   MatRef pm[NMAT];
   auto issue_next = [&]() {
     if (p_k < n_mine) {
-      if (p_c == 0) {
-        const VExp ve = task_slice(a, gw + p_k * nw, WE::ROWS, p_row0);
-        p_s16 = (a.K / 16) % WE::SR == 0;
+      if (p_c < 0) {
+        const int item = gw + p_k * nw;
+        const VExp ve = task_slice(a, item / S, WE::ROWS, p_row0);
+        p_c = chunk_lo(item);
+        p_cend = chunk_hi(item);
+        p_sal = (a.K / 16) % WE::SR == 0;
 #pragma unroll
         for (int mi = 0; mi < NMAT; ++mi) {
           const MatInfo m = task_info<FMT, PHASE, NMAT>(a, ve.expert, mi);
           pm[mi].w = m.w;
           pm[mi].s = m.s;
-          p_s16 = p_s16 && ((reinterpret_cast<uintptr_t>(m.s) & (WE::SR - 1)) == 0);
+          p_sal = p_sal && ((reinterpret_cast<uintptr_t>(m.s) & (WE::SR - 1)) == 0);
         }
       }
-      WE::issue(ring + p_slot * WE::UNIT, pm, a.rows, a.K, p_row0, p_c, p_s16);
-      if (++p_c == nch) { p_c = 0; ++p_k; }
+      WE::issue(ring + p_slot * WE::UNIT, pm, a.rows, a.K, p_row0, p_c, p_sal);
+      if (++p_c == p_cend) { p_c = -1; ++p_k; }
     }
     cp_async_commit();
     p_slot = p_slot + 1 == kStages ? 0 : p_slot + 1;
@@ -238,8 +361,9 @@ __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a
 
   int c_slot = 0;
   for (int k = 0; k < n_mine; ++k) {
+    const int item = gw + k * nw, task = item / S;
     int row0;
-    const VExp ve = task_slice(a, gw + k * nw, WE::ROWS, row0);
+    const VExp ve = task_slice(a, task, WE::ROWS, row0);
     const bool packed = ve.count <= 4;
     // this lane's MMA column: packed: token g&3, hi terms in columns 0-3 and
     // lo terms in 4-7; otherwise token g with separate hi / lo MMAs
@@ -259,7 +383,8 @@ __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a
       for (int i = 0; i < R; ++i)
 #pragma unroll
         for (int q = 0; q < 4; ++q) acc[mi][i][q] = 0.f;
-    for (int c = 0; c < nch; ++c) {
+    const int c_end = chunk_hi(item);
+    for (int c = chunk_lo(item); c < c_end; ++c) {
       issue_next();
       cp_async_wait<kStages - 1>();
       __syncwarp();
@@ -270,9 +395,9 @@ __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a
       __syncwarp();
     }
 
-    // Epilogue from the accumulators: lane (g, t) holds rows 16i+g and 16i+g+8,
-    // columns 2t and 2t+1.  Packed: token n = column n + column n+4, so lanes
-    // t < 2 add their partner lane t+2 and own tokens 2t, 2t+1.
+    // Lane (g, t) holds rows 16i+g and 16i+g+8, columns 2t and 2t+1.  Packed:
+    // token n = column n + column n+4, so lanes t < 2 add their partner lane
+    // t+2 and own tokens 2t, 2t+1.
     if (packed) {
 #pragma unroll
       for (int mi = 0; mi < NMAT; ++mi)
@@ -281,7 +406,58 @@ __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a
 #pragma unroll
           for (int q = 0; q < 4; ++q) acc[mi][i][q] += __shfl_xor_sync(0xffffffffu, acc[mi][i][q], 2);
     }
-    if (packed && t >= 2) continue;
+    const bool owner = !packed || t < 2;
+    if (S > 1) {
+      // leave this split's sums; the last split of the task adds all of them
+      float *pp = a.part + (size_t)task * S * NMAT * a.pt * WE::ROWS;
+      const int s = item % S;
+#pragma unroll
+      for (int mi = 0; mi < NMAT; ++mi)
+#pragma unroll
+        for (int i = 0; i < R; ++i)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int n = 2 * t + (q & 1), rl = 16 * i + g + 8 * (q >> 1);
+            if (owner && n < ve.count)
+              pp[(((size_t)s * NMAT + mi) * a.pt + n) * WE::ROWS + rl] = acc[mi][i][q];
+          }
+      __threadfence();
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) last = atomicAdd(a.cnt + task, 1) == S - 1;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (!last) continue;
+      __threadfence();
+      // Lane-parallel reduction: lane L sums values L, L+32, ... of the task
+      // over the splits in split order (8 loads in flight per value), writes
+      // the totals over split 0's slot, and reads back its own fragment.
+      const int V = NMAT * a.pt * WE::ROWS;
+      for (int v = lane; v < V; v += 32) {
+        float sum = 0.f;
+        for (int s0 = 0; s0 < S; s0 += 8) {
+          float part8[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) part8[u] = s0 + u < S ? __ldcg(pp + (size_t)(s0 + u) * V + v) : 0.f;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) sum += part8[u];
+        }
+        pp[v] = sum;
+      }
+      __threadfence_block();
+      __syncwarp();
+#pragma unroll
+      for (int mi = 0; mi < NMAT; ++mi)
+#pragma unroll
+        for (int i = 0; i < R; ++i)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int n = 2 * t + (q & 1), rl = 16 * i + g + 8 * (q >> 1);
+            acc[mi][i][q] = owner && n < ve.count ? __ldcg(pp + ((size_t)mi * a.pt + n) * WE::ROWS + rl) : 0.f;
+          }
+    }
+    if (!owner) continue;
+
+    // epilogue
     MatInfo mat[NMAT];
 #pragma unroll
     for (int mi = 0; mi < NMAT; ++mi) mat[mi] = task_info<FMT, PHASE, NMAT>(a, ve.expert, mi);
@@ -376,7 +552,7 @@ static int launch_phase_t(const PhaseArgs &a, long long tasks, cudaStream_t st) 
   return 0;
 }
 
-// `tasks` is an upper bound of the warp tasks (slices x row blocks).
+// `tasks` is an upper bound of the warp work items (slices x row blocks x splits).
 int launch_phase(int fmt, int phase, const PhaseArgs &a, long long tasks, cudaStream_t st) {
   if (fmt == FFN_B200_FMT_NVFP4) {
     if (phase == 1) return launch_phase_t<FFN_B200_FMT_NVFP4, 1>(a, tasks, st);
@@ -390,8 +566,13 @@ int launch_phase(int fmt, int phase, const PhaseArgs &a, long long tasks, cudaSt
 
 // ============================================================ rank-16 core z
 // z[pair][mat][r] = (sum_c A[r][c] * x[c]) * a_sc[r] * b_sc[r]   (flash1017.rs:2452-2463)
-// One CTA per (slice, matrix): 256 threads = 16 core rows x 16 column lanes.
-__global__ void __launch_bounds__(256) corez_kernel(const CoreZArgs a) {
+// One CTA of 512 threads per (slice, matrix).  Thread (rg, l) takes core rows
+// 4rg..4rg+3 and the 16-column blocks l, l+128, ...: one 16-byte load of A per
+// row and block, each activation block loaded once for four rows.  Lane sums
+// are combined with shuffles and then across the 4 warps of a row group in a
+// fixed order.
+constexpr int kCorezThreads = 512;
+__global__ void __launch_bounds__(kCorezThreads) corez_kernel(const CoreZArgs a) {
   const int n_vexp = a.vexp ? *a.n_vexp_dev : (a.n_tok_direct + kNTok - 1) / kNTok;
   const int item = blockIdx.x;
   const int v = item / a.nmat, mm = a.mat0 + item % a.nmat;
@@ -410,39 +591,86 @@ __global__ void __launch_bounds__(256) corez_kernel(const CoreZArgs a) {
     asc = a.direct.tn[mm].core_a_sc; bsc = a.direct.tn[mm].core_b_sc;
   }
   if (fmt != FFN_B200_FMT_TERNARY || A == nullptr) return;  // uniform per CTA
-  const int r = threadIdx.x >> 4, l = threadIdx.x & 15;
-  __shared__ float part[kNTok][16][17];
-  for (int n = 0; n < ve.count; ++n) {
-    const int p = ve.offset + n;
-    float acc = 0.f;
-    if (a.xf) {
-      const int xr = a.pair_tok ? a.pair_tok[p] : p;
-      const float *x = a.xf + (size_t)xr * a.ld_xf;
-      for (int c = l; c < a.K; c += 16) acc += (float)A[(size_t)r * a.K + c] * x[c];
-    } else {
-      const __half *xh = a.hh + (size_t)p * a.ld_h, *xl = a.hl + (size_t)p * a.ld_h;
-      for (int c = l; c < a.K; c += 16) {
-        const int q = tern_pos(c);
-        acc += (float)A[(size_t)r * a.K + c] * (__half2float(xh[q]) + __half2float(xl[q]));
+  const int rg = threadIdx.x >> 7, l = threadIdx.x & 127;
+  float acc[4][kNTok];
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int n = 0; n < kNTok; ++n) acc[q][n] = 0.f;
+  const int nblk = a.K / 16;
+  for (int blk = l; blk < nblk; blk += 128) {
+    int4 av[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      av[q] = __ldg(reinterpret_cast<const int4 *>(A + (size_t)(4 * rg + q) * a.K + 16 * blk));
+#pragma unroll
+    for (int n = 0; n < kNTok; ++n) {
+      if (n >= ve.count) break;
+      const int p = ve.offset + n;
+      float xv[16];
+      if (a.xf) {
+        const int xr = a.pair_tok ? __ldg(a.pair_tok + p) : p;
+        const float *xp = a.xf + (size_t)xr * a.ld_xf + 16 * blk;
+        if ((reinterpret_cast<uintptr_t>(xp) & 15) == 0) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 f = __ldg(reinterpret_cast<const float4 *>(xp) + q);
+            xv[4 * q] = f.x; xv[4 * q + 1] = f.y; xv[4 * q + 2] = f.z; xv[4 * q + 3] = f.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) xv[i] = __ldg(xp + i);
+        }
+      } else {
+        // pair order: column i (< 8) at 2i, column i + 8 at 2i + 1
+        const uint4 *hp = reinterpret_cast<const uint4 *>(a.hh + (size_t)p * a.ld_h + 16 * blk);
+        const uint4 *lp = reinterpret_cast<const uint4 *>(a.hl + (size_t)p * a.ld_h + 16 * blk);
+        const uint4 h0 = __ldg(hp), h1 = __ldg(hp + 1), l0 = __ldg(lp), l1 = __ldg(lp + 1);
+        const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+        const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const __half2 hh = *reinterpret_cast<const __half2 *>(&hw[i]);
+          const __half2 ll = *reinterpret_cast<const __half2 *>(&lw[i]);
+          xv[i] = __low2float(hh) + __low2float(ll);
+          xv[i + 8] = __high2float(hh) + __high2float(ll);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int8_t *ab = reinterpret_cast<const int8_t *>(&av[q]);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[q][n] = fmaf((float)ab[i], xv[i], acc[q][n]);
       }
     }
-    part[n][r][l] = acc;
   }
+  __shared__ float red[4][4][4][kNTok];  // [row group][warp of the group][row][token]
+  const int wg = l >> 5;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int n = 0; n < kNTok; ++n) {
+      float s = acc[q][n];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if ((l & 31) == 0) red[rg][wg][q][n] = s;
+    }
   __syncthreads();
   if (threadIdx.x < 16 * kNTok) {
-    const int n = threadIdx.x >> 4, rr = threadIdx.x & 15;
+    const int r = threadIdx.x / kNTok, n = threadIdx.x % kNTok;
     if (n < ve.count) {
       float s = 0.f;
-      for (int k = 0; k < 16; ++k) s += part[n][rr][k];
-      const int p = ve.offset + n;
-      a.z[((size_t)p * 3 + mm) * 16 + rr] = s * asc[rr] * bsc[rr];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) s += red[r >> 2][w][r & 3][n];
+      a.z[((size_t)(ve.offset + n) * 3 + mm) * 16 + r] = s * asc[r] * bsc[r];
     }
   }
 }
 
 int launch_corez(const CoreZArgs &a, int max_vexp, cudaStream_t st) {
   if (max_vexp <= 0) return 0;
-  FFN_LAUNCH(FFN_B200_K_COREZ, st, "corez_kernel", corez_kernel<<<max_vexp * a.nmat, 256, 0, st>>>(a));
+  FFN_LAUNCH(FFN_B200_K_COREZ, st, "corez_kernel",
+             corez_kernel<<<max_vexp * a.nmat, kCorezThreads, 0, st>>>(a));
   return 0;
 }
 

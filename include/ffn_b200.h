@@ -74,9 +74,9 @@ typedef struct ffn_b200_nvfp4_mat {
 typedef struct ffn_b200_ternary_mat {
     const uint8_t *p;        /* [rows, cols/4] */
     const float *rs;         /* [rows] */
-    const int8_t *core_a;    /* [16, cols] or NULL (no rank-16 core) */
+    const int8_t *core_a;    /* [16, cols] or NULL (no rank-16 core); 16-byte aligned */
     const float *core_a_sc;  /* [16] */
-    const int8_t *core_b;    /* [rows, 16] */
+    const int8_t *core_b;    /* [rows, 16]; 16-byte aligned */
     const float *core_b_sc;  /* [16] */
 } ffn_b200_ternary_mat;
 

@@ -230,6 +230,7 @@ def run_ours(a):
     import torch
 
     import ffn_b200 as F
+    from ep import EpStack, expert_range
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -239,11 +240,10 @@ def run_ours(a):
     dist = None
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     H, I, E, K, T, L = a.hidden, a.inter, a.experts, a.top_k, a.tokens, a.layers
-    assert E % world == 0, "experts must divide evenly over the ranks"
-    e_loc = E // world
-    e_lo = rank * e_loc
+    e_lo, e_hi = expert_range(rank, world, E)
+    e_loc = e_hi - e_lo
     ebytes = EXPERT_BYTES(H, I)
     layer_bytes = e_loc * ebytes
     free, _ = torch.cuda.mem_get_info(dev)
@@ -292,15 +292,19 @@ def run_ours(a):
     topk = [torch.empty(T, K, dtype=torch.int32, device=dev) for _ in range(L)]
     torch.cuda.synchronize()
 
+    capturing = [False]
+
+    def layer_fn(lay):
+        def run(x_in, out, residual):
+            layers[lay].forward(x_in, out=out, residual=residual,
+                                topk_idx=topk[lay] if capturing[0] else None)
+        return run
+
+    ep = EpStack([layer_fn(lay) for lay in range(L)], rank, world)
+
     def stack(x_in, capture=False):
-        cur, nxt = x_in, xb if x_in is not xb else xa
-        for lay in range(L):
-            layers[lay].forward(cur, out=nxt, residual=cur if rank == 0 else None,
-                                topk_idx=topk[lay] if capture else None)
-            if world > 1:
-                dist.all_reduce(nxt)
-            cur, nxt = nxt, cur
-        return cur
+        capturing[0] = capture
+        return ep.forward(x_in, xa, xb)
 
     def step():
         xa.copy_(x0)

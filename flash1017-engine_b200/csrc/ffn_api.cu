@@ -499,6 +499,8 @@ struct MoeWs {
   int *n_vexp;
   __half *hh, *hl;
   float *z, *y;
+  uint8_t *chunk;  // grouped path: chunk list
+  int *err;        // grouped path: timed-out wait flag
 };
 
 static MoeWs carve_moe(Carve &c, const ffn_b200_moe_desc &d, size_t T) {
@@ -509,7 +511,7 @@ static MoeWs carve_moe(Carve &c, const ffn_b200_moe_desc &d, size_t T) {
   if (d.has_ternary) { w.th = c.take<__half>(T * H); w.tl = c.take<__half>(T * H); }
   w.xn = d.norm_w ? c.take<float>(T * H) : nullptr;
   w.xe = c.take<int>(T);
-  w.logits = c.take<float>(T * E);
+  w.logits = c.take<float>(4 * T * E);  // partial planes of the tensor router
   w.idx = c.take<int32_t>(P);
   w.wt = c.take<float>(P);
   w.inv = c.take<int32_t>(P);
@@ -522,6 +524,8 @@ static MoeWs carve_moe(Carve &c, const ffn_b200_moe_desc &d, size_t T) {
   w.hl = c.take<__half>(P * I);
   w.z = d.has_ternary ? c.take<float>(P * 3 * 16) : nullptr;
   w.y = c.take<float>(P * H);
+  w.chunk = c.take<uint8_t>(gg_chunk_bytes((int)P, (int)E));
+  w.err = c.take<int>(1);
   return w;
 }
 
@@ -551,6 +555,12 @@ int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
     return fail(FFN_B200_EINVAL, "moe_layer: unknown score_fn");
   if (d->router_mode != FFN_B200_ROUTER_EXACT && d->router_mode != FFN_B200_ROUTER_TENSOR)
     return fail(FFN_B200_EINVAL, "moe_layer: unknown router_mode");
+  if (d->path != FFN_B200_PATH_AUTO && d->path != FFN_B200_PATH_GEMV && d->path != FFN_B200_PATH_GROUPED)
+    return fail(FFN_B200_EINVAL, "moe_layer: unknown path");
+  const bool grouped_ok = !d->has_ternary && H % 128 == 0 && I % 128 == 0;
+  if (d->path == FFN_B200_PATH_GROUPED && !grouped_ok)
+    return fail(FFN_B200_EUNSUP,
+                "moe_layer: the grouped path needs NVFP4-only experts and hidden, inter multiples of 128");
   if (n_tok == 0) return 0;
   if (!x || !out) return fail(FFN_B200_EINVAL, "moe_layer: null x/out");
   if (n_tok * k > (1u << 24)) return fail(FFN_B200_EINVAL, "moe_layer: too many tokens");
@@ -572,6 +582,37 @@ int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
   if ((rc = launch_group(w.idx, T, (int)k, (int)E, d->expert_begin, d->expert_end, d->experts,
                          w.ints, w.pair_tok, w.inv, w.vexp_nv, w.vexp_tn, w.n_vexp, st)))
     return rc;
+  const bool grouped =
+      grouped_ok && (d->path == FFN_B200_PATH_GROUPED ||
+                     (d->path == FFN_B200_PATH_AUTO && (size_t)P >= (size_t)FFN_B200_GROUPED_MIN_PAIRS * E));
+  if (grouped) {
+    GroupedArgs g{};
+    g.experts = d->experts;
+    g.e_begin = d->expert_begin;
+    g.e_end = d->expert_end;
+    g.n_pairs = P;
+    g.hidden = (int)H;
+    g.inter = (int)I;
+    g.counts = w.ints;
+    g.offsets = w.ints + E;
+    g.pair_tok = w.pair_tok;
+    g.xh = w.xh;
+    g.ld_x = (int)H;
+    g.xe = w.xe;
+    g.h = w.hh;
+    g.y = w.y;
+    g.chunk_ws = w.chunk;
+    g.err = w.err;
+    if ((rc = launch_grouped_moe(g, st))) return rc;
+    if ((rc = launch_combine(w.y, (int)H, w.idx, w.wt, w.inv, T, (int)k, d->experts, residual, out,
+                             (int)H, st, w.err)))
+      return rc;
+    if (topk_idx)
+      FFN_CUDA_TRY(cudaMemcpyAsync(topk_idx, w.idx, P * sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
+    if (topk_w)
+      FFN_CUDA_TRY(cudaMemcpyAsync(topk_w, w.wt, P * sizeof(float), cudaMemcpyDeviceToDevice, st));
+    return 0;
+  }
   // Upper bound of slices per format (the device count is <= this).
   const int e_local = d->expert_end - d->expert_begin;
   const long long max_vexp = std::min<long long>((long long)P, (long long)P / kNTok + e_local);

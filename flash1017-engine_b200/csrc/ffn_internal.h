@@ -38,6 +38,25 @@ struct PhaseArgs {
   int *cnt;
 };
 
+// Tensor-core grouped MoE path (many tokens per expert; NVFP4 experts).
+struct GroupedArgs {
+  const ffn_b200_expert *experts;
+  int e_begin, e_end;
+  int n_pairs;
+  int hidden, inter;
+  const int *counts, *offsets;  // per expert, from the grouping kernel
+  const int32_t *pair_tok;
+  const __half *xh;             // f16 of x * 2^-xe, natural order [token][hidden]
+  int ld_x;
+  const int *xe;
+  __half *h;                    // [pair][inter]
+  float *y;                     // [pair][hidden]
+  uint8_t *chunk_ws;            // gg_chunk_bytes(n_pairs, e_end - e_begin)
+  int *err;                     // device int, nonzero after a timed-out wait
+};
+size_t gg_chunk_bytes(int n_pairs, int n_local);
+int launch_grouped_moe(const GroupedArgs &g, cudaStream_t st);
+
 // Arguments of the rank-16 core z kernel.
 struct CoreZArgs {
   const ffn_b200_expert *experts;
@@ -67,14 +86,16 @@ int launch_exact_matvec(const float *w32, const uint16_t *w16, const float *x, i
                         int rows, int H, float *out, cudaStream_t st);
 int launch_router(const float *w, const float *bias, const float *x, const __half *xh,
                   const __half *xl, const int *xe, int mode, int n_tok, int n_exp, int H,
-                  int top_k, int score_fn, float *logits, int32_t *idx, float *wt,
+                  int top_k, int score_fn, float *logits /* 4 planes of n_tok x n_exp */,
+                  int32_t *idx, float *wt,
                   cudaStream_t st);
 int launch_group(const int32_t *idx, int n_tok, int top_k, int n_exp, int e_begin, int e_end,
                  const ffn_b200_expert *experts, int *ws_int, int32_t *pair_tok, int32_t *inv,
                  VExp *vexp_nv, VExp *vexp_tn, int *n_vexp, cudaStream_t st);
 int launch_combine(const float *y, int ld_y, const int32_t *idx, const float *wt,
                    const int32_t *inv, int n_tok, int top_k, const ffn_b200_expert *experts,
-                   const float *residual, float *out, int H, cudaStream_t st);
+                   const float *residual, float *out, int H, cudaStream_t st,
+                   const int *err = nullptr);
 int launch_scatter_axpy(const float *y, const int64_t *dst, const float *w, int m, int H,
                         float *out, cudaStream_t st);
 int launch_dot(int mode, const void *a, const void *aux, const float *x, size_t len, float *out,

@@ -734,8 +734,11 @@ int launch_exact_matvec(const float *w32, const uint16_t *w16, const float *x, i
 // k-step (wh*xh + wh*xl + wl*xh) leave an error of about 2^-22 relative.  The
 // summation order differs from the CPU loop, so selections can differ from the
 // reference's only where two biased scores are within that error.
-// CTA = 32 experts x 32 tokens; the 8 warps split K; shared-memory reduction.
+// CTA = 32 experts x 32 tokens x one of gridDim.z K-ranges; the 8 warps split
+// the range; shared-memory reduction.  Each K-range writes its own partial
+// logits (logits + z * n_tok * n_exp); top-k adds the partials in z order.
 constexpr int kRouterWarps = 8;  // router_tc_kernel runs 256 threads
+constexpr int kRouterKSplit = 4;  // K-ranges of the tensor router (partial logit planes)
 __global__ void __launch_bounds__(256) router_tc_kernel(const float *__restrict__ w,
                                                         const __half *__restrict__ xh,
                                                         const __half *__restrict__ xl,
@@ -746,6 +749,9 @@ __global__ void __launch_bounds__(256) router_tc_kernel(const float *__restrict_
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int e0 = blockIdx.x * 32, t0 = blockIdx.y * 32;
+  const int ksteps = H / 16, kz = (ksteps + gridDim.z - 1) / gridDim.z;
+  const int ks_lo = blockIdx.z * kz, ks_hi = min(ksteps, ks_lo + kz);
+  logits += (size_t)blockIdx.z * n_tok * n_exp;
   float acc[2][4][4];
 #pragma unroll
   for (int i = 0; i < 2; ++i)
@@ -768,7 +774,8 @@ __global__ void __launch_bounds__(256) router_tc_kernel(const float *__restrict_
     ph[j] = xh + (size_t)min(tok, n_tok - 1) * H;
     pl[j] = xl + (size_t)min(tok, n_tok - 1) * H;
   }
-  for (int ks = warp; ks < H / 16; ks += kRouterWarps) {
+#pragma unroll 2
+  for (int ks = ks_lo + warp; ks < ks_hi; ks += kRouterWarps) {
     const int c = ks * 16 + 4 * t;
     uint32_t ah[2][4], al[2][4];
 #pragma unroll
@@ -837,24 +844,56 @@ __device__ __forceinline__ float score_of(float l, int fn) {
 __global__ void __launch_bounds__(256) topk_kernel(const float *__restrict__ logits,
                                                    const float *__restrict__ bias, int n_tok,
                                                    int n_exp, int top_k, int score_fn,
-                                                   int32_t *idx, float *wt) {
+                                                   int n_part, int32_t *idx, float *wt) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= n_tok) return;
   const float *lg = logits + (size_t)warp * n_exp;
+  const size_t plane = (size_t)n_tok * n_exp;
+  // logit of expert e: the partial planes added in order
+  auto logit = [&](int e) {
+    float l = lg[e];
+#pragma unroll
+    for (int z = 1; z < kRouterKSplit; ++z)
+      if (z < n_part) l += lg[z * plane + e];
+    return l;
+  };
   float sel_score[kTopKMax];
   int sel_idx[kTopKMax];
   float prev_b = INFINITY;
   int prev_i = -1;
+  // scores and biased scores of this lane's experts (lane + 32j), computed once
+  constexpr int kCache = 16;
+  float cs[kCache], cb[kCache];
+  const bool cached = n_exp <= 32 * kCache;
+  if (cached) {
+#pragma unroll
+    for (int j = 0; j < kCache; ++j) {
+      const int e = lane + 32 * j;
+      cs[j] = e < n_exp ? score_of(logit(e), score_fn) : 0.f;
+      cb[j] = e < n_exp ? cs[j] + (bias ? bias[e] : 0.0f) : -INFINITY;
+    }
+  }
   for (int k = 0; k < top_k; ++k) {
     // best candidate strictly after (prev_b, prev_i) in (biased desc, index asc) order
     float bb = -INFINITY, bs = 0.f;
     int bi = 0x7fffffff;
-    for (int e = lane; e < n_exp; e += 32) {
-      const float s = score_of(lg[e], score_fn);
-      const float b = s + (bias ? bias[e] : 0.0f);
-      const bool after = b < prev_b || (b == prev_b && e > prev_i);
-      const bool better = b > bb || (b == bb && e < bi);
-      if (after && better) { bb = b; bs = s; bi = e; }
+    if (cached) {
+#pragma unroll
+      for (int j = 0; j < kCache; ++j) {
+        const int e = lane + 32 * j;
+        const float b = cb[j];
+        const bool after = b < prev_b || (b == prev_b && e > prev_i);
+        const bool better = b > bb || (b == bb && e < bi);
+        if (e < n_exp && after && better) { bb = b; bs = cs[j]; bi = e; }
+      }
+    } else {
+      for (int e = lane; e < n_exp; e += 32) {
+        const float s = score_of(logit(e), score_fn);
+        const float b = s + (bias ? bias[e] : 0.0f);
+        const bool after = b < prev_b || (b == prev_b && e > prev_i);
+        const bool better = b > bb || (b == bb && e < bi);
+        if (after && better) { bb = b; bs = s; bi = e; }
+      }
     }
     for (int o = 16; o; o >>= 1) {
       const float ob = __shfl_xor_sync(0xffffffffu, bb, o);
@@ -883,17 +922,20 @@ int launch_router(const float *w, const float *bias, const float *x, const __hal
                   const __half *xl, const int *xe, int mode, int n_tok, int n_exp, int H,
                   int top_k, int score_fn, float *logits, int32_t *idx, float *wt,
                   cudaStream_t st) {
+  int n_part = 1;  // partial logit planes top-k adds up
   if (mode == FFN_B200_ROUTER_EXACT) {
     int rc = launch_exact_matvec(w, nullptr, x, n_tok, n_exp, H, logits, st);
     if (rc) return rc;
   } else {
-    dim3 g1((n_exp + 31) / 32, (n_tok + 31) / 32);
+    n_part = std::max(1, std::min(kRouterKSplit, H / 16 / kRouterWarps));
+    dim3 g1((n_exp + 31) / 32, (n_tok + 31) / 32, n_part);
     if (g1.y > 65535) return fail(FFN_B200_EINVAL, "router: too many tokens");
     FFN_LAUNCH(FFN_B200_K_ROUTER, st, "router_tc_kernel",
                router_tc_kernel<<<g1, 256, 0, st>>>(w, xh, xl, xe, n_tok, n_exp, H, logits));
   }
-  FFN_LAUNCH(FFN_B200_K_TOPK, st, "topk_kernel", topk_kernel<<<(n_tok + 7) / 8, 256, 0, st>>>(logits, bias, n_tok, n_exp, top_k, score_fn, idx,
-                                               wt));
+  FFN_LAUNCH(FFN_B200_K_TOPK, st, "topk_kernel",
+             topk_kernel<<<(n_tok + 7) / 8, 256, 0, st>>>(logits, bias, n_tok, n_exp, top_k, score_fn,
+                                                          n_part, idx, wt));
   return 0;
 }
 
@@ -1015,8 +1057,13 @@ __global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ 
                                                       const float *__restrict__ wt,
                                                       const int32_t *__restrict__ inv, int top_k,
                                                       const ffn_b200_expert *__restrict__ experts,
-                                                      const float *residual, float *out, int H) {
+                                                      const float *residual, float *out, int H,
+                                                      const int *err) {
   const int t = blockIdx.x;
+  if (err && *err) {  // an upstream kernel gave up on a wait: make the failure visible
+    for (int c = threadIdx.x; c < H; c += blockDim.x) out[(size_t)t * H + c] = __int_as_float(0x7FC00000);
+    return;
+  }
   __shared__ float wk[kTopKMax];
   __shared__ int pk[kTopKMax];
   if (threadIdx.x < top_k) {
@@ -1028,6 +1075,35 @@ __global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ 
     pk[threadIdx.x] = inv[q];
   }
   __syncthreads();
+  if (H % 4 == 0 && ld_y % 4 == 0 && ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(out) |
+                                       reinterpret_cast<uintptr_t>(residual)) & 15) == 0) {
+    // four columns per thread and step, every load of a step in flight at once
+#pragma unroll 4
+    for (int c = 4 * threadIdx.x; c < H; c += 4 * blockDim.x) {
+      float4 yv[kTopKMax];
+#pragma unroll
+      for (int k = 0; k < kTopKMax; ++k)
+        if (k < top_k && pk[k] >= 0) yv[k] = __ldg(reinterpret_cast<const float4 *>(y + (size_t)pk[k] * ld_y + c));
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < kTopKMax; ++k)
+        if (k < top_k && pk[k] >= 0) {
+          acc.x = __fadd_rn(acc.x, __fmul_rn(wk[k], yv[k].x));
+          acc.y = __fadd_rn(acc.y, __fmul_rn(wk[k], yv[k].y));
+          acc.z = __fadd_rn(acc.z, __fmul_rn(wk[k], yv[k].z));
+          acc.w = __fadd_rn(acc.w, __fmul_rn(wk[k], yv[k].w));
+        }
+      if (residual) {
+        const float4 r = *reinterpret_cast<const float4 *>(residual + (size_t)t * H + c);
+        acc.x = __fadd_rn(r.x, acc.x);
+        acc.y = __fadd_rn(r.y, acc.y);
+        acc.z = __fadd_rn(r.z, acc.z);
+        acc.w = __fadd_rn(r.w, acc.w);
+      }
+      *reinterpret_cast<float4 *>(out + (size_t)t * H + c) = acc;
+    }
+    return;
+  }
   for (int c = threadIdx.x; c < H; c += blockDim.x) {
     float acc = 0.f;
     for (int k = 0; k < top_k; ++k) {
@@ -1041,9 +1117,10 @@ __global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ 
 
 int launch_combine(const float *y, int ld_y, const int32_t *idx, const float *wt,
                    const int32_t *inv, int n_tok, int top_k, const ffn_b200_expert *experts,
-                   const float *residual, float *out, int H, cudaStream_t st) {
+                   const float *residual, float *out, int H, cudaStream_t st, const int *err) {
   if (n_tok <= 0) return 0;
-  FFN_LAUNCH(FFN_B200_K_COMBINE, st, "combine_kernel", combine_kernel<<<n_tok, 256, 0, st>>>(y, ld_y, idx, wt, inv, top_k, experts, residual, out, H));
+  FFN_LAUNCH(FFN_B200_K_COMBINE, st, "combine_kernel",
+             combine_kernel<<<n_tok, 256, 0, st>>>(y, ld_y, idx, wt, inv, top_k, experts, residual, out, H, err));
   return 0;
 }
 

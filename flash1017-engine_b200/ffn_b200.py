@@ -18,6 +18,8 @@ LIB_PATH = os.path.join(HERE, "_build", "libffn_b200.so")
 FMT_NVFP4, FMT_TERNARY = 0, 1
 SCORE_REF, SCORE_SIGMOID = 0, 1
 ROUTER_EXACT, ROUTER_TENSOR = 0, 1
+PATH_AUTO, PATH_GEMV, PATH_GROUPED = 0, 1, 2
+GROUPED_MIN_PAIRS = 48
 ERRORS = {0: "OK", -1: "EINVAL", -2: "ECUDA", -3: "ENOSPC", -4: "ENCCL", -5: "EUNSUP"}
 
 # Symbols the public headers declare (checked by the CPU test suite).
@@ -39,8 +41,9 @@ EXPORTS = [
 # Kernel kinds of ffn_b200_profile_read (FFN_B200_K_*).
 K_XPREP, K_ROUTER, K_TOPK, K_GROUP, K_GATEUP_NVFP4, K_DOWN_NVFP4 = 0, 1, 2, 3, 4, 5
 K_GATEUP_TERNARY, K_DOWN_TERNARY, K_COREZ, K_COMBINE, K_MATVEC, K_OTHER = 6, 7, 8, 9, 10, 11
+K_GEMM_GATEUP, K_GEMM_DOWN = 12, 13
 K_NAMES = ["xprep", "router", "topk", "group", "gateup_nvfp4", "down_nvfp4", "gateup_ternary",
-           "down_ternary", "corez", "combine", "matvec", "other"]
+           "down_ternary", "corez", "combine", "matvec", "other", "gemm_gateup", "gemm_down"]
 
 
 def build() -> str:
@@ -75,7 +78,7 @@ class MoeDesc(C.Structure):
                 ("router_mode", C.c_int32), ("expert_begin", C.c_int32),
                 ("expert_end", C.c_int32), ("has_nvfp4", C.c_int32),
                 ("has_ternary", C.c_int32), ("norm_w", C.c_void_p), ("norm_eps", C.c_float),
-                ("reserved", C.c_int32)]
+                ("path", C.c_int32)]
 
 
 assert C.sizeof(Expert) == 224, C.sizeof(Expert)
@@ -387,7 +390,7 @@ class MoeLayer:
 
     def __init__(self, experts, router_w, hidden, inter, top_k=6, score_fn=SCORE_SIGMOID,
                  router_bias=None, router_mode=ROUTER_EXACT, expert_range=None, device="cuda",
-                 table=None, ws=None, norm_w=None, norm_eps=1e-20):
+                 table=None, ws=None, norm_w=None, norm_eps=1e-20, path=PATH_AUTO):
         self.experts = experts  # SwigluExpert list (None allowed outside expert_range)
         self.router_w = router_w
         self.router_bias = router_bias
@@ -402,7 +405,7 @@ class MoeLayer:
         self.desc = MoeDesc(hidden, inter, n, top_k, _ptr(self.table), _ptr(router_w),
                             _ptr(router_bias), score_fn, router_mode, lo, hi,
                             int(FMT_NVFP4 in fmts or not fmts), int(FMT_TERNARY in fmts),
-                            _ptr(norm_w), float(norm_eps), 0)
+                            _ptr(norm_w), float(norm_eps), int(path))
         self.ws = ws if ws is not None else Workspace(device)
 
     def ws_bytes(self, n_tok: int) -> int:

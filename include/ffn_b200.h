@@ -163,8 +163,17 @@ typedef struct ffn_b200_moe_desc {
      * + norm_eps) * norm_w.  NULL: the experts see x itself. */
     const float *norm_w;             /* DEVICE [hidden] or NULL */
     float norm_eps;
-    int32_t reserved;
+    /* FFN_B200_PATH_*: AUTO (0) takes the tensor-core grouped GEMM when the
+     * layer has only NVFP4 experts, hidden and inter are multiples of 128 and
+     * the routed pairs average >= FFN_B200_GROUPED_MIN_PAIRS per expert
+     * (prefill), else the GEMV slices (decode). */
+    int32_t path;
 } ffn_b200_moe_desc;
+
+#define FFN_B200_PATH_AUTO 0
+#define FFN_B200_PATH_GEMV 1    /* slices of <= 8 tokens, f16 hi/lo activations (~fp32) */
+#define FFN_B200_PATH_GROUPED 2 /* tcgen05 grouped GEMM, f16 activations (rel. err ~2e-4) */
+#define FFN_B200_GROUPED_MIN_PAIRS 48
 
 FFN_B200_EXPORT size_t ffn_b200_moe_ws_bytes(const ffn_b200_moe_desc *d, size_t max_tokens);
 /* x [n_tok, hidden] f32; out [n_tok, hidden] = residual + moe(xn) when
@@ -216,7 +225,9 @@ FFN_B200_EXPORT int ffn_b200_dequant_ternary(size_t rows, size_t cols, const uin
 #define FFN_B200_K_COMBINE 9
 #define FFN_B200_K_MATVEC 10
 #define FFN_B200_K_OTHER 11
-#define FFN_B200_K_COUNT 12
+#define FFN_B200_K_GEMM_GATEUP 12 /* grouped tensor-core path */
+#define FFN_B200_K_GEMM_DOWN 13
+#define FFN_B200_K_COUNT 14
 FFN_B200_EXPORT int ffn_b200_profile_enable(int enable);
 FFN_B200_EXPORT int ffn_b200_profile_read(int kind, double *total_ms, uint64_t *launches);
 

@@ -2,17 +2,21 @@
 // expert: the MoE prefill path (batched tokens of crates/flash-core/src/
 // flash1017.rs:8267-8326, the same arithmetic as the decode path).
 //
-// Per local expert the routed tokens form chunks of <= 256 pairs.  A tile is
+// Per local expert the routed tokens form chunks of <= 128 pairs.  A tile is
 // (chunk, block of 128 output rows); one CTA per SM walks the tiles.
 //
 //   phase 1:  D_g = W1[rows] . X^T, D_u = W3[rows] . X^T  (K = hidden)
 //             h[p][row] = f16( min(silu(g), 10) * clamp(u, -10, 10) ),
 //             g = D_g * 2^xe[tok] * gs1, u = D_u * 2^xe[tok] * gs3
 //   phase 2:  y[p][row] = (W2[rows] . H^T) * gs2                (K = inter)
+//             (a tile covers 256 down rows as two 128-row blocks, so each
+//             activation tile feeds as many MMAs as in phase 1)
 //
 // MMA: tcgen05.mma.cta_group::1.kind::f16, M = 128 weight rows, N = chunk
 // tokens rounded up to 16, K = 16 per instruction, fp32 accumulators in TMEM
-// (phase 1: gate in columns [0, 256), up in [256, 512)).  Operands are K-major
+// (double-buffered: tile t uses buffer t % 2, so the epilogue of one tile
+// overlaps the next tile's MMAs; phase 1 keeps gate in the buffer's first 128
+// columns and up in the next 128).  Operands are K-major
 // tiles of 64 columns in the 128-byte swizzled canonical layout.
 //
 // Weights: NVFP4 rows are decoded on the fly into f16 (exact: an E2M1 value
@@ -22,16 +26,19 @@
 // there); phase 2 takes h rounded to f16.  Relative error of an output about
 // 2^-12 (measured ~2e-4), inside the path's 1e-3 tolerance.
 //
-// Warp roles (256 threads):
-//   warps 0, 1, 3  producers: cp.async of the raw NVFP4 rows + scales of the
-//                  tile's K-step into a raw stage, and of the chunk's
-//                  activation rows straight into their swizzled B tile;
-//                  completion is an mbarrier arrive per lane (noinc).
+// Warp roles (384 threads):
+//   warp 0         weight producer: cp.async of the tile's NVFP4 rows + block
+//                  scales for each K-step into a 6-deep ring (from DRAM).
+//   warps 1, 3     activation producers: cp.async of the chunk's rows straight
+//                  into their swizzled B tile, 3-deep ring (L2 hits mostly).
+//                  Producer completion is an mbarrier arrive per lane (noinc).
 //   warp 2         TMEM allocation; lane 0 issues the MMAs and commits them to
-//                  the stage / accumulator barriers.
-//   warps 4-7      decode a raw stage into the f16 A tile(s) (thread = row),
-//                  and after a tile's last K-step run the epilogue from TMEM
-//                  (warp w reads TMEM lanes 32 (w % 4) ...).
+//                  the ring / accumulator barriers.
+//   warps 4-11     decode a weight stage into the f16 A tile(s) (thread = row of
+//                  one matrix, or half a row's columns in phase 2), and after
+//                  a tile's last K-step run the epilogue from TMEM (warp w
+//                  reads TMEM lanes 32 (w % 4) ..., warps 4-7 the first half
+//                  of the tile's columns, warps 8-11 the second).
 // Every mbarrier wait is bounded; a wait that runs out sets *err and the
 // kernel drains and returns (the host turns *err into FFN_B200_ECUDA).
 #include <algorithm>
@@ -42,26 +49,37 @@
 namespace ffn {
 namespace gg {
 
-constexpr int kThreadsGG = 256;
-constexpr int kRawStages = 3;
-constexpr int kAStages = 2;
+constexpr int kThreadsGG = 384;
+constexpr int kDecWarps = 8;   // warps 4-11: decode + epilogue
+constexpr int kWStages = 6;    // NVFP4 rows + scales per K-step (from DRAM: deep ring)
+constexpr int kXStages = 3;    // activation tiles per K-step (mostly L2 hits)
+constexpr int kAStages = 2;    // decoded f16 weight tiles
 constexpr int kTileM = 128;
 constexpr int kTileK = 64;
-constexpr int kMaxN = 256;
-constexpr int kProducerLanes = 96;  // warps 0, 1, 3
+constexpr int kMaxN = 256;     // tokens per chunk (MMA N)
+constexpr int kWLanes = 32;    // warp 0: weight producer
+constexpr int kXLanes = 64;    // warps 1, 3: activation producers
 constexpr long long kSpinLimit = 1LL << 22;  // try_wait polls per wait before giving up
 
+// A tile = 2 blocks of 128 weight rows sharing one activation tile: gate and
+// up rows (phase 1), or 256 consecutive down rows (phase 2).
 template <int PH>
 struct Layout {
-  static constexpr int NMAT = PH == 1 ? 2 : 1;
-  static constexpr int RAW_W = NMAT * kTileM * 32;   // NVFP4 bytes of a K-step
-  static constexpr int RAW_S = NMAT * kTileM * 4;    // scale bytes of a K-step
-  static constexpr int RAW_X = kMaxN * 128;          // activation tile (swizzled)
-  static constexpr int RAW = (RAW_X + RAW_W + RAW_S + 1023) & ~1023;  // x first, 1024-aligned stages
-  static constexpr int A_TILE = kTileM * 128;        // one f16 A tile
+  static constexpr int NMAT = 2;                                  // A blocks per tile
+  static constexpr int ROWS = PH == 1 ? kTileM : 2 * kTileM;      // output rows per tile
+  static constexpr int X_STAGE = kMaxN * 128;                    // swizzled B tile (1024-aligned)
+  static constexpr int A_TILE = kTileM * 128;                    // one f16 A tile
   static constexpr int A_STAGE = NMAT * A_TILE;
-  static constexpr int SMEM = 1024 + kRawStages * RAW + kAStages * A_STAGE;
-  static constexpr int TMEM_COLS = PH == 1 ? 512 : 256;
+  static constexpr int W_W = NMAT * kTileM * 32;                 // NVFP4 bytes of a K-step
+  static constexpr int W_S = NMAT * kTileM * 4;                  // scale bytes of a K-step
+  static constexpr int W_STAGE = W_W + W_S;
+  static constexpr int OFF_A = kXStages * X_STAGE;
+  static constexpr int OFF_W = OFF_A + kAStages * A_STAGE;
+  static constexpr int SMEM = 1024 + OFF_W + kWStages * W_STAGE;
+  // two blocks x 256 columns: one accumulator buffer
+  static constexpr int ACC_BUFS = 1;
+  static constexpr int ACC_COLS = NMAT * kMaxN;
+  static constexpr int TMEM_COLS = ACC_BUFS * ACC_COLS;         // 512
 };
 
 struct Chunk {
@@ -153,20 +171,21 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
   using L = Layout<PH>;
   constexpr int NMAT = L::NMAT;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t raw_full[kRawStages], raw_empty[kRawStages];
+  __shared__ __align__(8) uint64_t w_full[kWStages], w_empty[kWStages];
+  __shared__ __align__(8) uint64_t x_full[kXStages], x_empty[kXStages];
   __shared__ __align__(8) uint64_t a_full[kAStages], a_empty[kAStages];
-  __shared__ __align__(8) uint64_t acc_full, acc_empty, mma_done;
+  __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], mma_done;
   __shared__ uint32_t s_tmem;
+  __shared__ float s_xs[2][kMaxN];  // phase 1: 2^xe of the tile's tokens (by tile parity)
   uint8_t *smem = smem_raw + ((1024 - (sa(smem_raw) & 1023)) & 1023);
-  uint8_t *raw = smem;
-  uint8_t *abuf = smem + kRawStages * L::RAW;
+  uint8_t *xbuf = smem, *abuf = smem + L::OFF_A, *wbuf = smem + L::OFF_W;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
-    for (int s = 0; s < kRawStages; ++s) { bar_init(&raw_full[s], kProducerLanes); bar_init(&raw_empty[s], 5); }
-    for (int s = 0; s < kAStages; ++s) { bar_init(&a_full[s], 4); bar_init(&a_empty[s], 1); }
-    bar_init(&acc_full, 1);
-    bar_init(&acc_empty, 4);
+    for (int s = 0; s < kWStages; ++s) { bar_init(&w_full[s], kWLanes); bar_init(&w_empty[s], kDecWarps); }
+    for (int s = 0; s < kXStages; ++s) { bar_init(&x_full[s], kXLanes); bar_init(&x_empty[s], 1); }
+    for (int s = 0; s < kAStages; ++s) { bar_init(&a_full[s], kDecWarps); bar_init(&a_empty[s], 1); }
+    for (int b = 0; b < 2; ++b) { bar_init(&acc_full[b], 1); bar_init(&acc_empty[b], kDecWarps); }
     bar_init(&mma_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -181,83 +200,117 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
   const uint32_t tmem = s_tmem;
 
   const int n_chunks = *a.n_chunks;
-  const int fb_count = a.rows / kTileM;
+  const int fb_count = a.rows / L::ROWS;
   const int n_tiles = n_chunks * fb_count;
   const int KT = a.K / kTileK;
   const size_t wld = (size_t)a.K / 2, sld = (size_t)a.K / 16;
 
-  if (warp == 0 || warp == 1 || warp == 3) {
-    // ------------------------------------------------------------ producers
-    const int pl = warp == 3 ? 64 + lane : warp * 32 + lane;  // 0..95
+  if (warp == 0) {
+    // ------------------------------------------------ weight producer (32 lanes)
+    const int pl = lane;
+    constexpr int WI = NMAT * kTileM * 2 / kWLanes;  // 16-byte weight pieces per lane
+    constexpr int SI = NMAT * kTileM / kWLanes;      // 4-byte scale pieces per lane
     int it = 0;
     bool live = true;
     for (int tile = blockIdx.x; tile < n_tiles && live; tile += gridDim.x) {
       const Chunk ch = a.chunks[tile / fb_count];
-      const int row0 = (tile % fb_count) * kTileM;
+      const int row0 = (tile % fb_count) * L::ROWS;
       const ffn_b200_expert &E = a.experts[ch.expert];
-      const uint8_t *wsrc[NMAT], *ssrc[NMAT];
+      const uint8_t *ws_[WI], *ss[SI];
+      // block mi: phase 1 gate (mi 0) / up (mi 1) rows row0..; phase 2 down rows row0 + 128 mi..
+      auto blk_w = [&](int mi) { return PH == 1 ? E.nv[mi].w : E.nv[2].w + (size_t)mi * kTileM * wld; };
+      auto blk_s = [&](int mi) { return PH == 1 ? E.nv[mi].s : E.nv[2].s + (size_t)mi * kTileM * sld; };
+      uint32_t wd[WI], sd[SI];
 #pragma unroll
-      for (int mi = 0; mi < NMAT; ++mi) {
-        const ffn_b200_nvfp4_mat &m = E.nv[PH == 1 ? mi : 2];
-        wsrc[mi] = m.w + (size_t)row0 * wld;
-        ssrc[mi] = m.s + (size_t)row0 * sld;
+      for (int j = 0; j < WI; ++j) {
+        const int q = pl + kWLanes * j;
+        const int mi = q / (kTileM * 2), r = (q >> 1) % kTileM, half = q & 1;
+        ws_[j] = blk_w(mi) + (size_t)(row0 + r) * wld + half * 16;
+        wd[j] = mi * kTileM * 32 + r * 32 + half * 16;
+      }
+#pragma unroll
+      for (int j = 0; j < SI; ++j) {
+        const int q = pl + kWLanes * j;
+        const int mi = q / kTileM, r = q % kTileM;
+        ss[j] = blk_s(mi) + (size_t)(row0 + r) * sld;
+        sd[j] = L::W_W + mi * kTileM * 4 + r * 4;
       }
       for (int kt = 0; kt < KT; ++kt, ++it) {
-        const int s = it % kRawStages;
-        if (!bar_wait(&raw_empty[s], ((it / kRawStages) & 1) ^ 1, a.err)) { live = false; break; }
-        uint8_t *st = raw + s * L::RAW;
-        // activation rows: chunk row n, 16-byte piece kc -> swizzled B tile
-        for (int q = pl; q < ch.nn * 8; q += kProducerLanes) {
-          const int n = q >> 3, kc = q & 7;
+        const int s = it % kWStages;
+        if (!bar_wait(&w_empty[s], ((it / kWStages) & 1) ^ 1, a.err)) { live = false; break; }
+        uint8_t *st = wbuf + s * L::W_STAGE;
+#pragma unroll
+        for (int j = 0; j < WI; ++j) cp_async16(st + wd[j], ws_[j] + kt * 32);
+#pragma unroll
+        for (int j = 0; j < SI; ++j) cp_async4(st + sd[j], ss[j] + kt * 4);
+        cp_async_bar_arrive(&w_full[s]);
+      }
+    }
+  } else if (warp == 1 || warp == 3) {
+    // ------------------------------------------------ activation producers (64 lanes)
+    constexpr int RI = kMaxN / kXLanes;  // rows per lane
+    const int xl = warp == 1 ? lane : 32 + lane;
+    int it = 0;
+    bool live = true;
+    for (int tile = blockIdx.x; tile < n_tiles && live; tile += gridDim.x) {
+      const Chunk ch = a.chunks[tile / fb_count];
+      const __half *rp[RI];
+#pragma unroll
+      for (int j = 0; j < RI; ++j) {
+        const int n = xl + kXLanes * j;
+        rp[j] = nullptr;
+        if (n < ch.nn) {
           const int p = ch.p0 + n;
           const int xr = PH == 1 ? __ldg(a.pair_tok + p) : p;
-          cp_async16(st + sw128(n, kc), a.x + (size_t)xr * a.ld_x + kt * kTileK + kc * 8);
+          rp[j] = a.x + (size_t)xr * a.ld_x;
         }
-        // NVFP4 rows: 128 rows x 32 bytes per matrix (2 pieces of 16 bytes)
+      }
+      for (int kt = 0; kt < KT; ++kt, ++it) {
+        const int s = it % kXStages;
+        if (!bar_wait(&x_empty[s], ((it / kXStages) & 1) ^ 1, a.err)) { live = false; break; }
+        uint8_t *st = xbuf + s * L::X_STAGE;
 #pragma unroll
-        for (int mi = 0; mi < NMAT; ++mi)
-          for (int q = pl; q < kTileM * 2; q += kProducerLanes) {
-            const int r = q >> 1, half = q & 1;
-            cp_async16(st + L::RAW_X + mi * kTileM * 32 + r * 32 + half * 16,
-                       wsrc[mi] + (size_t)r * wld + kt * 32 + half * 16);
+        for (int j = 0; j < RI; ++j)
+          if (rp[j]) {
+            const int n = xl + kXLanes * j;
+#pragma unroll
+            for (int kc = 0; kc < 8; ++kc) cp_async16(st + sw128(n, kc), rp[j] + kt * kTileK + kc * 8);
           }
-        // block scales: 128 rows x 4 bytes per matrix
-#pragma unroll
-        for (int mi = 0; mi < NMAT; ++mi)
-          for (int r = pl; r < kTileM; r += kProducerLanes)
-            cp_async4(st + L::RAW_X + L::RAW_W + mi * kTileM * 4 + r * 4, ssrc[mi] + (size_t)r * sld + kt * 4);
-        cp_async_bar_arrive(&raw_full[s]);
+        cp_async_bar_arrive(&x_full[s]);
       }
     }
   } else if (warp == 2) {
-    // ------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------ MMA issuer
     if (lane == 0) {
-      int it = 0, ait = 0, tcount = 0;
+      int itx = 0, ita = 0, tcount = 0;
       bool live = true;
       for (int tile = blockIdx.x; tile < n_tiles && live; tile += gridDim.x, ++tcount) {
         const Chunk ch = a.chunks[tile / fb_count];
         const uint32_t id = idesc_f16(kTileM, ch.npad);
-        if (!bar_wait(&acc_empty, (tcount & 1) ^ 1, a.err)) break;
+        const int b = L::ACC_BUFS == 1 ? 0 : (tcount & 1);
+        const int use = L::ACC_BUFS == 1 ? tcount : (tcount >> 1);
+        if (!bar_wait(&acc_empty[b], (use & 1) ^ 1, a.err)) break;
         tc_fence_after();
-        for (int kt = 0; kt < KT; ++kt, ++it, ++ait) {
-          const int s = it % kRawStages, s2 = ait % kAStages;
-          if (!bar_wait(&raw_full[s], (it / kRawStages) & 1, a.err) ||
-              !bar_wait(&a_full[s2], (ait / kAStages) & 1, a.err)) { live = false; break; }
+        const uint32_t acc_col = tmem + b * L::ACC_COLS;
+        for (int kt = 0; kt < KT; ++kt, ++itx, ++ita) {
+          const int s3 = itx % kXStages, s2 = ita % kAStages;
+          if (!bar_wait(&x_full[s3], (itx / kXStages) & 1, a.err) ||
+              !bar_wait(&a_full[s2], (ita / kAStages) & 1, a.err)) { live = false; break; }
           fence_async_smem();
           tc_fence_after();
-          const uint32_t xb = sa(raw + s * L::RAW);
+          const uint32_t xb = sa(xbuf + s3 * L::X_STAGE);
           const uint32_t ab = sa(abuf + s2 * L::A_STAGE);
 #pragma unroll
           for (int mi = 0; mi < NMAT; ++mi)
 #pragma unroll
             for (int j = 0; j < kTileK / 16; ++j)
-              tc_mma(tmem + mi * 256, sdesc(ab + mi * L::A_TILE + 32 * j), sdesc(xb + 32 * j), id,
+              tc_mma(acc_col + mi * kMaxN, sdesc(ab + mi * L::A_TILE + 32 * j), sdesc(xb + 32 * j), id,
                      (kt > 0 || j > 0) ? 1u : 0u);
           tc_commit(&a_empty[s2]);
-          tc_commit(&raw_empty[s]);
+          tc_commit(&x_empty[s3]);
         }
         if (!live) break;
-        tc_commit(&acc_full);
+        tc_commit(&acc_full[b]);
       }
       // every MMA this thread issued has completed before TMEM is freed
       tc_commit(&mma_done);
@@ -265,75 +318,88 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------ decode + epilogue
-    const int r = tid - 128;  // tile row, 0..127 (warps 4-7 = TMEM lane quarters 0-3)
-    int it = 0, ait = 0, tcount = 0;
+    // ------------------------------------------------ decode + epilogue (8 warps)
+    const int d = tid - 128, half = d >> 7;
+    const int r = d & 127;  // tile row = TMEM lane (warp w: quarter w % 4)
+    // half h decodes row r of A block h
+    const int mi = half;
+    int itw = 0, ita = 0, tcount = 0;
     bool live = true;
     for (int tile = blockIdx.x; tile < n_tiles && live; tile += gridDim.x, ++tcount) {
       const Chunk ch = a.chunks[tile / fb_count];
-      const int row0 = (tile % fb_count) * kTileM;
-      for (int kt = 0; kt < KT; ++kt, ++it, ++ait) {
-        const int s = it % kRawStages, s2 = ait % kAStages;
-        const bool ok = bar_wait(&raw_full[s], (it / kRawStages) & 1, a.err) &&
-                        bar_wait(&a_empty[s2], ((ait / kAStages) & 1) ^ 1, a.err);
+      const int row0 = (tile % fb_count) * L::ROWS;
+      if (PH == 1) {
+        // token scales of the tile's columns, read by every epilogue thread;
+        // a buffer is rewritten two tiles later, after all decode warps have
+        // finished this tile's epilogue (the next tile's MMAs wait for that)
+        s_xs[tcount & 1][d] = d < ch.nn ? pow2f(__ldg(a.xe + __ldg(a.pair_tok + ch.p0 + d))) : 0.f;
+        asm volatile("bar.sync 1, %0;" ::"n"(kDecWarps * 32) : "memory");
+      }
+      for (int kt = 0; kt < KT; ++kt, ++itw, ++ita) {
+        const int s = itw % kWStages, s2 = ita % kAStages;
+        const bool ok = bar_wait(&w_full[s], (itw / kWStages) & 1, a.err) &&
+                        bar_wait(&a_empty[s2], ((ita / kAStages) & 1) ^ 1, a.err);
         if (!__all_sync(0xffffffffu, ok)) { live = false; break; }
-        const uint8_t *st = raw + s * L::RAW;
+        const uint8_t *st = wbuf + s * L::W_STAGE;
         uint8_t *at = abuf + s2 * L::A_STAGE;
-#pragma unroll
-        for (int mi = 0; mi < NMAT; ++mi) {
-          const uint4 w0 = *reinterpret_cast<const uint4 *>(st + L::RAW_X + mi * kTileM * 32 + r * 32);
-          const uint4 w1 = *reinterpret_cast<const uint4 *>(st + L::RAW_X + mi * kTileM * 32 + r * 32 + 16);
-          const uint32_t sc4 = *reinterpret_cast<const uint32_t *>(st + L::RAW_X + L::RAW_W + mi * kTileM * 4 + r * 4);
+        {
+          const uint4 w0 = *reinterpret_cast<const uint4 *>(st + mi * kTileM * 32 + r * 32);
+          const uint4 w1 = *reinterpret_cast<const uint4 *>(st + mi * kTileM * 32 + r * 32 + 16);
+          const uint32_t sc4 = *reinterpret_cast<const uint32_t *>(st + L::W_W + mi * kTileM * 4 + r * 4);
           const uint32_t s01 = e4m3x2_to_f16x2((uint16_t)(sc4 & 0xFFFFu));
           const uint32_t s23 = e4m3x2_to_f16x2((uint16_t)(sc4 >> 16));
           const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
           for (int j = 0; j < 8; ++j) {  // word j = columns 8j..8j+7 = 16-byte chunk j
-            uint32_t d[4];
-            e2m1x8_to_f16x2(words[j], d);
+            uint32_t dd[4];
+            e2m1x8_to_f16x2(words[j], dd);
             const uint32_t sc = j < 2 ? bcast_lo(s01) : j < 4 ? bcast_hi(s01) : j < 6 ? bcast_lo(s23) : bcast_hi(s23);
             uint4 o;
-            o.x = hmul2_u32(d[0], sc);
-            o.y = hmul2_u32(d[1], sc);
-            o.z = hmul2_u32(d[2], sc);
-            o.w = hmul2_u32(d[3], sc);
+            o.x = hmul2_u32(dd[0], sc);
+            o.y = hmul2_u32(dd[1], sc);
+            o.z = hmul2_u32(dd[2], sc);
+            o.w = hmul2_u32(dd[3], sc);
             *reinterpret_cast<uint4 *>(at + mi * L::A_TILE + sw128(r, j)) = o;
           }
         }
         fence_async_smem();
         __syncwarp();
-        if (lane == 0) { bar_arrive(&a_full[s2]); bar_arrive(&raw_empty[s]); }
+        if (lane == 0) { bar_arrive(&a_full[s2]); bar_arrive(&w_empty[s]); }
       }
       if (!live) break;
       // epilogue: this thread's TMEM lane = tile row r
-      if (!__all_sync(0xffffffffu, bar_wait(&acc_full, tcount & 1, a.err))) break;
+      const int b = L::ACC_BUFS == 1 ? 0 : (tcount & 1);
+      const int use = L::ACC_BUFS == 1 ? tcount : (tcount >> 1);
+      if (!__all_sync(0xffffffffu, bar_wait(&acc_full[b], use & 1, a.err))) break;
       tc_fence_after();
       const int row = row0 + r;
-      const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+      const uint32_t tl = tmem + b * L::ACC_COLS + ((uint32_t)(32 * (warp & 3)) << 16);
       const ffn_b200_expert &E = a.experts[ch.expert];
-      const float gs0 = E.nv[PH == 1 ? 0 : 2].gs, gs1 = E.nv[1].gs;
-      for (int n0 = 0; n0 < ch.npad; n0 += 16) {
+      const float gs0 = E.nv[PH == 1 ? 0 : 2].gs, gs1 = E.nv[PH == 1 ? 1 : 2].gs;
+      const int split = ((ch.npad / 16 + 1) / 2) * 16;  // columns [0, split) | [split, npad)
+      for (int n0 = half ? split : 0; n0 < (half ? ch.npad : split); n0 += 16) {
         uint32_t v0[16], v1[16];
         tc_ld16(tl + n0, v0);
-        if (PH == 1) tc_ld16(tl + 256 + n0, v1);
+        tc_ld16(tl + kMaxN + n0, v1);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int n = n0 + j;
-          if (n >= ch.nn) break;
+          if (n >= ch.nn) continue;
           const int p = ch.p0 + n;
           if (PH == 1) {
-            const float xs = pow2f(__ldg(a.xe + __ldg(a.pair_tok + p)));
+            const float xs = s_xs[tcount & 1][n];
             const float g = __uint_as_float(v0[j]) * xs * gs0;
             const float u = __uint_as_float(v1[j]) * xs * gs1;
             a.h[(size_t)p * a.ld_h + row] = __float2half_rn(silu10(g) * clamp10f(u));
           } else {
             a.y[(size_t)p * a.ld_y + row] = __uint_as_float(v0[j]) * gs0;
+            a.y[(size_t)p * a.ld_y + row + kTileM] = __uint_as_float(v1[j]) * gs1;
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) bar_arrive(&acc_empty);
+      if (lane == 0) bar_arrive(&acc_empty[b]);
     }
   }
   // drain: every cp.async of this thread has landed before the CTA leaves
@@ -346,8 +412,8 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
   }
 }
 
-// Chunks of <= 256 pairs per local expert, balanced inside an expert
-// (c pairs -> ceil(c / 256) chunks of equal size, rounded up to 16 columns).
+// Chunks of <= kMaxN pairs per local expert, balanced inside an expert
+// (c pairs -> ceil(c / kMaxN) chunks of equal size, rounded up to 16 columns).
 __global__ void __launch_bounds__(1024) chunk_kernel(const int *__restrict__ counts,
                                                      const int *__restrict__ offsets, int e_begin,
                                                      int e_end, Chunk *chunks, int *n_chunks) {
@@ -432,7 +498,7 @@ int launch_grouped_moe(const GroupedArgs &g, cudaStream_t st) {
   p.ld_x = g.ld_x;
   p.h = g.h;
   p.ld_h = g.inter;
-  int grid = (int)std::max(1LL, std::min<long long>(sms, max_chunks * (g.inter / kTileM)));
+  int grid = (int)std::max(1LL, std::min<long long>(sms, max_chunks * (g.inter / Layout<1>::ROWS)));
   FFN_LAUNCH(FFN_B200_K_GEMM_GATEUP, st, "grouped gemm_kernel<1>",
              (gemm_kernel<1><<<grid, kThreadsGG, Layout<1>::SMEM, st>>>(p)));
   GemmArgs q = p;
@@ -442,7 +508,7 @@ int launch_grouped_moe(const GroupedArgs &g, cudaStream_t st) {
   q.ld_x = g.inter;
   q.y = g.y;
   q.ld_y = g.hidden;
-  grid = (int)std::max(1LL, std::min<long long>(sms, max_chunks * (g.hidden / kTileM)));
+  grid = (int)std::max(1LL, std::min<long long>(sms, max_chunks * (g.hidden / Layout<2>::ROWS)));
   FFN_LAUNCH(FFN_B200_K_GEMM_DOWN, st, "grouped gemm_kernel<2>",
              (gemm_kernel<2><<<grid, kThreadsGG, Layout<2>::SMEM, st>>>(q)));
   return 0;

@@ -557,11 +557,11 @@ int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
     return fail(FFN_B200_EINVAL, "moe_layer: unknown router_mode");
   if (d->path != FFN_B200_PATH_AUTO && d->path != FFN_B200_PATH_GEMV && d->path != FFN_B200_PATH_GROUPED)
     return fail(FFN_B200_EINVAL, "moe_layer: unknown path");
-  const bool grouped_ok = !d->has_ternary && H % 256 == 0 && I % 128 == 0;
+  const bool grouped_ok = !d->has_ternary && H % 256 == 0 && I % 256 == 0;
   if (d->path == FFN_B200_PATH_GROUPED && !grouped_ok)
     return fail(FFN_B200_EUNSUP,
-                "moe_layer: the grouped path needs NVFP4-only experts, hidden a multiple of 256 and "
-                "inter a multiple of 128");
+                "moe_layer: the grouped path needs NVFP4-only experts and hidden, inter multiples "
+                "of 256");
   if (n_tok == 0) return 0;
   if (!x || !out) return fail(FFN_B200_EINVAL, "moe_layer: null x/out");
   if (n_tok * k > (1u << 24)) return fail(FFN_B200_EINVAL, "moe_layer: too many tokens");

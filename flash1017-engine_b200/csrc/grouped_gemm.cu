@@ -2,7 +2,7 @@
 // expert: the MoE prefill path (batched tokens of crates/flash-core/src/
 // flash1017.rs:8267-8326, the same arithmetic as the decode path).
 //
-// Per local expert the routed tokens form chunks of <= 128 pairs.  A tile is
+// Per local expert the routed tokens form chunks of <= 192 pairs.  A tile is
 // (chunk, block of 128 output rows); one CTA per SM walks the tiles.
 //
 //   phase 1:  D_g = W1[rows] . X^T, D_u = W3[rows] . X^T  (K = hidden)
@@ -28,7 +28,7 @@
 //
 // Warp roles (384 threads):
 //   warp 0         weight producer: cp.async of the tile's NVFP4 rows + block
-//                  scales for each K-step into a 6-deep ring (from DRAM).
+//                  scales, 4 K-steps (128 bytes of each row) per stage, 2 stages.
 //   warps 1, 3     activation producers: cp.async of the chunk's rows straight
 //                  into their swizzled B tile, 3-deep ring (L2 hits mostly).
 //                  Producer completion is an mbarrier arrive per lane (noinc).
@@ -51,12 +51,13 @@ namespace gg {
 
 constexpr int kThreadsGG = 384;
 constexpr int kDecWarps = 8;   // warps 4-11: decode + epilogue
-constexpr int kWStages = 6;    // NVFP4 rows + scales per K-step (from DRAM: deep ring)
+constexpr int kWSteps = 4;     // K-steps per weight stage: 128 contiguous bytes of each row
+constexpr int kWStages = 2;    // weight stages (NVFP4 rows + block scales, from DRAM)
 constexpr int kXStages = 3;    // activation tiles per K-step (mostly L2 hits)
 constexpr int kAStages = 2;    // decoded f16 weight tiles
 constexpr int kTileM = 128;
 constexpr int kTileK = 64;
-constexpr int kMaxN = 256;     // tokens per chunk (MMA N)
+constexpr int kMaxN = 192;     // tokens per chunk (MMA N)
 constexpr int kWLanes = 32;    // warp 0: weight producer
 constexpr int kXLanes = 64;    // warps 1, 3: activation producers
 constexpr long long kSpinLimit = 1LL << 22;  // try_wait polls per wait before giving up
@@ -70,8 +71,8 @@ struct Layout {
   static constexpr int X_STAGE = kMaxN * 128;                    // swizzled B tile (1024-aligned)
   static constexpr int A_TILE = kTileM * 128;                    // one f16 A tile
   static constexpr int A_STAGE = NMAT * A_TILE;
-  static constexpr int W_W = NMAT * kTileM * 32;                 // NVFP4 bytes of a K-step
-  static constexpr int W_S = NMAT * kTileM * 4;                  // scale bytes of a K-step
+  static constexpr int W_W = NMAT * kTileM * 32 * kWSteps;       // NVFP4 bytes of a weight stage
+  static constexpr int W_S = NMAT * kTileM * 4 * kWSteps;        // scale bytes of a weight stage
   static constexpr int W_STAGE = W_W + W_S;
   static constexpr int OFF_A = kXStages * X_STAGE;
   static constexpr int OFF_W = OFF_A + kAStages * A_STAGE;
@@ -79,7 +80,8 @@ struct Layout {
   // two blocks x 256 columns: one accumulator buffer
   static constexpr int ACC_BUFS = 1;
   static constexpr int ACC_COLS = NMAT * kMaxN;
-  static constexpr int TMEM_COLS = ACC_BUFS * ACC_COLS;         // 512
+  static constexpr int TMEM_COLS = 512;                          // >= ACC_BUFS * ACC_COLS, a power of 2
+  static_assert(ACC_BUFS * ACC_COLS <= TMEM_COLS, "TMEM");
 };
 
 struct Chunk {
@@ -208,48 +210,56 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
   if (warp == 0) {
     // ------------------------------------------------ weight producer (32 lanes)
     const int pl = lane;
-    constexpr int WI = NMAT * kTileM * 2 / kWLanes;  // 16-byte weight pieces per lane
-    constexpr int SI = NMAT * kTileM / kWLanes;      // 4-byte scale pieces per lane
+    // a stage: per row 128 weight bytes (8 pieces of 16, eight lanes per row so
+    // one instruction covers four whole 128-byte lines) and 16 scale bytes
+    constexpr int WI = NMAT * kTileM * 8 / kWLanes;  // 16-byte weight pieces per lane
+    constexpr int SI = NMAT * kTileM / kWLanes;      // 16-byte scale pieces per lane
     int it = 0;
     bool live = true;
     for (int tile = blockIdx.x; tile < n_tiles && live; tile += gridDim.x) {
       const Chunk ch = a.chunks[tile / fb_count];
       const int row0 = (tile % fb_count) * L::ROWS;
       const ffn_b200_expert &E = a.experts[ch.expert];
-      const uint8_t *ws_[WI], *ss[SI];
       // block mi: phase 1 gate (mi 0) / up (mi 1) rows row0..; phase 2 down rows row0 + 128 mi..
       auto blk_w = [&](int mi) { return PH == 1 ? E.nv[mi].w : E.nv[2].w + (size_t)mi * kTileM * wld; };
       auto blk_s = [&](int mi) { return PH == 1 ? E.nv[mi].s : E.nv[2].s + (size_t)mi * kTileM * sld; };
-      uint32_t wd[WI], sd[SI];
-#pragma unroll
-      for (int j = 0; j < WI; ++j) {
-        const int q = pl + kWLanes * j;
-        const int mi = q / (kTileM * 2), r = (q >> 1) % kTileM, half = q & 1;
-        ws_[j] = blk_w(mi) + (size_t)(row0 + r) * wld + half * 16;
-        wd[j] = mi * kTileM * 32 + r * 32 + half * 16;
-      }
-#pragma unroll
-      for (int j = 0; j < SI; ++j) {
-        const int q = pl + kWLanes * j;
-        const int mi = q / kTileM, r = q % kTileM;
-        ss[j] = blk_s(mi) + (size_t)(row0 + r) * sld;
-        sd[j] = L::W_W + mi * kTileM * 4 + r * 4;
-      }
-      for (int kt = 0; kt < KT; ++kt, ++it) {
+      const int pc = pl & 7, r0 = pl >> 3;  // piece of a row, first row of this lane
+      const uint8_t *wsrc0 = blk_w(0) + (size_t)row0 * wld + pc * 16;
+      const uint8_t *wsrc1 = blk_w(1) + (size_t)row0 * wld + pc * 16;
+      const uint8_t *ssrc0 = blk_s(0) + (size_t)row0 * sld;
+      const uint8_t *ssrc1 = blk_s(1) + (size_t)row0 * sld;
+      const bool s16 = ((reinterpret_cast<uintptr_t>(ssrc0) | reinterpret_cast<uintptr_t>(ssrc1)) & 15) == 0;
+      for (int kw = 0; kw < KT / kWSteps; ++kw, ++it) {
         const int s = it % kWStages;
         if (!bar_wait(&w_empty[s], ((it / kWStages) & 1) ^ 1, a.err)) { live = false; break; }
         uint8_t *st = wbuf + s * L::W_STAGE;
+#pragma unroll 8
+        for (int j = 0; j < WI; ++j) {  // piece pl + 32 j: block j / 32, row r0 + 4 (j % 32)
+          const int mi = j / (WI / NMAT), r = r0 + (kWLanes / 8) * (j % (WI / NMAT));
+          cp_async16(st + (mi * kTileM + r) * 128 + pc * 16, (mi ? wsrc1 : wsrc0) + (size_t)r * wld + kw * 128);
+        }
 #pragma unroll
-        for (int j = 0; j < WI; ++j) cp_async16(st + wd[j], ws_[j] + kt * 32);
+        for (int j = 0; j < SI; ++j) {  // scale row pl + 32 j
+          const int mi = j / (SI / NMAT), r = pl + kWLanes * (j % (SI / NMAT));
+          uint8_t *dst = st + L::W_W + (mi * kTileM + r) * 16;
+          const uint8_t *src = (mi ? ssrc1 : ssrc0) + (size_t)r * sld + kw * 16;
+          if (s16) {
+            cp_async16(dst, src);
+          } else {  // scale arrays only 4-byte aligned
 #pragma unroll
-        for (int j = 0; j < SI; ++j) cp_async4(st + sd[j], ss[j] + kt * 4);
+            for (int q = 0; q < 4; ++q) cp_async4(dst + 4 * q, src + 4 * q);
+          }
+        }
         cp_async_bar_arrive(&w_full[s]);
       }
     }
   } else if (warp == 1 || warp == 3) {
     // ------------------------------------------------ activation producers (64 lanes)
-    constexpr int RI = kMaxN / kXLanes;  // rows per lane
+    // eight lanes per row (one 16-byte piece each): an instruction covers
+    // whole 128-byte rows of 4 tokens
+    constexpr int RI = kMaxN * 8 / kXLanes;  // rows per lane
     const int xl = warp == 1 ? lane : 32 + lane;
+    const int kc = xl & 7;
     int it = 0;
     bool live = true;
     for (int tile = blockIdx.x; tile < n_tiles && live; tile += gridDim.x) {
@@ -257,12 +267,12 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
       const __half *rp[RI];
 #pragma unroll
       for (int j = 0; j < RI; ++j) {
-        const int n = xl + kXLanes * j;
+        const int n = (xl >> 3) + (kXLanes / 8) * j;
         rp[j] = nullptr;
         if (n < ch.nn) {
           const int p = ch.p0 + n;
           const int xr = PH == 1 ? __ldg(a.pair_tok + p) : p;
-          rp[j] = a.x + (size_t)xr * a.ld_x;
+          rp[j] = a.x + (size_t)xr * a.ld_x + kc * 8;
         }
       }
       for (int kt = 0; kt < KT; ++kt, ++it) {
@@ -271,11 +281,7 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
         uint8_t *st = xbuf + s * L::X_STAGE;
 #pragma unroll
         for (int j = 0; j < RI; ++j)
-          if (rp[j]) {
-            const int n = xl + kXLanes * j;
-#pragma unroll
-            for (int kc = 0; kc < 8; ++kc) cp_async16(st + sw128(n, kc), rp[j] + kt * kTileK + kc * 8);
-          }
+          if (rp[j]) cp_async16(st + sw128((xl >> 3) + (kXLanes / 8) * j, kc), rp[j] + kt * kTileK);
         cp_async_bar_arrive(&x_full[s]);
       }
     }
@@ -332,20 +338,23 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
         // token scales of the tile's columns, read by every epilogue thread;
         // a buffer is rewritten two tiles later, after all decode warps have
         // finished this tile's epilogue (the next tile's MMAs wait for that)
-        s_xs[tcount & 1][d] = d < ch.nn ? pow2f(__ldg(a.xe + __ldg(a.pair_tok + ch.p0 + d))) : 0.f;
+        static_assert(kMaxN <= kDecWarps * 32, "one decode thread per chunk column");
+        if (d < kMaxN) s_xs[tcount & 1][d] = d < ch.nn ? pow2f(__ldg(a.xe + __ldg(a.pair_tok + ch.p0 + d))) : 0.f;
         asm volatile("bar.sync 1, %0;" ::"n"(kDecWarps * 32) : "memory");
       }
-      for (int kt = 0; kt < KT; ++kt, ++itw, ++ita) {
+      for (int kt = 0; kt < KT; ++kt, ++ita) {
+        const int sub = kt % kWSteps;  // K-step inside the weight stage
         const int s = itw % kWStages, s2 = ita % kAStages;
-        const bool ok = bar_wait(&w_full[s], (itw / kWStages) & 1, a.err) &&
+        const bool ok = (sub != 0 || bar_wait(&w_full[s], (itw / kWStages) & 1, a.err)) &&
                         bar_wait(&a_empty[s2], ((ita / kAStages) & 1) ^ 1, a.err);
         if (!__all_sync(0xffffffffu, ok)) { live = false; break; }
         const uint8_t *st = wbuf + s * L::W_STAGE;
         uint8_t *at = abuf + s2 * L::A_STAGE;
         {
-          const uint4 w0 = *reinterpret_cast<const uint4 *>(st + mi * kTileM * 32 + r * 32);
-          const uint4 w1 = *reinterpret_cast<const uint4 *>(st + mi * kTileM * 32 + r * 32 + 16);
-          const uint32_t sc4 = *reinterpret_cast<const uint32_t *>(st + L::W_W + mi * kTileM * 4 + r * 4);
+          const uint8_t *wr = st + (mi * kTileM + r) * 128 + sub * 32;
+          const uint4 w0 = *reinterpret_cast<const uint4 *>(wr);
+          const uint4 w1 = *reinterpret_cast<const uint4 *>(wr + 16);
+          const uint32_t sc4 = *reinterpret_cast<const uint32_t *>(st + L::W_W + (mi * kTileM + r) * 16 + sub * 4);
           const uint32_t s01 = e4m3x2_to_f16x2((uint16_t)(sc4 & 0xFFFFu));
           const uint32_t s23 = e4m3x2_to_f16x2((uint16_t)(sc4 >> 16));
           const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
@@ -364,7 +373,11 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
         }
         fence_async_smem();
         __syncwarp();
-        if (lane == 0) { bar_arrive(&a_full[s2]); bar_arrive(&w_empty[s]); }
+        if (lane == 0) {
+          bar_arrive(&a_full[s2]);
+          if (sub == kWSteps - 1) bar_arrive(&w_empty[s]);
+        }
+        if (sub == kWSteps - 1) ++itw;
       }
       if (!live) break;
       // epilogue: this thread's TMEM lane = tile row r

@@ -164,7 +164,7 @@ typedef struct ffn_b200_moe_desc {
     const float *norm_w;             /* DEVICE [hidden] or NULL */
     float norm_eps;
     /* FFN_B200_PATH_*: AUTO (0) takes the tensor-core grouped GEMM when the
-     * layer has only NVFP4 experts, hidden is a multiple of 256, inter of 128 and
+     * layer has only NVFP4 experts, hidden and inter are multiples of 256 and
      * the routed pairs average >= FFN_B200_GROUPED_MIN_PAIRS per expert
      * (prefill), else the GEMV slices (decode). */
     int32_t path;

@@ -20,7 +20,14 @@ larger than L2, so every layer-step reads its expert bytes from HBM, as the
 full stack does; config.resident_layers records the number.
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+                       [--workload config4|config3]
 (N > 1 under torchrun, one rank per GPU).
+
+--workload config3 measures BASELINE config 3 instead: one NVFP4 MoE layer
+over a prefill of 8192 tokens (bf16-valued N(0,1) hidden states, seed 3,
+sigmoid top-6 of 384, no ffn_norm), which the library runs on its tensor-core
+grouped GEMM; a step is one layer pass, the roofline is the gate/up GEMM's
+TFLOP/s against the measured dense bf16 peak.
 """
 from __future__ import annotations
 
@@ -52,13 +59,14 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--tokens", type=int, default=256)
-    ap.add_argument("--layers", type=int, default=40)
+    ap.add_argument("--workload", choices=["config4", "config3"], default="config4")
+    ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--experts", type=int, default=384)
     ap.add_argument("--hidden", type=int, default=4096)
     ap.add_argument("--inter", type=int, default=2048)
     ap.add_argument("--top-k", type=int, default=6)
-    ap.add_argument("--seed", type=int, default=4)
+    ap.add_argument("--seed", type=int, default=None)
     ap.add_argument("--max-resident", type=int, default=0,
                     help="cap on resident layers (0: as many as fit)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -67,7 +75,24 @@ def parse_args():
     return ap.parse_args()
 
 
+METRIC3 = "MoE expert-FFN prefill tokens/s (one NVFP4 top-6/384 layer, 8192 tokens)"
+
+
+def metric_of(a):
+    return METRIC3 if a.workload == "config3" else METRIC
+
+
 def base_config(a, world, resident):
+    if a.workload == "config3":
+        return {
+            "workload": "config3: one NVFP4 MoE layer, prefill of 8192 tokens, top-6 of 384, "
+                        "tensor-core grouped GEMM",
+            "hidden": a.hidden, "inter": a.inter, "experts": a.experts, "top_k": a.top_k,
+            "tokens": a.tokens, "seed": a.seed,
+            "router": "fp32 weights, tensor-core split-f16, sigmoid top-k; bf16-valued inputs",
+            "parallelism": f"ep{world}",
+            "l2": "no flush: each step streams the layer's 5.4 GB of expert weights (> 126 MB L2)",
+        }
     return {
         "workload": "config4: 40-layer NVFP4 MoE-FFN stack, 256-token decode, top-6 of 384, "
                     "expert-parallel",
@@ -96,13 +121,16 @@ class CpuSample:
         import oracle as O
 
         self.O, self.a, self.threads = O, a, threads
+        self.n_lay = min(self.N_LAY, a.layers)
         O.set_threads(threads)
         H, I, E, K = a.hidden, a.inter, a.experts, a.top_k
         self.x = O.gen_hidden(a.seed, self.N_TOK, H)
-        self.norm_w = np.ones(H, dtype=np.float32)
+        if a.workload == "config3":  # bf16 hidden states, no ffn_norm
+            self.x = (self.x.view(np.uint32) & 0xFFFF0000).view(np.float32)
+        self.norm_w = np.ones(H, dtype=np.float32) if a.workload == "config4" else None
         self.routers, self.experts = [], {}
-        xn = O.rms_norm(self.x, self.norm_w)
-        for layer in range(self.N_LAY):
+        xn = O.rms_norm(self.x, self.norm_w) if self.norm_w is not None else self.x
+        for layer in range(self.n_lay):
             wr = O.gen_router(a.seed, layer, E, H)
             idx, _, _, _ = O.route(O.router_logits(wr, xn), K, None, 1)
             self.routers.append(wr)
@@ -113,15 +141,17 @@ class CpuSample:
         """One pass over the sample; returns the token-layers computed."""
         import numpy as np
         O, a = self.O, self.a
-        for layer in range(self.N_LAY):
+        for layer in range(self.n_lay):
             wr = self.routers[layer]
             for t in range(self.N_TOK):
-                xt = O.rms_norm(np.ascontiguousarray(self.x[t])[None, :], self.norm_w)[0]
+                xt = np.ascontiguousarray(self.x[t])
+                if self.norm_w is not None:
+                    xt = O.rms_norm(xt[None, :], self.norm_w)[0]
                 idx, wt, _, _ = O.route(O.router_logits(wr, xt), a.top_k, None, 1)
                 out = np.zeros(a.hidden, dtype=np.float32)
                 for k in range(a.top_k):
                     O.axpy(out, wt[0, k], self.experts[(layer, int(idx[0, k]))].forward(xt))
-        return self.N_LAY * self.N_TOK
+        return self.n_lay * self.N_TOK
 
     def measure(self, seconds: float):
         """(tokens/s of the full stack, seconds, token-layers) over repeated passes."""
@@ -136,7 +166,7 @@ class CpuSample:
 
     def describe(self, dt, n):
         return (f"oracle C restatement of the reference CPU path, {self.threads} threads: "
-                f"{n} token-layers ({self.N_TOK} tokens x {self.N_LAY} layers, repeated) in "
+                f"{n} token-layers ({self.N_TOK} tokens x {self.n_lay} layers, repeated) in "
                 f"{dt:.1f} s, scaled to the {self.a.layers}-layer stack")
 
 
@@ -158,7 +188,7 @@ def run_reference(a):
     value = statistics.median(vals)
     desc = sample.describe(tot_dt, tot_n)
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "impl": "reference", "metric": metric_of(a), "value": value, "unit": UNIT,
         "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": a.tokens / value * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -430,6 +460,158 @@ def run_ours(a):
     return 0
 
 
+def run_prefill(a):
+    """Config 3: one MoE layer over 8192 prefill tokens on the grouped GEMM."""
+    import torch
+
+    import ffn_b200 as F
+    from ep import expert_range
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    H, I, E, K, T = a.hidden, a.inter, a.experts, a.top_k, a.tokens
+    e_lo, e_hi = expert_range(rank, world, E)
+    experts = [None] * E
+    for e in range(e_lo, e_hi):
+        experts[e] = F.SwigluExpert.generate(F.FMT_NVFP4, a.seed, 0, e, I, H)
+    wr = F.gen_normal(F.path_key(a.seed, 0, 0, F.TAG_ROUTER), E * H, 0.02).view(E, H)
+    layer = F.MoeLayer(experts, wr, H, I, top_k=K, score_fn=F.SCORE_SIGMOID,
+                       router_mode=F.ROUTER_TENSOR, expert_range=(e_lo, e_hi))
+    x0 = F.gen_normal(F.path_key(a.seed, 0, 0, F.TAG_X), T * H).view(T, H)
+    x0 = x0.to(torch.bfloat16).to(torch.float32)  # config 3: bf16 hidden states
+    out = torch.empty_like(x0)
+    idx = torch.empty(T, K, dtype=torch.int32, device=dev)
+    layer.forward(x0, out=out, topk_idx=idx)
+    torch.cuda.synchronize()
+    ids, cnt = torch.unique(idx, return_counts=True)
+    local_pairs = int(cnt[(ids >= e_lo) & (ids < e_hi)].sum().item())
+
+    def step():
+        layer.forward(x0, out=out)
+        if world > 1:
+            dist.all_reduce(out)
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(_bus_id(dev, local))
+    if rank == 0:
+        clocks.start()
+        time.sleep(0.3)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    F.profile_enable(True)
+    n0 = F.launch_count()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(a.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    launches = F.launch_count() - n0
+    F.profile_enable(False)
+    prof = F.profile_read()
+    clk = clocks.stop() if rank == 0 else None
+    tt = torch.tensor([t0.elapsed_time(t1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = float(tt.item())
+    ms_step = ms / a.steps
+    value = T * a.steps / (ms * 1e-3)
+
+    # end to end: host x in, host out back, every step
+    x_host = x0.cpu().pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    xd = torch.empty_like(x0)
+    F.profile_enable(True)
+    for i in range(a.warmup + a.steps):
+        if i == a.warmup:
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        xd.copy_(x_host, non_blocking=True)
+        layer.forward(xd, out=out)
+        if world > 1:
+            dist.all_reduce(out)
+        if rank == 0:
+            out_host.copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    F.profile_enable(False)
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e = T * a.steps / (float(te.item()) * 1e-3)
+
+    # roofline: gate/up grouped GEMM, algorithmic FLOPs of this rank's pairs
+    gu_ms, gu_n = prof.get("gemm_gateup", (0.0, 0))
+    gu_flop = 2.0 * local_pairs * 2 * H * I
+    peak, src = _tensor_peak()
+    achieved = gu_flop * gu_n / (gu_ms * 1e-3) / 1e12 if gu_ms else None
+    dn_ms, dn_n = prof.get("gemm_down", (0.0, 0))
+    dn_tf = 2.0 * local_pairs * H * I * dn_n / (dn_ms * 1e-3) / 1e12 if dn_ms else None
+    roof = {"bound": "tensor", "kernel": "grouped gemm_kernel<1> (gate+up, tcgen05 kind::f16)",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": achieved / peak if achieved else None, "traffic": None, "peak_source": src,
+            "algorithmic_flop_per_launch": gu_flop, "launches": gu_n,
+            "avg_launch_us": gu_ms * 1e3 / gu_n if gu_n else None,
+            "down_tflops": dn_tf,
+            "fp4_dense_nominal_tflops": 9000.0,
+            "note": "f16 operands (weights dequantised exactly in smem); FP4 block-scaled MMA "
+                    "would need FP4 activations, outside the 1e-3 tolerance"}
+    kernels = {k: {"ms": round(v[0], 3), "launches": v[1]} for k, v in prof.items()}
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        sample = CpuSample(a, threads)
+        cv, dt, n = sample.measure(a.cpu_seconds)
+        cpu = {"value": cv, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": sample.describe(dt, n)}
+    if rank == 0:
+        cfg = base_config(a, world, 1)
+        cfg["routed_pairs_rank0"] = local_pairs
+        line = {
+            "metric": METRIC3, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "nvfp4 weights dequantised to f16 x f16 activations, f32 accumulate",
+            "data": "synthetic (seeded random-init weights, bf16-valued N(0,1) hidden states)",
+            "config": cfg,
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": T * H * 4,
+                    "d2h_bytes_per_step": T * H * 4},
+            "gpu_launches": launches, "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
+            "kernels": kernels,
+            "tflops_layer": 2.0 * T * K * 3 * H * I / (ms_step * 1e-3) / 1e12,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def _tensor_peak():
+    try:
+        d = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return float(d["bf16_tflops"]), "measured dense bf16 burst (MEASURED_PEAKS.json bf16_tflops)"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback (1.59 PFLOP/s)"
+
+
 def _bus_id(dev, local):
     """nvidia-smi -i selector of this rank's GPU (its UUID when torch knows it)."""
     import torch
@@ -466,8 +648,18 @@ def _traffic_per_launch(alg_bytes_per_launch):
 
 def main():
     a = parse_args()
+    if a.workload == "config3":
+        for k, v in (("tokens", 8192), ("layers", 1), ("seed", 3)):
+            if getattr(a, k) is None:
+                setattr(a, k, v)
+    else:
+        for k, v in (("tokens", 256), ("layers", 40), ("seed", 4)):
+            if getattr(a, k) is None:
+                setattr(a, k, v)
     if a.impl == "reference":
         return run_reference(a)
+    if a.workload == "config3":
+        return run_prefill(a)
     return run_ours(a)
 
 

@@ -738,7 +738,9 @@ int launch_exact_matvec(const float *w32, const uint16_t *w16, const float *x, i
 // the range; shared-memory reduction.  Each K-range writes its own partial
 // logits (logits + z * n_tok * n_exp); top-k adds the partials in z order.
 constexpr int kRouterWarps = 8;  // router_tc_kernel runs 256 threads
-constexpr int kRouterKSplit = 4;  // K-ranges of the tensor router (partial logit planes)
+// K-ranges of the tensor router (partial logit planes): 12 x 8 x 3 = 288 CTAs of a
+// 256-token, 384-expert layer fit one wave at 2 CTAs per SM
+constexpr int kRouterKSplit = 3;
 __global__ void __launch_bounds__(256) router_tc_kernel(const float *__restrict__ w,
                                                         const __half *__restrict__ xh,
                                                         const __half *__restrict__ xl,
@@ -841,7 +843,7 @@ __device__ __forceinline__ float score_of(float l, int fn) {
   return 1.0f / (1.0f + expf(-l));
 }
 
-__global__ void __launch_bounds__(256) topk_kernel(const float *__restrict__ logits,
+__global__ void __launch_bounds__(64) topk_kernel(const float *__restrict__ logits,
                                                    const float *__restrict__ bias, int n_tok,
                                                    int n_exp, int top_k, int score_fn,
                                                    int n_part, int32_t *idx, float *wt) {
@@ -857,8 +859,9 @@ __global__ void __launch_bounds__(256) topk_kernel(const float *__restrict__ log
       if (z < n_part) l += lg[z * plane + e];
     return l;
   };
-  float sel_score[kTopKMax];
-  int sel_idx[kTopKMax];
+  // round k's winner is kept by lane k (top_k <= 16 < 32)
+  float my_score = 0.f;
+  int my_idx = 0;
   float prev_b = INFINITY;
   int prev_i = -1;
   // scores and biased scores of this lane's experts (lane + 32j), computed once
@@ -901,20 +904,18 @@ __global__ void __launch_bounds__(256) topk_kernel(const float *__restrict__ log
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
       if (ob > bb || (ob == bb && oi < bi)) { bb = ob; bs = os; bi = oi; }
     }
-    sel_score[k] = bs;
-    sel_idx[k] = bi;
+    if (lane == k) { my_score = bs; my_idx = bi; }
     prev_b = bb;
     prev_i = bi;
   }
-  if (lane == 0) {
-    float sum = 0.f;
-    for (int k = 0; k < top_k; ++k) sum += sel_score[k];  // selection order, flash1017.rs:7370
-    const float num = score_fn == FFN_B200_SCORE_REF_SQRTSOFTPLUS ? 1.5f : 1.0f;
-    const float scale = sum > 1e-12f ? num / sum : 0.0f;
-    for (int k = 0; k < top_k; ++k) {
-      idx[(size_t)warp * top_k + k] = sel_idx[k];
-      wt[(size_t)warp * top_k + k] = sel_score[k] * scale;
-    }
+  // sum of the selected scores in selection order (flash1017.rs:7370)
+  float sum = 0.f;
+  for (int k = 0; k < top_k; ++k) sum += __shfl_sync(0xffffffffu, my_score, k);
+  const float num = score_fn == FFN_B200_SCORE_REF_SQRTSOFTPLUS ? 1.5f : 1.0f;
+  const float scale = sum > 1e-12f ? num / sum : 0.0f;
+  if (lane < top_k) {
+    idx[(size_t)warp * top_k + lane] = my_idx;
+    wt[(size_t)warp * top_k + lane] = my_score * scale;
   }
 }
 
@@ -934,7 +935,7 @@ int launch_router(const float *w, const float *bias, const float *x, const __hal
                router_tc_kernel<<<g1, 256, 0, st>>>(w, xh, xl, xe, n_tok, n_exp, H, logits));
   }
   FFN_LAUNCH(FFN_B200_K_TOPK, st, "topk_kernel",
-             topk_kernel<<<(n_tok + 7) / 8, 256, 0, st>>>(logits, bias, n_tok, n_exp, top_k, score_fn,
+             topk_kernel<<<(n_tok + 1) / 2, 64, 0, st>>>(logits, bias, n_tok, n_exp, top_k, score_fn,
                                                           n_part, idx, wt));
   return 0;
 }
@@ -1052,7 +1053,7 @@ int launch_group(const int32_t *idx, int n_tok, int top_k, int n_exp, int e_begi
 // selection order starting from zero with separate multiply and add, as
 // flash1017_axpy_f32 does (flash1017.rs:4900-4905, 7546-7547).  Ternary
 // experts weigh by w * proj_scale (flash1017.rs:7561).
-__global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ y, int ld_y,
+__global__ void __launch_bounds__(1024) combine_kernel(const float *__restrict__ y, int ld_y,
                                                       const int32_t *__restrict__ idx,
                                                       const float *__restrict__ wt,
                                                       const int32_t *__restrict__ inv, int top_k,
@@ -1077,24 +1078,30 @@ __global__ void __launch_bounds__(256) combine_kernel(const float *__restrict__ 
   __syncthreads();
   if (H % 4 == 0 && ld_y % 4 == 0 && ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(out) |
                                        reinterpret_cast<uintptr_t>(residual)) & 15) == 0) {
-    // four columns per thread and step, every load of a step in flight at once
-#pragma unroll 4
+    // four columns per thread; the terms' loads issue 8 at a time
     for (int c = 4 * threadIdx.x; c < H; c += 4 * blockDim.x) {
-      float4 yv[kTopKMax];
-#pragma unroll
-      for (int k = 0; k < kTopKMax; ++k)
-        if (k < top_k && pk[k] >= 0) yv[k] = __ldg(reinterpret_cast<const float4 *>(y + (size_t)pk[k] * ld_y + c));
+      const float4 r = residual ? *reinterpret_cast<const float4 *>(residual + (size_t)t * H + c)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k0 = 0; k0 < top_k; k0 += 8) {
+        float4 yv[8];
 #pragma unroll
-      for (int k = 0; k < kTopKMax; ++k)
-        if (k < top_k && pk[k] >= 0) {
-          acc.x = __fadd_rn(acc.x, __fmul_rn(wk[k], yv[k].x));
-          acc.y = __fadd_rn(acc.y, __fmul_rn(wk[k], yv[k].y));
-          acc.z = __fadd_rn(acc.z, __fmul_rn(wk[k], yv[k].z));
-          acc.w = __fadd_rn(acc.w, __fmul_rn(wk[k], yv[k].w));
+        for (int u = 0; u < 8; ++u) {
+          const int k = k0 + u;
+          if (k < top_k && pk[k] >= 0) yv[u] = __ldg(reinterpret_cast<const float4 *>(y + (size_t)pk[k] * ld_y + c));
         }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int k = k0 + u;
+          if (k < top_k && pk[k] >= 0) {
+            acc.x = __fadd_rn(acc.x, __fmul_rn(wk[k], yv[u].x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(wk[k], yv[u].y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(wk[k], yv[u].z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(wk[k], yv[u].w));
+          }
+        }
+      }
       if (residual) {
-        const float4 r = *reinterpret_cast<const float4 *>(residual + (size_t)t * H + c);
         acc.x = __fadd_rn(r.x, acc.x);
         acc.y = __fadd_rn(r.y, acc.y);
         acc.z = __fadd_rn(r.z, acc.z);
@@ -1120,7 +1127,8 @@ int launch_combine(const float *y, int ld_y, const int32_t *idx, const float *wt
                    const float *residual, float *out, int H, cudaStream_t st, const int *err) {
   if (n_tok <= 0) return 0;
   FFN_LAUNCH(FFN_B200_K_COMBINE, st, "combine_kernel",
-             combine_kernel<<<n_tok, 256, 0, st>>>(y, ld_y, idx, wt, inv, top_k, experts, residual, out, H, err));
+             combine_kernel<<<n_tok, std::min(1024, std::max(32, H / 4)), 0, st>>>(
+                 y, ld_y, idx, wt, inv, top_k, experts, residual, out, H, err));
   return 0;
 }
 

@@ -72,6 +72,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="CPU-baseline sample length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="per-layer sum over ranks: NVLink peer exchange or NCCL all-reduce")
     return ap.parse_args()
 
 
@@ -330,7 +332,8 @@ def run_ours(a):
                                 topk_idx=topk[lay] if capturing[0] else None)
         return run
 
-    ep = EpStack([layer_fn(lay) for lay in range(L)], rank, world)
+    exchange = F.EpExchange(rank, world, T, H) if world > 1 and a.exchange == "p2p" else None
+    ep = EpStack([layer_fn(lay) for lay in range(L)], rank, world, exchange=exchange)
 
     def stack(x_in, capture=False):
         capturing[0] = capture
@@ -363,6 +366,9 @@ def run_ours(a):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    # live roofline: event pairs only around the expert GEMV kernels (fewer
+    # event records between the kernels of the timed region)
+    F.profile_kinds(["gateup_nvfp4", "down_nvfp4"])
     F.profile_enable(True)
     n0 = F.launch_count()
     t_start = torch.cuda.Event(enable_timing=True)
@@ -379,6 +385,13 @@ def run_ours(a):
     prof = F.profile_read()
     clk = clocks.stop() if rank == 0 else None
     ms = t_start.elapsed_time(t_end)
+    # per-kernel breakdown: one more (untimed) step with every kind timed
+    F.profile_kinds(None)
+    F.profile_enable(True)
+    step()
+    torch.cuda.synchronize()
+    F.profile_enable(False)
+    breakdown = F.profile_read()
     tt = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -386,10 +399,11 @@ def run_ours(a):
     ms_step = ms / a.steps
     value = T * a.steps / (ms * 1e-3)
 
-    # ---- end to end through the public API with host buffers (kernel timing
-    # events on, as in the timed region above, so the two numbers compare)
+    # ---- end to end through the public API with host buffers (the same event
+    # pairs as in the timed region above, so the two numbers compare)
     x_host = x0.cpu().pin_memory()
     out_host = torch.empty_like(x_host).pin_memory()
+    F.profile_kinds(["gateup_nvfp4", "down_nvfp4"])
     F.profile_enable(True)
     for i in range(a.warmup + a.steps):
         if i == a.warmup:
@@ -423,7 +437,8 @@ def run_ours(a):
             "peak_source": peaks[1],
             "algorithmic_bytes_per_launch": gateup_bytes_step / L,
             "launches": gu_n, "avg_launch_us": gu_ms * 1e3 / gu_n if gu_n else None}
-    kernels = {k: {"ms": round(v[0], 3), "launches": v[1]} for k, v in prof.items()}
+    kernels = {k: {"us_per_launch_one_step": round(v[0] * 1e3 / v[1], 2), "launches": v[1]}
+               for k, v in breakdown.items()}
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:

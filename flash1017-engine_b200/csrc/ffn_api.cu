@@ -30,6 +30,7 @@ namespace {
 struct Prof {
   std::mutex mu;
   bool on = false;
+  uint32_t mask = ~0u;          // kinds timed while on
   std::vector<cudaEvent_t> ev;  // 2 per record
   std::vector<int> kind;        // per record
   size_t used = 0;              // records in use
@@ -47,7 +48,7 @@ constexpr size_t kProfRecords = 16384;
 
 void prof_begin(int kind, cudaStream_t st) {
   Prof &p = prof();
-  if (!p.on) return;
+  if (!p.on || !((p.mask >> kind) & 1u)) return;
   std::lock_guard<std::mutex> lk(p.mu);
   if (p.used >= p.kind.size()) { ++p.dropped; p.open_kind = -1; return; }
   cudaEventRecord(p.ev[2 * p.used], st);
@@ -57,7 +58,7 @@ void prof_begin(int kind, cudaStream_t st) {
 
 void prof_end(int kind, cudaStream_t st) {
   Prof &p = prof();
-  if (!p.on) return;
+  if (!p.on || !((p.mask >> kind) & 1u)) return;
   std::lock_guard<std::mutex> lk(p.mu);
   if (p.open_kind != kind || p.used >= p.kind.size()) return;
   cudaEventRecord(p.ev[2 * p.used + 1], st);
@@ -238,6 +239,13 @@ int ffn_b200_profile_enable(int enable) {
     p.dropped = 0;
   }
   p.on = enable != 0;
+  return 0;
+}
+
+int ffn_b200_profile_kinds(uint32_t mask) {
+  Prof &p = prof();
+  std::lock_guard<std::mutex> lk(p.mu);
+  p.mask = mask;
   return 0;
 }
 

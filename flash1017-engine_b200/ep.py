@@ -40,12 +40,17 @@ LayerFn = Callable[[object, object, Optional[object]], None]
 
 class EpStack:
     """A stack of MoE layers run expert-parallel: per layer, this rank's partial
-    output (residual on rank 0 only), then a sum all-reduce.  Every rank issues
-    the same collectives in the same order."""
+    output, then the sum over ranks.  The sum is either a torch.distributed
+    all-reduce (residual added by rank 0) or, given `exchange` (an
+    ffn_b200.EpExchange), the library's NVLink peer exchange, which reads every
+    rank's partial from the exchange's shared `part` buffer and adds the
+    residual itself.  Every rank issues the same collectives in the same order."""
 
-    def __init__(self, layers: Sequence[LayerFn], rank: int, world: int, group=None):
+    def __init__(self, layers: Sequence[LayerFn], rank: int, world: int, group=None,
+                 exchange=None):
         self.layers = list(layers)
         self.rank, self.world, self.group = rank, world, group
+        self.exchange = exchange if world > 1 else None
 
     def forward(self, x, buf_a, buf_b, on_layer: Optional[Callable[[int], None]] = None):
         """Runs every layer on x (not modified); buf_a / buf_b are ping-pong
@@ -53,8 +58,12 @@ class EpStack:
         cur = x
         for i, layer in enumerate(self.layers):
             nxt = buf_a if cur is not buf_a else buf_b
-            layer(cur, nxt, cur if self.rank == 0 else None)
-            if self.world > 1:
+            if self.exchange is not None:
+                layer(cur, self.exchange.part, None)
+                self.exchange.allreduce(cur.shape[0], cur, nxt)
+            else:
+                layer(cur, nxt, cur if self.rank == 0 else None)
+            if self.world > 1 and self.exchange is None:
                 import torch.distributed as dist
 
                 dist.all_reduce(nxt, group=self.group)

@@ -35,7 +35,9 @@ EXPORTS = [
     "ffn_b200_key", "ffn_b200_gen_nvfp4", "ffn_b200_gen_ternary", "ffn_b200_gen_core",
     "ffn_b200_gen_normal", "ffn_b200_dequant_nvfp4", "ffn_b200_dequant_ternary",
     "ffn_b200_set_batch_input", "ffn_b200_release_host_ranges", "ffn_b200_host_cache_bytes",
-    "ffn_b200_profile_enable", "ffn_b200_profile_read",
+    "ffn_b200_profile_enable", "ffn_b200_profile_kinds", "ffn_b200_profile_read",
+    "ffn_b200_ep_handle_bytes", "ffn_b200_ep_create", "ffn_b200_ep_connect", "ffn_b200_ep_part",
+    "ffn_b200_ep_allreduce", "ffn_b200_ep_error", "ffn_b200_ep_destroy",
 ]
 
 # Kernel kinds of ffn_b200_profile_read (FFN_B200_K_*).
@@ -124,6 +126,15 @@ def lib() -> C.CDLL:
         L.ffn_b200_host_cache_bytes.restype = sz
         L.merkaba_hardware_addon_v1.restype = vp
         L.ffn_b200_profile_enable.argtypes = [i32]
+        L.ffn_b200_profile_kinds.argtypes = [C.c_uint32]
+        L.ffn_b200_ep_handle_bytes.restype = sz
+        L.ffn_b200_ep_create.argtypes = [i32, i32, sz, sz, vp, C.POINTER(vp)]
+        L.ffn_b200_ep_connect.argtypes = [vp, vp]
+        L.ffn_b200_ep_part.argtypes = [vp]
+        L.ffn_b200_ep_part.restype = vp
+        L.ffn_b200_ep_allreduce.argtypes = [vp, sz, vp, vp, vp]
+        L.ffn_b200_ep_error.argtypes = [vp, C.POINTER(C.c_int)]
+        L.ffn_b200_ep_destroy.argtypes = [vp]
         L.ffn_b200_profile_read.argtypes = [i32, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]
         _lib = L
     return _lib
@@ -142,6 +153,12 @@ def launch_count() -> int:
 def profile_enable(on: bool) -> None:
     """Start (True: clears the totals) or stop per-kernel event timing."""
     check(lib().ffn_b200_profile_enable(int(on)), "profile_enable")
+
+
+def profile_kinds(names=None) -> None:
+    """Time only these kernel kinds (names from K_NAMES; None: all)."""
+    mask = 0xFFFFFFFF if names is None else sum(1 << K_NAMES.index(n) for n in names)
+    check(lib().ffn_b200_profile_kinds(C.c_uint32(mask)), "profile_kinds")
 
 
 def profile_read() -> dict:
@@ -181,6 +198,52 @@ def _stream(stream=None):
     torch = _torch()
     s = stream if stream is not None else torch.cuda.current_stream()
     return C.c_void_p(s.cuda_stream)
+
+
+class EpExchange:
+    """NVLink peer exchange of the expert-parallel partial outputs (one
+    process per GPU, torch.distributed initialised).  Every rank's MoE layer
+    writes its partial into `part` (residual None); allreduce() then forms
+    residual + sum of the parts on every rank."""
+
+    def __init__(self, rank: int, world: int, max_tokens: int, hidden: int, group=None):
+        import torch.distributed as dist
+        torch = _torch()
+        n = int(lib().ffn_b200_ep_handle_bytes())
+        h = (C.c_uint8 * n)()
+        ep = C.c_void_p()
+        check(lib().ffn_b200_ep_create(rank, world, max_tokens, hidden, C.cast(h, C.c_void_p),
+                                       C.byref(ep)), "ep_create")
+        self.ep = ep
+        mine = torch.tensor(list(bytes(h)), dtype=torch.uint8, device="cuda")
+        allh = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allh, mine, group=group)
+        blob = b"".join(bytes(t.cpu().tolist()) for t in allh)
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        check(lib().ffn_b200_ep_connect(ep, C.cast(buf, C.c_void_p)), "ep_connect")
+        ptr = int(lib().ffn_b200_ep_part(ep))
+
+        class _View:  # zero-copy torch view of the shared part buffer
+            __cuda_array_interface__ = {"shape": (max_tokens, hidden), "typestr": "<f4",
+                                        "data": (ptr, False), "version": 2}
+
+        self.part = torch.as_tensor(_View(), device=torch.device("cuda", torch.cuda.current_device()))
+        self.hidden = hidden
+
+    def allreduce(self, n_tok: int, residual, out, stream=None):
+        check(lib().ffn_b200_ep_allreduce(self.ep, n_tok, _ptr(residual), _ptr(out),
+                                          _stream(stream)), "ep_allreduce")
+        return out
+
+    def error(self) -> int:
+        flag = C.c_int(0)
+        check(lib().ffn_b200_ep_error(self.ep, C.byref(flag)), "ep_error")
+        return int(flag.value)
+
+    def close(self):
+        if self.ep:
+            lib().ffn_b200_ep_destroy(self.ep)
+            self.ep = None
 
 
 class Workspace:

@@ -229,7 +229,33 @@ FFN_B200_EXPORT int ffn_b200_dequant_ternary(size_t rows, size_t cols, const uin
 #define FFN_B200_K_GEMM_DOWN 13
 #define FFN_B200_K_COUNT 14
 FFN_B200_EXPORT int ffn_b200_profile_enable(int enable);
+/* Which kinds get event pairs while enabled: bit k = FFN_B200_K_* k (default
+ * all).  Timing fewer kinds puts fewer event records between the kernels. */
+FFN_B200_EXPORT int ffn_b200_profile_kinds(uint32_t mask);
 FFN_B200_EXPORT int ffn_b200_profile_read(int kind, double *total_ms, uint64_t *launches);
+
+/* ----------------------------------------- expert-parallel exchange (NVLink)
+ * No reference counterpart (the reference runs on one GB10).  One process per
+ * GPU; rank r's MoE layer (expert range r) writes its partial output into
+ * ffn_b200_ep_part(ep) with residual = NULL, then ffn_b200_ep_allreduce writes
+ * out = residual + sum over ranks of the parts on every rank: a two-shot
+ * exchange over peer memory in one cooperative kernel (bounded waits; on a
+ * timed-out wait it writes NaN over out and sets the flag ffn_b200_ep_error
+ * reads).  Set-up: every rank calls ffn_b200_ep_create (allocates its shared
+ * buffers and writes its IPC handle, ffn_b200_ep_handle_bytes() bytes), the
+ * handles are exchanged out of band (e.g. torch.distributed all_gather), then
+ * ffn_b200_ep_connect(ep, handles of all ranks in rank order).  Every rank must
+ * call ffn_b200_ep_allreduce the same number of times. */
+typedef struct ffn_b200_ep ffn_b200_ep;
+FFN_B200_EXPORT size_t ffn_b200_ep_handle_bytes(void);
+FFN_B200_EXPORT int ffn_b200_ep_create(int rank, int world, size_t max_tokens, size_t hidden,
+                                       void *my_handle, ffn_b200_ep **out);
+FFN_B200_EXPORT int ffn_b200_ep_connect(ffn_b200_ep *ep, const void *all_handles);
+FFN_B200_EXPORT float *ffn_b200_ep_part(ffn_b200_ep *ep);
+FFN_B200_EXPORT int ffn_b200_ep_allreduce(ffn_b200_ep *ep, size_t n_tok, const float *residual,
+                                          float *out, void *stream);
+FFN_B200_EXPORT int ffn_b200_ep_error(ffn_b200_ep *ep, int *flag);
+FFN_B200_EXPORT int ffn_b200_ep_destroy(ffn_b200_ep *ep);
 
 /* -------------------------------------------- reference-ABI support hooks
  * Host-side x_all buffer for gx10_rust_*_mlp_batch (the reference stages it

@@ -332,7 +332,17 @@ def run_ours(a):
                                 topk_idx=topk[lay] if capturing[0] else None)
         return run
 
-    exchange = F.EpExchange(rank, world, T, H) if world > 1 and a.exchange == "p2p" else None
+    exchange = None
+    if world > 1 and a.exchange == "p2p":
+        try:
+            exchange = F.EpExchange(rank, world, T, H)
+        except Exception as e:  # no peer access: NCCL all-reduce instead
+            print(f"rank {rank}: NVLink peer exchange unavailable ({e}); using NCCL", file=sys.stderr)
+        ok = torch.tensor([1 if exchange is not None else 0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if not int(ok.item()) and exchange is not None:
+            exchange.close()
+            exchange = None
     ep = EpStack([layer_fn(lay) for lay in range(L)], rank, world, exchange=exchange)
 
     def stack(x_in, capture=False):
@@ -357,6 +367,16 @@ def run_ours(a):
     for _ in range(a.warmup):
         step()
     torch.cuda.synchronize()
+    if exchange is not None:  # a timed-out exchange wait: fall back to NCCL
+        bad = torch.tensor([exchange.error()], device=dev)
+        dist.all_reduce(bad, op=dist.ReduceOp.MAX)
+        if int(bad.item()):
+            print("peer exchange reported a timed-out wait; using NCCL", file=sys.stderr)
+            ep.exchange = None
+            for _ in range(a.warmup):
+                step()
+            torch.cuda.synchronize()
+    exch_used = "nvlink-p2p" if ep.exchange is not None else ("nccl" if world > 1 else "none")
     if world > 1:
         dist.barrier()
     clocks = ClockSampler(_bus_id(dev, local))
@@ -450,6 +470,7 @@ def run_ours(a):
 
     if rank == 0:
         cfg = base_config(a, world, resident)
+        cfg["exchange"] = exch_used
         cfg["experts_hit_per_layer_rank0"] = u_loc
         cfg["weight_bytes_per_step_rank0"] = weight_bytes_step
         line = {
@@ -516,6 +537,16 @@ def run_prefill(a):
     for _ in range(a.warmup):
         step()
     torch.cuda.synchronize()
+    if exchange is not None:  # a timed-out exchange wait: fall back to NCCL
+        bad = torch.tensor([exchange.error()], device=dev)
+        dist.all_reduce(bad, op=dist.ReduceOp.MAX)
+        if int(bad.item()):
+            print("peer exchange reported a timed-out wait; using NCCL", file=sys.stderr)
+            ep.exchange = None
+            for _ in range(a.warmup):
+                step()
+            torch.cuda.synchronize()
+    exch_used = "nvlink-p2p" if ep.exchange is not None else ("nccl" if world > 1 else "none")
     if world > 1:
         dist.barrier()
     clocks = ClockSampler(_bus_id(dev, local))

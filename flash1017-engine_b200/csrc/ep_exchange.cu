@@ -88,23 +88,29 @@ __device__ bool ep_barrier(const EpArgs &a, int phase) {
   return s_ok != 0;
 }
 
+// W = world size (compile time: every peer's load of a step issues at once).
+template <int W>
 __global__ void __launch_bounds__(256) ep_exchange_kernel(const EpArgs a) {
   cg::grid_group grid = cg::this_grid();
   const int H4 = a.hidden / 4;
-  const int rows_per = (a.n_tok + a.world - 1) / a.world;
+  const int rows_per = (a.n_tok + W - 1) / W;
   const int r0 = min(a.n_tok, a.rank * rows_per), r1 = min(a.n_tok, r0 + rows_per);
+  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long nthr = (long long)gridDim.x * blockDim.x;
   bool ok = ep_barrier(a, 0);
   if (ok) {
     // step 2: own slice, summed over the ranks in rank order
     const long long n4 = (long long)(r1 - r0) * H4;
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
-         i += (long long)gridDim.x * blockDim.x) {
+    for (long long i = tid; i < n4; i += nthr) {
       const size_t off = (size_t)r0 * a.hidden + (size_t)i * 4;
+      float4 v[W];
+#pragma unroll
+      for (int src = 0; src < W; ++src) v[src] = __ldcg(reinterpret_cast<const float4 *>(a.part[src] + off));
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int src = 0; src < a.world; ++src) {
-        const float4 v = __ldcg(reinterpret_cast<const float4 *>(a.part[src] + off));
-        acc.x = __fadd_rn(acc.x, v.x); acc.y = __fadd_rn(acc.y, v.y);
-        acc.z = __fadd_rn(acc.z, v.z); acc.w = __fadd_rn(acc.w, v.w);
+#pragma unroll
+      for (int src = 0; src < W; ++src) {
+        acc.x = __fadd_rn(acc.x, v[src].x); acc.y = __fadd_rn(acc.y, v[src].y);
+        acc.z = __fadd_rn(acc.z, v[src].z); acc.w = __fadd_rn(acc.w, v[src].w);
       }
       if (a.residual) {
         const float4 r = *reinterpret_cast<const float4 *>(a.residual + off);
@@ -118,20 +124,41 @@ __global__ void __launch_bounds__(256) ep_exchange_kernel(const EpArgs a) {
   grid.sync();
   ok = ok && !*(volatile int *)a.err && ep_barrier(a, 1);
   if (ok) {
-    // step 4: every slice from its owner
+    // step 4: every slice from its owner, four 16-byte loads in flight per thread
     const long long n4 = (long long)a.n_tok * H4;
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
-         i += (long long)gridDim.x * blockDim.x) {
-      const int row = (int)(i / H4);
-      const int owner = min(a.world - 1, row / rows_per);
-      const size_t off = (size_t)i * 4;
-      *reinterpret_cast<float4 *>(a.out + off) = __ldcg(reinterpret_cast<const float4 *>(a.red[owner] + off));
+    for (long long i0 = tid; i0 < n4; i0 += 4 * nthr) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const long long i = i0 + u * nthr;
+        if (i < n4) {
+          const int owner = min(W - 1, (int)(i / H4) / rows_per);
+          v[u] = __ldcg(reinterpret_cast<const float4 *>(a.red[owner] + (size_t)i * 4));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const long long i = i0 + u * nthr;
+        if (i < n4) *reinterpret_cast<float4 *>(a.out + (size_t)i * 4) = v[u];
+      }
     }
   } else {
     const long long n = (long long)a.n_tok * a.hidden;
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-         i += (long long)gridDim.x * blockDim.x)
-      a.out[i] = __int_as_float(0x7FC00000);
+    for (long long i = tid; i < n; i += nthr) a.out[i] = __int_as_float(0x7FC00000);
+  }
+}
+
+using ExchangeFn = void (*)(const EpArgs);
+ExchangeFn exchange_kernel(int world) {
+  switch (world) {
+    case 1: return ep_exchange_kernel<1>;
+    case 2: return ep_exchange_kernel<2>;
+    case 3: return ep_exchange_kernel<3>;
+    case 4: return ep_exchange_kernel<4>;
+    case 5: return ep_exchange_kernel<5>;
+    case 6: return ep_exchange_kernel<6>;
+    case 7: return ep_exchange_kernel<7>;
+    default: return ep_exchange_kernel<8>;
   }
 }
 
@@ -181,7 +208,7 @@ int ffn_b200_ep_create(int rank, int world, size_t max_tokens, size_t hidden, vo
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ep->device);
   int per_sm = 0;
   if (e == cudaSuccess)
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ep_exchange_kernel, 256, 0);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, exchange_kernel(world), 256, 0);
   if (e != cudaSuccess) {
     if (ep->base) cudaFree(ep->base);
     delete ep;
@@ -240,7 +267,7 @@ int ffn_b200_ep_allreduce(ffn_b200_ep *ep, size_t n_tok, const float *residual, 
   void *args[] = {&a};
   cudaStream_t st = (cudaStream_t)stream;
   prof_begin(FFN_B200_K_OTHER, st);
-  cudaError_t e = cudaLaunchCooperativeKernel((const void *)ep_exchange_kernel, dim3(ep->grid),
+  cudaError_t e = cudaLaunchCooperativeKernel((const void *)exchange_kernel(ep->world), dim3(ep->grid),
                                               dim3(256), args, 0, st);
   prof_end(FFN_B200_K_OTHER, st);
   note_launch();

@@ -876,6 +876,45 @@ __global__ void __launch_bounds__(64) topk_kernel(const float *__restrict__ logi
       cb[j] = e < n_exp ? cs[j] + (bias ? bias[e] : 0.0f) : -INFINITY;
     }
   }
+  constexpr int kLocal = 8;  // lane-local candidate list (top_k <= 8 path)
+  if (cached && top_k <= kLocal) {
+    // Each lane keeps its best top_k of its 12 experts sorted in registers;
+    // then every round takes the best list head over the warp and the
+    // winning lane drops its head.  Order: biased score desc, index asc.
+    float lb[kLocal], ls[kLocal];
+    int li[kLocal];
+#pragma unroll
+    for (int q = 0; q < kLocal; ++q) { lb[q] = -INFINITY; ls[q] = 0.f; li[q] = 0x7fffffff; }
+#pragma unroll
+    for (int j = 0; j < kCache; ++j) {
+      float cb_ = cb[j], cs_ = cs[j];
+      int ci = lane + 32 * j;
+      if (ci >= n_exp) continue;
+#pragma unroll
+      for (int q = 0; q < kLocal; ++q) {  // insertion: carry the loser down the list
+        const bool better = cb_ > lb[q] || (cb_ == lb[q] && ci < li[q]);
+        const float tb = lb[q], ts = ls[q];
+        const int ti = li[q];
+        if (better) { lb[q] = cb_; ls[q] = cs_; li[q] = ci; cb_ = tb; cs_ = ts; ci = ti; }
+      }
+    }
+    for (int k = 0; k < top_k; ++k) {
+      // warp maximum of the heads by an order-preserving integer key of the
+      // biased score, then the lowest expert index among the heads that tie
+      const uint32_t u = __float_as_uint(lb[0]);
+      const uint32_t key = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+      const uint32_t kmax = __reduce_max_sync(0xffffffffu, key);
+      const int bi = (int)__reduce_min_sync(0xffffffffu, key == kmax ? (uint32_t)li[0] : 0xffffffffu);
+      const float bs = __shfl_sync(0xffffffffu, ls[0], bi & 31);  // expert e lives on lane e % 32
+      if (lane == k) { my_score = bs; my_idx = bi; }
+      if (li[0] == bi) {  // this lane's head won: pop it
+#pragma unroll
+        for (int q = 0; q + 1 < kLocal; ++q) { lb[q] = lb[q + 1]; ls[q] = ls[q + 1]; li[q] = li[q + 1]; }
+        lb[kLocal - 1] = -INFINITY;
+        li[kLocal - 1] = 0x7fffffff;
+      }
+    }
+  } else {
   for (int k = 0; k < top_k; ++k) {
     // best candidate strictly after (prev_b, prev_i) in (biased desc, index asc) order
     float bb = -INFINITY, bs = 0.f;
@@ -907,6 +946,7 @@ __global__ void __launch_bounds__(64) topk_kernel(const float *__restrict__ logi
     if (lane == k) { my_score = bs; my_idx = bi; }
     prev_b = bb;
     prev_i = bi;
+  }
   }
   // sum of the selected scores in selection order (flash1017.rs:7370)
   float sum = 0.f;

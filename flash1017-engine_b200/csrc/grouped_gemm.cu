@@ -28,7 +28,7 @@
 //
 // Warp roles (384 threads):
 //   warp 0         weight producer: cp.async of the tile's NVFP4 rows + block
-//                  scales, 4 K-steps (128 bytes of each row) per stage, 2 stages.
+//                  scales, 2 K-steps (64 bytes of each row) per stage, 4 stages.
 //   warps 1, 3     activation producers: cp.async of the chunk's rows straight
 //                  into their swizzled B tile, 3-deep ring (L2 hits mostly).
 //                  Producer completion is an mbarrier arrive per lane (noinc).
@@ -51,10 +51,10 @@ namespace gg {
 
 constexpr int kThreadsGG = 384;
 constexpr int kDecWarps = 8;   // warps 4-11: decode + epilogue
-constexpr int kWSteps = 4;     // K-steps per weight stage: 128 contiguous bytes of each row
-constexpr int kWStages = 2;    // weight stages (NVFP4 rows + block scales, from DRAM)
-constexpr int kXStages = 3;    // activation tiles per K-step (mostly L2 hits)
-constexpr int kAStages = 2;    // decoded f16 weight tiles
+constexpr int kWSteps = 2;     // K-steps per weight stage: 64 contiguous bytes of each row
+constexpr int kWStages = 4;    // weight stages (NVFP4 rows + block scales, from DRAM): 3 in flight
+constexpr int kXStages = 2;    // activation tiles per K-step (mostly L2 hits)
+constexpr int kAStages = 3;    // decoded f16 weight tiles
 constexpr int kTileM = 128;
 constexpr int kTileK = 64;
 constexpr int kMaxN = 192;     // tokens per chunk (MMA N)
@@ -73,6 +73,9 @@ struct Layout {
   static constexpr int A_STAGE = NMAT * A_TILE;
   static constexpr int W_W = NMAT * kTileM * 32 * kWSteps;       // NVFP4 bytes of a weight stage
   static constexpr int W_S = NMAT * kTileM * 4 * kWSteps;        // scale bytes of a weight stage
+  static constexpr int RB = 32 * kWSteps;                        // weight bytes of a row per stage
+  static constexpr int SB = 4 * kWSteps;                         // scale bytes of a row per stage
+  static constexpr int PPR = RB / 16;                            // 16-byte pieces per row
   static constexpr int W_STAGE = W_W + W_S;
   static constexpr int OFF_A = kXStages * X_STAGE;
   static constexpr int OFF_W = OFF_A + kAStages * A_STAGE;
@@ -210,10 +213,10 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
   if (warp == 0) {
     // ------------------------------------------------ weight producer (32 lanes)
     const int pl = lane;
-    // a stage: per row 128 weight bytes (8 pieces of 16, eight lanes per row so
-    // one instruction covers four whole 128-byte lines) and 16 scale bytes
-    constexpr int WI = NMAT * kTileM * 8 / kWLanes;  // 16-byte weight pieces per lane
-    constexpr int SI = NMAT * kTileM / kWLanes;      // 16-byte scale pieces per lane
+    // a stage: per row RB weight bytes (PPR pieces of 16, PPR adjacent lanes
+    // per row so one instruction covers whole row segments) and SB scale bytes
+    constexpr int WI = NMAT * kTileM * L::PPR / kWLanes;  // 16-byte weight pieces per lane
+    constexpr int SI = NMAT * kTileM / kWLanes;           // scale rows per lane
     int it = 0;
     bool live = true;
     for (int tile = blockIdx.x; tile < n_tiles && live; tile += gridDim.x) {
@@ -223,31 +226,32 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
       // block mi: phase 1 gate (mi 0) / up (mi 1) rows row0..; phase 2 down rows row0 + 128 mi..
       auto blk_w = [&](int mi) { return PH == 1 ? E.nv[mi].w : E.nv[2].w + (size_t)mi * kTileM * wld; };
       auto blk_s = [&](int mi) { return PH == 1 ? E.nv[mi].s : E.nv[2].s + (size_t)mi * kTileM * sld; };
-      const int pc = pl & 7, r0 = pl >> 3;  // piece of a row, first row of this lane
+      const int pc = pl % L::PPR, r0 = pl / L::PPR;  // piece of a row, first row of this lane
       const uint8_t *wsrc0 = blk_w(0) + (size_t)row0 * wld + pc * 16;
       const uint8_t *wsrc1 = blk_w(1) + (size_t)row0 * wld + pc * 16;
       const uint8_t *ssrc0 = blk_s(0) + (size_t)row0 * sld;
       const uint8_t *ssrc1 = blk_s(1) + (size_t)row0 * sld;
-      const bool s16 = ((reinterpret_cast<uintptr_t>(ssrc0) | reinterpret_cast<uintptr_t>(ssrc1)) & 15) == 0;
+      const bool s16 = ((reinterpret_cast<uintptr_t>(ssrc0) | reinterpret_cast<uintptr_t>(ssrc1)) & (L::SB - 1)) == 0;
       for (int kw = 0; kw < KT / kWSteps; ++kw, ++it) {
         const int s = it % kWStages;
         if (!bar_wait(&w_empty[s], ((it / kWStages) & 1) ^ 1, a.err)) { live = false; break; }
         uint8_t *st = wbuf + s * L::W_STAGE;
 #pragma unroll 8
-        for (int j = 0; j < WI; ++j) {  // piece pl + 32 j: block j / 32, row r0 + 4 (j % 32)
-          const int mi = j / (WI / NMAT), r = r0 + (kWLanes / 8) * (j % (WI / NMAT));
-          cp_async16(st + (mi * kTileM + r) * 128 + pc * 16, (mi ? wsrc1 : wsrc0) + (size_t)r * wld + kw * 128);
+        for (int j = 0; j < WI; ++j) {  // piece pl + 32 j: block j / (WI/2), row r0 + (32/PPR) (j % (WI/2))
+          const int mi = j / (WI / NMAT), r = r0 + (kWLanes / L::PPR) * (j % (WI / NMAT));
+          cp_async16(st + (mi * kTileM + r) * L::RB + pc * 16,
+                     (mi ? wsrc1 : wsrc0) + (size_t)r * wld + kw * L::RB);
         }
 #pragma unroll
         for (int j = 0; j < SI; ++j) {  // scale row pl + 32 j
           const int mi = j / (SI / NMAT), r = pl + kWLanes * (j % (SI / NMAT));
-          uint8_t *dst = st + L::W_W + (mi * kTileM + r) * 16;
-          const uint8_t *src = (mi ? ssrc1 : ssrc0) + (size_t)r * sld + kw * 16;
+          uint8_t *dst = st + L::W_W + (mi * kTileM + r) * L::SB;
+          const uint8_t *src = (mi ? ssrc1 : ssrc0) + (size_t)r * sld + kw * L::SB;
           if (s16) {
-            cp_async16(dst, src);
+            cp_async_n<L::SB>(dst, src);
           } else {  // scale arrays only 4-byte aligned
 #pragma unroll
-            for (int q = 0; q < 4; ++q) cp_async4(dst + 4 * q, src + 4 * q);
+            for (int q = 0; q < L::SB / 4; ++q) cp_async4(dst + 4 * q, src + 4 * q);
           }
         }
         cp_async_bar_arrive(&w_full[s]);
@@ -351,10 +355,10 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
         const uint8_t *st = wbuf + s * L::W_STAGE;
         uint8_t *at = abuf + s2 * L::A_STAGE;
         {
-          const uint8_t *wr = st + (mi * kTileM + r) * 128 + sub * 32;
+          const uint8_t *wr = st + (mi * kTileM + r) * L::RB + sub * 32;
           const uint4 w0 = *reinterpret_cast<const uint4 *>(wr);
           const uint4 w1 = *reinterpret_cast<const uint4 *>(wr + 16);
-          const uint32_t sc4 = *reinterpret_cast<const uint32_t *>(st + L::W_W + (mi * kTileM + r) * 16 + sub * 4);
+          const uint32_t sc4 = *reinterpret_cast<const uint32_t *>(st + L::W_W + (mi * kTileM + r) * L::SB + sub * 4);
           const uint32_t s01 = e4m3x2_to_f16x2((uint16_t)(sc4 & 0xFFFFu));
           const uint32_t s23 = e4m3x2_to_f16x2((uint16_t)(sc4 >> 16));
           const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};

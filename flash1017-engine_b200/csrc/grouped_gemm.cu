@@ -27,14 +27,15 @@
 // 2^-12 (measured ~2e-4), inside the path's 1e-3 tolerance.
 //
 // Warp roles (384 threads):
-//   warp 0         weight producer: cp.async of the tile's NVFP4 rows + block
-//                  scales, 2 K-steps (64 bytes of each row) per stage, 4 stages.
-//   warps 1, 3     activation producers: cp.async of the chunk's rows straight
+//   warps 0, 1, 3  activation producers: cp.async of the chunk's rows straight
 //                  into their swizzled B tile, 3-deep ring (L2 hits mostly).
 //                  Producer completion is an mbarrier arrive per lane (noinc).
 //   warp 2         TMEM allocation; lane 0 issues the MMAs and commits them to
 //                  the ring / accumulator barriers.
-//   warps 4-11     decode a weight stage into the f16 A tile(s) (thread = row of
+//   warps 4-11     stream their own 32 weight rows (NVFP4 + block scales) through
+//                  a private 4-stage cp.async ring (2 K-steps per stage), as the
+//                  decode GEMV engine does, and decode them into the f16 A tiles
+//                  (thread = row of
 //                  one matrix, or half a row's columns in phase 2), and after
 //                  a tile's last K-step run the epilogue from TMEM (warp w
 //                  reads TMEM lanes 32 (w % 4) ..., warps 4-7 the first half
@@ -52,14 +53,13 @@ namespace gg {
 constexpr int kThreadsGG = 384;
 constexpr int kDecWarps = 8;   // warps 4-11: decode + epilogue
 constexpr int kWSteps = 2;     // K-steps per weight stage: 64 contiguous bytes of each row
-constexpr int kWStages = 4;    // weight stages (NVFP4 rows + block scales, from DRAM): 3 in flight
+constexpr int kWStages = 4;    // weight stages per decode warp ring (3 in flight)
 constexpr int kXStages = 2;    // activation tiles per K-step (mostly L2 hits)
 constexpr int kAStages = 3;    // decoded f16 weight tiles
 constexpr int kTileM = 128;
 constexpr int kTileK = 64;
 constexpr int kMaxN = 192;     // tokens per chunk (MMA N)
-constexpr int kWLanes = 32;    // warp 0: weight producer
-constexpr int kXLanes = 64;    // warps 1, 3: activation producers
+constexpr int kXLanes = 96;    // warps 0, 1, 3: activation producers
 constexpr long long kSpinLimit = 1LL << 22;  // try_wait polls per wait before giving up
 
 // A tile = 2 blocks of 128 weight rows sharing one activation tile: gate and
@@ -76,7 +76,9 @@ struct Layout {
   static constexpr int RB = 32 * kWSteps;                        // weight bytes of a row per stage
   static constexpr int SB = 4 * kWSteps;                         // scale bytes of a row per stage
   static constexpr int PPR = RB / 16;                            // 16-byte pieces per row
+  static constexpr int WSLOT = 32 * (RB + SB);                   // one decode warp's rows, one stage
   static constexpr int W_STAGE = W_W + W_S;
+  static_assert(kDecWarps * WSLOT == W_STAGE, "the decode warps' rings fill the W region");
   static constexpr int OFF_A = kXStages * X_STAGE;
   static constexpr int OFF_W = OFF_A + kAStages * A_STAGE;
   static constexpr int SMEM = 1024 + OFF_W + kWStages * W_STAGE;
@@ -176,7 +178,6 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
   using L = Layout<PH>;
   constexpr int NMAT = L::NMAT;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t w_full[kWStages], w_empty[kWStages];
   __shared__ __align__(8) uint64_t x_full[kXStages], x_empty[kXStages];
   __shared__ __align__(8) uint64_t a_full[kAStages], a_empty[kAStages];
   __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], mma_done;
@@ -187,7 +188,6 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
-    for (int s = 0; s < kWStages; ++s) { bar_init(&w_full[s], kWLanes); bar_init(&w_empty[s], kDecWarps); }
     for (int s = 0; s < kXStages; ++s) { bar_init(&x_full[s], kXLanes); bar_init(&x_empty[s], 1); }
     for (int s = 0; s < kAStages; ++s) { bar_init(&a_full[s], kDecWarps); bar_init(&a_empty[s], 1); }
     for (int b = 0; b < 2; ++b) { bar_init(&acc_full[b], 1); bar_init(&acc_empty[b], kDecWarps); }
@@ -210,59 +210,12 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
   const int KT = a.K / kTileK;
   const size_t wld = (size_t)a.K / 2, sld = (size_t)a.K / 16;
 
-  if (warp == 0) {
-    // ------------------------------------------------ weight producer (32 lanes)
-    const int pl = lane;
-    // a stage: per row RB weight bytes (PPR pieces of 16, PPR adjacent lanes
-    // per row so one instruction covers whole row segments) and SB scale bytes
-    constexpr int WI = NMAT * kTileM * L::PPR / kWLanes;  // 16-byte weight pieces per lane
-    constexpr int SI = NMAT * kTileM / kWLanes;           // scale rows per lane
-    int it = 0;
-    bool live = true;
-    for (int tile = blockIdx.x; tile < n_tiles && live; tile += gridDim.x) {
-      const Chunk ch = a.chunks[tile / fb_count];
-      const int row0 = (tile % fb_count) * L::ROWS;
-      const ffn_b200_expert &E = a.experts[ch.expert];
-      // block mi: phase 1 gate (mi 0) / up (mi 1) rows row0..; phase 2 down rows row0 + 128 mi..
-      auto blk_w = [&](int mi) { return PH == 1 ? E.nv[mi].w : E.nv[2].w + (size_t)mi * kTileM * wld; };
-      auto blk_s = [&](int mi) { return PH == 1 ? E.nv[mi].s : E.nv[2].s + (size_t)mi * kTileM * sld; };
-      const int pc = pl % L::PPR, r0 = pl / L::PPR;  // piece of a row, first row of this lane
-      const uint8_t *wsrc0 = blk_w(0) + (size_t)row0 * wld + pc * 16;
-      const uint8_t *wsrc1 = blk_w(1) + (size_t)row0 * wld + pc * 16;
-      const uint8_t *ssrc0 = blk_s(0) + (size_t)row0 * sld;
-      const uint8_t *ssrc1 = blk_s(1) + (size_t)row0 * sld;
-      const bool s16 = ((reinterpret_cast<uintptr_t>(ssrc0) | reinterpret_cast<uintptr_t>(ssrc1)) & (L::SB - 1)) == 0;
-      for (int kw = 0; kw < KT / kWSteps; ++kw, ++it) {
-        const int s = it % kWStages;
-        if (!bar_wait(&w_empty[s], ((it / kWStages) & 1) ^ 1, a.err)) { live = false; break; }
-        uint8_t *st = wbuf + s * L::W_STAGE;
-#pragma unroll 8
-        for (int j = 0; j < WI; ++j) {  // piece pl + 32 j: block j / (WI/2), row r0 + (32/PPR) (j % (WI/2))
-          const int mi = j / (WI / NMAT), r = r0 + (kWLanes / L::PPR) * (j % (WI / NMAT));
-          cp_async16(st + (mi * kTileM + r) * L::RB + pc * 16,
-                     (mi ? wsrc1 : wsrc0) + (size_t)r * wld + kw * L::RB);
-        }
-#pragma unroll
-        for (int j = 0; j < SI; ++j) {  // scale row pl + 32 j
-          const int mi = j / (SI / NMAT), r = pl + kWLanes * (j % (SI / NMAT));
-          uint8_t *dst = st + L::W_W + (mi * kTileM + r) * L::SB;
-          const uint8_t *src = (mi ? ssrc1 : ssrc0) + (size_t)r * sld + kw * L::SB;
-          if (s16) {
-            cp_async_n<L::SB>(dst, src);
-          } else {  // scale arrays only 4-byte aligned
-#pragma unroll
-            for (int q = 0; q < L::SB / 4; ++q) cp_async4(dst + 4 * q, src + 4 * q);
-          }
-        }
-        cp_async_bar_arrive(&w_full[s]);
-      }
-    }
-  } else if (warp == 1 || warp == 3) {
-    // ------------------------------------------------ activation producers (64 lanes)
+  if (warp == 0 || warp == 1 || warp == 3) {
+    // ------------------------------------------------ activation producers (96 lanes)
     // eight lanes per row (one 16-byte piece each): an instruction covers
     // whole 128-byte rows of 4 tokens
     constexpr int RI = kMaxN * 8 / kXLanes;  // rows per lane
-    const int xl = warp == 1 ? lane : 32 + lane;
+    const int xl = (warp == 0 ? 0 : warp == 1 ? 32 : 64) + lane;
     const int kc = xl & 7;
     int it = 0;
     bool live = true;
@@ -333,6 +286,45 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
     const int r = d & 127;  // tile row = TMEM lane (warp w: quarter w % 4)
     // half h decodes row r of A block h
     const int mi = half;
+    // This warp's weight ring: its 32 rows of block mi, kWSteps K-steps per
+    // stage; lanes copy four 16-byte pieces of eight rows per instruction and
+    // one scale row each; kWStages - 1 stages in flight, across tiles.
+    const int dw = warp - 4, rw0 = 32 * (dw & 3);
+    uint8_t *ring = wbuf + dw * kWStages * L::WSLOT;
+    int p_tile = blockIdx.x, p_kw = 0, p_slot = 0;
+    const uint8_t *p_w = nullptr, *p_s = nullptr;
+    bool p_s8 = true;
+    auto issue_next = [&]() {
+      if (p_tile < n_tiles) {
+        if (p_kw == 0) {
+          const Chunk pc_ = a.chunks[p_tile / fb_count];
+          const int prow0 = (p_tile % fb_count) * L::ROWS;
+          const ffn_b200_expert &PE = a.experts[pc_.expert];
+          p_w = (PH == 1 ? PE.nv[mi].w : PE.nv[2].w + (size_t)mi * kTileM * wld) + (size_t)(prow0 + rw0) * wld;
+          p_s = (PH == 1 ? PE.nv[mi].s : PE.nv[2].s + (size_t)mi * kTileM * sld) + (size_t)(prow0 + rw0) * sld;
+          p_s8 = ((reinterpret_cast<uintptr_t>(p_s) | (sld * sizeof(uint8_t))) & (L::SB - 1)) == 0;
+        }
+        uint8_t *slot = ring + p_slot * L::WSLOT;
+#pragma unroll
+        for (int j = 0; j < 32 * L::PPR / 32; ++j) {
+          const int q = lane + 32 * j, rr = q / L::PPR, pc = q % L::PPR;
+          cp_async16(slot + rr * L::RB + pc * 16, p_w + (size_t)rr * wld + p_kw * L::RB + pc * 16);
+        }
+        uint8_t *sd = slot + 32 * L::RB + lane * L::SB;
+        const uint8_t *ss = p_s + (size_t)lane * sld + p_kw * L::SB;
+        if (p_s8) {
+          cp_async_n<L::SB>(sd, ss);
+        } else {
+#pragma unroll
+          for (int q = 0; q < L::SB / 4; ++q) cp_async4(sd + 4 * q, ss + 4 * q);
+        }
+        if (++p_kw == KT / kWSteps) { p_kw = 0; p_tile += gridDim.x; }
+      }
+      cp_async_commit();
+      p_slot = p_slot + 1 == kWStages ? 0 : p_slot + 1;
+    };
+#pragma unroll
+    for (int q = 0; q < kWStages - 1; ++q) issue_next();
     int itw = 0, ita = 0, tcount = 0;
     bool live = true;
     for (int tile = blockIdx.x; tile < n_tiles && live; tile += gridDim.x, ++tcount) {
@@ -349,16 +341,20 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
       for (int kt = 0; kt < KT; ++kt, ++ita) {
         const int sub = kt % kWSteps;  // K-step inside the weight stage
         const int s = itw % kWStages, s2 = ita % kAStages;
-        const bool ok = (sub != 0 || bar_wait(&w_full[s], (itw / kWStages) & 1, a.err)) &&
-                        bar_wait(&a_empty[s2], ((ita / kAStages) & 1) ^ 1, a.err);
+        if (sub == 0) {  // refill the slot consumed last, then wait for this stage
+          issue_next();
+          cp_async_wait<kWStages - 1>();
+          __syncwarp();
+        }
+        const bool ok = bar_wait(&a_empty[s2], ((ita / kAStages) & 1) ^ 1, a.err);
         if (!__all_sync(0xffffffffu, ok)) { live = false; break; }
-        const uint8_t *st = wbuf + s * L::W_STAGE;
+        const uint8_t *st = ring + s * L::WSLOT;
         uint8_t *at = abuf + s2 * L::A_STAGE;
         {
-          const uint8_t *wr = st + (mi * kTileM + r) * L::RB + sub * 32;
+          const uint8_t *wr = st + lane * L::RB + sub * 32;
           const uint4 w0 = *reinterpret_cast<const uint4 *>(wr);
           const uint4 w1 = *reinterpret_cast<const uint4 *>(wr + 16);
-          const uint32_t sc4 = *reinterpret_cast<const uint32_t *>(st + L::W_W + (mi * kTileM + r) * L::SB + sub * 4);
+          const uint32_t sc4 = *reinterpret_cast<const uint32_t *>(st + 32 * L::RB + lane * L::SB + sub * 4);
           const uint32_t s01 = e4m3x2_to_f16x2((uint16_t)(sc4 & 0xFFFFu));
           const uint32_t s23 = e4m3x2_to_f16x2((uint16_t)(sc4 >> 16));
           const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
@@ -377,10 +373,7 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
         }
         fence_async_smem();
         __syncwarp();
-        if (lane == 0) {
-          bar_arrive(&a_full[s2]);
-          if (sub == kWSteps - 1) bar_arrive(&w_empty[s]);
-        }
+        if (lane == 0) bar_arrive(&a_full[s2]);
         if (sub == kWSteps - 1) ++itw;
       }
       if (!live) break;

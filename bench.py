@@ -537,16 +537,6 @@ def run_prefill(a):
     for _ in range(a.warmup):
         step()
     torch.cuda.synchronize()
-    if exchange is not None:  # a timed-out exchange wait: fall back to NCCL
-        bad = torch.tensor([exchange.error()], device=dev)
-        dist.all_reduce(bad, op=dist.ReduceOp.MAX)
-        if int(bad.item()):
-            print("peer exchange reported a timed-out wait; using NCCL", file=sys.stderr)
-            ep.exchange = None
-            for _ in range(a.warmup):
-                step()
-            torch.cuda.synchronize()
-    exch_used = "nvlink-p2p" if ep.exchange is not None else ("nccl" if world > 1 else "none")
     if world > 1:
         dist.barrier()
     clocks = ClockSampler(_bus_id(dev, local))

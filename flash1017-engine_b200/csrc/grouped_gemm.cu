@@ -13,11 +13,12 @@
 //             activation tile feeds as many MMAs as in phase 1)
 //
 // MMA: tcgen05.mma.cta_group::1.kind::f16, M = 128 weight rows, N = chunk
-// tokens rounded up to 16, K = 16 per instruction, fp32 accumulators in TMEM
-// (double-buffered: tile t uses buffer t % 2, so the epilogue of one tile
-// overlaps the next tile's MMAs; phase 1 keeps gate in the buffer's first 128
-// columns and up in the next 128).  Operands are K-major
-// tiles of 64 columns in the 128-byte swizzled canonical layout.
+// tokens rounded up to 16, K = 16 per instruction.  A (the decoded weights)
+// comes from TMEM, B (the activations) from shared memory as K-major tiles of
+// 64 columns in the 128-byte swizzled canonical layout.  TMEM (512 columns):
+// one f32 accumulator buffer of 2 x kMaxN columns (phase 1: gate block, then
+// up block), then the decoded A stages, 2 x 32 columns each (lane = weight
+// row, column c = f16 pair (2c, 2c + 1) of the K-step's 64 values).
 //
 // Weights: NVFP4 rows are decoded on the fly into f16 (exact: an E2M1 value
 // times an E4M3 scale has at most 6 significant bits, inside f16's range), so
@@ -28,18 +29,19 @@
 //
 // Warp roles (384 threads):
 //   warps 0, 1, 3  activation producers: cp.async of the chunk's rows straight
-//                  into their swizzled B tile, 3-deep ring (L2 hits mostly).
-//                  Producer completion is an mbarrier arrive per lane (noinc).
+//                  into their swizzled B tile, kXStages-deep ring (L2 hits
+//                  mostly).  Producer completion is an mbarrier arrive per
+//                  lane (noinc).
 //   warp 2         TMEM allocation; lane 0 issues the MMAs and commits them to
 //                  the ring / accumulator barriers.
-//   warps 4-11     stream their own 32 weight rows (NVFP4 + block scales) through
-//                  a private 4-stage cp.async ring (2 K-steps per stage), as the
-//                  decode GEMV engine does, and decode them into the f16 A tiles
-//                  (thread = row of
-//                  one matrix, or half a row's columns in phase 2), and after
-//                  a tile's last K-step run the epilogue from TMEM (warp w
-//                  reads TMEM lanes 32 (w % 4) ..., warps 4-7 the first half
-//                  of the tile's columns, warps 8-11 the second).
+//   warps 4-11     stream their own 32 weight rows (NVFP4 + block scales)
+//                  through a private kWStages-deep cp.async ring (kWSteps
+//                  K-steps per stage), as the decode GEMV engine does, decode
+//                  them (thread = row of A block w / 4 - 1) and store the f16
+//                  row to TMEM with tcgen05.st; after a tile's last K-step they
+//                  run the epilogue from TMEM (warp w reads TMEM lanes
+//                  32 (w % 4) ..., warps 4-7 the first half of the tile's
+//                  columns, warps 8-11 the second).
 // Every mbarrier wait is bounded; a wait that runs out sets *err and the
 // kernel drains and returns (the host turns *err into FFN_B200_ECUDA).
 #include <algorithm>
@@ -52,13 +54,29 @@ namespace gg {
 
 constexpr int kThreadsGG = 384;
 constexpr int kDecWarps = 8;   // warps 4-11: decode + epilogue
-constexpr int kWSteps = 2;     // K-steps per weight stage: 64 contiguous bytes of each row
-constexpr int kWStages = 4;    // weight stages per decode warp ring (3 in flight)
-constexpr int kXStages = 2;    // activation tiles per K-step (mostly L2 hits)
-constexpr int kAStages = 3;    // decoded f16 weight tiles
+#ifndef GG_WSTEPS
+#define GG_WSTEPS 2
+#endif
+#ifndef GG_WSTAGES
+#define GG_WSTAGES 5
+#endif
+#ifndef GG_XSTAGES
+#define GG_XSTAGES 3
+#endif
+constexpr int kWSteps = GG_WSTEPS;    // K-steps per weight stage: 32 kWSteps contiguous bytes of each row
+constexpr int kWStages = GG_WSTAGES;  // weight stages per decode warp ring (kWStages - 1 in flight)
+constexpr int kXStages = GG_XSTAGES;  // activation tiles per K-step (mostly L2 hits)
+static_assert(kWSteps == 1 || kWSteps == 2 || kWSteps == 4, "K is a multiple of 256");
 constexpr int kTileM = 128;
 constexpr int kTileK = 64;
-constexpr int kMaxN = 192;     // tokens per chunk (MMA N)
+#ifndef GG_MAXN
+#define GG_MAXN 192
+#endif
+constexpr int kMaxN = GG_MAXN;  // tokens per chunk (MMA N)
+// decoded f16 weight tiles (2 blocks x 64 K = 64 TMEM columns each) in the
+// TMEM columns the accumulators (2 blocks x kMaxN) leave free
+constexpr int kAStages = (512 - 2 * kMaxN) / kTileK;
+static_assert(kMaxN % 16 == 0 && kAStages >= 2, "TMEM split");
 constexpr int kXLanes = 96;    // warps 0, 1, 3: activation producers
 constexpr long long kSpinLimit = 1LL << 22;  // try_wait polls per wait before giving up
 
@@ -69,24 +87,27 @@ struct Layout {
   static constexpr int NMAT = 2;                                  // A blocks per tile
   static constexpr int ROWS = PH == 1 ? kTileM : 2 * kTileM;      // output rows per tile
   static constexpr int X_STAGE = kMaxN * 128;                    // swizzled B tile (1024-aligned)
-  static constexpr int A_TILE = kTileM * 128;                    // one f16 A tile
-  static constexpr int A_STAGE = NMAT * A_TILE;
   static constexpr int W_W = NMAT * kTileM * 32 * kWSteps;       // NVFP4 bytes of a weight stage
   static constexpr int W_S = NMAT * kTileM * 4 * kWSteps;        // scale bytes of a weight stage
   static constexpr int RB = 32 * kWSteps;                        // weight bytes of a row per stage
   static constexpr int SB = 4 * kWSteps;                         // scale bytes of a row per stage
   static constexpr int PPR = RB / 16;                            // 16-byte pieces per row
+  // piece swizzle of row r: rows sharing a 128-byte bank window get distinct slots
+  static __device__ __forceinline__ int pswz(int r) { return (r / (128 / RB)) % PPR; }
   static constexpr int WSLOT = 32 * (RB + SB);                   // one decode warp's rows, one stage
   static constexpr int W_STAGE = W_W + W_S;
   static_assert(kDecWarps * WSLOT == W_STAGE, "the decode warps' rings fill the W region");
-  static constexpr int OFF_A = kXStages * X_STAGE;
-  static constexpr int OFF_W = OFF_A + kAStages * A_STAGE;
+  static constexpr int OFF_W = kXStages * X_STAGE;
   static constexpr int SMEM = 1024 + OFF_W + kWStages * W_STAGE;
-  // two blocks x 256 columns: one accumulator buffer
+  static_assert(SMEM + 2048 <= 227 * 1024, "shared memory");
+  // TMEM: one accumulator buffer (NMAT blocks x kMaxN f32 columns), then the
+  // decoded A stages (NMAT blocks x 64 f16 = 32 columns each; lane = row)
   static constexpr int ACC_BUFS = 1;
   static constexpr int ACC_COLS = NMAT * kMaxN;
-  static constexpr int TMEM_COLS = 512;                          // >= ACC_BUFS * ACC_COLS, a power of 2
-  static_assert(ACC_BUFS * ACC_COLS <= TMEM_COLS, "TMEM");
+  static constexpr int A_COL0 = ACC_BUFS * ACC_COLS;
+  static constexpr int A_COLS = NMAT * kTileK / 2;
+  static constexpr int TMEM_COLS = 512;                          // a power of 2
+  static_assert(A_COL0 + kAStages * A_COLS <= TMEM_COLS, "TMEM");
 };
 
 struct Chunk {
@@ -156,17 +177,37 @@ __device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint3
                "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n"
                ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
 }
-__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+// A from TMEM (M = 128 lanes = rows, K along columns, two f16 per column)
+__device__ __forceinline__ void tc_mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+               "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n"
+               ::"r"(d), "r"(a), "l"(b), "r"(id), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+// 32 columns of this thread's TMEM lane; complete (wait::st) on return
+__device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+               "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+               ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]),
+                 "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+                 "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]),
+                 "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]),
+                 "r"(v[31]) : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+// without the wait: several loads in flight, then one tcgen05.wait::ld
+__device__ __forceinline__ void tc_ld16_nw(uint32_t taddr, uint32_t (&v)[16]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
                  "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-               : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+               : "r"(taddr) : "memory");
 }
 
 // the decode path's SwiGLU (flash1017.rs:7539): min(silu(g), 10) * clamp(u, -10, 10),
 // NaN propagating like Rust's f32::clamp
 __device__ __forceinline__ float silu10(float g) { return fminf(g / (1.0f + expf(-g)), 10.0f); }
+// the same with the hardware exp2 approximation and a fast divide (relative
+// error ~1e-6, far inside the path's 1e-3 output tolerance; h is rounded to f16)
+__device__ __forceinline__ float silu10_fast(float g) { return fminf(__fdividef(g, 1.0f + __expf(-g)), 10.0f); }
 __device__ __forceinline__ float clamp10f(float u) {
   if (u < -10.f) u = -10.f;
   if (u > 10.f) u = 10.f;
@@ -184,7 +225,7 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
   __shared__ uint32_t s_tmem;
   __shared__ float s_xs[2][kMaxN];  // phase 1: 2^xe of the tile's tokens (by tile parity)
   uint8_t *smem = smem_raw + ((1024 - (sa(smem_raw) & 1023)) & 1023);
-  uint8_t *xbuf = smem, *abuf = smem + L::OFF_A, *wbuf = smem + L::OFF_W;
+  uint8_t *xbuf = smem, *wbuf = smem + L::OFF_W;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
@@ -214,7 +255,7 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
     // ------------------------------------------------ activation producers (96 lanes)
     // eight lanes per row (one 16-byte piece each): an instruction covers
     // whole 128-byte rows of 4 tokens
-    constexpr int RI = kMaxN * 8 / kXLanes;  // rows per lane
+    constexpr int RI = (kMaxN * 8 + kXLanes - 1) / kXLanes;  // rows per lane (rows >= nn skipped)
     const int xl = (warp == 0 ? 0 : warp == 1 ? 32 : 64) + lane;
     const int kc = xl & 7;
     int it = 0;
@@ -262,12 +303,12 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
           fence_async_smem();
           tc_fence_after();
           const uint32_t xb = sa(xbuf + s3 * L::X_STAGE);
-          const uint32_t ab = sa(abuf + s2 * L::A_STAGE);
+          const uint32_t ab = tmem + L::A_COL0 + s2 * L::A_COLS;
 #pragma unroll
           for (int mi = 0; mi < NMAT; ++mi)
 #pragma unroll
             for (int j = 0; j < kTileK / 16; ++j)
-              tc_mma(acc_col + mi * kMaxN, sdesc(ab + mi * L::A_TILE + 32 * j), sdesc(xb + 32 * j), id,
+              tc_mma_ts(acc_col + mi * kMaxN, ab + mi * (kTileK / 2) + 8 * j, sdesc(xb + 32 * j), id,
                      (kt > 0 || j > 0) ? 1u : 0u);
           tc_commit(&a_empty[s2]);
           tc_commit(&x_empty[s3]);
@@ -288,7 +329,10 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
     const int mi = half;
     // This warp's weight ring: its 32 rows of block mi, kWSteps K-steps per
     // stage; lanes copy four 16-byte pieces of eight rows per instruction and
-    // one scale row each; kWStages - 1 stages in flight, across tiles.
+    // one scale row each; kWStages - 1 stages in flight, across tiles.  Piece
+    // c of row r sits at piece slot c ^ pswz(r) of the row, so the decode's
+    // 16-byte row reads are free of bank conflicts while each copy
+    // instruction still fills 512 contiguous bytes.
     const int dw = warp - 4, rw0 = 32 * (dw & 3);
     uint8_t *ring = wbuf + dw * kWStages * L::WSLOT;
     int p_tile = blockIdx.x, p_kw = 0, p_slot = 0;
@@ -308,7 +352,7 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
 #pragma unroll
         for (int j = 0; j < 32 * L::PPR / 32; ++j) {
           const int q = lane + 32 * j, rr = q / L::PPR, pc = q % L::PPR;
-          cp_async16(slot + rr * L::RB + pc * 16, p_w + (size_t)rr * wld + p_kw * L::RB + pc * 16);
+          cp_async16(slot + rr * L::RB + ((pc ^ L::pswz(rr)) << 4), p_w + (size_t)rr * wld + p_kw * L::RB + pc * 16);
         }
         uint8_t *sd = slot + 32 * L::RB + lane * L::SB;
         const uint8_t *ss = p_s + (size_t)lane * sld + p_kw * L::SB;
@@ -349,29 +393,31 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
         const bool ok = bar_wait(&a_empty[s2], ((ita / kAStages) & 1) ^ 1, a.err);
         if (!__all_sync(0xffffffffu, ok)) { live = false; break; }
         const uint8_t *st = ring + s * L::WSLOT;
-        uint8_t *at = abuf + s2 * L::A_STAGE;
+        tc_fence_after();
+        // this warp's 32 lanes of block mi, stage s2
+        const uint32_t at = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + L::A_COL0 + s2 * L::A_COLS +
+                            mi * (kTileK / 2);
         {
-          const uint8_t *wr = st + lane * L::RB + sub * 32;
-          const uint4 w0 = *reinterpret_cast<const uint4 *>(wr);
-          const uint4 w1 = *reinterpret_cast<const uint4 *>(wr + 16);
+          const uint8_t *wr = st + lane * L::RB;
+          const int sw = L::pswz(lane);
+          const uint4 w0 = *reinterpret_cast<const uint4 *>(wr + (((2 * sub) ^ sw) << 4));
+          const uint4 w1 = *reinterpret_cast<const uint4 *>(wr + (((2 * sub + 1) ^ sw) << 4));
           const uint32_t sc4 = *reinterpret_cast<const uint32_t *>(st + 32 * L::RB + lane * L::SB + sub * 4);
           const uint32_t s01 = e4m3x2_to_f16x2((uint16_t)(sc4 & 0xFFFFu));
           const uint32_t s23 = e4m3x2_to_f16x2((uint16_t)(sc4 >> 16));
           const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+          uint32_t o[32];  // TMEM column c = f16 pair (2c, 2c + 1) of the row's 64 K values
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {  // word j = columns 8j..8j+7 = 16-byte chunk j
+          for (int j = 0; j < 8; ++j) {  // word j = K values 8j..8j+7
             uint32_t dd[4];
             e2m1x8_to_f16x2(words[j], dd);
             const uint32_t sc = j < 2 ? bcast_lo(s01) : j < 4 ? bcast_hi(s01) : j < 6 ? bcast_lo(s23) : bcast_hi(s23);
-            uint4 o;
-            o.x = hmul2_u32(dd[0], sc);
-            o.y = hmul2_u32(dd[1], sc);
-            o.z = hmul2_u32(dd[2], sc);
-            o.w = hmul2_u32(dd[3], sc);
-            *reinterpret_cast<uint4 *>(at + mi * L::A_TILE + sw128(r, j)) = o;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) o[4 * j + q] = hmul2_u32(dd[q], sc);
           }
+          tc_st32(at, o);
         }
-        fence_async_smem();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) bar_arrive(&a_full[s2]);
         if (sub == kWSteps - 1) ++itw;
@@ -387,10 +433,8 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
       const ffn_b200_expert &E = a.experts[ch.expert];
       const float gs0 = E.nv[PH == 1 ? 0 : 2].gs, gs1 = E.nv[PH == 1 ? 1 : 2].gs;
       const int split = ((ch.npad / 16 + 1) / 2) * 16;  // columns [0, split) | [split, npad)
-      for (int n0 = half ? split : 0; n0 < (half ? ch.npad : split); n0 += 16) {
-        uint32_t v0[16], v1[16];
-        tc_ld16(tl + n0, v0);
-        tc_ld16(tl + kMaxN + n0, v1);
+      // 16 columns of both blocks -> h (phase 1) or y (phase 2)
+      auto emit = [&](const uint32_t (&v0)[16], const uint32_t (&v1)[16], int n0) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int n = n0 + j;
@@ -400,12 +444,26 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
             const float xs = s_xs[tcount & 1][n];
             const float g = __uint_as_float(v0[j]) * xs * gs0;
             const float u = __uint_as_float(v1[j]) * xs * gs1;
-            a.h[(size_t)p * a.ld_h + row] = __float2half_rn(silu10(g) * clamp10f(u));
+            a.h[(size_t)p * a.ld_h + row] = __float2half_rn(silu10_fast(g) * clamp10f(u));
           } else {
             a.y[(size_t)p * a.ld_y + row] = __uint_as_float(v0[j]) * gs0;
             a.y[(size_t)p * a.ld_y + row + kTileM] = __uint_as_float(v1[j]) * gs1;
           }
         }
+      };
+      const int n_end = half ? ch.npad : split;
+      for (int n0 = half ? split : 0; n0 < n_end; n0 += 32) {
+        uint32_t g0[16], u0[16], g1[16], u1[16];
+        const bool two = n0 + 16 < n_end;  // warp-uniform
+        tc_ld16_nw(tl + n0, g0);
+        tc_ld16_nw(tl + kMaxN + n0, u0);
+        if (two) {
+          tc_ld16_nw(tl + n0 + 16, g1);
+          tc_ld16_nw(tl + kMaxN + n0 + 16, u1);
+        }
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        emit(g0, u0, n0);
+        if (two) emit(g1, u1, n0 + 16);
       }
       tc_fence_before();
       __syncwarp();

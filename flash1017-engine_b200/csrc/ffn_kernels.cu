@@ -734,26 +734,64 @@ int launch_exact_matvec(const float *w32, const uint16_t *w16, const float *x, i
 // k-step (wh*xh + wh*xl + wl*xh) leave an error of about 2^-22 relative.  The
 // summation order differs from the CPU loop, so selections can differ from the
 // reference's only where two biased scores are within that error.
-// CTA = 32 experts x 32 tokens x one of gridDim.z K-ranges; the 8 warps split
-// the range; shared-memory reduction.  Each K-range writes its own partial
-// logits (logits + z * n_tok * n_exp); top-k adds the partials in z order.
+// CTA = 32 experts x 32 tokens x one of gridDim.z K-ranges.  The range is
+// streamed through a 3-stage cp.async pipeline of 128-column stages (f32
+// weight rows, f16 hi and lo token rows; rows padded so the fragment reads are
+// free of bank conflicts); warp w computes k-step w of every stage, and the
+// 8 warps' partial tiles are added in warp order through shared memory.  Each
+// K-range writes its own partial logits (logits + z * n_tok * n_exp); top-k adds
+// the partials in z order.
 constexpr int kRouterWarps = 8;  // router_tc_kernel runs 256 threads
 // K-ranges of the tensor router (partial logit planes): 12 x 8 x 3 = 288 CTAs of a
 // 256-token, 384-expert layer fit one wave at 2 CTAs per SM
 constexpr int kRouterKSplit = 3;
-__global__ void __launch_bounds__(256) router_tc_kernel(const float *__restrict__ w,
-                                                        const __half *__restrict__ xh,
-                                                        const __half *__restrict__ xl,
-                                                        const int *__restrict__ xe, int n_tok,
-                                                        int n_exp, int H,
-                                                        float *__restrict__ logits) {
-  __shared__ float red[kRouterWarps][32][33];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+constexpr int kRtStages = 3;
+constexpr int kRtW = 128 * 4 + 64;   // weight row stride (bytes): 576, rows 16 banks apart
+constexpr int kRtX = 128 * 2 + 32;   // token row stride (bytes): 288, rows 8 banks apart
+constexpr int kRtStage = 32 * kRtW + 2 * 32 * kRtX;
+constexpr int kRtSmem = kRtStages * kRtStage;  // 110,592 bytes: 2 CTAs per SM
+static_assert(kRouterWarps * 32 * 33 * 4 <= kRtSmem, "reduction fits the pipeline buffers");
+__global__ void __launch_bounds__(256, 2) router_tc_kernel(const float *__restrict__ w,
+                                                           const __half *__restrict__ xh,
+                                                           const __half *__restrict__ xl,
+                                                           const int *__restrict__ xe, int n_tok,
+                                                           int n_exp, int H,
+                                                           float *__restrict__ logits) {
+  extern __shared__ __align__(16) uint8_t rt_smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int e0 = blockIdx.x * 32, t0 = blockIdx.y * 32;
   const int ksteps = H / 16, kz = (ksteps + gridDim.z - 1) / gridDim.z;
   const int ks_lo = blockIdx.z * kz, ks_hi = min(ksteps, ks_lo + kz);
+  const int n_st = ks_hi > ks_lo ? (ks_hi - ks_lo + 7) / 8 : 0;
   logits += (size_t)blockIdx.z * n_tok * n_exp;
+
+  // copies of stage s: 1024 16-byte weight pieces (32 rows x 32) and 1024 token
+  // pieces (hi and lo, 32 rows x 16); pieces of k-steps past the range are skipped
+  auto issue = [&](int s) {
+    if (s < n_st) {
+      uint8_t *sw = rt_smem + (s % kRtStages) * kRtStage, *sx = sw + 32 * kRtW;
+      const int kb = ks_lo + 8 * s;  // first k-step of the stage
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int p = tid + 256 * q;
+        const int r = p >> 5, pc = p & 31;
+        if (kb + (pc >> 2) < ks_hi)
+          cp_async16(sw + r * kRtW + pc * 16,
+                     w + (size_t)min(e0 + r, n_exp - 1) * H + (size_t)kb * 16 + pc * 4);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int p = tid + 256 * q;
+        const int arr = p >> 9, r = (p >> 4) & 31, pc = p & 15;
+        if (kb + (pc >> 1) < ks_hi)
+          cp_async16(sx + arr * 32 * kRtX + r * kRtX + pc * 16,
+                     (arr ? xl : xh) + (size_t)min(t0 + r, n_tok - 1) * H + (size_t)kb * 16 + pc * 8);
+      }
+    }
+    cp_async_commit();
+  };
+
   float acc[2][4][4];
 #pragma unroll
   for (int i = 0; i < 2; ++i)
@@ -761,56 +799,48 @@ __global__ void __launch_bounds__(256) router_tc_kernel(const float *__restrict_
     for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int q = 0; q < 4; ++q) acc[i][j][q] = 0.f;
-  const float *wa[2], *wb[2];
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    wa[i] = w + (size_t)min(e0 + 16 * i + g, n_exp - 1) * H;
-    wb[i] = w + (size_t)min(e0 + 16 * i + g + 8, n_exp - 1) * H;
-  }
-  const __half *ph[4], *pl[4];
-  bool tv[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int tok = t0 + 8 * j + g;
-    tv[j] = tok < n_tok;
-    ph[j] = xh + (size_t)min(tok, n_tok - 1) * H;
-    pl[j] = xl + (size_t)min(tok, n_tok - 1) * H;
-  }
-#pragma unroll 2
-  for (int ks = ks_lo + warp; ks < ks_hi; ks += kRouterWarps) {
-    const int c = ks * 16 + 4 * t;
-    uint32_t ah[2][4], al[2][4];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const float4 va = __ldg(reinterpret_cast<const float4 *>(wa[i] + c));
-      const float4 vb = __ldg(reinterpret_cast<const float4 *>(wb[i] + c));
-      __half h[8], l[8];
-      const float v[8] = {va.x, va.y, vb.x, vb.y, va.z, va.w, vb.z, vb.w};
-#pragma unroll
-      for (int q = 0; q < 8; ++q) split_f16(v[q], h[q], l[q]);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        __half2 hh = __halves2half2(h[2 * q], h[2 * q + 1]);
-        __half2 ll = __halves2half2(l[2 * q], l[2 * q + 1]);
-        ah[i][q] = *reinterpret_cast<uint32_t *>(&hh);
-        al[i][q] = *reinterpret_cast<uint32_t *>(&ll);
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint2 bh = make_uint2(0, 0), bl = make_uint2(0, 0);
-      if (tv[j]) {
-        bh = __ldg(reinterpret_cast<const uint2 *>(ph[j] + c));
-        bl = __ldg(reinterpret_cast<const uint2 *>(pl[j] + c));
-      }
+  for (int s = 0; s < kRtStages - 1; ++s) issue(s);
+  for (int s = 0; s < n_st; ++s) {
+    cp_async_wait<kRtStages - 2>();
+    __syncthreads();  // stage s visible to all; stage s - 1's slot is free
+    issue(s + kRtStages - 1);
+    if (ks_lo + 8 * s + warp < ks_hi) {
+      const uint8_t *sw = rt_smem + (s % kRtStages) * kRtStage, *sx = sw + 32 * kRtW;
+      const int cb = warp * 16 + 4 * t;  // this lane's 4 columns of the warp's k-step
+      uint32_t ah[2][4], al[2][4];
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
-        mma_f16(acc[i][j], ah[i][0], ah[i][1], ah[i][2], ah[i][3], bh.x, bh.y);
-        mma_f16(acc[i][j], ah[i][0], ah[i][1], ah[i][2], ah[i][3], bl.x, bl.y);
-        mma_f16(acc[i][j], al[i][0], al[i][1], al[i][2], al[i][3], bh.x, bh.y);
+        const float4 va = *reinterpret_cast<const float4 *>(sw + (16 * i + g) * kRtW + cb * 4);
+        const float4 vb = *reinterpret_cast<const float4 *>(sw + (16 * i + g + 8) * kRtW + cb * 4);
+        __half h[8], l[8];
+        const float v[8] = {va.x, va.y, vb.x, vb.y, va.z, va.w, vb.z, vb.w};
+#pragma unroll
+        for (int q = 0; q < 8; ++q) split_f16(v[q], h[q], l[q]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          __half2 hh = __halves2half2(h[2 * q], h[2 * q + 1]);
+          __half2 ll = __halves2half2(l[2 * q], l[2 * q + 1]);
+          ah[i][q] = *reinterpret_cast<uint32_t *>(&hh);
+          al[i][q] = *reinterpret_cast<uint32_t *>(&ll);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint2 bh = *reinterpret_cast<const uint2 *>(sx + (8 * j + g) * kRtX + cb * 2);
+        const uint2 bl = *reinterpret_cast<const uint2 *>(sx + 32 * kRtX + (8 * j + g) * kRtX + cb * 2);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          mma_f16(acc[i][j], ah[i][0], ah[i][1], ah[i][2], ah[i][3], bh.x, bh.y);
+          mma_f16(acc[i][j], ah[i][0], ah[i][1], ah[i][2], ah[i][3], bl.x, bl.y);
+          mma_f16(acc[i][j], al[i][0], al[i][1], al[i][2], al[i][3], bh.x, bh.y);
+        }
       }
     }
   }
+  cp_async_wait<0>();
+  __syncthreads();  // every warp is done with the pipeline buffers
+  float(*red)[32][33] = reinterpret_cast<float(*)[32][33]>(rt_smem);
 #pragma unroll
   for (int i = 0; i < 2; ++i)
 #pragma unroll
@@ -826,10 +856,10 @@ __global__ void __launch_bounds__(256) router_tc_kernel(const float *__restrict_
     const int el = q & 31, tl = q >> 5;
     const int e = e0 + el, tok = t0 + tl;
     if (e >= n_exp || tok >= n_tok) continue;
-    float s = 0.f;
+    float sum = 0.f;
 #pragma unroll
-    for (int wv = 0; wv < kRouterWarps; ++wv) s += red[wv][el][tl];
-    logits[(size_t)tok * n_exp + e] = s * pow2f(xe[tok]);
+    for (int wv = 0; wv < kRouterWarps; ++wv) sum += red[wv][el][tl];
+    logits[(size_t)tok * n_exp + e] = sum * pow2f(xe[tok]);
   }
 }
 
@@ -876,42 +906,38 @@ __global__ void __launch_bounds__(64) topk_kernel(const float *__restrict__ logi
       cb[j] = e < n_exp ? cs[j] + (bias ? bias[e] : 0.0f) : -INFINITY;
     }
   }
-  constexpr int kLocal = 8;  // lane-local candidate list (top_k <= 8 path)
-  if (cached && top_k <= kLocal) {
-    // Each lane keeps its best top_k of its 12 experts sorted in registers;
-    // then every round takes the best list head over the warp and the
-    // winning lane drops its head.  Order: biased score desc, index asc.
-    float lb[kLocal], ls[kLocal];
-    int li[kLocal];
+  if (cached && top_k <= 32) {
+    // Each lane keeps the best of its own live experts (lane + 32j); a round
+    // takes the warp's best lane head (biased score desc, index asc) and the
+    // winning lane retires that expert and rescans its <= 16.  NaN scores are
+    // never candidates; if no candidate is left the round yields index
+    // 0x7fffffff with score 0.
+    uint32_t alive = 0;
 #pragma unroll
-    for (int q = 0; q < kLocal; ++q) { lb[q] = -INFINITY; ls[q] = 0.f; li[q] = 0x7fffffff; }
+    for (int j = 0; j < kCache; ++j)
+      if (lane + 32 * j < n_exp && cb[j] == cb[j]) alive |= 1u << j;
+    float hb = 0.f, hs = 0.f;  // this lane's head: biased score, score, slot
+    int hj = -1;
+    auto rescan = [&]() {
+      hj = -1;
+      hb = -INFINITY;
+      hs = 0.f;
 #pragma unroll
-    for (int j = 0; j < kCache; ++j) {
-      float cb_ = cb[j], cs_ = cs[j];
-      int ci = lane + 32 * j;
-      if (ci >= n_exp) continue;
-#pragma unroll
-      for (int q = 0; q < kLocal; ++q) {  // insertion: carry the loser down the list
-        const bool better = cb_ > lb[q] || (cb_ == lb[q] && ci < li[q]);
-        const float tb = lb[q], ts = ls[q];
-        const int ti = li[q];
-        if (better) { lb[q] = cb_; ls[q] = cs_; li[q] = ci; cb_ = tb; cs_ = ts; ci = ti; }
-      }
-    }
+      for (int j = 0; j < kCache; ++j)
+        if (((alive >> j) & 1u) && (hj < 0 || cb[j] > hb)) { hb = cb[j]; hs = cs[j]; hj = j; }
+    };
+    rescan();
     for (int k = 0; k < top_k; ++k) {
-      // warp maximum of the heads by an order-preserving integer key of the
-      // biased score, then the lowest expert index among the heads that tie
-      const uint32_t u = __float_as_uint(lb[0]);
-      const uint32_t key = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+      const uint32_t u = __float_as_uint(hb);
+      const uint32_t key = hj < 0 ? 0u : ((u & 0x80000000u) ? ~u : (u | 0x80000000u));
       const uint32_t kmax = __reduce_max_sync(0xffffffffu, key);
-      const int bi = (int)__reduce_min_sync(0xffffffffu, key == kmax ? (uint32_t)li[0] : 0xffffffffu);
-      const float bs = __shfl_sync(0xffffffffu, ls[0], bi & 31);  // expert e lives on lane e % 32
-      if (lane == k) { my_score = bs; my_idx = bi; }
-      if (li[0] == bi) {  // this lane's head won: pop it
-#pragma unroll
-        for (int q = 0; q + 1 < kLocal; ++q) { lb[q] = lb[q + 1]; ls[q] = ls[q + 1]; li[q] = li[q + 1]; }
-        lb[kLocal - 1] = -INFINITY;
-        li[kLocal - 1] = 0x7fffffff;
+      const uint32_t cand = (key == kmax && hj >= 0) ? (uint32_t)(lane + 32 * hj) : 0x7fffffffu;
+      const int bi = (int)__reduce_min_sync(0xffffffffu, cand);
+      const float bs = __shfl_sync(0xffffffffu, hs, bi & 31);
+      if (lane == k) { my_score = bi == 0x7fffffff ? 0.f : bs; my_idx = bi; }
+      if (bi != 0x7fffffff && lane == (bi & 31)) {  // this lane's head won: retire it
+        alive &= ~(1u << hj);
+        rescan();
       }
     }
   } else {
@@ -971,8 +997,16 @@ int launch_router(const float *w, const float *bias, const float *x, const __hal
     n_part = std::max(1, std::min(kRouterKSplit, H / 16 / kRouterWarps));
     dim3 g1((n_exp + 31) / 32, (n_tok + 31) / 32, n_part);
     if (g1.y > 65535) return fail(FFN_B200_EINVAL, "router: too many tokens");
+    static bool attr_set[64] = {false};  // > 48 KB of dynamic shared memory, once per device
+    int dev = 0;
+    FFN_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(FFN_B200_EUNSUP, "router: device index >= 64");
+    if (!attr_set[dev]) {
+      FFN_CUDA_TRY(cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRtSmem));
+      attr_set[dev] = true;
+    }
     FFN_LAUNCH(FFN_B200_K_ROUTER, st, "router_tc_kernel",
-               router_tc_kernel<<<g1, 256, 0, st>>>(w, xh, xl, xe, n_tok, n_exp, H, logits));
+               router_tc_kernel<<<g1, 256, kRtSmem, st>>>(w, xh, xl, xe, n_tok, n_exp, H, logits));
   }
   FFN_LAUNCH(FFN_B200_K_TOPK, st, "topk_kernel",
              topk_kernel<<<(n_tok + 1) / 2, 64, 0, st>>>(logits, bias, n_tok, n_exp, top_k, score_fn,

@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "ffn_b200.h"
 
@@ -37,6 +38,50 @@ void prof_end(int kind, cudaStream_t st);
     ::ffn::note_launch();                                           \
     cudaError_t _e = cudaGetLastError();                            \
     if (_e != cudaSuccess) return ::ffn::cuda_fail(_e, name);       \
+  } while (0)
+
+// Programmatic dependent launch.  The kernels of the MoE layer chain
+// (xprep, router, top-k, grouping, the expert phases, combine) are launched
+// with cudaLaunchAttributeProgrammaticStreamSerialization, so a kernel's CTAs
+// may be scheduled while the previous kernel in the stream drains; each such
+// kernel calls pdl_enter() before it reads anything an earlier kernel wrote.
+// griddepcontrol.wait returns once the previous grid has completed and its
+// memory is visible (immediately when the launch had no such dependency);
+// launch_dependents then lets the next kernel be scheduled early in turn.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+bool pdl_allowed();  // false when FFN_B200_NO_PDL is set in the environment
+
+template <typename... P, typename... A>
+inline cudaError_t launch_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              A &&...args) {
+  cudaLaunchAttribute at;
+  at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at.val.programmaticStreamSerializationAllowed = pdl_allowed() ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = &at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<A>(args)...);
+}
+
+// FFN_LAUNCH for a kernel that calls pdl_enter(): kern (parenthesised if it
+// has template arguments), grid, block, dynamic shared memory, then the
+// kernel's arguments.
+#define FFN_LAUNCH_PDL(kind, st, name, kern, grid, block, smem, ...)          \
+  do {                                                                        \
+    ::ffn::prof_begin(kind, st);                                              \
+    cudaError_t _l = ::ffn::launch_pdl(kern, grid, block, smem, st, __VA_ARGS__); \
+    ::ffn::prof_end(kind, st);                                                \
+    ::ffn::note_launch();                                                     \
+    cudaError_t _e = cudaGetLastError();                                      \
+    if (_l != cudaSuccess) _e = _l;                                           \
+    if (_e != cudaSuccess) return ::ffn::cuda_fail(_e, name);                 \
   } while (0)
 
 constexpr int kTopKMax = 16;   // router top_k upper bound

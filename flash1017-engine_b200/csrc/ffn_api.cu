@@ -1,6 +1,7 @@
 // ffn_api.cu -- the device-resident extension ABI (include/ffn_b200.h).
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -22,6 +23,13 @@ int cuda_fail(cudaError_t e, const char *what) {
   return fail(FFN_B200_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 void note_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+bool pdl_allowed() {
+  static const bool on = [] {
+    const char *v = std::getenv("FFN_B200_NO_PDL");
+    return !(v && *v && *v != '0');
+  }();
+  return on;
+}
 
 // ------------------------------------------------------------- profiling
 // A fixed pool of event pairs, created when profiling is enabled; launches

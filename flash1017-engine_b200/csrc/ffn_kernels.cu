@@ -25,6 +25,7 @@ __global__ void __launch_bounds__(256) xprep_loop_kernel(const float *__restrict
                                                     __half *tl, int ld_o, int *xe,
                                                     const float *__restrict__ norm_w,
                                                     float norm_eps, int seq_norm, float *xn) {
+  pdl_enter();
   const int row = blockIdx.x;
   const float *xr = x + (size_t)row * ld_x;
   __shared__ float red[32];
@@ -103,6 +104,7 @@ __global__ void __launch_bounds__(256) xprep_reg_kernel(const float *__restrict_
                                                         __half *tl, int ld_o, int *xe,
                                                         const float *__restrict__ norm_w,
                                                         float norm_eps, int seq_norm, float *xn) {
+  pdl_enter();
   const int row = blockIdx.x;
   const float *xr = x + (size_t)row * ld_x;
   __shared__ float red[32];
@@ -206,13 +208,9 @@ int launch_xprep(const float *x, int ld_x, int rows, int K, __half *nh, __half *
                    (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(norm_w) & 15) == 0;
   if (reg)
-    FFN_LAUNCH(FFN_B200_K_XPREP, st, "xprep_reg_kernel",
-               xprep_reg_kernel<<<rows, 256, 0, st>>>(x, ld_x, K, nh, nl, th, tl, ld_o, xe, norm_w,
-                                                      norm_eps, seq_norm, xn));
+    FFN_LAUNCH_PDL(FFN_B200_K_XPREP, st, "xprep_reg_kernel", xprep_reg_kernel, rows, 256, 0, x, ld_x, K, nh, nl, th, tl, ld_o, xe, norm_w, norm_eps, seq_norm, xn);
   else
-    FFN_LAUNCH(FFN_B200_K_XPREP, st, "xprep_loop_kernel",
-               xprep_loop_kernel<<<rows, 256, 0, st>>>(x, ld_x, K, nh, nl, th, tl, ld_o, xe, norm_w,
-                                                       norm_eps, seq_norm, xn));
+    FFN_LAUNCH_PDL(FFN_B200_K_XPREP, st, "xprep_loop_kernel", xprep_loop_kernel, rows, 256, 0, x, ld_x, K, nh, nl, th, tl, ld_o, xe, norm_w, norm_eps, seq_norm, xn);
   return 0;
 }
 
@@ -313,6 +311,7 @@ __device__ __forceinline__ MatInfo task_info(const PhaseArgs &a, int expert, int
 // of one slice, so the slice's activation rows are shared in L1.
 template <int FMT, int PHASE, int MINB>
 __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a) {
+  pdl_enter();
   constexpr int NMAT = PHASE == 1 ? 2 : 1;
   constexpr int R = task_r<PHASE>();
   using WE = WarpEngine<FMT, NMAT, R, kStages, kSub>;
@@ -547,8 +546,7 @@ static int launch_phase_t(const PhaseArgs &a, long long tasks, cudaStream_t st) 
   }
   const long long want = (tasks + kWarps - 1) / kWarps;
   const int grid = (int)std::max<long long>(1, std::min<long long>(want, (long long)MINB * sm_count_of(dev)));
-  FFN_LAUNCH(phase_kind(FMT, PHASE), st, "phase_kernel",
-             (phase_kernel<FMT, PHASE, MINB><<<grid, kThreads, smem, st>>>(a)));
+  FFN_LAUNCH_PDL(phase_kind(FMT, PHASE), st, "phase_kernel", (phase_kernel<FMT, PHASE, MINB>), grid, kThreads, smem, a);
   return 0;
 }
 
@@ -573,6 +571,7 @@ int launch_phase(int fmt, int phase, const PhaseArgs &a, long long tasks, cudaSt
 // fixed order.
 constexpr int kCorezThreads = 512;
 __global__ void __launch_bounds__(kCorezThreads) corez_kernel(const CoreZArgs a) {
+  pdl_enter();
   const int n_vexp = a.vexp ? *a.n_vexp_dev : (a.n_tok_direct + kNTok - 1) / kNTok;
   const int item = blockIdx.x;
   const int v = item / a.nmat, mm = a.mat0 + item % a.nmat;
@@ -669,8 +668,7 @@ __global__ void __launch_bounds__(kCorezThreads) corez_kernel(const CoreZArgs a)
 
 int launch_corez(const CoreZArgs &a, int max_vexp, cudaStream_t st) {
   if (max_vexp <= 0) return 0;
-  FFN_LAUNCH(FFN_B200_K_COREZ, st, "corez_kernel",
-             corez_kernel<<<max_vexp * a.nmat, kCorezThreads, 0, st>>>(a));
+  FFN_LAUNCH_PDL(FFN_B200_K_COREZ, st, "corez_kernel", corez_kernel, max_vexp * a.nmat, kCorezThreads, 0, a);
   return 0;
 }
 
@@ -688,6 +686,7 @@ __global__ void __launch_bounds__(256) router_exact_kernel(const WT *__restrict_
                                                            const float *__restrict__ x, int n_tok,
                                                            int n_exp, int H,
                                                            float *__restrict__ logits) {
+  pdl_enter();
   __shared__ float ws[32][65];
   __shared__ float xs[8][64];
   const int el = threadIdx.x & 31, tl = threadIdx.x >> 5;
@@ -720,11 +719,9 @@ int launch_exact_matvec(const float *w32, const uint16_t *w16, const float *x, i
   dim3 g1((rows + 31) / 32, (n_tok + 7) / 8);
   if (g1.y > 65535) return fail(FFN_B200_EINVAL, "exact matvec: too many tokens");
   if (w32)
-    FFN_LAUNCH(FFN_B200_K_ROUTER, st, "router_exact_kernel",
-               (router_exact_kernel<float><<<g1, 256, 0, st>>>(w32, x, n_tok, rows, H, out)));
+    FFN_LAUNCH_PDL(FFN_B200_K_ROUTER, st, "router_exact_kernel", (router_exact_kernel<float>), g1, 256, 0, w32, x, n_tok, rows, H, out);
   else
-    FFN_LAUNCH(FFN_B200_K_ROUTER, st, "router_exact_kernel",
-               (router_exact_kernel<uint16_t><<<g1, 256, 0, st>>>(w16, x, n_tok, rows, H, out)));
+    FFN_LAUNCH_PDL(FFN_B200_K_ROUTER, st, "router_exact_kernel", (router_exact_kernel<uint16_t>), g1, 256, 0, w16, x, n_tok, rows, H, out);
   return 0;
 }
 
@@ -757,6 +754,7 @@ __global__ void __launch_bounds__(256, 2) router_tc_kernel(const float *__restri
                                                            const int *__restrict__ xe, int n_tok,
                                                            int n_exp, int H,
                                                            float *__restrict__ logits) {
+  pdl_enter();
   extern __shared__ __align__(16) uint8_t rt_smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
@@ -877,6 +875,7 @@ __global__ void __launch_bounds__(64) topk_kernel(const float *__restrict__ logi
                                                    const float *__restrict__ bias, int n_tok,
                                                    int n_exp, int top_k, int score_fn,
                                                    int n_part, int32_t *idx, float *wt) {
+  pdl_enter();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= n_tok) return;
   const float *lg = logits + (size_t)warp * n_exp;
@@ -1005,12 +1004,9 @@ int launch_router(const float *w, const float *bias, const float *x, const __hal
       FFN_CUDA_TRY(cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRtSmem));
       attr_set[dev] = true;
     }
-    FFN_LAUNCH(FFN_B200_K_ROUTER, st, "router_tc_kernel",
-               router_tc_kernel<<<g1, 256, kRtSmem, st>>>(w, xh, xl, xe, n_tok, n_exp, H, logits));
+    FFN_LAUNCH_PDL(FFN_B200_K_ROUTER, st, "router_tc_kernel", router_tc_kernel, g1, 256, kRtSmem, w, xh, xl, xe, n_tok, n_exp, H, logits);
   }
-  FFN_LAUNCH(FFN_B200_K_TOPK, st, "topk_kernel",
-             topk_kernel<<<(n_tok + 1) / 2, 64, 0, st>>>(logits, bias, n_tok, n_exp, top_k, score_fn,
-                                                          n_part, idx, wt));
+  FFN_LAUNCH_PDL(FFN_B200_K_TOPK, st, "topk_kernel", topk_kernel, (n_tok + 1) / 2, 64, 0, logits, bias, n_tok, n_exp, top_k, score_fn, n_part, idx, wt);
   return 0;
 }
 
@@ -1024,6 +1020,7 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__
                                                      int *counts, int *offsets, int *cursor,
                                                      int *vbase, int32_t *pair_tok, int32_t *inv,
                                                      VExp *vexp_nv, VExp *vexp_tn, int *n_vexp) {
+  pdl_enter();
   __shared__ int s_tot[2];
   __shared__ int ws_p[32], ws_n[32], ws_t[32];
   const int tid = threadIdx.x;
@@ -1116,9 +1113,7 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__
 int launch_group(const int32_t *idx, int n_tok, int top_k, int n_exp, int e_begin, int e_end,
                  const ffn_b200_expert *experts, int *ws_int, int32_t *pair_tok, int32_t *inv,
                  VExp *vexp_nv, VExp *vexp_tn, int *n_vexp, cudaStream_t st) {
-  FFN_LAUNCH(FFN_B200_K_GROUP, st, "group_kernel", group_kernel<<<1, 1024, 0, st>>>(idx, n_tok * top_k, top_k, n_exp, e_begin, e_end, experts,
-                                   ws_int, ws_int + n_exp, ws_int + 2 * n_exp,
-                                   ws_int + 3 * n_exp, pair_tok, inv, vexp_nv, vexp_tn, n_vexp));
+  FFN_LAUNCH_PDL(FFN_B200_K_GROUP, st, "group_kernel", group_kernel, 1, 1024, 0, idx, n_tok * top_k, top_k, n_exp, e_begin, e_end, experts, ws_int, ws_int + n_exp, ws_int + 2 * n_exp, ws_int + 3 * n_exp, pair_tok, inv, vexp_nv, vexp_tn, n_vexp);
   return 0;
 }
 
@@ -1134,6 +1129,7 @@ __global__ void __launch_bounds__(1024) combine_kernel(const float *__restrict__
                                                       const ffn_b200_expert *__restrict__ experts,
                                                       const float *residual, float *out, int H,
                                                       const int *err) {
+  pdl_enter();
   const int t = blockIdx.x;
   if (err && *err) {  // an upstream kernel gave up on a wait: make the failure visible
     for (int c = threadIdx.x; c < H; c += blockDim.x) out[(size_t)t * H + c] = __int_as_float(0x7FC00000);
@@ -1200,9 +1196,7 @@ int launch_combine(const float *y, int ld_y, const int32_t *idx, const float *wt
                    const int32_t *inv, int n_tok, int top_k, const ffn_b200_expert *experts,
                    const float *residual, float *out, int H, cudaStream_t st, const int *err) {
   if (n_tok <= 0) return 0;
-  FFN_LAUNCH(FFN_B200_K_COMBINE, st, "combine_kernel",
-             combine_kernel<<<n_tok, std::min(1024, std::max(32, H / 4)), 0, st>>>(
-                 y, ld_y, idx, wt, inv, top_k, experts, residual, out, H, err));
+  FFN_LAUNCH_PDL(FFN_B200_K_COMBINE, st, "combine_kernel", combine_kernel, n_tok, std::min(1024, std::max(32, H / 4)), 0, y, ld_y, idx, wt, inv, top_k, experts, residual, out, H, err);
   return 0;
 }
 

@@ -216,6 +216,7 @@ __device__ __forceinline__ float clamp10f(float u) {
 
 template <int PH>
 __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
+  pdl_enter();
   using L = Layout<PH>;
   constexpr int NMAT = L::NMAT;
   extern __shared__ uint8_t smem_raw[];
@@ -485,6 +486,7 @@ __global__ void __launch_bounds__(kThreadsGG, 1) gemm_kernel(const GemmArgs a) {
 __global__ void __launch_bounds__(1024) chunk_kernel(const int *__restrict__ counts,
                                                      const int *__restrict__ offsets, int e_begin,
                                                      int e_end, Chunk *chunks, int *n_chunks) {
+  pdl_enter();
   __shared__ int warp_sum[32];
   __shared__ int s_base;
   if (threadIdx.x == 0) s_base = 0;
@@ -549,8 +551,7 @@ int launch_grouped_moe(const GroupedArgs &g, cudaStream_t st) {
   Chunk *chunks = reinterpret_cast<Chunk *>(g.chunk_ws);
   int *n_chunks = reinterpret_cast<int *>(g.chunk_ws + gg_chunk_bytes(g.n_pairs, g.e_end - g.e_begin) - 64);
   FFN_CUDA_TRY(cudaMemsetAsync(g.err, 0, sizeof(int), st));
-  FFN_LAUNCH(FFN_B200_K_GROUP, st, "chunk_kernel",
-             chunk_kernel<<<1, 1024, 0, st>>>(g.counts, g.offsets, g.e_begin, g.e_end, chunks, n_chunks));
+  FFN_LAUNCH_PDL(FFN_B200_K_GROUP, st, "chunk_kernel", chunk_kernel, 1, 1024, 0, g.counts, g.offsets, g.e_begin, g.e_end, chunks, n_chunks);
   const int sms = sm_count_of(dev);
   const long long max_chunks = g.n_pairs / 16 + (g.e_end - g.e_begin);
   GemmArgs p{};
@@ -567,8 +568,7 @@ int launch_grouped_moe(const GroupedArgs &g, cudaStream_t st) {
   p.h = g.h;
   p.ld_h = g.inter;
   int grid = (int)std::max(1LL, std::min<long long>(sms, max_chunks * (g.inter / Layout<1>::ROWS)));
-  FFN_LAUNCH(FFN_B200_K_GEMM_GATEUP, st, "grouped gemm_kernel<1>",
-             (gemm_kernel<1><<<grid, kThreadsGG, Layout<1>::SMEM, st>>>(p)));
+  FFN_LAUNCH_PDL(FFN_B200_K_GEMM_GATEUP, st, "grouped gemm_kernel<1>", (gemm_kernel<1>), grid, kThreadsGG, Layout<1>::SMEM, p);
   GemmArgs q = p;
   q.K = g.inter;
   q.rows = g.hidden;
@@ -577,8 +577,7 @@ int launch_grouped_moe(const GroupedArgs &g, cudaStream_t st) {
   q.y = g.y;
   q.ld_y = g.hidden;
   grid = (int)std::max(1LL, std::min<long long>(sms, max_chunks * (g.hidden / Layout<2>::ROWS)));
-  FFN_LAUNCH(FFN_B200_K_GEMM_DOWN, st, "grouped gemm_kernel<2>",
-             (gemm_kernel<2><<<grid, kThreadsGG, Layout<2>::SMEM, st>>>(q)));
+  FFN_LAUNCH_PDL(FFN_B200_K_GEMM_DOWN, st, "grouped gemm_kernel<2>", (gemm_kernel<2>), grid, kThreadsGG, Layout<2>::SMEM, q);
   return 0;
 }
 

@@ -1012,8 +1012,9 @@ int launch_router(const float *w, const float *bias, const float *x, const __hal
 
 // ============================================================ grouping
 // Token->expert groups (flash1017.rs:8088-8099 builds the same groups by a
-// linear scan).  Single CTA: counts per local expert, exclusive scans, pair
-// placement, and slices of <= 8 tokens per expert, listed per weight format.
+// linear scan).  Single CTA: counts per local expert (shared-memory atomics),
+// exclusive scans, pair placement in pair order, and slices of <= 8 tokens per
+// expert, listed per weight format.
 __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__ idx, int n_pairs,
                                                      int top_k, int n_exp, int e_begin, int e_end,
                                                      const ffn_b200_expert *__restrict__ experts,
@@ -1021,14 +1022,48 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__
                                                      int *vbase, int32_t *pair_tok, int32_t *inv,
                                                      VExp *vexp_nv, VExp *vexp_tn, int *n_vexp) {
   pdl_enter();
+  extern __shared__ int g_smem[];
+  int *s_cnt = g_smem;                   // [32 warps][n_exp]: counts, then bases
+  int *s_counts = g_smem + 32 * n_exp;   // [n_exp] pairs per expert
+  int *s_off = s_counts + n_exp;         // [n_exp] first position of each expert
   __shared__ int s_tot[2];
   __shared__ int ws_p[32], ws_n[32], ws_t[32];
-  const int tid = threadIdx.x;
-  for (int e = tid; e < n_exp; e += blockDim.x) { counts[e] = 0; cursor[e] = 0; }
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  // Warp w owns the pair range [w * span, (w + 1) * span) and walks it in
+  // order, 32 pairs per step; lanes holding the same expert find each other
+  // with match.any, the lowest of them updates the warp's count.
+  const int span = (n_pairs + 31) / 32;
+  const int q_lo = wid * span, q_hi = min(n_pairs, q_lo + span);
+  for (int i = tid; i < 32 * n_exp; i += blockDim.x) s_cnt[i] = 0;
   __syncthreads();
-  for (int q = tid; q < n_pairs; q += blockDim.x) {
-    const int e = idx[q];
-    if (e >= e_begin && e < e_end) atomicAdd(&counts[e], 1);
+  constexpr int kU = 8;  // steps whose expert ids are loaded together
+  for (int q0 = q_lo; q0 < q_hi; q0 += 32 * kU) {
+    int ev[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int q = q0 + 32 * u + lane;
+      ev[u] = q < q_hi ? idx[q] : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      if (q0 + 32 * u >= q_hi) break;  // warp-uniform
+      int e = ev[u];
+      if (e < e_begin || e >= e_end) e = -1;
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      if (e >= 0 && (peers & ((1u << lane) - 1u)) == 0) s_cnt[wid * n_exp + e] += __popc(peers);
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  // per expert: warp counts -> exclusive bases in warp order, and the total
+  for (int e = tid; e < n_exp; e += blockDim.x) {
+    int run = 0;
+    for (int w2 = 0; w2 < 32; ++w2) {
+      const int c = s_cnt[w2 * n_exp + e];
+      s_cnt[w2 * n_exp + e] = run;
+      run += c;
+    }
+    s_counts[e] = run;
   }
   __syncthreads();
   // each thread owns a contiguous run of `per` experts
@@ -1037,14 +1072,13 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__
   for (int i = 0; i < per; ++i) {
     const int e = tid * per + i;
     if (e < n_exp) {
-      const int c = counts[e], s = (c + kNTok - 1) / kNTok;
+      const int c = s_counts[e], s = (c + kNTok - 1) / kNTok;
       loc_pairs += c;
       if (experts[e].format == FFN_B200_FMT_NVFP4) loc_nv += s; else loc_tn += s;
     }
   }
   // block-wide exclusive scans of the three per-thread totals
   int inc_p = loc_pairs, inc_n = loc_nv, inc_t = loc_tn;
-  const int lane = tid & 31, wid = tid >> 5;
   for (int o = 1; o < 32; o <<= 1) {
     const int a = __shfl_up_sync(0xffffffffu, inc_p, o);
     const int b = __shfl_up_sync(0xffffffffu, inc_n, o);
@@ -1074,29 +1108,52 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__
   for (int i = 0; i < per; ++i) {
     const int e = tid * per + i;
     if (e < n_exp) {
-      const int c = counts[e], s = (c + kNTok - 1) / kNTok;
+      const int c = s_counts[e], s = (c + kNTok - 1) / kNTok;
+      counts[e] = c;
       offsets[e] = base_p;
+      s_off[e] = base_p;
       base_p += c;
       if (experts[e].format == FFN_B200_FMT_NVFP4) { vbase[e] = base_n; base_n += s; }
       else { vbase[e] = base_t; base_t += s; }
     }
   }
   __syncthreads();
-  // Pair placement.  The order of tokens inside an expert group does not change
-  // any result: each MMA output column depends only on its own token.
-  for (int q = tid; q < n_pairs; q += blockDim.x) {
-    const int e = idx[q];
-    if (e >= e_begin && e < e_end) {
-      const int pos = offsets[e] + atomicAdd(&cursor[e], 1);
-      pair_tok[pos] = q / top_k;
-      inv[q] = pos;
-    } else {
-      inv[q] = -1;
+  // Pair placement in pair order (the reference's linear scan, flash1017.rs:
+  // 8088-8099): inside an expert group, tokens are in token order, so every
+  // run groups the same tokens into the same slices.  A pair's position = the
+  // expert's offset + its expert's pairs in earlier warps' ranges + those
+  // earlier in its own warp's walk.
+  for (int q0 = q_lo; q0 < q_hi; q0 += 32 * kU) {
+    int ev[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int q = q0 + 32 * u + lane;
+      ev[u] = q < q_hi ? idx[q] : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      if (q0 + 32 * u >= q_hi) break;  // warp-uniform
+      const int q = q0 + 32 * u + lane;
+      int e = ev[u];
+      const bool mine = e >= e_begin && e < e_end;
+      if (!mine) e = -1;
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      const int rank = __popc(peers & ((1u << lane) - 1u));
+      if (mine) {
+        const int pos = s_off[e] + s_cnt[wid * n_exp + e] + rank;
+        pair_tok[pos] = q / top_k;
+        inv[q] = pos;
+      } else if (q < q_hi) {
+        inv[q] = -1;
+      }
+      __syncwarp();
+      if (mine && rank == 0) s_cnt[wid * n_exp + e] += __popc(peers);
+      __syncwarp();
     }
   }
   __syncthreads();
   for (int e = tid; e < n_exp; e += blockDim.x) {
-    const int c = counts[e];
+    const int c = s_counts[e];
     VExp *dst = experts[e].format == FFN_B200_FMT_NVFP4 ? vexp_nv : vexp_tn;
     for (int j = 0; j * kNTok < c; ++j) {
       VExp v;
@@ -1113,7 +1170,17 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__
 int launch_group(const int32_t *idx, int n_tok, int top_k, int n_exp, int e_begin, int e_end,
                  const ffn_b200_expert *experts, int *ws_int, int32_t *pair_tok, int32_t *inv,
                  VExp *vexp_nv, VExp *vexp_tn, int *n_vexp, cudaStream_t st) {
-  FFN_LAUNCH_PDL(FFN_B200_K_GROUP, st, "group_kernel", group_kernel, 1, 1024, 0, idx, n_tok * top_k, top_k, n_exp, e_begin, e_end, experts, ws_int, ws_int + n_exp, ws_int + 2 * n_exp, ws_int + 3 * n_exp, pair_tok, inv, vexp_nv, vexp_tn, n_vexp);
+  const size_t smem = (size_t)(32 + 2) * n_exp * sizeof(int);
+  if (smem > 200 * 1024) return fail(FFN_B200_EUNSUP, "group: too many experts");
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  FFN_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(FFN_B200_EUNSUP, "group: device index >= 64");
+  if (!attr_set[dev]) {
+    FFN_CUDA_TRY(cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    attr_set[dev] = true;
+  }
+  FFN_LAUNCH_PDL(FFN_B200_K_GROUP, st, "group_kernel", group_kernel, 1, 1024, smem, idx, n_tok * top_k, top_k, n_exp, e_begin, e_end, experts, ws_int, ws_int + n_exp, ws_int + 2 * n_exp, ws_int + 3 * n_exp, pair_tok, inv, vexp_nv, vexp_tn, n_vexp);
   return 0;
 }
 

@@ -219,6 +219,24 @@ def test_moe_layer_small(oracle, ffn, cuda, score_fn, fmt):
     oracle.assert_close(out, ref, what=f"moe small fmt {fmt} score {score_fn}")
 
 
+def test_moe_layer_deterministic(oracle, ffn, cuda):
+    """Pairs are grouped in token order (the reference's linear scan), so the
+    slices of every expert hold the same tokens on every run and the output is
+    bit-identical across runs: 2400 pairs (three placement chunks), ~150 pairs
+    per expert (many <= 8-token slices)."""
+    import torch
+    E, H, I, T, K = 16, 256, 128, 400, 6
+    experts, wr = _moe_small(ffn, 0, E, H, I, seed=26)
+    layer = ffn.MoeLayer(experts, wr, H, I, top_k=K, path=ffn.PATH_GEMV)
+    x = ffn.gen_normal(ffn.path_key(26, 0, 0, ffn.TAG_X), T * H).view(T, H)
+    outs = [layer.forward(x).clone() for _ in range(3)]
+    torch.cuda.synchronize()
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
+    oe = [oracle_nvfp4_expert(oracle, e) for e in experts]
+    ref, _, _ = oracle.moe_layer(oe, host(wr), host(x), top_k=K)
+    oracle.assert_close(host(outs[0]), ref, what="moe deterministic")
+
+
 def test_moe_layer_mixed_formats(oracle, ffn, cuda):
     """A layer whose experts alternate NVFP4 / ternary+core (tier A / tier B)."""
     E, H, I, T, K = 10, 256, 128, 9, 4

@@ -898,11 +898,19 @@ __global__ void __launch_bounds__(64) topk_kernel(const float *__restrict__ logi
   float cs[kCache], cb[kCache];
   const bool cached = n_exp <= 32 * kCache;
   if (cached) {
+    // all logit (and bias) loads first, so they are in flight together; then
+    // the scores
 #pragma unroll
     for (int j = 0; j < kCache; ++j) {
       const int e = lane + 32 * j;
-      cs[j] = e < n_exp ? score_of(logit(e), score_fn) : 0.f;
-      cb[j] = e < n_exp ? cs[j] + (bias ? bias[e] : 0.0f) : -INFINITY;
+      cs[j] = e < n_exp ? logit(e) : 0.f;
+      cb[j] = e < n_exp && bias ? bias[e] : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < kCache; ++j) {
+      const int e = lane + 32 * j;
+      cs[j] = e < n_exp ? score_of(cs[j], score_fn) : 0.f;
+      cb[j] = e < n_exp ? cs[j] + cb[j] : -INFINITY;
     }
   }
   if (cached && top_k <= 32) {

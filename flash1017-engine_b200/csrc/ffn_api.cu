@@ -139,6 +139,8 @@ static int check_nvfp4(const ffn_b200_nvfp4_mat &m, const char *what) {
   return 0;
 }
 
+static_assert(sizeof(ffn_b200_expert) == 248, "ffn_b200_expert is part of the extension ABI");
+
 static int check_ternary(const ffn_b200_ternary_mat &m, const char *what) {
   if (!m.p || !m.rs) return fail(FFN_B200_EINVAL, std::string(what) + ": null ternary pointer");
   if (!aligned(m.p, 16) || !aligned(m.rs, 4))
@@ -146,6 +148,14 @@ static int check_ternary(const ffn_b200_ternary_mat &m, const char *what) {
   if (m.core_a && (!m.core_b || !m.core_a_sc || !m.core_b_sc || !aligned(m.core_a, 16) ||
                    !aligned(m.core_b, 16)))
     return fail(FFN_B200_EINVAL, std::string(what) + ": incomplete or misaligned rank-16 core");
+  if (m.bs && !aligned(m.bs, 4))
+    return fail(FFN_B200_EINVAL, std::string(what) + ": ternary block scales must be 4-byte aligned");
+  return 0;
+}
+// Block-scaled ternary rows are copied in 4-byte pieces of whole rows of scales.
+static int check_ternary_bs(const ffn_b200_ternary_mat &m, size_t cols, const char *what) {
+  if (m.bs && cols % 256)
+    return fail(FFN_B200_EUNSUP, std::string(what) + ": block-scaled ternary needs cols % 256 == 0");
   return 0;
 }
 
@@ -363,6 +373,7 @@ int ffn_b200_ternary_matvec(size_t rows, size_t cols, size_t seq, const ffn_b200
   if (!m) return fail(FFN_B200_EINVAL, "ternary_matvec: null matrix");
   int rc = check_mat_shape(FFN_B200_FMT_TERNARY, rows, cols, "ternary_matvec");
   if (!rc) rc = check_ternary(*m, "ternary_matvec");
+  if (!rc) rc = check_ternary_bs(*m, cols, "ternary_matvec");
   if (rc) return rc;
   ffn_b200_expert E{};
   E.format = FFN_B200_FMT_TERNARY;
@@ -408,6 +419,7 @@ static int check_expert(const ffn_b200_expert &e, size_t inter, size_t hidden, c
   if ((rc = check_mat_shape(e.format, hidden, inter, what))) return rc;
   for (int i = 0; i < 3; ++i) {
     rc = e.format == FFN_B200_FMT_NVFP4 ? check_nvfp4(e.nv[i], what) : check_ternary(e.tn[i], what);
+    if (!rc && e.format == FFN_B200_FMT_TERNARY) rc = check_ternary_bs(e.tn[i], i == 2 ? inter : hidden, what);
     if (rc) return rc;
   }
   return 0;

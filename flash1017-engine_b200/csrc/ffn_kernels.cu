@@ -248,7 +248,7 @@ __device__ __forceinline__ MatInfo mat_info(const ffn_b200_expert &E, int mm) {
   if (FMT == FFN_B200_FMT_NVFP4) {
     r.w = E.nv[mm].w; r.s = E.nv[mm].s; r.gs = E.nv[mm].gs; r.rs = nullptr; r.core_b = nullptr;
   } else {
-    r.w = E.tn[mm].p; r.s = nullptr; r.gs = 1.0f; r.rs = E.tn[mm].rs;
+    r.w = E.tn[mm].p; r.s = E.tn[mm].bs; r.gs = 1.0f; r.rs = E.tn[mm].rs;
     r.core_b = E.tn[mm].core_a ? E.tn[mm].core_b : nullptr;
   }
   return r;
@@ -340,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a
         const VExp ve = task_slice(a, item / S, WE::ROWS, p_row0);
         p_c = chunk_lo(item);
         p_cend = chunk_hi(item);
-        p_sal = (a.K / 16) % WE::SR == 0;
+        p_sal = WE::sld_of(a.K) % WE::SR == 0;
 #pragma unroll
         for (int mi = 0; mi < NMAT; ++mi) {
           const MatInfo m = task_info<FMT, PHASE, NMAT>(a, ve.expert, mi);
@@ -363,6 +363,13 @@ __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a
     const int item = gw + k * nw, task = item / S;
     int row0;
     const VExp ve = task_slice(a, task, WE::ROWS, row0);
+    // ternary matrices with U8 block scales (bit mi)
+    uint32_t bs_mask = 0;
+    if (FMT == FFN_B200_FMT_TERNARY) {
+#pragma unroll
+      for (int mi = 0; mi < NMAT; ++mi)
+        if (task_info<FMT, PHASE, NMAT>(a, ve.expert, mi).s) bs_mask |= 1u << mi;
+    }
     const bool packed = ve.count <= 4;
     // this lane's MMA column: packed: token g&3, hi terms in columns 0-3 and
     // lo terms in 4-7; otherwise token g with separate hi / lo MMAs
@@ -389,8 +396,8 @@ __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a
       __syncwarp();
       const uint8_t *slot = ring + c_slot * WE::UNIT;
       c_slot = c_slot + 1 == kStages ? 0 : c_slot + 1;
-      if (packed) WE::template compute<true>(slot, a.K, c, xa, xb, acc);
-      else WE::template compute<false>(slot, a.K, c, xa, xb, acc);
+      if (packed) WE::template compute<true>(slot, a.K, c, xa, xb, acc, bs_mask);
+      else WE::template compute<false>(slot, a.K, c, xa, xb, acc, bs_mask);
       __syncwarp();
     }
 

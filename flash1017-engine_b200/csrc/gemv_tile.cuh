@@ -86,13 +86,17 @@ struct WarpEngine {
   static constexpr int CHUNK = FMT == FFN_B200_FMT_NVFP4 ? 128 : 256;  // columns per sub-chunk
   static constexpr int SUB_W = MT * 2 * 32 * 16;                        // weight bytes per sub-chunk
   static constexpr int UNIT_W = SUB * SUB_W;
-  static constexpr int SR = 8 * SUB;                                    // scale bytes per row per unit
-  static constexpr int UNIT_S = FMT == FFN_B200_FMT_NVFP4 ? MT * 16 * SR : 0;
+  // scale bytes per row per unit: NVFP4 E4M3 per 16 columns; ternary U8 block
+  // scales per 64 columns (copied only for matrices that have them)
+  static constexpr int SR = FMT == FFN_B200_FMT_NVFP4 ? 8 * SUB : 4 * SUB;
+  static constexpr int UNIT_S = MT * 16 * SR;
   static constexpr int UNIT = UNIT_W + UNIT_S;                          // [SUB weight blocks][scales]
   static constexpr int RING = STAGES * UNIT;                            // per warp
   static constexpr size_t SMEM = (size_t)kWarps * RING;
 
   static __device__ __forceinline__ int nchunks(int K) { return (K + CHUNK * SUB - 1) / (CHUNK * SUB); }
+  // scale bytes per matrix row
+  static __host__ __device__ __forceinline__ int sld_of(int K) { return FMT == FFN_B200_FMT_NVFP4 ? K / 16 : K / 64; }
 
   // Issue the copies of unit c (columns [c*CHUNK*SUB, +CHUNK*SUB)) of the task
   // whose rows start at row0 into `slot`.  Weights: per sub-chunk and m-tile,
@@ -123,8 +127,11 @@ struct WarpEngine {
           }
       }
     }
-    if constexpr (FMT == FFN_B200_FMT_NVFP4) {
-      const int sld = K / 16;
+    bool any_s = FMT == FFN_B200_FMT_NVFP4;
+#pragma unroll
+    for (int mi = 0; mi < NMAT; ++mi) any_s = any_s || m[mi].s != nullptr;
+    if (any_s) {  // ternary: only the matrices that have block scales are copied
+      const int sld = sld_of(K);
       uint8_t *sbase = slot + UNIT_W;
       constexpr int NROW = MT * 16;
       if (s_al) {
@@ -135,7 +142,7 @@ struct WarpEngine {
           if (rr < NROW && c * SR < sld) {
             const int mt = rr >> 4, mi = mt / R, i = mt % R;
             const int sr = min(row0 + 16 * i + (rr & 15), rows - 1);
-            cp_async_n<SR>(sbase + rr * SR, m[mi].s + (size_t)sr * sld + c * SR);
+            if (m[mi].s) cp_async_n<SR>(sbase + rr * SR, m[mi].s + (size_t)sr * sld + c * SR);
           }
         }
       } else {
@@ -148,7 +155,7 @@ struct WarpEngine {
             const int mt = rr >> 4, mi = mt / R, i = mt % R;
             const int sr = min(row0 + 16 * i + (rr & 15), rows - 1);
             const int sc = c * SR + 4 * q;
-            if (sc < sld) cp_async4(sbase + rr * SR + 4 * q, m[mi].s + (size_t)sr * sld + sc);
+            if (sc < sld && m[mi].s) cp_async4(sbase + rr * SR + 4 * q, m[mi].s + (size_t)sr * sld + sc);
           }
         }
       }
@@ -157,9 +164,10 @@ struct WarpEngine {
 
   template <bool PACKED>
   __device__ static __forceinline__ void compute(const uint8_t *slot, int K, int c, const __half *xa,
-                                                 const __half *xb, float (&acc)[NMAT][R][4]) {
+                                                 const __half *xb, float (&acc)[NMAT][R][4],
+                                                 uint32_t bs_mask = 0) {
 #pragma unroll
-    for (int sb = 0; sb < SUB; ++sb) compute_sub<PACKED>(slot, sb, K, c * SUB + sb, xa, xb, acc);
+    for (int sb = 0; sb < SUB; ++sb) compute_sub<PACKED>(slot, sb, K, c * SUB + sb, xa, xb, acc, bs_mask);
   }
 
   // Accumulate one sub-chunk c from `slot` into acc.  xa/xb: this lane's
@@ -170,7 +178,7 @@ struct WarpEngine {
   // next to the k-steps that use them.
   template <bool PACKED>
   __device__ static void compute_sub(const uint8_t *unit, int sb, int K, int c, const __half *xa,
-                                     const __half *xb, float (&acc)[NMAT][R][4]) {
+                                     const __half *xb, float (&acc)[NMAT][R][4], uint32_t bs_mask) {
     const uint8_t *slot = unit + sb * SUB_W;
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int col0 = c * CHUNK + (FMT == FFN_B200_FMT_NVFP4 ? 32 : 64) * t;
@@ -231,6 +239,19 @@ struct WarpEngine {
         }
       }
     } else {
+      // block scales: lane t's 64 columns of this sub-chunk are one block
+      // (rows g and g+8 of every m-tile); 1 (f16 0x3C00) without block scales
+      uint32_t sba[MT], sbb[MT];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        sba[mt] = sbb[mt] = 0x3C003C00u;
+        if ((bs_mask >> (mt / R)) & 1u) {
+          const uint8_t *sp = unit + UNIT_W + mt * 16 * SR + 4 * sb + t;
+          const __half ha = __ushort2half_rn(sp[g * SR]), hb = __ushort2half_rn(sp[(g + 8) * SR]);
+          sba[mt] = (uint32_t)__half_as_ushort(ha) * 0x10001u;
+          sbb[mt] = (uint32_t)__half_as_ushort(hb) * 0x10001u;
+        }
+      }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const uint4 h0 = xload(xa, 2 * q), h1 = xload(xa, 2 * q + 1);
@@ -243,7 +264,8 @@ struct WarpEngine {
           const int mi = mt / R, i = mt % R;
           const uint32_t wa = q == 0 ? wq[mt][0].x : q == 1 ? wq[mt][0].y : q == 2 ? wq[mt][0].z : wq[mt][0].w;
           const uint32_t wb = q == 0 ? wq[mt][1].x : q == 1 ? wq[mt][1].y : q == 2 ? wq[mt][1].z : wq[mt][1].w;
-          tern_steps<PACKED>(acc[mi][i], wa, wb, bh, bl);
+          if ((bs_mask >> mi) & 1u) tern_steps_scaled<PACKED>(acc[mi][i], wa, wb, sba[mt], sbb[mt], bh, bl);
+          else tern_steps<PACKED>(acc[mi][i], wa, wb, bh, bl);
         }
       }
     }
@@ -258,6 +280,26 @@ struct WarpEngine {
   {                                                                                   \
     const uint32_t a0 = tern_pair<2 * S>(xa), a1 = tern_pair<2 * S>(xb);              \
     const uint32_t a2 = tern_pair<2 * S + 1>(xa), a3 = tern_pair<2 * S + 1>(xb);      \
+    mma_f16(d, a0, a1, a2, a3, bh[2 * S], bh[2 * S + 1]);                             \
+    if (!PACKED) mma_f16(d, a0, a1, a2, a3, bl[2 * S], bl[2 * S + 1]);                \
+  }
+    FFN_TSTEP(0) FFN_TSTEP(1) FFN_TSTEP(2) FFN_TSTEP(3)
+#undef FFN_TSTEP
+  }
+
+  // The same with the rows' U8 block scales (f16x2 broadcasts sa: row g,
+  // sb: row g+8) folded into A: 2 * L * scale <= 510 is exact in f16.
+  template <bool PACKED>
+  __device__ static __forceinline__ void tern_steps_scaled(float (&d)[4], uint32_t xa, uint32_t xb,
+                                                           uint32_t sa, uint32_t sb,
+                                                           const uint32_t (&bh)[8],
+                                                           const uint32_t (&bl)[8]) {
+#define FFN_TSTEP(S)                                                                  \
+  {                                                                                   \
+    const uint32_t a0 = hmul2_u32(tern_pair<2 * S>(xa), sa);                          \
+    const uint32_t a1 = hmul2_u32(tern_pair<2 * S>(xb), sb);                          \
+    const uint32_t a2 = hmul2_u32(tern_pair<2 * S + 1>(xa), sa);                      \
+    const uint32_t a3 = hmul2_u32(tern_pair<2 * S + 1>(xb), sb);                      \
     mma_f16(d, a0, a1, a2, a3, bh[2 * S], bh[2 * S + 1]);                             \
     if (!PACKED) mma_f16(d, a0, a1, a2, a3, bl[2 * S], bl[2 * S + 1]);                \
   }

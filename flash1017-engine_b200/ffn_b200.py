@@ -65,7 +65,8 @@ class NvMat(C.Structure):
 
 class TnMat(C.Structure):
     _fields_ = [("p", C.c_void_p), ("rs", C.c_void_p), ("core_a", C.c_void_p),
-                ("core_a_sc", C.c_void_p), ("core_b", C.c_void_p), ("core_b_sc", C.c_void_p)]
+                ("core_a_sc", C.c_void_p), ("core_b", C.c_void_p), ("core_b_sc", C.c_void_p),
+                ("bs", C.c_void_p)]
 
 
 class Expert(C.Structure):
@@ -83,7 +84,7 @@ class MoeDesc(C.Structure):
                 ("path", C.c_int32)]
 
 
-assert C.sizeof(Expert) == 224, C.sizeof(Expert)
+assert C.sizeof(Expert) == 248, C.sizeof(Expert)
 
 _lib = None
 
@@ -318,16 +319,18 @@ class Nvfp4Matrix:
 
 class TernaryMatrix:
     """Packed ternary matrix p [rows, cols/4] u8 + rs [rows] f32 (+ optional
-    rank-16 core a [16, cols] i8, a_sc [16], b [rows, 16] i8, b_sc [16])."""
+    rank-16 core a [16, cols] i8, a_sc [16], b [rows, 16] i8, b_sc [16]; +
+    optional U8 block scales bs [rows, cols/64])."""
 
-    def __init__(self, p, rs, rows, cols, core=None):
+    def __init__(self, p, rs, rows, cols, core=None, bs=None):
         self.p, self.rs, self.rows, self.cols, self.core = p, rs, rows, cols, core
+        self.bs = bs
 
     def cstruct(self) -> TnMat:
         c = self.core
         return TnMat(_ptr(self.p), _ptr(self.rs), _ptr(c[0]) if c else None,
                      _ptr(c[1]) if c else None, _ptr(c[2]) if c else None,
-                     _ptr(c[3]) if c else None)
+                     _ptr(c[3]) if c else None, _ptr(self.bs) if self.bs is not None else None)
 
     @classmethod
     def generate(cls, k: int, rows: int, cols: int, with_core: bool = True, device="cuda",
@@ -370,6 +373,8 @@ class TernaryMatrix:
 
     def nbytes(self) -> int:
         n = self.p.numel() + 4 * self.rs.numel()
+        if self.bs is not None:
+            n += self.bs.numel()
         if self.core:
             n += self.core[0].numel() + self.core[2].numel() + 128
         return n

@@ -78,6 +78,11 @@ typedef struct ffn_b200_ternary_mat {
     const float *core_a_sc;  /* [16] */
     const int8_t *core_b;    /* [rows, 16]; 16-byte aligned */
     const float *core_b_sc;  /* [16] */
+    /* U8 block scales [rows, cols/64] (one per 64 columns, 4-byte aligned) or
+     * NULL: row r = rs[r] * sum_b bs[r][b] * sum_{64 columns of b} L(code) x
+     * (flash1017.rs:2567-2601, the `.block_scales` tensor the 106 GB
+     * compressor writes, :10783-10787). */
+    const uint8_t *bs;
 } ffn_b200_ternary_mat;
 
 /* One SwiGLU expert: matrix 0 = gate (w1), 1 = up (w3), 2 = down (w2). */

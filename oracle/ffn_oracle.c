@@ -331,14 +331,18 @@ ORC_API void orc_nvfp4_expert(size_t inter, size_t hidden, const uint8_t *const 
 
 /* One ternary SwiGLU expert, F:7548-7561 (with the rank-16 cores applied inside
  * each matvec as F:2623-2625 does).  g, u are pre-multiplied by proj_scale. */
+/* bs: NULL, or 3 pointers (each NULL or U8 block scales [rows, cols/64]) --
+ * the 106 GB format writes block scales for every ternary matrix
+ * (F:10783-10787), read by F:2567-2601. */
 ORC_API void orc_ternary_expert(size_t inter, size_t hidden, const uint8_t *const *p,
                                 const float *const *rs, const orc_core *cores /* 3 or NULL */,
-                                float proj_scale, const float *x, float *y, float *scratch) {
+                                const uint8_t *const *bs, float proj_scale, const float *x,
+                                float *y, float *scratch) {
     float *g = scratch, *u = scratch + inter, *h = scratch + 2 * inter;
-    orc_ternary_matvec(inter, hidden, p[0], rs[0], NULL, cores ? &cores[0] : NULL, x, g);
-    orc_ternary_matvec(inter, hidden, p[1], rs[1], NULL, cores ? &cores[1] : NULL, x, u);
+    orc_ternary_matvec(inter, hidden, p[0], rs[0], bs ? bs[0] : NULL, cores ? &cores[0] : NULL, x, g);
+    orc_ternary_matvec(inter, hidden, p[1], rs[1], bs ? bs[1] : NULL, cores ? &cores[1] : NULL, x, u);
     orc_swiglu(inter, g, u, proj_scale, 1, h);
-    orc_ternary_matvec(hidden, inter, p[2], rs[2], NULL, cores ? &cores[2] : NULL, h, y);
+    orc_ternary_matvec(hidden, inter, p[2], rs[2], bs ? bs[2] : NULL, cores ? &cores[2] : NULL, h, y);
 }
 
 /* ------------------------------------------------------------------------- */

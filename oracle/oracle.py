@@ -60,7 +60,7 @@ def lib() -> C.CDLL:
         L.orc_axpy.argtypes = [sz, f32, vp, vp]
         L.orc_rms_norm.argtypes = [sz, vp, vp, f32, vp]
         L.orc_nvfp4_expert.argtypes = [sz, sz, vp, vp, vp, vp, vp, vp]
-        L.orc_ternary_expert.argtypes = [sz, sz, vp, vp, vp, f32, vp, vp, vp]
+        L.orc_ternary_expert.argtypes = [sz, sz, vp, vp, vp, vp, f32, vp, vp, vp]
         L.orc_route.argtypes = [sz, sz, sz, vp, vp, i32, vp, vp, vp, vp]
         L.orc_combine.argtypes = [sz, sz, sz, vp, vp, vp]
         L.orc_derive.restype = u64
@@ -288,6 +288,7 @@ class TernaryExpert:
     rs: tuple  # row scales
     cores: tuple | None  # (Core, Core, Core) or None
     proj_scale: float = 1.0
+    bs: tuple | None = None  # (w1, w3, w2) U8 block scales [rows, cols/64], or None
 
     def forward(self, x: np.ndarray) -> np.ndarray:
         y = np.zeros(self.hidden, dtype=np.float32)
@@ -297,13 +298,18 @@ class TernaryExpert:
         cores = None
         if self.cores is not None:
             cores = (_Core * 3)(*[c.cstruct() for c in self.cores])
+        bp = None
+        if self.bs is not None:
+            bp = (C.c_void_p * 3)(*[_p(a) for a in self.bs])
         lib().orc_ternary_expert(self.inter, self.hidden, pp, rp,
                                  C.addressof(cores) if cores is not None else None,
-                                 float(self.proj_scale), _p(x), _p(y), _p(scratch))
+                                 bp, float(self.proj_scale), _p(x), _p(y), _p(scratch))
         return y
 
     def nbytes(self) -> int:
         n = sum(a.nbytes for a in self.p) + sum(a.nbytes for a in self.rs)
+        if self.bs is not None:
+            n += sum(a.nbytes for a in self.bs)
         if self.cores is not None:
             for c in self.cores:
                 n += c.a.nbytes + c.b.nbytes + c.a_sc.nbytes + c.b_sc.nbytes

@@ -45,8 +45,24 @@ def oracle_ternary_expert(oracle, e):
     cores = None
     if e.mats[0].core is not None:
         cores = tuple(oracle_core(oracle, m) for m in e.mats)
+    bs = None
+    if e.mats[0].bs is not None:
+        bs = tuple(host(m.bs) for m in e.mats)
     return oracle.TernaryExpert(e.inter, e.hidden, tuple(host(m.p) for m in e.mats),
-                                tuple(host(m.rs) for m in e.mats), cores, e.proj_scale)
+                                tuple(host(m.rs) for m in e.mats), cores, e.proj_scale, bs)
+
+
+def block_scales(rows, cols, seed, cuda):
+    """U8 block scales [rows, cols/64] as the 106 GB compressor writes them:
+    uniform over 0..255, zeros included (the reference skips those blocks)."""
+    rng = np.random.default_rng(seed)
+    return dev(rng.integers(0, 256, size=rows * cols // 64, dtype=np.uint8), cuda)
+
+
+def with_block_scales(e, seed, cuda):
+    for k, m in enumerate(e.mats):
+        m.bs = block_scales(m.rows, m.cols, seed + k, cuda)
+    return e
 
 
 # ---------------------------------------------------------------- generators
@@ -133,6 +149,38 @@ def test_ternary_matvec(oracle, ffn, cuda, rows, cols, seq, with_core):
     oracle.assert_close(y, ref, what=f"ternary {rows}x{cols} seq {seq} core {with_core}")
 
 
+@pytest.mark.parametrize("rows,cols", [(32, 256), (2048, 4096), (4096, 2048), (96, 768)])
+@pytest.mark.parametrize("seq", [1, 4, 8, 11])
+@pytest.mark.parametrize("with_core", [False, True])
+def test_ternary_block_scaled_matvec(oracle, ffn, cuda, rows, cols, seq, with_core):
+    """U8 per-64-column block scales (flash1017.rs:2567-2601)."""
+    m = ffn.TernaryMatrix.generate(ffn.path_key(15, rows, cols, 1), rows, cols, with_core)
+    m.bs = block_scales(rows, cols, rows + cols, cuda)
+    x = ffn.gen_normal(ffn.path_key(15, seq, cols, ffn.TAG_X), seq * cols).view(seq, cols)
+    y = host(m.matvec(x))
+    ref = oracle.ternary_matbatch(host(m.p), host(m.rs), host(x), rows, cols, seq,
+                                  core=oracle_core(oracle, m), bs=host(m.bs))
+    oracle.assert_close(y, ref, what=f"block-scaled ternary {rows}x{cols} seq {seq} core {with_core}")
+
+
+def test_ternary_block_scaled_fixture(oracle, ffn, cuda):
+    """The known-answer block-scale vector (golden, pinned term by term)."""
+    f = json.load(open(os.path.join(GOLD, "known_answers.json")))["ternary"]
+    m = ffn.TernaryMatrix(dev(np.array(f["p"], dtype=np.uint8), cuda),
+                          dev(np.array(f["rs"], dtype=np.float32), cuda), f["rows"], f["cols"],
+                          bs=dev(np.array(f["bs"], dtype=np.uint8), cuda))
+    y = host(m.matvec(dev(bench_x(f["cols"]), cuda)))[0]
+    oracle.assert_close(y, np.array(f["y_bs"], dtype=np.float32), what="block-scaled ternary fixture")
+
+
+def test_ternary_block_scales_need_whole_rows(ffn, cuda):
+    m = ffn.TernaryMatrix.generate(ffn.path_key(16, 32, 320, 1), 32, 320, False)
+    m.bs = block_scales(32, 320, 1, cuda)
+    x = ffn.gen_normal(ffn.path_key(16, 1, 320, ffn.TAG_X), 320).view(1, 320)
+    with pytest.raises(ffn.FfnError):
+        m.matvec(x)
+
+
 def test_ternary_known_answer_fixture(oracle, ffn, cuda):
     f = json.load(open(os.path.join(GOLD, "known_answers.json")))["ternary"]
     m = ffn.TernaryMatrix(dev(np.array(f["p"], dtype=np.uint8), cuda),
@@ -168,6 +216,20 @@ def test_ternary_expert_config1(oracle, ffn, cuda, seq, with_core):
     xs = host(x)
     ref = np.stack([oe.forward(np.ascontiguousarray(xs[t])) for t in range(seq)])
     oracle.assert_close(y, ref, what=f"ternary expert seq {seq} core {with_core}")
+
+
+@pytest.mark.parametrize("seq", [1, 6])
+def test_ternary_block_scaled_expert(oracle, ffn, cuda, seq):
+    """The 106 GB format's expert: ternary + U8 block scales + rank-16 cores."""
+    H, I = 4096, 2048
+    e = with_block_scales(ffn.SwigluExpert.generate(ffn.FMT_TERNARY, 17, 0, 0, I, H, with_core=True,
+                                                    proj_scale=1.0), 170, cuda)
+    x = ffn.gen_normal(ffn.path_key(17, 0, 0, ffn.TAG_X), seq * H).view(seq, H)
+    y = host(e.forward(x))
+    oe = oracle_ternary_expert(oracle, e)
+    xs = host(x)
+    ref = np.stack([oe.forward(np.ascontiguousarray(xs[t])) for t in range(seq)])
+    oracle.assert_close(y, ref, what=f"block-scaled ternary expert seq {seq}")
 
 
 def test_ternary_expert_proj_scale(oracle, ffn, cuda):
@@ -235,6 +297,24 @@ def test_moe_layer_deterministic(oracle, ffn, cuda):
     oe = [oracle_nvfp4_expert(oracle, e) for e in experts]
     ref, _, _ = oracle.moe_layer(oe, host(wr), host(x), top_k=K)
     oracle.assert_close(host(outs[0]), ref, what="moe deterministic")
+
+
+def test_moe_layer_block_scaled_ternary(oracle, ffn, cuda):
+    """A layer of 106 GB-format experts (ternary + block scales + cores) next to
+    NVFP4 experts."""
+    E, H, I, T, K = 12, 512, 256, 21, 6
+    experts = [ffn.SwigluExpert.generate(e % 3 != 0, 27, 0, e, I, H, with_core=True)
+               for e in range(E)]
+    for e, ex in enumerate(experts):
+        if ex.fmt == ffn.FMT_TERNARY:
+            with_block_scales(ex, 270 + 3 * e, cuda)
+    wr = ffn.gen_normal(ffn.path_key(27, 0, 0, ffn.TAG_ROUTER), E * H, 0.02).view(E, H)
+    x = ffn.gen_normal(ffn.path_key(27, 0, 0, ffn.TAG_X), T * H).view(T, H)
+    out = host(ffn.MoeLayer(experts, wr, H, I, top_k=K, score_fn=0).forward(x))
+    oe = [oracle_nvfp4_expert(oracle, e) if e.fmt == 0 else oracle_ternary_expert(oracle, e)
+          for e in experts]
+    ref, _, _ = oracle.moe_layer(oe, host(wr), host(x), top_k=K, score_fn=0)
+    oracle.assert_close(out, ref, what="moe with block-scaled ternary experts")
 
 
 def test_moe_layer_mixed_formats(oracle, ffn, cuda):

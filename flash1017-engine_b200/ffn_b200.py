@@ -38,6 +38,8 @@ EXPORTS = [
     "ffn_b200_profile_enable", "ffn_b200_profile_kinds", "ffn_b200_profile_read",
     "ffn_b200_ep_handle_bytes", "ffn_b200_ep_create", "ffn_b200_ep_connect", "ffn_b200_ep_part",
     "ffn_b200_ep_allreduce", "ffn_b200_ep_error", "ffn_b200_ep_destroy",
+    "ffn_b200_st_open", "ffn_b200_st_close", "ffn_b200_st_count", "ffn_b200_st_name",
+    "ffn_b200_st_find", "ffn_b200_st_expert_bytes", "ffn_b200_st_load_expert",
 ]
 
 # Kernel kinds of ffn_b200_profile_read (FFN_B200_K_*).
@@ -137,6 +139,16 @@ def lib() -> C.CDLL:
         L.ffn_b200_ep_error.argtypes = [vp, C.POINTER(C.c_int)]
         L.ffn_b200_ep_destroy.argtypes = [vp]
         L.ffn_b200_profile_read.argtypes = [i32, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]
+        L.ffn_b200_st_open.argtypes = [C.c_char_p, C.POINTER(vp)]
+        L.ffn_b200_st_close.argtypes = [vp]
+        L.ffn_b200_st_count.argtypes = [vp]
+        L.ffn_b200_st_count.restype = sz
+        L.ffn_b200_st_name.argtypes = [vp, sz]
+        L.ffn_b200_st_name.restype = C.c_char_p
+        L.ffn_b200_st_find.argtypes = [vp, C.c_char_p, C.POINTER(C.c_char_p), C.POINTER(C.c_int64),
+                                       C.POINTER(C.c_int), C.POINTER(vp), C.POINTER(sz)]
+        L.ffn_b200_st_expert_bytes.argtypes = [vp, C.c_char_p, sz, sz, C.POINTER(C.c_int), C.POINTER(sz)]
+        L.ffn_b200_st_load_expert.argtypes = [vp, C.c_char_p, sz, sz, vp, sz, vp, C.POINTER(Expert)]
         _lib = L
     return _lib
 
@@ -431,6 +443,82 @@ class SwigluExpert:
 
     def nbytes(self) -> int:
         return sum(m.nbytes() for m in self.mats)
+
+
+class LoadedExpert(SwigluExpert):
+    """An expert whose tensors were copied from a shard into one device buffer."""
+
+    def __init__(self, desc: "Expert", buf, inter, hidden):
+        super().__init__(desc.format, None, inter, hidden, desc.proj_scale)
+        self.desc, self.buf = desc, buf
+
+    def cstruct(self) -> "Expert":
+        e = Expert.from_buffer_copy(self.desc)
+        e.proj_scale = self.proj_scale
+        return e
+
+    def nbytes(self) -> int:
+        return int(self.buf.numel())
+
+
+class SafetensorsShard:
+    """A .safetensors shard mapped read-only by the library (ffn_b200_st_*,
+    the reference's Flash1017ShardInspector, flash1017.rs:108-235): tensor
+    lookup and routed experts copied straight into HBM."""
+
+    def __init__(self, path):
+        h = C.c_void_p()
+        check(lib().ffn_b200_st_open(os.fsencode(str(path)), C.byref(h)), "st_open")
+        self._h = h
+
+    def close(self):
+        if self._h:
+            lib().ffn_b200_st_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def names(self):
+        L = lib()
+        return [L.ffn_b200_st_name(self._h, i).decode() for i in range(L.ffn_b200_st_count(self._h))]
+
+    def __contains__(self, name) -> bool:
+        return name in set(self.names())
+
+    def tensor(self, name):
+        """(dtype, shape, bytes): a copy of the tensor's bytes from the mapping."""
+        dt, nd, data, nb = C.c_char_p(), C.c_int(), C.c_void_p(), C.c_size_t()
+        shape = (C.c_int64 * 8)()
+        check(lib().ffn_b200_st_find(self._h, name.encode(), C.byref(dt), shape, C.byref(nd),
+                                     C.byref(data), C.byref(nb)), "st_find")
+        return dt.value.decode(), tuple(shape[i] for i in range(nd.value)), C.string_at(data, nb.value)
+
+    def expert_bytes(self, prefix, hidden, inter):
+        fmt, nb = C.c_int(), C.c_size_t()
+        check(lib().ffn_b200_st_expert_bytes(self._h, prefix.encode(), hidden, inter, C.byref(fmt),
+                                             C.byref(nb)), "st_expert_bytes")
+        return fmt.value, nb.value
+
+    def load_expert(self, prefix, hidden, inter, device="cuda", stream=None) -> LoadedExpert:
+        torch = _torch()
+        _, nb = self.expert_bytes(prefix, hidden, inter)
+        buf = torch.empty(nb + 256, dtype=torch.uint8, device=device)
+        off = (-buf.data_ptr()) % 256
+        view = buf[off:off + nb]
+        e = Expert()
+        check(lib().ffn_b200_st_load_expert(self._h, prefix.encode(), hidden, inter, _ptr(view), nb,
+                                            _stream(stream), C.byref(e)), "st_load_expert")
+        ex = LoadedExpert(e, buf, inter, hidden)
+        return ex
+
+    def load_layer(self, layer, n_experts, hidden, inter, device="cuda", stream=None):
+        """The routed experts layers.<layer>.ffn.experts.<e> (flash1017.rs:5219-5262)."""
+        return [self.load_expert(f"layers.{layer}.ffn.experts.{e}", hidden, inter, device, stream)
+                for e in range(n_experts)]
 
 
 def gen_normal(k: int, n: int, stdev: float = 1.0, device="cuda", stream=None):

@@ -262,6 +262,37 @@ FFN_B200_EXPORT int ffn_b200_ep_allreduce(ffn_b200_ep *ep, size_t n_tok, const f
 FFN_B200_EXPORT int ffn_b200_ep_error(ffn_b200_ep *ep, int *flag);
 FFN_B200_EXPORT int ffn_b200_ep_destroy(ffn_b200_ep *ep);
 
+/* ------------------------------------------------ safetensors expert loader
+ * Replaces the reference's shard mapping and tensor lookup
+ * (Flash1017ShardInspector::open / get_tensor_data, flash1017.rs:108-235)
+ * and its per-expert matrix constructors (CachedNvfp4Mat::from_shard
+ * :2295-2309, CachedTernary158Mat::from_shard :2495-2525,
+ * CachedRank16Q8Core::from_shard :2415-2440) for the routed experts of a
+ * layer (names as flash1017.rs:5219-5262 builds them, e.g. prefix
+ * "layers.3.ffn.experts.17"; matrices <prefix>.w1 gate, .w3 up, .w2 down).
+ * The shard is mapped read-only; st_load_expert copies one expert's tensors
+ * into a caller-owned device buffer (st_expert_bytes of it, 256-byte aligned)
+ * on `stream` and fills *e with device pointers into it.  NVFP4 when
+ * <prefix>.w1.weight exists (weight u8 [rows, cols/2], weight_scale
+ * [rows, cols/16], weight_scale_2 f32 scalar -> gs), else ternary
+ * (packed_ternary [rows, cols/4], row_scales f32 [rows], optional
+ * block_scales u8 [rows, cols/64], optional rank-16 core).  Shapes are checked
+ * against inter x hidden; proj_scale is set to 1. */
+typedef struct ffn_b200_st ffn_b200_st;
+FFN_B200_EXPORT int ffn_b200_st_open(const char *path, ffn_b200_st **out);
+FFN_B200_EXPORT int ffn_b200_st_close(ffn_b200_st *st);
+FFN_B200_EXPORT size_t ffn_b200_st_count(const ffn_b200_st *st);
+FFN_B200_EXPORT const char *ffn_b200_st_name(const ffn_b200_st *st, size_t i);
+/* dtype string ("U8", "F32", "F8_E4M3", ...), shape (up to 8 dims), bytes in the
+ * mapping; FFN_B200_EINVAL when the tensor is absent. */
+FFN_B200_EXPORT int ffn_b200_st_find(const ffn_b200_st *st, const char *name, const char **dtype,
+                                     int64_t *shape, int *ndim, const void **data, size_t *nbytes);
+FFN_B200_EXPORT int ffn_b200_st_expert_bytes(const ffn_b200_st *st, const char *prefix, size_t hidden,
+                                             size_t inter, int *format, size_t *bytes);
+FFN_B200_EXPORT int ffn_b200_st_load_expert(const ffn_b200_st *st, const char *prefix, size_t hidden,
+                                            size_t inter, void *dev, size_t dev_bytes, void *stream,
+                                            ffn_b200_expert *e);
+
 /* -------------------------------------------- reference-ABI support hooks
  * Host-side x_all buffer for gx10_rust_*_mlp_batch (the reference stages it
  * through the shared-expert call, flash1017.rs:8170-8186). */

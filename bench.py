@@ -53,6 +53,15 @@ UNIT = "tokens/s"
 EXPERT_BYTES = lambda H, I: 3 * (I * H // 2 + I * H // 16)  # noqa: E731
 
 
+def tern106_mat_bytes(rows, cols):
+    """One matrix of the 106 GB format: codes, row scales, U8 block scales,
+    rank-16 core (B rows x 16, A 16 x cols, two 16-float scale vectors)."""
+    return rows * cols // 4 + 4 * rows + rows * cols // 64 + 16 * rows + 16 * cols + 128
+
+
+METRIC106 = "MoE expert-FFN tokens/s (40-layer 106 GB-format ternary top-6/384 decode stack)"
+
+
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -72,6 +81,9 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="CPU-baseline sample length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--format", choices=["nvfp4", "ternary106"], default="nvfp4",
+                    help="config4 expert format: NVFP4 (BASELINE) or the reference compressor's "
+                         "106 GB format (ternary + U8 block-64 scales + rank-16 Q8 core)")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="per-layer sum over ranks: NVLink peer exchange or NCCL all-reduce")
     return ap.parse_args()
@@ -81,7 +93,9 @@ METRIC3 = "MoE expert-FFN prefill tokens/s (one NVFP4 top-6/384 layer, 8192 toke
 
 
 def metric_of(a):
-    return METRIC3 if a.workload == "config3" else METRIC
+    if a.workload == "config3":
+        return METRIC3
+    return METRIC106 if a.format == "ternary106" else METRIC
 
 
 def base_config(a, world, resident):
@@ -95,9 +109,12 @@ def base_config(a, world, resident):
             "parallelism": f"ep{world}",
             "l2": "no flush: each step streams the layer's 5.4 GB of expert weights (> 126 MB L2)",
         }
+    wl = ("config4: 40-layer NVFP4 MoE-FFN stack, 256-token decode, top-6 of 384, expert-parallel"
+          if a.format == "nvfp4" else
+          "config4 shape with the 106 GB format: 40-layer ternary (U8 block-64 scales, rank-16 Q8 "
+          "core) MoE-FFN stack, 256-token decode, top-6 of 384, expert-parallel")
     return {
-        "workload": "config4: 40-layer NVFP4 MoE-FFN stack, 256-token decode, top-6 of 384, "
-                    "expert-parallel",
+        "workload": wl,
         "hidden": a.hidden, "inter": a.inter, "experts": a.experts, "top_k": a.top_k,
         "layers": a.layers, "tokens": a.tokens, "seed": a.seed,
         "router": "fp32 weights, tensor-core split-f16 (about fp32 accurate), sigmoid top-k",
@@ -276,11 +293,13 @@ def run_ours(a):
     H, I, E, K, T, L = a.hidden, a.inter, a.experts, a.top_k, a.tokens, a.layers
     e_lo, e_hi = expert_range(rank, world, E)
     e_loc = e_hi - e_lo
-    ebytes = EXPERT_BYTES(H, I)
+    tern = a.format == "ternary106"
+    fk = "ternary" if tern else "nvfp4"  # kernel kinds of the expert phases
+    ebytes = (2 * tern106_mat_bytes(I, H) + tern106_mat_bytes(H, I)) if tern else EXPERT_BYTES(H, I)
     layer_bytes = e_loc * ebytes
     free, _ = torch.cuda.mem_get_info(dev)
     reserve = 4 << 30
-    resident = max(1, min(L, (free - reserve - L * E * H * 4) // layer_bytes))
+    resident = max(1, min(L, (free - reserve - L * E * H * 4) // (layer_bytes + 512 * e_loc)))
     if a.max_resident:
         resident = min(resident, a.max_resident)
     if world > 1:  # every rank streams the same layer schedule
@@ -292,23 +311,48 @@ def run_ours(a):
     n1, n1s = I * H // 2, I * H // 16
     tables = []
     buffers = []
+    gen = torch.Generator(device=dev)
     for lay in range(resident):
-        buf = torch.empty(layer_bytes, dtype=torch.uint8, device=dev)
+        buf = torch.empty(layer_bytes + 512 * e_loc, dtype=torch.uint8, device=dev)
         buffers.append(buf)
         experts = [None] * E
         off = 0
+
+        def take(n, align=16):
+            nonlocal off
+            off = (off + align - 1) // align * align
+            t = buf.narrow(0, off, n)
+            off += n
+            return t
+
         for j in range(e_loc):
             e = e_lo + j
             mats = []
             for tag, (r, c) in zip((F.TAG_W1, F.TAG_W3, F.TAG_W2), ((I, H), (I, H), (H, I))):
-                w = buf.narrow(0, off, n1)
-                s = buf.narrow(0, off + n1, n1s)
-                off += n1 + n1s
-                F.check(F.lib().ffn_b200_gen_nvfp4(F.path_key(a.seed, lay, e, tag), r, c,
-                                                   w.data_ptr(), s.data_ptr(), F._stream()),
-                        "gen_nvfp4")
-                mats.append(F.Nvfp4Matrix(w, s, 1.0, r, c))
-            experts[e] = F.SwigluExpert(F.FMT_NVFP4, mats, I, H)
+                k = F.path_key(a.seed, lay, e, tag)
+                if not tern:
+                    w = buf.narrow(0, off, n1)
+                    s = buf.narrow(0, off + n1, n1s)
+                    off += n1 + n1s
+                    F.check(F.lib().ffn_b200_gen_nvfp4(k, r, c, w.data_ptr(), s.data_ptr(),
+                                                       F._stream()), "gen_nvfp4")
+                    mats.append(F.Nvfp4Matrix(w, s, 1.0, r, c))
+                    continue
+                p = take(r * c // 4)
+                rs = take(4 * r).view(torch.float32)
+                bs = take(r * c // 64, 4)
+                ca, cb = take(16 * c).view(torch.int8), take(16 * r).view(torch.int8)
+                cas, cbs = take(64).view(torch.float32), take(64).view(torch.float32)
+                F.check(F.lib().ffn_b200_gen_ternary(k, r, c, p.data_ptr(), rs.data_ptr(),
+                                                     F._stream()), "gen_ternary")
+                F.check(F.lib().ffn_b200_gen_core(k, r, c, ca.data_ptr(), cas.data_ptr(),
+                                                  cb.data_ptr(), cbs.data_ptr(), F._stream()),
+                        "gen_core")
+                gen.manual_seed(k & 0x7FFFFFFFFFFFFFFF)
+                bs.copy_(torch.randint(0, 256, (r * c // 64,), dtype=torch.uint8, device=dev,
+                                       generator=gen))
+                mats.append(F.TernaryMatrix(p, rs, r, c, core=(ca, cas, cb, cbs), bs=bs))
+            experts[e] = F.SwigluExpert(F.FMT_TERNARY if tern else F.FMT_NVFP4, mats, I, H)
         tables.append((experts, F.expert_table(experts, dev)))
     routers = [F.gen_normal(F.path_key(a.seed, lay, 0, F.TAG_ROUTER), E * H, 0.02).view(E, H)
                for lay in range(L)]
@@ -361,7 +405,10 @@ def run_ours(a):
     for lay in range(L):
         ids = torch.unique(topk[lay])
         u_loc.append(int(((ids >= e_lo) & (ids < e_lo + e_loc)).sum().item()))
-    gateup_bytes_step = sum(u * 2 * (n1 + n1s) for u in u_loc)
+    # gate/up kernel bytes per expert hit: NVFP4 weights + scales, or ternary
+    # codes + row scales + block scales + the core's B rows (A is read by corez)
+    gu_hit = 2 * (I * H // 4 + 4 * I + I * H // 64 + 16 * I) if tern else 2 * (n1 + n1s)
+    gateup_bytes_step = sum(u * gu_hit for u in u_loc)
     weight_bytes_step = sum(u * ebytes for u in u_loc)
 
     for _ in range(a.warmup):
@@ -388,7 +435,7 @@ def run_ours(a):
         dist.barrier()
     # live roofline: event pairs only around the expert GEMV kernels (fewer
     # event records between the kernels of the timed region)
-    F.profile_kinds(["gateup_nvfp4", "down_nvfp4"])
+    F.profile_kinds([f"gateup_{fk}", f"down_{fk}"])
     F.profile_enable(True)
     n0 = F.launch_count()
     t_start = torch.cuda.Event(enable_timing=True)
@@ -423,7 +470,7 @@ def run_ours(a):
     # pairs as in the timed region above, so the two numbers compare)
     x_host = x0.cpu().pin_memory()
     out_host = torch.empty_like(x_host).pin_memory()
-    F.profile_kinds(["gateup_nvfp4", "down_nvfp4"])
+    F.profile_kinds([f"gateup_{fk}", f"down_{fk}"])
     F.profile_enable(True)
     for i in range(a.warmup + a.steps):
         if i == a.warmup:
@@ -446,12 +493,12 @@ def run_ours(a):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e = T * a.steps / (float(te.item()) * 1e-3)
 
-    # ---- roofline of the dominant kernel (gate/up NVFP4 GEMV), live event timing
-    gu_ms, gu_n = prof.get("gateup_nvfp4", (0.0, 0))
+    # ---- roofline of the dominant kernel (gate/up GEMV), live event timing
+    gu_ms, gu_n = prof.get(f"gateup_{fk}", (0.0, 0))
     peaks = _peaks()
     achieved = gateup_bytes_step * a.steps / (gu_ms * 1e-3) / 1e9 if gu_ms else None
-    traffic = _traffic_per_launch(gateup_bytes_step / L)
-    roof = {"bound": "hbm", "kernel": "phase_kernel<NVFP4, gate+up>",
+    traffic = None if tern else _traffic_per_launch(gateup_bytes_step / L)
+    roof = {"bound": "hbm", "kernel": f"phase_kernel<{'TERNARY' if tern else 'NVFP4'}, gate+up>",
             "achieved": achieved, "peak": peaks[0], "unit": "GB/s",
             "frac": achieved / peaks[0] if achieved else None, "traffic": traffic,
             "peak_source": peaks[1],
@@ -461,7 +508,7 @@ def run_ours(a):
                for k, v in breakdown.items()}
 
     cpu = None
-    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+    if rank == 0 and world == 1 and not a.no_cpu_baseline and not tern:
         threads = os.cpu_count() or 1
         sample = CpuSample(a, threads)
         cv, dt, n = sample.measure(a.cpu_seconds)
@@ -474,10 +521,12 @@ def run_ours(a):
         cfg["experts_hit_per_layer_rank0"] = u_loc
         cfg["weight_bytes_per_step_rank0"] = weight_bytes_step
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "metric": metric_of(a), "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None,
-            "dtype": "nvfp4 weights x f16x2 split activations, f32 accumulate",
+            "dtype": ("ternary (block-64 U8 scales, rank-16 Q8 core) weights x f16x2 split "
+                      "activations, f32 accumulate" if tern else
+                      "nvfp4 weights x f16x2 split activations, f32 accumulate"),
             "data": "synthetic (seeded random-init weights and N(0,1) hidden states)",
             "config": cfg,
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": T * H * 4,

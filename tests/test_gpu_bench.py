@@ -16,7 +16,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     ["--workload", "config4", "--layers", "2", "--steps", "3", "--warmup", "3", "--no-cpu-baseline"],
     ["--workload", "config3", "--experts", "96", "--tokens", "2048", "--steps", "2", "--warmup", "3",
      "--no-cpu-baseline"],
-], ids=["config4", "config3"])
+    ["--workload", "config4", "--format", "ternary106", "--layers", "2", "--steps", "3", "--warmup", "3"],
+], ids=["config4", "config3", "config4-ternary106"])
 def test_bench_line(args):
     r = subprocess.run([sys.executable, "bench.py", *args], cwd=ROOT, capture_output=True, text=True,
                        timeout=900)

@@ -66,6 +66,51 @@ ORC_API float orc_e4m3_to_f32(uint8_t b) {
 
 ORC_API float orc_e2m1_to_f32(uint8_t nibble) { return E2M1_LUT[nibble & 15u]; }
 
+/* F:1049-1057 f8_e8m0_to_f32: 0xFF -> NaN, 0 -> 2^-127 (f32 bits 0x00400000),
+ * else 2^(b - 127) (bits b << 23). */
+ORC_API float orc_e8m0_to_f32(uint8_t b) {
+    if (b == 0xFFu) return bits_f32(0x7FC00000u);
+    if (b == 0u) return bits_f32(0x00400000u);
+    return bits_f32((uint32_t)b << 23);
+}
+
+/* F:2717-2744 -- one row of CachedMxfp4Mat::matvec: E2M1 pairs, E8M0 scale
+ * per 32 columns, no global scale. */
+static float mxfp4_row(const uint8_t *w_row, const uint8_t *s_row, size_t cols, const float *x) {
+    size_t scale_cols = cols / 32;
+    float acc = 0.0f;
+    for (size_t g = 0; g < scale_cols; ++g) {
+        float sc = orc_e8m0_to_f32(s_row[g]);
+        size_t b_off = g * 16, x_off = g * 32;
+        float b_sum = 0.0f;
+        for (size_t k = 0; k < 16; ++k) {
+            uint8_t b = w_row[b_off + k];
+            float w0 = E2M1_LUT[b & 0x0F];
+            float w1 = E2M1_LUT[b >> 4];
+            b_sum += w0 * x[x_off + k * 2] + w1 * x[x_off + k * 2 + 1];
+        }
+        acc += b_sum * sc;
+    }
+    return acc;
+}
+
+/* F:1960-1982 -- row r of CachedMxfp8Mat::matvec: E4M3 values [rows, cols],
+ * E8M0 scales per 32 x 32 block ([ceil(rows/32)... ] row (r/32), column block c/32). */
+static float mxfp8_row(const uint8_t *w, const uint8_t *s, size_t r, size_t cols, const float *x) {
+    size_t scale_cols = (cols + 31) / 32;
+    const uint8_t *w_row = w + r * cols;
+    size_t sc_row_off = (r / 32) * scale_cols;
+    float acc = 0.0f;
+    for (size_t bc = 0; bc < scale_cols; ++bc) {
+        float sc = orc_e8m0_to_f32(s[sc_row_off + bc]);
+        size_t c_start = bc * 32, c_end = c_start + 32 < cols ? c_start + 32 : cols;
+        float b_sum = 0.0f;
+        for (size_t c = c_start; c < c_end; ++c) b_sum += orc_e4m3_to_f32(w_row[c]) * x[c];
+        acc += b_sum * sc;
+    }
+    return acc;
+}
+
 /* ------------------------------------------------------------------------- */
 /* NVFP4 matrix  (F:2282-2391, CachedNvfp4Mat)                                */
 /* ------------------------------------------------------------------------- */
@@ -138,7 +183,7 @@ static float ternary_row_bs(const uint8_t *row_b, const uint8_t *bs_row, size_t 
 /* ------------------------------------------------------------------------- */
 
 typedef struct {
-    int kind; /* 0 nvfp4, 1 ternary, 2 ternary+block scales */
+    int kind; /* 0 nvfp4, 1 ternary, 2 ternary+block scales, 3 mxfp4, 4 mxfp8 */
     size_t rows, cols;
     const uint8_t *w, *s;
     const float *rs;
@@ -155,6 +200,10 @@ static void run_rows(row_job *j) {
                                   j->cols, j->gs, j->x);
         } else if (j->kind == 1) {
             j->out[r] = ternary_row(j->w + r * (j->cols / 4), j->cols / 4, j->rs[r], j->x);
+        } else if (j->kind == 3) {
+            j->out[r] = mxfp4_row(j->w + r * (j->cols / 2), j->s + r * (j->cols / 32), j->cols, j->x);
+        } else if (j->kind == 4) {
+            j->out[r] = mxfp8_row(j->w, j->s, r, j->cols, j->x);
         } else {
             j->out[r] = ternary_row_bs(j->w + r * (j->cols / 4), j->s + r * (j->cols / 64),
                                        j->cols, j->rs[r], j->x);
@@ -201,6 +250,21 @@ static void par_rows(row_job base) {
 ORC_API void orc_nvfp4_matvec(size_t rows, size_t cols, const uint8_t *w, const uint8_t *s,
                               float gs, const float *x, float *out) {
     row_job j = {0, rows, cols, w, s, NULL, gs, x, out, 0, 0};
+    par_rows(j);
+}
+
+/* F:2700-2746 CachedMxfp4Mat::matvec (CPU branch): w [rows, cols/2], s E8M0 [rows, cols/32]. */
+ORC_API void orc_mxfp4_matvec(size_t rows, size_t cols, const uint8_t *w, const uint8_t *s,
+                              const float *x, float *out) {
+    row_job j = {3, rows, cols, w, s, NULL, 1.0f, x, out, 0, 0};
+    par_rows(j);
+}
+
+/* F:1940-1984 CachedMxfp8Mat::matvec (CPU branch): w E4M3 [rows, cols], s E8M0
+ * [ceil(rows/32), ceil(cols/32)]. */
+ORC_API void orc_mxfp8_matvec(size_t rows, size_t cols, const uint8_t *w, const uint8_t *s,
+                              const float *x, float *out) {
+    row_job j = {4, rows, cols, w, s, NULL, 1.0f, x, out, 0, 0};
     par_rows(j);
 }
 
@@ -327,6 +391,20 @@ ORC_API void orc_nvfp4_expert(size_t inter, size_t hidden, const uint8_t *const 
     orc_nvfp4_matvec(inter, hidden, w[1], s[1], gs[1], x, u);
     orc_swiglu(inter, g, u, 1.0f, 0, h);
     orc_nvfp4_matvec(hidden, inter, w[2], s[2], gs[2], h, y);
+}
+
+/* One MXFP4 (F:9103-9158, MTP routed experts) or MXFP8 (F:9132-9142, shared
+ * expert) SwiGLU expert: the NVFP4 expert's arithmetic on the other matvecs.
+ * fmt 3 = MXFP4, 4 = MXFP8 (row_job kinds). */
+ORC_API void orc_mx_expert(int fmt, size_t inter, size_t hidden, const uint8_t *const *w,
+                           const uint8_t *const *s, const float *x, float *y, float *scratch) {
+    float *g = scratch, *u = scratch + inter, *h = scratch + 2 * inter;
+    void (*mv)(size_t, size_t, const uint8_t *, const uint8_t *, const float *, float *) =
+        fmt == 3 ? orc_mxfp4_matvec : orc_mxfp8_matvec;
+    mv(inter, hidden, w[0], s[0], x, g);
+    mv(inter, hidden, w[1], s[1], x, u);
+    orc_swiglu(inter, g, u, 1.0f, 0, h);
+    mv(hidden, inter, w[2], s[2], h, y);
 }
 
 /* One ternary SwiGLU expert, F:7548-7561 (with the rank-16 cores applied inside

@@ -62,6 +62,11 @@ def lib() -> C.CDLL:
         L.orc_nvfp4_expert.argtypes = [sz, sz, vp, vp, vp, vp, vp, vp]
         L.orc_ternary_expert.argtypes = [sz, sz, vp, vp, vp, vp, f32, vp, vp, vp]
         L.orc_route.argtypes = [sz, sz, sz, vp, vp, i32, vp, vp, vp, vp]
+        L.orc_e8m0_to_f32.restype = f32
+        L.orc_e8m0_to_f32.argtypes = [C.c_uint8]
+        L.orc_mxfp4_matvec.argtypes = [sz, sz, vp, vp, vp, vp]
+        L.orc_mxfp8_matvec.argtypes = [sz, sz, vp, vp, vp, vp]
+        L.orc_mx_expert.argtypes = [i32, sz, sz, vp, vp, vp, vp, vp]
         L.orc_combine.argtypes = [sz, sz, sz, vp, vp, vp]
         L.orc_derive.restype = u64
         L.orc_derive.argtypes = [u64, u64]
@@ -99,6 +104,24 @@ def f32_to_e4m3(v: float) -> int:
 
 def e4m3_table() -> np.ndarray:
     return np.array([e4m3_to_f32(b) for b in range(256)], dtype=np.float32)
+
+
+def e8m0_to_f32(b: int) -> float:
+    return float(lib().orc_e8m0_to_f32(b))
+
+
+def mxfp4_matvec(w, s, x, rows, cols) -> np.ndarray:
+    """F:2700-2746: E2M1 [rows, cols/2] with E8M0 scales per 32 columns."""
+    out = np.empty(rows, dtype=np.float32)
+    lib().orc_mxfp4_matvec(rows, cols, _p(w), _p(s), _p(np.ascontiguousarray(x, np.float32)), _p(out))
+    return out
+
+
+def mxfp8_matvec(w, s, x, rows, cols) -> np.ndarray:
+    """F:1940-1984: E4M3 [rows, cols] with E8M0 scales per 32 x 32 block."""
+    out = np.empty(rows, dtype=np.float32)
+    lib().orc_mxfp8_matvec(rows, cols, _p(w), _p(s), _p(np.ascontiguousarray(x, np.float32)), _p(out))
+    return out
 
 
 def dequant_nvfp4(w: np.ndarray, s: np.ndarray, gs: float, rows: int, cols: int) -> np.ndarray:
@@ -278,6 +301,27 @@ class Nvfp4Expert:
 
     def nbytes(self) -> int:
         return sum(a.nbytes for a in self.w) + sum(a.nbytes for a in self.s) + 12
+
+
+@dataclass
+class MxExpert:
+    """gate (w1), up (w3), down (w2) of an MXFP4 (fmt 3: the MTP routed
+    experts, F:9103-9158) or MXFP8 (fmt 4: the shared expert, F:9132-9142)
+    SwiGLU expert."""
+    fmt: int
+    inter: int
+    hidden: int
+    w: tuple
+    s: tuple
+
+    def forward(self, x: np.ndarray) -> np.ndarray:
+        y = np.zeros(self.hidden, dtype=np.float32)
+        scratch = np.zeros(3 * self.inter, dtype=np.float32)
+        wp = (C.c_void_p * 3)(*[_p(a) for a in self.w])
+        sp = (C.c_void_p * 3)(*[_p(a) for a in self.s])
+        lib().orc_mx_expert(self.fmt, self.inter, self.hidden, wp, sp,
+                            _p(np.ascontiguousarray(x, np.float32)), _p(y), _p(scratch))
+        return y
 
 
 @dataclass

@@ -8,7 +8,8 @@ it, since the Rust reference itself cannot be executed here:
   * known_answers.json -- outputs of pure-Python float32 restatements of the
     reference loops (terox27/Flash1017-Engine, crates/flash-core/src/
     flash1017.rs: NVFP4 :2331-2357, ternary :2602-2621 and :2567-2601, rank-16
-    :2446-2472, router :7280-7376), evaluated term by term with numpy float32
+    :2446-2472, router :7280-7376, MXFP4 :2717-2744, MXFP8 :1960-1982 with the
+    E8M0 decode :1049-1057), evaluated term by term with numpy float32
     scalars in the reference's order, on deterministic inputs.  The NVFP4 input
     is the reference's own test fixture (flash1017.rs:10974-10990: nibbles
     (i*7+3)%16 / (i*13+5)%16, scales alternating 0x38/0x3C, global scale 0.02);
@@ -46,6 +47,47 @@ def e4m3(b: int) -> F:
         bits = struct.unpack("<I", struct.pack("<f", sub))[0]
         return F(struct.unpack("<f", struct.pack("<I", sign | bits))[0])
     return F(struct.unpack("<f", struct.pack("<I", sign | ((em + 960) << 20)))[0])
+
+
+def e8m0(b: int) -> F:
+    """flash1017.rs:1049-1057 restated: 0xFF NaN, 0 -> bits 0x00400000, else b << 23."""
+    if b == 0xFF:
+        return F("nan")
+    bits = 0x00400000 if b == 0 else (b << 23)
+    return F(struct.unpack("<f", struct.pack("<I", bits))[0])
+
+
+def mxfp4_matvec_py(w, s, x, rows, cols):
+    out = []
+    spr = cols // 32
+    for r in range(rows):
+        wr = w[r * cols // 2:(r + 1) * cols // 2]
+        acc = F(0)
+        for g in range(spr):
+            sc = e8m0(int(s[r * spr + g]))
+            bsum = F(0)
+            for k in range(16):
+                b = int(wr[g * 16 + k])
+                w0, w1 = F(LUT4[b & 15]), F(LUT4[b >> 4])
+                bsum = F(bsum + F(F(w0 * x[g * 32 + 2 * k]) + F(w1 * x[g * 32 + 2 * k + 1])))
+            acc = F(acc + F(bsum * sc))
+        out.append(acc)
+    return np.array(out, dtype=np.float32)
+
+
+def mxfp8_matvec_py(w, s, x, rows, cols):
+    out = []
+    scols = (cols + 31) // 32
+    for r in range(rows):
+        acc = F(0)
+        for bc in range(scols):
+            sc = e8m0(int(s[(r // 32) * scols + bc]))
+            bsum = F(0)
+            for c in range(bc * 32, min(bc * 32 + 32, cols)):
+                bsum = F(bsum + F(e4m3(int(w[r * cols + c])) * x[c]))
+            acc = F(acc + F(bsum * sc))
+        out.append(acc)
+    return np.array(out, dtype=np.float32)
 
 
 def nvfp4_matvec_py(w, s, gs, x, rows, cols):
@@ -176,6 +218,21 @@ def main():
                      "y": ternary_matvec_py(p, rs, xt, rows3, cols3).tolist(),
                      "bs": bs.tolist(),
                      "y_bs": ternary_matvec_py(p, rs, xt, rows3, cols3, bs).tolist()}
+    # MXFP4: all 16 E2M1 codes, E8M0 scales around 2^0 (120..134)
+    rows4, cols4 = 16, 256
+    w4 = np.array([(i * 53 + 7) & 0xFF for i in range(rows4 * cols4 // 2)], dtype=np.uint8)
+    s4 = np.array([120 + (i * 5) % 15 for i in range(rows4 * cols4 // 32)], dtype=np.uint8)
+    ka["mxfp4"] = {"rows": rows4, "cols": cols4, "w": w4.tolist(), "s": s4.tolist(),
+                   "y": mxfp4_matvec_py(w4, s4, bench_x(cols4), rows4, cols4).tolist()}
+    # MXFP8: E4M3 codes (NaN codes 0x7F / 0xFF avoided), 32 x 32 block scales
+    rows5, cols5 = 64, 96
+    w5 = np.array([(i * 29 + 3) & 0xFF for i in range(rows5 * cols5)], dtype=np.uint8)
+    w5[(w5 & 0x7F) == 0x7F] = 0x3C
+    s5 = np.array([118 + (i * 7) % 13 for i in range(((rows5 + 31) // 32) * ((cols5 + 31) // 32))],
+                  dtype=np.uint8)
+    ka["mxfp8"] = {"rows": rows5, "cols": cols5, "w": w5.tolist(), "s": s5.tolist(),
+                   "y": mxfp8_matvec_py(w5, s5, bench_x(cols5), rows5, cols5).tolist()}
+    ka["e8m0"] = {"bits": [int(np.float32(e8m0(b)).view(np.uint32)) for b in range(256)]}
     # rank-16 core added onto a zero output
     a = np.array([((i * 31 + 7) % 255) - 127 for i in range(16 * cols3)], dtype=np.int8)
     b = np.array([((i * 17 + 3) % 255) - 127 for i in range(rows3 * 16)], dtype=np.int8)

@@ -230,3 +230,26 @@ def test_rms_norm_matches_restatement(oracle):
     inv = np.float32(1.0) / np.float32(np.sqrt(np.float32(ss / np.float32(256) + np.float32(1e-20))))
     want = np.array([np.float32(np.float32(x[i] * inv) * w[i]) for i in range(256)], dtype=np.float32)
     assert np.array_equal(oracle.rms_norm(x[None, :], w)[0], want)
+
+
+def test_e8m0_decode_pinned(oracle):
+    """flash1017.rs:1049-1057 on all 256 codes against the independent restatement."""
+    ka = json.load(open(os.path.join(GOLD, "known_answers.json")))["e8m0"]
+    got = [int(np.float32(oracle.e8m0_to_f32(b)).view(np.uint32)) for b in range(256)]
+    assert got == ka["bits"]
+
+
+def test_mxfp4_known_answer(oracle):
+    """F:2717-2744 restated term by term (tests/golden/make_golden.py)."""
+    ka = json.load(open(os.path.join(GOLD, "known_answers.json")))["mxfp4"]
+    y = oracle.mxfp4_matvec(np.array(ka["w"], dtype=np.uint8), np.array(ka["s"], dtype=np.uint8),
+                            bench_x(ka["cols"]), ka["rows"], ka["cols"])
+    assert np.array_equal(y, np.array(ka["y"], dtype=np.float32))
+
+
+def test_mxfp8_known_answer(oracle):
+    """F:1960-1982 (32 x 32 E8M0 blocks) restated term by term."""
+    ka = json.load(open(os.path.join(GOLD, "known_answers.json")))["mxfp8"]
+    y = oracle.mxfp8_matvec(np.array(ka["w"], dtype=np.uint8), np.array(ka["s"], dtype=np.uint8),
+                            bench_x(ka["cols"]), ka["rows"], ka["cols"])
+    assert np.array_equal(y, np.array(ka["y"], dtype=np.float32))

@@ -292,9 +292,9 @@ int resolve_expert(Ctx &c, ffn_b200_expert &e, size_t inter, size_t hidden) {
     const size_t r = i == 2 ? hidden : inter, k = i == 2 ? inter : hidden;
     const void *a, *b;
     int rc;
-    if (e.format == FFN_B200_FMT_NVFP4) {
+    if (e.format == FFN_B200_FMT_NVFP4 || e.format == FFN_B200_FMT_MXFP4) {
       if ((rc = dev_ptr(c, e.nv[i].w, r * k / 2, &a))) return rc;
-      if ((rc = dev_ptr(c, e.nv[i].s, r * k / 16, &b))) return rc;
+      if ((rc = dev_ptr(c, e.nv[i].s, r * k / (e.format == FFN_B200_FMT_MXFP4 ? 32 : 16), &b))) return rc;
       e.nv[i].w = (const uint8_t *)a;
       e.nv[i].s = (const uint8_t *)b;
     } else {
@@ -454,6 +454,60 @@ bool gx10_rust_nvfp4_mlp_accum(size_t inter_rows, size_t hidden_cols, const uint
   const ffn_b200_expert e =
       nvfp4_expert(w1_fp4, w1_s, w1_sc2, w3_fp4, w3_s, w3_sc2, w2_fp4, w2_s, w2_sc2);
   return mlp_accum(e, inter_rows, hidden_cols, x, out, accum_weight, accumulate, sync_now);
+}
+
+bool gx10_rust_mxfp4_mlp_accum(size_t inter_rows, size_t hidden_cols, const uint8_t *w1_fp4,
+                               const uint8_t *w1_s, const uint8_t *w3_fp4, const uint8_t *w3_s,
+                               const uint8_t *w2_fp4, const uint8_t *w2_s, const float *x, float *out,
+                               float accum_weight, bool accumulate, bool sync_now) {
+  ffn_b200_expert e{};
+  e.format = FFN_B200_FMT_MXFP4;
+  e.proj_scale = 1.0f;
+  const uint8_t *w[3] = {w1_fp4, w3_fp4, w2_fp4}, *sc[3] = {w1_s, w3_s, w2_s};
+  for (int i = 0; i < 3; ++i) {
+    e.nv[i].w = w[i];
+    e.nv[i].s = sc[i];
+    e.nv[i].gs = 1.0f;  // the reference's MXFP4 tensors have no global scale
+  }
+  return mlp_accum(e, inter_rows, hidden_cols, x, out, accum_weight, accumulate, sync_now);
+}
+
+bool gx10_rust_mxfp4_matvec(size_t rows, size_t cols, const uint8_t *packed_fp4,
+                            const uint8_t *scales_e8m0, const float *x, float *out) {
+  Ctx &c = ctx();
+  std::lock_guard<std::mutex> lk(c.mu);
+  int rc = ensure_init(c);
+  if (!rc) rc = flush_pending(c);  // a pending fused-expert output first
+  if (!rc && (!packed_fp4 || !scales_e8m0 || !x || !out || cols % 128))
+    rc = fail(FFN_B200_EINVAL, "mxfp4_matvec: bad arguments");
+  const void *dw = nullptr, *ds = nullptr;
+  if (!rc) rc = dev_ptr(c, packed_fp4, rows * cols / 2, &dw);
+  if (!rc) rc = dev_ptr(c, scales_e8m0, rows * cols / 32, &ds);
+  if (!rc) rc = c.x.ensure(cols * 4);
+  if (!rc) rc = c.out.ensure(rows * 4);
+  if (!rc) rc = c.ws.ensure(ffn_b200_matvec_ws_bytes(1, cols));
+  if (!rc) {
+    cudaError_t er = cudaMemcpyAsync(c.x.p, x, cols * 4, cudaMemcpyHostToDevice, c.st);
+    if (er != cudaSuccess) rc = cuda_fail(er, "x upload");
+  }
+  if (!rc) {
+    ffn_b200_nvfp4_mat m{};
+    m.w = (const uint8_t *)dw;
+    m.s = (const uint8_t *)ds;
+    m.gs = 1.0f;
+    rc = ffn_b200_mxfp4_matvec(rows, cols, 1, &m, (const float *)c.x.p, (float *)c.out.p, c.ws.p, c.ws.n,
+                               c.st);
+  }
+  if (!rc) {
+    cudaError_t er = cudaMemcpyAsync(out, c.out.p, rows * 4, cudaMemcpyDeviceToHost, c.st);
+    if (er == cudaSuccess) er = cudaStreamSynchronize(c.st);
+    if (er != cudaSuccess) rc = cuda_fail(er, "out download");
+  }
+  if (rc) {
+    std::fprintf(stderr, "[ffn_b200] %s\n", ffn_b200_last_error());
+    return false;
+  }
+  return true;
 }
 
 bool gx10_rust_ternary_158_mlp_accum(size_t inter_rows, size_t hidden_cols, const uint8_t *w1_p,

@@ -96,6 +96,22 @@ struct VExp {
 };
 
 // ------------------------------------------------------------ decoders
+// An E8M0 block scale 2^(e - 127) (flash1017.rs:1049-1057) divided by the
+// matrix's power-of-two post-scale 2^bias, as an f16 pair: exact for
+// -24 <= e - 127 - bias <= 15 (subnormal below -14), 0 further down, +inf
+// above; e = 0xFF -> NaN.  Times an E2M1 value (0.5 .. 6, 2 significant bits)
+// the product is exact in f16 while -23 <= e - 127 - bias <= 13.
+__device__ __forceinline__ uint32_t e8m0_f16x2(uint32_t e, int bias) {
+  const int k = (int)e - 127 - bias;
+  uint32_t h;
+  if (e == 0xFFu) h = 0x7E00u;
+  else if (k > 15) h = 0x7C00u;
+  else if (k >= -14) h = (uint32_t)(k + 15) << 10;
+  else if (k >= -24) h = 1u << (k + 24);
+  else h = 0u;
+  return h * 0x10001u;
+}
+
 // Four E2M1 pairs of a 32-bit word (byte b: low nibble = even column) -> four
 // f16x2 {even, odd}; exact.
 __device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t (&o)[4]) {

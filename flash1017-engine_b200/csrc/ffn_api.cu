@@ -1,6 +1,7 @@
 // ffn_api.cu -- the device-resident extension ABI (include/ffn_b200.h).
 #include <algorithm>
 #include <atomic>
+#include <cmath>
 #include <cstdlib>
 #include <mutex>
 #include <string>
@@ -129,6 +130,23 @@ static int check_mat_shape(int fmt, size_t rows, size_t cols, const char *what) 
   if (cols % q)
     return fail(FFN_B200_EUNSUP, std::string(what) + ": cols must be a multiple of " +
                                      std::to_string(q) + " for this format");
+  return 0;
+}
+
+// The kernel family of a format: MXFP4 experts run on the NVFP4 instances
+// (same packed nibbles; the kernels read the E8M0 block scales per task).
+static int kfam(int fmt) { return fmt == FFN_B200_FMT_TERNARY ? FFN_B200_FMT_TERNARY : FFN_B200_FMT_NVFP4; }
+
+// MXFP4 rows of scales (cols/32 bytes) are copied in 4-byte pieces: cols % 128.
+static int check_mxfp4(const ffn_b200_nvfp4_mat &m, size_t cols, const char *what) {
+  if (cols % 128)
+    return fail(FFN_B200_EUNSUP, std::string(what) + ": MXFP4 needs cols % 128 == 0");
+  if (!m.w || !m.s) return fail(FFN_B200_EINVAL, std::string(what) + ": null MXFP4 pointer");
+  if (!aligned(m.w, 16) || !aligned(m.s, 4))
+    return fail(FFN_B200_EINVAL, std::string(what) + ": MXFP4 w must be 16-byte and s 4-byte aligned");
+  int ex = 0;
+  if (!(m.gs > 0.0f) || !std::isfinite(m.gs) || std::frexp(m.gs, &ex) != 0.5f)
+    return fail(FFN_B200_EINVAL, std::string(what) + ": MXFP4 gs must be a power of two");
   return 0;
 }
 
@@ -382,6 +400,19 @@ int ffn_b200_ternary_matvec(size_t rows, size_t cols, size_t seq, const ffn_b200
   return matvec_common(FFN_B200_FMT_TERNARY, rows, cols, seq, E, x, out, ws, ws_bytes, stream);
 }
 
+int ffn_b200_mxfp4_matvec(size_t rows, size_t cols, size_t seq, const ffn_b200_nvfp4_mat *m,
+                          const float *x, float *out, void *ws, size_t ws_bytes, void *stream) {
+  if (!m) return fail(FFN_B200_EINVAL, "mxfp4_matvec: null matrix");
+  int rc = check_mat_shape(FFN_B200_FMT_NVFP4, rows, cols, "mxfp4_matvec");
+  if (!rc) rc = check_mxfp4(*m, cols, "mxfp4_matvec");
+  if (rc) return rc;
+  ffn_b200_expert E{};
+  E.format = FFN_B200_FMT_MXFP4;
+  E.proj_scale = 1.0f;
+  E.nv[0] = *m;
+  return matvec_common(FFN_B200_FMT_NVFP4, rows, cols, seq, E, x, out, ws, ws_bytes, stream);
+}
+
 // --------------------------------------------------------------- one expert
 // Both formats plan the same way up to the unit width; size for the larger.
 static void expert_plans(int fmt, size_t inter, size_t hidden, size_t seq, SplitPlan &s1, SplitPlan &s2) {
@@ -413,12 +444,14 @@ size_t ffn_b200_expert_ws_bytes(size_t inter, size_t hidden, size_t seq) {
 
 static int check_expert(const ffn_b200_expert &e, size_t inter, size_t hidden, const char *what) {
   int rc;
-  if (e.format != FFN_B200_FMT_NVFP4 && e.format != FFN_B200_FMT_TERNARY)
+  if (e.format != FFN_B200_FMT_NVFP4 && e.format != FFN_B200_FMT_TERNARY && e.format != FFN_B200_FMT_MXFP4)
     return fail(FFN_B200_EINVAL, std::string(what) + ": unknown expert format");
   if ((rc = check_mat_shape(e.format, inter, hidden, what))) return rc;
   if ((rc = check_mat_shape(e.format, hidden, inter, what))) return rc;
   for (int i = 0; i < 3; ++i) {
-    rc = e.format == FFN_B200_FMT_NVFP4 ? check_nvfp4(e.nv[i], what) : check_ternary(e.tn[i], what);
+    rc = e.format == FFN_B200_FMT_NVFP4   ? check_nvfp4(e.nv[i], what)
+         : e.format == FFN_B200_FMT_MXFP4 ? check_mxfp4(e.nv[i], i == 2 ? inter : hidden, what)
+                                          : check_ternary(e.tn[i], what);
     if (!rc && e.format == FFN_B200_FMT_TERNARY) rc = check_ternary_bs(e.tn[i], i == 2 ? inter : hidden, what);
     if (rc) return rc;
   }
@@ -437,7 +470,7 @@ int ffn_b200_expert_forward(size_t inter, size_t hidden, size_t seq, const ffn_b
   if (!ws || ws_bytes < ffn_b200_expert_ws_bytes(inter, hidden, seq))
     return fail(FFN_B200_ENOSPC, "expert_forward: workspace too small (see ffn_b200_expert_ws_bytes)");
   cudaStream_t st = (cudaStream_t)stream;
-  const int fmt = e->format;
+  const int fmt = kfam(e->format);  // kernel family
   const bool tern = fmt == FFN_B200_FMT_TERNARY;
   Carve c(ws);
   ActWs a;
@@ -585,7 +618,7 @@ int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
     return fail(FFN_B200_EINVAL, "moe_layer: unknown router_mode");
   if (d->path != FFN_B200_PATH_AUTO && d->path != FFN_B200_PATH_GEMV && d->path != FFN_B200_PATH_GROUPED)
     return fail(FFN_B200_EINVAL, "moe_layer: unknown path");
-  const bool grouped_ok = !d->has_ternary && H % 256 == 0 && I % 256 == 0;
+  const bool grouped_ok = !d->has_ternary && !d->has_mxfp4 && H % 256 == 0 && I % 256 == 0;
   if (d->path == FFN_B200_PATH_GROUPED && !grouped_ok)
     return fail(FFN_B200_EUNSUP,
                 "moe_layer: the grouped path needs NVFP4-only experts and hidden, inter multiples "

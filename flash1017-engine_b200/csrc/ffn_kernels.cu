@@ -245,7 +245,7 @@ struct MatInfo {
 template <int FMT>
 __device__ __forceinline__ MatInfo mat_info(const ffn_b200_expert &E, int mm) {
   MatInfo r;
-  if (FMT == FFN_B200_FMT_NVFP4) {
+  if (FMT == FFN_B200_FMT_NVFP4) {  // NVFP4 and MXFP4 experts (nv[] descriptors)
     r.w = E.nv[mm].w; r.s = E.nv[mm].s; r.gs = E.nv[mm].gs; r.rs = nullptr; r.core_b = nullptr;
   } else {
     r.w = E.tn[mm].p; r.s = E.tn[mm].bs; r.gs = 1.0f; r.rs = E.tn[mm].rs;
@@ -299,6 +299,9 @@ template <int FMT, int PHASE, int NMAT>
 __device__ __forceinline__ int task_mat(const PhaseArgs &a, int mi) {
   return PHASE == 1 ? (mi == 0 ? 0 : 1) : (PHASE == 2 ? 2 : a.mat);
 }
+__device__ __forceinline__ int expert_format(const PhaseArgs &a, int expert) {
+  return expert >= 0 ? a.experts[expert].format : a.direct.format;
+}
 template <int FMT, int PHASE, int NMAT>
 __device__ __forceinline__ MatInfo task_info(const PhaseArgs &a, int expert, int mi) {
   return mat_info<FMT>(expert >= 0 ? a.experts[expert] : a.direct, task_mat<FMT, PHASE, NMAT>(a, mi));
@@ -332,6 +335,7 @@ __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a
   // chunk p_c), STAGES - 1 units ahead of the consumer
   int p_k = 0, p_c = -1, p_cend = 0, p_slot = 0, p_row0 = 0;
   bool p_sal = false;  // scale rows aligned for one SR-byte copy each
+  bool p_mx = false;   // the item's expert is MXFP4 (NVFP4 instance)
   MatRef pm[NMAT];
   auto issue_next = [&]() {
     if (p_k < n_mine) {
@@ -340,16 +344,18 @@ __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a
         const VExp ve = task_slice(a, item / S, WE::ROWS, p_row0);
         p_c = chunk_lo(item);
         p_cend = chunk_hi(item);
-        p_sal = WE::sld_of(a.K) % WE::SR == 0;
+        p_mx = FMT == FFN_B200_FMT_NVFP4 && expert_format(a, ve.expert) == FFN_B200_FMT_MXFP4;
+        const int srb = p_mx ? WE::SR / 2 : WE::SR;  // scale bytes per row and unit
+        p_sal = (p_mx ? a.K / 32 : WE::sld_of(a.K)) % srb == 0;
 #pragma unroll
         for (int mi = 0; mi < NMAT; ++mi) {
           const MatInfo m = task_info<FMT, PHASE, NMAT>(a, ve.expert, mi);
           pm[mi].w = m.w;
           pm[mi].s = m.s;
-          p_sal = p_sal && ((reinterpret_cast<uintptr_t>(m.s) & (WE::SR - 1)) == 0);
+          p_sal = p_sal && ((reinterpret_cast<uintptr_t>(m.s) & (srb - 1)) == 0);
         }
       }
-      WE::issue(ring + p_slot * WE::UNIT, pm, a.rows, a.K, p_row0, p_c, p_sal);
+      WE::issue(ring + p_slot * WE::UNIT, pm, a.rows, a.K, p_row0, p_c, p_sal, p_mx);
       if (++p_c == p_cend) { p_c = -1; ++p_k; }
     }
     cp_async_commit();
@@ -364,11 +370,19 @@ __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a
     int row0;
     const VExp ve = task_slice(a, task, WE::ROWS, row0);
     // ternary matrices with U8 block scales (bit mi)
-    uint32_t bs_mask = 0;
+    uint32_t bs_mask = 0, mxinfo = 0;
     if (FMT == FFN_B200_FMT_TERNARY) {
 #pragma unroll
       for (int mi = 0; mi < NMAT; ++mi)
         if (task_info<FMT, PHASE, NMAT>(a, ve.expert, mi).s) bs_mask |= 1u << mi;
+    } else if (expert_format(a, ve.expert) == FFN_B200_FMT_MXFP4) {
+      // MXFP4: bit 31, and per matrix the exponent of its power-of-two gs + 128
+      mxinfo = 1u << 31;
+#pragma unroll
+      for (int mi = 0; mi < NMAT; ++mi) {
+        const int b = max(-128, min(127, ilogbf(task_info<FMT, PHASE, NMAT>(a, ve.expert, mi).gs)));
+        mxinfo |= (uint32_t)(b + 128) << (8 * mi);
+      }
     }
     const bool packed = ve.count <= 4;
     // this lane's MMA column: packed: token g&3, hi terms in columns 0-3 and
@@ -396,8 +410,8 @@ __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a
       __syncwarp();
       const uint8_t *slot = ring + c_slot * WE::UNIT;
       c_slot = c_slot + 1 == kStages ? 0 : c_slot + 1;
-      if (packed) WE::template compute<true>(slot, a.K, c, xa, xb, acc, bs_mask);
-      else WE::template compute<false>(slot, a.K, c, xa, xb, acc, bs_mask);
+      if (packed) WE::template compute<true>(slot, a.K, c, xa, xb, acc, bs_mask, mxinfo);
+      else WE::template compute<false>(slot, a.K, c, xa, xb, acc, bs_mask, mxinfo);
       __syncwarp();
     }
 
@@ -1089,7 +1103,7 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__
     if (e < n_exp) {
       const int c = s_counts[e], s = (c + kNTok - 1) / kNTok;
       loc_pairs += c;
-      if (experts[e].format == FFN_B200_FMT_NVFP4) loc_nv += s; else loc_tn += s;
+      if (experts[e].format != FFN_B200_FMT_TERNARY) loc_nv += s; else loc_tn += s;
     }
   }
   // block-wide exclusive scans of the three per-thread totals
@@ -1128,7 +1142,7 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__
       offsets[e] = base_p;
       s_off[e] = base_p;
       base_p += c;
-      if (experts[e].format == FFN_B200_FMT_NVFP4) { vbase[e] = base_n; base_n += s; }
+      if (experts[e].format != FFN_B200_FMT_TERNARY) { vbase[e] = base_n; base_n += s; }
       else { vbase[e] = base_t; base_t += s; }
     }
   }
@@ -1169,7 +1183,7 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__
   __syncthreads();
   for (int e = tid; e < n_exp; e += blockDim.x) {
     const int c = s_counts[e];
-    VExp *dst = experts[e].format == FFN_B200_FMT_NVFP4 ? vexp_nv : vexp_tn;
+    VExp *dst = experts[e].format != FFN_B200_FMT_TERNARY ? vexp_nv : vexp_tn;  // NVFP4, MXFP4 | ternary
     for (int j = 0; j * kNTok < c; ++j) {
       VExp v;
       v.expert = e;

@@ -105,8 +105,10 @@ struct WarpEngine {
   // zero).  NVFP4 scales: SR bytes of each of the unit's 16*MT rows, one
   // SR-byte copy per row when every scale row is SR-byte aligned (s_al),
   // otherwise 4-byte copies.
+  // mx: an MXFP4 task on the NVFP4 instance (E8M0 scales per 32 columns:
+  // SR / 2 bytes per row and unit, stored at the start of the row's SR slot)
   __device__ static void issue(uint8_t *slot, const MatRef (&m)[NMAT], int rows, int K, int row0, int c,
-                               bool s_al) {
+                               bool s_al, bool mx = false) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     constexpr int LB = FMT == FFN_B200_FMT_NVFP4 ? 32 : 64;  // columns per lane per sub-chunk
     const size_t wld = (size_t)K / (FMT == FFN_B200_FMT_NVFP4 ? 2 : 4);
@@ -130,7 +132,36 @@ struct WarpEngine {
     bool any_s = FMT == FFN_B200_FMT_NVFP4;
 #pragma unroll
     for (int mi = 0; mi < NMAT; ++mi) any_s = any_s || m[mi].s != nullptr;
-    if (any_s) {  // ternary: only the matrices that have block scales are copied
+    if (any_s && mx) {
+      constexpr int SRM = SR / 2;
+      const int sld = K / 32;
+      uint8_t *sbase = slot + UNIT_W;
+      constexpr int NROW = MT * 16;
+      if (s_al) {
+#pragma unroll
+        for (int j = 0; j < (NROW + 31) / 32; ++j) {
+          const int rr = lane + 32 * j;
+          if (rr < NROW && c * SRM < sld) {
+            const int mt = rr >> 4, mi = mt / R, i = mt % R;
+            const int sr = min(row0 + 16 * i + (rr & 15), rows - 1);
+            cp_async_n<SRM>(sbase + rr * SR, m[mi].s + (size_t)sr * sld + c * SRM);
+          }
+        }
+      } else {
+        constexpr int PIECES = NROW * SRM / 4;
+#pragma unroll
+        for (int j = 0; j < (PIECES + 31) / 32; ++j) {
+          const int p = lane + 32 * j;
+          if (p < PIECES) {
+            const int rr = p / (SRM / 4), q = p % (SRM / 4);
+            const int mt = rr >> 4, mi = mt / R, i = mt % R;
+            const int sr = min(row0 + 16 * i + (rr & 15), rows - 1);
+            const int sc = c * SRM + 4 * q;
+            if (sc < sld) cp_async4(sbase + rr * SR + 4 * q, m[mi].s + (size_t)sr * sld + sc);
+          }
+        }
+      }
+    } else if (any_s) {  // ternary: only the matrices that have block scales are copied
       const int sld = sld_of(K);
       uint8_t *sbase = slot + UNIT_W;
       constexpr int NROW = MT * 16;
@@ -165,9 +196,9 @@ struct WarpEngine {
   template <bool PACKED>
   __device__ static __forceinline__ void compute(const uint8_t *slot, int K, int c, const __half *xa,
                                                  const __half *xb, float (&acc)[NMAT][R][4],
-                                                 uint32_t bs_mask = 0) {
+                                                 uint32_t bs_mask = 0, uint32_t mxinfo = 0) {
 #pragma unroll
-    for (int sb = 0; sb < SUB; ++sb) compute_sub<PACKED>(slot, sb, K, c * SUB + sb, xa, xb, acc, bs_mask);
+    for (int sb = 0; sb < SUB; ++sb) compute_sub<PACKED>(slot, sb, K, c * SUB + sb, xa, xb, acc, bs_mask, mxinfo);
   }
 
   // Accumulate one sub-chunk c from `slot` into acc.  xa/xb: this lane's
@@ -178,7 +209,8 @@ struct WarpEngine {
   // next to the k-steps that use them.
   template <bool PACKED>
   __device__ static void compute_sub(const uint8_t *unit, int sb, int K, int c, const __half *xa,
-                                     const __half *xb, float (&acc)[NMAT][R][4], uint32_t bs_mask) {
+                                     const __half *xb, float (&acc)[NMAT][R][4], uint32_t bs_mask,
+                                     uint32_t mxinfo) {
     const uint8_t *slot = unit + sb * SUB_W;
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int col0 = c * CHUNK + (FMT == FFN_B200_FMT_NVFP4 ? 32 : 64) * t;
@@ -205,9 +237,18 @@ struct WarpEngine {
       for (int mt = 0; mt < MT; ++mt) {
         // lanes past K read no scale bytes (they may be stale: an E4M3 NaN there
         // would turn the zero weights into NaN)
-        const uint8_t *sp = unit + UNIT_W + mt * 16 * SR + 8 * sb + 2 * t;
-        sfa[mt] = valid ? e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t *>(sp + g * SR)) : 0u;
-        sfb[mt] = valid ? e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t *>(sp + (g + 8) * SR)) : 0u;
+        if (mxinfo >> 31) {
+          // MXFP4: the lane's 32 columns are one E8M0 block (block t of the
+          // sub-chunk); both halves carry it, so the word's lo/hi broadcasts agree
+          const uint8_t *sp = unit + UNIT_W + mt * 16 * SR + 4 * sb + t;
+          const int bias = (int)((mxinfo >> (8 * (mt / R))) & 0xFFu) - 128;
+          sfa[mt] = valid ? e8m0_f16x2(sp[g * SR], bias) : 0u;
+          sfb[mt] = valid ? e8m0_f16x2(sp[(g + 8) * SR], bias) : 0u;
+        } else {
+          const uint8_t *sp = unit + UNIT_W + mt * 16 * SR + 8 * sb + 2 * t;
+          sfa[mt] = valid ? e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t *>(sp + g * SR)) : 0u;
+          sfb[mt] = valid ? e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t *>(sp + (g + 8) * SR)) : 0u;
+        }
       }
 #pragma unroll
       for (int wd = 0; wd < 4; ++wd) {

@@ -20,6 +20,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <cmath>
 #include <cstring>
 #include <string>
 #include <unordered_map>
@@ -296,7 +297,11 @@ int plan_expert(const ffn_b200_st *st, const std::string &prefix, size_t hidden,
   const char *mname[3] = {".w1", ".w3", ".w2"};  // gate, up, down
   const size_t rows_of[3] = {inter, inter, hidden}, cols_of[3] = {hidden, hidden, inter};
   pl = ExpertPlan{};
-  pl.format = has(st, prefix + ".w1.weight") ? FFN_B200_FMT_NVFP4 : FFN_B200_FMT_TERNARY;
+  // NVFP4: .weight + .weight_scale (+ .weight_scale_2); MXFP4 (CachedMxfp4Mat,
+  // flash1017.rs:2688-2699): .weight + .scale; else ternary
+  pl.format = has(st, prefix + ".w1.weight")
+                  ? (has(st, prefix + ".w1.weight_scale") ? FFN_B200_FMT_NVFP4 : FFN_B200_FMT_MXFP4)
+                  : FFN_B200_FMT_TERNARY;
   if (pl.format == FFN_B200_FMT_TERNARY && !has(st, prefix + ".w1.packed_ternary"))
     return fail(FFN_B200_EINVAL, "safetensors: no expert '" + prefix + "' (neither .w1.weight nor .w1.packed_ternary)");
   auto add = [&](const uint8_t *src, size_t n) {
@@ -319,6 +324,17 @@ int plan_expert(const ffn_b200_st *st, const std::string &prefix, size_t hidden,
       pl.e.nv[i].s = (const uint8_t *)(uintptr_t)add(d, n);
       ST_TRY(get(st, p + ".weight_scale_2", 4, {1}, &d, &n));
       std::memcpy(&pl.e.nv[i].gs, d, 4);  // little-endian f32 (flash1017.rs:2299)
+    } else if (pl.format == FFN_B200_FMT_MXFP4) {
+      ST_TRY(get(st, p + ".weight", 1, {R, Cc / 2}, &d, &n));
+      pl.e.nv[i].w = (const uint8_t *)(uintptr_t)add(d, n);
+      ST_TRY(get(st, p + ".scale", 1, {R, Cc / 32}, &d, &n));
+      pl.e.nv[i].s = (const uint8_t *)(uintptr_t)add(d, n);
+      // gs = 2^B, B = largest finite block scale byte - 140: that block
+      // decodes to 2^13 in f16 (FFN_B200_FMT_MXFP4)
+      int mx = -1;
+      for (size_t q = 0; q < n; ++q)
+        if (d[q] != 0xFF && d[q] > mx) mx = d[q];
+      pl.e.nv[i].gs = std::ldexp(1.0f, mx < 0 ? 0 : mx - 140);
     } else {
       ffn_b200_ternary_mat &m = pl.e.tn[i];
       ST_TRY(get(st, p + ".packed_ternary", 1, {R, Cc / 4}, &d, &n));
@@ -462,7 +478,7 @@ int ffn_b200_st_load_expert(const ffn_b200_st *st, const char *prefix, size_t hi
     FFN_CUDA_TRY(cudaMemcpyAsync(base + pc.off, pc.src, pc.n, cudaMemcpyHostToDevice, s));
   ffn_b200_expert out = pl.e;
   for (int i = 0; i < 3; ++i) {
-    if (pl.format == FFN_B200_FMT_NVFP4) {
+    if (pl.format != FFN_B200_FMT_TERNARY) {
       out.nv[i].w = reloc_first(pl.e.nv[i].w, base);
       out.nv[i].s = reloc_first(pl.e.nv[i].s, base);
     } else {

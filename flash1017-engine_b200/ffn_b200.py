@@ -15,7 +15,7 @@ import subprocess
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "libffn_b200.so")
 
-FMT_NVFP4, FMT_TERNARY = 0, 1
+FMT_NVFP4, FMT_TERNARY, FMT_MXFP4 = 0, 1, 2
 SCORE_REF, SCORE_SIGMOID = 0, 1
 ROUTER_EXACT, ROUTER_TENSOR = 0, 1
 PATH_AUTO, PATH_GEMV, PATH_GROUPED = 0, 1, 2
@@ -38,6 +38,7 @@ EXPORTS = [
     "ffn_b200_profile_enable", "ffn_b200_profile_kinds", "ffn_b200_profile_read",
     "ffn_b200_ep_handle_bytes", "ffn_b200_ep_create", "ffn_b200_ep_connect", "ffn_b200_ep_part",
     "ffn_b200_ep_allreduce", "ffn_b200_ep_error", "ffn_b200_ep_destroy",
+    "ffn_b200_mxfp4_matvec", "gx10_rust_mxfp4_matvec", "gx10_rust_mxfp4_mlp_accum",
     "ffn_b200_st_open", "ffn_b200_st_close", "ffn_b200_st_count", "ffn_b200_st_name",
     "ffn_b200_st_find", "ffn_b200_st_expert_bytes", "ffn_b200_st_load_expert",
 ]
@@ -83,7 +84,7 @@ class MoeDesc(C.Structure):
                 ("router_mode", C.c_int32), ("expert_begin", C.c_int32),
                 ("expert_end", C.c_int32), ("has_nvfp4", C.c_int32),
                 ("has_ternary", C.c_int32), ("norm_w", C.c_void_p), ("norm_eps", C.c_float),
-                ("path", C.c_int32)]
+                ("path", C.c_int32), ("has_mxfp4", C.c_int32)]
 
 
 assert C.sizeof(Expert) == 248, C.sizeof(Expert)
@@ -108,6 +109,12 @@ def lib() -> C.CDLL:
         L.ffn_b200_matvec_ws_bytes.argtypes = [sz, sz]
         L.ffn_b200_nvfp4_matvec.argtypes = [sz, sz, sz, C.POINTER(NvMat), vp, vp, vp, sz, vp]
         L.ffn_b200_ternary_matvec.argtypes = [sz, sz, sz, C.POINTER(TnMat), vp, vp, vp, sz, vp]
+        L.ffn_b200_mxfp4_matvec.argtypes = [sz, sz, sz, C.POINTER(NvMat), vp, vp, vp, sz, vp]
+        L.gx10_rust_mxfp4_matvec.argtypes = [sz, sz, vp, vp, vp, vp]
+        L.gx10_rust_mxfp4_matvec.restype = C.c_bool
+        L.gx10_rust_mxfp4_mlp_accum.argtypes = [sz, sz, vp, vp, vp, vp, vp, vp, vp, vp, f32,
+                                                C.c_bool, C.c_bool]
+        L.gx10_rust_mxfp4_mlp_accum.restype = C.c_bool
         L.ffn_b200_expert_ws_bytes.restype = sz
         L.ffn_b200_expert_ws_bytes.argtypes = [sz, sz, sz]
         L.ffn_b200_expert_forward.argtypes = [sz, sz, sz, C.POINTER(Expert), vp, vp, f32, i32,
@@ -329,6 +336,37 @@ class Nvfp4Matrix:
         return self.w.numel() + self.s.numel()
 
 
+class Mxfp4Matrix(Nvfp4Matrix):
+    """MXFP4 matrix on the device (FMT_MXFP4, flash1017.rs:2674-2747): w
+    [rows, cols/2] E2M1 pairs, s [rows, cols/32] E8M0 block scales, gs a power
+    of two 2^B taken out of the block scales (1 for the reference's tensors)."""
+
+    @staticmethod
+    def bias_for(s_bytes) -> float:
+        """gs = 2^B with B = (largest finite block scale byte) - 140: the
+        largest block decodes to 2^13 in f16 (E2M1 6 x 2^13 < 65504)."""
+        torch = _torch()
+        t = s_bytes if torch.is_tensor(s_bytes) else torch.as_tensor(s_bytes)
+        t = t[t != 0xFF]
+        return 2.0 ** (int(t.max().item()) - 140) if t.numel() else 1.0
+
+    def matvec(self, x, out=None, stream=None):
+        torch = _torch()
+        x = x.contiguous()
+        seq = x.numel() // self.cols
+        if out is None:
+            out = torch.empty(seq, self.rows, dtype=torch.float32, device=x.device)
+        ws = _default_ws(x.device).get(lib().ffn_b200_matvec_ws_bytes(seq, self.cols))
+        m = self.cstruct()
+        check(lib().ffn_b200_mxfp4_matvec(self.rows, self.cols, seq, C.byref(m), _ptr(x),
+                                          _ptr(out), _ptr(ws), ws.numel(), _stream(stream)),
+              "mxfp4_matvec")
+        return out
+
+    def nbytes(self) -> int:
+        return self.w.numel() + self.s.numel()
+
+
 class TernaryMatrix:
     """Packed ternary matrix p [rows, cols/4] u8 + rs [rows] f32 (+ optional
     rank-16 core a [16, cols] i8, a_sc [16], b [rows, 16] i8, b_sc [16]; +
@@ -408,10 +446,10 @@ class SwigluExpert:
         e.format = self.fmt
         e.proj_scale = self.proj_scale
         for i, m in enumerate(self.mats):
-            if self.fmt == FMT_NVFP4:
-                e.nv[i] = m.cstruct()
-            else:
+            if self.fmt == FMT_TERNARY:
                 e.tn[i] = m.cstruct()
+            else:  # NVFP4 and MXFP4 use nv[]
+                e.nv[i] = m.cstruct()
         return e
 
     @classmethod
@@ -560,8 +598,9 @@ class MoeLayer:
         lo, hi = expert_range if expert_range else (0, n)
         self.desc = MoeDesc(hidden, inter, n, top_k, _ptr(self.table), _ptr(router_w),
                             _ptr(router_bias), score_fn, router_mode, lo, hi,
-                            int(FMT_NVFP4 in fmts or not fmts), int(FMT_TERNARY in fmts),
-                            _ptr(norm_w), float(norm_eps), int(path))
+                            int(FMT_NVFP4 in fmts or FMT_MXFP4 in fmts or not fmts),
+                            int(FMT_TERNARY in fmts), _ptr(norm_w), float(norm_eps), int(path),
+                            int(FMT_MXFP4 in fmts))
         self.ws = ws if ws is not None else Workspace(device)
 
     def ws_bytes(self, n_tok: int) -> int:

@@ -50,6 +50,14 @@ extern "C" {
 
 #define FFN_B200_FMT_NVFP4 0
 #define FFN_B200_FMT_TERNARY 1
+/* MXFP4 experts (the MTP routed experts, flash1017.rs:2674-2747) use the nv[]
+ * descriptors: w E2M1 pairs [rows, cols/2], s E8M0 block scales [rows, cols/32]
+ * (2^(s - 127), flash1017.rs:1049-1057), gs a power of two 2^B (1 for the
+ * reference's tensors, which have no global scale).  The kernels decode each
+ * block scale as 2^(s - 127 - B) in f16 and multiply the f32 sums by gs, so a
+ * matrix is decoded exactly while every block obeys -23 <= s - 127 - B <= 13;
+ * st_load_expert picks B from the largest block scale.  cols % 128 == 0. */
+#define FFN_B200_FMT_MXFP4 2
 
 /* Router score functions.  REF: sqrt(softplus(l)) + bias, weights
  * score * 1.5 / sum (flash1017.rs:7280-7376).  SIGMOID: sigmoid(l) + bias,
@@ -111,6 +119,11 @@ FFN_B200_EXPORT size_t ffn_b200_matvec_ws_bytes(size_t seq, size_t cols);
 FFN_B200_EXPORT int ffn_b200_nvfp4_matvec(size_t rows, size_t cols, size_t seq,
                                           const ffn_b200_nvfp4_mat *m, const float *x,
                                           float *out, void *ws, size_t ws_bytes, void *stream);
+/* MXFP4 rows (CachedMxfp4Mat::matvec, flash1017.rs:2700-2746): m->s holds the
+ * E8M0 scales [rows, cols/32], m->gs a power of two (FFN_B200_FMT_MXFP4). */
+FFN_B200_EXPORT int ffn_b200_mxfp4_matvec(size_t rows, size_t cols, size_t seq,
+                                          const ffn_b200_nvfp4_mat *m, const float *x,
+                                          float *out, void *ws, size_t ws_bytes, void *stream);
 /* Ternary rows, then y += B (diag(a_sc b_sc) A x) when m->core_a != NULL
  * (flash1017.rs:2538-2627, rank-16 core :2446-2472). */
 FFN_B200_EXPORT int ffn_b200_ternary_matvec(size_t rows, size_t cols, size_t seq,
@@ -162,7 +175,7 @@ typedef struct ffn_b200_moe_desc {
     int32_t score_fn;                /* FFN_B200_SCORE_* */
     int32_t router_mode;             /* FFN_B200_ROUTER_* */
     int32_t expert_begin, expert_end;
-    int32_t has_nvfp4, has_ternary;  /* which formats occur in experts[] */
+    int32_t has_nvfp4, has_ternary;  /* which formats occur in experts[] (has_nvfp4: NVFP4 or MXFP4) */
     /* Optional RMSNorm of the layer input before routing and the experts, the
      * reference's ffn_norm (flash1017.rs:7637, 4880-4891): xn = x / sqrt(mean(x^2)
      * + norm_eps) * norm_w.  NULL: the experts see x itself. */
@@ -173,6 +186,9 @@ typedef struct ffn_b200_moe_desc {
      * the routed pairs average >= FFN_B200_GROUPED_MIN_PAIRS per expert
      * (prefill), else the GEMV slices (decode). */
     int32_t path;
+    /* MXFP4 experts occur in experts[] (they count as has_nvfp4 too: same
+     * kernel family; the grouped GEMM is NVFP4-only). */
+    int32_t has_mxfp4;
 } ffn_b200_moe_desc;
 
 #define FFN_B200_PATH_AUTO 0
@@ -273,8 +289,10 @@ FFN_B200_EXPORT int ffn_b200_ep_destroy(ffn_b200_ep *ep);
  * The shard is mapped read-only; st_load_expert copies one expert's tensors
  * into a caller-owned device buffer (st_expert_bytes of it, 256-byte aligned)
  * on `stream` and fills *e with device pointers into it.  NVFP4 when
- * <prefix>.w1.weight exists (weight u8 [rows, cols/2], weight_scale
- * [rows, cols/16], weight_scale_2 f32 scalar -> gs), else ternary
+ * <prefix>.w1.weight and .weight_scale exist (weight u8 [rows, cols/2],
+ * weight_scale [rows, cols/16], weight_scale_2 f32 scalar -> gs); MXFP4 when
+ * .weight and .scale exist (CachedMxfp4Mat::from_shard :2688-2699; scale E8M0
+ * [rows, cols/32]; gs = 2^(largest scale byte - 140)); else ternary
  * (packed_ternary [rows, cols/4], row_scales f32 [rows], optional
  * block_scales u8 [rows, cols/64], optional rank-16 core).  Shapes are checked
  * against inter x hidden; proj_scale is set to 1. */

@@ -155,6 +155,21 @@ FFN_B200_EXPORT bool gx10_rust_nvfp4_mlp_accum(size_t inter_rows, size_t hidden_
                                                float accum_weight, bool accumulate,
                                                bool sync_now);
 
+/* HA:359-373 (call site flash1017.rs:9103-9123, CPU twin :9145-9158): the MTP
+ * layer's MXFP4 routed experts (E2M1 [rows, cols/2], E8M0 scales per 32
+ * columns, no global scale), same SwiGLU and accumulate / sync_now semantics
+ * as gx10_rust_nvfp4_mlp_accum. */
+FFN_B200_EXPORT bool gx10_rust_mxfp4_mlp_accum(size_t inter_rows, size_t hidden_cols,
+                                               const uint8_t *w1_fp4, const uint8_t *w1_s,
+                                               const uint8_t *w3_fp4, const uint8_t *w3_s,
+                                               const uint8_t *w2_fp4, const uint8_t *w2_s,
+                                               const float *x, float *out, float accum_weight,
+                                               bool accumulate, bool sync_now);
+/* HA:298-305 (call sites flash1017.rs:940-956, 2704-2716): out [rows] =
+ * MXFP4 W x, synchronous; false on error (the host then runs its CPU loop). */
+FFN_B200_EXPORT bool gx10_rust_mxfp4_matvec(size_t rows, size_t cols, const uint8_t *packed_fp4,
+                                            const uint8_t *scales_e8m0, const float *x, float *out);
+
 /* HA:342-357 (call site flash1017.rs:7488-7504, CPU twin :7551-7561): gate/up
  * outputs are multiplied by proj_scale before the SwiGLU; the caller passes
  * accum_weight = weight * proj_scale. */

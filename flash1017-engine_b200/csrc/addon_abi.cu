@@ -265,6 +265,37 @@ const char kDesc[] =
     "B200 (sm_100a) quantized expert-FFN backend: NVFP4 + 1.58-bit ternary (+rank-16 Q8) "
     "tensor-core GEMV/GEMM, routed SwiGLU MoE";
 
+// MXFP8 post-scale 2^B from the host scale bytes: the largest finite E8M0
+// scale decodes to 2^7 (E4M3 448 x 2^7 < 65504, FFN_B200_FMT_MXFP8).
+float mxfp8_gs(const uint8_t *s, size_t n) {
+  int mx = -1;
+  for (size_t q = 0; q < n; ++q)
+    if (s[q] != 0xFF && s[q] > mx) mx = s[q];
+  return std::ldexp(1.0f, mx < 0 ? 0 : mx - 134);
+}
+
+void v3_matbatch_mxfp8(size_t rows, size_t cols, size_t seq, const uint8_t *w, const uint8_t *s,
+                       const float *xb, float *ob) {
+  run_sync(seq * cols, xb, seq * rows, ob, [&](Ctx &c, const float *dx, float *dout) {
+    if (!w || !s || cols % 128) return fail(FFN_B200_EINVAL, "matbatch_mxfp8: bad arguments");
+    const size_t sn = ((rows + 31) / 32) * (cols / 32);
+    ffn_b200_nvfp4_mat m{};
+    const void *dw, *ds;
+    int rc = dev_ptr(c, w, rows * cols, &dw);
+    if (!rc) rc = dev_ptr(c, s, sn, &ds);
+    if (rc) return rc;
+    m.w = (const uint8_t *)dw;
+    m.s = (const uint8_t *)ds;
+    m.gs = mxfp8_gs(s, sn);
+    if ((rc = c.ws.ensure(ffn_b200_matvec_ws_bytes(seq, cols)))) return rc;
+    return ffn_b200_mxfp8_matvec(rows, cols, seq, &m, dx, dout, c.ws.p, c.ws.n, c.st);
+  });
+}
+void v3_matvec_mxfp8(size_t rows, size_t cols, const uint8_t *w, const uint8_t *s, const float *x,
+                     float *out) {
+  v3_matbatch_mxfp8(rows, cols, 1, w, s, x, out);
+}
+
 HardwareAddonVTable make_vtable() {
   HardwareAddonVTable v;
   std::memset(&v, 0, sizeof(v));
@@ -283,6 +314,8 @@ HardwareAddonVTable make_vtable() {
   v.matbatch_nvfp4 = v3_matbatch_nvfp4;
   v.matvec_ternary_158 = v3_matvec_ternary;
   v.matbatch_ternary_158 = v3_matbatch_ternary;
+  v.matvec_mxfp8 = v3_matvec_mxfp8;
+  v.matbatch_mxfp8 = v3_matbatch_mxfp8;
   return v;
 }
 
@@ -292,7 +325,12 @@ int resolve_expert(Ctx &c, ffn_b200_expert &e, size_t inter, size_t hidden) {
     const size_t r = i == 2 ? hidden : inter, k = i == 2 ? inter : hidden;
     const void *a, *b;
     int rc;
-    if (e.format == FFN_B200_FMT_NVFP4 || e.format == FFN_B200_FMT_MXFP4) {
+    if (e.format == FFN_B200_FMT_MXFP8) {
+      if ((rc = dev_ptr(c, e.nv[i].w, r * k, &a))) return rc;
+      if ((rc = dev_ptr(c, e.nv[i].s, ((r + 31) / 32) * ((k + 31) / 32), &b))) return rc;
+      e.nv[i].w = (const uint8_t *)a;
+      e.nv[i].s = (const uint8_t *)b;
+    } else if (e.format == FFN_B200_FMT_NVFP4 || e.format == FFN_B200_FMT_MXFP4) {
       if ((rc = dev_ptr(c, e.nv[i].w, r * k / 2, &a))) return rc;
       if ((rc = dev_ptr(c, e.nv[i].s, r * k / (e.format == FFN_B200_FMT_MXFP4 ? 32 : 16), &b))) return rc;
       e.nv[i].w = (const uint8_t *)a;
@@ -468,6 +506,23 @@ bool gx10_rust_mxfp4_mlp_accum(size_t inter_rows, size_t hidden_cols, const uint
     e.nv[i].w = w[i];
     e.nv[i].s = sc[i];
     e.nv[i].gs = 1.0f;  // the reference's MXFP4 tensors have no global scale
+  }
+  return mlp_accum(e, inter_rows, hidden_cols, x, out, accum_weight, accumulate, sync_now);
+}
+
+bool gx10_rust_mxfp8_mlp_accum(size_t inter_rows, size_t hidden_cols, const uint8_t *w1_w,
+                               const uint8_t *w1_s, const uint8_t *w3_w, const uint8_t *w3_s,
+                               const uint8_t *w2_w, const uint8_t *w2_s, const float *x, float *out,
+                               float accum_weight, bool accumulate, bool sync_now) {
+  ffn_b200_expert e{};
+  e.format = FFN_B200_FMT_MXFP8;
+  e.proj_scale = 1.0f;
+  const uint8_t *w[3] = {w1_w, w3_w, w2_w}, *sc[3] = {w1_s, w3_s, w2_s};
+  for (int i = 0; i < 3; ++i) {
+    const size_t r = i == 2 ? hidden_cols : inter_rows, k = i == 2 ? inter_rows : hidden_cols;
+    e.nv[i].w = w[i];
+    e.nv[i].s = sc[i];
+    e.nv[i].gs = sc[i] ? mxfp8_gs(sc[i], ((r + 31) / 32) * ((k + 31) / 32)) : 1.0f;
   }
   return mlp_accum(e, inter_rows, hidden_cols, x, out, accum_weight, accumulate, sync_now);
 }

@@ -135,7 +135,23 @@ static int check_mat_shape(int fmt, size_t rows, size_t cols, const char *what) 
 
 // The kernel family of a format: MXFP4 experts run on the NVFP4 instances
 // (same packed nibbles; the kernels read the E8M0 block scales per task).
-static int kfam(int fmt) { return fmt == FFN_B200_FMT_TERNARY ? FFN_B200_FMT_TERNARY : FFN_B200_FMT_NVFP4; }
+static int kfam(int fmt) {
+  return fmt == FFN_B200_FMT_TERNARY || fmt == FFN_B200_FMT_MXFP8 ? fmt : FFN_B200_FMT_NVFP4;
+}
+
+// MXFP8: E4M3 [rows, cols], E8M0 [ceil(rows/32), cols/32]; 4-byte scale copies
+// per 128 columns need cols % 128.
+static int check_mxfp8(const ffn_b200_nvfp4_mat &m, size_t cols, const char *what) {
+  if (cols % 128)
+    return fail(FFN_B200_EUNSUP, std::string(what) + ": MXFP8 needs cols % 128 == 0");
+  if (!m.w || !m.s) return fail(FFN_B200_EINVAL, std::string(what) + ": null MXFP8 pointer");
+  if (!aligned(m.w, 16) || !aligned(m.s, 4))
+    return fail(FFN_B200_EINVAL, std::string(what) + ": MXFP8 w must be 16-byte and s 4-byte aligned");
+  int ex = 0;
+  if (!(m.gs > 0.0f) || !std::isfinite(m.gs) || std::frexp(m.gs, &ex) != 0.5f)
+    return fail(FFN_B200_EINVAL, std::string(what) + ": MXFP8 gs must be a power of two");
+  return 0;
+}
 
 // MXFP4 rows of scales (cols/32 bytes) are copied in 4-byte pieces: cols % 128.
 static int check_mxfp4(const ffn_b200_nvfp4_mat &m, size_t cols, const char *what) {
@@ -413,6 +429,19 @@ int ffn_b200_mxfp4_matvec(size_t rows, size_t cols, size_t seq, const ffn_b200_n
   return matvec_common(FFN_B200_FMT_NVFP4, rows, cols, seq, E, x, out, ws, ws_bytes, stream);
 }
 
+int ffn_b200_mxfp8_matvec(size_t rows, size_t cols, size_t seq, const ffn_b200_nvfp4_mat *m,
+                          const float *x, float *out, void *ws, size_t ws_bytes, void *stream) {
+  if (!m) return fail(FFN_B200_EINVAL, "mxfp8_matvec: null matrix");
+  int rc = check_mat_shape(FFN_B200_FMT_MXFP8, rows, cols, "mxfp8_matvec");
+  if (!rc) rc = check_mxfp8(*m, cols, "mxfp8_matvec");
+  if (rc) return rc;
+  ffn_b200_expert E{};
+  E.format = FFN_B200_FMT_MXFP8;
+  E.proj_scale = 1.0f;
+  E.nv[0] = *m;
+  return matvec_common(FFN_B200_FMT_MXFP8, rows, cols, seq, E, x, out, ws, ws_bytes, stream);
+}
+
 // --------------------------------------------------------------- one expert
 // Both formats plan the same way up to the unit width; size for the larger.
 static void expert_plans(int fmt, size_t inter, size_t hidden, size_t seq, SplitPlan &s1, SplitPlan &s2) {
@@ -434,7 +463,7 @@ static void carve_expert(Carve &c, int fmt, size_t inter, size_t hidden, size_t 
 
 size_t ffn_b200_expert_ws_bytes(size_t inter, size_t hidden, size_t seq) {
   size_t need = 0;
-  for (int fmt : {FFN_B200_FMT_NVFP4, FFN_B200_FMT_TERNARY}) {
+  for (int fmt : {FFN_B200_FMT_NVFP4, FFN_B200_FMT_TERNARY, FFN_B200_FMT_MXFP8}) {
     Carve c(nullptr);
     carve_expert(c, fmt, inter, hidden, seq, nullptr, nullptr, nullptr, nullptr);
     need = std::max(need, c.off + 256);
@@ -444,13 +473,15 @@ size_t ffn_b200_expert_ws_bytes(size_t inter, size_t hidden, size_t seq) {
 
 static int check_expert(const ffn_b200_expert &e, size_t inter, size_t hidden, const char *what) {
   int rc;
-  if (e.format != FFN_B200_FMT_NVFP4 && e.format != FFN_B200_FMT_TERNARY && e.format != FFN_B200_FMT_MXFP4)
+  if (e.format != FFN_B200_FMT_NVFP4 && e.format != FFN_B200_FMT_TERNARY && e.format != FFN_B200_FMT_MXFP4 &&
+      e.format != FFN_B200_FMT_MXFP8)
     return fail(FFN_B200_EINVAL, std::string(what) + ": unknown expert format");
   if ((rc = check_mat_shape(e.format, inter, hidden, what))) return rc;
   if ((rc = check_mat_shape(e.format, hidden, inter, what))) return rc;
   for (int i = 0; i < 3; ++i) {
     rc = e.format == FFN_B200_FMT_NVFP4   ? check_nvfp4(e.nv[i], what)
          : e.format == FFN_B200_FMT_MXFP4 ? check_mxfp4(e.nv[i], i == 2 ? inter : hidden, what)
+         : e.format == FFN_B200_FMT_MXFP8 ? check_mxfp8(e.nv[i], i == 2 ? inter : hidden, what)
                                           : check_ternary(e.tn[i], what);
     if (!rc && e.format == FFN_B200_FMT_TERNARY) rc = check_ternary_bs(e.tn[i], i == 2 ? inter : hidden, what);
     if (rc) return rc;

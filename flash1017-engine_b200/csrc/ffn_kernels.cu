@@ -245,7 +245,7 @@ struct MatInfo {
 template <int FMT>
 __device__ __forceinline__ MatInfo mat_info(const ffn_b200_expert &E, int mm) {
   MatInfo r;
-  if (FMT == FFN_B200_FMT_NVFP4) {  // NVFP4 and MXFP4 experts (nv[] descriptors)
+  if (FMT != FFN_B200_FMT_TERNARY) {  // NVFP4, MXFP4 and MXFP8 (nv[] descriptors)
     r.w = E.nv[mm].w; r.s = E.nv[mm].s; r.gs = E.nv[mm].gs; r.rs = nullptr; r.core_b = nullptr;
   } else {
     r.w = E.tn[mm].p; r.s = E.tn[mm].bs; r.gs = 1.0f; r.rs = E.tn[mm].rs;
@@ -279,7 +279,9 @@ template <int PHASE>
 __host__ __device__ constexpr int task_r() { return PHASE == 1 ? FFN_R_GATEUP : FFN_R_SINGLE; }
 
 int rows_per_tile(int phase) { return 16 * (phase == 1 ? task_r<1>() : task_r<2>()); }
-int chunk_cols(int fmt) { return (fmt == FFN_B200_FMT_NVFP4 ? 128 : 256) * kSub; }
+int chunk_cols(int fmt) {
+  return (fmt == FFN_B200_FMT_NVFP4 ? 128 : fmt == FFN_B200_FMT_MXFP8 ? 64 : 256) * kSub;
+}
 
 // A task's slice and first row.
 __device__ __forceinline__ VExp task_slice(const PhaseArgs &a, int task, int rows_per_task, int &row0) {
@@ -375,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a
 #pragma unroll
       for (int mi = 0; mi < NMAT; ++mi)
         if (task_info<FMT, PHASE, NMAT>(a, ve.expert, mi).s) bs_mask |= 1u << mi;
-    } else if (expert_format(a, ve.expert) == FFN_B200_FMT_MXFP4) {
+    } else if (FMT == FFN_B200_FMT_MXFP8 || expert_format(a, ve.expert) == FFN_B200_FMT_MXFP4) {
       // MXFP4: bit 31, and per matrix the exponent of its power-of-two gs + 128
       mxinfo = 1u << 31;
 #pragma unroll
@@ -499,7 +501,7 @@ __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a
 #pragma unroll
           for (int mi = 0; mi < NMAT; ++mi) {
             float s = acc[mi][i][2 * jr + jn];
-            if (FMT == FFN_B200_FMT_NVFP4) {
+            if (FMT != FFN_B200_FMT_TERNARY) {
               s = s * xsc * mat[mi].gs;
             } else {
               const int mm = task_mat<FMT, PHASE, NMAT>(a, mi);
@@ -515,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a
             const float h = silu_clamped(gv) * clamp10(uv);
             __half hi, lo;
             split_f16(h, hi, lo);
-            const int col = FMT == FFN_B200_FMT_NVFP4 ? row : tern_pos(row);
+            const int col = FMT != FFN_B200_FMT_TERNARY ? row : tern_pos(row);
             a.hh[(size_t)p * a.ld_h + col] = hi;
             a.hl[(size_t)p * a.ld_h + col] = lo;
           } else {
@@ -535,7 +537,7 @@ __global__ void __launch_bounds__(kThreads, MINB) phase_kernel(const PhaseArgs a
 
 constexpr int phase_kind(int fmt, int phase) {
   return phase == 0 ? FFN_B200_K_MATVEC
-                    : (fmt == FFN_B200_FMT_NVFP4 ? (phase == 1 ? FFN_B200_K_GATEUP_NVFP4 : FFN_B200_K_DOWN_NVFP4)
+                    : (fmt != FFN_B200_FMT_TERNARY ? (phase == 1 ? FFN_B200_K_GATEUP_NVFP4 : FFN_B200_K_DOWN_NVFP4)
                                                  : (phase == 1 ? FFN_B200_K_GATEUP_TERNARY : FFN_B200_K_DOWN_TERNARY));
 }
 
@@ -573,6 +575,11 @@ static int launch_phase_t(const PhaseArgs &a, long long tasks, cudaStream_t st) 
 
 // `tasks` is an upper bound of the warp work items (slices x row blocks x splits).
 int launch_phase(int fmt, int phase, const PhaseArgs &a, long long tasks, cudaStream_t st) {
+  if (fmt == FFN_B200_FMT_MXFP8) {
+    if (phase == 1) return launch_phase_t<FFN_B200_FMT_MXFP8, 1>(a, tasks, st);
+    if (phase == 2) return launch_phase_t<FFN_B200_FMT_MXFP8, 2>(a, tasks, st);
+    return launch_phase_t<FFN_B200_FMT_MXFP8, 0>(a, tasks, st);
+  }
   if (fmt == FFN_B200_FMT_NVFP4) {
     if (phase == 1) return launch_phase_t<FFN_B200_FMT_NVFP4, 1>(a, tasks, st);
     if (phase == 2) return launch_phase_t<FFN_B200_FMT_NVFP4, 2>(a, tasks, st);

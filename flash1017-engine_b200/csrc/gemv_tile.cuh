@@ -83,20 +83,26 @@ template <int FMT, int NMAT, int R, int STAGES, int SUB = 1>
 struct WarpEngine {
   static constexpr int ROWS = 16 * R;
   static constexpr int MT = NMAT * R;                                   // m-tiles per unit
-  static constexpr int CHUNK = FMT == FFN_B200_FMT_NVFP4 ? 128 : 256;  // columns per sub-chunk
+  static constexpr bool F8 = FMT == FFN_B200_FMT_MXFP8;                // one byte per weight
+  // columns per sub-chunk: a lane holds 16 bytes of each of its rows
+  static constexpr int CHUNK = FMT == FFN_B200_FMT_NVFP4 ? 128 : F8 ? 64 : 256;
   static constexpr int SUB_W = MT * 2 * 32 * 16;                        // weight bytes per sub-chunk
   static constexpr int UNIT_W = SUB * SUB_W;
   // scale bytes per row per unit: NVFP4 E4M3 per 16 columns; ternary U8 block
   // scales per 64 columns (copied only for matrices that have them)
+  // (MXFP8: one E8M0 scale per 32 x 32 block -- 2 * SUB bytes per m-tile and
+  // unit, 16 bytes reserved per m-tile)
   static constexpr int SR = FMT == FFN_B200_FMT_NVFP4 ? 8 * SUB : 4 * SUB;
-  static constexpr int UNIT_S = MT * 16 * SR;
+  static constexpr int UNIT_S = F8 ? MT * 16 : MT * 16 * SR;
   static constexpr int UNIT = UNIT_W + UNIT_S;                          // [SUB weight blocks][scales]
   static constexpr int RING = STAGES * UNIT;                            // per warp
   static constexpr size_t SMEM = (size_t)kWarps * RING;
 
   static __device__ __forceinline__ int nchunks(int K) { return (K + CHUNK * SUB - 1) / (CHUNK * SUB); }
   // scale bytes per matrix row
-  static __host__ __device__ __forceinline__ int sld_of(int K) { return FMT == FFN_B200_FMT_NVFP4 ? K / 16 : K / 64; }
+  static __host__ __device__ __forceinline__ int sld_of(int K) {
+    return FMT == FFN_B200_FMT_NVFP4 ? K / 16 : F8 ? (K + 31) / 32 : K / 64;
+  }
 
   // Issue the copies of unit c (columns [c*CHUNK*SUB, +CHUNK*SUB)) of the task
   // whose rows start at row0 into `slot`.  Weights: per sub-chunk and m-tile,
@@ -110,13 +116,14 @@ struct WarpEngine {
   __device__ static void issue(uint8_t *slot, const MatRef (&m)[NMAT], int rows, int K, int row0, int c,
                                bool s_al, bool mx = false) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    constexpr int LB = FMT == FFN_B200_FMT_NVFP4 ? 32 : 64;  // columns per lane per sub-chunk
-    const size_t wld = (size_t)K / (FMT == FFN_B200_FMT_NVFP4 ? 2 : 4);
+    constexpr int LB = FMT == FFN_B200_FMT_NVFP4 ? 32 : F8 ? 16 : 64;  // columns per lane per sub-chunk
+    constexpr int EPB = FMT == FFN_B200_FMT_NVFP4 ? 2 : F8 ? 1 : 4;     // elements per byte
+    const size_t wld = (size_t)K / EPB;
 #pragma unroll
     for (int sb = 0; sb < SUB; ++sb) {
       const int col0 = (c * SUB + sb) * CHUNK + LB * t;
       if (col0 < K) {
-        const size_t boff = (size_t)col0 / (FMT == FFN_B200_FMT_NVFP4 ? 2 : 4);
+        const size_t boff = (size_t)col0 / EPB;
 #pragma unroll
         for (int mi = 0; mi < NMAT; ++mi)
 #pragma unroll
@@ -128,6 +135,19 @@ struct WarpEngine {
             cp_async16(d + 512, m[mi].w + rb * wld + boff);
           }
       }
+    }
+    if constexpr (F8) {
+      // lane mt copies the 2 * SUB block scales of m-tile mt (row block
+      // (first row) / 32, block columns [2 SUB c, +2 SUB)); K % 128 keeps the
+      // 4-byte copies aligned and inside the scale row
+      const int scols = sld_of(K);
+      if (lane < MT && c * 2 * SUB < scols) {
+        const int mi = lane / R, i = lane % R;
+        const int rblk = min(row0 + 16 * i, rows - 1) / 32;
+        static_assert(2 * SUB == 4, "one 4-byte copy per m-tile");
+        cp_async4(slot + UNIT_W + lane * 16, m[mi].s + (size_t)rblk * scols + c * 2 * SUB);
+      }
+      return;
     }
     bool any_s = FMT == FFN_B200_FMT_NVFP4;
 #pragma unroll
@@ -213,7 +233,7 @@ struct WarpEngine {
                                      uint32_t mxinfo) {
     const uint8_t *slot = unit + sb * SUB_W;
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int col0 = c * CHUNK + (FMT == FFN_B200_FMT_NVFP4 ? 32 : 64) * t;
+    const int col0 = c * CHUNK + (FMT == FFN_B200_FMT_NVFP4 ? 32 : F8 ? 16 : 64) * t;
     const bool valid = col0 < K;
     // activation words are loaded one 16-byte word at a time (hi and lo),
     // next to their use, which keeps the live registers at ~80 per thread
@@ -231,7 +251,40 @@ struct WarpEngine {
       for (int h = 0; h < 2; ++h)
         wq[mt][h] = valid ? *reinterpret_cast<const uint4 *>(slot + mt * 1024 + h * 512 + lane * 16)
                           : zero;  // code 1 (ternary) / E2M1 0 (NVFP4) decode to zero
-    if constexpr (FMT == FFN_B200_FMT_NVFP4) {
+    if constexpr (F8) {
+      // MXFP8: lane t's 16 columns lie in block column (4 sub-chunk + t) / 2;
+      // rows g and g+8 share the m-tile's row block, so one scale per m-tile
+      uint32_t sf[MT];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const int bias = (int)((mxinfo >> (8 * (mt / R))) & 0xFFu) - 128;
+        sf[mt] = valid ? e8m0_f16x2(unit[UNIT_W + mt * 16 + 2 * sb + (t >> 1)], bias) : 0u;
+      }
+#pragma unroll
+      for (int v = 0; v < 2; ++v) {
+        // activation word v = columns col0 + 8v .. +7 = k-steps 2v, 2v+1
+        const uint4 xh = xload(xa, v);
+        const uint4 xl = PACKED ? make_uint4(0u, 0u, 0u, 0u) : xload(xb, v);
+        const uint32_t bh[4] = {xh.x, xh.y, xh.z, xh.w};
+        const uint32_t bl[4] = {xl.x, xl.y, xl.z, xl.w};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int j = 2 * v + h;  // weight word j = columns col0 + 4j .. +3
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            const int mi = mt / R, i = mt % R;
+            const uint32_t wa = j == 0 ? wq[mt][0].x : j == 1 ? wq[mt][0].y : j == 2 ? wq[mt][0].z : wq[mt][0].w;
+            const uint32_t wb = j == 0 ? wq[mt][1].x : j == 1 ? wq[mt][1].y : j == 2 ? wq[mt][1].z : wq[mt][1].w;
+            const uint32_t a0 = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(wa & 0xFFFFu)), sf[mt]);
+            const uint32_t a1 = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(wb & 0xFFFFu)), sf[mt]);
+            const uint32_t a2 = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(wa >> 16)), sf[mt]);
+            const uint32_t a3 = hmul2_u32(e4m3x2_to_f16x2((uint16_t)(wb >> 16)), sf[mt]);
+            mma_f16(acc[mi][i], a0, a1, a2, a3, bh[2 * h], bh[2 * h + 1]);
+            if (!PACKED) mma_f16(acc[mi][i], a0, a1, a2, a3, bl[2 * h], bl[2 * h + 1]);
+          }
+        }
+      }
+    } else if constexpr (FMT == FFN_B200_FMT_NVFP4) {
       uint32_t sfa[MT], sfb[MT];
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {

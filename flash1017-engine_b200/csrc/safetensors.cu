@@ -302,6 +302,12 @@ int plan_expert(const ffn_b200_st *st, const std::string &prefix, size_t hidden,
   pl.format = has(st, prefix + ".w1.weight")
                   ? (has(st, prefix + ".w1.weight_scale") ? FFN_B200_FMT_NVFP4 : FFN_B200_FMT_MXFP4)
                   : FFN_B200_FMT_TERNARY;
+  // MXFP8 (CachedMxfp8Mat, the shared experts, flash1017.rs:1928-1939): .weight
+  // + .scale with one byte per weight
+  if (pl.format == FFN_B200_FMT_MXFP4) {
+    const StTensor &w1 = st->tensors.at(prefix + ".w1.weight");
+    if (w1.shape.size() == 2 && (size_t)w1.shape[1] == hidden) pl.format = FFN_B200_FMT_MXFP8;
+  }
   if (pl.format == FFN_B200_FMT_TERNARY && !has(st, prefix + ".w1.packed_ternary"))
     return fail(FFN_B200_EINVAL, "safetensors: no expert '" + prefix + "' (neither .w1.weight nor .w1.packed_ternary)");
   auto add = [&](const uint8_t *src, size_t n) {
@@ -324,6 +330,16 @@ int plan_expert(const ffn_b200_st *st, const std::string &prefix, size_t hidden,
       pl.e.nv[i].s = (const uint8_t *)(uintptr_t)add(d, n);
       ST_TRY(get(st, p + ".weight_scale_2", 4, {1}, &d, &n));
       std::memcpy(&pl.e.nv[i].gs, d, 4);  // little-endian f32 (flash1017.rs:2299)
+    } else if (pl.format == FFN_B200_FMT_MXFP8) {
+      ST_TRY(get(st, p + ".weight", 1, {R, Cc}, &d, &n));
+      pl.e.nv[i].w = (const uint8_t *)(uintptr_t)add(d, n);
+      ST_TRY(get(st, p + ".scale", 1, {(R + 31) / 32, (Cc + 31) / 32}, &d, &n));
+      pl.e.nv[i].s = (const uint8_t *)(uintptr_t)add(d, n);
+      // gs = 2^B, B = largest finite scale byte - 134 (FFN_B200_FMT_MXFP8)
+      int mx = -1;
+      for (size_t q = 0; q < n; ++q)
+        if (d[q] != 0xFF && d[q] > mx) mx = d[q];
+      pl.e.nv[i].gs = std::ldexp(1.0f, mx < 0 ? 0 : mx - 134);
     } else if (pl.format == FFN_B200_FMT_MXFP4) {
       ST_TRY(get(st, p + ".weight", 1, {R, Cc / 2}, &d, &n));
       pl.e.nv[i].w = (const uint8_t *)(uintptr_t)add(d, n);

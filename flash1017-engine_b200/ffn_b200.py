@@ -15,7 +15,7 @@ import subprocess
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "libffn_b200.so")
 
-FMT_NVFP4, FMT_TERNARY, FMT_MXFP4 = 0, 1, 2
+FMT_NVFP4, FMT_TERNARY, FMT_MXFP4, FMT_MXFP8 = 0, 1, 2, 3
 SCORE_REF, SCORE_SIGMOID = 0, 1
 ROUTER_EXACT, ROUTER_TENSOR = 0, 1
 PATH_AUTO, PATH_GEMV, PATH_GROUPED = 0, 1, 2
@@ -39,6 +39,7 @@ EXPORTS = [
     "ffn_b200_ep_handle_bytes", "ffn_b200_ep_create", "ffn_b200_ep_connect", "ffn_b200_ep_part",
     "ffn_b200_ep_allreduce", "ffn_b200_ep_error", "ffn_b200_ep_destroy",
     "ffn_b200_mxfp4_matvec", "gx10_rust_mxfp4_matvec", "gx10_rust_mxfp4_mlp_accum",
+    "ffn_b200_mxfp8_matvec", "gx10_rust_mxfp8_mlp_accum",
     "ffn_b200_st_open", "ffn_b200_st_close", "ffn_b200_st_count", "ffn_b200_st_name",
     "ffn_b200_st_find", "ffn_b200_st_expert_bytes", "ffn_b200_st_load_expert",
 ]
@@ -115,6 +116,10 @@ def lib() -> C.CDLL:
         L.gx10_rust_mxfp4_mlp_accum.argtypes = [sz, sz, vp, vp, vp, vp, vp, vp, vp, vp, f32,
                                                 C.c_bool, C.c_bool]
         L.gx10_rust_mxfp4_mlp_accum.restype = C.c_bool
+        L.ffn_b200_mxfp8_matvec.argtypes = [sz, sz, sz, C.POINTER(NvMat), vp, vp, vp, sz, vp]
+        L.gx10_rust_mxfp8_mlp_accum.argtypes = [sz, sz, vp, vp, vp, vp, vp, vp, vp, vp, f32,
+                                                C.c_bool, C.c_bool]
+        L.gx10_rust_mxfp8_mlp_accum.restype = C.c_bool
         L.ffn_b200_expert_ws_bytes.restype = sz
         L.ffn_b200_expert_ws_bytes.argtypes = [sz, sz, sz]
         L.ffn_b200_expert_forward.argtypes = [sz, sz, sz, C.POINTER(Expert), vp, vp, f32, i32,
@@ -367,6 +372,37 @@ class Mxfp4Matrix(Nvfp4Matrix):
         return self.w.numel() + self.s.numel()
 
 
+class Mxfp8Matrix(Nvfp4Matrix):
+    """MXFP8 matrix on the device (FMT_MXFP8, the shared expert's format,
+    flash1017.rs:1920-1984): w [rows, cols] E4M3, s [ceil(rows/32), cols/32]
+    E8M0 scales of 32 x 32 blocks, gs a power of two 2^B taken out of them."""
+
+    @staticmethod
+    def bias_for(s_bytes) -> float:
+        """gs = 2^B, B = (largest finite scale byte) - 134: the largest block
+        decodes to 2^7 in f16 (E4M3 448 x 2^7 < 65504)."""
+        torch = _torch()
+        t = s_bytes if torch.is_tensor(s_bytes) else torch.as_tensor(s_bytes)
+        t = t[t != 0xFF]
+        return 2.0 ** (int(t.max().item()) - 134) if t.numel() else 1.0
+
+    def matvec(self, x, out=None, stream=None):
+        torch = _torch()
+        x = x.contiguous()
+        seq = x.numel() // self.cols
+        if out is None:
+            out = torch.empty(seq, self.rows, dtype=torch.float32, device=x.device)
+        ws = _default_ws(x.device).get(lib().ffn_b200_matvec_ws_bytes(seq, self.cols))
+        m = self.cstruct()
+        check(lib().ffn_b200_mxfp8_matvec(self.rows, self.cols, seq, C.byref(m), _ptr(x),
+                                          _ptr(out), _ptr(ws), ws.numel(), _stream(stream)),
+              "mxfp8_matvec")
+        return out
+
+    def nbytes(self) -> int:
+        return self.w.numel() + self.s.numel()
+
+
 class TernaryMatrix:
     """Packed ternary matrix p [rows, cols/4] u8 + rs [rows] f32 (+ optional
     rank-16 core a [16, cols] i8, a_sc [16], b [rows, 16] i8, b_sc [16]; +
@@ -591,6 +627,9 @@ class MoeLayer:
         self.norm_w = norm_w
         self.hidden, self.inter, self.top_k = hidden, inter, top_k
         n = len(experts)
+        if any(e is not None and e.fmt == FMT_MXFP8 for e in experts):
+            raise FfnError("MoE tables hold NVFP4, MXFP4 and ternary experts; MXFP8 is for "
+                           "dense (shared) experts")
         if table is None:
             self.table, fmts = expert_table(experts, device)
         else:  # a shared (table, formats) pair

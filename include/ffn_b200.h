@@ -58,6 +58,14 @@ extern "C" {
  * matrix is decoded exactly while every block obeys -23 <= s - 127 - B <= 13;
  * st_load_expert picks B from the largest block scale.  cols % 128 == 0. */
 #define FFN_B200_FMT_MXFP4 2
+/* MXFP8 matrices (the shared expert, CachedMxfp8Mat, flash1017.rs:1920-1984)
+ * also use nv[]: w E4M3 [rows, cols], s E8M0 [ceil(rows/32), cols/32] (one
+ * scale per 32 x 32 block), gs a power of two 2^B; decoded as E4M3 x
+ * 2^(s - 127 - B) in f16, exact while -15 <= s - 127 - B <= 7 (the caller's B
+ * from the largest scale: B = max(s) - 134).  cols % 128 == 0.  Dense experts
+ * (expert_forward, gx10_rust_mxfp8_mlp_accum) and matvecs only: MoE tables
+ * hold NVFP4, MXFP4 and ternary experts. */
+#define FFN_B200_FMT_MXFP8 3
 
 /* Router score functions.  REF: sqrt(softplus(l)) + bias, weights
  * score * 1.5 / sum (flash1017.rs:7280-7376).  SIGMOID: sigmoid(l) + bias,
@@ -122,6 +130,12 @@ FFN_B200_EXPORT int ffn_b200_nvfp4_matvec(size_t rows, size_t cols, size_t seq,
 /* MXFP4 rows (CachedMxfp4Mat::matvec, flash1017.rs:2700-2746): m->s holds the
  * E8M0 scales [rows, cols/32], m->gs a power of two (FFN_B200_FMT_MXFP4). */
 FFN_B200_EXPORT int ffn_b200_mxfp4_matvec(size_t rows, size_t cols, size_t seq,
+                                          const ffn_b200_nvfp4_mat *m, const float *x,
+                                          float *out, void *ws, size_t ws_bytes, void *stream);
+/* MXFP8 rows (CachedMxfp8Mat::matvec, flash1017.rs:1940-1984): m->w E4M3
+ * [rows, cols], m->s E8M0 [ceil(rows/32), cols/32], m->gs a power of two
+ * (FFN_B200_FMT_MXFP8). */
+FFN_B200_EXPORT int ffn_b200_mxfp8_matvec(size_t rows, size_t cols, size_t seq,
                                           const ffn_b200_nvfp4_mat *m, const float *x,
                                           float *out, void *ws, size_t ws_bytes, void *stream);
 /* Ternary rows, then y += B (diag(a_sc b_sc) A x) when m->core_a != NULL
@@ -292,7 +306,9 @@ FFN_B200_EXPORT int ffn_b200_ep_destroy(ffn_b200_ep *ep);
  * <prefix>.w1.weight and .weight_scale exist (weight u8 [rows, cols/2],
  * weight_scale [rows, cols/16], weight_scale_2 f32 scalar -> gs); MXFP4 when
  * .weight and .scale exist (CachedMxfp4Mat::from_shard :2688-2699; scale E8M0
- * [rows, cols/32]; gs = 2^(largest scale byte - 140)); else ternary
+ * [rows, cols/32]; gs = 2^(largest scale byte - 140)); MXFP8 when .weight
+ * has one byte per weight (the shared experts, CachedMxfp8Mat :1928-1939;
+ * scale [ceil(rows/32), cols/32]; gs = 2^(largest - 134)); else ternary
  * (packed_ternary [rows, cols/4], row_scales f32 [rows], optional
  * block_scales u8 [rows, cols/64], optional rank-16 core).  Shapes are checked
  * against inter x hidden; proj_scale is set to 1. */

@@ -155,6 +155,18 @@ FFN_B200_EXPORT bool gx10_rust_nvfp4_mlp_accum(size_t inter_rows, size_t hidden_
                                                float accum_weight, bool accumulate,
                                                bool sync_now);
 
+/* HA:307-320 (call sites flash1017.rs:7401-7405 and 9075-9091, CPU twin
+ * :9132-9142): the shared expert, MXFP8 (E4M3 [rows, cols], E8M0 scales per
+ * 32 x 32 block), same SwiGLU and accumulate / sync_now semantics as
+ * gx10_rust_nvfp4_mlp_accum.  With it, nvfp4 and ternary present, the
+ * reference takes its fused GPU MoE path (flash1017.rs:7401-7405). */
+FFN_B200_EXPORT bool gx10_rust_mxfp8_mlp_accum(size_t inter_rows, size_t hidden_cols,
+                                               const uint8_t *w1_w, const uint8_t *w1_s,
+                                               const uint8_t *w3_w, const uint8_t *w3_s,
+                                               const uint8_t *w2_w, const uint8_t *w2_s,
+                                               const float *x, float *out, float accum_weight,
+                                               bool accumulate, bool sync_now);
+
 /* HA:359-373 (call site flash1017.rs:9103-9123, CPU twin :9145-9158): the MTP
  * layer's MXFP4 routed experts (E2M1 [rows, cols/2], E8M0 scales per 32
  * columns, no global scale), same SwiGLU and accumulate / sync_now semantics

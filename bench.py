@@ -68,7 +68,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["config4", "config3"], default="config4")
+    ap.add_argument("--workload", choices=["config4", "config3", "expert"], default="config4")
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--experts", type=int, default=384)
@@ -81,9 +81,14 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="CPU-baseline sample length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--format", choices=["nvfp4", "ternary106"], default="nvfp4",
-                    help="config4 expert format: NVFP4 (BASELINE) or the reference compressor's "
-                         "106 GB format (ternary + U8 block-64 scales + rank-16 Q8 core)")
+    ap.add_argument("--format", choices=["nvfp4", "ternary106", "ternary", "mxfp4", "mxfp8"],
+                    default="nvfp4",
+                    help="expert format: NVFP4 (BASELINE), the reference compressor's 106 GB "
+                         "format (ternary + U8 block-64 scales + rank-16 Q8 core), config 1's "
+                         "ternary + rank-16 core, MXFP4 (MTP experts), MXFP8 (shared expert); "
+                         "config4 takes nvfp4 / ternary106, --workload expert all of them")
+    ap.add_argument("--pool", type=int, default=64,
+                    help="--workload expert: distinct experts cycled per step (> L2)")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="per-layer sum over ranks: NVLink peer exchange or NCCL all-reduce")
     return ap.parse_args()
@@ -95,6 +100,9 @@ METRIC3 = "MoE expert-FFN prefill tokens/s (one NVFP4 top-6/384 layer, 8192 toke
 def metric_of(a):
     if a.workload == "config3":
         return METRIC3
+    if a.workload == "expert":
+        return (f"SwiGLU expert forwards/s ({a.format}, {a.tokens} token(s), rotating pool of "
+                f"{a.pool} experts)")
     return METRIC106 if a.format == "ternary106" else METRIC
 
 
@@ -731,8 +739,178 @@ def _traffic_per_launch(alg_bytes_per_launch):
         return None
 
 
+# --------------------------------------------------------------- one expert
+def _expert_mat_bytes(fmt, r, c):
+    if fmt == "nvfp4":
+        return r * c // 2 + r * c // 16
+    if fmt == "mxfp4":
+        return r * c // 2 + r * c // 32
+    if fmt == "mxfp8":
+        return r * c + ((r + 31) // 32) * (c // 32)
+    if fmt == "ternary106":
+        return tern106_mat_bytes(r, c)
+    return r * c // 4 + 4 * r + 16 * r + 16 * c + 128  # ternary + rank-16 core (config 1)
+
+
+def run_expert(a):
+    """BASELINE configs 0 (NVFP4) and 1 (ternary + rank-16 core) and the other
+    expert formats: one SwiGLU expert forward over `tokens` rows, cycling
+    through a pool of distinct experts larger than L2 (a step = one pass over
+    the pool); roofline = the expert's weight bytes over HBM."""
+    import numpy as np
+    import torch
+
+    import ffn_b200 as F
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    H, I, T, P = a.hidden, a.inter, a.tokens, a.pool
+    fmt = a.format
+    shapes = ((I, H), (I, H), (H, I))
+    ebytes = sum(_expert_mat_bytes(fmt, r, c) for r, c in shapes)
+    gen = torch.Generator(device=dev)
+    experts = []
+    for e in range(P):
+        keys = [F.path_key(a.seed, 0, e, tag) for tag in (F.TAG_W1, F.TAG_W3, F.TAG_W2)]
+        if fmt == "nvfp4":
+            experts.append(F.SwigluExpert.generate(F.FMT_NVFP4, a.seed, 0, e, I, H))
+        elif fmt in ("ternary", "ternary106"):
+            ex = F.SwigluExpert.generate(F.FMT_TERNARY, a.seed, 0, e, I, H, with_core=True)
+            if fmt == "ternary106":
+                for k, m in zip(keys, ex.mats):
+                    gen.manual_seed(k & 0x7FFFFFFFFFFFFFFF)
+                    m.bs = torch.randint(0, 256, (m.rows * m.cols // 64,), dtype=torch.uint8,
+                                         device=dev, generator=gen)
+            experts.append(ex)
+        else:
+            mats = []
+            for k, (r, c) in zip(keys, shapes):
+                gen.manual_seed(k & 0x7FFFFFFFFFFFFFFF)
+                if fmt == "mxfp4":
+                    w = torch.randint(0, 256, (r * c // 2,), dtype=torch.uint8, device=dev, generator=gen)
+                    sc = torch.randint(110, 131, (r * c // 32,), dtype=torch.uint8, device=dev, generator=gen)
+                    mats.append(F.Mxfp4Matrix(w, sc, F.Mxfp4Matrix.bias_for(sc), r, c))
+                else:
+                    w = torch.randint(0, 256, (r * c,), dtype=torch.uint8, device=dev, generator=gen)
+                    w[(w & 0x7F) == 0x7F] = 0x38  # no E4M3 NaN codes
+                    sc = torch.randint(118, 131, (((r + 31) // 32) * (c // 32),), dtype=torch.uint8,
+                                       device=dev, generator=gen)
+                    mats.append(F.Mxfp8Matrix(w, sc, F.Mxfp8Matrix.bias_for(sc), r, c))
+            experts.append(F.SwigluExpert(F.FMT_MXFP4 if fmt == "mxfp4" else F.FMT_MXFP8, mats, I, H))
+    x = F.gen_normal(F.path_key(a.seed, 0, 0, F.TAG_X), T * H).view(T, H)
+    out = torch.zeros(T, H, dtype=torch.float32, device=dev)
+
+    def step():
+        for ex in experts:
+            ex.forward(x, out=out, weight=1.0, accumulate=True)
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(_bus_id(dev, 0))
+    clocks.start()
+    time.sleep(0.3)
+    n0 = F.launch_count()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record()
+    for _ in range(a.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    launches = F.launch_count() - n0
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    fwd = P * a.steps
+    value = fwd / (ms * 1e-3)
+    us_fwd = ms * 1e3 / fwd
+    # end to end: the step's x uploaded from pinned host memory, out read back
+    x_host = x.cpu().pin_memory()
+    o_host = torch.empty_like(x_host).pin_memory()
+    for i in range(a.warmup + a.steps):
+        if i == a.warmup:
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        x.copy_(x_host, non_blocking=True)
+        step()
+        o_host.copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e = fwd / (e0.elapsed_time(e1) * 1e-3)
+    # per-kernel breakdown of one step
+    F.profile_kinds(None)
+    F.profile_enable(True)
+    step()
+    torch.cuda.synchronize()
+    F.profile_enable(False)
+    kernels = {k: {"us_per_launch": round(v[0] * 1e3 / v[1], 2), "launches": v[1]}
+               for k, v in F.profile_read().items()}
+    peaks = _peaks()
+    achieved = ebytes / (us_fwd * 1e-6) / 1e9
+    cpu = None
+    if not a.no_cpu_baseline:
+        import oracle as O
+        O.set_threads(os.cpu_count() or 1)
+        e0h = experts[0]
+        if fmt == "nvfp4":
+            oe = O.Nvfp4Expert(I, H, tuple(m.w.cpu().numpy() for m in e0h.mats),
+                               tuple(m.s.cpu().numpy() for m in e0h.mats),
+                               tuple(m.gs for m in e0h.mats))
+        elif fmt in ("ternary", "ternary106"):
+            cores = tuple(O.Core(m.core[0].cpu().numpy(), m.core[1].cpu().numpy(),
+                                 m.core[2].cpu().numpy(), m.core[3].cpu().numpy()) for m in e0h.mats)
+            bs = tuple(m.bs.cpu().numpy() for m in e0h.mats) if fmt == "ternary106" else None
+            oe = O.TernaryExpert(I, H, tuple(m.p.cpu().numpy() for m in e0h.mats),
+                                 tuple(m.rs.cpu().numpy() for m in e0h.mats), cores, 1.0, bs)
+        else:
+            oe = O.MxExpert(3 if fmt == "mxfp4" else 4, I, H, tuple(m.w.cpu().numpy() for m in e0h.mats),
+                            tuple(m.s.cpu().numpy() for m in e0h.mats))
+        xs = x.cpu().numpy()
+        n, c0 = 0, time.perf_counter()
+        while time.perf_counter() - c0 < min(a.cpu_seconds, 6.0):
+            for t in range(T):
+                oe.forward(np.ascontiguousarray(xs[t]))
+            n += 1
+        dt = time.perf_counter() - c0
+        cpu = {"value": n / dt, "unit": "expert forwards/s", "cores": os.cpu_count() or 1,
+               "kind": "port", "sample": f"oracle expert forward over the same {T} token(s), {n} "
+                                         f"repetitions in {dt:.1f} s"}
+    line = {
+        "metric": metric_of(a), "value": value, "unit": "expert forwards/s", "n_gpus": 1,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": f"{fmt} weights x f16x2 split activations, f32 accumulate",
+        "data": "synthetic (seeded random-init weights and N(0,1) hidden states)",
+        "config": {"workload": f"one SwiGLU expert ({fmt}), {T} token(s), pool of {P} experts "
+                               f"({P * ebytes / 1e9:.2f} GB > 126 MB L2)",
+                   "hidden": H, "inter": I, "tokens": T, "pool": P, "seed": a.seed,
+                   "l2": "no flush: the pool exceeds L2, every forward reads its weights from HBM"},
+        "e2e": {"value": e2e, "unit": "expert forwards/s", "h2d_bytes_per_step": T * H * 4,
+                "d2h_bytes_per_step": T * H * 4},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "kernel": f"expert forward ({fmt}, all its launches)",
+                     "achieved": achieved, "peak": peaks[0], "unit": "GB/s", "frac": achieved / peaks[0],
+                     "traffic": None, "peak_source": peaks[1], "algorithmic_bytes_per_forward": ebytes,
+                     "us_per_forward": us_fwd},
+        "cpu_baseline": cpu,
+        "clocks": clk,
+        "kernels": kernels,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     a = parse_args()
+    if a.workload == "expert":
+        for k, v in (("tokens", 1), ("layers", 1), ("seed", 0 if a.format == "nvfp4" else 1)):
+            if getattr(a, k) is None:
+                setattr(a, k, v)
+        if a.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "--workload expert has no "
+                              "reference arm; its cpu_baseline times the oracle"}))
+            return 0
+        return run_expert(a)
     if a.workload == "config3":
         for k, v in (("tokens", 8192), ("layers", 1), ("seed", 3)):
             if getattr(a, k) is None:

@@ -17,7 +17,11 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     ["--workload", "config3", "--experts", "96", "--tokens", "2048", "--steps", "2", "--warmup", "3",
      "--no-cpu-baseline"],
     ["--workload", "config4", "--format", "ternary106", "--layers", "2", "--steps", "3", "--warmup", "3"],
-], ids=["config4", "config3", "config4-ternary106"])
+    ["--workload", "expert", "--format", "mxfp4", "--pool", "8", "--steps", "3", "--warmup", "3",
+     "--cpu-seconds", "1"],
+    ["--workload", "expert", "--format", "ternary106", "--pool", "8", "--steps", "3", "--warmup", "3",
+     "--no-cpu-baseline"],
+], ids=["config4", "config3", "config4-ternary106", "expert-mxfp4", "expert-ternary106"])
 def test_bench_line(args):
     r = subprocess.run([sys.executable, "bench.py", *args], cwd=ROOT, capture_output=True, text=True,
                        timeout=900)

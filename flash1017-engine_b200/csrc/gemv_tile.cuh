@@ -303,12 +303,16 @@ struct WarpEngine {
           sfb[mt] = valid ? e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t *>(sp + (g + 8) * SR)) : 0u;
         }
       }
+      uint4 xhs[4], xls[4];
 #pragma unroll
       for (int wd = 0; wd < 4; ++wd) {
-        // word wd = bytes 4wd..4wd+3 = columns col0+8wd.. = k-steps 2wd, 2wd+1;
-        // group 0 (the lane's first 16 columns) for words 0, 1
-        const uint4 xh = xload(xa, wd);
-        const uint4 xl = PACKED ? make_uint4(0u, 0u, 0u, 0u) : xload(xb, wd);
+        xhs[wd] = xload(xa, wd);
+        xls[wd] = PACKED ? make_uint4(0u, 0u, 0u, 0u) : xload(xb, wd);
+      }
+#pragma unroll
+      for (int wd = 0; wd < 4; ++wd) {
+        const uint4 xh = xhs[wd];
+        const uint4 xl = xls[wd];
         const uint32_t bh[4] = {xh.x, xh.y, xh.z, xh.w};
         const uint32_t bl[4] = {xl.x, xl.y, xl.z, xl.w};
 #pragma unroll

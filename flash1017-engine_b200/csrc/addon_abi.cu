@@ -62,6 +62,29 @@ struct Ctx {
   // pending accumulation of gx10_rust_*_mlp_accum / _mlp_batch
   float *pend_host = nullptr;
   size_t pend_n = 0;
+  // Routed calls not yet run: accumulating *_mlp_accum calls (x rows in bx)
+  // or *_mlp_batch calls (x rows in xall).  They run together as one routed
+  // layer (ffn::routed_calls) when the host needs `out`.
+  struct Call {
+    ffn_b200_expert e;
+    int32_t row0, m;
+    int32_t dst[8];  // out rows
+    float w[8];
+  };
+  std::vector<Call> queue;
+  int q_src = 0;  // 1: bx, 2: xall
+  size_t q_inter = 0, q_hidden = 0;
+  int q_out_rows = 0;
+  DevBuf bx;  // the queued *_mlp_accum calls' x rows
+  // pinned host stages of the call tables, reused once their upload is done
+  struct Stage {
+    void *h = nullptr;
+    size_t n = 0;
+    cudaEvent_t ev = nullptr;
+    bool used = false;
+  };
+  Stage stage[2];
+  int stage_i = 0;
   // batched-layer input x_all (ffn_b200_set_batch_input)
   const float *xall_host = nullptr;
   size_t xall_tok = 0, xall_hidden = 0;
@@ -115,7 +138,85 @@ int dev_ptr(Ctx &c, const void *hp, size_t n, const void **out) {
   return 0;
 }
 
+int stage_get(Ctx &c, size_t bytes, void **out) {
+  Ctx::Stage &s = c.stage[c.stage_i];
+  if (s.used) {
+    cudaError_t e = cudaEventSynchronize(s.ev);  // its previous upload has been read
+    if (e != cudaSuccess) return cuda_fail(e, "call-table stage wait");
+    s.used = false;
+  }
+  if (!s.ev) FFN_CUDA_TRY(cudaEventCreateWithFlags(&s.ev, cudaEventDisableTiming));
+  if (bytes > s.n) {
+    if (s.h) cudaFreeHost(s.h);
+    s.h = nullptr;
+    s.n = 0;
+    const size_t want = std::max<size_t>(bytes, 64 << 10);
+    FFN_CUDA_TRY(cudaHostAlloc(&s.h, want, cudaHostAllocDefault));
+    s.n = want;
+  }
+  *out = s.h;
+  return 0;
+}
+
+// Run the queued routed calls (in call order) into c.out.
+int run_queue(Ctx &c) {
+  if (c.queue.empty()) return 0;
+  const int n = (int)c.queue.size(), R = c.q_out_rows;
+  std::vector<ffn_b200_expert> es(n);
+  std::vector<int32_t> row0(n), m(n), tok_ptr((size_t)R + 1, 0), pair, cur;
+  std::vector<float> wts;
+  int P = 0;
+  for (int k = 0; k < n; ++k) {
+    const Ctx::Call &q = c.queue[k];
+    es[k] = q.e;
+    row0[k] = q.row0;
+    m[k] = q.m;
+    for (int j = 0; j < q.m; ++j) ++tok_ptr[q.dst[j] + 1];
+    P += q.m;
+  }
+  for (int r = 0; r < R; ++r) tok_ptr[r + 1] += tok_ptr[r];
+  // combine list per out row, entries in call order
+  pair.resize(P);
+  wts.resize(P);
+  cur.assign(tok_ptr.begin(), tok_ptr.end() - 1);
+  for (int k = 0, pos = 0; k < n; ++k)
+    for (int j = 0; j < c.queue[k].m; ++j, ++pos) {
+      const int e = cur[c.queue[k].dst[j]]++;
+      pair[e] = pos;
+      wts[e] = c.queue[k].w[j];
+    }
+  const bool from_bx = c.q_src == 1;
+  c.queue.clear();
+  ffn::RoutedCalls q{};
+  q.experts = es.data();
+  q.row0 = row0.data();
+  q.m = m.data();
+  q.n = n;
+  q.tok_ptr = tok_ptr.data();
+  q.ent_pair = pair.data();
+  q.ent_w = wts.data();
+  q.out_rows = R;
+  q.x = (const float *)(from_bx ? c.bx.p : c.xall.p);
+  q.x_rows = from_bx ? n : (int)c.xall_tok;
+  q.out = (float *)c.out.p;
+  int rc = c.ws.ensure(ffn::routed_calls_ws_bytes(c.q_inter, c.q_hidden, n, q.x_rows, R));
+  void *h = nullptr;
+  if (!rc) rc = stage_get(c, ffn::routed_calls_stage_bytes(n, R), &h);
+  if (!rc) {
+    rc = ffn::routed_calls(q, c.q_inter, c.q_hidden, h, c.ws.p, c.ws.n, c.st);
+    Ctx::Stage &s = c.stage[c.stage_i];
+    if (cudaEventRecord(s.ev, c.st) == cudaSuccess) s.used = true;
+    c.stage_i ^= 1;
+  }
+  return rc;
+}
+
 int flush_pending(Ctx &c) {
+  if (int rc = run_queue(c)) {
+    c.pend_host = nullptr;
+    c.pend_n = 0;
+    return rc;
+  }
   if (!c.pend_host) return 0;
   cudaError_t e = cudaMemcpyAsync(c.pend_host, c.out.p, c.pend_n * sizeof(float),
                                   cudaMemcpyDeviceToHost, c.st);
@@ -345,32 +446,69 @@ int resolve_expert(Ctx &c, ffn_b200_expert &e, size_t inter, size_t hidden) {
   return 0;
 }
 
+// Queue one routed call (the caller holds the lock and has made c.out the
+// call's target); the queue runs when it is full.
+int enqueue(Ctx &c, const ffn_b200_expert &e, int src, size_t inter, size_t hidden, int out_rows,
+            int32_t row0, int32_t m, const int32_t *dst, const float *w) {
+  Ctx::Call q{};
+  q.e = e;
+  q.row0 = row0;
+  q.m = m;
+  for (int j = 0; j < m; ++j) {
+    q.dst[j] = dst[j];
+    q.w[j] = w[j];
+  }
+  c.queue.push_back(q);
+  c.q_src = src;
+  c.q_inter = inter;
+  c.q_hidden = hidden;
+  c.q_out_rows = out_rows;
+  return c.queue.size() == (size_t)ffn::kCallsMax ? run_queue(c) : 0;
+}
+
 // Shared by the *_mlp_accum entry points: x is one token, out [hidden].
+// Accumulating calls on NVFP4, MXFP4 and ternary experts are queued and run
+// together (one routed layer, calls in order) when the host needs `out`
+// (sync_now, another target, another entry point); an overwriting call
+// (accumulate = false) or an MXFP8 expert runs at once, after the queue.
 bool mlp_accum(const ffn_b200_expert &he, size_t inter, size_t hidden, const float *x, float *out,
                float w, bool accumulate, bool sync_now) {
   Ctx &c = ctx();
   std::lock_guard<std::mutex> lk(c.mu);
   int rc = ensure_init(c);
   if (!rc && (!x || !out)) rc = fail(FFN_B200_EINVAL, "mlp_accum: null x/out");
-  // A new target flushes the previous pending one.
+  // A new target flushes the previous pending one (and its queued calls).
   if (!rc && c.pend_host && (c.pend_host != out || c.pend_n != hidden)) rc = flush_pending(c);
+  if (!rc && !c.queue.empty() && (c.q_src != 1 || c.q_inter != inter || c.q_hidden != hidden))
+    rc = run_queue(c);
   if (!rc) rc = c.x.ensure(hidden * 4);
   if (!rc) rc = c.out.ensure(hidden * 4);
   if (!rc) rc = c.ws.ensure(ffn_b200_expert_ws_bytes(inter, hidden, 1));
+  if (!rc) rc = c.bx.ensure((size_t)ffn::kCallsMax * hidden * 4);
   ffn_b200_expert e = he;
   if (!rc) rc = resolve_expert(c, e, inter, hidden);
+  const bool queue = accumulate && e.format != FFN_B200_FMT_MXFP8;
   if (!rc && accumulate && !c.pend_host) {
     // accumulate onto the host's current contents
     cudaError_t er = cudaMemcpyAsync(c.out.p, out, hidden * 4, cudaMemcpyHostToDevice, c.st);
     if (er != cudaSuccess) rc = cuda_fail(er, "out upload");
   }
-  if (!rc) {
-    cudaError_t er = cudaMemcpyAsync(c.x.p, x, hidden * 4, cudaMemcpyHostToDevice, c.st);
+  if (!rc && queue) {
+    const int32_t k = (int32_t)c.queue.size(), dst0 = 0;
+    cudaError_t er = cudaMemcpyAsync((float *)c.bx.p + (size_t)k * hidden, x, hidden * 4,
+                                     cudaMemcpyHostToDevice, c.st);
     if (er != cudaSuccess) rc = cuda_fail(er, "x upload");
+    if (!rc) rc = enqueue(c, e, 1, inter, hidden, 1, k, 1, &dst0, &w);
+  } else if (!rc) {
+    rc = run_queue(c);  // queued calls come first
+    if (!rc) {
+      cudaError_t er = cudaMemcpyAsync(c.x.p, x, hidden * 4, cudaMemcpyHostToDevice, c.st);
+      if (er != cudaSuccess) rc = cuda_fail(er, "x upload");
+    }
+    if (!rc)
+      rc = ffn_b200_expert_forward(inter, hidden, 1, &e, (const float *)c.x.p, (float *)c.out.p, w,
+                                   accumulate ? 1 : 0, c.ws.p, c.ws.n, c.st);
   }
-  if (!rc)
-    rc = ffn_b200_expert_forward(inter, hidden, 1, &e, (const float *)c.x.p, (float *)c.out.p, w,
-                                 accumulate ? 1 : 0, c.ws.p, c.ws.n, c.st);
   if (!rc) {
     c.pend_host = out;
     c.pend_n = hidden;
@@ -378,6 +516,7 @@ bool mlp_accum(const ffn_b200_expert &he, size_t inter, size_t hidden, const flo
   }
   if (rc) {
     std::fprintf(stderr, "[ffn_b200] %s\n", ffn_b200_last_error());
+    c.queue.clear();
     c.pend_host = nullptr;
     c.pend_n = 0;
     return false;
@@ -385,56 +524,58 @@ bool mlp_accum(const ffn_b200_expert &he, size_t inter, size_t hidden, const flo
   return true;
 }
 
-bool mlp_batch(const ffn_b200_expert &he, size_t inter, size_t hidden, size_t m, size_t x_off,
-               const size_t *dst, const float *dw, size_t b_len, float *out, bool sync_now) {
+// Upload the host's x_all rows if they are not on the device yet.
+int ensure_xall(Ctx &c) {
+  if (c.xall_dev_valid) return 0;
+  int rc = c.xall.ensure(c.xall_tok * c.xall_hidden * 4);
+  if (rc) return rc;
+  cudaError_t er = cudaMemcpyAsync(c.xall.p, c.xall_host, c.xall_tok * c.xall_hidden * 4,
+                                   cudaMemcpyHostToDevice, c.st);
+  if (er != cudaSuccess) return cuda_fail(er, "x_all upload");
+  c.xall_dev_valid = true;
+  return 0;
+}
+
+// Shared by the *_mlp_batch entry points (HA:441-479, call site
+// flash1017.rs:8193-8262): expert(x_all rows x_off .. x_off + m - 1), row k
+// added to out_batch row dst[k] with weight wscale * dw[k].  The calls are
+// queued (one routed layer at sync_now).  wscale is the ternary proj_scale:
+// the host passes unscaled weights here, and its CPU twin adds weight * sc
+// (flash1017.rs:8317-8321).
+bool mlp_batch(const ffn_b200_expert &he, float wscale, size_t inter, size_t hidden, size_t m,
+               size_t x_off, const size_t *dst, const float *dw, size_t b_len, float *out,
+               bool sync_now) {
   Ctx &c = ctx();
   std::lock_guard<std::mutex> lk(c.mu);
   int rc = ensure_init(c);
   if (!rc && (!dst || !dw || !out)) rc = fail(FFN_B200_EINVAL, "mlp_batch: null pointer");
   if (!rc && (!c.xall_host || c.xall_hidden != hidden || x_off + m > c.xall_tok))
-    rc = fail(FFN_B200_EINVAL, "mlp_batch: x rows outside the ffn_b200_set_batch_input buffer");
+    rc = fail(FFN_B200_EINVAL, "mlp_batch: x rows outside the x_all of the layer's mxfp8_mlp_batch call");
   if (!rc && (m == 0 || m > 8)) rc = fail(FFN_B200_EINVAL, "mlp_batch: 1..8 tokens per call");
+  if (!rc && (b_len == 0 || b_len > 65535)) rc = fail(FFN_B200_EINVAL, "mlp_batch: b_len must be 1..65535");
   for (size_t k = 0; !rc && k < m; ++k)
     if (dst[k] >= b_len) rc = fail(FFN_B200_EINVAL, "mlp_batch: destination token out of range");
   if (!rc && c.pend_host && (c.pend_host != out || c.pend_n != b_len * hidden)) rc = flush_pending(c);
-  const size_t ews = ffn_b200_expert_ws_bytes(inter, hidden, m);
+  if (!rc && !c.queue.empty() && (c.q_src != 2 || c.q_inter != inter || c.q_hidden != hidden))
+    rc = run_queue(c);
   if (!rc) rc = c.out.ensure(b_len * hidden * 4);
-  if (!rc) rc = c.ws.ensure(ews + 256 + m * hidden * 4);
-  if (!rc) rc = c.tmp.ensure(1024);
-  if (!rc && !c.xall_dev_valid) {
-    rc = c.xall.ensure(c.xall_tok * hidden * 4);
-    if (!rc) {
-      cudaError_t er = cudaMemcpyAsync(c.xall.p, c.xall_host, c.xall_tok * hidden * 4,
-                                       cudaMemcpyHostToDevice, c.st);
-      if (er != cudaSuccess) rc = cuda_fail(er, "x_all upload");
-      else c.xall_dev_valid = true;
-    }
-  }
+  if (!rc) rc = ensure_xall(c);
   ffn_b200_expert e = he;
   if (!rc) rc = resolve_expert(c, e, inter, hidden);
+  if (!rc && e.format == FFN_B200_FMT_MXFP8) rc = fail(FFN_B200_EINVAL, "mlp_batch: MXFP8 expert");
   if (!rc && !c.pend_host) {
     cudaError_t er = cudaMemcpyAsync(c.out.p, out, b_len * hidden * 4, cudaMemcpyHostToDevice, c.st);
     if (er != cudaSuccess) rc = cuda_fail(er, "out_batch upload");
   }
-  // expert outputs y [m, hidden] land after the expert workspace
-  float *y = (float *)((char *)c.ws.p + ((ews + 255) & ~(size_t)255));
   if (!rc) {
-    int64_t d64[8];
+    int32_t d32[8];
     float w8[8];
-    for (size_t k = 0; k < m; ++k) { d64[k] = (int64_t)dst[k]; w8[k] = dw[k]; }
-    cudaError_t er = cudaMemcpyAsync(c.tmp.p, d64, m * 8, cudaMemcpyHostToDevice, c.st);
-    if (er == cudaSuccess)
-      er = cudaMemcpyAsync((char *)c.tmp.p + 512, w8, m * 4, cudaMemcpyHostToDevice, c.st);
-    // the copies read these stack arrays: wait for them before they go out of scope
-    if (er == cudaSuccess) er = cudaStreamSynchronize(c.st);
-    if (er != cudaSuccess) rc = cuda_fail(er, "dst upload");
+    for (size_t k = 0; k < m; ++k) {
+      d32[k] = (int32_t)dst[k];
+      w8[k] = dw[k] * wscale;
+    }
+    rc = enqueue(c, e, 2, inter, hidden, (int)b_len, (int32_t)x_off, (int32_t)m, d32, w8);
   }
-  if (!rc)
-    rc = ffn_b200_expert_forward(inter, hidden, m, &e, (const float *)c.xall.p + x_off * hidden, y,
-                                 1.0f, 0, c.ws.p, ews, c.st);
-  if (!rc)
-    rc = launch_scatter_axpy(y, (const int64_t *)c.tmp.p, (const float *)((char *)c.tmp.p + 512),
-                             (int)m, (int)hidden, (float *)c.out.p, c.st);
   if (!rc) {
     c.pend_host = out;
     c.pend_n = b_len * hidden;
@@ -442,6 +583,7 @@ bool mlp_batch(const ffn_b200_expert &he, size_t inter, size_t hidden, size_t m,
   }
   if (rc) {
     std::fprintf(stderr, "[ffn_b200] %s\n", ffn_b200_last_error());
+    c.queue.clear();
     c.pend_host = nullptr;
     c.pend_n = 0;
     return false;
@@ -583,7 +725,7 @@ bool gx10_rust_nvfp4_mlp_batch(size_t inter_rows, size_t hidden_cols, size_t seq
                                bool sync_now) {
   const ffn_b200_expert e =
       nvfp4_expert(w1_fp4, w1_s, w1_sc2, w3_fp4, w3_s, w3_sc2, w2_fp4, w2_s, w2_sc2);
-  return mlp_batch(e, inter_rows, hidden_cols, seq_len, x_tok_offset, dst_tok_indices,
+  return mlp_batch(e, 1.0f, inter_rows, hidden_cols, seq_len, x_tok_offset, dst_tok_indices,
                    dst_weights, b_len, out_batch, sync_now);
 }
 
@@ -594,8 +736,63 @@ bool gx10_rust_ternary_158_mlp_batch(size_t inter_rows, size_t hidden_cols, size
                                      const size_t *dst_tok_indices, const float *dst_weights,
                                      size_t b_len, float *out_batch, bool sync_now) {
   const ffn_b200_expert e = ternary_expert(w1_p, w1_s, w3_p, w3_s, w2_p, w2_s, proj_scale);
-  return mlp_batch(e, inter_rows, hidden_cols, seq_len, x_tok_offset, dst_tok_indices,
+  return mlp_batch(e, proj_scale, inter_rows, hidden_cols, seq_len, x_tok_offset, dst_tok_indices,
                    dst_weights, b_len, out_batch, sync_now);
+}
+
+bool gx10_rust_mxfp8_mlp_batch(size_t inter_rows, size_t hidden_cols, size_t seq_len,
+                               const uint8_t *w1_w, const uint8_t *w1_s, const uint8_t *w3_w,
+                               const uint8_t *w3_s, const uint8_t *w2_w, const uint8_t *w2_s,
+                               const float *x_all, size_t x_total_tokens, float *out_batch,
+                               bool sync_now) {
+  Ctx &c = ctx();
+  std::lock_guard<std::mutex> lk(c.mu);
+  int rc = ensure_init(c);
+  const size_t b_len = seq_len, H = hidden_cols, I = inter_rows;
+  if (!rc && (seq_len >> 31))
+    rc = fail(FFN_B200_EUNSUP,
+              "mxfp8_mlp_batch: the NVFP4 q4-backbone shared expert (seq_len bit 31) is not supported");
+  if (!rc && (!x_all || !out_batch)) rc = fail(FFN_B200_EINVAL, "mxfp8_mlp_batch: null x_all/out_batch");
+  if (!rc && (b_len == 0 || b_len > 65535 || b_len > x_total_tokens || x_total_tokens > (1u << 20)))
+    rc = fail(FFN_B200_EINVAL, "mxfp8_mlp_batch: need 1 <= seq_len <= min(x_total_tokens, 65535)");
+  if (!rc) rc = flush_pending(c);  // a new layer: earlier work first
+  if (!rc) {
+    // x_all also holds the rows of this layer's routed *_mlp_batch calls
+    c.xall_host = x_all;
+    c.xall_tok = x_total_tokens;
+    c.xall_hidden = H;
+    c.xall_dev_valid = false;
+    rc = ensure_xall(c);
+  }
+  ffn_b200_expert e{};
+  e.format = FFN_B200_FMT_MXFP8;
+  e.proj_scale = 1.0f;
+  const uint8_t *w[3] = {w1_w, w3_w, w2_w}, *sc[3] = {w1_s, w3_s, w2_s};
+  for (int i = 0; i < 3; ++i) {
+    const size_t r = i == 2 ? H : I, k = i == 2 ? I : H;
+    e.nv[i].w = w[i];
+    e.nv[i].s = sc[i];
+    e.nv[i].gs = sc[i] ? mxfp8_gs(sc[i], ((r + 31) / 32) * ((k + 31) / 32)) : 1.0f;
+  }
+  if (!rc) rc = resolve_expert(c, e, I, H);
+  if (!rc) rc = c.out.ensure(b_len * H * 4);
+  if (!rc) rc = c.ws.ensure(ffn_b200_expert_ws_bytes(I, H, b_len));
+  if (!rc)
+    rc = ffn_b200_expert_forward(I, H, b_len, &e, (const float *)c.xall.p, (float *)c.out.p, 1.0f, 0,
+                                 c.ws.p, c.ws.n, c.st);
+  if (!rc) {
+    c.pend_host = out_batch;
+    c.pend_n = b_len * H;
+    if (sync_now) rc = flush_pending(c);
+  }
+  if (rc) {
+    std::fprintf(stderr, "[ffn_b200] %s\n", ffn_b200_last_error());
+    c.queue.clear();
+    c.pend_host = nullptr;
+    c.pend_n = 0;
+    return false;
+  }
+  return true;
 }
 
 void gx10_rust_register_host_range(const void *ptr, size_t bytes) {
@@ -618,6 +815,10 @@ void gx10_rust_register_shard_bounds(const void *ptr, size_t bytes) {
 int ffn_b200_set_batch_input(const float *x_all_host, size_t x_total_tokens, size_t hidden) {
   Ctx &c = ctx();
   std::lock_guard<std::mutex> lk(c.mu);
+  // queued *_mlp_batch calls read the current device copy of x_all
+  if (c.q_src == 2) {
+    if (int rc = run_queue(c)) return rc;
+  }
   c.xall_host = x_all_host;
   c.xall_tok = x_total_tokens;
   c.xall_hidden = hidden;

@@ -3,6 +3,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -628,6 +629,213 @@ size_t ffn_b200_moe_ws_bytes(const ffn_b200_moe_desc *d, size_t max_tokens) {
   return c.off + 256;
 }
 
+// The GEMV path's experts of a routed layer: per format, [rank-16 core z,]
+// gate/up + SwiGLU -> h, [core z of h,] down -> y [pair][H] (unweighted).
+// w.pair_tok / w.vexp_* / w.n_vexp come from launch_group.
+static int moe_gemv_experts(const ffn_b200_moe_desc *d, MoeWs &w, int P, const float *xin,
+                            cudaStream_t st) {
+  const size_t H = d->hidden, I = d->inter;
+  int rc;
+  // Upper bound of slices per format (the device count is <= this).
+  const int e_local = d->expert_end - d->expert_begin;
+  const long long max_vexp = std::min<long long>((long long)P, (long long)P / kNTok + e_local);
+  for (int f = 0; f < 2; ++f) {
+    const int fmt = f == 0 ? FFN_B200_FMT_NVFP4 : FFN_B200_FMT_TERNARY;
+    if ((fmt == FFN_B200_FMT_NVFP4 && !d->has_nvfp4) || (fmt == FFN_B200_FMT_TERNARY && !d->has_ternary))
+      continue;
+    const VExp *vl = f == 0 ? w.vexp_nv : w.vexp_tn;
+    const int *nvd = w.n_vexp + f;
+    const bool tern = fmt == FFN_B200_FMT_TERNARY;
+    if (tern) {
+      CoreZArgs z{};
+      z.experts = d->experts;
+      z.vexp = vl;
+      z.n_vexp_dev = nvd;
+      z.K = (int)H;
+      z.mat0 = 0;
+      z.nmat = 2;
+      z.xf = xin;
+      z.ld_xf = (int)H;
+      z.pair_tok = w.pair_tok;
+      z.z = w.z;
+      if ((rc = launch_corez(z, (int)max_vexp, st))) return rc;
+    }
+    PhaseArgs p{};
+    p.experts = d->experts;
+    p.vexp = vl;
+    p.n_vexp_dev = nvd;
+    p.rows = (int)I;
+    p.K = (int)H;
+    p.blocks = (int)((I + rows_per_tile(1) - 1) / rows_per_tile(1));
+    p.xh = tern ? w.th : w.xh;
+    p.xl = tern ? w.tl : w.xl;
+    p.xe = w.xe;
+    p.ld_x = (int)H;
+    p.pair_tok = w.pair_tok;
+    p.z = w.z;
+    p.hh = w.hh;
+    p.hl = w.hl;
+    p.ld_h = (int)I;
+    if ((rc = launch_phase(fmt, 1, p, max_vexp * p.blocks, st))) return rc;
+    if (tern) {
+      CoreZArgs z{};
+      z.experts = d->experts;
+      z.vexp = vl;
+      z.n_vexp_dev = nvd;
+      z.K = (int)I;
+      z.mat0 = 2;
+      z.nmat = 1;
+      z.hh = w.hh;
+      z.hl = w.hl;
+      z.ld_h = (int)I;
+      z.z = w.z;
+      if ((rc = launch_corez(z, (int)max_vexp, st))) return rc;
+    }
+    PhaseArgs q{};
+    q.experts = d->experts;
+    q.vexp = vl;
+    q.n_vexp_dev = nvd;
+    q.rows = (int)H;
+    q.K = (int)I;
+    q.blocks = (int)((H + rows_per_tile(2) - 1) / rows_per_tile(2));
+    q.xh = w.hh;
+    q.xl = w.hl;
+    q.xe = nullptr;
+    q.ld_x = (int)I;
+    q.z = w.z;
+    q.y = w.y;
+    q.ld_y = (int)H;
+    if ((rc = launch_phase(fmt, 2, q, max_vexp * q.blocks, st))) return rc;
+  }
+  return 0;
+}
+
+// ----------------------------------------------------- queued routed calls
+static ffn_b200_moe_desc calls_desc(size_t inter, size_t hidden, int n, bool nv, bool tern, bool mx) {
+  ffn_b200_moe_desc d{};
+  d.hidden = hidden;
+  d.inter = inter;
+  d.n_experts = (size_t)n;
+  d.top_k = 1;
+  d.expert_begin = 0;
+  d.expert_end = n;
+  d.has_nvfp4 = nv ? 1 : 0;
+  d.has_ternary = tern ? 1 : 0;
+  d.has_mxfp4 = mx ? 1 : 0;
+  d.path = FFN_B200_PATH_GEMV;
+  return d;
+}
+
+}  // extern "C"
+
+namespace {
+// Byte offsets of the call tables, the same in the host stage and in the
+// device copy (one upload).
+struct CallTables {
+  size_t experts, pair_tok, vexp_nv, vexp_tn, n_vexp, tok_ptr, ent_pair, ent_w, total;
+};
+CallTables call_tables(int n, int out_rows) {
+  const size_t P = (size_t)n * kNTok;  // upper bound of the pairs
+  CallTables t{};
+  size_t o = 0;
+  auto take = [&o](size_t bytes) {
+    const size_t at = o;
+    o = (o + bytes + 15) & ~(size_t)15;
+    return at;
+  };
+  t.experts = take((size_t)n * sizeof(ffn_b200_expert));
+  t.pair_tok = take(P * 4);
+  t.vexp_nv = take((size_t)n * sizeof(VExp));  // one slice per call (m <= kNTok)
+  t.vexp_tn = take((size_t)n * sizeof(VExp));
+  t.n_vexp = take(4 * sizeof(int));
+  t.tok_ptr = take(((size_t)out_rows + 1) * 4);
+  t.ent_pair = take(P * 4);
+  t.ent_w = take(P * 4);
+  t.total = o;
+  return t;
+}
+}  // namespace
+
+size_t ffn::routed_calls_stage_bytes(int n, int out_rows) { return call_tables(n, out_rows).total; }
+
+size_t ffn::routed_calls_ws_bytes(size_t inter, size_t hidden, int n, int x_rows, int out_rows) {
+  const ffn_b200_moe_desc d = calls_desc(inter, hidden, n, true, true, true);
+  const size_t rows = std::max<size_t>((size_t)x_rows, (size_t)n * kNTok);
+  return ((call_tables(n, out_rows).total + 255) & ~(size_t)255) + ffn_b200_moe_ws_bytes(&d, rows);
+}
+
+int ffn::routed_calls(const RoutedCalls &q, size_t inter, size_t hidden, void *stage, void *ws,
+                      size_t ws_bytes, cudaStream_t st) {
+  const int n = q.n;
+  if (n <= 0) return 0;
+  if (n > kCallsMax) return fail(FFN_B200_EINVAL, "routed calls: too many calls");
+  if (!q.experts || !q.row0 || !q.m || !q.tok_ptr || !q.ent_pair || !q.ent_w || !q.x || !q.out || !stage)
+    return fail(FFN_B200_EINVAL, "routed calls: null pointer");
+  if (q.out_rows <= 0 || q.x_rows <= 0) return fail(FFN_B200_EINVAL, "routed calls: no rows");
+  bool nv = false, tern = false, mx = false;
+  int P = 0, rc;
+  for (int c = 0; c < n; ++c) {
+    const ffn_b200_expert &e = q.experts[c];
+    if ((rc = check_expert(e, inter, hidden, "routed calls"))) return rc;
+    if (e.format == FFN_B200_FMT_MXFP8)
+      return fail(FFN_B200_EINVAL, "routed calls: MXFP8 experts run one by one");
+    if (q.m[c] < 1 || q.m[c] > kNTok || q.row0[c] < 0 || q.row0[c] + q.m[c] > q.x_rows)
+      return fail(FFN_B200_EINVAL, "routed calls: a call's x rows are out of range");
+    tern = tern || e.format == FFN_B200_FMT_TERNARY;
+    mx = mx || e.format == FFN_B200_FMT_MXFP4;
+    nv = nv || e.format != FFN_B200_FMT_TERNARY;
+    P += q.m[c];
+  }
+  if (q.tok_ptr[0] != 0 || q.tok_ptr[q.out_rows] != P)
+    return fail(FFN_B200_EINVAL, "routed calls: the combine list must hold every pair once");
+  for (int r = 0; r < q.out_rows; ++r)
+    if (q.tok_ptr[r + 1] < q.tok_ptr[r]) return fail(FFN_B200_EINVAL, "routed calls: tok_ptr decreases");
+  for (int e = 0; e < P; ++e)
+    if (q.ent_pair[e] < 0 || q.ent_pair[e] >= P) return fail(FFN_B200_EINVAL, "routed calls: bad pair");
+  if (ws_bytes < routed_calls_ws_bytes(inter, hidden, n, q.x_rows, q.out_rows))
+    return fail(FFN_B200_ENOSPC, "routed calls: workspace too small");
+  // host tables: slices (one per call), pair -> x row, the combine list
+  const CallTables t = call_tables(n, q.out_rows);
+  char *h = (char *)stage;
+  std::memcpy(h + t.experts, q.experts, (size_t)n * sizeof(ffn_b200_expert));
+  int32_t *pair_tok = (int32_t *)(h + t.pair_tok);
+  VExp *vnv = (VExp *)(h + t.vexp_nv), *vtn = (VExp *)(h + t.vexp_tn);
+  int *nvx = (int *)(h + t.n_vexp);
+  nvx[0] = nvx[1] = nvx[2] = nvx[3] = 0;
+  for (int c = 0, pos = 0; c < n; ++c) {
+    for (int j = 0; j < q.m[c]; ++j) pair_tok[pos + j] = q.row0[c] + j;
+    const bool is_tn = q.experts[c].format == FFN_B200_FMT_TERNARY;
+    VExp &v = is_tn ? vtn[nvx[1]++] : vnv[nvx[0]++];
+    v.expert = c;
+    v.offset = pos;
+    v.count = q.m[c];
+    v.pad = 0;
+    pos += q.m[c];
+  }
+  std::memcpy(h + t.tok_ptr, q.tok_ptr, ((size_t)q.out_rows + 1) * 4);
+  std::memcpy(h + t.ent_pair, q.ent_pair, (size_t)P * 4);
+  std::memcpy(h + t.ent_w, q.ent_w, (size_t)P * 4);
+  char *dt = (char *)ws;
+  FFN_CUDA_TRY(cudaMemcpyAsync(dt, h, t.total, cudaMemcpyHostToDevice, st));
+  ffn_b200_moe_desc d = calls_desc(inter, hidden, n, nv, tern, mx);
+  d.experts = (const ffn_b200_expert *)(dt + t.experts);
+  Carve cv(dt + ((t.total + 255) & ~(size_t)255));
+  MoeWs mw = carve_moe(cv, d, std::max<size_t>((size_t)q.x_rows, (size_t)P));
+  mw.pair_tok = (int32_t *)(dt + t.pair_tok);
+  mw.vexp_nv = (VExp *)(dt + t.vexp_nv);
+  mw.vexp_tn = (VExp *)(dt + t.vexp_tn);
+  mw.n_vexp = (int *)(dt + t.n_vexp);
+  const int H = (int)hidden;
+  if ((rc = launch_xprep(q.x, H, q.x_rows, H, nv ? mw.xh : nullptr, nv ? mw.xl : nullptr, mw.th, mw.tl, H,
+                         mw.xe, st)))
+    return rc;
+  if ((rc = moe_gemv_experts(&d, mw, P, q.x, st))) return rc;
+  return launch_rows_accum(mw.y, (const int32_t *)(dt + t.tok_ptr), (const int32_t *)(dt + t.ent_pair),
+                           (const float *)(dt + t.ent_w), q.out_rows, H, q.out, st);
+}
+
+extern "C" {
+
 int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
                        const float *residual, float *out, int32_t *topk_idx, float *topk_w,
                        void *ws, size_t ws_bytes, void *stream) {
@@ -706,77 +914,7 @@ int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
       FFN_CUDA_TRY(cudaMemcpyAsync(topk_w, w.wt, P * sizeof(float), cudaMemcpyDeviceToDevice, st));
     return 0;
   }
-  // Upper bound of slices per format (the device count is <= this).
-  const int e_local = d->expert_end - d->expert_begin;
-  const long long max_vexp = std::min<long long>((long long)P, (long long)P / kNTok + e_local);
-  for (int f = 0; f < 2; ++f) {
-    const int fmt = f == 0 ? FFN_B200_FMT_NVFP4 : FFN_B200_FMT_TERNARY;
-    if ((fmt == FFN_B200_FMT_NVFP4 && !d->has_nvfp4) || (fmt == FFN_B200_FMT_TERNARY && !d->has_ternary))
-      continue;
-    const VExp *vl = f == 0 ? w.vexp_nv : w.vexp_tn;
-    const int *nvd = w.n_vexp + f;
-    const bool tern = fmt == FFN_B200_FMT_TERNARY;
-    if (tern) {
-      CoreZArgs z{};
-      z.experts = d->experts;
-      z.vexp = vl;
-      z.n_vexp_dev = nvd;
-      z.K = (int)H;
-      z.mat0 = 0;
-      z.nmat = 2;
-      z.xf = xin;
-      z.ld_xf = (int)H;
-      z.pair_tok = w.pair_tok;
-      z.z = w.z;
-      if ((rc = launch_corez(z, (int)max_vexp, st))) return rc;
-    }
-    PhaseArgs p{};
-    p.experts = d->experts;
-    p.vexp = vl;
-    p.n_vexp_dev = nvd;
-    p.rows = (int)I;
-    p.K = (int)H;
-    p.blocks = (int)((I + rows_per_tile(1) - 1) / rows_per_tile(1));
-    p.xh = tern ? w.th : w.xh;
-    p.xl = tern ? w.tl : w.xl;
-    p.xe = w.xe;
-    p.ld_x = (int)H;
-    p.pair_tok = w.pair_tok;
-    p.z = w.z;
-    p.hh = w.hh;
-    p.hl = w.hl;
-    p.ld_h = (int)I;
-    if ((rc = launch_phase(fmt, 1, p, max_vexp * p.blocks, st))) return rc;
-    if (tern) {
-      CoreZArgs z{};
-      z.experts = d->experts;
-      z.vexp = vl;
-      z.n_vexp_dev = nvd;
-      z.K = (int)I;
-      z.mat0 = 2;
-      z.nmat = 1;
-      z.hh = w.hh;
-      z.hl = w.hl;
-      z.ld_h = (int)I;
-      z.z = w.z;
-      if ((rc = launch_corez(z, (int)max_vexp, st))) return rc;
-    }
-    PhaseArgs q{};
-    q.experts = d->experts;
-    q.vexp = vl;
-    q.n_vexp_dev = nvd;
-    q.rows = (int)H;
-    q.K = (int)I;
-    q.blocks = (int)((H + rows_per_tile(2) - 1) / rows_per_tile(2));
-    q.xh = w.hh;
-    q.xl = w.hl;
-    q.xe = nullptr;
-    q.ld_x = (int)I;
-    q.z = w.z;
-    q.y = w.y;
-    q.ld_y = (int)H;
-    if ((rc = launch_phase(fmt, 2, q, max_vexp * q.blocks, st))) return rc;
-  }
+  if ((rc = moe_gemv_experts(d, w, P, xin, st))) return rc;
   if ((rc = launch_combine(w.y, (int)H, w.idx, w.wt, w.inv, T, (int)k, d->experts, residual, out,
                            (int)H, st)))
     return rc;

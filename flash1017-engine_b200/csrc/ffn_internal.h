@@ -76,6 +76,36 @@ struct CoreZArgs {
 
 int rows_per_tile(int phase);
 int chunk_cols(int fmt);  // K columns per ring unit
+
+// A queue of routed expert calls run together as one routed layer.  Call c
+// applies experts[c] to the x rows row0[c] .. row0[c] + m[c] - 1 (1 <= m[c]
+// <= kNTok); its m[c] output rows are the pairs pos0[c] .. pos0[c] + m[c] - 1,
+// numbered in call order.  Output row r then receives, in list order,
+//   out[r] = fl(out[r] + fl(w[e] * y[pair[e]]))  for e in [tok_ptr[r], tok_ptr[r + 1]),
+// which is the one-call-at-a-time arithmetic when the list is in call order.
+// All arrays here are HOST arrays; experts hold device weight pointers.
+struct RoutedCalls {
+  const ffn_b200_expert *experts;
+  const int32_t *row0, *m;
+  int n;
+  const int32_t *tok_ptr;  // [out_rows + 1], tok_ptr[out_rows] = sum of m
+  const int32_t *ent_pair;
+  const float *ent_w;
+  int out_rows;
+  const float *x;  // device [x_rows][hidden]
+  int x_rows;
+  float *out;      // device [out_rows][hidden]
+};
+constexpr int kCallsMax = 64;  // calls per routed_calls run
+size_t routed_calls_ws_bytes(size_t inter, size_t hidden, int n, int x_rows, int out_rows);
+size_t routed_calls_stage_bytes(int n, int out_rows);
+// `stage`: routed_calls_stage_bytes of host memory for the call tables (pinned
+// or pageable), which the caller leaves untouched until the stream has passed
+// this point.
+int routed_calls(const RoutedCalls &q, size_t inter, size_t hidden, void *stage, void *ws,
+                 size_t ws_bytes, cudaStream_t st);
+int launch_rows_accum(const float *y, const int32_t *tok_ptr, const int32_t *ent_pair,
+                      const float *ent_w, int out_rows, int H, float *out, cudaStream_t st);
 int sm_count_of(int dev);  // multiprocessors of device `dev` (cached)
 int launch_xprep(const float *x, int ld_x, int rows, int K, __half *nh, __half *nl, __half *th,
                  __half *tl, int ld_o, int *xe, cudaStream_t st, const float *norm_w = nullptr,
@@ -96,8 +126,6 @@ int launch_combine(const float *y, int ld_y, const int32_t *idx, const float *wt
                    const int32_t *inv, int n_tok, int top_k, const ffn_b200_expert *experts,
                    const float *residual, float *out, int H, cudaStream_t st,
                    const int *err = nullptr);
-int launch_scatter_axpy(const float *y, const int64_t *dst, const float *w, int m, int H,
-                        float *out, cudaStream_t st);
 int launch_dot(int mode, const void *a, const void *aux, const float *x, size_t len, float *out,
                cudaStream_t st);
 int launch_gen_nvfp4(uint64_t kw, uint64_t ks, size_t rows, size_t cols, uint8_t *w, uint8_t *s,

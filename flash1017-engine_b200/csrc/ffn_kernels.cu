@@ -1303,23 +1303,46 @@ int launch_combine(const float *y, int ld_y, const int32_t *idx, const float *wt
   return 0;
 }
 
-// ============================================================ reference-ABI helpers
-// out[dst[k]] += w[k] * y[k] for k < m, in k order (flash1017.rs:8297-8303).
-__global__ void scatter_axpy_kernel(const float *__restrict__ y, const int64_t *__restrict__ dst,
-                                    const float *__restrict__ w, int m, int H, float *out) {
-  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < H; c += gridDim.x * blockDim.x)
-    for (int k = 0; k < m; ++k) {
-      float *o = out + (size_t)dst[k] * H + c;
-      *o = __fadd_rn(*o, __fmul_rn(w[k], y[(size_t)k * H + c]));
+// ============================================================ queued routed calls
+// out[r] += w[e] * y[pair[e]] for the entries of row r in
+// list order (call order), each term rounded as fl(out + fl(w * y)), as the
+// reference's per-call axpy does (flash1017.rs:4900-4905, 8297-8303).  Grid:
+// (column blocks, out rows); 4 columns per thread (hidden % 64 == 0).
+__global__ void __launch_bounds__(256) rows_accum_kernel(const float *__restrict__ y,
+                                                         const int32_t *__restrict__ tok_ptr,
+                                                         const int32_t *__restrict__ ent_pair,
+                                                         const float *__restrict__ ent_w, int H,
+                                                         float *out) {
+  pdl_enter();
+  const int r = blockIdx.y;
+  const int e0 = __ldg(tok_ptr + r), e1 = __ldg(tok_ptr + r + 1);
+  if (e0 == e1) return;
+  float4 *o4 = reinterpret_cast<float4 *>(out + (size_t)r * H);
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < H / 4; c += gridDim.x * blockDim.x) {
+    float4 acc = o4[c];
+    for (int e = e0; e < e1; ++e) {
+      const float w = __ldg(ent_w + e);
+      const float4 v = __ldg(reinterpret_cast<const float4 *>(y + (size_t)__ldg(ent_pair + e) * H) + c);
+      acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
     }
+    o4[c] = acc;
+  }
 }
-int launch_scatter_axpy(const float *y, const int64_t *dst, const float *w, int m, int H,
-                        float *out, cudaStream_t st) {
-  if (m <= 0) return 0;
-  FFN_LAUNCH(FFN_B200_K_OTHER, st, "scatter_axpy_kernel", scatter_axpy_kernel<<<(H + 255) / 256, 256, 0, st>>>(y, dst, w, m, H, out));
+
+int launch_rows_accum(const float *y, const int32_t *tok_ptr, const int32_t *ent_pair,
+                      const float *ent_w, int out_rows, int H, float *out, cudaStream_t st) {
+  if (out_rows <= 0) return 0;
+  if (H % 4) return fail(FFN_B200_EINVAL, "rows_accum: hidden must be a multiple of 4");
+  const dim3 grid((unsigned)((H / 4 + 255) / 256), (unsigned)out_rows);
+  FFN_LAUNCH_PDL(FFN_B200_K_COMBINE, st, "rows_accum_kernel", rows_accum_kernel, grid, 256, 0, y, tok_ptr,
+                 ent_pair, ent_w, H, out);
   return 0;
 }
 
+// ============================================================ reference-ABI helpers
 // Single-row dots of the V1 vtable slots (HA:150-159).  mode 0: f32 . f32,
 // 1: i8 . f32, 2: Q4_G32 (int4 - 8, bf16 scale per 32; twin HA:1159-1179),
 // 3: ternary 2-bit codes (no scale).  One CTA, fixed-order tree reduction.

@@ -39,7 +39,7 @@ EXPORTS = [
     "ffn_b200_ep_handle_bytes", "ffn_b200_ep_create", "ffn_b200_ep_connect", "ffn_b200_ep_part",
     "ffn_b200_ep_allreduce", "ffn_b200_ep_error", "ffn_b200_ep_destroy",
     "ffn_b200_mxfp4_matvec", "gx10_rust_mxfp4_matvec", "gx10_rust_mxfp4_mlp_accum",
-    "ffn_b200_mxfp8_matvec", "gx10_rust_mxfp8_mlp_accum",
+    "ffn_b200_mxfp8_matvec", "gx10_rust_mxfp8_mlp_accum", "gx10_rust_mxfp8_mlp_batch",
     "ffn_b200_st_open", "ffn_b200_st_close", "ffn_b200_st_count", "ffn_b200_st_name",
     "ffn_b200_st_find", "ffn_b200_st_expert_bytes", "ffn_b200_st_load_expert",
 ]
@@ -120,6 +120,21 @@ def lib() -> C.CDLL:
         L.gx10_rust_mxfp8_mlp_accum.argtypes = [sz, sz, vp, vp, vp, vp, vp, vp, vp, vp, f32,
                                                 C.c_bool, C.c_bool]
         L.gx10_rust_mxfp8_mlp_accum.restype = C.c_bool
+        L.gx10_rust_mxfp8_mlp_batch.argtypes = [sz, sz, sz, vp, vp, vp, vp, vp, vp, vp, sz, vp,
+                                                C.c_bool]
+        L.gx10_rust_mxfp8_mlp_batch.restype = C.c_bool
+        L.gx10_rust_nvfp4_mlp_accum.argtypes = [sz, sz, vp, vp, f32, vp, vp, f32, vp, vp, f32, vp,
+                                                vp, f32, C.c_bool, C.c_bool]
+        L.gx10_rust_nvfp4_mlp_accum.restype = C.c_bool
+        L.gx10_rust_ternary_158_mlp_accum.argtypes = [sz, sz, vp, vp, vp, vp, vp, vp, f32, vp, vp,
+                                                      f32, C.c_bool, C.c_bool]
+        L.gx10_rust_ternary_158_mlp_accum.restype = C.c_bool
+        L.gx10_rust_nvfp4_mlp_batch.argtypes = [sz, sz, sz, vp, vp, f32, vp, vp, f32, vp, vp, f32,
+                                                sz, vp, vp, sz, vp, C.c_bool]
+        L.gx10_rust_nvfp4_mlp_batch.restype = C.c_bool
+        L.gx10_rust_ternary_158_mlp_batch.argtypes = [sz, sz, sz, vp, vp, vp, vp, vp, vp, f32, sz,
+                                                      vp, vp, sz, vp, C.c_bool]
+        L.gx10_rust_ternary_158_mlp_batch.restype = C.c_bool
         L.ffn_b200_expert_ws_bytes.restype = sz
         L.ffn_b200_expert_ws_bytes.argtypes = [sz, sz, sz]
         L.ffn_b200_expert_forward.argtypes = [sz, sz, sz, C.POINTER(Expert), vp, vp, f32, i32,

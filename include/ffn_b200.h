@@ -328,8 +328,10 @@ FFN_B200_EXPORT int ffn_b200_st_load_expert(const ffn_b200_st *st, const char *p
                                             ffn_b200_expert *e);
 
 /* -------------------------------------------- reference-ABI support hooks
- * Host-side x_all buffer for gx10_rust_*_mlp_batch (the reference stages it
- * through the shared-expert call, flash1017.rs:8170-8186). */
+ * Host-side x_all buffer for gx10_rust_*_mlp_batch, for hosts that do not make
+ * the shared-expert call (gx10_rust_mxfp8_mlp_batch hands x_all over itself,
+ * as the reference does, flash1017.rs:8170-8186).  The rows are read when the
+ * first *_mlp_batch call needs them. */
 FFN_B200_EXPORT int ffn_b200_set_batch_input(const float *x_all_host, size_t x_total_tokens,
                                              size_t hidden);
 /* Drops every HBM weight copy made for host pointers. */

@@ -193,12 +193,27 @@ FFN_B200_EXPORT bool gx10_rust_ternary_158_mlp_accum(size_t inter_rows, size_t h
                                                      float *out, float accum_weight,
                                                      bool accumulate, bool sync_now);
 
+/* HA:425-439 (call site flash1017.rs:8146-8186, CPU twin :8268-8277): the
+ * batched layer's shared MXFP8 expert, out_batch[t] = expert(x_all[t]) for
+ * t < seq_len (overwrite), and the hand-over of x_all [x_total_tokens,
+ * hidden_cols], whose rows the layer's *_mlp_batch calls then read.  seq_len
+ * with bit 31 set (the NVFP4 q4-backbone shared expert, flash1017.rs:8148-8158)
+ * is not supported: false, and the host runs its CPU twin. */
+FFN_B200_EXPORT bool gx10_rust_mxfp8_mlp_batch(size_t inter_rows, size_t hidden_cols,
+                                               size_t seq_len, const uint8_t *w1_w,
+                                               const uint8_t *w1_s, const uint8_t *w3_w,
+                                               const uint8_t *w3_s, const uint8_t *w2_w,
+                                               const uint8_t *w2_s, const float *x_all,
+                                               size_t x_total_tokens, float *out_batch,
+                                               bool sync_now);
+
 /* HA:441-460 (call site flash1017.rs:8199-8223, CPU twin :8285-8303): one
  * expert over seq_len <= 8 tokens whose rows are x_all[x_tok_offset .. +seq_len]
  * of the batched layer's input; y_k is scatter-added as
  * out_batch[dst_tok_indices[k]] += dst_weights[k] * y_k.  out_batch is
- * [b_len, hidden_cols].  The reference hands x_all to the addon through its
- * shared-expert call; this backend takes it from ffn_b200_set_batch_input. */
+ * [b_len, hidden_cols].  x_all comes from the layer's gx10_rust_mxfp8_mlp_batch
+ * call (or ffn_b200_set_batch_input).  Calls are queued and run together as
+ * one routed layer when the host needs out_batch (sync_now). */
 FFN_B200_EXPORT bool gx10_rust_nvfp4_mlp_batch(size_t inter_rows, size_t hidden_cols,
                                                size_t seq_len, const uint8_t *w1_fp4,
                                                const uint8_t *w1_s, float w1_sc2,
@@ -210,7 +225,8 @@ FFN_B200_EXPORT bool gx10_rust_nvfp4_mlp_batch(size_t inter_rows, size_t hidden_
                                                const float *dst_weights, size_t b_len,
                                                float *out_batch, bool sync_now);
 
-/* HA:462-479 */
+/* HA:462-479.  The weights added are dst_weights[k] * proj_scale, the
+ * CPU twin's `weight * sc` (flash1017.rs:8317-8321). */
 FFN_B200_EXPORT bool gx10_rust_ternary_158_mlp_batch(size_t inter_rows, size_t hidden_cols,
                                                      size_t seq_len, const uint8_t *w1_p,
                                                      const float *w1_s, const uint8_t *w3_p,

@@ -38,6 +38,18 @@ def ffn():
     return ffn_b200
 
 
+@pytest.fixture(autouse=True)
+def _release_host_weight_copies(request):
+    """The reference ABI keeps one HBM copy per host weight range, valid while
+    the host keeps those weights alive (the reference's mmap'd shards live for
+    the whole process).  A test's numpy weights are freed when it ends, and a
+    later test's arrays can reuse their addresses, so the copies are dropped
+    after every GPU test."""
+    yield
+    if request.node.get_closest_marker("gpu") and "ffn_b200" in sys.modules:
+        sys.modules["ffn_b200"].lib().ffn_b200_release_host_ranges()
+
+
 @pytest.fixture(scope="session")
 def cuda():
     import torch

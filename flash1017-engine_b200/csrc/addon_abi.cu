@@ -85,6 +85,12 @@ struct Ctx {
   };
   Stage stage[2];
   int stage_i = 0;
+  // pinned host stages of the queued *_mlp_accum calls' x rows (one upload
+  // per run); a call whose x equals the previous staged row reuses it
+  Stage xstage[2];
+  int xstage_i = 0;
+  int q_xrows = 0;
+  bool q_zero = false;  // the queue began with an overwriting call
   // batched-layer input x_all (ffn_b200_set_batch_input)
   const float *xall_host = nullptr;
   size_t xall_tok = 0, xall_hidden = 0;
@@ -138,11 +144,11 @@ int dev_ptr(Ctx &c, const void *hp, size_t n, const void **out) {
   return 0;
 }
 
-int stage_get(Ctx &c, size_t bytes, void **out) {
-  Ctx::Stage &s = c.stage[c.stage_i];
+// Wait until the stage's last upload has been read, and give it `bytes`.
+int stage_ready(Ctx::Stage &s, size_t bytes) {
   if (s.used) {
-    cudaError_t e = cudaEventSynchronize(s.ev);  // its previous upload has been read
-    if (e != cudaSuccess) return cuda_fail(e, "call-table stage wait");
+    cudaError_t e = cudaEventSynchronize(s.ev);
+    if (e != cudaSuccess) return cuda_fail(e, "host stage wait");
     s.used = false;
   }
   if (!s.ev) FFN_CUDA_TRY(cudaEventCreateWithFlags(&s.ev, cudaEventDisableTiming));
@@ -154,8 +160,18 @@ int stage_get(Ctx &c, size_t bytes, void **out) {
     FFN_CUDA_TRY(cudaHostAlloc(&s.h, want, cudaHostAllocDefault));
     s.n = want;
   }
-  *out = s.h;
   return 0;
+}
+
+// The stage's upload has been issued on the stream.
+void stage_issued(Ctx &c, Ctx::Stage &s) {
+  if (cudaEventRecord(s.ev, c.st) == cudaSuccess) s.used = true;
+}
+
+void clear_queue(Ctx &c) {
+  c.queue.clear();
+  c.q_xrows = 0;
+  c.q_zero = false;
 }
 
 // Run the queued routed calls (in call order) into c.out.
@@ -186,7 +202,17 @@ int run_queue(Ctx &c) {
       wts[e] = c.queue[k].w[j];
     }
   const bool from_bx = c.q_src == 1;
-  c.queue.clear();
+  const int xrows = c.q_xrows;
+  const uint8_t zero = c.q_zero ? 1 : 0;
+  clear_queue(c);
+  if (from_bx) {
+    // the staged x rows, one pinned upload
+    Ctx::Stage &xs = c.xstage[c.xstage_i];
+    cudaError_t er = cudaMemcpyAsync(c.bx.p, xs.h, (size_t)xrows * c.q_hidden * 4, cudaMemcpyHostToDevice, c.st);
+    if (er != cudaSuccess) return cuda_fail(er, "x rows upload");
+    stage_issued(c, xs);
+    c.xstage_i ^= 1;
+  }
   ffn::RoutedCalls q{};
   q.experts = es.data();
   q.row0 = row0.data();
@@ -196,16 +222,16 @@ int run_queue(Ctx &c) {
   q.ent_pair = pair.data();
   q.ent_w = wts.data();
   q.out_rows = R;
+  q.row_zero = from_bx ? &zero : nullptr;  // accumulate mode: one out row
   q.x = (const float *)(from_bx ? c.bx.p : c.xall.p);
-  q.x_rows = from_bx ? n : (int)c.xall_tok;
+  q.x_rows = from_bx ? xrows : (int)c.xall_tok;
   q.out = (float *)c.out.p;
   int rc = c.ws.ensure(ffn::routed_calls_ws_bytes(c.q_inter, c.q_hidden, n, q.x_rows, R));
-  void *h = nullptr;
-  if (!rc) rc = stage_get(c, ffn::routed_calls_stage_bytes(n, R), &h);
+  Ctx::Stage &s = c.stage[c.stage_i];
+  if (!rc) rc = stage_ready(s, ffn::routed_calls_stage_bytes(n, R));
   if (!rc) {
-    rc = ffn::routed_calls(q, c.q_inter, c.q_hidden, h, c.ws.p, c.ws.n, c.st);
-    Ctx::Stage &s = c.stage[c.stage_i];
-    if (cudaEventRecord(s.ev, c.st) == cudaSuccess) s.used = true;
+    rc = ffn::routed_calls(q, c.q_inter, c.q_hidden, s.h, c.ws.p, c.ws.n, c.st);
+    stage_issued(c, s);
     c.stage_i ^= 1;
   }
   return rc;
@@ -466,11 +492,31 @@ int enqueue(Ctx &c, const ffn_b200_expert &e, int src, size_t inter, size_t hidd
   return c.queue.size() == (size_t)ffn::kCallsMax ? run_queue(c) : 0;
 }
 
-// Shared by the *_mlp_accum entry points: x is one token, out [hidden].
-// Accumulating calls on NVFP4, MXFP4 and ternary experts are queued and run
-// together (one routed layer, calls in order) when the host needs `out`
-// (sync_now, another target, another entry point); an overwriting call
-// (accumulate = false) or an MXFP8 expert runs at once, after the queue.
+// Stage one call's x row in the queue's pinned x stage; `row` = its index.
+int stage_x(Ctx &c, const float *x, size_t hidden, int32_t *row) {
+  Ctx::Stage &xs = c.xstage[c.xstage_i];
+  if (c.queue.empty()) {  // a new queue takes the next stage
+    c.q_xrows = 0;
+    if (int rc = stage_ready(xs, (size_t)ffn::kCallsMax * hidden * 4)) return rc;
+  }
+  float *rows = (float *)xs.h;
+  const size_t nb = hidden * 4;
+  if (c.q_xrows > 0 && std::memcmp(rows + (size_t)(c.q_xrows - 1) * hidden, x, nb) == 0) {
+    *row = c.q_xrows - 1;  // the same x as the previous call (the reference's routed calls)
+    return 0;
+  }
+  std::memcpy(rows + (size_t)c.q_xrows * hidden, x, nb);
+  *row = c.q_xrows++;
+  return 0;
+}
+
+// Shared by the *_mlp_accum entry points: x is one token, out [hidden].  Every
+// call is queued, and the queue runs as one routed layer (calls in order) when
+// the host needs `out`: sync_now, another target or dims, 64 calls, or another
+// entry point.  An overwriting call (accumulate = false) starts a new queue
+// whose output starts from zero; the reference's sequence per token (shared
+// expert overwriting, then the routed experts accumulating, sync on the last,
+// flash1017.rs:7401-7512) thus runs as one layer of 7 experts.
 bool mlp_accum(const ffn_b200_expert &he, size_t inter, size_t hidden, const float *x, float *out,
                float w, bool accumulate, bool sync_now) {
   Ctx &c = ctx();
@@ -479,35 +525,24 @@ bool mlp_accum(const ffn_b200_expert &he, size_t inter, size_t hidden, const flo
   if (!rc && (!x || !out)) rc = fail(FFN_B200_EINVAL, "mlp_accum: null x/out");
   // A new target flushes the previous pending one (and its queued calls).
   if (!rc && c.pend_host && (c.pend_host != out || c.pend_n != hidden)) rc = flush_pending(c);
-  if (!rc && !c.queue.empty() && (c.q_src != 1 || c.q_inter != inter || c.q_hidden != hidden))
+  if (!rc && !c.queue.empty() &&
+      (c.q_src != 1 || c.q_inter != inter || c.q_hidden != hidden || !accumulate))
     rc = run_queue(c);
-  if (!rc) rc = c.x.ensure(hidden * 4);
   if (!rc) rc = c.out.ensure(hidden * 4);
-  if (!rc) rc = c.ws.ensure(ffn_b200_expert_ws_bytes(inter, hidden, 1));
   if (!rc) rc = c.bx.ensure((size_t)ffn::kCallsMax * hidden * 4);
   ffn_b200_expert e = he;
   if (!rc) rc = resolve_expert(c, e, inter, hidden);
-  const bool queue = accumulate && e.format != FFN_B200_FMT_MXFP8;
   if (!rc && accumulate && !c.pend_host) {
     // accumulate onto the host's current contents
     cudaError_t er = cudaMemcpyAsync(c.out.p, out, hidden * 4, cudaMemcpyHostToDevice, c.st);
     if (er != cudaSuccess) rc = cuda_fail(er, "out upload");
   }
-  if (!rc && queue) {
-    const int32_t k = (int32_t)c.queue.size(), dst0 = 0;
-    cudaError_t er = cudaMemcpyAsync((float *)c.bx.p + (size_t)k * hidden, x, hidden * 4,
-                                     cudaMemcpyHostToDevice, c.st);
-    if (er != cudaSuccess) rc = cuda_fail(er, "x upload");
-    if (!rc) rc = enqueue(c, e, 1, inter, hidden, 1, k, 1, &dst0, &w);
-  } else if (!rc) {
-    rc = run_queue(c);  // queued calls come first
-    if (!rc) {
-      cudaError_t er = cudaMemcpyAsync(c.x.p, x, hidden * 4, cudaMemcpyHostToDevice, c.st);
-      if (er != cudaSuccess) rc = cuda_fail(er, "x upload");
-    }
-    if (!rc)
-      rc = ffn_b200_expert_forward(inter, hidden, 1, &e, (const float *)c.x.p, (float *)c.out.p, w,
-                                   accumulate ? 1 : 0, c.ws.p, c.ws.n, c.st);
+  int32_t row = 0;
+  const int32_t dst0 = 0;
+  if (!rc) rc = stage_x(c, x, hidden, &row);
+  if (!rc) {
+    if (!accumulate) c.q_zero = true;  // the queue is empty here: this is its first call
+    rc = enqueue(c, e, 1, inter, hidden, 1, row, 1, &dst0, &w);
   }
   if (!rc) {
     c.pend_host = out;
@@ -516,7 +551,7 @@ bool mlp_accum(const ffn_b200_expert &he, size_t inter, size_t hidden, const flo
   }
   if (rc) {
     std::fprintf(stderr, "[ffn_b200] %s\n", ffn_b200_last_error());
-    c.queue.clear();
+    clear_queue(c);
     c.pend_host = nullptr;
     c.pend_n = 0;
     return false;
@@ -583,7 +618,7 @@ bool mlp_batch(const ffn_b200_expert &he, float wscale, size_t inter, size_t hid
   }
   if (rc) {
     std::fprintf(stderr, "[ffn_b200] %s\n", ffn_b200_last_error());
-    c.queue.clear();
+    clear_queue(c);
     c.pend_host = nullptr;
     c.pend_n = 0;
     return false;
@@ -787,7 +822,7 @@ bool gx10_rust_mxfp8_mlp_batch(size_t inter_rows, size_t hidden_cols, size_t seq
   }
   if (rc) {
     std::fprintf(stderr, "[ffn_b200] %s\n", ffn_b200_last_error());
-    c.queue.clear();
+    clear_queue(c);
     c.pend_host = nullptr;
     c.pend_n = 0;
     return false;

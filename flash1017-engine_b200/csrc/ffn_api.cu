@@ -729,10 +729,22 @@ static ffn_b200_moe_desc calls_desc(size_t inter, size_t hidden, int n, bool nv,
 }  // extern "C"
 
 namespace {
+// Slice lists of queued calls, one per engine instance: 0 NVFP4 and MXFP4,
+// 1 ternary, 2 MXFP8.  Two phase launches per list, each with its own split
+// arrival counters.
+constexpr int kCallLists = 3;
+constexpr int kCallLaunches = 2 * kCallLists;
+int call_list(int format) {
+  return format == FFN_B200_FMT_TERNARY ? 1 : format == FFN_B200_FMT_MXFP8 ? 2 : 0;
+}
+int list_format(int l) {
+  return l == 0 ? FFN_B200_FMT_NVFP4 : l == 1 ? FFN_B200_FMT_TERNARY : FFN_B200_FMT_MXFP8;
+}
+
 // Byte offsets of the call tables, the same in the host stage and in the
-// device copy (one upload).
+// device copy (one upload; the split counters travel as zeros).
 struct CallTables {
-  size_t experts, pair_tok, vexp_nv, vexp_tn, n_vexp, tok_ptr, ent_pair, ent_w, total;
+  size_t experts, pair_tok, vexp[kCallLists], n_vexp, cnt, tok_ptr, ent_pair, ent_w, row_zero, total;
 };
 CallTables call_tables(int n, int out_rows) {
   const size_t P = (size_t)n * kNTok;  // upper bound of the pairs
@@ -745,14 +757,31 @@ CallTables call_tables(int n, int out_rows) {
   };
   t.experts = take((size_t)n * sizeof(ffn_b200_expert));
   t.pair_tok = take(P * 4);
-  t.vexp_nv = take((size_t)n * sizeof(VExp));  // one slice per call (m <= kNTok)
-  t.vexp_tn = take((size_t)n * sizeof(VExp));
+  for (int l = 0; l < kCallLists; ++l) t.vexp[l] = take((size_t)n * sizeof(VExp));  // one slice per call
   t.n_vexp = take(4 * sizeof(int));
+  t.cnt = take((size_t)kCallLaunches * kSplitItems * sizeof(int));
   t.tok_ptr = take(((size_t)out_rows + 1) * 4);
   t.ent_pair = take(P * 4);
   t.ent_w = take(P * 4);
+  t.row_zero = take((size_t)out_rows);
   t.total = o;
   return t;
+}
+
+// K-splits of a list-mode phase launch whose slices the host knows: the same
+// rule as plan_splits (one wave of warps, at most one split per ring unit,
+// partials within kSplitBytes).  pt = the largest slice.
+SplitPlan plan_list_splits(int fmt, int phase, size_t rows, size_t K, int n_slices, int pt) {
+  SplitPlan sp;
+  sp.tasks = (long long)n_slices * (long long)((rows + rows_per_tile(phase) - 1) / rows_per_tile(phase));
+  sp.pt = pt;
+  const long long nch = (long long)((K + chunk_cols(fmt) - 1) / chunk_cols(fmt));
+  const size_t per = (size_t)pt * rows_per_tile(phase) * (phase == 1 ? 2 : 1) * sizeof(float);
+  long long s = std::min<long long>(kSplitItems / sp.tasks, nch);
+  s = std::min<long long>(s, (long long)(kSplitBytes / ((size_t)sp.tasks * per)));
+  sp.splits = (int)std::max<long long>(1, s);
+  sp.part_bytes = sp.splits > 1 ? (size_t)sp.tasks * sp.splits * per : 0;
+  return sp;
 }
 }  // namespace
 
@@ -761,7 +790,8 @@ size_t ffn::routed_calls_stage_bytes(int n, int out_rows) { return call_tables(n
 size_t ffn::routed_calls_ws_bytes(size_t inter, size_t hidden, int n, int x_rows, int out_rows) {
   const ffn_b200_moe_desc d = calls_desc(inter, hidden, n, true, true, true);
   const size_t rows = std::max<size_t>((size_t)x_rows, (size_t)n * kNTok);
-  return ((call_tables(n, out_rows).total + 255) & ~(size_t)255) + ffn_b200_moe_ws_bytes(&d, rows);
+  return ((call_tables(n, out_rows).total + 255) & ~(size_t)255) + ffn_b200_moe_ws_bytes(&d, rows) +
+         kSplitBytes + 256;
 }
 
 int ffn::routed_calls(const RoutedCalls &q, size_t inter, size_t hidden, void *stage, void *ws,
@@ -772,18 +802,18 @@ int ffn::routed_calls(const RoutedCalls &q, size_t inter, size_t hidden, void *s
   if (!q.experts || !q.row0 || !q.m || !q.tok_ptr || !q.ent_pair || !q.ent_w || !q.x || !q.out || !stage)
     return fail(FFN_B200_EINVAL, "routed calls: null pointer");
   if (q.out_rows <= 0 || q.x_rows <= 0) return fail(FFN_B200_EINVAL, "routed calls: no rows");
-  bool nv = false, tern = false, mx = false;
+  int n_slices[kCallLists] = {0, 0, 0}, pt[kCallLists] = {0, 0, 0};
+  bool mx = false;
   int P = 0, rc;
   for (int c = 0; c < n; ++c) {
     const ffn_b200_expert &e = q.experts[c];
     if ((rc = check_expert(e, inter, hidden, "routed calls"))) return rc;
-    if (e.format == FFN_B200_FMT_MXFP8)
-      return fail(FFN_B200_EINVAL, "routed calls: MXFP8 experts run one by one");
     if (q.m[c] < 1 || q.m[c] > kNTok || q.row0[c] < 0 || q.row0[c] + q.m[c] > q.x_rows)
       return fail(FFN_B200_EINVAL, "routed calls: a call's x rows are out of range");
-    tern = tern || e.format == FFN_B200_FMT_TERNARY;
+    const int l = call_list(e.format);
+    ++n_slices[l];
+    pt[l] = std::max(pt[l], (int)q.m[c]);
     mx = mx || e.format == FFN_B200_FMT_MXFP4;
-    nv = nv || e.format != FFN_B200_FMT_TERNARY;
     P += q.m[c];
   }
   if (q.tok_ptr[0] != 0 || q.tok_ptr[q.out_rows] != P)
@@ -794,44 +824,122 @@ int ffn::routed_calls(const RoutedCalls &q, size_t inter, size_t hidden, void *s
     if (q.ent_pair[e] < 0 || q.ent_pair[e] >= P) return fail(FFN_B200_EINVAL, "routed calls: bad pair");
   if (ws_bytes < routed_calls_ws_bytes(inter, hidden, n, q.x_rows, q.out_rows))
     return fail(FFN_B200_ENOSPC, "routed calls: workspace too small");
-  // host tables: slices (one per call), pair -> x row, the combine list
+  // host tables: slices (one per call, per list), pair -> x row, zeroed split
+  // counters, the combine list
   const CallTables t = call_tables(n, q.out_rows);
   char *h = (char *)stage;
   std::memcpy(h + t.experts, q.experts, (size_t)n * sizeof(ffn_b200_expert));
   int32_t *pair_tok = (int32_t *)(h + t.pair_tok);
-  VExp *vnv = (VExp *)(h + t.vexp_nv), *vtn = (VExp *)(h + t.vexp_tn);
   int *nvx = (int *)(h + t.n_vexp);
   nvx[0] = nvx[1] = nvx[2] = nvx[3] = 0;
   for (int c = 0, pos = 0; c < n; ++c) {
     for (int j = 0; j < q.m[c]; ++j) pair_tok[pos + j] = q.row0[c] + j;
-    const bool is_tn = q.experts[c].format == FFN_B200_FMT_TERNARY;
-    VExp &v = is_tn ? vtn[nvx[1]++] : vnv[nvx[0]++];
+    const int l = call_list(q.experts[c].format);
+    VExp &v = ((VExp *)(h + t.vexp[l]))[nvx[l]++];
     v.expert = c;
     v.offset = pos;
     v.count = q.m[c];
     v.pad = 0;
     pos += q.m[c];
   }
+  std::memset(h + t.cnt, 0, (size_t)kCallLaunches * kSplitItems * sizeof(int));
   std::memcpy(h + t.tok_ptr, q.tok_ptr, ((size_t)q.out_rows + 1) * 4);
   std::memcpy(h + t.ent_pair, q.ent_pair, (size_t)P * 4);
   std::memcpy(h + t.ent_w, q.ent_w, (size_t)P * 4);
+  if (q.row_zero) std::memcpy(h + t.row_zero, q.row_zero, (size_t)q.out_rows);
+  else std::memset(h + t.row_zero, 0, (size_t)q.out_rows);
   char *dt = (char *)ws;
   FFN_CUDA_TRY(cudaMemcpyAsync(dt, h, t.total, cudaMemcpyHostToDevice, st));
-  ffn_b200_moe_desc d = calls_desc(inter, hidden, n, nv, tern, mx);
+  ffn_b200_moe_desc d = calls_desc(inter, hidden, n, n_slices[0] + n_slices[2] > 0, n_slices[1] > 0, mx);
   d.experts = (const ffn_b200_expert *)(dt + t.experts);
   Carve cv(dt + ((t.total + 255) & ~(size_t)255));
   MoeWs mw = carve_moe(cv, d, std::max<size_t>((size_t)q.x_rows, (size_t)P));
+  float *part = cv.take<float>(kSplitBytes / sizeof(float));
   mw.pair_tok = (int32_t *)(dt + t.pair_tok);
-  mw.vexp_nv = (VExp *)(dt + t.vexp_nv);
-  mw.vexp_tn = (VExp *)(dt + t.vexp_tn);
   mw.n_vexp = (int *)(dt + t.n_vexp);
-  const int H = (int)hidden;
-  if ((rc = launch_xprep(q.x, H, q.x_rows, H, nv ? mw.xh : nullptr, nv ? mw.xl : nullptr, mw.th, mw.tl, H,
-                         mw.xe, st)))
+  int *cnt = (int *)(dt + t.cnt);
+  const size_t H = hidden, I = inter;
+  const bool natural = n_slices[0] + n_slices[2] > 0;  // NVFP4/MXFP4/MXFP8 read natural-order rows
+  if ((rc = launch_xprep(q.x, (int)H, q.x_rows, (int)H, natural ? mw.xh : nullptr, natural ? mw.xl : nullptr,
+                         mw.th, mw.tl, (int)H, mw.xe, st)))
     return rc;
-  if ((rc = moe_gemv_experts(&d, mw, P, q.x, st))) return rc;
+  // per list: [core z], gate/up + SwiGLU -> h, [core z of h], down -> y [pair][H]
+  for (int l = 0; l < kCallLists; ++l) {
+    if (!n_slices[l]) continue;
+    const int fmt = list_format(l);
+    const bool tern = fmt == FFN_B200_FMT_TERNARY;
+    const VExp *vl = (const VExp *)(dt + t.vexp[l]);
+    const int *nvd = mw.n_vexp + l;
+    const SplitPlan s1 = plan_list_splits(fmt, 1, I, H, n_slices[l], pt[l]);
+    const SplitPlan s2 = plan_list_splits(fmt, 2, H, I, n_slices[l], pt[l]);
+    SplitWs sw;
+    sw.part = part;
+    if (tern) {
+      CoreZArgs z{};
+      z.experts = d.experts;
+      z.vexp = vl;
+      z.n_vexp_dev = nvd;
+      z.K = (int)H;
+      z.mat0 = 0;
+      z.nmat = 2;
+      z.xf = q.x;
+      z.ld_xf = (int)H;
+      z.pair_tok = mw.pair_tok;
+      z.z = mw.z;
+      if ((rc = launch_corez(z, n_slices[l], st))) return rc;
+    }
+    PhaseArgs p{};
+    p.experts = d.experts;
+    p.vexp = vl;
+    p.n_vexp_dev = nvd;
+    p.rows = (int)I;
+    p.K = (int)H;
+    p.blocks = (int)((I + rows_per_tile(1) - 1) / rows_per_tile(1));
+    p.xh = tern ? mw.th : mw.xh;
+    p.xl = tern ? mw.tl : mw.xl;
+    p.xe = mw.xe;
+    p.ld_x = (int)H;
+    p.pair_tok = mw.pair_tok;
+    p.z = mw.z;
+    p.hh = mw.hh;
+    p.hl = mw.hl;
+    p.ld_h = (int)I;
+    apply_split(p, s1, sw, cnt + (size_t)(2 * l) * kSplitItems);
+    if ((rc = launch_phase(fmt, 1, p, s1.tasks * s1.splits, st))) return rc;
+    if (tern) {
+      CoreZArgs z{};
+      z.experts = d.experts;
+      z.vexp = vl;
+      z.n_vexp_dev = nvd;
+      z.K = (int)I;
+      z.mat0 = 2;
+      z.nmat = 1;
+      z.hh = mw.hh;
+      z.hl = mw.hl;
+      z.ld_h = (int)I;
+      z.z = mw.z;
+      if ((rc = launch_corez(z, n_slices[l], st))) return rc;
+    }
+    PhaseArgs r{};
+    r.experts = d.experts;
+    r.vexp = vl;
+    r.n_vexp_dev = nvd;
+    r.rows = (int)H;
+    r.K = (int)I;
+    r.blocks = (int)((H + rows_per_tile(2) - 1) / rows_per_tile(2));
+    r.xh = mw.hh;
+    r.xl = mw.hl;
+    r.xe = nullptr;
+    r.ld_x = (int)I;
+    r.z = mw.z;
+    r.y = mw.y;
+    r.ld_y = (int)H;
+    apply_split(r, s2, sw, cnt + (size_t)(2 * l + 1) * kSplitItems);
+    if ((rc = launch_phase(fmt, 2, r, s2.tasks * s2.splits, st))) return rc;
+  }
   return launch_rows_accum(mw.y, (const int32_t *)(dt + t.tok_ptr), (const int32_t *)(dt + t.ent_pair),
-                           (const float *)(dt + t.ent_w), q.out_rows, H, q.out, st);
+                           (const float *)(dt + t.ent_w), (const uint8_t *)(dt + t.row_zero), q.out_rows,
+                           (int)H, q.out, st);
 }
 
 extern "C" {

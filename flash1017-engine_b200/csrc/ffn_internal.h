@@ -78,12 +78,15 @@ int rows_per_tile(int phase);
 int chunk_cols(int fmt);  // K columns per ring unit
 
 // A queue of routed expert calls run together as one routed layer.  Call c
-// applies experts[c] to the x rows row0[c] .. row0[c] + m[c] - 1 (1 <= m[c]
-// <= kNTok); its m[c] output rows are the pairs pos0[c] .. pos0[c] + m[c] - 1,
-// numbered in call order.  Output row r then receives, in list order,
+// applies experts[c] (NVFP4, MXFP4, ternary or MXFP8) to the x rows row0[c] ..
+// row0[c] + m[c] - 1 (1 <= m[c] <= kNTok); its m[c] output rows are the pairs
+// pos0[c] .. pos0[c] + m[c] - 1, numbered in call order.  Output row r then
+// receives, in list order, starting from 0 when row_zero[r] is set, else from
+// out[r],
 //   out[r] = fl(out[r] + fl(w[e] * y[pair[e]]))  for e in [tok_ptr[r], tok_ptr[r + 1]),
-// which is the one-call-at-a-time arithmetic when the list is in call order.
-// All arrays here are HOST arrays; experts hold device weight pointers.
+// which is the one-call-at-a-time arithmetic when the list is in call order
+// (a first call that overwrites: row_zero).  All arrays here are HOST arrays;
+// experts hold device weight pointers.
 struct RoutedCalls {
   const ffn_b200_expert *experts;
   const int32_t *row0, *m;
@@ -91,6 +94,7 @@ struct RoutedCalls {
   const int32_t *tok_ptr;  // [out_rows + 1], tok_ptr[out_rows] = sum of m
   const int32_t *ent_pair;
   const float *ent_w;
+  const uint8_t *row_zero;  // [out_rows] or nullptr (none)
   int out_rows;
   const float *x;  // device [x_rows][hidden]
   int x_rows;
@@ -105,7 +109,8 @@ size_t routed_calls_stage_bytes(int n, int out_rows);
 int routed_calls(const RoutedCalls &q, size_t inter, size_t hidden, void *stage, void *ws,
                  size_t ws_bytes, cudaStream_t st);
 int launch_rows_accum(const float *y, const int32_t *tok_ptr, const int32_t *ent_pair,
-                      const float *ent_w, int out_rows, int H, float *out, cudaStream_t st);
+                      const float *ent_w, const uint8_t *row_zero, int out_rows, int H, float *out,
+                      cudaStream_t st);
 int sm_count_of(int dev);  // multiprocessors of device `dev` (cached)
 int launch_xprep(const float *x, int ld_x, int rows, int K, __half *nh, __half *nl, __half *th,
                  __half *tl, int ld_o, int *xe, cudaStream_t st, const float *norm_w = nullptr,

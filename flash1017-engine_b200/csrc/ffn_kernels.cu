@@ -1304,22 +1304,25 @@ int launch_combine(const float *y, int ld_y, const int32_t *idx, const float *wt
 }
 
 // ============================================================ queued routed calls
-// out[r] += w[e] * y[pair[e]] for the entries of row r in
-// list order (call order), each term rounded as fl(out + fl(w * y)), as the
-// reference's per-call axpy does (flash1017.rs:4900-4905, 8297-8303).  Grid:
-// (column blocks, out rows); 4 columns per thread (hidden % 64 == 0).
+// out[r] += w[e] * y[pair[e]] for the entries of row r in list order (call
+// order), each term rounded as fl(out + fl(w * y)), as the reference's per-call
+// axpy does (flash1017.rs:4900-4905, 8297-8303); rows with row_zero[r] start
+// from 0 (the queue began with an overwriting call).  Grid: (column blocks,
+// out rows); 4 columns per thread (hidden % 64 == 0).
 __global__ void __launch_bounds__(256) rows_accum_kernel(const float *__restrict__ y,
                                                          const int32_t *__restrict__ tok_ptr,
                                                          const int32_t *__restrict__ ent_pair,
-                                                         const float *__restrict__ ent_w, int H,
+                                                         const float *__restrict__ ent_w,
+                                                         const uint8_t *__restrict__ row_zero, int H,
                                                          float *out) {
   pdl_enter();
   const int r = blockIdx.y;
   const int e0 = __ldg(tok_ptr + r), e1 = __ldg(tok_ptr + r + 1);
-  if (e0 == e1) return;
+  const bool zero = __ldg(row_zero + r) != 0;
+  if (e0 == e1 && !zero) return;
   float4 *o4 = reinterpret_cast<float4 *>(out + (size_t)r * H);
   for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < H / 4; c += gridDim.x * blockDim.x) {
-    float4 acc = o4[c];
+    float4 acc = zero ? make_float4(0.f, 0.f, 0.f, 0.f) : o4[c];
     for (int e = e0; e < e1; ++e) {
       const float w = __ldg(ent_w + e);
       const float4 v = __ldg(reinterpret_cast<const float4 *>(y + (size_t)__ldg(ent_pair + e) * H) + c);
@@ -1333,12 +1336,13 @@ __global__ void __launch_bounds__(256) rows_accum_kernel(const float *__restrict
 }
 
 int launch_rows_accum(const float *y, const int32_t *tok_ptr, const int32_t *ent_pair,
-                      const float *ent_w, int out_rows, int H, float *out, cudaStream_t st) {
+                      const float *ent_w, const uint8_t *row_zero, int out_rows, int H, float *out,
+                      cudaStream_t st) {
   if (out_rows <= 0) return 0;
   if (H % 4) return fail(FFN_B200_EINVAL, "rows_accum: hidden must be a multiple of 4");
   const dim3 grid((unsigned)((H / 4 + 255) / 256), (unsigned)out_rows);
   FFN_LAUNCH_PDL(FFN_B200_K_COMBINE, st, "rows_accum_kernel", rows_accum_kernel, grid, 256, 0, y, tok_ptr,
-                 ent_pair, ent_w, H, out);
+                 ent_pair, ent_w, row_zero, H, out);
   return 0;
 }
 

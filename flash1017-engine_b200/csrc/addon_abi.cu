@@ -394,12 +394,39 @@ const char kDesc[] =
 
 // MXFP8 post-scale 2^B from the host scale bytes: the largest finite E8M0
 // scale decodes to 2^7 (E4M3 448 x 2^7 < 65504, FFN_B200_FMT_MXFP8).
-float mxfp8_gs(const uint8_t *s, size_t n) {
+// Power-of-two post-scales gs = 2^B of E8M0 scale arrays, B = (largest finite
+// scale byte) - top, so the largest block decodes to 2^(top - 127) in f16:
+// top 134 for MXFP8 (E4M3 448 x 2^7 < 65504), 140 for MXFP4 (E2M1 6 x 2^13).
+// Computed once per array: the host keeps a scale array's bytes unchanged
+// while the process runs (the same assumption as the weight copies;
+// ffn_b200_release_host_ranges drops both).
+struct GsCache {
+  std::mutex mu;
+  std::map<std::pair<uintptr_t, size_t>, float> m;
+};
+GsCache &gs_cache() {
+  static GsCache *g = new GsCache();
+  return *g;
+}
+
+float mx_gs(const uint8_t *s, size_t n, int top) {
+  GsCache &g = gs_cache();
+  const std::pair<uintptr_t, size_t> key((uintptr_t)s, n * 256 + (size_t)top);
+  {
+    std::lock_guard<std::mutex> lk(g.mu);
+    auto it = g.m.find(key);
+    if (it != g.m.end()) return it->second;
+  }
   int mx = -1;
   for (size_t q = 0; q < n; ++q)
     if (s[q] != 0xFF && s[q] > mx) mx = s[q];
-  return std::ldexp(1.0f, mx < 0 ? 0 : mx - 134);
+  const float gs = std::ldexp(1.0f, mx < 0 ? 0 : mx - top);
+  std::lock_guard<std::mutex> lk(g.mu);
+  g.m[key] = gs;
+  return gs;
 }
+float mxfp8_gs(const uint8_t *s, size_t n) { return mx_gs(s, n, 134); }
+float mxfp4_gs(const uint8_t *s, size_t n) { return mx_gs(s, n, 140); }
 
 void v3_matbatch_mxfp8(size_t rows, size_t cols, size_t seq, const uint8_t *w, const uint8_t *s,
                        const float *xb, float *ob) {
@@ -680,9 +707,12 @@ bool gx10_rust_mxfp4_mlp_accum(size_t inter_rows, size_t hidden_cols, const uint
   e.proj_scale = 1.0f;
   const uint8_t *w[3] = {w1_fp4, w3_fp4, w2_fp4}, *sc[3] = {w1_s, w3_s, w2_s};
   for (int i = 0; i < 3; ++i) {
+    const size_t r = i == 2 ? hidden_cols : inter_rows, k = i == 2 ? inter_rows : hidden_cols;
     e.nv[i].w = w[i];
     e.nv[i].s = sc[i];
-    e.nv[i].gs = 1.0f;  // the reference's MXFP4 tensors have no global scale
+    // the reference's MXFP4 tensors have no global scale: gs is only the
+    // power-of-two bias of the f16 decode
+    e.nv[i].gs = sc[i] ? mxfp4_gs(sc[i], r * (k / 32)) : 1.0f;
   }
   return mlp_accum(e, inter_rows, hidden_cols, x, out, accum_weight, accumulate, sync_now);
 }
@@ -726,7 +756,7 @@ bool gx10_rust_mxfp4_matvec(size_t rows, size_t cols, const uint8_t *packed_fp4,
     ffn_b200_nvfp4_mat m{};
     m.w = (const uint8_t *)dw;
     m.s = (const uint8_t *)ds;
-    m.gs = 1.0f;
+    m.gs = mxfp4_gs(scales_e8m0, rows * (cols / 32));  // the f16 decode's power-of-two bias
     rc = ffn_b200_mxfp4_matvec(rows, cols, 1, &m, (const float *)c.x.p, (float *)c.out.p, c.ws.p, c.ws.n,
                                c.st);
   }
@@ -870,6 +900,11 @@ int ffn_b200_release_host_ranges(void) {
     for (Range &r : kv.second) cudaFree(r.d);
   c.ranges.clear();
   c.cached = 0;
+  {
+    GsCache &g = gs_cache();
+    std::lock_guard<std::mutex> lk2(g.mu);
+    g.m.clear();
+  }
   return rc;
 }
 

@@ -237,3 +237,24 @@ def test_q4_backbone_flag_is_refused(oracle, ffn, cuda, L):
     assert not L.gx10_rust_mxfp8_mlp_batch(I, H, 2 | (1 << 31), p(shared.w[0]), p(shared.s[0]),
                                            p(shared.w[1]), p(shared.s[1]), p(shared.w[2]),
                                            p(shared.s[2]), p(x), 2, p(out), True)
+
+
+def test_mxfp4_wide_scale_range_through_the_abi(oracle, ffn, cuda, L):
+    """MXFP4 block scales over 2^-37 .. 2^13 through gx10_rust_mxfp4_matvec and
+    gx10_rust_mxfp4_mlp_accum: the library derives the f16 decode's power-of-two
+    bias from the largest scale, as the device-resident Mxfp4Matrix does."""
+    H, I = 1024, 512
+    rng = np.random.default_rng(9)
+    ws = []
+    for r, c in ((I, H), (I, H), (H, I)):
+        ws.append((rng.integers(0, 256, size=r * c // 2, dtype=np.uint8),
+                   rng.integers(90, 141, size=r * c // 32, dtype=np.uint8)))
+    x = bench_x(H)
+    y = np.zeros(I, dtype=np.float32)
+    assert L.gx10_rust_mxfp4_matvec(I, H, p(ws[0][0]), p(ws[0][1]), p(x), p(y))
+    oracle.assert_close(y, oracle.mxfp4_matvec(ws[0][0], ws[0][1], x, I, H), what="mxfp4 matvec, wide scales")
+    oe = oracle.MxExpert(3, I, H, tuple(a for a, _ in ws), tuple(b for _, b in ws))
+    out = np.zeros(H, dtype=np.float32)
+    assert L.gx10_rust_mxfp4_mlp_accum(I, H, p(ws[0][0]), p(ws[0][1]), p(ws[1][0]), p(ws[1][1]),
+                                       p(ws[2][0]), p(ws[2][1]), p(x), p(out), 0.5, False, True)
+    oracle.assert_close(out, 0.5 * oe.forward(x), what="mxfp4 expert, wide scales")

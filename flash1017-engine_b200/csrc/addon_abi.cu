@@ -55,6 +55,8 @@ struct Ctx {
   bool init = false;
   int device = -1;
   cudaStream_t st = nullptr;
+  cudaStream_t st2 = nullptr;  // side stream of queued runs (independent slice lists)
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   DevBuf x, out, ws, tmp;
   std::map<uintptr_t, std::vector<Range>> ranges;  // by start address
   size_t cached = 0;
@@ -112,6 +114,9 @@ int ensure_init(Ctx &c) {
   }
   FFN_CUDA_TRY(cudaGetDevice(&c.device));
   FFN_CUDA_TRY(cudaStreamCreateWithFlags(&c.st, cudaStreamNonBlocking));
+  FFN_CUDA_TRY(cudaStreamCreateWithFlags(&c.st2, cudaStreamNonBlocking));
+  FFN_CUDA_TRY(cudaEventCreateWithFlags(&c.ev_fork, cudaEventDisableTiming));
+  FFN_CUDA_TRY(cudaEventCreateWithFlags(&c.ev_join, cudaEventDisableTiming));
   c.init = true;
   return 0;
 }
@@ -226,6 +231,9 @@ int run_queue(Ctx &c) {
   q.x = (const float *)(from_bx ? c.bx.p : c.xall.p);
   q.x_rows = from_bx ? xrows : (int)c.xall_tok;
   q.out = (float *)c.out.p;
+  q.side = c.st2;
+  q.fork = c.ev_fork;
+  q.join = c.ev_join;
   int rc = c.ws.ensure(ffn::routed_calls_ws_bytes(c.q_inter, c.q_hidden, n, q.x_rows, R));
   Ctx::Stage &s = c.stage[c.stage_i];
   if (!rc) rc = stage_ready(s, ffn::routed_calls_stage_bytes(n, R));

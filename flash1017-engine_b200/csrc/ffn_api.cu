@@ -791,7 +791,7 @@ size_t ffn::routed_calls_ws_bytes(size_t inter, size_t hidden, int n, int x_rows
   const ffn_b200_moe_desc d = calls_desc(inter, hidden, n, true, true, true);
   const size_t rows = std::max<size_t>((size_t)x_rows, (size_t)n * kNTok);
   return ((call_tables(n, out_rows).total + 255) & ~(size_t)255) + ffn_b200_moe_ws_bytes(&d, rows) +
-         kSplitBytes + 256;
+         2 * kSplitBytes + 512;
 }
 
 int ffn::routed_calls(const RoutedCalls &q, size_t inter, size_t hidden, void *stage, void *ws,
@@ -854,7 +854,7 @@ int ffn::routed_calls(const RoutedCalls &q, size_t inter, size_t hidden, void *s
   d.experts = (const ffn_b200_expert *)(dt + t.experts);
   Carve cv(dt + ((t.total + 255) & ~(size_t)255));
   MoeWs mw = carve_moe(cv, d, std::max<size_t>((size_t)q.x_rows, (size_t)P));
-  float *part = cv.take<float>(kSplitBytes / sizeof(float));
+  float *part[2] = {cv.take<float>(kSplitBytes / sizeof(float)), cv.take<float>(kSplitBytes / sizeof(float))};
   mw.pair_tok = (int32_t *)(dt + t.pair_tok);
   mw.n_vexp = (int *)(dt + t.n_vexp);
   int *cnt = (int *)(dt + t.cnt);
@@ -863,9 +863,9 @@ int ffn::routed_calls(const RoutedCalls &q, size_t inter, size_t hidden, void *s
   if ((rc = launch_xprep(q.x, (int)H, q.x_rows, (int)H, natural ? mw.xh : nullptr, natural ? mw.xl : nullptr,
                          mw.th, mw.tl, (int)H, mw.xe, st)))
     return rc;
-  // per list: [core z], gate/up + SwiGLU -> h, [core z of h], down -> y [pair][H]
-  for (int l = 0; l < kCallLists; ++l) {
-    if (!n_slices[l]) continue;
+  // one list: [core z], gate/up + SwiGLU -> h, [core z of h], down -> y [pair][H]
+  auto run_list = [&](int l, cudaStream_t ls, float *lpart) -> int {
+    int rc;
     const int fmt = list_format(l);
     const bool tern = fmt == FFN_B200_FMT_TERNARY;
     const VExp *vl = (const VExp *)(dt + t.vexp[l]);
@@ -873,7 +873,7 @@ int ffn::routed_calls(const RoutedCalls &q, size_t inter, size_t hidden, void *s
     const SplitPlan s1 = plan_list_splits(fmt, 1, I, H, n_slices[l], pt[l]);
     const SplitPlan s2 = plan_list_splits(fmt, 2, H, I, n_slices[l], pt[l]);
     SplitWs sw;
-    sw.part = part;
+    sw.part = lpart;
     if (tern) {
       CoreZArgs z{};
       z.experts = d.experts;
@@ -886,7 +886,7 @@ int ffn::routed_calls(const RoutedCalls &q, size_t inter, size_t hidden, void *s
       z.ld_xf = (int)H;
       z.pair_tok = mw.pair_tok;
       z.z = mw.z;
-      if ((rc = launch_corez(z, n_slices[l], st))) return rc;
+      if ((rc = launch_corez(z, n_slices[l], ls))) return rc;
     }
     PhaseArgs p{};
     p.experts = d.experts;
@@ -905,7 +905,7 @@ int ffn::routed_calls(const RoutedCalls &q, size_t inter, size_t hidden, void *s
     p.hl = mw.hl;
     p.ld_h = (int)I;
     apply_split(p, s1, sw, cnt + (size_t)(2 * l) * kSplitItems);
-    if ((rc = launch_phase(fmt, 1, p, s1.tasks * s1.splits, st))) return rc;
+    if ((rc = launch_phase(fmt, 1, p, s1.tasks * s1.splits, ls))) return rc;
     if (tern) {
       CoreZArgs z{};
       z.experts = d.experts;
@@ -918,7 +918,7 @@ int ffn::routed_calls(const RoutedCalls &q, size_t inter, size_t hidden, void *s
       z.hl = mw.hl;
       z.ld_h = (int)I;
       z.z = mw.z;
-      if ((rc = launch_corez(z, n_slices[l], st))) return rc;
+      if ((rc = launch_corez(z, n_slices[l], ls))) return rc;
     }
     PhaseArgs r{};
     r.experts = d.experts;
@@ -935,7 +935,35 @@ int ffn::routed_calls(const RoutedCalls &q, size_t inter, size_t hidden, void *s
     r.y = mw.y;
     r.ld_y = (int)H;
     apply_split(r, s2, sw, cnt + (size_t)(2 * l + 1) * kSplitItems);
-    if ((rc = launch_phase(fmt, 2, r, s2.tasks * s2.splits, st))) return rc;
+    return launch_phase(fmt, 2, r, s2.tasks * s2.splits, ls);
+  };
+  // The lists are independent until the combine (disjoint pairs): with a side
+  // stream, the largest list (by weight bytes) runs on `st` and the others on
+  // the side stream, forked after the activation prep and joined before the
+  // combine.
+  static const double kBytesPerWeight[kCallLists] = {0.5625, 0.25, 1.0};
+  int main_l = -1, lists = 0;
+  for (int l = 0; l < kCallLists; ++l)
+    if (n_slices[l]) {
+      ++lists;
+      if (main_l < 0 || n_slices[l] * kBytesPerWeight[l] > n_slices[main_l] * kBytesPerWeight[main_l]) main_l = l;
+    }
+  const bool fork = q.side && q.fork && q.join && lists > 1;
+  if (fork) {
+    FFN_CUDA_TRY(cudaEventRecord(q.fork, st));
+    FFN_CUDA_TRY(cudaStreamWaitEvent(q.side, q.fork, 0));
+    rc = 0;
+    for (int l = 0; l < kCallLists && !rc; ++l)
+      if (n_slices[l] && l != main_l) rc = run_list(l, q.side, part[1]);
+    if (!rc) rc = run_list(main_l, st, part[0]);
+    // join even after a failed launch: later work on `st` reuses the workspace
+    cudaError_t e = cudaEventRecord(q.join, q.side);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, q.join, 0);
+    if (rc) return rc;
+    if (e != cudaSuccess) return cuda_fail(e, "routed calls: side-stream join");
+  } else {
+    for (int l = 0; l < kCallLists; ++l)
+      if (n_slices[l] && (rc = run_list(l, st, part[0]))) return rc;
   }
   return launch_rows_accum(mw.y, (const int32_t *)(dt + t.tok_ptr), (const int32_t *)(dt + t.ent_pair),
                            (const float *)(dt + t.ent_w), (const uint8_t *)(dt + t.row_zero), q.out_rows,

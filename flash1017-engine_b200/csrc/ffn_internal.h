@@ -99,6 +99,10 @@ struct RoutedCalls {
   const float *x;  // device [x_rows][hidden]
   int x_rows;
   float *out;      // device [out_rows][hidden]
+  // optional side stream and two events: independent slice lists run on it
+  // concurrently with the largest one (forked and joined on the call's stream)
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
 };
 constexpr int kCallsMax = 64;  // calls per routed_calls run
 size_t routed_calls_ws_bytes(size_t inter, size_t hidden, int n, int x_rows, int out_rows);

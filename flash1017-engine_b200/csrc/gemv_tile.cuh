@@ -350,23 +350,47 @@ struct WarpEngine {
           sbb[mt] = (uint32_t)__half_as_ushort(hb) * 0x10001u;
         }
       }
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      // activation halves of ternary word q: 8 consecutive pair-order values
+      // of the hi row (and of the lo row unless PACKED)
+      auto txload = [&](int q, uint32_t(&bh)[8], uint32_t(&bl)[8]) {
         const uint4 h0 = xload(xa, 2 * q), h1 = xload(xa, 2 * q + 1);
         const uint4 l0 = PACKED ? make_uint4(0u, 0u, 0u, 0u) : xload(xb, 2 * q);
         const uint4 l1 = PACKED ? make_uint4(0u, 0u, 0u, 0u) : xload(xb, 2 * q + 1);
-        const uint32_t bh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-        const uint32_t bl[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+        bh[0] = h0.x; bh[1] = h0.y; bh[2] = h0.z; bh[3] = h0.w;
+        bh[4] = h1.x; bh[5] = h1.y; bh[6] = h1.z; bh[7] = h1.w;
+        bl[0] = l0.x; bl[1] = l0.y; bl[2] = l0.z; bl[3] = l0.w;
+        bl[4] = l1.x; bl[5] = l1.y; bl[6] = l1.z; bl[7] = l1.w;
+      };
+      // One unrolled loop per case, chosen once per sub-chunk (warp-uniform):
+      // no block scales, or block scales (a matrix without them multiplies
+      // by 1.0, exact).  Choosing per m-tile inside the loop interleaves both
+      // unrolled bodies in the instruction stream, and the warps then stall
+      // on instruction fetch.
+      if (bs_mask == 0) {
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          const int mi = mt / R, i = mt % R;
-          const uint32_t wa = q == 0 ? wq[mt][0].x : q == 1 ? wq[mt][0].y : q == 2 ? wq[mt][0].z : wq[mt][0].w;
-          const uint32_t wb = q == 0 ? wq[mt][1].x : q == 1 ? wq[mt][1].y : q == 2 ? wq[mt][1].z : wq[mt][1].w;
-          if ((bs_mask >> mi) & 1u) tern_steps_scaled<PACKED>(acc[mi][i], wa, wb, sba[mt], sbb[mt], bh, bl);
-          else tern_steps<PACKED>(acc[mi][i], wa, wb, bh, bl);
+        for (int q = 0; q < 4; ++q) {
+          uint32_t bh[8], bl[8];
+          txload(q, bh, bl);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+            tern_steps<PACKED>(acc[mt / R][mt % R], tern_word(wq[mt][0], q), tern_word(wq[mt][1], q), bh, bl);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t bh[8], bl[8];
+          txload(q, bh, bl);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+            tern_steps_scaled<PACKED>(acc[mt / R][mt % R], tern_word(wq[mt][0], q), tern_word(wq[mt][1], q),
+                                      sba[mt], sbb[mt], bh, bl);
         }
       }
     }
+  }
+
+  __device__ static __forceinline__ uint32_t tern_word(const uint4 &w, int q) {
+    return q == 0 ? w.x : q == 1 ? w.y : q == 2 ? w.z : w.w;
   }
 
   // Four MMA k-steps of one 16-column ternary word (rows g and g+8).

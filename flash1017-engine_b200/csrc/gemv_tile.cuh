@@ -217,15 +217,11 @@ struct WarpEngine {
   __device__ static __forceinline__ void compute(const uint8_t *slot, int K, int c, const __half *xa,
                                                  const __half *xb, float (&acc)[NMAT][R][4],
                                                  uint32_t bs_mask = 0, uint32_t mxinfo = 0) {
-    if constexpr (FMT == FFN_B200_FMT_TERNARY) {
-      // ternary: one copy of the (large) unrolled sub-chunk body, so the
-      // warps' instruction fetches stay in cache
+    // One copy of the (large) unrolled sub-chunk body, so the warps'
+    // instruction fetches stay in cache (ternary gate/up 8 % and down 12 %
+    // faster, NVFP4 down 3 %, than with the sub-chunks unrolled).
 #pragma unroll 1
-      for (int sb = 0; sb < SUB; ++sb) compute_sub<PACKED>(slot, sb, K, c * SUB + sb, xa, xb, acc, bs_mask, mxinfo);
-    } else {
-#pragma unroll
-      for (int sb = 0; sb < SUB; ++sb) compute_sub<PACKED>(slot, sb, K, c * SUB + sb, xa, xb, acc, bs_mask, mxinfo);
-    }
+    for (int sb = 0; sb < SUB; ++sb) compute_sub<PACKED>(slot, sb, K, c * SUB + sb, xa, xb, acc, bs_mask, mxinfo);
   }
 
   // Accumulate one sub-chunk c from `slot` into acc.  xa/xb: this lane's

@@ -216,6 +216,8 @@ static ActWs carve_act(Carve &c, size_t n_rows, size_t K) {
 // depend on the device.
 constexpr long long kSplitItems = 148 * 12;
 constexpr size_t kSplitBytes = 512u << 10;
+// partial sums of list-mode splits (MoE-layer and queued-call workspaces)
+constexpr size_t kListSplitBytes = 2u << 20;
 
 struct SplitPlan {
   int splits = 1, pt = 0;
@@ -594,6 +596,8 @@ struct MoeWs {
   float *z, *y;
   uint8_t *chunk;  // grouped path: chunk list
   int *err;        // grouped path: timed-out wait flag
+  float *part;     // GEMV path: K-split partial sums (kListSplitBytes)
+  int *cnt;        // GEMV path: split arrival counters, kSplitItems per phase launch (4)
 };
 
 static MoeWs carve_moe(Carve &c, const ffn_b200_moe_desc &d, size_t T) {
@@ -619,6 +623,8 @@ static MoeWs carve_moe(Carve &c, const ffn_b200_moe_desc &d, size_t T) {
   w.y = c.take<float>(P * H);
   w.chunk = c.take<uint8_t>(gg_chunk_bytes((int)P, (int)E));
   w.err = c.take<int>(1);
+  w.part = c.take<float>(kListSplitBytes / sizeof(float));
+  w.cnt = c.take<int>(4 * (size_t)kSplitItems);
   return w;
 }
 
@@ -629,6 +635,23 @@ size_t ffn_b200_moe_ws_bytes(const ffn_b200_moe_desc *d, size_t max_tokens) {
   return c.off + 256;
 }
 
+// K-splits of a list-mode phase launch over at most n_slices slices: the same
+// rule as plan_splits (one wave of warps, at most one split per ring unit),
+// partials within kListSplitBytes (a list launch has more row blocks than one
+// expert's, so its partials need more room than kSplitBytes gives; only the
+// MoE-layer and queued-call workspaces hold them).  pt = the largest slice.
+static SplitPlan plan_list_splits(int fmt, int phase, size_t rows, size_t K, int n_slices, int pt) {
+  SplitPlan sp;
+  sp.tasks = (long long)n_slices * (long long)((rows + rows_per_tile(phase) - 1) / rows_per_tile(phase));
+  sp.pt = pt;
+  const long long nch = (long long)((K + chunk_cols(fmt) - 1) / chunk_cols(fmt));
+  const size_t per = (size_t)pt * rows_per_tile(phase) * (phase == 1 ? 2 : 1) * sizeof(float);
+  long long s = std::min<long long>(kSplitItems / sp.tasks, nch);
+  s = std::min<long long>(s, (long long)(kListSplitBytes / ((size_t)sp.tasks * per)));
+  sp.splits = (int)std::max<long long>(1, s);
+  sp.part_bytes = sp.splits > 1 ? (size_t)sp.tasks * sp.splits * per : 0;
+  return sp;
+}
 // The GEMV path's experts of a routed layer: per format, [rank-16 core z,]
 // gate/up + SwiGLU -> h, [core z of h,] down -> y [pair][H] (unweighted).
 // w.pair_tok / w.vexp_* / w.n_vexp come from launch_group.
@@ -639,6 +662,21 @@ static int moe_gemv_experts(const ffn_b200_moe_desc *d, MoeWs &w, int P, const f
   // Upper bound of slices per format (the device count is <= this).
   const int e_local = d->expert_end - d->expert_begin;
   const long long max_vexp = std::min<long long>((long long)P, (long long)P / kNTok + e_local);
+  // K-splits from the slice bound: a few-token layer (single-token decode:
+  // top_k slices) would otherwise leave most of the GPU idle; a layer with
+  // many slices (config 4) plans one split, i.e. none.
+  const int pt = (int)std::min<long long>(kNTok, (long long)P / (long long)d->top_k);
+  SplitPlan plans[2][2];
+  bool any_split = false;
+  for (int f = 0; f < 2; ++f) {
+    const int fmt = f == 0 ? FFN_B200_FMT_NVFP4 : FFN_B200_FMT_TERNARY;
+    plans[f][0] = plan_list_splits(fmt, 1, I, H, (int)max_vexp, pt);
+    plans[f][1] = plan_list_splits(fmt, 2, H, I, (int)max_vexp, pt);
+    any_split = any_split || plans[f][0].splits > 1 || plans[f][1].splits > 1;
+  }
+  if (any_split) FFN_CUDA_TRY(cudaMemsetAsync(w.cnt, 0, 4 * (size_t)kSplitItems * sizeof(int), st));
+  SplitWs sw;
+  sw.part = w.part;
   for (int f = 0; f < 2; ++f) {
     const int fmt = f == 0 ? FFN_B200_FMT_NVFP4 : FFN_B200_FMT_TERNARY;
     if ((fmt == FFN_B200_FMT_NVFP4 && !d->has_nvfp4) || (fmt == FFN_B200_FMT_TERNARY && !d->has_ternary))
@@ -676,7 +714,8 @@ static int moe_gemv_experts(const ffn_b200_moe_desc *d, MoeWs &w, int P, const f
     p.hh = w.hh;
     p.hl = w.hl;
     p.ld_h = (int)I;
-    if ((rc = launch_phase(fmt, 1, p, max_vexp * p.blocks, st))) return rc;
+    apply_split(p, plans[f][0], sw, w.cnt + (size_t)(2 * f) * kSplitItems);
+    if ((rc = launch_phase(fmt, 1, p, max_vexp * p.blocks * plans[f][0].splits, st))) return rc;
     if (tern) {
       CoreZArgs z{};
       z.experts = d->experts;
@@ -705,7 +744,8 @@ static int moe_gemv_experts(const ffn_b200_moe_desc *d, MoeWs &w, int P, const f
     q.z = w.z;
     q.y = w.y;
     q.ld_y = (int)H;
-    if ((rc = launch_phase(fmt, 2, q, max_vexp * q.blocks, st))) return rc;
+    apply_split(q, plans[f][1], sw, w.cnt + (size_t)(2 * f + 1) * kSplitItems);
+    if ((rc = launch_phase(fmt, 2, q, max_vexp * q.blocks * plans[f][1].splits, st))) return rc;
   }
   return 0;
 }
@@ -768,21 +808,6 @@ CallTables call_tables(int n, int out_rows) {
   return t;
 }
 
-// K-splits of a list-mode phase launch whose slices the host knows: the same
-// rule as plan_splits (one wave of warps, at most one split per ring unit,
-// partials within kSplitBytes).  pt = the largest slice.
-SplitPlan plan_list_splits(int fmt, int phase, size_t rows, size_t K, int n_slices, int pt) {
-  SplitPlan sp;
-  sp.tasks = (long long)n_slices * (long long)((rows + rows_per_tile(phase) - 1) / rows_per_tile(phase));
-  sp.pt = pt;
-  const long long nch = (long long)((K + chunk_cols(fmt) - 1) / chunk_cols(fmt));
-  const size_t per = (size_t)pt * rows_per_tile(phase) * (phase == 1 ? 2 : 1) * sizeof(float);
-  long long s = std::min<long long>(kSplitItems / sp.tasks, nch);
-  s = std::min<long long>(s, (long long)(kSplitBytes / ((size_t)sp.tasks * per)));
-  sp.splits = (int)std::max<long long>(1, s);
-  sp.part_bytes = sp.splits > 1 ? (size_t)sp.tasks * sp.splits * per : 0;
-  return sp;
-}
 }  // namespace
 
 size_t ffn::routed_calls_stage_bytes(int n, int out_rows) { return call_tables(n, out_rows).total; }
@@ -791,7 +816,7 @@ size_t ffn::routed_calls_ws_bytes(size_t inter, size_t hidden, int n, int x_rows
   const ffn_b200_moe_desc d = calls_desc(inter, hidden, n, true, true, true);
   const size_t rows = std::max<size_t>((size_t)x_rows, (size_t)n * kNTok);
   return ((call_tables(n, out_rows).total + 255) & ~(size_t)255) + ffn_b200_moe_ws_bytes(&d, rows) +
-         2 * kSplitBytes + 512;
+         2 * kListSplitBytes + 512;
 }
 
 int ffn::routed_calls(const RoutedCalls &q, size_t inter, size_t hidden, void *stage, void *ws,
@@ -854,7 +879,8 @@ int ffn::routed_calls(const RoutedCalls &q, size_t inter, size_t hidden, void *s
   d.experts = (const ffn_b200_expert *)(dt + t.experts);
   Carve cv(dt + ((t.total + 255) & ~(size_t)255));
   MoeWs mw = carve_moe(cv, d, std::max<size_t>((size_t)q.x_rows, (size_t)P));
-  float *part[2] = {cv.take<float>(kSplitBytes / sizeof(float)), cv.take<float>(kSplitBytes / sizeof(float))};
+  float *part[2] = {cv.take<float>(kListSplitBytes / sizeof(float)),
+                    cv.take<float>(kListSplitBytes / sizeof(float))};
   mw.pair_tok = (int32_t *)(dt + t.pair_tok);
   mw.n_vexp = (int *)(dt + t.n_vexp);
   int *cnt = (int *)(dt + t.cnt);

@@ -208,7 +208,10 @@ int run_queue(Ctx &c) {
     }
   const bool from_bx = c.q_src == 1;
   const int xrows = c.q_xrows;
-  const uint8_t zero = c.q_zero ? 1 : 0;
+  // the queue began with an overwriting call: every out row starts from zero
+  // (accumulate mode: the one row; batched layer: the shared expert's rows,
+  // which are all of them)
+  std::vector<uint8_t> zero((size_t)R, c.q_zero ? 1 : 0);
   clear_queue(c);
   if (from_bx) {
     // the staged x rows, one pinned upload
@@ -227,7 +230,7 @@ int run_queue(Ctx &c) {
   q.ent_pair = pair.data();
   q.ent_w = wts.data();
   q.out_rows = R;
-  q.row_zero = from_bx ? &zero : nullptr;  // accumulate mode: one out row
+  q.row_zero = zero.data();
   q.x = (const float *)(from_bx ? c.bx.p : c.xall.p);
   q.x_rows = from_bx ? xrows : (int)c.xall_tok;
   q.out = (float *)c.out.p;
@@ -849,10 +852,23 @@ bool gx10_rust_mxfp8_mlp_batch(size_t inter_rows, size_t hidden_cols, size_t seq
   }
   if (!rc) rc = resolve_expert(c, e, I, H);
   if (!rc) rc = c.out.ensure(b_len * H * 4);
-  if (!rc) rc = c.ws.ensure(ffn_b200_expert_ws_bytes(I, H, b_len));
-  if (!rc)
-    rc = ffn_b200_expert_forward(I, H, b_len, &e, (const float *)c.xall.p, (float *)c.out.p, 1.0f, 0,
-                                 c.ws.p, c.ws.n, c.st);
+  if (!rc && b_len <= (size_t)kNTok) {
+    // one slice: queued as the layer's first call (its rows start from
+    // zero), so the layer's routed calls run with it as one routed layer
+    int32_t dst[kNTok];
+    float w1[kNTok];
+    for (size_t t = 0; t < b_len; ++t) {
+      dst[t] = (int32_t)t;
+      w1[t] = 1.0f;
+    }
+    c.q_zero = true;
+    rc = enqueue(c, e, 2, I, H, (int)b_len, 0, (int32_t)b_len, dst, w1);
+  } else {
+    if (!rc) rc = c.ws.ensure(ffn_b200_expert_ws_bytes(I, H, b_len));
+    if (!rc)
+      rc = ffn_b200_expert_forward(I, H, b_len, &e, (const float *)c.xall.p, (float *)c.out.p, 1.0f, 0,
+                                   c.ws.p, c.ws.n, c.st);
+  }
   if (!rc) {
     c.pend_host = out_batch;
     c.pend_n = b_len * H;

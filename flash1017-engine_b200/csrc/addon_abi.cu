@@ -569,7 +569,10 @@ bool mlp_accum(const ffn_b200_expert &he, size_t inter, size_t hidden, const flo
   if (!rc) rc = c.out.ensure(hidden * 4);
   if (!rc) rc = c.bx.ensure((size_t)ffn::kCallsMax * hidden * 4);
   ffn_b200_expert e = he;
+  // shapes before any weight byte is read; the rest on the device copies
+  if (!rc) rc = ffn::validate_expert_shape(e.format, inter, hidden, "mlp_accum");
   if (!rc) rc = resolve_expert(c, e, inter, hidden);
+  if (!rc) rc = ffn::validate_expert(e, inter, hidden, "mlp_accum");
   if (!rc && accumulate && !c.pend_host) {
     // accumulate onto the host's current contents
     cudaError_t er = cudaMemcpyAsync(c.out.p, out, hidden * 4, cudaMemcpyHostToDevice, c.st);
@@ -634,7 +637,9 @@ bool mlp_batch(const ffn_b200_expert &he, float wscale, size_t inter, size_t hid
   if (!rc) rc = c.out.ensure(b_len * hidden * 4);
   if (!rc) rc = ensure_xall(c);
   ffn_b200_expert e = he;
+  if (!rc) rc = ffn::validate_expert_shape(e.format, inter, hidden, "mlp_batch");
   if (!rc) rc = resolve_expert(c, e, inter, hidden);
+  if (!rc) rc = ffn::validate_expert(e, inter, hidden, "mlp_batch");
   if (!rc && e.format == FFN_B200_FMT_MXFP8) rc = fail(FFN_B200_EINVAL, "mlp_batch: MXFP8 expert");
   if (!rc && !c.pend_host) {
     cudaError_t er = cudaMemcpyAsync(c.out.p, out, b_len * hidden * 4, cudaMemcpyHostToDevice, c.st);
@@ -717,13 +722,15 @@ bool gx10_rust_mxfp4_mlp_accum(size_t inter_rows, size_t hidden_cols, const uint
   e.format = FFN_B200_FMT_MXFP4;
   e.proj_scale = 1.0f;
   const uint8_t *w[3] = {w1_fp4, w3_fp4, w2_fp4}, *sc[3] = {w1_s, w3_s, w2_s};
+  // the scale arrays are read only for shapes that pass (mlp_accum reports the error)
+  const bool shape_ok = ffn::validate_expert_shape(e.format, inter_rows, hidden_cols, "mxfp4_mlp_accum") == 0;
   for (int i = 0; i < 3; ++i) {
     const size_t r = i == 2 ? hidden_cols : inter_rows, k = i == 2 ? inter_rows : hidden_cols;
     e.nv[i].w = w[i];
     e.nv[i].s = sc[i];
     // the reference's MXFP4 tensors have no global scale: gs is only the
     // power-of-two bias of the f16 decode
-    e.nv[i].gs = sc[i] ? mxfp4_gs(sc[i], r * (k / 32)) : 1.0f;
+    e.nv[i].gs = sc[i] && shape_ok ? mxfp4_gs(sc[i], r * (k / 32)) : 1.0f;
   }
   return mlp_accum(e, inter_rows, hidden_cols, x, out, accum_weight, accumulate, sync_now);
 }
@@ -736,11 +743,13 @@ bool gx10_rust_mxfp8_mlp_accum(size_t inter_rows, size_t hidden_cols, const uint
   e.format = FFN_B200_FMT_MXFP8;
   e.proj_scale = 1.0f;
   const uint8_t *w[3] = {w1_w, w3_w, w2_w}, *sc[3] = {w1_s, w3_s, w2_s};
+  // the scale arrays are read only for shapes that pass (mlp_accum reports the error)
+  const bool shape_ok = ffn::validate_expert_shape(e.format, inter_rows, hidden_cols, "mxfp8_mlp_accum") == 0;
   for (int i = 0; i < 3; ++i) {
     const size_t r = i == 2 ? hidden_cols : inter_rows, k = i == 2 ? inter_rows : hidden_cols;
     e.nv[i].w = w[i];
     e.nv[i].s = sc[i];
-    e.nv[i].gs = sc[i] ? mxfp8_gs(sc[i], ((r + 31) / 32) * ((k + 31) / 32)) : 1.0f;
+    e.nv[i].gs = sc[i] && shape_ok ? mxfp8_gs(sc[i], ((r + 31) / 32) * ((k + 31) / 32)) : 1.0f;
   }
   return mlp_accum(e, inter_rows, hidden_cols, x, out, accum_weight, accumulate, sync_now);
 }
@@ -844,13 +853,15 @@ bool gx10_rust_mxfp8_mlp_batch(size_t inter_rows, size_t hidden_cols, size_t seq
   e.format = FFN_B200_FMT_MXFP8;
   e.proj_scale = 1.0f;
   const uint8_t *w[3] = {w1_w, w3_w, w2_w}, *sc[3] = {w1_s, w3_s, w2_s};
+  if (!rc) rc = ffn::validate_expert_shape(e.format, I, H, "mxfp8_mlp_batch");
   for (int i = 0; i < 3; ++i) {
     const size_t r = i == 2 ? H : I, k = i == 2 ? I : H;
     e.nv[i].w = w[i];
     e.nv[i].s = sc[i];
-    e.nv[i].gs = sc[i] ? mxfp8_gs(sc[i], ((r + 31) / 32) * ((k + 31) / 32)) : 1.0f;
+    e.nv[i].gs = sc[i] && !rc ? mxfp8_gs(sc[i], ((r + 31) / 32) * ((k + 31) / 32)) : 1.0f;
   }
   if (!rc) rc = resolve_expert(c, e, I, H);
+  if (!rc) rc = ffn::validate_expert(e, I, H, "mxfp8_mlp_batch");
   if (!rc) rc = c.out.ensure(b_len * H * 4);
   if (!rc && b_len <= (size_t)kNTok) {
     // one slice: queued as the layer's first call (its rows start from

@@ -810,6 +810,22 @@ CallTables call_tables(int n, int out_rows) {
 
 }  // namespace
 
+int ffn::validate_expert_shape(int format, size_t inter, size_t hidden, const char *what) {
+  if (format != FFN_B200_FMT_NVFP4 && format != FFN_B200_FMT_TERNARY && format != FFN_B200_FMT_MXFP4 &&
+      format != FFN_B200_FMT_MXFP8)
+    return fail(FFN_B200_EINVAL, std::string(what) + ": unknown expert format");
+  int rc;
+  if ((rc = check_mat_shape(format, inter, hidden, what))) return rc;
+  if ((rc = check_mat_shape(format, hidden, inter, what))) return rc;
+  if ((format == FFN_B200_FMT_MXFP4 || format == FFN_B200_FMT_MXFP8) && (hidden % 128 || inter % 128))
+    return fail(FFN_B200_EUNSUP, std::string(what) + ": MXFP4 / MXFP8 experts need hidden and inter % 128 == 0");
+  return 0;
+}
+
+int ffn::validate_expert(const ffn_b200_expert &e, size_t inter, size_t hidden, const char *what) {
+  return check_expert(e, inter, hidden, what);
+}
+
 size_t ffn::routed_calls_stage_bytes(int n, int out_rows) { return call_tables(n, out_rows).total; }
 
 size_t ffn::routed_calls_ws_bytes(size_t inter, size_t hidden, int n, int x_rows, int out_rows) {

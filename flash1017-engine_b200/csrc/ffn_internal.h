@@ -104,6 +104,11 @@ struct RoutedCalls {
   cudaStream_t side = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
 };
+// Argument checks of the expert entry points: the shape rules alone (before
+// any weight bytes are read from the caller's pointers), and the full check
+// of a descriptor holding device pointers.
+int validate_expert_shape(int format, size_t inter, size_t hidden, const char *what);
+int validate_expert(const ffn_b200_expert &e, size_t inter, size_t hidden, const char *what);
 constexpr int kCallsMax = 64;  // calls per routed_calls run
 size_t routed_calls_ws_bytes(size_t inter, size_t hidden, int n, int x_rows, int out_rows);
 size_t routed_calls_stage_bytes(int n, int out_rows);

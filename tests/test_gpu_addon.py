@@ -258,3 +258,34 @@ def test_mxfp4_wide_scale_range_through_the_abi(oracle, ffn, cuda, L):
     assert L.gx10_rust_mxfp4_mlp_accum(I, H, p(ws[0][0]), p(ws[0][1]), p(ws[1][0]), p(ws[1][1]),
                                        p(ws[2][0]), p(ws[2][1]), p(x), p(out), 0.5, False, True)
     oracle.assert_close(out, 0.5 * oe.forward(x), what="mxfp4 expert, wide scales")
+
+
+def test_bad_shape_fails_at_the_call_and_leaves_a_clean_state(oracle, ffn, cuda, L):
+    """Shapes the kernels cannot run (NVFP4 hidden % 64, MXFP4 hidden % 128) make
+    that call return false (the host then runs its CPU twin), with the weight
+    arrays sized for the claimed dims.  A pending sequence to another target is
+    delivered first, and the next sequence is unaffected."""
+    H, I = 512, 256
+    es = [nv_expert(oracle, 70 + k, I, H) for k in range(2)]
+    x = bench_x(H)
+    out = np.zeros(H, dtype=np.float32)
+    assert call(L, es[0], I, H, x, out, 0.5, True, False)  # queued
+    bH = 96
+    w = np.zeros(I * bH // 2, dtype=np.uint8)
+    s = np.full(I * bH // 16, 0x38, dtype=np.uint8)
+    bad = oracle.Nvfp4Expert(I, bH, (w, w, w), (s, s, s), (1.0, 1.0, 1.0))
+    xb, ob = bench_x(bH), np.zeros(bH, dtype=np.float32)
+    assert not call(L, bad, I, bH, xb, ob, 0.5, True, True)
+    oracle.assert_close(out, np.float32(0.5) * es[0].forward(x), rel=1e-4, what="sequence before the failure")
+    mH = 320
+    mw = np.zeros(I * mH // 2, dtype=np.uint8)
+    ms = np.full(I * mH // 32, 127, dtype=np.uint8)
+    mo = np.zeros(mH, dtype=np.float32)
+    xm = bench_x(mH)
+    assert not L.gx10_rust_mxfp4_mlp_accum(I, mH, p(mw), p(ms), p(mw), p(ms), p(mw), p(ms), p(xm), p(mo),
+                                           1.0, False, True)
+    out2 = np.zeros(H, dtype=np.float32)
+    assert call(L, es[0], I, H, x, out2, 1.0, False, False)
+    assert call(L, es[1], I, H, x, out2, 0.25, True, True)
+    ref = reference(oracle, [(es[0], 1.0, False), (es[1], 0.25, True)], x)
+    oracle.assert_close(out2, ref, rel=1e-4, what="sequence after the failures")

@@ -42,6 +42,7 @@ EXPORTS = [
     "ffn_b200_mxfp8_matvec", "gx10_rust_mxfp8_mlp_accum", "gx10_rust_mxfp8_mlp_batch",
     "ffn_b200_st_open", "ffn_b200_st_close", "ffn_b200_st_count", "ffn_b200_st_name",
     "ffn_b200_st_find", "ffn_b200_st_expert_bytes", "ffn_b200_st_load_expert",
+    "ffn_b200_compress_ws_bytes", "ffn_b200_compress_ternary_b64",
 ]
 
 # Kernel kinds of ffn_b200_profile_read (FFN_B200_K_*).
@@ -135,6 +136,10 @@ def lib() -> C.CDLL:
         L.gx10_rust_ternary_158_mlp_batch.argtypes = [sz, sz, sz, vp, vp, vp, vp, vp, vp, f32, sz,
                                                       vp, vp, sz, vp, C.c_bool]
         L.gx10_rust_ternary_158_mlp_batch.restype = C.c_bool
+        L.ffn_b200_compress_ws_bytes.restype = sz
+        L.ffn_b200_compress_ws_bytes.argtypes = [sz, sz]
+        L.ffn_b200_compress_ternary_b64.argtypes = [sz, sz, vp, vp, f32, u64, vp, vp, vp, vp, vp, vp,
+                                                    vp, vp, sz, vp]
         L.ffn_b200_expert_ws_bytes.restype = sz
         L.ffn_b200_expert_ws_bytes.argtypes = [sz, sz, sz]
         L.ffn_b200_expert_forward.argtypes = [sz, sz, sz, C.POINTER(Expert), vp, vp, f32, i32,
@@ -451,6 +456,29 @@ class TernaryMatrix:
                                           _stream(stream)), "gen_core")
             core = (a, a_sc, b, b_sc)
         return cls(p, rs, rows, cols, core)
+
+    @classmethod
+    def compress(cls, w, s, gs: float, rows: int, cols: int, seed: int, stream=None):
+        """The 106 GB format's compressor (ffn_b200_compress_ternary_b64): an
+        NVFP4 matrix (device w [rows, cols/2], s [rows, cols/16], per-tensor
+        scale gs) -> ternary codes, row scales, U8 block-64 scales and the
+        rank-16 Q8 core of the residual."""
+        torch = _torch()
+        dev = w.device
+        p = torch.empty(rows * cols // 4, dtype=torch.uint8, device=dev)
+        rs = torch.empty(rows, dtype=torch.float32, device=dev)
+        bs = torch.empty(rows * cols // 64, dtype=torch.uint8, device=dev)
+        a = torch.empty(16 * cols, dtype=torch.int8, device=dev)
+        a_sc = torch.empty(16, dtype=torch.float32, device=dev)
+        b = torch.empty(rows * 16, dtype=torch.int8, device=dev)
+        b_sc = torch.empty(16, dtype=torch.float32, device=dev)
+        ws = _default_ws(dev).get(lib().ffn_b200_compress_ws_bytes(rows, cols))
+        check(lib().ffn_b200_compress_ternary_b64(rows, cols, _ptr(w), _ptr(s), float(gs),
+                                                  int(seed) & (2**64 - 1), _ptr(p), _ptr(rs),
+                                                  _ptr(bs), _ptr(b), _ptr(b_sc), _ptr(a), _ptr(a_sc),
+                                                  _ptr(ws), ws.numel(), _stream(stream)),
+              "compress_ternary_b64")
+        return cls(p, rs, rows, cols, (a, a_sc, b, b_sc), bs)
 
     def matvec(self, x, out=None, stream=None):
         torch = _torch()

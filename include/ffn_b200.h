@@ -327,6 +327,25 @@ FFN_B200_EXPORT int ffn_b200_st_load_expert(const ffn_b200_st *st, const char *p
                                             size_t inter, void *dev, size_t dev_bytes, void *stream,
                                             ffn_b200_expert *e);
 
+/* ------------------------------------------- 106 GB format compressor
+ * compress_nvfp4_matrix_to_158_jepa_q8 (flash1017.rs:10377-10645, with
+ * orthonormalize_cols_16 :10342-10372), which the reference runs on the CPU
+ * when it writes the 106 GB shards (:10700-10811).  One NVFP4 matrix (w [rows,
+ * cols/2] E2M1 pairs, s [rows, cols/16] E4M3, per-tensor scale gs; cols % 64
+ * == 0) becomes ternary codes packed [rows, cols/4] (16-byte aligned), row
+ * scales [rows], U8 block-64 scales [rows, cols/64], and the rank-16 Q8 core
+ * core_b [rows, 16] / core_b_sc [16] / core_a [16, cols] / core_a_sc [16] of
+ * the residual (seed: the reference's subspace-iteration seed).  The outputs
+ * are exactly the tensors ffn_b200_ternary_mat reads.  Device pointers, caller
+ * workspace, enqueued on `stream`. */
+FFN_B200_EXPORT size_t ffn_b200_compress_ws_bytes(size_t rows, size_t cols);
+FFN_B200_EXPORT int ffn_b200_compress_ternary_b64(size_t rows, size_t cols, const uint8_t *w,
+                                                  const uint8_t *s, float gs, uint64_t seed,
+                                                  uint8_t *packed, float *row_scales,
+                                                  uint8_t *block_scales, int8_t *core_b,
+                                                  float *core_b_sc, int8_t *core_a, float *core_a_sc,
+                                                  void *ws, size_t ws_bytes, void *stream);
+
 /* -------------------------------------------- reference-ABI support hooks
  * Host-side x_all buffer for gx10_rust_*_mlp_batch, for hosts that do not make
  * the shared-expert call (gx10_rust_mxfp8_mlp_batch hands x_all over itself,

@@ -600,3 +600,193 @@ ORC_API void orc_gen_core(uint64_t key, size_t rows, size_t cols, size_t rank, i
 ORC_API void orc_gen_normal(uint64_t key, size_t n, float stdev, float *out) {
     for (size_t i = 0; i < n; ++i) out[i] = normal_at(key, i) * stdev;
 }
+
+/* ------------------------------------------------------------------------- */
+/* NVFP4 -> 1.58-bit block-64 ternary + rank-16 Q8 core compressor            */
+/* (F:10342-10372 orthonormalize_cols_16, F:10377-10645                       */
+/* compress_nvfp4_matrix_to_158_jepa_q8), loop for loop.  The writer of the   */
+/* 106 GB format stores these outputs as .packed_ternary, .row_scales,        */
+/* .block_scales and .core_* (F:10783-10811).                                 */
+/* ------------------------------------------------------------------------- */
+static void orc_orthonormalize16(float *m /* [n][16] */, size_t n) {
+    if (n == 0) return;
+    for (int k = 0; k < 16; ++k) {
+        for (int j = 0; j < k; ++j) {
+            double dot = 0.0;
+            for (size_t r = 0; r < n; ++r) dot += (double)m[r * 16 + k] * (double)m[r * 16 + j];
+            const float d = (float)dot;
+            for (size_t r = 0; r < n; ++r) m[r * 16 + k] -= d * m[r * 16 + j];
+        }
+        double norm_sq = 0.0;
+        for (size_t r = 0; r < n; ++r) {
+            const double v = (double)m[r * 16 + k];
+            norm_sq += v * v;
+        }
+        const float inv_norm = norm_sq > 1e-24 ? (float)(1.0 / sqrt(norm_sq)) : 0.0f;
+        for (size_t r = 0; r < n; ++r) m[r * 16 + k] *= inv_norm;
+    }
+}
+
+static float orc_clampf(float v, float lo, float hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+/* w [rows, cols/2] packed E2M1, s [rows, cols/16] E4M3, gs the per-tensor
+ * scale; cols % 64 == 0.  Outputs: packed [rows, cols/4], row_scales [rows],
+ * block_scales [rows, cols/64], core_b [rows, 16], core_b_sc [16], core_a
+ * [16, cols], core_a_sc [16]; stats (or NULL) = orig_frob_sq, ternary_err_sq,
+ * jepa_err_sq.  Returns 0, or -1 for a bad shape / allocation failure. */
+ORC_API int orc_compress_ternary_b64(size_t rows, size_t cols, const uint8_t *w, const uint8_t *s,
+                                     float gs, uint64_t seed, uint8_t *packed, float *row_scales,
+                                     uint8_t *block_scales, int8_t *core_b, float *core_b_sc,
+                                     int8_t *core_a, float *core_a_sc, double *stats) {
+    if (rows == 0 || cols == 0 || cols % 64) return -1;
+    const size_t packed_cols = cols / 2, groups = cols / 16, pcols = (cols + 3) / 4, nblk = cols / 64;
+    float *res = (float *)malloc(rows * cols * sizeof(float));
+    float *gam = (float *)malloc(nblk * sizeof(float));
+    float *p = (float *)malloc(cols * 16 * sizeof(float));
+    float *q = (float *)malloc(rows * 16 * sizeof(float));
+    float *z = (float *)malloc(cols * 16 * sizeof(float));
+    if (!res || !gam || !p || !q || !z) {
+        free(res); free(gam); free(p); free(q); free(z);
+        return -1;
+    }
+    memset(packed, 0, rows * pcols);
+    double orig = 0.0, terr = 0.0;
+    static const float LUT[4] = {-1.0f, 0.0f, 1.0f, 0.0f};
+    for (size_t r = 0; r < rows; ++r) {
+        const uint8_t *wr = w + r * packed_cols, *sr = s + r * groups;
+        float *rr = res + r * cols;
+        for (size_t g = 0; g < groups; ++g) {
+            const float g_sc = orc_e4m3_to_f32(sr[g]) * gs;
+            for (int k = 0; k < 8; ++k) {
+                const uint8_t b = wr[g * 8 + k];
+                const float w0 = E2M1_LUT[b & 0x0F] * g_sc, w1 = E2M1_LUT[b >> 4] * g_sc;
+                rr[g * 16 + 2 * k] = w0;
+                rr[g * 16 + 2 * k + 1] = w1;
+                orig += (double)w0 * (double)w0 + (double)w1 * (double)w1;
+            }
+        }
+        uint8_t *pr = packed + r * pcols;
+        float max_gamma = 0.0f;
+        for (size_t blk = 0; blk < nblk; ++blk) {
+            const float *wb = rr + blk * 64;
+            float sq = 0.0f;
+            for (int i = 0; i < 64; ++i) sq += wb[i] * wb[i];
+            const float rms = sqrtf(sq * (1.0f / 64.0f));
+            if (rms <= 1e-12f) {
+                gam[blk] = 0.0f;
+                memset(pr + blk * 16, 0x55, 16);
+                continue;
+            }
+            static const float F[4] = {0.42f, 0.54f, 0.66f, 0.78f};
+            float best_score = -1.0f, best_gamma = 0.0f, best_th = 0.58f * rms;
+            for (int f = 0; f < 4; ++f) {
+                const float th = F[f] * rms;
+                float dot = 0.0f;
+                uint32_t cnt = 0;
+                for (int i = 0; i < 64; ++i) {
+                    if (wb[i] > th) { dot += wb[i]; ++cnt; }
+                    else if (wb[i] < -th) { dot -= wb[i]; ++cnt; }
+                }
+                if (cnt > 0) {
+                    const float score = (dot * dot) / (float)cnt;
+                    if (score > best_score) {
+                        best_score = score;
+                        best_gamma = dot / (float)cnt;
+                        best_th = th;
+                    }
+                }
+            }
+            gam[blk] = best_gamma;
+            if (best_gamma > max_gamma) max_gamma = best_gamma;
+            for (int i = 0; i < 64; ++i) {
+                const uint8_t code = wb[i] > best_th ? 2 : (wb[i] < -best_th ? 0 : 1);
+                pr[blk * 16 + (i >> 2)] |= (uint8_t)(code << ((i & 3) * 2));
+            }
+        }
+        const float row_sc = max_gamma > 1e-12f ? max_gamma / 255.0f : 0.0f;
+        row_scales[r] = row_sc;
+        for (size_t blk = 0; blk < nblk; ++blk) {
+            const uint8_t u8 = row_sc > 0.0f ? (uint8_t)orc_clampf(roundf(gam[blk] / row_sc), 0.0f, 255.0f) : 0;
+            block_scales[r * nblk + blk] = u8;
+            const float qg = (float)u8 * row_sc;
+            float *rb = rr + blk * 64;
+            for (int i = 0; i < 16; ++i) {
+                const uint8_t pb = pr[blk * 16 + i];
+                for (int u = 0; u < 4; ++u) {
+                    const float v = rb[4 * i + u] - LUT[(pb >> (2 * u)) & 3] * qg;
+                    rb[4 * i + u] = v;
+                    terr += (double)v * (double)v;
+                }
+            }
+        }
+    }
+    /* randomized subspace iteration, rank 16, two sweeps */
+    uint64_t rng = seed ^ 0x9E3779B97F4A7C15ull;
+    for (size_t c = 0; c < cols; ++c)
+        for (int k = 0; k < 16; ++k) {
+            rng += 0x9E3779B97F4A7C15ull;
+            uint64_t x = rng;
+            x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+            x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+            x ^= x >> 31;
+            p[c * 16 + k] = (float)((int32_t)(x >> 40) - (1 << 23)) * (1.0f / (float)(1 << 23));
+        }
+    orc_orthonormalize16(p, cols);
+    for (int sweep = 0; sweep < 2; ++sweep) {
+        for (size_t r = 0; r < rows; ++r) {
+            float acc[16] = {0};
+            const float *rr = res + r * cols;
+            for (size_t c = 0; c < cols; ++c)
+                for (int k = 0; k < 16; ++k) acc[k] += rr[c] * p[c * 16 + k];
+            memcpy(q + r * 16, acc, sizeof(acc));
+        }
+        orc_orthonormalize16(q, rows);
+        memset(z, 0, cols * 16 * sizeof(float));
+        for (size_t r = 0; r < rows; ++r) {
+            const float *rr = res + r * cols;
+            for (size_t c = 0; c < cols; ++c)
+                for (int k = 0; k < 16; ++k) z[c * 16 + k] += rr[c] * q[r * 16 + k];
+        }
+        if (sweep == 0) {
+            memcpy(p, z, cols * 16 * sizeof(float));
+            orc_orthonormalize16(p, cols);
+        }
+    }
+    double captured = 0.0;
+    for (int k = 0; k < 16; ++k) {
+        float max_u = 0.0f;
+        for (size_t r = 0; r < rows; ++r)
+            if (fabsf(q[r * 16 + k]) > max_u) max_u = fabsf(q[r * 16 + k]);
+        const float b_sc = max_u > 1e-12f ? max_u / 127.0f : 0.0f;
+        core_b_sc[k] = b_sc;
+        for (size_t r = 0; r < rows; ++r) core_b[r * 16 + k] = 0;
+        if (b_sc > 0.0f) {
+            const float inv_b = 1.0f / b_sc;
+            for (size_t r = 0; r < rows; ++r)
+                core_b[r * 16 + k] = (int8_t)orc_clampf(roundf(q[r * 16 + k] * inv_b), -127.0f, 127.0f);
+        }
+        float max_z = 0.0f;
+        double col_norm_sq = 0.0;
+        for (size_t c = 0; c < cols; ++c) {
+            const float zv = z[c * 16 + k];
+            if (fabsf(zv) > max_z) max_z = fabsf(zv);
+            col_norm_sq += (double)zv * (double)zv;
+        }
+        captured += col_norm_sq;
+        const float a_sc = max_z > 1e-12f ? max_z / 127.0f : 0.0f;
+        core_a_sc[k] = a_sc;
+        for (size_t c = 0; c < cols; ++c) core_a[k * cols + c] = 0;
+        if (a_sc > 0.0f) {
+            const float inv_a = 1.0f / a_sc;
+            for (size_t c = 0; c < cols; ++c)
+                core_a[k * cols + c] = (int8_t)orc_clampf(roundf(z[c * 16 + k] * inv_a), -127.0f, 127.0f);
+        }
+    }
+    if (stats) {
+        stats[0] = orig;
+        stats[1] = terr;
+        stats[2] = terr - captured > 0.0 ? terr - captured : 0.0;
+    }
+    free(res); free(gam); free(p); free(q); free(z);
+    return 0;
+}

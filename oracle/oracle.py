@@ -66,6 +66,9 @@ def lib() -> C.CDLL:
         L.orc_e8m0_to_f32.argtypes = [C.c_uint8]
         L.orc_mxfp4_matvec.argtypes = [sz, sz, vp, vp, vp, vp]
         L.orc_mxfp8_matvec.argtypes = [sz, sz, vp, vp, vp, vp]
+        L.orc_compress_ternary_b64.argtypes = [sz, sz, vp, vp, f32, C.c_uint64, vp, vp, vp, vp, vp, vp,
+                                               vp, vp]
+        L.orc_compress_ternary_b64.restype = C.c_int
         L.orc_mx_expert.argtypes = [i32, sz, sz, vp, vp, vp, vp, vp]
         L.orc_combine.argtypes = [sz, sz, sz, vp, vp, vp]
         L.orc_derive.restype = u64
@@ -121,6 +124,28 @@ def mxfp8_matvec(w, s, x, rows, cols) -> np.ndarray:
     """F:1940-1984: E4M3 [rows, cols] with E8M0 scales per 32 x 32 block."""
     out = np.empty(rows, dtype=np.float32)
     lib().orc_mxfp8_matvec(rows, cols, _p(w), _p(s), _p(np.ascontiguousarray(x, np.float32)), _p(out))
+    return out
+
+
+def compress_ternary_b64(w: np.ndarray, s: np.ndarray, gs: float, rows: int, cols: int,
+                         seed: int) -> dict:
+    """The reference's NVFP4 -> 1.58-bit block-64 ternary + rank-16 Q8 core
+    compressor (F:10377-10645): packed [rows, cols/4], row_scales [rows],
+    block_scales [rows, cols/64], core_b [rows, 16] int8, core_b_sc [16],
+    core_a [16, cols] int8, core_a_sc [16], and the f64 error sums
+    orig_frob_sq, ternary_err_sq, jepa_err_sq."""
+    out = dict(packed=np.empty(rows * cols // 4, np.uint8), row_scales=np.empty(rows, np.float32),
+               block_scales=np.empty(rows * cols // 64, np.uint8), core_b=np.empty(rows * 16, np.int8),
+               core_b_sc=np.empty(16, np.float32), core_a=np.empty(16 * cols, np.int8),
+               core_a_sc=np.empty(16, np.float32))
+    st = np.empty(3, np.float64)
+    rc = lib().orc_compress_ternary_b64(rows, cols, _p(np.ascontiguousarray(w)), _p(np.ascontiguousarray(s)),
+                                        float(gs), int(seed) & (2**64 - 1), _p(out["packed"]),
+                                        _p(out["row_scales"]), _p(out["block_scales"]), _p(out["core_b"]),
+                                        _p(out["core_b_sc"]), _p(out["core_a"]), _p(out["core_a_sc"]), _p(st))
+    if rc:
+        raise ValueError("compress_ternary_b64: cols must be a positive multiple of 64")
+    out.update(orig_frob_sq=float(st[0]), ternary_err_sq=float(st[1]), jepa_err_sq=float(st[2]))
     return out
 
 

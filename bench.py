@@ -68,7 +68,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["config4", "config3", "expert"], default="config4")
+    ap.add_argument("--workload", choices=["config4", "config3", "expert", "compress"], default="config4")
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--experts", type=int, default=384)
@@ -900,8 +900,133 @@ def run_expert(a):
     return 0
 
 
+def run_compress(a):
+    """The 106 GB format's compressor (flash1017.rs:10377-10645) on the GPU: a
+    step compresses every NVFP4 matrix of a pool of experts (gate, up, down of
+    each) into ternary codes + block-64 scales + the rank-16 Q8 core."""
+    import ctypes as C
+
+    import numpy as np
+    import torch
+
+    import ffn_b200 as F
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    H, I, P = a.hidden, a.inter, a.pool
+    shapes = ((I, H), (I, H), (H, I))
+    experts = [F.SwigluExpert.generate(F.FMT_NVFP4, a.seed, 0, e, I, H) for e in range(P)]
+    L = F.lib()
+    jobs = []  # (matrix, rows, cols, outputs)
+    for e, ex in enumerate(experts):
+        for k, (m, (r, c)) in enumerate(zip(ex.mats, shapes)):
+            outs = (torch.empty(r * c // 4, dtype=torch.uint8, device=dev),
+                    torch.empty(r, dtype=torch.float32, device=dev),
+                    torch.empty(r * c // 64, dtype=torch.uint8, device=dev),
+                    torch.empty(r * 16, dtype=torch.int8, device=dev),
+                    torch.empty(16, dtype=torch.float32, device=dev),
+                    torch.empty(16 * c, dtype=torch.int8, device=dev),
+                    torch.empty(16, dtype=torch.float32, device=dev))
+            jobs.append((m, r, c, outs, 1000 * e + k))
+    ws = torch.empty(max(L.ffn_b200_compress_ws_bytes(r, c) for r, c in shapes), dtype=torch.uint8,
+                     device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    ptr = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+
+    def step():
+        for m, r, c, o, seed in jobs:
+            rc = L.ffn_b200_compress_ternary_b64(r, c, ptr(m.w), ptr(m.s), float(m.gs), seed, *map(ptr, o),
+                                                 ptr(ws), ws.numel(), C.c_void_p(stream))
+            if rc:
+                raise RuntimeError(L.ffn_b200_last_error().decode())
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(_bus_id(dev, 0))
+    clocks.start()
+    time.sleep(0.3)
+    n0 = F.launch_count()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(a.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    launches = F.launch_count() - n0
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    n_exp = P * a.steps
+    value = n_exp / (ms * 1e-3)
+    in_b = sum(r * c // 2 + r * c // 16 for r, c in shapes)
+    out_b = sum(r * c // 4 + r * 4 + r * c // 64 + 16 * (r + c) + 128 for r, c in shapes)
+    achieved = (in_b + out_b) * n_exp / (ms * 1e-3) / 1e9
+    # end to end: each matrix's NVFP4 bytes uploaded from pinned host memory, the outputs read back
+    w_h = [m.w.cpu().pin_memory() for m, *_ in jobs]
+    s_h = [m.s.cpu().pin_memory() for m, *_ in jobs]
+    o_h = [[t.cpu().pin_memory() for t in o] for _, _, _, o, _ in jobs]
+    for i in range(a.warmup + a.steps):
+        if i == a.warmup:
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        for j, (m, r, c, o, seed) in enumerate(jobs):
+            m.w.copy_(w_h[j], non_blocking=True)
+            m.s.copy_(s_h[j], non_blocking=True)
+        step()
+        for j, (_, _, _, o, _) in enumerate(jobs):
+            for hdst, dsrc in zip(o_h[j], o):
+                hdst.copy_(dsrc, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e = n_exp / (e0.elapsed_time(e1) * 1e-3)
+    peaks = _peaks()
+    cpu = None
+    if not a.no_cpu_baseline:
+        import oracle as O
+        m, r, c, _, seed = jobs[0]
+        w0, s0 = m.w.cpu().numpy(), m.s.cpu().numpy()
+        n, c0 = 0, time.perf_counter()
+        while n == 0 or time.perf_counter() - c0 < min(a.cpu_seconds, 6.0):
+            O.compress_ternary_b64(w0, s0, m.gs, r, c, seed)
+            n += 1
+        dt = time.perf_counter() - c0
+        cpu = {"value": n / dt / 3, "unit": "expert compressions/s", "cores": 1, "kind": "port",
+               "sample": f"oracle compression of one {r}x{c} matrix, {n} times in {dt:.1f} s "
+                         f"(an expert = 3 matrices of that size)"}
+    line = {
+        "metric": f"106 GB-format expert compressions/s (3 NVFP4 matrices of {I}x{H} each)",
+        "value": value, "unit": "expert compressions/s", "n_gpus": 1, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32 (bit-exact to the reference's f32 compressor)",
+        "data": "synthetic (seeded random-init NVFP4 experts)",
+        "config": {"workload": f"compressor: pool of {P} NVFP4 experts per step", "hidden": H, "inter": I,
+                   "pool": P, "seed": a.seed,
+                   "l2": "no flush: each matrix's workspace residual is written and read twice per call"},
+        "e2e": {"value": e2e, "unit": "expert compressions/s", "h2d_bytes_per_step": in_b * P,
+                "d2h_bytes_per_step": out_b * P},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "kernel": "compressor (all its launches)", "achieved": achieved,
+                     "peak": peaks[0], "unit": "GB/s", "frac": achieved / peaks[0], "traffic": None,
+                     "peak_source": peaks[1], "algorithmic_bytes_per_expert": in_b + out_b},
+        "cpu_baseline": cpu,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     a = parse_args()
+    if a.workload == "compress":
+        if a.seed is None:
+            a.seed = 5
+        if a.pool == 64:
+            a.pool = 8
+        if a.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "--workload compress has no "
+                              "reference arm; its cpu_baseline times the oracle"}))
+            return 0
+        return run_compress(a)
     if a.workload == "expert":
         for k, v in (("tokens", 1), ("layers", 1), ("seed", 0 if a.format == "nvfp4" else 1)):
             if getattr(a, k) is None:

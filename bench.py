@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""bench.py -- MoE expert-FFN tokens/s on 1/2/4/8 B200.
+"""bench.py -- MoE expert-FFN tokens/s on 1/2/4/8 B200 (benchmark config 4).
 
 Workload: a 40-layer NVFP4 MoE-FFN stack (hidden 4096, intermediate 2048, 384
 routed SwiGLU experts per layer, the reference's ffn_norm RMSNorm on the layer
@@ -23,7 +23,7 @@ Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
                        [--workload config4|config3]
 (N > 1 under torchrun, one rank per GPU).
 
---workload config3 measures BASELINE config 3 instead: one NVFP4 MoE layer
+--workload config3 measures benchmark config 3 instead: one NVFP4 MoE layer
 over a prefill of 8192 tokens (bf16-valued N(0,1) hidden states, seed 3,
 sigmoid top-6 of 384, no ffn_norm), which the library runs on its tensor-core
 grouped GEMM; a step is one layer pass, the roofline is the gate/up GEMM's
@@ -83,7 +83,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--format", choices=["nvfp4", "ternary106", "ternary", "mxfp4", "mxfp8"],
                     default="nvfp4",
-                    help="expert format: NVFP4 (BASELINE), the reference compressor's 106 GB "
+                    help="expert format: NVFP4 (the benchmark configs), the reference compressor's 106 GB "
                          "format (ternary + U8 block-64 scales + rank-16 Q8 core), config 1's "
                          "ternary + rank-16 core, MXFP4 (MTP experts), MXFP8 (shared expert); "
                          "config4 takes nvfp4 / ternary106, --workload expert all of them")
@@ -753,7 +753,7 @@ def _expert_mat_bytes(fmt, r, c):
 
 
 def run_expert(a):
-    """BASELINE configs 0 (NVFP4) and 1 (ternary + rank-16 core) and the other
+    """Benchmark configs 0 (NVFP4) and 1 (ternary + rank-16 core) and the other
     expert formats: one SwiGLU expert forward over `tokens` rows, cycling
     through a pool of distinct experts larger than L2 (a step = one pass over
     the pool); roofline = the expert's weight bytes over HBM."""

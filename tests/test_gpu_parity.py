@@ -1,6 +1,6 @@
 """GPU parity tests: the CUDA library (through its C-ABI) against the CPU oracle.
 
-Tolerance: decoded weights and top-k indices bit-exact
+Tolerance (the benchmark configs'): decoded weights and top-k indices bit-exact
 (ties excepted), fp32-accumulated outputs max|y-ref|/max|ref| <= 1e-3 and
 cosine >= 0.99999 (oracle.assert_close).
 """
@@ -192,7 +192,7 @@ def test_ternary_known_answer_fixture(oracle, ffn, cuda):
 # ----------------------------------------------------------------- experts
 @pytest.mark.parametrize("seq", [1, 4, 8, 13])
 def test_nvfp4_expert_config0(oracle, ffn, cuda, seq):
-    """BASELINE config 0 shapes (H 4096, I 2048), seed 0."""
+    """Benchmark config 0 shapes (H 4096, I 2048), seed 0."""
     H, I = 4096, 2048
     e = ffn.SwigluExpert.generate(ffn.FMT_NVFP4, 0, 0, 0, I, H)
     x = ffn.gen_normal(ffn.path_key(0, 0, 0, ffn.TAG_X), seq * H).view(seq, H)
@@ -206,7 +206,7 @@ def test_nvfp4_expert_config0(oracle, ffn, cuda, seq):
 @pytest.mark.parametrize("seq", [1, 6])
 @pytest.mark.parametrize("with_core", [True, False])
 def test_ternary_expert_config1(oracle, ffn, cuda, seq, with_core):
-    """BASELINE config 1 shapes, seed 1, rank-16 Q8 cores on all three matrices."""
+    """Benchmark config 1 shapes, seed 1, rank-16 Q8 cores on all three matrices."""
     H, I = 4096, 2048
     e = ffn.SwigluExpert.generate(ffn.FMT_TERNARY, 1, 0, 0, I, H, with_core=with_core,
                                   proj_scale=1.0)
@@ -345,7 +345,7 @@ def test_moe_layer_residual_and_expert_range(oracle, ffn, cuda):
 
 
 def test_moe_config2_sampled(oracle, ffn, cuda):
-    """384 NVFP4 experts (H 4096, I 2048), 64 tokens, router
+    """Benchmark config 2: 384 NVFP4 experts (H 4096, I 2048), 64 tokens, router
     fp32 N(0, 0.02), sigmoid top-6, seed 2.  All 64 tokens' top-6 indices are
     compared with the oracle router; outputs of a sample of tokens with the
     oracle experts they hit."""

@@ -7,7 +7,7 @@ Shards are written here the way the reference's 106 GB writer lays them out
 aligned), with weights from the oracle's generators.  CPU tests: header
 parsing, lookup, expert planning and malformed files.  GPU tests: experts
 loaded into HBM run through the kernels and match the oracle on the same
-bytes, at the BASELINE dims and at the reference checkpoint's own dims
+bytes, at the benchmark configs' dims and at the reference checkpoint's own dims
 (H 5120, I 2304, flash1017.rs:7268-7269)."""
 import json
 import os

@@ -712,11 +712,14 @@ ORC_API int orc_compress_ternary_b64(size_t rows, size_t cols, const uint8_t *w,
             float *rb = rr + blk * 64;
             for (int i = 0; i < 16; ++i) {
                 const uint8_t pb = pr[blk * 16 + i];
+                float v[4];
                 for (int u = 0; u < 4; ++u) {
-                    const float v = rb[4 * i + u] - LUT[(pb >> (2 * u)) & 3] * qg;
-                    rb[4 * i + u] = v;
-                    terr += (double)v * (double)v;
+                    v[u] = rb[4 * i + u] - LUT[(pb >> (2 * u)) & 3] * qg;
+                    rb[4 * i + u] = v[u];
                 }
+                /* one expression of four squares, as F:10514-10517 adds them */
+                terr += (double)v[0] * (double)v[0] + (double)v[1] * (double)v[1] +
+                        (double)v[2] * (double)v[2] + (double)v[3] * (double)v[3];
             }
         }
     }

@@ -17,6 +17,11 @@ it, since the Rust reference itself cannot be executed here:
     (hardware_addon.rs:1074: sin(0.013 i) * 0.5).
   * generator.json -- SHA-256 of seeded generator outputs (pins the generator
     that the CUDA library's device generator must reproduce byte for byte).
+  * compress.json -- the 106 GB format's compressor (flash1017.rs:10342-10645:
+    block-64 ternary quantisation, rank-16 subspace iteration with f64
+    Gram-Schmidt, int8 core) restated term by term in numpy float32 scalars and
+    Python f64 floats, on the reference's own compressor-test input: SHA-256 of
+    every output array and the three f64 error sums.
 """
 import hashlib
 import json
@@ -180,6 +185,160 @@ def route_py(logits, top_k, score_fn):
     return [c[0] for c in sel], [c[1] * num / tot for c in sel]
 
 
+def round_away(v) -> F:
+    """Rust f32::round: halves away from zero."""
+    return F(math.copysign(math.floor(abs(float(v)) + 0.5), float(v)))
+
+
+def ortho16_py(m):
+    """flash1017.rs:10342-10372 on a list of 16-float rows (in place)."""
+    n = len(m)
+    for k in range(16):
+        for j in range(k):
+            dot = 0.0
+            for r in range(n):
+                dot += float(m[r][k]) * float(m[r][j])
+            d = F(dot)
+            for r in range(n):
+                m[r][k] = F(m[r][k] - F(d * m[r][j]))
+        norm_sq = 0.0
+        for r in range(n):
+            v = float(m[r][k])
+            norm_sq += v * v
+        inv = F(1.0 / math.sqrt(norm_sq)) if norm_sq > 1e-24 else F(0.0)
+        for r in range(n):
+            m[r][k] = F(m[r][k] * inv)
+
+
+def compress_py(w, s, gs, rows, cols, seed):
+    """flash1017.rs:10377-10645 restated loop for loop."""
+    gs = F(gs)
+    pcols, groups, nblk, tcols = cols // 2, cols // 16, cols // 64, cols // 4
+    e4 = [e4m3(b) for b in range(256)]
+    packed = np.zeros(rows * tcols, np.uint8)
+    row_scales = np.zeros(rows, np.float32)
+    block_scales = np.zeros(rows * nblk, np.uint8)
+    res = [[F(0.0)] * cols for _ in range(rows)]
+    orig = terr = 0.0
+    for r in range(rows):
+        rr = res[r]
+        for g in range(groups):
+            g_sc = F(e4[int(s[r * groups + g])] * gs)
+            for k in range(8):
+                b = int(w[r * pcols + g * 8 + k])
+                w0, w1 = F(F(LUT4[b & 15]) * g_sc), F(F(LUT4[b >> 4]) * g_sc)
+                rr[g * 16 + 2 * k], rr[g * 16 + 2 * k + 1] = w0, w1
+                orig += float(w0) * float(w0) + float(w1) * float(w1)
+        gam = [F(0.0)] * nblk
+        max_gamma = F(0.0)
+        for blk in range(nblk):
+            wb = rr[blk * 64:(blk + 1) * 64]
+            sq = F(0.0)
+            for v in wb:
+                sq = F(sq + F(v * v))
+            rms = F(np.sqrt(F(sq * F(1.0 / 64.0))))
+            base = r * tcols + blk * 16
+            if rms <= F(1e-12):
+                packed[base:base + 16] = 0x55
+                continue
+            best_score, best_gamma, best_th = F(-1.0), F(0.0), F(F(0.58) * rms)
+            for fac in (0.42, 0.54, 0.66, 0.78):
+                th = F(F(fac) * rms)
+                dot, cnt = F(0.0), 0
+                for v in wb:
+                    if v > th:
+                        dot, cnt = F(dot + v), cnt + 1
+                    elif v < -th:
+                        dot, cnt = F(dot - v), cnt + 1
+                if cnt > 0:
+                    score = F(F(dot * dot) / F(cnt))
+                    if score > best_score:
+                        best_score, best_gamma, best_th = score, F(dot / F(cnt)), th
+            gam[blk] = best_gamma
+            if best_gamma > max_gamma:
+                max_gamma = best_gamma
+            for i, v in enumerate(wb):
+                code = 2 if v > best_th else (0 if v < -best_th else 1)
+                packed[base + (i >> 2)] |= code << ((i & 3) * 2)
+        row_sc = F(max_gamma / F(255.0)) if max_gamma > F(1e-12) else F(0.0)
+        row_scales[r] = row_sc
+        for blk in range(nblk):
+            u8 = int(min(max(round_away(F(gam[blk] / row_sc)), 0.0), 255.0)) if row_sc > F(0.0) else 0
+            block_scales[r * nblk + blk] = u8
+            qg = F(F(u8) * row_sc)
+            for i in range(16):
+                pb = int(packed[r * tcols + blk * 16 + i])
+                v = []
+                for u in range(4):
+                    c = blk * 64 + 4 * i + u
+                    rr[c] = F(rr[c] - F(F(TLUT[(pb >> (2 * u)) & 3]) * qg))
+                    v.append(float(rr[c]))
+                terr += v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]
+    M, G = (1 << 64) - 1, 0x9E3779B97F4A7C15
+    rng = (seed ^ G) & M
+    p = []
+    for c in range(cols):
+        row = []
+        for k in range(16):
+            rng = (rng + G) & M
+            x = rng
+            x = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & M
+            x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & M
+            x ^= x >> 31
+            row.append(F(F((x >> 40) - (1 << 23)) * F(1.0 / (1 << 23))))
+        p.append(row)
+    ortho16_py(p)
+    for sweep in range(2):
+        q = []
+        for r in range(rows):
+            acc = [F(0.0)] * 16
+            for c in range(cols):
+                v = res[r][c]
+                for k in range(16):
+                    acc[k] = F(acc[k] + F(v * p[c][k]))
+            q.append(acc)
+        ortho16_py(q)
+        z = [[F(0.0)] * 16 for _ in range(cols)]
+        for r in range(rows):
+            for c in range(cols):
+                v = res[r][c]
+                for k in range(16):
+                    z[c][k] = F(z[c][k] + F(v * q[r][k]))
+        if sweep == 0:
+            p = [list(row) for row in z]
+            ortho16_py(p)
+    core_b, core_a = np.zeros(rows * 16, np.int8), np.zeros(16 * cols, np.int8)
+    b_sc, a_sc = np.zeros(16, np.float32), np.zeros(16, np.float32)
+    captured = 0.0
+    for k in range(16):
+        mx = F(0.0)
+        for r in range(rows):
+            if abs(q[r][k]) > mx:
+                mx = abs(q[r][k])
+        b_sc[k] = F(mx / F(127.0)) if mx > F(1e-12) else F(0.0)
+        if b_sc[k] > 0:
+            inv = F(F(1.0) / b_sc[k])
+            for r in range(rows):
+                core_b[r * 16 + k] = int(min(max(round_away(F(q[r][k] * inv)), -127.0), 127.0))
+        mz, cn = F(0.0), 0.0
+        for c in range(cols):
+            if abs(z[c][k]) > mz:
+                mz = abs(z[c][k])
+            cn += float(z[c][k]) * float(z[c][k])
+        captured += cn
+        a_sc[k] = F(mz / F(127.0)) if mz > F(1e-12) else F(0.0)
+        if a_sc[k] > 0:
+            inv = F(F(1.0) / a_sc[k])
+            for c in range(cols):
+                core_a[k * cols + c] = int(min(max(round_away(F(z[c][k] * inv)), -127.0), 127.0))
+    return dict(packed=packed, row_scales=row_scales, block_scales=block_scales, core_b=core_b,
+                core_b_sc=b_sc, core_a=core_a, core_a_sc=a_sc, orig_frob_sq=orig, ternary_err_sq=terr,
+                jepa_err_sq=max(terr - captured, 0.0))
+
+
+COMPRESS_ARRAYS = ("packed", "row_scales", "block_scales", "core_b", "core_b_sc", "core_a", "core_a_sc")
+
+
 def bench_x(n):
     return np.array([F(math.sin(i * 0.013) * 0.5) for i in range(n)], dtype=np.float32)
 
@@ -261,6 +420,13 @@ def main():
     gen["core_64x4096"] = [h(c_.a), h(c_.a_sc), h(c_.b), h(c_.b_sc)]
     gen["normal_100000"] = h(O.gen_normal(O.key(2, 0, 0, O.TAG_X), 100000))
     json.dump(gen, open(os.path.join(HERE, "generator.json"), "w"), indent=1)
+    # compressor on the reference's compressor-test input (flash1017.rs:10975-10995)
+    cp = compress_py(w, s, 0.02, rows, cols, 42)
+    json.dump({"rows": rows, "cols": cols, "gs": 0.02, "seed": 42,
+               "sha256": {k: h(cp[k]) for k in COMPRESS_ARRAYS},
+               "orig_frob_sq": cp["orig_frob_sq"], "ternary_err_sq": cp["ternary_err_sq"],
+               "jepa_err_sq": cp["jepa_err_sq"]},
+              open(os.path.join(HERE, "compress.json"), "w"), indent=1)
     print("wrote", sorted(os.listdir(HERE)))
 
 

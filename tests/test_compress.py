@@ -60,3 +60,18 @@ def test_zero_block_and_bad_shape(oracle):
     assert np.all(c["packed"] == 0x55) and np.all(c["block_scales"] == 0) and c["row_scales"][0] == 0.0
     with pytest.raises(ValueError):
         oracle.compress_ternary_b64(np.zeros(48, np.uint8), np.zeros(6, np.uint8), 1.0, 1, 96, 1)
+
+
+def test_oracle_matches_golden_restatement(oracle):
+    """The C oracle against the independent float32 / f64 restatement of
+    tests/golden/make_golden.py on the same input: every output byte (SHA-256)
+    and the three f64 error sums."""
+    import hashlib
+    import json
+    g = json.load(open(os.path.join(ROOT, "tests", "golden", "compress.json")))
+    w, s, gs, rows, cols = reference_test_input()
+    c = oracle.compress_ternary_b64(w, s, gs, rows, cols, g["seed"])
+    for k, digest in g["sha256"].items():
+        assert hashlib.sha256(np.ascontiguousarray(c[k]).tobytes()).hexdigest() == digest, k
+    for k in ("orig_frob_sq", "ternary_err_sq", "jepa_err_sq"):
+        assert c[k] == g[k], k

@@ -18,7 +18,8 @@
 //      (core_b = q, core_a = z^T).
 // Every f32 operation is rounded separately (__fmul_rn / __fadd_rn, no FMA
 // contraction) and every sum runs in the reference's order (the 64 values of a
-// block, R p over the columns of a row, R^T q over the rows of a column), so
+// block, R p over the columns of a row, R^T q over the rows of a column, one thread
+// per output element), so
 // codes, scales and the residual are bit-exact.  The Gram-Schmidt dots and
 // norms are f64 sums rounded to f32 as in the reference; here they are summed
 // in a fixed tree order, which rounds to the same f32 value except in rare
@@ -187,45 +188,42 @@ __global__ void __launch_bounds__(1024) orthonormalize16_kernel(float *m, int n)
   }
 }
 
-// q[r][k] = sum over c (in order) of R[r][c] p[c][k]; one thread per row.
-__global__ void __launch_bounds__(128) rsi_rp_kernel(int rows, int cols, const float *__restrict__ R,
+// q[r][k] = sum over c (in order) of R[r][c] p[c][k]; one thread per (row, k),
+// so each sum keeps the reference's order and 16x as many threads hide the
+// load latency.
+__global__ void __launch_bounds__(256) rsi_rp_kernel(int rows, int cols, const float *__restrict__ R,
                                                      const float *__restrict__ p, float *q) {
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= rows) return;
-  float acc[16];
-#pragma unroll
-  for (int k = 0; k < 16; ++k) acc[k] = 0.0f;
+  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (long long)rows * 16) return;
+  const int r = (int)(t >> 4), k = (int)(t & 15);
   const float4 *row = reinterpret_cast<const float4 *>(R + (size_t)r * cols);
+  const float *pk = p + k;
+  float acc = 0.0f;
+#pragma unroll 4
   for (int c4 = 0; c4 < cols / 4; ++c4) {
     const float4 v4 = __ldg(row + c4);
-    const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const float *pc = p + (size_t)(4 * c4 + u) * 16;
-#pragma unroll
-      for (int k = 0; k < 16; ++k) acc[k] = __fadd_rn(acc[k], __fmul_rn(vv[u], __ldg(pc + k)));
-    }
+    const float *pc = pk + (size_t)c4 * 64;
+    acc = __fadd_rn(acc, __fmul_rn(v4.x, __ldg(pc)));
+    acc = __fadd_rn(acc, __fmul_rn(v4.y, __ldg(pc + 16)));
+    acc = __fadd_rn(acc, __fmul_rn(v4.z, __ldg(pc + 32)));
+    acc = __fadd_rn(acc, __fmul_rn(v4.w, __ldg(pc + 48)));
   }
-#pragma unroll
-  for (int k = 0; k < 16; ++k) q[(size_t)r * 16 + k] = acc[k];
+  q[(size_t)r * 16 + k] = acc;
 }
 
-// z[c][k] = sum over r (in order) of R[r][c] q[r][k]; one thread per column.
-__global__ void __launch_bounds__(128) rsi_rtq_kernel(int rows, int cols, const float *__restrict__ R,
+// z[c][k] = sum over r (in order) of R[r][c] q[r][k]; one thread per (column, k).
+__global__ void __launch_bounds__(256) rsi_rtq_kernel(int rows, int cols, const float *__restrict__ R,
                                                       const float *__restrict__ q, float *z) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= cols) return;
-  float acc[16];
-#pragma unroll
-  for (int k = 0; k < 16; ++k) acc[k] = 0.0f;
-  for (int r = 0; r < rows; ++r) {
-    const float v = __ldg(R + (size_t)r * cols + c);
-    const float *qr = q + (size_t)r * 16;
-#pragma unroll
-    for (int k = 0; k < 16; ++k) acc[k] = __fadd_rn(acc[k], __fmul_rn(v, __ldg(qr + k)));
-  }
-#pragma unroll
-  for (int k = 0; k < 16; ++k) z[(size_t)c * 16 + k] = acc[k];
+  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (long long)cols * 16) return;
+  const int c = (int)(t >> 4), k = (int)(t & 15);
+  const float *col = R + c;
+  const float *qk = q + k;
+  float acc = 0.0f;
+#pragma unroll 8
+  for (int r = 0; r < rows; ++r)
+    acc = __fadd_rn(acc, __fmul_rn(__ldg(col + (size_t)r * cols), __ldg(qk + (size_t)r * 16)));
+  z[(size_t)c * 16 + k] = acc;
 }
 
 // Column k of m [n][16] -> int8 with scale max|.| / 127 (flash1017.rs:10583-10628);
@@ -309,11 +307,11 @@ int ffn_b200_compress_ternary_b64(size_t rows, size_t cols, const uint8_t *w, co
   float *p = c.p, *z = c.z;
   for (int sweep = 0; sweep < 2; ++sweep) {
     FFN_LAUNCH(FFN_B200_K_OTHER, st, "rsi_rp_kernel",
-               rsi_rp_kernel<<<(R + 127) / 128, 128, 0, st>>>(R, Cn, c.res, p, c.q));
+               rsi_rp_kernel<<<(R * 16 + 255) / 256, 256, 0, st>>>(R, Cn, c.res, p, c.q));
     FFN_LAUNCH(FFN_B200_K_OTHER, st, "orthonormalize16_kernel",
                orthonormalize16_kernel<<<1, 1024, 0, st>>>(c.q, R));
     FFN_LAUNCH(FFN_B200_K_OTHER, st, "rsi_rtq_kernel",
-               rsi_rtq_kernel<<<(Cn + 127) / 128, 128, 0, st>>>(R, Cn, c.res, c.q, z));
+               rsi_rtq_kernel<<<(Cn * 16 + 255) / 256, 256, 0, st>>>(R, Cn, c.res, c.q, z));
     if (sweep == 0) {  // p <- z, orthonormalised; the old p buffer takes the next z
       std::swap(p, z);
       FFN_LAUNCH(FFN_B200_K_OTHER, st, "orthonormalize16_kernel",

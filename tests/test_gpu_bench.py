@@ -1,4 +1,4 @@
-"""bench.py end to end on one GPU, both workloads at reduced sizes: the run
+"""bench.py end to end on one GPU, every workload at reduced sizes: the run
 exits 0 and prints one JSON line with the contract's keys."""
 import json
 import os
@@ -21,7 +21,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
      "--cpu-seconds", "1"],
     ["--workload", "expert", "--format", "ternary106", "--pool", "8", "--steps", "3", "--warmup", "3",
      "--no-cpu-baseline"],
-], ids=["config4", "config3", "config4-ternary106", "expert-mxfp4", "expert-ternary106"])
+    ["--workload", "compress", "--pool", "2", "--steps", "2", "--warmup", "3", "--no-cpu-baseline"],
+], ids=["config4", "config3", "config4-ternary106", "expert-mxfp4", "expert-ternary106", "compress"])
 def test_bench_line(args):
     r = subprocess.run([sys.executable, "bench.py", *args], cwd=ROOT, capture_output=True, text=True,
                        timeout=900)

@@ -248,7 +248,20 @@ int run_queue(Ctx &c) {
   return rc;
 }
 
-int flush_pending(Ctx &c) {
+// The host reads a fused call's `out` only after the call of the sequence that
+// passes sync_now (flash1017.rs:7440-7512, 8193-8262).  A sequence it abandons
+// (it breaks out of the loop and recomputes on its CPU path, dropping the
+// buffer: flash1017.rs:7483-7486, 8228-8229) is never written back, because
+// that memory may already be freed: the next call of any kind drops it.
+void drop_pending(Ctx &c) {
+  clear_queue(c);
+  c.pend_host = nullptr;
+  c.pend_n = 0;
+}
+
+// Run the queue and copy the result into the host's `out`: only while serving
+// a sync_now call that passed that same pointer.
+int deliver_pending(Ctx &c) {
   if (int rc = run_queue(c)) {
     c.pend_host = nullptr;
     c.pend_n = 0;
@@ -277,7 +290,7 @@ void run_sync(size_t x_n, const float *x, size_t out_n, float *out, F body) {
   Ctx &c = ctx();
   std::lock_guard<std::mutex> lk(c.mu);
   int rc = ensure_init(c);
-  if (!rc) rc = flush_pending(c);
+  drop_pending(c);
   if (!rc && (!x || !out)) rc = fail(FFN_B200_EINVAL, "reference ABI: null x/out");
   if (!rc) rc = c.x.ensure(x_n * sizeof(float));
   if (!rc) rc = c.out.ensure(out_n * sizeof(float));
@@ -304,7 +317,7 @@ float dot_common(int mode, const void *a, size_t a_bytes, const void *aux, size_
   std::lock_guard<std::mutex> lk(c.mu);
   float r = std::nanf("");
   int rc = ensure_init(c);
-  if (!rc) rc = flush_pending(c);
+  drop_pending(c);
   if (!rc && (!a || !x)) rc = fail(FFN_B200_EINVAL, "dot: null pointer");
   if (!rc) rc = c.tmp.ensure(a_bytes + aux_bytes + x_n * 4 + 1024);
   if (!rc) {
@@ -561,11 +574,11 @@ bool mlp_accum(const ffn_b200_expert &he, size_t inter, size_t hidden, const flo
   std::lock_guard<std::mutex> lk(c.mu);
   int rc = ensure_init(c);
   if (!rc && (!x || !out)) rc = fail(FFN_B200_EINVAL, "mlp_accum: null x/out");
-  // A new target flushes the previous pending one (and its queued calls).
-  if (!rc && c.pend_host && (c.pend_host != out || c.pend_n != hidden)) rc = flush_pending(c);
-  if (!rc && !c.queue.empty() &&
-      (c.q_src != 1 || c.q_inter != inter || c.q_hidden != hidden || !accumulate))
-    rc = run_queue(c);
+  // Another target, other dims, or an overwriting call (which replaces the
+  // whole row) begin a new sequence: the unsynced one is dropped.
+  if (c.pend_host && (c.pend_host != out || c.pend_n != hidden)) drop_pending(c);
+  if (!c.queue.empty() && (c.q_src != 1 || c.q_inter != inter || c.q_hidden != hidden || !accumulate))
+    drop_pending(c);
   if (!rc) rc = c.out.ensure(hidden * 4);
   if (!rc) rc = c.bx.ensure((size_t)ffn::kCallsMax * hidden * 4);
   ffn_b200_expert e = he;
@@ -588,13 +601,11 @@ bool mlp_accum(const ffn_b200_expert &he, size_t inter, size_t hidden, const flo
   if (!rc) {
     c.pend_host = out;
     c.pend_n = hidden;
-    if (sync_now) rc = flush_pending(c);
+    if (sync_now) rc = deliver_pending(c);
   }
   if (rc) {
     std::fprintf(stderr, "[ffn_b200] %s\n", ffn_b200_last_error());
-    clear_queue(c);
-    c.pend_host = nullptr;
-    c.pend_n = 0;
+    drop_pending(c);
     return false;
   }
   return true;
@@ -631,9 +642,8 @@ bool mlp_batch(const ffn_b200_expert &he, float wscale, size_t inter, size_t hid
   if (!rc && (b_len == 0 || b_len > 65535)) rc = fail(FFN_B200_EINVAL, "mlp_batch: b_len must be 1..65535");
   for (size_t k = 0; !rc && k < m; ++k)
     if (dst[k] >= b_len) rc = fail(FFN_B200_EINVAL, "mlp_batch: destination token out of range");
-  if (!rc && c.pend_host && (c.pend_host != out || c.pend_n != b_len * hidden)) rc = flush_pending(c);
-  if (!rc && !c.queue.empty() && (c.q_src != 2 || c.q_inter != inter || c.q_hidden != hidden))
-    rc = run_queue(c);
+  if (c.pend_host && (c.pend_host != out || c.pend_n != b_len * hidden)) drop_pending(c);
+  if (!c.queue.empty() && (c.q_src != 2 || c.q_inter != inter || c.q_hidden != hidden)) drop_pending(c);
   if (!rc) rc = c.out.ensure(b_len * hidden * 4);
   if (!rc) rc = ensure_xall(c);
   ffn_b200_expert e = he;
@@ -657,13 +667,11 @@ bool mlp_batch(const ffn_b200_expert &he, float wscale, size_t inter, size_t hid
   if (!rc) {
     c.pend_host = out;
     c.pend_n = b_len * hidden;
-    if (sync_now) rc = flush_pending(c);
+    if (sync_now) rc = deliver_pending(c);
   }
   if (rc) {
     std::fprintf(stderr, "[ffn_b200] %s\n", ffn_b200_last_error());
-    clear_queue(c);
-    c.pend_host = nullptr;
-    c.pend_n = 0;
+    drop_pending(c);
     return false;
   }
   return true;
@@ -759,7 +767,7 @@ bool gx10_rust_mxfp4_matvec(size_t rows, size_t cols, const uint8_t *packed_fp4,
   Ctx &c = ctx();
   std::lock_guard<std::mutex> lk(c.mu);
   int rc = ensure_init(c);
-  if (!rc) rc = flush_pending(c);  // a pending fused-expert output first
+  drop_pending(c);  // an unsynced fused-expert sequence was abandoned
   if (!rc && (!packed_fp4 || !scales_e8m0 || !x || !out || cols % 128))
     rc = fail(FFN_B200_EINVAL, "mxfp4_matvec: bad arguments");
   const void *dw = nullptr, *ds = nullptr;
@@ -840,7 +848,7 @@ bool gx10_rust_mxfp8_mlp_batch(size_t inter_rows, size_t hidden_cols, size_t seq
   if (!rc && (!x_all || !out_batch)) rc = fail(FFN_B200_EINVAL, "mxfp8_mlp_batch: null x_all/out_batch");
   if (!rc && (b_len == 0 || b_len > 65535 || b_len > x_total_tokens || x_total_tokens > (1u << 20)))
     rc = fail(FFN_B200_EINVAL, "mxfp8_mlp_batch: need 1 <= seq_len <= min(x_total_tokens, 65535)");
-  if (!rc) rc = flush_pending(c);  // a new layer: earlier work first
+  drop_pending(c);  // a new layer: an unsynced earlier one was abandoned
   if (!rc) {
     // x_all also holds the rows of this layer's routed *_mlp_batch calls
     c.xall_host = x_all;
@@ -883,13 +891,11 @@ bool gx10_rust_mxfp8_mlp_batch(size_t inter_rows, size_t hidden_cols, size_t seq
   if (!rc) {
     c.pend_host = out_batch;
     c.pend_n = b_len * H;
-    if (sync_now) rc = flush_pending(c);
+    if (sync_now) rc = deliver_pending(c);
   }
   if (rc) {
     std::fprintf(stderr, "[ffn_b200] %s\n", ffn_b200_last_error());
-    clear_queue(c);
-    c.pend_host = nullptr;
-    c.pend_n = 0;
+    drop_pending(c);
     return false;
   }
   return true;
@@ -929,8 +935,13 @@ int ffn_b200_set_batch_input(const float *x_all_host, size_t x_total_tokens, siz
 int ffn_b200_release_host_ranges(void) {
   Ctx &c = ctx();
   std::lock_guard<std::mutex> lk(c.mu);
-  int rc = flush_pending(c);
-  if (c.init) cudaStreamSynchronize(c.st);
+  // queued calls read the device copies freed here: an unsynced sequence is dropped
+  drop_pending(c);
+  int rc = 0;
+  if (c.init) {
+    const cudaError_t e = cudaStreamSynchronize(c.st);
+    if (e != cudaSuccess) rc = cuda_fail(e, "release: stream");
+  }
   for (auto &kv : c.ranges)
     for (Range &r : kv.second) cudaFree(r.d);
   c.ranges.clear();

@@ -92,9 +92,9 @@ def test_fused_decode_sequence(oracle, ffn, cuda, L):
     oracle.assert_close(out, ref, rel=1e-4, what="fused decode sequence")
 
 
-def test_queue_longer_than_a_batch_and_target_switch(oracle, ffn, cuda, L):
-    """20 accumulating calls (more than one queued batch) onto one output, then a
-    second output: the first must be complete when the target changes."""
+def test_queue_longer_than_a_batch(oracle, ffn, cuda, L):
+    """20 accumulating calls (more than one queued batch) onto one output, sync
+    on the last; then a second output."""
     H, I = 512, 256
     es = [nv_expert(oracle, 40 + k, I, H) for k in range(5)]
     x1, x2 = bench_x(H), bench_x(H, 1.0)
@@ -103,12 +103,59 @@ def test_queue_longer_than_a_batch_and_target_switch(oracle, ffn, cuda, L):
     seq = []
     for k in range(20):
         e, w = es[k % 5], 0.05 * (k + 1)
-        assert call(L, e, I, H, x1, o1, w, True, False)
+        assert call(L, e, I, H, x1, o1, w, True, k == 19)
         seq.append((e, w, True))
-    assert call(L, es[0], I, H, x2, o2, 2.0, False, True)  # another target: o1 is flushed first
+    assert call(L, es[0], I, H, x2, o2, 2.0, False, True)
     r1 = reference(oracle, seq, x1, 0.5)
     oracle.assert_close(o1, r1, rel=1e-4, what="20 queued calls")
     oracle.assert_close(o2, 2.0 * es[0].forward(x2), rel=1e-4, what="second target")
+
+
+def test_abandoned_sequence_is_never_written_back(oracle, ffn, cuda, L):
+    """The host breaks out of a fused sequence before its sync_now call and
+    frees `out` (flash1017.rs:7483-7486): no later call may write to that
+    buffer.  The abandoned buffer keeps a sentinel here, through a call to
+    another target, a call of another entry point, and a new batched layer."""
+    H, I = 512, 256
+    es = [nv_expert(oracle, 70 + k, I, H) for k in range(3)]
+    x = bench_x(H)
+    sentinel = np.float32(-7.25)
+    gone = np.full(H, sentinel, dtype=np.float32)  # stands for the freed buffer
+    assert call(L, es[0], I, H, x, gone, 1.0, False, False)
+    assert call(L, es[1], I, H, x, gone, 0.5, True, False)  # ... and the host breaks out here
+    fresh = np.zeros(H, dtype=np.float32)
+    assert call(L, es[2], I, H, x, fresh, 1.0, False, True)
+    assert np.all(gone == sentinel), "an abandoned sequence was written to its old target"
+    oracle.assert_close(fresh, es[2].forward(x), rel=1e-4, what="the next sequence")
+    # an abandoned sequence followed by another entry point (V3 matvec slot)
+    assert call(L, es[0], I, H, x, gone, 1.0, False, False)
+    fn = C.CFUNCTYPE(None, C.c_size_t, C.c_size_t, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_void_p)
+    slot = C.c_void_p.from_address(L.merkaba_hardware_addon_v1() + 120).value  # matvec_nvfp4 (HA:143-174)
+    y = np.zeros(I, dtype=np.float32)
+    m = es[0]
+    fn(slot)(I, H, p(m.w[0]), p(m.s[0]), m.gs[0], p(x), p(y))
+    oracle.assert_close(y, oracle.nvfp4_matvec(m.w[0], m.s[0], m.gs[0], x, I, H), what="vtable matvec_nvfp4")
+    assert np.all(gone == sentinel), "an abandoned sequence was written back by another entry point"
+    # an abandoned batched layer, then the next layer's shared-expert call
+    shared = f8_expert(oracle, 5, I, H)
+    x_all = np.ascontiguousarray(np.stack([bench_x(H, 0.1 * t) for t in range(2)]), dtype=np.float32)
+    old = np.full((2, H), sentinel, dtype=np.float32)
+    assert L.gx10_rust_mxfp8_mlp_batch(I, H, 2, p(shared.w[0]), p(shared.s[0]), p(shared.w[1]),
+                                       p(shared.s[1]), p(shared.w[2]), p(shared.s[2]), p(x_all), 2,
+                                       p(old), False)
+    dst = np.array([0, 1], dtype=np.uint64)
+    wts = np.array([0.3, 0.2], dtype=np.float32)
+    e = es[1]
+    assert L.gx10_rust_nvfp4_mlp_batch(I, H, 2, p(e.w[0]), p(e.s[0]), e.gs[0], p(e.w[1]), p(e.s[1]),
+                                       e.gs[1], p(e.w[2]), p(e.s[2]), e.gs[2], 0, p(dst), p(wts), 2,
+                                       p(old), False)
+    new = np.zeros((2, H), dtype=np.float32)
+    assert L.gx10_rust_mxfp8_mlp_batch(I, H, 2, p(shared.w[0]), p(shared.s[0]), p(shared.w[1]),
+                                       p(shared.s[1]), p(shared.w[2]), p(shared.s[2]), p(x_all), 2,
+                                       p(new), True)
+    assert np.all(old == sentinel), "an abandoned batched layer was written back"
+    ref = np.stack([shared.forward(x_all[t]) for t in range(2)])
+    oracle.assert_close(new, ref, rel=1e-4, what="the next batched layer")
 
 
 def test_calls_with_different_inputs(oracle, ffn, cuda, L):

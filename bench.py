@@ -91,6 +91,10 @@ def parse_args():
                     help="--workload expert: distinct experts cycled per step (> L2)")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="per-layer sum over ranks: NVLink peer exchange or NCCL all-reduce")
+    ap.add_argument("--path", choices=["auto", "gemv", "fp4", "grouped"], default="auto",
+                    help="MoE expert path: the layer's own choice (NVFP4 decode: block-scaled FP4 "
+                         "tensor cores; prefill: grouped GEMM), the f16x2 GEMV slices, the FP4 "
+                         "path, or the grouped GEMM")
     return ap.parse_args()
 
 
@@ -303,6 +307,9 @@ def run_ours(a):
     e_loc = e_hi - e_lo
     tern = a.format == "ternary106"
     fk = "ternary" if tern else "nvfp4"  # kernel kinds of the expert phases
+    path = _path_code(a)
+    fp4 = not tern and path in (0, 3)  # NVFP4 decode layers take the FP4 path under AUTO
+    gu_kind, dn_kind = ("fp4_gateup", "fp4_down") if fp4 else (f"gateup_{fk}", f"down_{fk}")
     ebytes = (2 * tern106_mat_bytes(I, H) + tern106_mat_bytes(H, I)) if tern else EXPERT_BYTES(H, I)
     layer_bytes = e_loc * ebytes
     free, _ = torch.cuda.mem_get_info(dev)
@@ -369,7 +376,7 @@ def run_ours(a):
     layers = [F.MoeLayer(tables[lay % resident][0], routers[lay], H, I, top_k=K,
                          score_fn=F.SCORE_SIGMOID, expert_range=(e_lo, e_lo + e_loc),
                          table=tables[lay % resident][1], ws=ws, norm_w=norm_w,
-                         norm_eps=1e-20, router_mode=F.ROUTER_TENSOR) for lay in range(L)]
+                         norm_eps=1e-20, router_mode=F.ROUTER_TENSOR, path=path) for lay in range(L)]
     x0 = F.gen_normal(F.path_key(a.seed, 0, 0, F.TAG_X), T * H).view(T, H)
     xa = torch.empty_like(x0)
     xb = torch.empty_like(x0)
@@ -443,7 +450,7 @@ def run_ours(a):
         dist.barrier()
     # live roofline: event pairs only around the expert GEMV kernels (fewer
     # event records between the kernels of the timed region)
-    F.profile_kinds([f"gateup_{fk}", f"down_{fk}"])
+    F.profile_kinds([gu_kind, dn_kind])
     F.profile_enable(True)
     n0 = F.launch_count()
     t_start = torch.cuda.Event(enable_timing=True)
@@ -478,7 +485,7 @@ def run_ours(a):
     # pairs as in the timed region above, so the two numbers compare)
     x_host = x0.cpu().pin_memory()
     out_host = torch.empty_like(x_host).pin_memory()
-    F.profile_kinds([f"gateup_{fk}", f"down_{fk}"])
+    F.profile_kinds([gu_kind, dn_kind])
     F.profile_enable(True)
     for i in range(a.warmup + a.steps):
         if i == a.warmup:
@@ -502,11 +509,13 @@ def run_ours(a):
     e2e = T * a.steps / (float(te.item()) * 1e-3)
 
     # ---- roofline of the dominant kernel (gate/up GEMV), live event timing
-    gu_ms, gu_n = prof.get(f"gateup_{fk}", (0.0, 0))
+    gu_ms, gu_n = prof.get(gu_kind, (0.0, 0))
     peaks = _peaks()
     achieved = gateup_bytes_step * a.steps / (gu_ms * 1e-3) / 1e9 if gu_ms else None
-    traffic = None if tern else _traffic_per_launch(gateup_bytes_step / L)
-    roof = {"bound": "hbm", "kernel": f"phase_kernel<{'TERNARY' if tern else 'NVFP4'}, gate+up>",
+    traffic = None if tern else _traffic_per_launch(gu_kind, gateup_bytes_step / L)
+    kname = ("fp4_gemm_kernel<1> (tcgen05 kind::mxf4nvf4, gate+up)" if fp4 else
+             f"phase_kernel<{'TERNARY' if tern else 'NVFP4'}, gate+up>")
+    roof = {"bound": "hbm", "kernel": kname,
             "achieved": achieved, "peak": peaks[0], "unit": "GB/s",
             "frac": achieved / peaks[0] if achieved else None, "traffic": traffic,
             "peak_source": peaks[1],
@@ -526,6 +535,8 @@ def run_ours(a):
     if rank == 0:
         cfg = base_config(a, world, resident)
         cfg["exchange"] = exch_used
+        cfg["expert_path"] = ("tcgen05 block-scaled FP4 (kind::mxf4nvf4), activations as 4 NVFP4 terms"
+                              if fp4 else "warp GEMV slices, f16x2 activations")
         cfg["experts_hit_per_layer_rank0"] = u_loc
         cfg["weight_bytes_per_step_rank0"] = weight_bytes_step
         line = {
@@ -534,6 +545,8 @@ def run_ours(a):
             "scaling": "strong", "vs_baseline": None,
             "dtype": ("ternary (block-64 U8 scales, rank-16 Q8 core) weights x f16x2 split "
                       "activations, f32 accumulate" if tern else
+                      "nvfp4 weights x 4-term nvfp4 activations (tcgen05 block-scaled FP4 MMA), f32 "
+                      "accumulate" if fp4 else
                       "nvfp4 weights x f16x2 split activations, f32 accumulate"),
             "data": "synthetic (seeded random-init weights and N(0,1) hidden states)",
             "config": cfg,
@@ -728,15 +741,25 @@ def _peaks():
         return 6650.0, "fallback (6.65 TB/s)"
 
 
-def _traffic_per_launch(alg_bytes_per_launch):
-    """DRAM bytes per launch of the gate/up kernel from the committed ncu
-    summary (profiles/gateup_nvfp4.json: measured traffic / algorithmic bytes
-    of the captured launch), scaled to this launch's algorithmic bytes."""
+def _traffic_per_launch(kind, alg_bytes_per_launch):
+    """DRAM bytes per launch of the gate/up kernel `kind` from its committed
+    ncu summary (profiles/<kind>.json: measured traffic / algorithmic bytes of
+    the captured launch), scaled to this launch's algorithmic bytes; None when
+    no capture of that kernel is committed."""
+    name = {"gateup_nvfp4": "gateup_nvfp4.json", "fp4_gateup": "fp4_gateup_nvfp4.json"}.get(kind)
+    if name is None:
+        return None
     try:
-        d = json.load(open(os.path.join(ROOT, "profiles", "gateup_nvfp4.json")))
+        d = json.load(open(os.path.join(ROOT, "profiles", name)))
         return alg_bytes_per_launch * float(d["traffic_over_algorithmic"])
     except (OSError, KeyError, ValueError):
         return None
+
+
+def _path_code(a):
+    import ffn_b200 as F
+    return {"auto": F.PATH_AUTO, "gemv": F.PATH_GEMV, "fp4": F.PATH_FP4,
+            "grouped": F.PATH_GROUPED}[a.path]
 
 
 # --------------------------------------------------------------- one expert

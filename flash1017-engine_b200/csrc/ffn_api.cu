@@ -598,7 +598,18 @@ struct MoeWs {
   int *err;        // grouped path: timed-out wait flag
   float *part;     // GEMV path: K-split partial sums (kListSplitBytes)
   int *cnt;        // GEMV path: split arrival counters, kSplitItems per phase launch (4)
+  // FP4 path: x and h as four NVFP4 terms, h in f32, the chunk list
+  uint8_t *xq, *xs, *hq, *hs, *f4chunk;
+  int *xqe, *hqe;
+  float *hf;
 };
+
+// The block-scaled FP4 path can run the layer: NVFP4 experts only, shapes
+// in whole 256-column stages and quantiser rows.
+static bool fp4_path_ok(const ffn_b200_moe_desc &d) {
+  return d.has_nvfp4 && !d.has_ternary && !d.has_mxfp4 && d.hidden % 256 == 0 && d.inter % 256 == 0 &&
+         d.hidden <= 16384 && d.inter <= 16384;
+}
 
 static MoeWs carve_moe(Carve &c, const ffn_b200_moe_desc &d, size_t T) {
   MoeWs w{};
@@ -625,6 +636,16 @@ static MoeWs carve_moe(Carve &c, const ffn_b200_moe_desc &d, size_t T) {
   w.err = c.take<int>(1);
   w.part = c.take<float>(kListSplitBytes / sizeof(float));
   w.cnt = c.take<int>(4 * (size_t)kSplitItems);
+  if (fp4_path_ok(d)) {
+    w.xq = c.take<uint8_t>(T * 4 * H / 2);
+    w.xs = c.take<uint8_t>(T * 4 * H / 16);
+    w.xqe = c.take<int>(T * 4);
+    w.hf = c.take<float>(P * I);
+    w.hq = c.take<uint8_t>(P * 4 * I / 2);
+    w.hs = c.take<uint8_t>(P * 4 * I / 16);
+    w.hqe = c.take<int>(P * 4);
+    w.f4chunk = c.take<uint8_t>(fp4_chunk_bytes((int)P, (int)E));
+  }
   return w;
 }
 
@@ -1033,8 +1054,14 @@ int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
     return fail(FFN_B200_EINVAL, "moe_layer: unknown score_fn");
   if (d->router_mode != FFN_B200_ROUTER_EXACT && d->router_mode != FFN_B200_ROUTER_TENSOR)
     return fail(FFN_B200_EINVAL, "moe_layer: unknown router_mode");
-  if (d->path != FFN_B200_PATH_AUTO && d->path != FFN_B200_PATH_GEMV && d->path != FFN_B200_PATH_GROUPED)
+  if (d->path != FFN_B200_PATH_AUTO && d->path != FFN_B200_PATH_GEMV && d->path != FFN_B200_PATH_GROUPED &&
+      d->path != FFN_B200_PATH_FP4)
     return fail(FFN_B200_EINVAL, "moe_layer: unknown path");
+  const bool fp4_ok = fp4_path_ok(*d);
+  if (d->path == FFN_B200_PATH_FP4 && !fp4_ok)
+    return fail(FFN_B200_EUNSUP,
+                "moe_layer: the FP4 path needs NVFP4-only experts and hidden, inter multiples of 256 "
+                "up to 16384");
   const bool grouped_ok = !d->has_ternary && !d->has_mxfp4 && H % 256 == 0 && I % 256 == 0;
   if (d->path == FFN_B200_PATH_GROUPED && !grouped_ok)
     return fail(FFN_B200_EUNSUP,
@@ -1092,9 +1119,38 @@ int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
       FFN_CUDA_TRY(cudaMemcpyAsync(topk_w, w.wt, P * sizeof(float), cudaMemcpyDeviceToDevice, st));
     return 0;
   }
-  if ((rc = moe_gemv_experts(d, w, P, xin, st))) return rc;
+  // (AUTO keeps the GEMV slices for an input row that is not 16-byte aligned)
+  const bool fp4 = fp4_ok && (d->path == FFN_B200_PATH_FP4 ||
+                              (d->path == FFN_B200_PATH_AUTO && (reinterpret_cast<uintptr_t>(xin) & 15) == 0));
+  if (fp4) {
+    Fp4Args g{};
+    g.experts = d->experts;
+    g.e_begin = d->expert_begin;
+    g.e_end = d->expert_end;
+    g.n_tok = T;
+    g.n_pairs = P;
+    g.hidden = (int)H;
+    g.inter = (int)I;
+    g.counts = w.ints;
+    g.offsets = w.ints + E;
+    g.pair_tok = w.pair_tok;
+    g.x = xin;
+    g.xq = w.xq;
+    g.xs = w.xs;
+    g.xqe = w.xqe;
+    g.h = w.hf;
+    g.hq = w.hq;
+    g.hs = w.hs;
+    g.hqe = w.hqe;
+    g.y = w.y;
+    g.chunk_ws = w.f4chunk;
+    g.err = w.err;
+    if ((rc = launch_fp4_moe(g, st))) return rc;
+  } else if ((rc = moe_gemv_experts(d, w, P, xin, st))) {
+    return rc;
+  }
   if ((rc = launch_combine(w.y, (int)H, w.idx, w.wt, w.inv, T, (int)k, d->experts, residual, out,
-                           (int)H, st)))
+                           (int)H, st, fp4 ? w.err : nullptr)))
     return rc;
   if (topk_idx)
     FFN_CUDA_TRY(cudaMemcpyAsync(topk_idx, w.idx, P * sizeof(int32_t), cudaMemcpyDeviceToDevice, st));

@@ -57,6 +57,29 @@ struct GroupedArgs {
 size_t gg_chunk_bytes(int n_pairs, int n_local);
 int launch_grouped_moe(const GroupedArgs &g, cudaStream_t st);
 
+// Block-scaled FP4 tensor-core MoE path (NVFP4 experts, decode-sized chunks).
+struct Fp4Args {
+  const ffn_b200_expert *experts;
+  int e_begin, e_end;
+  int n_tok, n_pairs;
+  int hidden, inter;
+  const int *counts, *offsets;  // per expert, from the grouping kernel
+  const int32_t *pair_tok;
+  const float *x;               // [n_tok][hidden] f32, the layer input the experts see
+  uint8_t *xq, *xs;             // x as 4 NVFP4 terms: codes [tok][4][hidden/2], scales [tok][4][hidden/16]
+  int *xqe;                     // [tok][4] exponents
+  float *h;                     // [pair][inter] f32
+  uint8_t *hq, *hs;             // h as 4 NVFP4 terms
+  int *hqe;
+  float *y;                     // [pair][hidden]
+  uint8_t *chunk_ws;            // fp4_chunk_bytes(n_pairs, e_end - e_begin)
+  int *err;                     // device int: 1 timed-out wait, 2 scale outside UE4M3, 3 misaligned
+};
+size_t fp4_chunk_bytes(int n_pairs, int n_local);
+int launch_fp4_moe(const Fp4Args &g, cudaStream_t st);
+// rows of f32 (K % 256 == 0, K <= 16384, 16-byte aligned rows) -> 4 NVFP4 terms
+int launch_q4(const float *x, int ld_x, int rows, int K, uint8_t *qc, uint8_t *qs, int *qe, cudaStream_t st);
+
 // Arguments of the rank-16 core z kernel.
 struct CoreZArgs {
   const ffn_b200_expert *experts;

@@ -18,7 +18,7 @@ LIB_PATH = os.path.join(HERE, "_build", "libffn_b200.so")
 FMT_NVFP4, FMT_TERNARY, FMT_MXFP4, FMT_MXFP8 = 0, 1, 2, 3
 SCORE_REF, SCORE_SIGMOID = 0, 1
 ROUTER_EXACT, ROUTER_TENSOR = 0, 1
-PATH_AUTO, PATH_GEMV, PATH_GROUPED = 0, 1, 2
+PATH_AUTO, PATH_GEMV, PATH_GROUPED, PATH_FP4 = 0, 1, 2, 3
 GROUPED_MIN_PAIRS = 48
 ERRORS = {0: "OK", -1: "EINVAL", -2: "ECUDA", -3: "ENOSPC", -4: "ENCCL", -5: "EUNSUP"}
 
@@ -43,14 +43,16 @@ EXPORTS = [
     "ffn_b200_st_open", "ffn_b200_st_close", "ffn_b200_st_count", "ffn_b200_st_name",
     "ffn_b200_st_find", "ffn_b200_st_expert_bytes", "ffn_b200_st_load_expert",
     "ffn_b200_compress_ws_bytes", "ffn_b200_compress_ternary_b64",
+    "ffn_b200_quantize_nvfp4x4",
 ]
 
 # Kernel kinds of ffn_b200_profile_read (FFN_B200_K_*).
 K_XPREP, K_ROUTER, K_TOPK, K_GROUP, K_GATEUP_NVFP4, K_DOWN_NVFP4 = 0, 1, 2, 3, 4, 5
 K_GATEUP_TERNARY, K_DOWN_TERNARY, K_COREZ, K_COMBINE, K_MATVEC, K_OTHER = 6, 7, 8, 9, 10, 11
-K_GEMM_GATEUP, K_GEMM_DOWN = 12, 13
+K_GEMM_GATEUP, K_GEMM_DOWN, K_QUANT, K_FP4_GATEUP, K_FP4_DOWN = 12, 13, 14, 15, 16
 K_NAMES = ["xprep", "router", "topk", "group", "gateup_nvfp4", "down_nvfp4", "gateup_ternary",
-           "down_ternary", "corez", "combine", "matvec", "other", "gemm_gateup", "gemm_down"]
+           "down_ternary", "corez", "combine", "matvec", "other", "gemm_gateup", "gemm_down",
+           "quant", "fp4_gateup", "fp4_down"]
 
 
 def build() -> str:
@@ -112,6 +114,7 @@ def lib() -> C.CDLL:
         L.ffn_b200_nvfp4_matvec.argtypes = [sz, sz, sz, C.POINTER(NvMat), vp, vp, vp, sz, vp]
         L.ffn_b200_ternary_matvec.argtypes = [sz, sz, sz, C.POINTER(TnMat), vp, vp, vp, sz, vp]
         L.ffn_b200_mxfp4_matvec.argtypes = [sz, sz, sz, C.POINTER(NvMat), vp, vp, vp, sz, vp]
+        L.ffn_b200_quantize_nvfp4x4.argtypes = [sz, sz, vp, sz, vp, vp, vp, vp]
         L.gx10_rust_mxfp4_matvec.argtypes = [sz, sz, vp, vp, vp, vp]
         L.gx10_rust_mxfp4_matvec.restype = C.c_bool
         L.gx10_rust_mxfp4_mlp_accum.argtypes = [sz, sz, vp, vp, vp, vp, vp, vp, vp, vp, f32,

@@ -195,10 +195,11 @@ typedef struct ffn_b200_moe_desc {
      * + norm_eps) * norm_w.  NULL: the experts see x itself. */
     const float *norm_w;             /* DEVICE [hidden] or NULL */
     float norm_eps;
-    /* FFN_B200_PATH_*: AUTO (0) takes the tensor-core grouped GEMM when the
-     * layer has only NVFP4 experts, hidden and inter are multiples of 256 and
-     * the routed pairs average >= FFN_B200_GROUPED_MIN_PAIRS per expert
-     * (prefill), else the GEMV slices (decode). */
+    /* FFN_B200_PATH_*: AUTO (0), for a layer with only NVFP4 experts and
+     * hidden, inter multiples of 256: the tensor-core grouped GEMM when the
+     * routed pairs average >= FFN_B200_GROUPED_MIN_PAIRS per expert (prefill),
+     * else the block-scaled FP4 path (decode; hidden, inter <= 16384); any
+     * other layer takes the GEMV slices. */
     int32_t path;
     /* MXFP4 experts occur in experts[] (they count as has_nvfp4 too: same
      * kernel family; the grouped GEMM is NVFP4-only). */
@@ -208,7 +209,24 @@ typedef struct ffn_b200_moe_desc {
 #define FFN_B200_PATH_AUTO 0
 #define FFN_B200_PATH_GEMV 1    /* slices of <= 8 tokens, f16 hi/lo activations (~fp32) */
 #define FFN_B200_PATH_GROUPED 2 /* tcgen05 grouped GEMM, f16 activations (rel. err ~2e-4) */
+/* tcgen05 kind::mxf4nvf4: the NVFP4 weights and their E4M3 block scales enter
+ * the tensor core as stored (scale bytes must be UE4M3: sign bit clear, not
+ * 0x7F; otherwise the layer's outputs are NaN), activations as four NVFP4
+ * residual terms (rel. err ~2e-4); chunks of <= 8 tokens per expert */
+#define FFN_B200_PATH_FP4 3
 #define FFN_B200_GROUPED_MIN_PAIRS 48
+
+/* The FP4 path's activation format (no reference counterpart: the reference
+ * multiplies f32 activations).  Each row x of K values (K % 256 == 0, K <=
+ * 16384; rows 16-byte aligned, ld_x % 4 == 0) becomes four NVFP4 terms,
+ * x ~= sum_t 2^exps[t] * q_t: codes [rows][4][K/2] (E2M1 pairs, low nibble =
+ * even column), scales [rows][4][K/16] (UE4M3 per 16 values), exps [rows][4].
+ * Term t quantises what terms < t left: E_t = floor(log2 max|r_t|) - 8, block
+ * scale = UE4M3 ceiling of max|r_t| 2^-E_t / 6, codes = E2M1 round-to-nearest-
+ * even of r_t 2^-E_t / scale. */
+FFN_B200_EXPORT int ffn_b200_quantize_nvfp4x4(size_t rows, size_t K, const float *x, size_t ld_x,
+                                              uint8_t *codes, uint8_t *scales, int32_t *exps,
+                                              void *stream);
 
 FFN_B200_EXPORT size_t ffn_b200_moe_ws_bytes(const ffn_b200_moe_desc *d, size_t max_tokens);
 /* x [n_tok, hidden] f32; out [n_tok, hidden] = residual + moe(xn) when
@@ -262,7 +280,10 @@ FFN_B200_EXPORT int ffn_b200_dequant_ternary(size_t rows, size_t cols, const uin
 #define FFN_B200_K_OTHER 11
 #define FFN_B200_K_GEMM_GATEUP 12 /* grouped tensor-core path */
 #define FFN_B200_K_GEMM_DOWN 13
-#define FFN_B200_K_COUNT 14
+#define FFN_B200_K_QUANT 14       /* activation rows -> four NVFP4 terms (FP4 path) */
+#define FFN_B200_K_FP4_GATEUP 15  /* block-scaled FP4 tensor-core path */
+#define FFN_B200_K_FP4_DOWN 16
+#define FFN_B200_K_COUNT 17
 FFN_B200_EXPORT int ffn_b200_profile_enable(int enable);
 /* Which kinds get event pairs while enabled: bit k = FFN_B200_K_* k (default
  * all).  Timing fewer kinds puts fewer event records between the kernels. */

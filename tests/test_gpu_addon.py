@@ -311,7 +311,8 @@ def test_bad_shape_fails_at_the_call_and_leaves_a_clean_state(oracle, ffn, cuda,
     """Shapes the kernels cannot run (NVFP4 hidden % 64, MXFP4 hidden % 128) make
     that call return false (the host then runs its CPU twin), with the weight
     arrays sized for the claimed dims.  A pending sequence to another target is
-    delivered first, and the next sequence is unaffected."""
+    abandoned (never written back: the host recomputes it on its CPU path),
+    and the next sequence is unaffected."""
     H, I = 512, 256
     es = [nv_expert(oracle, 70 + k, I, H) for k in range(2)]
     x = bench_x(H)
@@ -323,7 +324,7 @@ def test_bad_shape_fails_at_the_call_and_leaves_a_clean_state(oracle, ffn, cuda,
     bad = oracle.Nvfp4Expert(I, bH, (w, w, w), (s, s, s), (1.0, 1.0, 1.0))
     xb, ob = bench_x(bH), np.zeros(bH, dtype=np.float32)
     assert not call(L, bad, I, bH, xb, ob, 0.5, True, True)
-    oracle.assert_close(out, np.float32(0.5) * es[0].forward(x), rel=1e-4, what="sequence before the failure")
+    assert np.all(out == 0), "the abandoned sequence was written back"
     mH = 320
     mw = np.zeros(I * mH // 2, dtype=np.uint8)
     ms = np.full(I * mH // 32, 127, dtype=np.uint8)

@@ -68,8 +68,9 @@ def test_grouped_matches_gemv_path(ffn, oracle, cuda, E, T, rng):
 
 
 def test_grouped_auto_selection(ffn, cuda):
-    """AUTO picks the grouped path only at >= GROUPED_MIN_PAIRS pairs per expert;
-    a ternary layer or odd dims are refused by PATH_GROUPED."""
+    """AUTO picks the grouped path only at >= GROUPED_MIN_PAIRS pairs per expert
+    (below: the block-scaled FP4 path for this NVFP4 layer); a ternary layer or
+    odd dims are refused by PATH_GROUPED."""
     import torch
     F = ffn
     E, H, I = 8, 512, 256
@@ -86,4 +87,4 @@ def test_grouped_auto_selection(ffn, cuda):
         torch.cuda.synchronize()
         prof = F.profile_read()
         F.profile_enable(False)
-        assert ("gemm_gateup" in prof) == grouped and ("gateup_nvfp4" in prof) == (not grouped)
+        assert ("gemm_gateup" in prof) == grouped and ("fp4_gateup" in prof) == (not grouped)

@@ -344,16 +344,16 @@ def test_moe_layer_residual_and_expert_range(oracle, ffn, cuda):
     oracle.assert_close(res, full + host(x), rel=1e-6, cos=0.9999999, what="residual")
 
 
-def test_moe_config2_sampled(oracle, ffn, cuda):
+def test_moe_config2_all_tokens_gemv_path(oracle, ffn, cuda):
     """Benchmark config 2: 384 NVFP4 experts (H 4096, I 2048), 64 tokens, router
-    fp32 N(0, 0.02), sigmoid top-6, seed 2.  All 64 tokens' top-6 indices are
-    compared with the oracle router; outputs of a sample of tokens with the
-    oracle experts they hit."""
+    fp32 N(0, 0.02), sigmoid top-6, seed 2, on the f16x2 GEMV path (the FP4 path
+    has its own test): all 64 tokens' top-6 indices against the oracle router,
+    all 64 outputs against the oracle experts they hit."""
     import torch
     E, H, I, T, K, seed = 384, 4096, 2048, 64, 6, 2
     experts = [ffn.SwigluExpert.generate(ffn.FMT_NVFP4, seed, 0, e, I, H) for e in range(E)]
     wr = ffn.gen_normal(ffn.path_key(seed, 0, 0, ffn.TAG_ROUTER), E * H, 0.02).view(E, H)
-    layer = ffn.MoeLayer(experts, wr, H, I, top_k=K, score_fn=ffn.SCORE_SIGMOID)
+    layer = ffn.MoeLayer(experts, wr, H, I, top_k=K, score_fn=ffn.SCORE_SIGMOID, path=ffn.PATH_GEMV)
     x = ffn.gen_normal(ffn.path_key(seed, 0, 0, ffn.TAG_X), T * H).view(T, H)
     idx = torch.empty(T, K, dtype=torch.int32, device=cuda)
     wt = torch.empty(T, K, dtype=torch.float32, device=cuda)
@@ -362,11 +362,13 @@ def test_moe_config2_sampled(oracle, ffn, cuda):
     logits = oracle.router_logits(host(wr), xs)
     ridx, rwt, _, _ = oracle.route(logits, K, None, 1)
     assert np.array_equal(host(idx), ridx)
-    for t in (0, 17, 63):
+    oracle.set_threads(16)
+    oe = {e: oracle_nvfp4_expert(oracle, experts[e]) for e in sorted(set(ridx.ravel().tolist()))}
+    for t in range(T):
         ref = np.zeros(H, dtype=np.float32)
+        xt = np.ascontiguousarray(xs[t])
         for k in range(K):
-            y = oracle_nvfp4_expert(oracle, experts[ridx[t, k]]).forward(np.ascontiguousarray(xs[t]))
-            oracle.axpy(ref, rwt[t, k], y)
+            oracle.axpy(ref, rwt[t, k], oe[ridx[t, k]].forward(xt))
         oracle.assert_close(out[t], ref, what=f"config2 token {t}")
 
 

@@ -81,6 +81,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="CPU-baseline sample length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-subrecords", action="store_true",
+                    help="config4 on one GPU: skip the configs 0-3 sub-records")
     ap.add_argument("--format", choices=["nvfp4", "ternary106", "ternary", "mxfp4", "mxfp8"],
                     default="nvfp4",
                     help="expert format: NVFP4 (the benchmark configs), the reference compressor's 106 GB "
@@ -156,8 +158,9 @@ class CpuSample:
         O.set_threads(threads)
         H, I, E, K = a.hidden, a.inter, a.experts, a.top_k
         self.x = O.gen_hidden(a.seed, self.N_TOK, H)
-        if a.workload == "config3":  # bf16 hidden states, no ffn_norm
-            self.x = (self.x.view(np.uint32) & 0xFFFF0000).view(np.float32)
+        if a.workload == "config3":  # bf16 hidden states (round to nearest even, as torch), no ffn_norm
+            u = self.x.view(np.uint32).astype(np.uint64)
+            self.x = (((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)).view(np.float32)
         self.norm_w = np.ones(H, dtype=np.float32) if a.workload == "config4" else None
         self.routers, self.experts = [], {}
         xn = O.rms_norm(self.x, self.norm_w) if self.norm_w is not None else self.x
@@ -167,6 +170,25 @@ class CpuSample:
             self.routers.append(wr)
             for e in set(idx.ravel().tolist()):
                 self.experts[(layer, e)] = O.gen_nvfp4_expert(a.seed, layer, e, I, H)
+
+    def first_layer_outputs(self):
+        """The oracle's outputs of the sample tokens through the first layer
+        (what the GPU's layer gives for the same tokens), for the parity figure
+        of the CPU leg."""
+        import numpy as np
+        O, a = self.O, self.a
+        wr = self.routers[0]
+        outs = []
+        for t in range(self.N_TOK):
+            xt = np.ascontiguousarray(self.x[t])
+            if self.norm_w is not None:
+                xt = O.rms_norm(xt[None, :], self.norm_w)[0]
+            idx, wt, _, _ = O.route(O.router_logits(wr, xt), a.top_k, None, 1)
+            out = np.zeros(a.hidden, dtype=np.float32)
+            for k in range(a.top_k):
+                O.axpy(out, wt[0, k], self.experts[(0, int(idx[0, k]))].forward(xt))
+            outs.append(out)
+        return np.stack(outs)
 
     def run_once(self) -> int:
         """One pass over the sample; returns the token-layers computed."""
@@ -312,6 +334,16 @@ def run_ours(a):
     gu_kind, dn_kind = ("fp4_gateup", "fp4_down") if fp4 else (f"gateup_{fk}", f"down_{fk}")
     ebytes = (2 * tern106_mat_bytes(I, H) + tern106_mat_bytes(H, I)) if tern else EXPERT_BYTES(H, I)
     layer_bytes = e_loc * ebytes
+    subs = None
+    if world == 1 and not tern and not a.no_subrecords:
+        # configs 0-3, measured before config 4 fills the HBM
+        cs = 0.0 if a.no_cpu_baseline else min(3.0, a.cpu_seconds)
+        subs = {"config0": _sub_expert(a, F, dev, "nvfp4", 0, cs),
+                "config1": _sub_expert(a, F, dev, "ternary", 1, cs),
+                "config2": _sub_layer(a, F, dev, 2, cs),
+                "config3": _sub_layer(a, F, dev, 3, cs)}
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
     free, _ = torch.cuda.mem_get_info(dev)
     reserve = 4 << 30
     resident = max(1, min(L, (free - reserve - L * E * H * 4) // (layer_bytes + 512 * e_loc)))
@@ -385,10 +417,15 @@ def run_ours(a):
 
     capturing = [False]
 
+    fused = [None]  # the exchange, while layers run fused with it
+
     def layer_fn(lay):
         def run(x_in, out, residual):
-            layers[lay].forward(x_in, out=out, residual=residual,
-                                topk_idx=topk[lay] if capturing[0] else None)
+            idx = topk[lay] if capturing[0] else None
+            if fused[0] is not None:
+                layers[lay].forward_ep(fused[0], x_in, out, residual=residual, topk_idx=idx)
+            else:
+                layers[lay].forward(x_in, out=out, residual=residual, topk_idx=idx)
         return run
 
     exchange = None
@@ -402,7 +439,9 @@ def run_ours(a):
         if not int(ok.item()) and exchange is not None:
             exchange.close()
             exchange = None
-    ep = EpStack([layer_fn(lay) for lay in range(L)], rank, world, exchange=exchange)
+    ep = EpStack([layer_fn(lay) for lay in range(L)], rank, world, exchange=exchange,
+                 fused=exchange is not None)
+    fused[0] = exchange if ep.fused else None
 
     def stack(x_in, capture=False):
         capturing[0] = capture
@@ -416,6 +455,8 @@ def run_ours(a):
     xa.copy_(x0)
     stack(xa, capture=True)
     torch.cuda.synchronize()
+    if world > 1:  # the ranks enter the warm-up together
+        dist.barrier()
     u_loc = []
     for lay in range(L):
         ids = torch.unique(topk[lay])
@@ -435,6 +476,8 @@ def run_ours(a):
         if int(bad.item()):
             print("peer exchange reported a timed-out wait; using NCCL", file=sys.stderr)
             ep.exchange = None
+            ep.fused = False
+            fused[0] = None
             for _ in range(a.warmup):
                 step()
             torch.cuda.synchronize()
@@ -508,6 +551,42 @@ def run_ours(a):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e = T * a.steps / (float(te.item()) * 1e-3)
 
+    # ---- untimed checks.  (1) The timed TENSOR router's top-k sets against the
+    # bit-exact EXACT router on layer 0's input.  (2) N > 1: the expert-parallel
+    # output of the first two layers against the same two layers with every
+    # expert on rank 0 (the part of the stack one GPU can hold).
+    checks = {}
+    if not tern:
+        ex_layer = F.MoeLayer(tables[0][0], routers[0], H, I, top_k=K, score_fn=F.SCORE_SIGMOID,
+                              expert_range=(e_lo, e_lo + e_loc), table=tables[0][1], ws=ws, norm_w=norm_w,
+                              norm_eps=1e-20, router_mode=F.ROUTER_EXACT, path=path)
+        ex_idx = torch.empty(T, K, dtype=torch.int32, device=dev)
+        ex_layer.forward(x0, topk_idx=ex_idx)
+        torch.cuda.synchronize()
+        same = (torch.sort(ex_idx, 1).values == torch.sort(topk[0], 1).values).all(1)
+        checks["router_tensor_vs_exact"] = {"layer": 0, "tokens": T, "same_top_k_set": int(same.sum().item())}
+    if world > 1 and not tern:
+        xe2 = torch.empty_like(x0)
+        two = EpStack([layer_fn(lay) for lay in range(2)], rank, world, exchange=ep.exchange,
+                      fused=ep.fused)
+        y2 = two.forward(x0, xe2, torch.empty_like(x0))
+        torch.cuda.synchronize()
+        if rank == 0:
+            cur = x0
+            for lay in range(2):
+                full = [F.SwigluExpert.generate(F.FMT_NVFP4, a.seed, lay, e, I, H) for e in range(E)]
+                lf = F.MoeLayer(full, routers[lay], H, I, top_k=K, score_fn=F.SCORE_SIGMOID, norm_w=norm_w,
+                                norm_eps=1e-20, router_mode=F.ROUTER_TENSOR, path=path)
+                cur = lf.forward(cur, residual=cur)
+                del full, lf
+            yy, rr = y2.double(), cur.double()
+            err = float((yy - rr).abs().max() / rr.abs().max())
+            cos = float((yy * rr).sum() / (yy.norm() * rr.norm()))
+            checks["ep_vs_single_gpu"] = {"layers": 2, "max_rel_err": err, "cosine": cos,
+                                          "ok": bool(err <= 1e-3 and cos >= 0.99999)}
+            torch.cuda.empty_cache()
+        dist.barrier()
+
     # ---- roofline of the dominant kernel (gate/up GEMV), live event timing
     gu_ms, gu_n = prof.get(gu_kind, (0.0, 0))
     peaks = _peaks()
@@ -559,6 +638,9 @@ def run_ours(a):
             "kernels": kernels,
             "hbm_weight_gbs_rank0": weight_bytes_step / (ms_step * 1e-3) / 1e9,
         }
+        if subs is not None:
+            line["configs"] = subs
+        line["checks"] = checks
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -921,6 +1003,164 @@ def run_expert(a):
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+# --------------------------------------------------------------- configs 0-3
+# Sub-records of the default (config 4) run on one GPU: the other benchmark
+# configurations measured in the same process, before config 4 fills the HBM,
+# each with its own roofline, an oracle CPU sample and the parity of the
+# sampled tokens against that sample's oracle outputs (the CPU leg, where the
+# oracle serves as the checker).
+
+def _event_ms(step, steps, warmup):
+    """Device ms per step: CUDA events on the current stream, synchronised on both sides."""
+    import torch
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    return t0.elapsed_time(t1) / steps
+
+
+def _cpu_rate(fn, seconds):
+    """(calls/s, calls, seconds) of fn() repeated for about `seconds`."""
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        fn()
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds:
+            return n / dt, n, dt
+
+
+def _parity(O, y, ref, what):
+    e, c = O.max_rel_err(y, ref), O.cosine(y, ref)
+    return {"checked": what, "max_rel_err": e, "cosine": c,
+            "ok": bool(e <= O.REL_TOL and c >= O.COS_TOL),
+            "tolerance": f"max|y-ref|/max|ref| <= {O.REL_TOL}, cosine >= {O.COS_TOL}"}
+
+
+def _host(t):
+    import numpy as np
+    return np.ascontiguousarray(t.detach().cpu().numpy())
+
+
+def _sub_expert(a, F, dev, fmt, seed, cpu_s):
+    """Config 0 (NVFP4) or 1 (ternary + rank-16 core): one SwiGLU expert, one
+    token, cycling through 64 distinct experts (906 / 424 MB, > L2)."""
+    import torch
+    H, I, pool = a.hidden, a.inter, 64
+    tern = fmt == "ternary"
+    experts = [F.SwigluExpert.generate(F.FMT_TERNARY if tern else F.FMT_NVFP4, seed, 0, e, I, H,
+                                       **({"with_core": True} if tern else {})) for e in range(pool)]
+    x = F.gen_normal(F.path_key(seed, 0, 0, F.TAG_X), H).view(1, H)
+    out = torch.zeros(1, H, dtype=torch.float32, device=dev)
+
+    def step():
+        for ex in experts:
+            ex.forward(x, out=out, weight=1.0, accumulate=True)
+
+    ms = _event_ms(step, 20, 3)
+    us = ms * 1e3 / pool
+    ebytes = sum(_expert_mat_bytes(fmt, r, c) for r, c in ((I, H), (I, H), (H, I)))
+    peak, src = _peaks()
+    gbs = ebytes / (us * 1e-6) / 1e9
+    rec = {"workload": f"config{1 if tern else 0}: one {'ternary + rank-16 Q8 core' if tern else 'NVFP4'} "
+                       f"SwiGLU expert, batch-1 decode, H {H}, I {I}, seed {seed}, pool of {pool} experts",
+           "metric": "expert forwards/s", "value": 1e6 / us, "us_per_forward": us,
+           "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                        "peak_source": src, "algorithmic_bytes_per_forward": ebytes}}
+    y = _host(experts[0].forward(x))[0]
+    if cpu_s > 0:
+        import numpy as np
+        import oracle as O  # the CPU leg: baseline and checker
+        O.set_threads(os.cpu_count() or 1)
+        e0 = experts[0]
+        if tern:
+            cores = tuple(O.Core(*(_host(t) for t in m.core)) for m in e0.mats)
+            oe = O.TernaryExpert(I, H, tuple(_host(m.p) for m in e0.mats), tuple(_host(m.rs) for m in e0.mats),
+                                 cores, e0.proj_scale)
+        else:
+            oe = O.Nvfp4Expert(I, H, tuple(_host(m.w) for m in e0.mats), tuple(_host(m.s) for m in e0.mats),
+                               tuple(m.gs for m in e0.mats))
+        xs = np.ascontiguousarray(_host(x)[0])
+        rate, n, dt = _cpu_rate(lambda: oe.forward(xs), cpu_s)
+        rec["cpu_baseline"] = {"value": rate, "unit": "expert forwards/s", "cores": os.cpu_count() or 1,
+                               "kind": "port", "sample": f"oracle expert forward, 1 token, {n} calls in {dt:.1f} s"}
+        rec["parity"] = _parity(O, y, oe.forward(xs), "expert 0, token 0, against the oracle")
+    del experts
+    torch.cuda.empty_cache()
+    return rec
+
+
+def _sub_layer(a, F, dev, cfg, cpu_s):
+    """Config 2 (one NVFP4 MoE layer, 64-token decode, sigmoid top-6 of 384,
+    seed 2: the block-scaled FP4 path) or config 3 (8192-token prefill,
+    bf16-valued hidden states, seed 3: the grouped GEMM)."""
+    import copy
+
+    import torch
+    H, I, E, K = a.hidden, a.inter, a.experts, a.top_k
+    T, seed = (64, 2) if cfg == 2 else (8192, 3)
+    experts = [F.SwigluExpert.generate(F.FMT_NVFP4, seed, 0, e, I, H) for e in range(E)]
+    wr = F.gen_normal(F.path_key(seed, 0, 0, F.TAG_ROUTER), E * H, 0.02).view(E, H)
+    layer = F.MoeLayer(experts, wr, H, I, top_k=K, score_fn=F.SCORE_SIGMOID, router_mode=F.ROUTER_TENSOR)
+    x = F.gen_normal(F.path_key(seed, 0, 0, F.TAG_X), T * H).view(T, H)
+    if cfg == 3:
+        x = x.to(torch.bfloat16).to(torch.float32)
+    out = torch.empty_like(x)
+    idx = torch.empty(T, K, dtype=torch.int32, device=dev)
+    layer.forward(x, out=out, topk_idx=idx)
+    torch.cuda.synchronize()
+    hit = int(torch.unique(idx).numel())
+    kinds = ("fp4_gateup", "fp4_down") if cfg == 2 else ("gemm_gateup", "gemm_down")
+    F.profile_kinds(list(kinds))
+    F.profile_enable(True)
+    ms = _event_ms(lambda: layer.forward(x, out=out), 10 if cfg == 2 else 5, 3)
+    F.profile_enable(False)
+    prof = F.profile_read()
+    F.profile_kinds(None)
+    gu_ms, gu_n = prof.get(kinds[0], (0.0, 0))
+    gu_us = gu_ms * 1e3 / gu_n if gu_n else None
+    rec = {"workload": (f"config2: one NVFP4 MoE layer, decode batch of 64 tokens, sigmoid top-6 of {E}, "
+                        f"seed 2, block-scaled FP4 path" if cfg == 2 else
+                        f"config3: one NVFP4 MoE layer, prefill of 8192 bf16-valued tokens, top-6 of {E}, "
+                        f"seed 3, tensor-core grouped GEMM"),
+           "metric": "tokens/s", "value": T / (ms * 1e-3), "ms_per_layer": ms, "experts_hit": hit,
+           "l2": "no flush: each pass streams the hit experts' weights (> 126 MB L2)"}
+    if cfg == 2:
+        peak, src = _peaks()
+        gbs = hit * 2 * (I * H // 2 + I * H // 16) / (gu_us * 1e-6) / 1e9 if gu_us else None
+        rec["roofline"] = {"bound": "hbm", "kernel": "fp4_gemm_kernel<1> (gate+up)", "achieved": gbs,
+                           "peak": peak, "unit": "GB/s", "frac": gbs / peak if gbs else None,
+                           "peak_source": src, "avg_launch_us": gu_us}
+    else:
+        peak, src = _tensor_peak()
+        tf = 2.0 * T * K * 2 * H * I / (gu_us * 1e-6) / 1e12 if gu_us else None
+        rec["roofline"] = {"bound": "tensor", "kernel": "grouped gemm_kernel<1> (gate+up, tcgen05 kind::f16)",
+                           "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak if tf else None,
+                           "peak_source": src, "avg_launch_us": gu_us,
+                           "layer_tflops": 2.0 * T * K * 3 * H * I / (ms * 1e-3) / 1e12}
+    if cpu_s > 0:
+        import oracle as O  # the CPU leg: baseline and checker
+        b = copy.copy(a)
+        b.workload, b.tokens, b.seed, b.layers = ("config3" if cfg == 3 else "config2"), T, seed, 1
+        sample = CpuSample(b, os.cpu_count() or 1)
+        cv, dt, n = sample.measure(cpu_s)
+        rec["cpu_baseline"] = {"value": cv, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+                               "sample": sample.describe(dt, n)}
+        got = _host(out)[: CpuSample.N_TOK]
+        rec["parity"] = _parity(O, got, sample.first_layer_outputs(),
+                                f"tokens 0-{CpuSample.N_TOK - 1} of the layer against the oracle")
+    del experts, layer
+    torch.cuda.empty_cache()
+    return rec
 
 
 def run_compress(a):

@@ -3,12 +3,18 @@
 // The Rust host (crates/flash-core/src/hardware_addon.rs, "HA") calls these
 // functions with HOST pointers and reads `out` right after they return.  B200
 // memory is discrete, so this layer
-//   * keeps one HBM copy per weight range: ranges registered through
+//   * keeps HBM copies of weight ranges: ranges registered through
 //     gx10_rust_register_host_range are copied eagerly; any other weight
 //     pointer (inside gx10_rust_register_shard_bounds ranges or not) is copied
 //     the first time a kernel needs it, as exactly the bytes that call reads.
 //     Weights are immutable for the process lifetime in the reference (mmap'd
-//     read-only safetensors), which is what makes the cache valid;
+//     read-only safetensors), which is what makes the cache valid.  The copies
+//     are disjoint intervals (one predecessor search per lookup); when a budget
+//     (ffn_b200_set_host_cache_budget) or the GPU's memory runs out, the least
+//     recently used copies go first (first-use copies before registered
+//     ranges) and are copied again when needed, so a model larger than HBM
+//     (the reference registers only its hot experts, hardware_addon.rs:681-697,
+//     flash1017.rs:5228-5239) keeps running on the GPU;
 //   * stages x / out through device buffers on one internal stream;
 //   * runs the same kernels as the device-resident ABI (ffn_b200.h).
 // Calls are serialised by a mutex (the reference calls from one thread at a
@@ -44,10 +50,15 @@ struct DevBuf {
   }
 };
 
+// One HBM copy of host bytes [h, h + n).  The copies are disjoint (a new range
+// that overlaps copies replaces them with one copy of the union), so the copy
+// holding an address is its predecessor in the map.
 struct Range {
   uintptr_t h;
   size_t n;
   char *d;
+  uint64_t last_use;  // call number of the last call that resolved an address in it
+  bool registered;    // through gx10_rust_register_host_range (evicted after first-use copies)
 };
 
 struct Ctx {
@@ -58,8 +69,10 @@ struct Ctx {
   cudaStream_t st2 = nullptr;  // side stream of queued runs (independent slice lists)
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   DevBuf x, out, ws, tmp;
-  std::map<uintptr_t, std::vector<Range>> ranges;  // by start address
+  std::map<uintptr_t, Range> ranges;  // disjoint copies, by host start address
   size_t cached = 0;
+  size_t budget = 0;       // bytes the copies may hold (0: as much as the GPU gives)
+  uint64_t call_no = 0;    // entry-point calls so far (a call never evicts its own copies)
   std::vector<std::pair<uintptr_t, size_t>> shard_bounds;
   // pending accumulation of gx10_rust_*_mlp_accum / _mlp_batch
   float *pend_host = nullptr;
@@ -106,6 +119,7 @@ Ctx &ctx() {
 }
 
 int ensure_init(Ctx &c) {
+  ++c.call_no;
   if (c.init) {
     int dev = -1;
     cudaGetDevice(&dev);
@@ -121,31 +135,106 @@ int ensure_init(Ctx &c) {
   return 0;
 }
 
-// Device address of host bytes [h, h+n): an existing copy containing them, or
-// a new copy of exactly those bytes.
-int dev_ptr(Ctx &c, const void *hp, size_t n, const void **out) {
+int run_queue(Ctx &c);
+
+// Before a copy is freed: no queued or running work may still read it.
+int quiesce(Ctx &c) {
+  if (int rc = run_queue(c)) return rc;
+  cudaError_t e = cudaStreamSynchronize(c.st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c.st2);
+  if (e != cudaSuccess) return cuda_fail(e, "weight cache: stream");
+  return 0;
+}
+
+// Free the least recently used copy that the current call has not resolved
+// and that does not overlap [lo, hi) (first-use copies before registered
+// ranges); false when there is none.
+bool evict_one(Ctx &c, uintptr_t lo, uintptr_t hi, bool &quiet, int &rc) {
+  auto best = c.ranges.end();
+  for (auto it = c.ranges.begin(); it != c.ranges.end(); ++it) {
+    const Range &r = it->second;
+    if (r.last_use == c.call_no || (r.h < hi && lo < r.h + r.n)) continue;
+    if (best == c.ranges.end() || r.registered < best->second.registered ||
+        (r.registered == best->second.registered && r.last_use < best->second.last_use))
+      best = it;
+  }
+  if (best == c.ranges.end()) return false;
+  if (!quiet) {
+    if ((rc = quiesce(c))) return false;
+    quiet = true;
+  }
+  cudaFree(best->second.d);
+  c.cached -= best->second.n;
+  c.ranges.erase(best);
+  return true;
+}
+
+// Device address of host bytes [h, h+n): the copy containing them, or a new
+// copy.  A new copy spans the union of [h, h+n) and every copy it overlaps
+// (those are freed), so the copies stay disjoint and a lookup is one
+// predecessor search.  When the budget or the GPU's memory runs out, least
+// recently used copies are evicted (never one the current call resolved) and
+// the bytes are copied again when a later call needs them.
+int dev_ptr(Ctx &c, const void *hp, size_t n, const void **out, bool registered = false) {
   if (!hp) return fail(FFN_B200_EINVAL, "reference ABI: null weight pointer");
   const uintptr_t h = (uintptr_t)hp;
   auto it = c.ranges.upper_bound(h);
-  while (it != c.ranges.begin()) {
-    --it;
-    for (const Range &r : it->second)
-      if (r.h <= h && h + n <= r.h + r.n) {
-        *out = r.d + (h - r.h);
-        return 0;
-      }
-    if (it->first + (1ull << 40) < h) break;  // ranges are tensors, far smaller than 1 TiB
+  if (it != c.ranges.begin()) {
+    auto p = std::prev(it);
+    if (h + n <= p->second.h + p->second.n) {
+      p->second.last_use = c.call_no;
+      p->second.registered = p->second.registered || registered;
+      *out = p->second.d + (h - p->second.h);
+      return 0;
+    }
+    if (h < p->second.h + p->second.n) it = p;  // overlaps from below
   }
+  uintptr_t lo = h, hi = h + n;
+  std::vector<uintptr_t> merged;
+  for (auto q = it; q != c.ranges.end() && q->second.h < hi; ++q) {
+    if (q->second.last_use == c.call_no)  // this call holds an address in it: it must not move
+      return fail(FFN_B200_EUNSUP, "reference ABI: weight ranges of one call overlap");
+    lo = std::min(lo, q->second.h);
+    hi = std::max(hi, q->second.h + q->second.n);
+    registered = registered || q->second.registered;
+    merged.push_back(q->first);
+  }
+  size_t freed = 0;
+  for (uintptr_t k : merged) freed += c.ranges[k].n;
+  const size_t need = hi - lo;
+  bool quiet = false;
+  int rc = 0;
+  while (c.budget && c.cached - freed + need > c.budget)
+    if (!evict_one(c, lo, hi, quiet, rc)) {
+      if (rc) return rc;
+      break;  // nothing evictable: go over the budget rather than fail the call
+    }
   char *d = nullptr;
-  FFN_CUDA_TRY(cudaMalloc(&d, n));
-  cudaError_t e = cudaMemcpy(d, hp, n, cudaMemcpyHostToDevice);
+  cudaError_t e;
+  while ((e = cudaMalloc(&d, need)) == cudaErrorMemoryAllocation) {
+    cudaGetLastError();
+    if (!evict_one(c, lo, hi, quiet, rc)) return rc ? rc : cuda_fail(e, "cudaMalloc(weight copy)");
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(weight copy)");
+  e = cudaMemcpy(d, reinterpret_cast<const void *>(lo), need, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) {
     cudaFree(d);
     return cuda_fail(e, "cudaMemcpy(weight upload)");
   }
-  c.ranges[h].push_back(Range{h, n, d});
-  c.cached += n;
-  *out = d;
+  if (!merged.empty()) {
+    if (!quiet && (rc = quiesce(c))) {
+      cudaFree(d);
+      return rc;
+    }
+    for (uintptr_t k : merged) {
+      cudaFree(c.ranges[k].d);
+      c.cached -= c.ranges[k].n;
+      c.ranges.erase(k);
+    }
+  }
+  c.ranges[lo] = Range{lo, need, d, c.call_no, registered};
+  c.cached += need;
+  *out = d + (h - lo);
   return 0;
 }
 
@@ -906,7 +995,7 @@ void gx10_rust_register_host_range(const void *ptr, size_t bytes) {
   Ctx &c = ctx();
   std::lock_guard<std::mutex> lk(c.mu);
   const void *d;
-  if (ensure_init(c) || dev_ptr(c, ptr, bytes, &d))
+  if (ensure_init(c) || dev_ptr(c, ptr, bytes, &d, true))
     std::fprintf(stderr, "[ffn_b200] register_host_range: %s\n", ffn_b200_last_error());
 }
 
@@ -942,14 +1031,27 @@ int ffn_b200_release_host_ranges(void) {
     const cudaError_t e = cudaStreamSynchronize(c.st);
     if (e != cudaSuccess) rc = cuda_fail(e, "release: stream");
   }
-  for (auto &kv : c.ranges)
-    for (Range &r : kv.second) cudaFree(r.d);
+  for (auto &kv : c.ranges) cudaFree(kv.second.d);
   c.ranges.clear();
   c.cached = 0;
   {
     GsCache &g = gs_cache();
     std::lock_guard<std::mutex> lk2(g.mu);
     g.m.clear();
+  }
+  return rc;
+}
+
+int ffn_b200_set_host_cache_budget(size_t bytes) {
+  Ctx &c = ctx();
+  std::lock_guard<std::mutex> lk(c.mu);
+  c.budget = bytes;
+  if (!bytes || c.cached <= bytes) return 0;
+  // over the new budget: evict now (least recently used first)
+  bool quiet = false;
+  int rc = 0;
+  ++c.call_no;  // no copy belongs to a call in progress
+  while (c.cached > c.budget && evict_one(c, 0, 0, quiet, rc)) {
   }
   return rc;
 }

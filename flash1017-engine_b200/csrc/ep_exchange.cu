@@ -2,163 +2,232 @@
 // over NVLink peer memory, one process per GPU.
 //
 // Every rank owns one block of experts and computes, for all tokens, the
-// weighted sum of its own experts' outputs (its "part").  The layer output is
-// residual + sum over ranks of the parts, needed on every rank (the reference's
-// decode MoE block, crates/flash-core/src/flash1017.rs:7521-7567, with the
-// residual add of flash1017.rs:4900-4905).  Instead of an NCCL all-reduce, one
-// cooperative kernel per GPU does a two-shot exchange over peer memory:
+// weighted sum of its own experts' outputs (its "partial").  The layer output is
+// residual + sum over ranks of the partials, needed on every rank (the
+// reference's decode MoE block, crates/flash-core/src/flash1017.rs:7521-7567,
+// with the residual add of flash1017.rs:4900-4905).  One cooperative kernel per
+// GPU (one CTA per SM) does it by pushing, never by polling a peer:
 //
-//   1. signal "part ready" (epoch e) to every peer; wait for every peer's
-//      signal (bounded);
-//   2. rank r sums its slice of token rows [r T/N, (r+1) T/N) from all parts
-//      in rank order (deterministic), adds the residual, and writes the rows to
-//      its result buffer red[e % 2];
-//   3. grid-wide sync, signal "slice ready"; wait for every peer's signal;
-//   4. every rank copies all slices from the owners' result buffers into out.
+//   A. every CTA forms its share of this rank's partial rows -- from the part
+//      buffer the MoE layer wrote, or (fused) straight from the layer's expert
+//      outputs, combined per token as the combine kernel does -- and stores
+//      each row into the inbox of the rank that owns the row's slice of tokens
+//      (rank s owns rows [s R, (s+1) R), R = ceil(tokens / world)); then it adds
+//      1 to every rank's arrival counter 1 (red.release.sys).
+//   B. once counter 1 of this rank has reached world x grid x calls, every
+//      sender's rows have landed in this rank's inbox: the CTAs sum the slice's
+//      rows over the senders in rank order (deterministic), add the residual,
+//      and store each result row into every rank's output slot; then they add 1
+//      to every rank's counter 2.
+//   C. once counter 2 has reached its target, the whole layer output sits in
+//      this rank's slot; the CTAs copy it to `out`.
 //
-// Bytes over NVLink per rank: (N-1)/N of the parts' rows in step 2 and (N-1)/N
-// of the output in step 4.  Buffers live in one allocation per rank shared
-// through CUDA IPC (cudaIpcGetMemHandle / cudaIpcOpenMemHandle; peers' memory
-// is read with plain loads, no TMA and no multicast).  The result buffer is
-// double-buffered by epoch: a rank can be at most one call ahead of a peer
-// (step 1 of call e+1 waits for the peer to finish call e), so it never
-// overwrites rows a peer is still reading.  Every wait gives up after a bounded
-// number of polls, sets the error word and returns; the kernel then writes NaN
-// over `out` so a failed exchange is visible.
+// NVLink traffic per rank and call: (N-1)/N of the partial rows out in A and
+// (N-1)/N of the output rows out in B, all as plain 16-byte stores to peer
+// memory (CUDA IPC mappings; no TMA of any form).  The counters only grow
+// (each call adds world x grid), so no reset is needed; a rank can start call
+// e+1 only after counter 2 of call e told it that every rank finished reading
+// its inbox (B), so the inboxes need no double buffering; the output slots
+// alternate by call parity, so the rows a peer writes for call e+1 never land
+// on the slot this rank still reads as call e's input.  Every wait polls local
+// memory only and gives up after a bounded time (kEpWaitNs): it sets the error
+// word, the CTA writes NaN, and ffn_b200_ep_error reports it.
 #include <cooperative_groups.h>
 
 #include <algorithm>
 
 #include "ffn_internal.h"
 
-namespace cg = cooperative_groups;
-
 namespace ffn {
 namespace {
 
 constexpr int kEpMax = 8;
-constexpr long long kEpSpin = 1LL << 22;  // flag polls per wait before giving up
+// A wait gives up after this long (ns of %globaltimer): well above any skew
+// between ranks that reach the same call (a step's host work, a slow launch),
+// short enough that a rank that never arrives ends the call.
+constexpr unsigned long long kEpWaitNs = 5000000000ull;
+constexpr int kEpThreads = 256;
+constexpr int kEpChunk = 4 * kEpThreads;  // floats of a row per work unit
 
-struct EpShared {        // header of every rank's shared allocation
-  uint32_t flags[2][kEpMax];  // [phase][source rank] = last epoch signalled
+struct EpShared {  // header of every rank's shared allocation
+  unsigned long long cnt1;  // arrivals of phase A
+  unsigned long long pad1[15];
+  unsigned long long cnt2;  // arrivals of phase B
+  unsigned long long pad2[15];
   int err;
-  uint32_t pad[64 - 2 * kEpMax - 1];
+  int pad3[63];
 };
 
-struct EpArgs {
-  int rank, world, n_tok, hidden;
-  uint32_t epoch;
-  const float *part[kEpMax];   // every rank's part (own entry local)
-  float *red_local;            // own result buffer for this epoch
-  const float *red[kEpMax];    // every rank's result buffer for this epoch
-  uint32_t *flags_peer[kEpMax];// every rank's flags
-  uint32_t *flags_local;
+struct PushArgs {
+  int rank, world, n_tok, hidden, rows_per, chunks;
+  unsigned long long target;      // counter value once every CTA of every rank arrived
+  const float *part;              // the partial rows (unfused), or
+  EpCombine comb;                 // the MoE layer's expert outputs (fused)
+  int fused;
+  float *inbox[kEpMax];           // every rank's inbox: [sender][rows_per][hidden]
+  float *slot[kEpMax];            // every rank's output slot of this call
+  unsigned long long *cnt1[kEpMax], *cnt2[kEpMax];
+  const unsigned long long *cnt1_local, *cnt2_local;
   int *err;
-  const float *residual;       // nullable
+  const float *residual;          // nullable
   float *out;
 };
 
-__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void red_release_sys(unsigned long long *p, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
-// Block 0 tells every peer that this rank reached `phase` of call `epoch`;
-// then every block waits until all peers did (epochs only grow, so >= works).
-__device__ bool ep_barrier(const EpArgs &a, int phase) {
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Thread 0 polls the local counter until it reaches `target` (bounded in
+// time); the CTA learns the outcome through shared memory.
+__device__ bool wait_count(const unsigned long long *c, unsigned long long target, int *err) {
   __shared__ int s_ok;
-  if (blockIdx.x == 0 && threadIdx.x < a.world)
-    st_release_sys(a.flags_peer[threadIdx.x] + phase * kEpMax + a.rank, a.epoch);
   if (threadIdx.x == 0) {
     int ok = 1;
-    for (int src = 0; src < a.world && ok; ++src) {
-      long long it = 0;
-      while ((int32_t)(ld_acquire_sys(a.flags_local + phase * kEpMax + src) - a.epoch) < 0) {
-        if (++it > kEpSpin || *(volatile int *)a.err) { ok = 0; break; }
-      }
+    const unsigned long long t0 = global_ns();
+    long long it = 0;
+    while ((long long)(ld_acquire_sys(c) - target) < 0) {
+      if ((++it & 255) == 0 && (global_ns() - t0 > kEpWaitNs || *(volatile int *)err)) { ok = 0; break; }
     }
-    if (!ok) atomicExch(a.err, 1);
+    if (!ok) atomicExch(err, 1);
     s_ok = ok;
   }
   __syncthreads();
   return s_ok != 0;
 }
 
-// W = world size (compile time: every peer's load of a step issues at once).
+__device__ __forceinline__ float4 nan4() {
+  const float q = __int_as_float(0x7FC00000);
+  return make_float4(q, q, q, q);
+}
+
+// W = world size (compile time: every sender's load of a phase-B row issues at once).
 template <int W>
-__global__ void __launch_bounds__(256) ep_exchange_kernel(const EpArgs a) {
-  cg::grid_group grid = cg::this_grid();
+__global__ void __launch_bounds__(kEpThreads) ep_push_kernel(const PushArgs a) {
+  __shared__ float wk[kTopKMax];
+  __shared__ int pk[kTopKMax];
+  __shared__ int s_bad;
   const int H4 = a.hidden / 4;
-  const int rows_per = (a.n_tok + W - 1) / W;
-  const int r0 = min(a.n_tok, a.rank * rows_per), r1 = min(a.n_tok, r0 + rows_per);
-  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const long long nthr = (long long)gridDim.x * blockDim.x;
-  bool ok = ep_barrier(a, 0);
-  if (ok) {
-    // step 2: own slice, summed over the ranks in rank order
-    const long long n4 = (long long)(r1 - r0) * H4;
-    for (long long i = tid; i < n4; i += nthr) {
-      const size_t off = (size_t)r0 * a.hidden + (size_t)i * 4;
-      float4 v[W];
-#pragma unroll
-      for (int src = 0; src < W; ++src) v[src] = __ldcg(reinterpret_cast<const float4 *>(a.part[src] + off));
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int src = 0; src < W; ++src) {
-        acc.x = __fadd_rn(acc.x, v[src].x); acc.y = __fadd_rn(acc.y, v[src].y);
-        acc.z = __fadd_rn(acc.z, v[src].z); acc.w = __fadd_rn(acc.w, v[src].w);
-      }
-      if (a.residual) {
-        const float4 r = *reinterpret_cast<const float4 *>(a.residual + off);
-        acc.x = __fadd_rn(r.x, acc.x); acc.y = __fadd_rn(r.y, acc.y);
-        acc.z = __fadd_rn(r.z, acc.z); acc.w = __fadd_rn(r.w, acc.w);
-      }
-      *reinterpret_cast<float4 *>(a.red_local + off) = acc;
-    }
-  }
-  __threadfence_system();
-  grid.sync();
-  ok = ok && !*(volatile int *)a.err && ep_barrier(a, 1);
-  if (ok) {
-    // step 4: every slice from its owner, four 16-byte loads in flight per thread
-    const long long n4 = (long long)a.n_tok * H4;
-    for (long long i0 = tid; i0 < n4; i0 += 4 * nthr) {
-      float4 v[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const long long i = i0 + u * nthr;
-        if (i < n4) {
-          const int owner = min(W - 1, (int)(i / H4) / rows_per);
-          v[u] = __ldcg(reinterpret_cast<const float4 *>(a.red[owner] + (size_t)i * 4));
+  const bool moe_bad = a.fused && a.comb.err && *a.comb.err;
+  // ---- A: this rank's partial rows into the owners' inboxes
+  const int units_a = a.n_tok * a.chunks;
+  for (int u = blockIdx.x; u < units_a; u += gridDim.x) {
+    const int t = u / a.chunks, c4 = (u % a.chunks) * kEpThreads + threadIdx.x;
+    if (a.fused) {
+      __syncthreads();  // wk / pk of the previous unit are no longer read
+      if (threadIdx.x == 0) s_bad = 0;
+      __syncthreads();
+      if (threadIdx.x < a.comb.top_k) {
+        const int q = t * a.comb.top_k + threadIdx.x;
+        const int e = a.comb.idx[q];
+        if (e < 0 || e >= a.comb.n_exp) {  // no expert selected (every score NaN): no table read
+          s_bad = 1;
+          wk[threadIdx.x] = 0.f;
+          pk[threadIdx.x] = -1;
+        } else {
+          float w = a.comb.wt[q];
+          if (a.comb.experts[e].format == FFN_B200_FMT_TERNARY) w = w * a.comb.experts[e].proj_scale;
+          const int pp = a.comb.inv[q];
+          if (pp >= a.comb.y_rows) s_bad = 1;  // not a row of y: no read
+          wk[threadIdx.x] = w;
+          pk[threadIdx.x] = pp < a.comb.y_rows ? pp : -1;
         }
       }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const long long i = i0 + u * nthr;
-        if (i < n4) *reinterpret_cast<float4 *>(a.out + (size_t)i * 4) = v[u];
-      }
+      __syncthreads();
     }
-  } else {
-    const long long n = (long long)a.n_tok * a.hidden;
-    for (long long i = tid; i < n; i += nthr) a.out[i] = __int_as_float(0x7FC00000);
+    if (c4 < H4) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (!a.fused) {
+        acc = __ldcg(reinterpret_cast<const float4 *>(a.part + (size_t)t * a.hidden) + c4);
+      } else if (moe_bad || s_bad) {
+        acc = nan4();
+      } else {
+        // the combine kernel's arithmetic: acc += w_k * y_k over this rank's experts, in k order
+        for (int k = 0; k < a.comb.top_k; ++k) {
+          const int pp = pk[k];
+          if (pp < 0) continue;
+          const float4 y = __ldg(reinterpret_cast<const float4 *>(a.comb.y + (size_t)pp * a.comb.ld_y) + c4);
+          acc.x = __fadd_rn(acc.x, __fmul_rn(wk[k], y.x));
+          acc.y = __fadd_rn(acc.y, __fmul_rn(wk[k], y.y));
+          acc.z = __fadd_rn(acc.z, __fmul_rn(wk[k], y.z));
+          acc.w = __fadd_rn(acc.w, __fmul_rn(wk[k], y.w));
+        }
+      }
+      const int s = t / a.rows_per, j = t - s * a.rows_per;
+      float *dst = a.inbox[s] + ((size_t)a.rank * a.rows_per + j) * a.hidden;
+      reinterpret_cast<float4 *>(dst)[c4] = acc;
+    }
+  }
+  // the CTA's stores, then one system-scope fence and the releases (cumulative
+  // over the stores the barrier ordered before them)
+  __syncthreads();
+  if (threadIdx.x == 0) __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < W) red_release_sys(a.cnt1[threadIdx.x], 1ull);
+  // ---- B: this rank's slice, summed over the senders, pushed to every rank
+  const bool ok_a = wait_count(a.cnt1_local, a.target, a.err);
+  const int r0 = a.rank * a.rows_per;
+  const int nr = max(0, min(a.n_tok - r0, a.rows_per));
+  const float *inbox = a.inbox[a.rank];
+  for (int u = blockIdx.x; u < nr * a.chunks; u += gridDim.x) {
+    const int j = u / a.chunks, c4 = (u % a.chunks) * kEpThreads + threadIdx.x;
+    if (c4 >= H4) continue;
+    const int t = r0 + j;
+    float4 v[W];
+#pragma unroll
+    for (int src = 0; src < W; ++src)
+      v[src] = __ldcg(reinterpret_cast<const float4 *>(inbox + ((size_t)src * a.rows_per + j) * a.hidden) + c4);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int src = 0; src < W; ++src) {
+      acc.x = __fadd_rn(acc.x, v[src].x); acc.y = __fadd_rn(acc.y, v[src].y);
+      acc.z = __fadd_rn(acc.z, v[src].z); acc.w = __fadd_rn(acc.w, v[src].w);
+    }
+    if (a.residual) {
+      const float4 r = reinterpret_cast<const float4 *>(a.residual + (size_t)t * a.hidden)[c4];
+      acc.x = __fadd_rn(r.x, acc.x); acc.y = __fadd_rn(r.y, acc.y);
+      acc.z = __fadd_rn(r.z, acc.z); acc.w = __fadd_rn(r.w, acc.w);
+    }
+    if (!ok_a) acc = nan4();
+#pragma unroll
+    for (int dst = 0; dst < W; ++dst) reinterpret_cast<float4 *>(a.slot[dst] + (size_t)t * a.hidden)[c4] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < W) red_release_sys(a.cnt2[threadIdx.x], 1ull);
+  // ---- C: every slice has arrived in this rank's slot
+  const bool ok = wait_count(a.cnt2_local, a.target, a.err) && ok_a;
+  if (a.out) {
+    const float *mine = a.slot[a.rank];
+    const long long n4 = (long long)a.n_tok * H4;
+    for (long long i = (long long)blockIdx.x * kEpThreads + threadIdx.x; i < n4;
+         i += (long long)gridDim.x * kEpThreads)
+      reinterpret_cast<float4 *>(a.out)[i] = ok ? __ldcg(reinterpret_cast<const float4 *>(mine) + i) : nan4();
   }
 }
 
-using ExchangeFn = void (*)(const EpArgs);
+using ExchangeFn = void (*)(const PushArgs);
 ExchangeFn exchange_kernel(int world) {
   switch (world) {
-    case 1: return ep_exchange_kernel<1>;
-    case 2: return ep_exchange_kernel<2>;
-    case 3: return ep_exchange_kernel<3>;
-    case 4: return ep_exchange_kernel<4>;
-    case 5: return ep_exchange_kernel<5>;
-    case 6: return ep_exchange_kernel<6>;
-    case 7: return ep_exchange_kernel<7>;
-    default: return ep_exchange_kernel<8>;
+    case 1: return ep_push_kernel<1>;
+    case 2: return ep_push_kernel<2>;
+    case 3: return ep_push_kernel<3>;
+    case 4: return ep_push_kernel<4>;
+    case 5: return ep_push_kernel<5>;
+    case 6: return ep_push_kernel<6>;
+    case 7: return ep_push_kernel<7>;
+    default: return ep_push_kernel<8>;
   }
 }
 
@@ -170,17 +239,74 @@ using namespace ffn;
 struct ffn_b200_ep {
   int rank = 0, world = 1, device = 0;
   size_t max_tokens = 0, hidden = 0;
-  size_t part_bytes = 0;
-  uint8_t *base = nullptr;              // own allocation: header | part | red[2]
+  size_t part_bytes = 0, inbox_bytes = 0;
+  uint8_t *base = nullptr;              // own allocation: header | part | inbox | slot[2]
   uint8_t *peer[kEpMax] = {nullptr};    // every rank's allocation (own = base)
-  uint32_t epoch = 0;
+  unsigned long long epoch = 0;
   int grid = 0;
 };
 
-static size_t ep_alloc_bytes(size_t max_tokens, size_t hidden) {
-  const size_t part = (max_tokens * hidden * sizeof(float) + 255) & ~(size_t)255;
-  return sizeof(EpShared) + 3 * part;
+static size_t round256(size_t n) { return (n + 255) & ~(size_t)255; }
+static size_t rows_max(size_t max_tokens, int world) { return (max_tokens + world - 1) / world; }
+static size_t ep_alloc_bytes(const ffn_b200_ep &ep) {
+  return sizeof(EpShared) + ep.part_bytes + ep.inbox_bytes + 2 * ep.part_bytes;
 }
+
+namespace ffn {
+
+// One exchange call: this rank's partial (the part buffer, or the MoE layer's
+// expert outputs when comb != nullptr) summed over every rank, + residual, into out.
+int ep_exchange(ffn_b200_ep *ep, size_t n_tok, const EpCombine *comb, const float *residual, float *out,
+                cudaStream_t st) {
+  if (!ep || !out) return fail(FFN_B200_EINVAL, "ep exchange: null argument");
+  if (n_tok > ep->max_tokens) return fail(FFN_B200_EINVAL, "ep exchange: more tokens than ep_create's");
+  for (int r = 0; r < ep->world; ++r)
+    if (!ep->peer[r]) return fail(FFN_B200_EINVAL, "ep exchange: ep_connect has not opened every peer");
+  if ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(residual)) & 15)
+    return fail(FFN_B200_EINVAL, "ep exchange: out and residual must be 16-byte aligned");
+  if (comb && (comb->ld_y % 4 || (reinterpret_cast<uintptr_t>(comb->y) & 15) || comb->top_k > kTopKMax))
+    return fail(FFN_B200_EINVAL, "ep exchange: expert outputs must be 16-byte aligned rows");
+  if (n_tok == 0) return 0;
+  ++ep->epoch;
+  PushArgs a{};
+  a.rank = ep->rank;
+  a.world = ep->world;
+  a.n_tok = (int)n_tok;
+  a.hidden = (int)ep->hidden;
+  a.rows_per = (int)((n_tok + ep->world - 1) / ep->world);
+  a.chunks = (int)((ep->hidden + kEpChunk - 1) / kEpChunk);
+  a.target = ep->epoch * (unsigned long long)ep->world * (unsigned long long)ep->grid;
+  a.part = reinterpret_cast<const float *>(ep->base + sizeof(EpShared));
+  if (comb) {
+    a.comb = *comb;
+    a.fused = 1;
+  }
+  const size_t inbox_off = sizeof(EpShared) + ep->part_bytes;
+  const size_t slot_off = inbox_off + ep->inbox_bytes + (ep->epoch & 1) * ep->part_bytes;
+  for (int r = 0; r < ep->world; ++r) {
+    EpShared *h = reinterpret_cast<EpShared *>(ep->peer[r]);
+    a.inbox[r] = reinterpret_cast<float *>(ep->peer[r] + inbox_off);
+    a.slot[r] = reinterpret_cast<float *>(ep->peer[r] + slot_off);
+    a.cnt1[r] = &h->cnt1;
+    a.cnt2[r] = &h->cnt2;
+  }
+  EpShared *mine = reinterpret_cast<EpShared *>(ep->base);
+  a.cnt1_local = &mine->cnt1;
+  a.cnt2_local = &mine->cnt2;
+  a.err = &mine->err;
+  a.residual = residual;
+  a.out = out;
+  void *args[] = {&a};
+  prof_begin(FFN_B200_K_OTHER, st);
+  cudaError_t e = cudaLaunchCooperativeKernel((const void *)exchange_kernel(ep->world), dim3(ep->grid),
+                                              dim3(kEpThreads), args, 0, st);
+  prof_end(FFN_B200_K_OTHER, st);
+  note_launch();
+  if (e != cudaSuccess) return cuda_fail(e, "ep exchange: cooperative launch");
+  return 0;
+}
+
+}  // namespace ffn
 
 extern "C" {
 
@@ -199,22 +325,26 @@ int ffn_b200_ep_create(int rank, int world, size_t max_tokens, size_t hidden, vo
   ep->world = world;
   ep->max_tokens = max_tokens;
   ep->hidden = hidden;
-  ep->part_bytes = (max_tokens * hidden * sizeof(float) + 255) & ~(size_t)255;
+  ep->part_bytes = round256(max_tokens * hidden * sizeof(float));
+  ep->inbox_bytes = round256((size_t)world * rows_max(max_tokens, world) * hidden * sizeof(float));
   cudaError_t e = cudaGetDevice(&ep->device);
-  if (e == cudaSuccess) e = cudaMalloc(&ep->base, ep_alloc_bytes(max_tokens, hidden));
+  if (e == cudaSuccess) e = cudaMalloc(&ep->base, ep_alloc_bytes(*ep));
   if (e == cudaSuccess) e = cudaMemset(ep->base, 0, sizeof(EpShared));
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t *>(my_handle), ep->base);
   int sms = 0;
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ep->device);
   int per_sm = 0;
   if (e == cudaSuccess)
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, exchange_kernel(world), 256, 0);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, exchange_kernel(world), kEpThreads, 0);
+  if (e == cudaSuccess && per_sm < 1) e = cudaErrorCooperativeLaunchTooLarge;
   if (e != cudaSuccess) {
     if (ep->base) cudaFree(ep->base);
     delete ep;
     return cuda_fail(e, "ep_create");
   }
-  ep->grid = std::max(1, sms * std::min(per_sm, 2));  // co-resident (cooperative launch)
+  // one CTA per SM: every CTA of every rank must be resident at once (each
+  // waits for the others' arrivals), and every rank uses the same count
+  ep->grid = sms;
   ep->peer[rank] = ep->base;
   *out = ep;
   return 0;
@@ -239,40 +369,7 @@ float *ffn_b200_ep_part(ffn_b200_ep *ep) {
 
 int ffn_b200_ep_allreduce(ffn_b200_ep *ep, size_t n_tok, const float *residual, float *out,
                           void *stream) {
-  if (!ep || !out) return fail(FFN_B200_EINVAL, "ep_allreduce: null argument");
-  if (n_tok > ep->max_tokens) return fail(FFN_B200_EINVAL, "ep_allreduce: more tokens than ep_create's");
-  for (int r = 0; r < ep->world; ++r)
-    if (!ep->peer[r]) return fail(FFN_B200_EINVAL, "ep_allreduce: ep_connect has not opened every peer");
-  if ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(residual)) & 15)
-    return fail(FFN_B200_EINVAL, "ep_allreduce: out and residual must be 16-byte aligned");
-  if (n_tok == 0) return 0;
-  ++ep->epoch;
-  EpArgs a{};
-  a.rank = ep->rank;
-  a.world = ep->world;
-  a.n_tok = (int)n_tok;
-  a.hidden = (int)ep->hidden;
-  a.epoch = ep->epoch;
-  const size_t red_off = sizeof(EpShared) + ep->part_bytes * (1 + (ep->epoch & 1));
-  for (int r = 0; r < ep->world; ++r) {
-    a.part[r] = reinterpret_cast<const float *>(ep->peer[r] + sizeof(EpShared));
-    a.red[r] = reinterpret_cast<const float *>(ep->peer[r] + red_off);
-    a.flags_peer[r] = reinterpret_cast<EpShared *>(ep->peer[r])->flags[0];
-  }
-  a.red_local = reinterpret_cast<float *>(ep->base + red_off);
-  a.flags_local = reinterpret_cast<EpShared *>(ep->base)->flags[0];
-  a.err = &reinterpret_cast<EpShared *>(ep->base)->err;
-  a.residual = residual;
-  a.out = out;
-  void *args[] = {&a};
-  cudaStream_t st = (cudaStream_t)stream;
-  prof_begin(FFN_B200_K_OTHER, st);
-  cudaError_t e = cudaLaunchCooperativeKernel((const void *)exchange_kernel(ep->world), dim3(ep->grid),
-                                              dim3(256), args, 0, st);
-  prof_end(FFN_B200_K_OTHER, st);
-  note_launch();
-  if (e != cudaSuccess) return cuda_fail(e, "ep_allreduce: cooperative launch");
-  return 0;
+  return ffn::ep_exchange(ep, n_tok, nullptr, residual, out, (cudaStream_t)stream);
 }
 
 int ffn_b200_ep_error(ffn_b200_ep *ep, int *flag) {

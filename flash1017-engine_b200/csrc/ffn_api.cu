@@ -599,7 +599,7 @@ struct MoeWs {
   float *part;     // GEMV path: K-split partial sums (kListSplitBytes)
   int *cnt;        // GEMV path: split arrival counters, kSplitItems per phase launch (4)
   // FP4 path: x and h as four NVFP4 terms, h in f32, the chunk list
-  uint8_t *xq, *xs, *hq, *hs, *f4chunk;
+  uint8_t *xq, *xs, *hq, *hs;
   int *xqe, *hqe;
   float *hf;
 };
@@ -644,7 +644,6 @@ static MoeWs carve_moe(Carve &c, const ffn_b200_moe_desc &d, size_t T) {
     w.hq = c.take<uint8_t>(P * 4 * I / 2);
     w.hs = c.take<uint8_t>(P * 4 * I / 16);
     w.hqe = c.take<int>(P * 4);
-    w.f4chunk = c.take<uint8_t>(fp4_chunk_bytes((int)P, (int)E));
   }
   return w;
 }
@@ -1033,11 +1032,22 @@ int ffn::routed_calls(const RoutedCalls &q, size_t inter, size_t hidden, void *s
                            (int)H, q.out, st);
 }
 
-extern "C" {
+// Per token: out = residual + sum of w * y over the layer's routes (combine
+// kernel), or, expert-parallel, over every rank's routes (exchange).
+static int finish_layer(const ffn_b200_moe_desc *d, const MoeWs &w, int T, const float *residual, float *out,
+                        const int *err, ffn_b200_ep *ep, cudaStream_t st) {
+  const int H = (int)d->hidden, k = (int)d->top_k;
+  const int E = (int)d->n_experts;
+  if (!ep) return launch_combine(w.y, H, w.idx, w.wt, w.inv, T, k, d->experts, residual, out, H, st, err, E);
+  EpCombine cb{w.y, H, w.idx, w.wt, w.inv, k, d->experts, err, E, T * k};
+  return ep_exchange(ep, (size_t)T, &cb, residual, out, st);
+}
 
-int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
-                       const float *residual, float *out, int32_t *topk_idx, float *topk_w,
-                       void *ws, size_t ws_bytes, void *stream) {
+// The MoE layer; with `ep`, this rank's partial goes through the expert-parallel
+// exchange (combined per token inside it) instead of the combine kernel.
+static int moe_layer_impl(const ffn_b200_moe_desc *d, size_t n_tok, const float *x, const float *residual,
+                          float *out, int32_t *topk_idx, float *topk_w, void *ws, size_t ws_bytes,
+                          void *stream, ffn_b200_ep *ep) {
   if (!d) return fail(FFN_B200_EINVAL, "moe_layer: null descriptor");
   const size_t H = d->hidden, I = d->inter, E = d->n_experts, k = d->top_k;
   if (!d->experts || !d->router_w) return fail(FFN_B200_EINVAL, "moe_layer: null experts/router");
@@ -1110,9 +1120,7 @@ int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
     g.chunk_ws = w.chunk;
     g.err = w.err;
     if ((rc = launch_grouped_moe(g, st))) return rc;
-    if ((rc = launch_combine(w.y, (int)H, w.idx, w.wt, w.inv, T, (int)k, d->experts, residual, out,
-                             (int)H, st, w.err)))
-      return rc;
+    if ((rc = finish_layer(d, w, T, residual, out, w.err, ep, st))) return rc;
     if (topk_idx)
       FFN_CUDA_TRY(cudaMemcpyAsync(topk_idx, w.idx, P * sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
     if (topk_w)
@@ -1131,8 +1139,8 @@ int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
     g.n_pairs = P;
     g.hidden = (int)H;
     g.inter = (int)I;
-    g.counts = w.ints;
-    g.offsets = w.ints + E;
+    g.slices = w.vexp_nv;
+    g.n_slices = w.n_vexp;
     g.pair_tok = w.pair_tok;
     g.x = xin;
     g.xq = w.xq;
@@ -1143,20 +1151,32 @@ int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
     g.hs = w.hs;
     g.hqe = w.hqe;
     g.y = w.y;
-    g.chunk_ws = w.f4chunk;
     g.err = w.err;
     if ((rc = launch_fp4_moe(g, st))) return rc;
   } else if ((rc = moe_gemv_experts(d, w, P, xin, st))) {
     return rc;
   }
-  if ((rc = launch_combine(w.y, (int)H, w.idx, w.wt, w.inv, T, (int)k, d->experts, residual, out,
-                           (int)H, st, fp4 ? w.err : nullptr)))
-    return rc;
+  if ((rc = finish_layer(d, w, T, residual, out, fp4 ? w.err : nullptr, ep, st))) return rc;
   if (topk_idx)
     FFN_CUDA_TRY(cudaMemcpyAsync(topk_idx, w.idx, P * sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
   if (topk_w)
     FFN_CUDA_TRY(cudaMemcpyAsync(topk_w, w.wt, P * sizeof(float), cudaMemcpyDeviceToDevice, st));
   return 0;
+}
+
+extern "C" {
+
+int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
+                       const float *residual, float *out, int32_t *topk_idx, float *topk_w,
+                       void *ws, size_t ws_bytes, void *stream) {
+  return moe_layer_impl(d, n_tok, x, residual, out, topk_idx, topk_w, ws, ws_bytes, stream, nullptr);
+}
+
+int ffn_b200_ep_moe_layer(ffn_b200_ep *ep, const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
+                          const float *residual, float *out, int32_t *topk_idx, float *topk_w, void *ws,
+                          size_t ws_bytes, void *stream) {
+  if (!ep) return fail(FFN_B200_EINVAL, "ep_moe_layer: null exchange");
+  return moe_layer_impl(d, n_tok, x, residual, out, topk_idx, topk_w, ws, ws_bytes, stream, ep);
 }
 
 // -------------------------------------------------------------- generators

@@ -63,7 +63,8 @@ struct Fp4Args {
   int e_begin, e_end;
   int n_tok, n_pairs;
   int hidden, inter;
-  const int *counts, *offsets;  // per expert, from the grouping kernel
+  const VExp *slices;           // the grouping kernel's NVFP4 slices (<= 8 pairs of one expert)
+  const int *n_slices;          // their count (device)
   const int32_t *pair_tok;
   const float *x;               // [n_tok][hidden] f32, the layer input the experts see
   uint8_t *xq, *xs;             // x as 4 NVFP4 terms: codes [tok][4][hidden/2], scales [tok][4][hidden/16]
@@ -72,13 +73,30 @@ struct Fp4Args {
   uint8_t *hq, *hs;             // h as 4 NVFP4 terms
   int *hqe;
   float *y;                     // [pair][hidden]
-  uint8_t *chunk_ws;            // fp4_chunk_bytes(n_pairs, e_end - e_begin)
   int *err;                     // device int: 1 timed-out wait, 2 scale outside UE4M3, 3 misaligned
 };
-size_t fp4_chunk_bytes(int n_pairs, int n_local);
 int launch_fp4_moe(const Fp4Args &g, cudaStream_t st);
 // rows of f32 (K % 256 == 0, K <= 16384, 16-byte aligned rows) -> 4 NVFP4 terms
 int launch_q4(const float *x, int ld_x, int rows, int K, uint8_t *qc, uint8_t *qs, int *qe, cudaStream_t st);
+
+// The MoE layer's per-pair expert outputs, combined per token inside the
+// expert-parallel exchange (the fused form of launch_combine).
+struct EpCombine {
+  const float *y;             // [pair][ld_y] expert outputs (unweighted)
+  int ld_y;
+  const int32_t *idx;         // [tok][top_k] routed experts
+  const float *wt;            // [tok][top_k] routing weights
+  const int32_t *inv;         // [tok][top_k] pair row of each local route, -1 when not local
+  int top_k;
+  const ffn_b200_expert *experts;
+  const int *err;             // upstream error word (nonzero: NaN partials), or nullptr
+  int n_exp;                  // experts in the table (a route outside it: NaN partial)
+  int y_rows;                 // rows of y (the layer's routed pairs)
+};
+// One exchange call over ep's ranks: out = residual + sum over ranks of each
+// rank's partial (its part buffer, or its combined expert outputs).
+int ep_exchange(ffn_b200_ep *ep, size_t n_tok, const EpCombine *comb, const float *residual, float *out,
+                cudaStream_t st);
 
 // Arguments of the rank-16 core z kernel.
 struct CoreZArgs {
@@ -162,7 +180,7 @@ int launch_group(const int32_t *idx, int n_tok, int top_k, int n_exp, int e_begi
 int launch_combine(const float *y, int ld_y, const int32_t *idx, const float *wt,
                    const int32_t *inv, int n_tok, int top_k, const ffn_b200_expert *experts,
                    const float *residual, float *out, int H, cudaStream_t st,
-                   const int *err = nullptr);
+                   const int *err, int n_exp);
 int launch_dot(int mode, const void *a, const void *aux, const float *x, size_t len, float *out,
                cudaStream_t st);
 int launch_gen_nvfp4(uint64_t kw, uint64_t ks, size_t rows, size_t cols, uint8_t *w, uint8_t *s,

@@ -1231,24 +1231,33 @@ __global__ void __launch_bounds__(1024) combine_kernel(const float *__restrict__
                                                       const int32_t *__restrict__ inv, int top_k,
                                                       const ffn_b200_expert *__restrict__ experts,
                                                       const float *residual, float *out, int H,
-                                                      const int *err) {
+                                                      const int *err, int n_exp) {
   pdl_enter();
   const int t = blockIdx.x;
-  if (err && *err) {  // an upstream kernel gave up on a wait: make the failure visible
-    for (int c = threadIdx.x; c < H; c += blockDim.x) out[(size_t)t * H + c] = __int_as_float(0x7FC00000);
-    return;
-  }
   __shared__ float wk[kTopKMax];
   __shared__ int pk[kTopKMax];
+  __shared__ int s_bad;
+  if (threadIdx.x == 0) s_bad = err && *err;  // an upstream kernel gave up on a wait
+  __syncthreads();
   if (threadIdx.x < top_k) {
     const int q = t * top_k + threadIdx.x;
     const int e = idx[q];
-    float w = wt[q];
-    if (experts[e].format == FFN_B200_FMT_TERNARY) w = w * experts[e].proj_scale;
-    wk[threadIdx.x] = w;
-    pk[threadIdx.x] = inv[q];
+    if (e < 0 || e >= n_exp) {  // no expert selected (every score NaN): no table read
+      s_bad = 1;
+      wk[threadIdx.x] = 0.f;
+      pk[threadIdx.x] = -1;
+    } else {
+      float w = wt[q];
+      if (experts[e].format == FFN_B200_FMT_TERNARY) w = w * experts[e].proj_scale;
+      wk[threadIdx.x] = w;
+      pk[threadIdx.x] = inv[q];
+    }
   }
   __syncthreads();
+  if (s_bad) {  // make the failure visible
+    for (int c = threadIdx.x; c < H; c += blockDim.x) out[(size_t)t * H + c] = __int_as_float(0x7FC00000);
+    return;
+  }
   if (H % 4 == 0 && ld_y % 4 == 0 && ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(out) |
                                        reinterpret_cast<uintptr_t>(residual)) & 15) == 0) {
     // four columns per thread; the terms' loads issue 8 at a time
@@ -1297,9 +1306,9 @@ __global__ void __launch_bounds__(1024) combine_kernel(const float *__restrict__
 
 int launch_combine(const float *y, int ld_y, const int32_t *idx, const float *wt,
                    const int32_t *inv, int n_tok, int top_k, const ffn_b200_expert *experts,
-                   const float *residual, float *out, int H, cudaStream_t st, const int *err) {
+                   const float *residual, float *out, int H, cudaStream_t st, const int *err, int n_exp) {
   if (n_tok <= 0) return 0;
-  FFN_LAUNCH_PDL(FFN_B200_K_COMBINE, st, "combine_kernel", combine_kernel, n_tok, std::min(1024, std::max(32, H / 4)), 0, y, ld_y, idx, wt, inv, top_k, experts, residual, out, H, err);
+  FFN_LAUNCH_PDL(FFN_B200_K_COMBINE, st, "combine_kernel", combine_kernel, n_tok, std::min(1024, std::max(32, H / 4)), 0, y, ld_y, idx, wt, inv, top_k, experts, residual, out, H, err, n_exp);
   return 0;
 }
 

@@ -20,8 +20,8 @@
 //
 // Kernels:
 //   q4_kernel        rows of f32 -> 4 NVFP4 terms (codes [row][t][K/2], scales
-//                    [row][t][K/16], exponents [row][t]); one CTA per row.
-//   f4_chunk_kernel  per local expert, chunks of <= 8 routed pairs.
+//                    [row][t][K/16], exponents [row][t]); one CTA per row, one
+//                    thread per 16-value block.
 //   fp4_gemm_kernel  PH 1: h[p][r] = SwiGLU(gate, up) for 128 rows of W1 and W3;
 //                    PH 2: y[p][r] for 256 rows of W2 (two 128-row blocks).
 // The gemm is persistent (one CTA per SM walks the (chunk, row block) tiles)
@@ -52,8 +52,14 @@ namespace f4 {
 
 constexpr int kThreads = 256;
 constexpr int kStages = 4;
-constexpr int kLag = 2;            // cp.async groups in flight past the one being handed over
-static_assert(kLag < kStages, "a producer hands a stage over before it needs the slot again");
+#ifndef F4_LAG
+#define F4_LAG 2
+#endif
+constexpr int kLag = F4_LAG;       // cp.async groups in flight past the one being handed over
+// kLag <= kStages - 2: one stage of slack between the hand-over of stage j and
+// the producer's wait for slot j + kStages (with kLag = kStages - 1 every stage
+// waits for the MMA commit round trip: 3.46 instead of 5.32 TB/s at config 4)
+static_assert(kLag <= kStages - 2, "a producer hands a stage over one stage before it needs the slot again");
 constexpr int kTileM = 128;
 constexpr int kKC = 256;           // K values per stage (128 bytes of a row)
 constexpr int kTerms = 4;
@@ -80,9 +86,10 @@ constexpr int kSf0 = 2 * kAccCols;
 constexpr int kTmemCols = 256;
 static_assert(kSf0 + 2 * kSfCols <= kTmemCols, "TMEM");
 
-struct Chunk {
-  int32_t expert, p0, nn, pad;
-};
+// A chunk = the grouping kernel's slice of one expert's routed pairs
+// (VExp: expert, first pair, count <= 8).
+using Chunk = VExp;
+static_assert(kNTok == ::ffn::kNTok, "a slice holds at most kNTok pairs");
 
 struct GemmArgs {
   const ffn_b200_expert *experts;
@@ -245,14 +252,14 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
       const Chunk ch = a.chunks[tile / rb_count];
       // this lane's B row n = lane: token i = n / 4, term t = n % 4
       const int i = lane >> 2, t = lane & 3;
-      const bool have = i < ch.nn;
+      const bool have = i < ch.count;
       const uint8_t *cb = nullptr, *sbp = nullptr;
       if (have) {
-        const int xr = a.pair_tok ? __ldg(a.pair_tok + ch.p0 + i) : ch.p0 + i;
+        const int xr = a.pair_tok ? __ldg(a.pair_tok + ch.offset + i) : ch.offset + i;
         cb = a.qc + ((size_t)xr * kTerms + t) * cld;
         sbp = a.qs + ((size_t)xr * kTerms + t) * qsld;
       }
-      const int nrows = kTerms * ch.nn;
+      const int nrows = kTerms * ch.count;
       for (int kt = 0; kt < KT; ++kt, ++it) {
         const int s = it % kStages;
         if (!__all_sync(0xffffffffu, tc::bar_wait(&empty[s], ((it / kStages) & 1) ^ 1, a.err))) {
@@ -288,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
       bool live = true;
       for (int tile = blockIdx.x; tile < n_tiles && live; tile += gridDim.x, ++tcount) {
         const Chunk ch = a.chunks[tile / rb_count];
-        const int N = (kTerms * ch.nn + 7) & ~7;
+        const int N = (kTerms * ch.count + 7) & ~7;
         const uint32_t id = tc::idesc_nvf4(kTileM, N);
         const int b = tcount & 1, use = tcount >> 1;
         if (!tc::bar_wait(&acc_empty[b], (use & 1) ^ 1, a.err)) break;
@@ -337,8 +344,8 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
       float csl = 0.f;
       {
         const int i = lane >> 2, t = lane & 3;
-        if (i < ch.nn) {
-          const int xr = a.pair_tok ? __ldg(a.pair_tok + ch.p0 + i) : ch.p0 + i;
+        if (i < ch.count) {
+          const int xr = a.pair_tok ? __ldg(a.pair_tok + ch.offset + i) : ch.offset + i;
           csl = pow2f(__ldg(a.qe + (size_t)xr * kTerms + t));
         }
       }
@@ -354,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
       const int r = 32 * q + lane;
 #pragma unroll
       for (int i = 0; i < kNTok; ++i) {
-        if (i >= ch.nn) break;
+        if (i >= ch.count) break;
         float d0 = 0.f, d1 = 0.f;
 #pragma unroll
         for (int t = kTerms - 1; t >= 0; --t) {  // smallest term first
@@ -362,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
           d0 += __uint_as_float(v0[kTerms * i + t]) * c;
           d1 += __uint_as_float(v1[kTerms * i + t]) * c;
         }
-        float *o = a.out + (size_t)(ch.p0 + i) * a.ld_out + row0 + r;
+        float *o = a.out + (size_t)(ch.offset + i) * a.ld_out + row0 + r;
         if (PH == 1) {
           *o = silu10(d0 * gs0) * clamp10(d1 * gs1);
         } else {
@@ -385,8 +392,6 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
 }
 
 // ---------------------------------------------------------------- quantiser
-constexpr int kQThreads = 256;
-constexpr int kQMaxB = 4;  // 16-value blocks per thread: K <= 256 * 16 * 4
 
 // Smallest UE4M3 code whose value is >= s (s >= 0), at most 448 (0x7E).
 __device__ __forceinline__ uint32_t ue4m3_ceil(float s) {
@@ -428,144 +433,89 @@ __device__ __forceinline__ float e2m1_value(uint32_t c) {
   return (c & 8u) ? -a : a;
 }
 
+// Quantise one 16-value block v of the remainder for term scale 2^e (inv =
+// 2^-e, sc = 2^e): block scale = UE4M3 ceiling of max|v| 2^-e / 6, codes =
+// E2M1(v 2^-e * (1/s)) with the correctly rounded reciprocal; v becomes the
+// new remainder v - 2^e s q.  Writes the 8 code bytes and returns the scale.
+__device__ __forceinline__ uint32_t quant_block(float (&v)[16], float inv, float sc, uint2 &codes) {
+  float bm = 0.f;
+#pragma unroll
+  for (int u = 0; u < 16; ++u) bm = fmaxf(bm, fabsf(v[u]));
+  const uint32_t code = ue4m3_ceil(__fdiv_rn(bm * inv, 6.0f));
+  codes = make_uint2(0u, 0u);
+  if (!code) return 0u;
+  const float sv = ue4m3_value(code), rcp = __frcp_rn(sv);
+  float qv[16];
+#pragma unroll
+  for (int u = 0; u < 16; ++u) qv[u] = __fmul_rn(__fmul_rn(v[u], inv), rcp);
+  codes.x = e2m1x8(qv);
+  codes.y = e2m1x8(qv + 8);
+  // remainder: the codes' values (exact, from the code words' nibbles) times s 2^e
+  const float ss = sv * sc;
+#pragma unroll
+  for (int u = 0; u < 16; ++u) v[u] -= e2m1_value(((u < 8 ? codes.x : codes.y) >> (4 * (u & 7))) & 15u) * ss;
+  return code;
+}
+
+// Term exponent from the remainder's max: E = floor(log2 m) - 8 (the largest
+// block scale stays below 512/6), 0 for a zero remainder.
+__device__ __forceinline__ int term_exp(float m) {
+  if (!(m > 0.f) || !isfinite(m)) return 0;
+  int ex;
+  frexpf(m, &ex);  // m = f 2^ex, f in [0.5, 1)
+  return max(-110, min(110, ex - 1 - 8));
+}
+
 // x row (f32, K values) -> 4 NVFP4 terms.  Term t: E_t = floor(log2 max|r_t|)
-// - 8 over the row's remainder r_t (so the largest block scale is below 512/6),
-// per 16-value block the scale s = UE4M3 ceiling of max|r_t| 2^-E_t / 6 and
-// codes q = E2M1(r_t 2^-E_t / s); r_{t+1} = r_t - 2^E_t s q.  A zero remainder
-// gives E_t = 0 and zero codes.
-__global__ void __launch_bounds__(kQThreads) q4_kernel(const float *__restrict__ x, int ld_x, int K,
-                                                       uint8_t *qc, uint8_t *qs, int *qe) {
+// - 8 over the row's remainder r_t, then every 16-value block quantised by
+// quant_block.  A zero remainder gives E_t = 0 and zero codes.
+// One CTA per row and one thread per 16-value block (blockDim = K / 16 rounded
+// up to a warp): each term costs one CTA-wide maximum (warp shuffles, then
+// the warps' maxima through shared memory) and one block quantisation per
+// thread, so a row's four terms are four short dependent steps.
+__global__ void __launch_bounds__(1024) q4_kernel(const float *__restrict__ x, int ld_x, int K,
+                                                  uint8_t *qc, uint8_t *qs, int *qe) {
   pdl_enter();
-  const int row = blockIdx.x, tid = threadIdx.x;
-  const int nb = K / 16;
-  const float *xr = x + (size_t)row * ld_x;
-  __shared__ float red[kQThreads / 32];
-  __shared__ int s_e;
-  float v[kQMaxB][16];
+  const int row = blockIdx.x, blk = threadIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nb = K / 16, nw = (int)(blockDim.x >> 5);
+  const bool mine = blk < nb;
+  __shared__ float red[2][32];  // warps' maxima, double-buffered by term parity
+  float v[16];
 #pragma unroll
-  for (int j = 0; j < kQMaxB; ++j) {
-    const int blk = tid + kQThreads * j;
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const float4 f = blk < nb ? __ldg(reinterpret_cast<const float4 *>(xr + 16 * blk) + u)
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
-      v[j][4 * u] = f.x; v[j][4 * u + 1] = f.y; v[j][4 * u + 2] = f.z; v[j][4 * u + 3] = f.w;
-    }
+  for (int u = 0; u < 4; ++u) {
+    const float4 f = mine ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)row * ld_x + 16 * blk) + u)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+    v[4 * u] = f.x; v[4 * u + 1] = f.y; v[4 * u + 2] = f.z; v[4 * u + 3] = f.w;
   }
+#pragma unroll 1
   for (int t = 0; t < kTerms; ++t) {
     float am = 0.f;
 #pragma unroll
-    for (int j = 0; j < kQMaxB; ++j)
-#pragma unroll
-      for (int u = 0; u < 16; ++u) am = fmaxf(am, fabsf(v[j][u]));
+    for (int u = 0; u < 16; ++u) am = fmaxf(am, fabsf(v[u]));
     for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    if ((tid & 31) == 0) red[tid >> 5] = am;
-    __syncthreads();
-    if (tid == 0) {
-      float m = 0.f;
-      for (int w = 0; w < kQThreads / 32; ++w) m = fmaxf(m, red[w]);
-      int e = 0;
-      if (m > 0.f && isfinite(m)) {
-        int ex;
-        frexpf(m, &ex);  // m = f 2^ex, f in [0.5, 1)
-        e = max(-110, min(110, ex - 1 - 8));
-      }
-      s_e = e;
-      qe[(size_t)row * kTerms + t] = e;
+    if (lane == 0) red[t & 1][wid] = am;
+    __syncthreads();  // (the other buffer was last read before the previous term's barrier)
+    float m = lane < nw ? red[t & 1][lane] : 0.f;
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const int e = term_exp(m);
+    if (threadIdx.x == 0) qe[(size_t)row * kTerms + t] = e;
+    if (mine) {
+      uint2 cw;
+      const uint32_t code = quant_block(v, pow2f(-e), pow2f(e), cw);
+      *reinterpret_cast<uint2 *>(qc + ((size_t)row * kTerms + t) * (K / 2) + 8 * blk) = cw;
+      qs[((size_t)row * kTerms + t) * (K / 16) + blk] = (uint8_t)code;
     }
-    __syncthreads();
-    const int e = s_e;
-    const float inv = pow2f(-e), sc = pow2f(e);
-    uint8_t *cr = qc + ((size_t)row * kTerms + t) * (K / 2);
-    uint8_t *sr = qs + ((size_t)row * kTerms + t) * (K / 16);
-#pragma unroll
-    for (int j = 0; j < kQMaxB; ++j) {
-      const int blk = tid + kQThreads * j;
-      if (blk >= nb) continue;
-      float bm = 0.f;
-#pragma unroll
-      for (int u = 0; u < 16; ++u) bm = fmaxf(bm, fabsf(v[j][u]));
-      const uint32_t code = ue4m3_ceil(__fdiv_rn(bm * inv, 6.0f));
-      const float sv = ue4m3_value(code);
-      uint32_t w[2] = {0u, 0u};
-      if (code) {
-        float qv[16];
-#pragma unroll
-        for (int u = 0; u < 16; ++u) qv[u] = __fdiv_rn(v[j][u] * inv, sv);
-        w[0] = e2m1x8(qv);
-        w[1] = e2m1x8(qv + 8);
-        // remainder: the codes' values (exact) times s 2^E
-        const float ss = sv * sc;
-#pragma unroll
-        for (int u = 0; u < 16; ++u) v[j][u] -= e2m1_value((w[u >> 3] >> (4 * (u & 7))) & 15u) * ss;
-      }
-      *reinterpret_cast<uint2 *>(cr + 8 * blk) = make_uint2(w[0], w[1]);
-      sr[blk] = (uint8_t)code;
-    }
-    __syncthreads();  // red / s_e reused by the next term
   }
-}
-
-// Chunks of <= kNTok pairs per local expert, balanced inside an expert.
-__global__ void __launch_bounds__(1024) f4_chunk_kernel(const int *__restrict__ counts,
-                                                        const int *__restrict__ offsets, int e_begin,
-                                                        int e_end, Chunk *chunks, int *n_chunks) {
-  pdl_enter();
-  __shared__ int warp_sum[32];
-  __shared__ int s_base;
-  if (threadIdx.x == 0) s_base = 0;
-  __syncthreads();
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  for (int e0 = e_begin; e0 < e_end; e0 += blockDim.x) {
-    const int e = e0 + threadIdx.x;
-    const int c = e < e_end ? counts[e] : 0;
-    const int nch = (c + kNTok - 1) / kNTok;
-    int inc = nch;
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, inc, o);
-      if (lane >= o) inc += v;
-    }
-    if (lane == 31) warp_sum[wid] = inc;
-    __syncthreads();
-    if (wid == 0) {
-      int v = lane < (int)(blockDim.x >> 5) ? warp_sum[lane] : 0;
-      for (int o = 1; o < 32; o <<= 1) {
-        const int u = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += u;
-      }
-      warp_sum[lane] = v;
-    }
-    __syncthreads();
-    const int base = s_base + (wid ? warp_sum[wid - 1] : 0) + inc - nch;
-    if (nch) {
-      const int per = (c + nch - 1) / nch;
-      for (int j = 0; j < nch; ++j) {
-        Chunk ch;
-        ch.expert = e;
-        ch.p0 = offsets[e] + j * per;
-        ch.nn = min(per, c - j * per);
-        ch.pad = 0;
-        chunks[base + j] = ch;
-      }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) s_base += warp_sum[(blockDim.x >> 5) - 1];
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) *n_chunks = s_base;
 }
 
 }  // namespace f4
 
-size_t fp4_chunk_bytes(int n_pairs, int n_local) {
-  return (size_t)(n_pairs / f4::kNTok + n_local + 1) * sizeof(f4::Chunk) + 64;
-}
-
 int launch_q4(const float *x, int ld_x, int rows, int K, uint8_t *qc, uint8_t *qs, int *qe, cudaStream_t st) {
   if (rows <= 0) return 0;
-  if (K % 256 || K > f4::kQThreads * 16 * f4::kQMaxB || ld_x % 4 || (reinterpret_cast<uintptr_t>(x) & 15))
+  if (K % 256 || K > 16384 || ld_x % 4 || (reinterpret_cast<uintptr_t>(x) & 15))
     return fail(FFN_B200_EUNSUP, "q4: K must be a multiple of 256 up to 16384, rows 16-byte aligned");
-  FFN_LAUNCH_PDL(FFN_B200_K_QUANT, st, "q4_kernel", f4::q4_kernel, rows, f4::kQThreads, 0, x, ld_x, K, qc, qs, qe);
+  const int threads = (K / 16 + 31) / 32 * 32;  // one thread per 16-value block
+  FFN_LAUNCH_PDL(FFN_B200_K_QUANT, st, "q4_kernel", f4::q4_kernel, rows, threads, 0, x, ld_x, K, qc, qs, qe);
   return 0;
 }
 
@@ -582,11 +532,9 @@ int launch_fp4_moe(const Fp4Args &g, cudaStream_t st) {
   }
   const int H = g.hidden, I = g.inter, T = g.n_tok, P = g.n_pairs;
   const int e_loc = g.e_end - g.e_begin;
-  Chunk *chunks = reinterpret_cast<Chunk *>(g.chunk_ws);
-  int *n_chunks = reinterpret_cast<int *>(g.chunk_ws + fp4_chunk_bytes(P, e_loc) - 64);
+  const Chunk *chunks = g.slices;
+  const int *n_chunks = g.n_slices;
   FFN_CUDA_TRY(cudaMemsetAsync(g.err, 0, sizeof(int), st));
-  FFN_LAUNCH_PDL(FFN_B200_K_GROUP, st, "f4_chunk_kernel", f4_chunk_kernel, 1, 1024, 0, g.counts, g.offsets,
-                 g.e_begin, g.e_end, chunks, n_chunks);
   int rc = launch_q4(g.x, H, T, H, g.xq, g.xs, g.xqe, st);
   if (rc) return rc;
   const int sms = sm_count_of(dev);

@@ -44,13 +44,18 @@ class EpStack:
     all-reduce (residual added by rank 0) or, given `exchange` (an
     ffn_b200.EpExchange), the library's NVLink peer exchange, which reads every
     rank's partial from the exchange's shared `part` buffer and adds the
-    residual itself.  Every rank issues the same collectives in the same order."""
+    residual itself; with fused=True each layer callable runs the layer and
+    the exchange in one library call.  Every rank issues the same collectives
+    in the same order."""
 
     def __init__(self, layers: Sequence[LayerFn], rank: int, world: int, group=None,
-                 exchange=None):
+                 exchange=None, fused: bool = False):
         self.layers = list(layers)
         self.rank, self.world, self.group = rank, world, group
         self.exchange = exchange if world > 1 else None
+        # fused: a layer callable runs the whole layer, exchange included
+        # (ffn_b200.MoeLayer.forward_ep), given (x_in, out, residual=x_in)
+        self.fused = fused and self.exchange is not None
 
     def forward(self, x, buf_a, buf_b, on_layer: Optional[Callable[[int], None]] = None):
         """Runs every layer on x (not modified); buf_a / buf_b are ping-pong
@@ -58,7 +63,9 @@ class EpStack:
         cur = x
         for i, layer in enumerate(self.layers):
             nxt = buf_a if cur is not buf_a else buf_b
-            if self.exchange is not None:
+            if self.fused:
+                layer(cur, nxt, cur)
+            elif self.exchange is not None:
                 layer(cur, self.exchange.part, None)
                 self.exchange.allreduce(cur.shape[0], cur, nxt)
             else:

@@ -43,7 +43,7 @@ EXPORTS = [
     "ffn_b200_st_open", "ffn_b200_st_close", "ffn_b200_st_count", "ffn_b200_st_name",
     "ffn_b200_st_find", "ffn_b200_st_expert_bytes", "ffn_b200_st_load_expert",
     "ffn_b200_compress_ws_bytes", "ffn_b200_compress_ternary_b64",
-    "ffn_b200_quantize_nvfp4x4",
+    "ffn_b200_quantize_nvfp4x4", "ffn_b200_ep_moe_layer", "ffn_b200_set_host_cache_budget",
 ]
 
 # Kernel kinds of ffn_b200_profile_read (FFN_B200_K_*).
@@ -162,6 +162,7 @@ def lib() -> C.CDLL:
         L.ffn_b200_dequant_ternary.argtypes = [sz, sz, vp, vp, vp]
         L.ffn_b200_set_batch_input.argtypes = [vp, sz, sz]
         L.ffn_b200_host_cache_bytes.restype = sz
+        L.ffn_b200_set_host_cache_budget.argtypes = [sz]
         L.merkaba_hardware_addon_v1.restype = vp
         L.ffn_b200_profile_enable.argtypes = [i32]
         L.ffn_b200_profile_kinds.argtypes = [C.c_uint32]
@@ -171,6 +172,7 @@ def lib() -> C.CDLL:
         L.ffn_b200_ep_part.argtypes = [vp]
         L.ffn_b200_ep_part.restype = vp
         L.ffn_b200_ep_allreduce.argtypes = [vp, sz, vp, vp, vp]
+        L.ffn_b200_ep_moe_layer.argtypes = [vp, C.POINTER(MoeDesc), sz, vp, vp, vp, vp, vp, vp, sz, vp]
         L.ffn_b200_ep_error.argtypes = [vp, C.POINTER(C.c_int)]
         L.ffn_b200_ep_destroy.argtypes = [vp]
         L.ffn_b200_profile_read.argtypes = [i32, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]
@@ -690,6 +692,17 @@ class MoeLayer:
 
     def ws_bytes(self, n_tok: int) -> int:
         return int(lib().ffn_b200_moe_ws_bytes(C.byref(self.desc), n_tok))
+
+    def forward_ep(self, exchange, x, out, residual=None, topk_idx=None, topk_w=None, stream=None):
+        """This rank's experts (expert_range) with the expert-parallel exchange
+        fused in: out = residual + the layer over every rank's experts."""
+        x = x.contiguous()
+        n_tok = x.numel() // self.hidden
+        ws = self.ws.get(self.ws_bytes(n_tok))
+        check(lib().ffn_b200_ep_moe_layer(exchange.ep, C.byref(self.desc), n_tok, _ptr(x), _ptr(residual),
+                                          _ptr(out), _ptr(topk_idx), _ptr(topk_w), _ptr(ws), ws.numel(),
+                                          _stream(stream)), "ep_moe_layer")
+        return out
 
     def forward(self, x, out=None, residual=None, topk_idx=None, topk_w=None, stream=None):
         torch = _torch()

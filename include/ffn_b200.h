@@ -294,14 +294,18 @@ FFN_B200_EXPORT int ffn_b200_profile_read(int kind, double *total_ms, uint64_t *
  * No reference counterpart (the reference runs on one GB10).  One process per
  * GPU; rank r's MoE layer (expert range r) writes its partial output into
  * ffn_b200_ep_part(ep) with residual = NULL, then ffn_b200_ep_allreduce writes
- * out = residual + sum over ranks of the parts on every rank: a two-shot
- * exchange over peer memory in one cooperative kernel (bounded waits; on a
- * timed-out wait it writes NaN over out and sets the flag ffn_b200_ep_error
- * reads).  Set-up: every rank calls ffn_b200_ep_create (allocates its shared
- * buffers and writes its IPC handle, ffn_b200_ep_handle_bytes() bytes), the
- * handles are exchanged out of band (e.g. torch.distributed all_gather), then
- * ffn_b200_ep_connect(ep, handles of all ranks in rank order).  Every rank must
- * call ffn_b200_ep_allreduce the same number of times. */
+ * out = residual + sum over ranks of the parts on every rank (or
+ * ffn_b200_ep_moe_layer does both in one go).  One cooperative kernel per GPU:
+ * each rank pushes its partial rows to the rank that owns their slice of tokens,
+ * the owner sums the slice in rank order and pushes the result rows to every
+ * rank, all by plain stores to peer memory with arrival counters (bounded
+ * waits on local memory; on a timed-out wait it writes NaN over out and sets the
+ * flag ffn_b200_ep_error reads).  Set-up: every rank calls ffn_b200_ep_create
+ * (allocates its shared buffers and writes its IPC handle,
+ * ffn_b200_ep_handle_bytes() bytes), the handles are exchanged out of band
+ * (e.g. torch.distributed all_gather), then ffn_b200_ep_connect(ep, handles of
+ * all ranks in rank order).  Every rank must make the same exchange calls in
+ * the same order. */
 typedef struct ffn_b200_ep ffn_b200_ep;
 FFN_B200_EXPORT size_t ffn_b200_ep_handle_bytes(void);
 FFN_B200_EXPORT int ffn_b200_ep_create(int rank, int world, size_t max_tokens, size_t hidden,
@@ -310,6 +314,17 @@ FFN_B200_EXPORT int ffn_b200_ep_connect(ffn_b200_ep *ep, const void *all_handles
 FFN_B200_EXPORT float *ffn_b200_ep_part(ffn_b200_ep *ep);
 FFN_B200_EXPORT int ffn_b200_ep_allreduce(ffn_b200_ep *ep, size_t n_tok, const float *residual,
                                           float *out, void *stream);
+/* The MoE layer of this rank's experts (d->expert_begin .. d->expert_end) with
+ * the exchange fused in: routing for all tokens, this rank's experts, then one
+ * exchange kernel that combines this rank's routes per token and pushes them
+ * through the exchange, so out = residual + the layer over every rank's
+ * experts on every rank (no reference counterpart: the reference runs on one
+ * GB10).  It counts as one ffn_b200_ep_allreduce call for the every-rank-the-
+ * same-calls rule. */
+FFN_B200_EXPORT int ffn_b200_ep_moe_layer(ffn_b200_ep *ep, const ffn_b200_moe_desc *d, size_t n_tok,
+                                          const float *x, const float *residual, float *out,
+                                          int32_t *topk_idx, float *topk_w, void *ws, size_t ws_bytes,
+                                          void *stream);
 FFN_B200_EXPORT int ffn_b200_ep_error(ffn_b200_ep *ep, int *flag);
 FFN_B200_EXPORT int ffn_b200_ep_destroy(ffn_b200_ep *ep);
 
@@ -378,6 +393,12 @@ FFN_B200_EXPORT int ffn_b200_set_batch_input(const float *x_all_host, size_t x_t
 FFN_B200_EXPORT int ffn_b200_release_host_ranges(void);
 /* Bytes of HBM currently held for host-pointer weight copies. */
 FFN_B200_EXPORT size_t ffn_b200_host_cache_bytes(void);
+/* HBM budget of those copies (no reference counterpart: GB10 memory is unified).
+ * 0 (the default): as much as the GPU gives.  Past the budget, or when an
+ * allocation fails, the least recently used copies are freed (first-use copies
+ * before registered ranges, never one the current call uses) and copied again
+ * when a later call needs them. */
+FFN_B200_EXPORT int ffn_b200_set_host_cache_budget(size_t bytes);
 
 #ifdef __cplusplus
 }

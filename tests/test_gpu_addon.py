@@ -158,6 +158,38 @@ def test_abandoned_sequence_is_never_written_back(oracle, ffn, cuda, L):
     oracle.assert_close(new, ref, rel=1e-4, what="the next batched layer")
 
 
+def test_hbm_budget_evicts_and_copies_again(oracle, ffn, cuda, L):
+    """A model larger than the HBM the weight copies may use (the reference's
+    404 GB checkpoint on a 180 GB GPU): with a budget of three experts'
+    weights, calls cycling through eight experts evict the least recently used
+    copies and copy them again.  Every call succeeds (a false return would send
+    the host to its CPU path), results equal the oracle, the copies stay within
+    the budget, and a queued sequence of five experts, whose first copies are
+    evicted while they are still queued, is still right."""
+    H, I = 512, 256
+    es = [nv_expert(oracle, 200 + k, I, H) for k in range(8)]
+    ebytes = 3 * (I * H // 2 + I * H // 16)
+    L.ffn_b200_release_host_ranges()
+    L.ffn_b200_set_host_cache_budget(3 * ebytes)
+    try:
+        x = bench_x(H)
+        for _ in range(2):
+            for k, e in enumerate(es):
+                out = np.zeros(H, dtype=np.float32)
+                assert call(L, e, I, H, x, out, 1.0, False, True)
+                oracle.assert_close(out, e.forward(x), rel=1e-4, what=f"expert {k} under the budget")
+                assert L.ffn_b200_host_cache_bytes() <= 3 * ebytes
+        out = np.zeros(H, dtype=np.float32)
+        seq = []
+        for k, e in enumerate(es[3:8]):
+            assert call(L, e, I, H, x, out, 0.2 + 0.1 * k, k > 0, k == 4)
+            seq.append((e, 0.2 + 0.1 * k, k > 0))
+        oracle.assert_close(out, reference(oracle, seq, x), rel=1e-4, what="queued sequence under the budget")
+    finally:
+        L.ffn_b200_set_host_cache_budget(0)
+        L.ffn_b200_release_host_ranges()
+
+
 def test_calls_with_different_inputs(oracle, ffn, cuda, L):
     """Each queued call keeps its own x (the host may reuse its buffer)."""
     H, I = 512, 256

@@ -6,7 +6,9 @@
    bit-exact, over several calls (epochs, both result buffers).
 2. A two-layer MoE stack run expert-parallel through EpStack with the
    exchange equals the same stack on one GPU with every expert (tolerance of
-   the path: summation order differs)."""
+   the path: summation order differs), and the same stack with the exchange
+   fused into each layer (ffn_b200_ep_moe_layer) equals the unfused one bit
+   for bit."""
 import os
 import socket
 
@@ -88,6 +90,19 @@ def _worker(rank, world, port, q):
         yy, rr = y.cpu().numpy().astype(np.float64), ref.cpu().numpy().astype(np.float64)
         res["max_rel"] = float(np.abs(yy - rr).max() / np.abs(rr).max())
         res["finite"] = bool(np.isfinite(yy).all())
+
+        # the same stack with the exchange fused into each layer (ffn_b200_ep_moe_layer):
+        # the same arithmetic as the part buffer + allreduce path, so equal bit for bit
+        def fn_fused(lay):
+            def run(x_in, o, residual):
+                loc[lay].forward_ep(ex, x_in, o, residual=residual)
+            return run
+
+        fstack = EpStack([fn_fused(lay) for lay in range(L)], rank, world, exchange=ex, fused=True)
+        c, d = torch.empty_like(x), torch.empty_like(x)
+        yf = fstack.forward(x, c, d)
+        torch.cuda.synchronize()
+        res["fused_equal"] = bool(torch.equal(yf, y)) and ex.error() == 0
         ex.close()
     except Exception as e:  # reported to the parent
         res["error"] = repr(e)
@@ -121,3 +136,4 @@ def test_ep_exchange_two_gpus():
         assert "error" not in out[r], out[r]
         assert out[r]["exact"], out[r]
         assert out[r]["finite"] and out[r]["max_rel"] <= 1e-3, out[r]
+        assert out[r]["fused_equal"], out[r]

@@ -71,7 +71,8 @@ def quantize_ref(x):
         code = _ue4m3_ceil((bm / np.float32(6)).astype(np.float32)[..., 0])
         sv = _ue4m3_value(code)[..., None]
         with np.errstate(divide="ignore", invalid="ignore"):
-            q = np.where(sv > 0, (b * inv).astype(np.float32) / sv, 0).astype(np.float32)
+            rcp = (np.float32(1) / sv).astype(np.float32)  # correctly rounded reciprocal
+            q = np.where(sv > 0, ((b * inv).astype(np.float32) * rcp).astype(np.float32), 0).astype(np.float32)
         c = np.where(sv > 0, _e2m1_rne(q), 0).astype(np.uint8)
         val = np.where(c & 8, -_E2M1[c & 7], _E2M1[c & 7]).astype(np.float32)
         r = (b - val * (sv * sc)).astype(np.float32).reshape(rows, K)
@@ -104,7 +105,7 @@ def gpu_quantize(ffn, cuda, x):
     return host(codes), host(scales), host(exps)
 
 
-@pytest.mark.parametrize("K", [256, 2048, 4096])
+@pytest.mark.parametrize("K", [256, 2048, 4096, 7168])
 def test_quantizer_bit_exact_and_accurate(ffn, cuda, K):
     rng = np.random.default_rng(K)
     rows = [rng.standard_normal(K), rng.standard_normal(K) * 1e-6, np.zeros(K),

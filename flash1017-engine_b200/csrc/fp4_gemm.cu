@@ -27,18 +27,20 @@
 // The gemm is persistent (one CTA per SM walks the (chunk, row block) tiles)
 // and warp-specialised (256 threads):
 //   warps 0, 1  A producers: 128 weight rows each, 256 K values (128 bytes) per
-//               stage by cp.async into the 128-byte-swizzled K-major tile; the
-//               rows' 16 scale bytes per stage land in a staging area and are
-//               transposed into the four scale-factor atoms of the stage.
-//   warp 2      B producer: the chunk's 4 x tokens activation rows and scales.
+//               stage by cp.async into the 128-byte-swizzled K-major tile, and
+//               the rows' 16 scale bytes per stage into a staging area; the
+//               copies' completion arrives on the stage's `landed` barrier by
+//               itself, so a producer only ever waits for a free slot.
+//   warp 2      B producer: the chunk's 4 x tokens activation rows and scales;
+//               kLag stages behind, it transposes each landed stage's scales
+//               into the scale-factor atoms and hands the stage over (`full`).
 //   warp 3      TMEM owner; lane 0 copies the stage's scale atoms to TMEM
 //               (tcgen05.cp) and issues the MMAs (M = 128, N = 4 x tokens
 //               rounded to 8, K = 64), committing to the stage and
 //               accumulator barriers.
 //   warps 4-7   epilogue: thread = TMEM lane = output row of the tile.
-// Producers keep kLag cp.async groups in flight beyond the stage they hand
-// over; a stage is handed over (mbarrier arrive) by the producer itself after
-// its copies landed and after fence.proxy.async.  All waits are bounded
+// A stage is handed over by the B warp after its copies landed and its atoms
+// are written (fence.proxy.async, then mbarrier arrive).  All waits are bounded
 // (tcgen05.cuh); a wait that runs out sets the error word, the other roles
 // see it and drain, and the combine kernel writes NaN outputs.
 #include <algorithm>
@@ -55,11 +57,11 @@ constexpr int kStages = 4;
 #ifndef F4_LAG
 #define F4_LAG 2
 #endif
-constexpr int kLag = F4_LAG;       // cp.async groups in flight past the one being handed over
+constexpr int kLag = F4_LAG;       // stages the B warp's issue runs ahead of its hand-overs
 // kLag <= kStages - 2: one stage of slack between the hand-over of stage j and
-// the producer's wait for slot j + kStages (with kLag = kStages - 1 every stage
-// waits for the MMA commit round trip: 3.46 instead of 5.32 TB/s at config 4)
-static_assert(kLag <= kStages - 2, "a producer hands a stage over one stage before it needs the slot again");
+// the B warp's wait for slot j + kStages (with kLag = kStages - 1 every stage
+// waits for the MMA commit round trip)
+static_assert(kLag <= kStages - 2, "the B warp hands a stage over one stage before it needs the slot again");
 constexpr int kTileM = 128;
 constexpr int kKC = 256;           // K values per stage (128 bytes of a row)
 constexpr int kTerms = 4;
@@ -117,7 +119,7 @@ template <int PH>
 __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a) {
   pdl_enter();
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full[kStages], empty[kStages];
+  __shared__ __align__(8) uint64_t landed[kStages], full[kStages], empty[kStages];
   __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], mma_done;
   __shared__ uint32_t s_tmem;
   uint8_t *smem = smem_raw + ((1024 - (tc::sa(smem_raw) & 1023)) & 1023);
@@ -126,7 +128,8 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
-      tc::bar_init(&full[s], 3);  // A0, A1 and B producers
+      tc::bar_init(&landed[s], 96);  // every A and B producer lane's copies (noinc arrivals)
+      tc::bar_init(&full[s], 1);     // the hand-over by the B warp
       tc::bar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -149,37 +152,12 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
 
   if (warp < 2) {
     // ------------------------------------------------------ A producers
+    // Issue a stage's copies and move on: the copies' completion arrives on
+    // landed[s] by itself (cp.async.mbarrier.arrive.noinc), so a producer waits
+    // only for free slots and every free stage can be in flight.
     const int mi = warp;
     int it = 0;
     bool live = true;
-    // hand stage j over: scales staging -> atoms, fence, arrive
-    auto finish = [&](int j) {
-      uint8_t *st = smem + (j % kStages) * STAGE;
-      const uint8_t *stg = st + OFF_SAS + mi * (kTileM * 16);
-      uint4 r[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) r[q] = *reinterpret_cast<const uint4 *>(stg + (lane + 32 * q) * 16);
-      // a byte with the sign bit set or 0x7F is not a UE4M3 scale: flag the
-      // layer (NaN outputs) and hand the tensor core a zero scale instead
-      uint32_t bad = 0;
-      auto clean = [&](uint32_t w) {
-        const uint32_t off = (w & 0x80808080u) | __vcmpeq4(w & 0x7F7F7F7Fu, 0x7F7F7F7Fu);
-        bad |= off;
-        const uint32_t sel = ((off >> 7) & 0x01010101u) * 0xFFu;  // bytes to clear
-        return w & ~sel;
-      };
-#pragma unroll
-      for (int q = 0; q < 4; ++q) r[q] = make_uint4(clean(r[q].x), clean(r[q].y), clean(r[q].z), clean(r[q].w));
-      uint8_t *atoms = st + OFF_SAA + mi * 2048;
-      *reinterpret_cast<uint4 *>(atoms + 0 * 512 + lane * 16) = make_uint4(r[0].x, r[1].x, r[2].x, r[3].x);
-      *reinterpret_cast<uint4 *>(atoms + 1 * 512 + lane * 16) = make_uint4(r[0].y, r[1].y, r[2].y, r[3].y);
-      *reinterpret_cast<uint4 *>(atoms + 2 * 512 + lane * 16) = make_uint4(r[0].z, r[1].z, r[2].z, r[3].z);
-      *reinterpret_cast<uint4 *>(atoms + 3 * 512 + lane * 16) = make_uint4(r[0].w, r[1].w, r[2].w, r[3].w);
-      if (bad) atomicExch(a.err, 2);
-      tc::fence_async_smem();
-      __syncwarp();
-      if (lane == 0) tc::bar_arrive(&full[j % kStages]);
-    };
     for (int tile = blockIdx.x; tile < n_tiles && live; tile += gridDim.x) {
       const Chunk ch = a.chunks[tile / rb_count];
       const int row0 = (tile % rb_count) * ROWS + (PH == 2 ? mi * kTileM : 0);
@@ -218,24 +196,44 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
             for (int u = 0; u < 4; ++u) cp_async4(stg + rr * 16 + 4 * u, src + 4 * u);
           }
         }
-        cp_async_commit();
-        if (it >= kLag) {
-          cp_async_wait<kLag>();
-          __syncwarp();
-          finish(it - kLag);
-        }
+        tc::cp_async_arrive(&landed[s]);
       }
     }
-    cp_async_wait<0>();
-    __syncwarp();
-    if (live)
-      for (int j = max(0, it - kLag); j < it; ++j) finish(j);
   } else if (warp == 2) {
-    // ------------------------------------------------------ B producer
+    // ------------------------------------------------------ B producer + hand-over
+    // Issues the chunk's activation rows; kLag stages behind, once a stage's
+    // copies have all landed, transposes its A and B scales into the
+    // scale-factor atoms, fences the async proxy and hands the stage over.
     int it = 0;
     bool live = true;
-    auto finish = [&](int j) {
-      uint8_t *st = smem + (j % kStages) * STAGE;
+    auto finish = [&](int j) -> bool {
+      const int sj = j % kStages;
+      if (!__all_sync(0xffffffffu, tc::bar_wait(&landed[sj], (j / kStages) & 1, a.err))) return false;
+      uint8_t *st = smem + sj * STAGE;
+      // a byte with the sign bit set or 0x7F is not a UE4M3 scale: flag the
+      // layer (NaN outputs) and hand the tensor core a zero scale instead
+      uint32_t bad = 0;
+      auto clean = [&](uint32_t w) {
+        const uint32_t off = (w & 0x80808080u) | __vcmpeq4(w & 0x7F7F7F7Fu, 0x7F7F7F7Fu);
+        bad |= off;
+        const uint32_t sel = ((off >> 7) & 0x01010101u) * 0xFFu;  // bytes to clear
+        return w & ~sel;
+      };
+#pragma unroll
+      for (int mi = 0; mi < 2; ++mi) {
+        const uint8_t *stg = st + OFF_SAS + mi * (kTileM * 16);
+        uint4 r[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) r[q] = *reinterpret_cast<const uint4 *>(stg + (lane + 32 * q) * 16);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) r[q] = make_uint4(clean(r[q].x), clean(r[q].y), clean(r[q].z), clean(r[q].w));
+        uint8_t *atoms = st + OFF_SAA + mi * 2048;
+        *reinterpret_cast<uint4 *>(atoms + 0 * 512 + lane * 16) = make_uint4(r[0].x, r[1].x, r[2].x, r[3].x);
+        *reinterpret_cast<uint4 *>(atoms + 1 * 512 + lane * 16) = make_uint4(r[0].y, r[1].y, r[2].y, r[3].y);
+        *reinterpret_cast<uint4 *>(atoms + 2 * 512 + lane * 16) = make_uint4(r[0].z, r[1].z, r[2].z, r[3].z);
+        *reinterpret_cast<uint4 *>(atoms + 3 * 512 + lane * 16) = make_uint4(r[0].w, r[1].w, r[2].w, r[3].w);
+      }
+      if (bad) atomicExch(a.err, 2);
       const uint4 r = *reinterpret_cast<const uint4 *>(st + OFF_SBS + lane * 16);  // row = lane (kNMax = 32)
       uint8_t *atoms = st + OFF_SBA;
       *reinterpret_cast<uint4 *>(atoms + 0 * 512 + lane * 16) = make_uint4(r.x, 0u, 0u, 0u);
@@ -244,7 +242,8 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
       *reinterpret_cast<uint4 *>(atoms + 3 * 512 + lane * 16) = make_uint4(r.w, 0u, 0u, 0u);
       tc::fence_async_smem();
       __syncwarp();
-      if (lane == 0) tc::bar_arrive(&full[j % kStages]);
+      if (lane == 0) tc::bar_arrive(&full[sj]);
+      return true;
     };
     static_assert(kNMax == 32, "one B row per lane");
     const size_t cld = (size_t)a.K / 2, qsld = (size_t)a.K / 16;
@@ -276,18 +275,16 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
         }
         if (have) cp_async16(st + OFF_SBS + lane * 16, sbp + (size_t)kt * 16);
         else *reinterpret_cast<uint4 *>(st + OFF_SBS + lane * 16) = make_uint4(0u, 0u, 0u, 0u);
-        cp_async_commit();
-        if (it >= kLag) {
-          cp_async_wait<kLag>();
-          __syncwarp();
-          finish(it - kLag);
+        tc::cp_async_arrive(&landed[s]);
+        if (it >= kLag && !finish(it - kLag)) {
+          live = false;
+          break;
         }
       }
     }
-    cp_async_wait<0>();
-    __syncwarp();
     if (live)
-      for (int j = max(0, it - kLag); j < it; ++j) finish(j);
+      for (int j = max(0, it - kLag); j < it; ++j)
+        if (!finish(j)) break;
   } else if (warp == 3) {
     // ------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -304,6 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
         for (int kt = 0; kt < KT; ++kt, ++it) {
           const int s = it % kStages;
           if (!tc::bar_wait(&full[s], (it / kStages) & 1, a.err)) { live = false; break; }
+          tc::fence_async_smem();  // the producers' cp.async data, for the tensor core's reads
           tc::fence_after();
           const uint8_t *st = smem + s * STAGE;
           const uint32_t sf = tmem + kSf0 + (it & 1) * kSfCols;

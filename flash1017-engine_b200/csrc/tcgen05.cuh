@@ -75,6 +75,11 @@ __device__ __forceinline__ bool bar_wait_drain(uint64_t *b, uint32_t par) {
                  : "=r"(ok) : "r"(sa(b)), "r"(par) : "memory");
   return ok != 0;
 }
+// arrive (without a pending-count increment) on `b` once every cp.async this
+// thread issued so far has landed
+__device__ __forceinline__ void cp_async_arrive(uint64_t *b) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(sa(b)) : "memory");
+}
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }

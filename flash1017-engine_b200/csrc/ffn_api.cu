@@ -1088,19 +1088,31 @@ static int moe_layer_impl(const ffn_b200_moe_desc *d, size_t n_tok, const float 
   const int T = (int)n_tok, P = (int)(n_tok * k);
   int rc;
   const bool exact = d->router_mode == FFN_B200_ROUTER_EXACT;
-  if ((rc = launch_xprep(x, (int)H, T, (int)H, w.xh, w.xl, w.th, w.tl, (int)H, w.xe, st,
-                         d->norm_w, d->norm_eps, exact ? 1 : 0, w.xn)))
-    return rc;
   const float *xin = d->norm_w ? w.xn : x;  // what the router and the experts see
+  const bool grouped =
+      grouped_ok && (d->path == FFN_B200_PATH_GROUPED ||
+                     (d->path == FFN_B200_PATH_AUTO && (size_t)P >= (size_t)FFN_B200_GROUPED_MIN_PAIRS * E));
+  // (AUTO keeps the GEMV slices for an input row that is not 16-byte aligned)
+  const bool fp4 = !grouped && fp4_ok &&
+                   (d->path == FFN_B200_PATH_FP4 ||
+                    (d->path == FFN_B200_PATH_AUTO && (reinterpret_cast<uintptr_t>(xin) & 15) == 0));
+  const bool fused_q = fp4 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(d->norm_w)) & 15) == 0;
+  if (fused_q) {
+    // one pass: RMSNorm, the router's f16 split and the experts' four NVFP4
+    // terms (xn reaches global memory only for the exact router)
+    if ((rc = launch_xprep_q4(x, (int)H, T, (int)H, w.xh, w.xl, (int)H, w.xe, d->norm_w, d->norm_eps,
+                              exact ? 1 : 0, exact && d->norm_w ? w.xn : nullptr, w.xq, w.xs, w.xqe, st)))
+      return rc;
+  } else if ((rc = launch_xprep(x, (int)H, T, (int)H, w.xh, w.xl, w.th, w.tl, (int)H, w.xe, st,
+                                d->norm_w, d->norm_eps, exact ? 1 : 0, w.xn))) {
+    return rc;
+  }
   if ((rc = launch_router(d->router_w, d->router_bias, xin, w.xh, w.xl, w.xe, d->router_mode, T,
                           (int)E, (int)H, (int)k, d->score_fn, w.logits, w.idx, w.wt, st)))
     return rc;
   if ((rc = launch_group(w.idx, T, (int)k, (int)E, d->expert_begin, d->expert_end, d->experts,
                          w.ints, w.pair_tok, w.inv, w.vexp_nv, w.vexp_tn, w.n_vexp, st)))
     return rc;
-  const bool grouped =
-      grouped_ok && (d->path == FFN_B200_PATH_GROUPED ||
-                     (d->path == FFN_B200_PATH_AUTO && (size_t)P >= (size_t)FFN_B200_GROUPED_MIN_PAIRS * E));
   if (grouped) {
     GroupedArgs g{};
     g.experts = d->experts;
@@ -1127,9 +1139,6 @@ static int moe_layer_impl(const ffn_b200_moe_desc *d, size_t n_tok, const float 
       FFN_CUDA_TRY(cudaMemcpyAsync(topk_w, w.wt, P * sizeof(float), cudaMemcpyDeviceToDevice, st));
     return 0;
   }
-  // (AUTO keeps the GEMV slices for an input row that is not 16-byte aligned)
-  const bool fp4 = fp4_ok && (d->path == FFN_B200_PATH_FP4 ||
-                              (d->path == FFN_B200_PATH_AUTO && (reinterpret_cast<uintptr_t>(xin) & 15) == 0));
   if (fp4) {
     Fp4Args g{};
     g.experts = d->experts;
@@ -1142,7 +1151,7 @@ static int moe_layer_impl(const ffn_b200_moe_desc *d, size_t n_tok, const float 
     g.slices = w.vexp_nv;
     g.n_slices = w.n_vexp;
     g.pair_tok = w.pair_tok;
-    g.x = xin;
+    g.x = fused_q ? nullptr : xin;  // nullptr: quantised above
     g.xq = w.xq;
     g.xs = w.xs;
     g.xqe = w.xqe;
@@ -1170,6 +1179,20 @@ int ffn_b200_moe_layer(const ffn_b200_moe_desc *d, size_t n_tok, const float *x,
                        const float *residual, float *out, int32_t *topk_idx, float *topk_w,
                        void *ws, size_t ws_bytes, void *stream) {
   return moe_layer_impl(d, n_tok, x, residual, out, topk_idx, topk_w, ws, ws_bytes, stream, nullptr);
+}
+
+int ffn_b200_topk(size_t n_tok, size_t n_exp, size_t top_k, int32_t score_fn, const float *logits,
+                  size_t n_part, const float *bias, int32_t *idx, float *wt, void *stream) {
+  if (n_tok == 0) return 0;
+  if (!logits || !idx || !wt) return fail(FFN_B200_EINVAL, "topk: null pointer");
+  if (n_exp == 0 || n_exp > 4096 || top_k == 0 || top_k > (size_t)kTopKMax || top_k > n_exp)
+    return fail(FFN_B200_EINVAL, "topk: n_exp must be in 1..4096 and top_k in 1..min(16, n_exp)");
+  if (n_part == 0 || n_part > (size_t)kRouterPlanes) return fail(FFN_B200_EINVAL, "topk: n_part must be 1..3");
+  if (n_tok > (1u << 24)) return fail(FFN_B200_EINVAL, "topk: too many tokens");
+  if (score_fn != FFN_B200_SCORE_REF_SQRTSOFTPLUS && score_fn != FFN_B200_SCORE_SIGMOID)
+    return fail(FFN_B200_EINVAL, "topk: unknown score_fn");
+  return launch_topk(logits, (int)n_part, bias, (int)n_tok, (int)n_exp, (int)top_k, score_fn, idx, wt,
+                     (cudaStream_t)stream);
 }
 
 int ffn_b200_ep_moe_layer(ffn_b200_ep *ep, const ffn_b200_moe_desc *d, size_t n_tok, const float *x,

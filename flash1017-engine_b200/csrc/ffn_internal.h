@@ -66,7 +66,8 @@ struct Fp4Args {
   const VExp *slices;           // the grouping kernel's NVFP4 slices (<= 8 pairs of one expert)
   const int *n_slices;          // their count (device)
   const int32_t *pair_tok;
-  const float *x;               // [n_tok][hidden] f32, the layer input the experts see
+  const float *x;               // [n_tok][hidden] f32, the layer input the experts see, or
+                                // nullptr when xq/xs/xqe already hold its terms (launch_xprep_q4)
   uint8_t *xq, *xs;             // x as 4 NVFP4 terms: codes [tok][4][hidden/2], scales [tok][4][hidden/16]
   int *xqe;                     // [tok][4] exponents
   float *h;                     // [pair][inter] f32
@@ -78,6 +79,11 @@ struct Fp4Args {
 int launch_fp4_moe(const Fp4Args &g, cudaStream_t st);
 // rows of f32 (K % 256 == 0, K <= 16384, 16-byte aligned rows) -> 4 NVFP4 terms
 int launch_q4(const float *x, int ld_x, int rows, int K, uint8_t *qc, uint8_t *qs, int *qe, cudaStream_t st);
+// launch_xprep's natural-order output (RMSNorm, f16 hi/lo split, exponents;
+// xn only when non-null) and launch_q4 of the normalised rows, in one kernel
+int launch_xprep_q4(const float *x, int ld_x, int rows, int K, __half *nh, __half *nl, int ld_o, int *xe,
+                    const float *norm_w, float norm_eps, int seq_norm, float *xn, uint8_t *qc,
+                    uint8_t *qs, int *qe, cudaStream_t st);
 
 // The MoE layer's per-pair expert outputs, combined per token inside the
 // expert-parallel exchange (the fused form of launch_combine).
@@ -174,6 +180,10 @@ int launch_router(const float *w, const float *bias, const float *x, const __hal
                   int top_k, int score_fn, float *logits /* 4 planes of n_tok x n_exp */,
                   int32_t *idx, float *wt,
                   cudaStream_t st);
+// top_k per token from n_part partial logit planes [n_part][n_tok][n_exp] (added in plane order)
+int launch_topk(const float *logits, int n_part, const float *bias, int n_tok, int n_exp, int top_k,
+                int score_fn, int32_t *idx, float *wt, cudaStream_t st);
+constexpr int kRouterPlanes = 3;  // partial logit planes the tensor router writes at most
 int launch_group(const int32_t *idx, int n_tok, int top_k, int n_exp, int e_begin, int e_end,
                  const ffn_b200_expert *experts, int *ws_int, int32_t *pair_tok, int32_t *inv,
                  VExp *vexp_nv, VExp *vexp_tn, int *n_vexp, cudaStream_t st);

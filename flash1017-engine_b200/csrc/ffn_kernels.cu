@@ -769,7 +769,7 @@ int launch_exact_matvec(const float *w32, const uint16_t *w16, const float *x, i
 constexpr int kRouterWarps = 8;  // router_tc_kernel runs 256 threads
 // K-ranges of the tensor router (partial logit planes): 12 x 8 x 3 = 288 CTAs of a
 // 256-token, 384-expert layer fit one wave at 2 CTAs per SM
-constexpr int kRouterKSplit = 3;
+constexpr int kRouterKSplit = kRouterPlanes;
 constexpr int kRtStages = 3;
 constexpr int kRtW = 128 * 4 + 64;   // weight row stride (bytes): 576, rows 16 banks apart
 constexpr int kRtX = 128 * 2 + 32;   // token row stride (bytes): 288, rows 8 banks apart
@@ -1020,6 +1020,156 @@ __global__ void __launch_bounds__(64) topk_kernel(const float *__restrict__ logi
   }
 }
 
+// The same selection with four warps per token (up to 512 experts, four per
+// lane), for a shorter dependent chain than topk_kernel's one warp: each warp
+// picks its own top_k in order (biased score desc, index asc) out of its
+// experts e = lane + 32 (w + 4 j), then warp 0 of the token merges the four
+// sorted lists by the same order.  Every member of the token's top_k is in the
+// top_k of its own warp, so the result (set, order, weights) is topk_kernel's.
+// Two tokens per 256-thread CTA.
+constexpr int kTkWarps = 4;   // warps per token
+constexpr int kTkPer = 4;     // experts per lane and warp
+constexpr int kTkMaxExp = 32 * kTkWarps * kTkPer;
+
+// biased score -> a key whose unsigned order is the float order
+__device__ __forceinline__ uint32_t order_key(float b) {
+  const uint32_t u = __float_as_uint(b);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(256) topk4_kernel(const float *__restrict__ logits,
+                                                    const float *__restrict__ bias, int n_tok,
+                                                    int n_exp, int top_k, int score_fn, int n_part,
+                                                    int32_t *idx, float *wt) {
+  pdl_enter();
+  __shared__ uint32_t s_key[2][kTkWarps][kTopKMax];
+  __shared__ int s_idx[2][kTkWarps][kTopKMax];
+  __shared__ float s_sc[2][kTkWarps][kTopKMax];
+  __shared__ int s_n[2][kTkWarps];
+  const int lane = threadIdx.x & 31, w = (threadIdx.x >> 5) & (kTkWarps - 1), g = threadIdx.x >> 7;
+  const int tok = blockIdx.x * 2 + g;
+  const bool live = tok < n_tok;  // (no early return: the CTA meets at a barrier)
+  if (live) {
+    const float *lg = logits + (size_t)tok * n_exp;
+    const size_t plane = (size_t)n_tok * n_exp;
+    float l[kTkPer], bb[kTkPer];
+#pragma unroll
+    for (int j = 0; j < kTkPer; ++j) {
+      const int e = lane + 32 * (w + kTkWarps * j);
+      l[j] = e < n_exp ? lg[e] : 0.f;
+      bb[j] = e < n_exp && bias ? bias[e] : 0.0f;
+    }
+    // the partial planes added in order, as topk_kernel does
+#pragma unroll
+    for (int z = 1; z < kRouterKSplit; ++z)
+      if (z < n_part) {
+#pragma unroll
+        for (int j = 0; j < kTkPer; ++j) {
+          const int e = lane + 32 * (w + kTkWarps * j);
+          if (e < n_exp) l[j] += lg[z * plane + e];
+        }
+      }
+    float cs[kTkPer];
+    uint32_t ck[kTkPer];
+    uint32_t alive = 0;
+#pragma unroll
+    for (int j = 0; j < kTkPer; ++j) {
+      const int e = lane + 32 * (w + kTkWarps * j);
+      cs[j] = 0.f;
+      ck[j] = 0u;
+      if (e < n_exp) {
+        cs[j] = score_of(l[j], score_fn);
+        const float b = cs[j] + bb[j];
+        ck[j] = order_key(b);
+        if (b == b) alive |= 1u << j;  // NaN is never a candidate
+      }
+    }
+    int n_sel = 0;
+    for (int k = 0; k < top_k; ++k) {
+      // this lane's head: the largest key, the lowest slot (= lowest index) on ties
+      uint32_t hk = 0u;
+      float hs = 0.f;
+      int hj = -1;
+#pragma unroll
+      for (int j = 0; j < kTkPer; ++j)
+        if (((alive >> j) & 1u) && (hj < 0 || ck[j] > hk)) { hk = ck[j]; hs = cs[j]; hj = j; }
+      const uint32_t key = hj < 0 ? 0u : hk;  // non-NaN keys are >= 1
+      const uint32_t kmax = __reduce_max_sync(0xffffffffu, key);
+      const uint32_t cand = (hj >= 0 && key == kmax) ? (uint32_t)(lane + 32 * (w + kTkWarps * hj)) : 0x7fffffffu;
+      const uint32_t bi = __reduce_min_sync(0xffffffffu, cand);
+      if (bi == 0x7fffffffu) break;  // warp-uniform: no candidate left
+      if (lane == (int)(bi & 31u)) {
+        alive &= ~(1u << hj);
+        s_key[g][w][k] = kmax;
+        s_idx[g][w][k] = (int)bi;
+        s_sc[g][w][k] = hs;
+      }
+      n_sel = k + 1;
+    }
+    if (lane == 0) s_n[g][w] = n_sel;
+  }
+  __syncthreads();
+  if (!live || w != 0) return;
+  // merge: candidate slot c = (warp c / top_k, rank c % top_k); lane holds c = lane, lane + 32
+  uint32_t mk[2];
+  int mi[2];
+  float ms[2];
+  uint32_t malive = 0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int c = lane + 32 * h;
+    const int ww = c / top_k, kk = c - ww * top_k;
+    mk[h] = 0u;
+    mi[h] = 0x7fffffff;
+    ms[h] = 0.f;
+    if (ww < kTkWarps && kk < s_n[g][ww]) {
+      mk[h] = s_key[g][ww][kk];
+      mi[h] = s_idx[g][ww][kk];
+      ms[h] = s_sc[g][ww][kk];
+      malive |= 1u << h;
+    }
+  }
+  float my_score = 0.f;
+  int my_idx = 0x7fffffff;
+  for (int k = 0; k < top_k; ++k) {
+    uint32_t hk = 0u;
+    int hi = 0x7fffffff, hh = -1;
+    float hs = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      if (((malive >> h) & 1u) && (hh < 0 || mk[h] > hk || (mk[h] == hk && mi[h] < hi))) {
+        hk = mk[h]; hi = mi[h]; hs = ms[h]; hh = h;
+      }
+    const uint32_t key = hh < 0 ? 0u : hk;
+    const uint32_t kmax = __reduce_max_sync(0xffffffffu, key);
+    const uint32_t cand = (hh >= 0 && key == kmax) ? (uint32_t)hi : 0x7fffffffu;
+    const int bi = (int)__reduce_min_sync(0xffffffffu, cand);
+    const bool won = bi != 0x7fffffff && hh >= 0 && hi == bi && key == kmax;
+    const float bs = __shfl_sync(0xffffffffu, hs, (__ffs(__ballot_sync(0xffffffffu, won)) - 1) & 31);
+    if (lane == k) { my_score = bi == 0x7fffffff ? 0.f : bs; my_idx = bi; }
+    if (won) malive &= ~(1u << hh);
+  }
+  // sum of the selected scores in selection order (flash1017.rs:7370)
+  float sum = 0.f;
+  for (int k = 0; k < top_k; ++k) sum += __shfl_sync(0xffffffffu, my_score, k);
+  const float num = score_fn == FFN_B200_SCORE_REF_SQRTSOFTPLUS ? 1.5f : 1.0f;
+  const float scale = sum > 1e-12f ? num / sum : 0.0f;
+  if (lane < top_k) {
+    idx[(size_t)tok * top_k + lane] = my_idx;
+    wt[(size_t)tok * top_k + lane] = my_score * scale;
+  }
+}
+
+int launch_topk(const float *logits, int n_part, const float *bias, int n_tok, int n_exp, int top_k,
+                int score_fn, int32_t *idx, float *wt, cudaStream_t st) {
+  if (n_exp <= kTkMaxExp) {
+    FFN_LAUNCH_PDL(FFN_B200_K_TOPK, st, "topk4_kernel", topk4_kernel, (n_tok + 1) / 2, 256, 0, logits, bias, n_tok, n_exp, top_k, score_fn, n_part, idx, wt);
+  } else {
+    FFN_LAUNCH_PDL(FFN_B200_K_TOPK, st, "topk_kernel", topk_kernel, (n_tok + 1) / 2, 64, 0, logits, bias, n_tok, n_exp, top_k, score_fn, n_part, idx, wt);
+  }
+  return 0;
+}
+
 int launch_router(const float *w, const float *bias, const float *x, const __half *xh,
                   const __half *xl, const int *xe, int mode, int n_tok, int n_exp, int H,
                   int top_k, int score_fn, float *logits, int32_t *idx, float *wt,
@@ -1042,35 +1192,41 @@ int launch_router(const float *w, const float *bias, const float *x, const __hal
     }
     FFN_LAUNCH_PDL(FFN_B200_K_ROUTER, st, "router_tc_kernel", router_tc_kernel, g1, 256, kRtSmem, w, xh, xl, xe, n_tok, n_exp, H, logits);
   }
-  FFN_LAUNCH_PDL(FFN_B200_K_TOPK, st, "topk_kernel", topk_kernel, (n_tok + 1) / 2, 64, 0, logits, bias, n_tok, n_exp, top_k, score_fn, n_part, idx, wt);
-  return 0;
+  return launch_topk(logits, n_part, bias, n_tok, n_exp, top_k, score_fn, idx, wt, st);
 }
 
 // ============================================================ grouping
 // Token->expert groups (flash1017.rs:8088-8099 builds the same groups by a
 // linear scan).  Single CTA: counts per local expert (shared-memory atomics),
 // exclusive scans, pair placement in pair order, and slices of <= 8 tokens per
-// expert, listed per weight format.
+// expert, listed per weight format.  Shared memory: per-warp counts with a row
+// stride of n_exp + 1 words (a warp reading one expert's 32 counts hits 32
+// banks), then counts, offsets, the experts' formats and slice bases.
 __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__ idx, int n_pairs,
                                                      int top_k, int n_exp, int e_begin, int e_end,
                                                      const ffn_b200_expert *__restrict__ experts,
                                                      int *counts, int *offsets, int *cursor,
                                                      int *vbase, int32_t *pair_tok, int32_t *inv,
                                                      VExp *vexp_nv, VExp *vexp_tn, int *n_vexp) {
-  pdl_enter();
   extern __shared__ int g_smem[];
-  int *s_cnt = g_smem;                   // [32 warps][n_exp]: counts, then bases
-  int *s_counts = g_smem + 32 * n_exp;   // [n_exp] pairs per expert
+  const int sp = n_exp + 1;              // row stride of the per-warp counts
+  int *s_cnt = g_smem;                   // [32 warps][sp]: counts, then bases
+  int *s_counts = g_smem + 32 * sp;      // [n_exp] pairs per expert
   int *s_off = s_counts + n_exp;         // [n_exp] first position of each expert
+  int *s_nv = s_off + n_exp;             // [n_exp] 1: NVFP4 / MXFP4 slice list, 0: ternary
+  int *s_vb = s_nv + n_exp;              // [n_exp] first slice of each expert in its list
   __shared__ int s_tot[2];
   __shared__ int ws_p[32], ws_n[32], ws_t[32];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  // nothing here depends on the previous kernel: runs while it finishes
+  for (int i = tid; i < 32 * sp; i += blockDim.x) s_cnt[i] = 0;
+  for (int e = tid; e < n_exp; e += blockDim.x) s_nv[e] = experts[e].format != FFN_B200_FMT_TERNARY;
+  pdl_enter();
   // Warp w owns the pair range [w * span, (w + 1) * span) and walks it in
   // order, 32 pairs per step; lanes holding the same expert find each other
   // with match.any, the lowest of them updates the warp's count.
   const int span = (n_pairs + 31) / 32;
   const int q_lo = wid * span, q_hi = min(n_pairs, q_lo + span);
-  for (int i = tid; i < 32 * n_exp; i += blockDim.x) s_cnt[i] = 0;
   __syncthreads();
   constexpr int kU = 8;  // steps whose expert ids are loaded together
   for (int q0 = q_lo; q0 < q_hi; q0 += 32 * kU) {
@@ -1086,20 +1242,22 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__
       int e = ev[u];
       if (e < e_begin || e >= e_end) e = -1;
       const unsigned peers = __match_any_sync(0xffffffffu, e);
-      if (e >= 0 && (peers & ((1u << lane) - 1u)) == 0) s_cnt[wid * n_exp + e] += __popc(peers);
+      if (e >= 0 && (peers & ((1u << lane) - 1u)) == 0) s_cnt[wid * sp + e] += __popc(peers);
       __syncwarp();
     }
   }
   __syncthreads();
-  // per expert: warp counts -> exclusive bases in warp order, and the total
-  for (int e = tid; e < n_exp; e += blockDim.x) {
-    int run = 0;
-    for (int w2 = 0; w2 < 32; ++w2) {
-      const int c = s_cnt[w2 * n_exp + e];
-      s_cnt[w2 * n_exp + e] = run;
-      run += c;
+  // per expert (one warp each, lane = counting warp): warp counts -> exclusive
+  // bases in warp order, and the total
+  for (int e = wid; e < n_exp; e += 32) {
+    const int c = s_cnt[lane * sp + e];
+    int inc = c;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int a = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += a;
     }
-    s_counts[e] = run;
+    s_cnt[lane * sp + e] = inc - c;
+    if (lane == 31) s_counts[e] = inc;
   }
   __syncthreads();
   // each thread owns a contiguous run of `per` experts
@@ -1110,7 +1268,7 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__
     if (e < n_exp) {
       const int c = s_counts[e], s = (c + kNTok - 1) / kNTok;
       loc_pairs += c;
-      if (experts[e].format != FFN_B200_FMT_TERNARY) loc_nv += s; else loc_tn += s;
+      if (s_nv[e]) loc_nv += s; else loc_tn += s;
     }
   }
   // block-wide exclusive scans of the three per-thread totals
@@ -1149,8 +1307,10 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__
       offsets[e] = base_p;
       s_off[e] = base_p;
       base_p += c;
-      if (experts[e].format != FFN_B200_FMT_TERNARY) { vbase[e] = base_n; base_n += s; }
-      else { vbase[e] = base_t; base_t += s; }
+      const int vb = s_nv[e] ? base_n : base_t;
+      vbase[e] = vb;
+      s_vb[e] = vb;
+      if (s_nv[e]) base_n += s; else base_t += s;
     }
   }
   __syncthreads();
@@ -1176,28 +1336,28 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__
       const unsigned peers = __match_any_sync(0xffffffffu, e);
       const int rank = __popc(peers & ((1u << lane) - 1u));
       if (mine) {
-        const int pos = s_off[e] + s_cnt[wid * n_exp + e] + rank;
+        const int pos = s_off[e] + s_cnt[wid * sp + e] + rank;
         pair_tok[pos] = q / top_k;
         inv[q] = pos;
       } else if (q < q_hi) {
         inv[q] = -1;
       }
       __syncwarp();
-      if (mine && rank == 0) s_cnt[wid * n_exp + e] += __popc(peers);
+      if (mine && rank == 0) s_cnt[wid * sp + e] += __popc(peers);
       __syncwarp();
     }
   }
   __syncthreads();
   for (int e = tid; e < n_exp; e += blockDim.x) {
     const int c = s_counts[e];
-    VExp *dst = experts[e].format != FFN_B200_FMT_TERNARY ? vexp_nv : vexp_tn;  // NVFP4, MXFP4 | ternary
+    VExp *dst = s_nv[e] ? vexp_nv : vexp_tn;  // NVFP4, MXFP4 | ternary
     for (int j = 0; j * kNTok < c; ++j) {
       VExp v;
       v.expert = e;
-      v.offset = offsets[e] + j * kNTok;
+      v.offset = s_off[e] + j * kNTok;
       v.count = min(kNTok, c - j * kNTok);
       v.pad = 0;
-      dst[vbase[e] + j] = v;
+      dst[s_vb[e] + j] = v;
     }
   }
   if (tid == 0) { n_vexp[0] = s_tot[0]; n_vexp[1] = s_tot[1]; }
@@ -1206,7 +1366,7 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__
 int launch_group(const int32_t *idx, int n_tok, int top_k, int n_exp, int e_begin, int e_end,
                  const ffn_b200_expert *experts, int *ws_int, int32_t *pair_tok, int32_t *inv,
                  VExp *vexp_nv, VExp *vexp_tn, int *n_vexp, cudaStream_t st) {
-  const size_t smem = (size_t)(32 + 2) * n_exp * sizeof(int);
+  const size_t smem = ((size_t)32 * (n_exp + 1) + 4 * (size_t)n_exp) * sizeof(int);
   if (smem > 200 * 1024) return fail(FFN_B200_EUNSUP, "group: too many experts");
   static bool attr_set[64] = {false};
   int dev = 0;

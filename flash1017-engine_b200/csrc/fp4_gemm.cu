@@ -22,6 +22,8 @@
 //   q4_kernel        rows of f32 -> 4 NVFP4 terms (codes [row][t][K/2], scales
 //                    [row][t][K/16], exponents [row][t]); one CTA per row, one
 //                    thread per 16-value block.
+//   xq_kernel        the layer input's RMSNorm and router split (xprep's
+//                    output) and its four terms in one pass.
 //   fp4_gemm_kernel  PH 1: h[p][r] = SwiGLU(gate, up) for 128 rows of W1 and W3;
 //                    PH 2: y[p][r] for 256 rows of W2 (two 128-row blocks).
 // The gemm is persistent (one CTA per SM walks the (chunk, row block) tiles)
@@ -464,27 +466,14 @@ __device__ __forceinline__ int term_exp(float m) {
   return max(-110, min(110, ex - 1 - 8));
 }
 
-// x row (f32, K values) -> 4 NVFP4 terms.  Term t: E_t = floor(log2 max|r_t|)
-// - 8 over the row's remainder r_t, then every 16-value block quantised by
-// quant_block.  A zero remainder gives E_t = 0 and zero codes.
-// One CTA per row and one thread per 16-value block (blockDim = K / 16 rounded
-// up to a warp): each term costs one CTA-wide maximum (warp shuffles, then
-// the warps' maxima through shared memory) and one block quantisation per
-// thread, so a row's four terms are four short dependent steps.
-__global__ void __launch_bounds__(1024) q4_kernel(const float *__restrict__ x, int ld_x, int K,
-                                                  uint8_t *qc, uint8_t *qs, int *qe) {
-  pdl_enter();
-  const int row = blockIdx.x, blk = threadIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int nb = K / 16, nw = (int)(blockDim.x >> 5);
-  const bool mine = blk < nb;
-  __shared__ float red[2][32];  // warps' maxima, double-buffered by term parity
-  float v[16];
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const float4 f = mine ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)row * ld_x + 16 * blk) + u)
-                          : make_float4(0.f, 0.f, 0.f, 0.f);
-    v[4 * u] = f.x; v[4 * u + 1] = f.y; v[4 * u + 2] = f.z; v[4 * u + 3] = f.w;
-  }
+// The four terms of one row, thread = 16-value block `threadIdx.x` holding
+// v (its values; the remainder afterwards).  Term t: one CTA-wide maximum
+// (warp shuffles, then the warps' maxima through red[t & 1]), the exponent,
+// and one block quantisation per thread.  Every thread of the CTA calls it.
+__device__ __forceinline__ void q4_terms(float (&v)[16], bool mine, int row, int K, float (*red)[32],
+                                         uint8_t *qc, uint8_t *qs, int *qe) {
+  const int blk = threadIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nw = (int)(blockDim.x >> 5);
 #pragma unroll 1
   for (int t = 0; t < kTerms; ++t) {
     float am = 0.f;
@@ -506,7 +495,152 @@ __global__ void __launch_bounds__(1024) q4_kernel(const float *__restrict__ x, i
   }
 }
 
+// x row (f32, K values) -> 4 NVFP4 terms.  Term t: E_t = floor(log2 max|r_t|)
+// - 8 over the row's remainder r_t, then every 16-value block quantised by
+// quant_block.  A zero remainder gives E_t = 0 and zero codes.
+// One CTA per row and one thread per 16-value block (blockDim = K / 16 rounded
+// up to a warp): each term costs one CTA-wide maximum (warp shuffles, then
+// the warps' maxima through shared memory) and one block quantisation per
+// thread, so a row's four terms are four short dependent steps.
+__global__ void __launch_bounds__(1024) q4_kernel(const float *__restrict__ x, int ld_x, int K,
+                                                  uint8_t *qc, uint8_t *qs, int *qe) {
+  pdl_enter();
+  const int row = blockIdx.x, blk = threadIdx.x;
+  const bool mine = blk < K / 16;
+  __shared__ float red[2][32];  // warps' maxima, double-buffered by term parity
+  float v[16];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const float4 f = mine ? __ldg(reinterpret_cast<const float4 *>(x + (size_t)row * ld_x + 16 * blk) + u)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+    v[4 * u] = f.x; v[4 * u + 1] = f.y; v[4 * u + 2] = f.z; v[4 * u + 3] = f.w;
+  }
+  q4_terms(v, mine, row, K, red, qc, qs, qe);
+}
+
+// The layer input's preparation and its quantisation in one pass (the FP4
+// path's first kernel): per row, the optional RMSNorm (flash1017.rs:4880-4891;
+// with seq_norm the sum of squares in column order, as xprep does), xn to
+// global only when asked (the exact router reads it), the tensor router's hi/lo
+// f16 split of xn 2^-e (e = floor(log2 max|xn|) - 15, xprep's rule), then the
+// four NVFP4 terms of xn exactly as q4_kernel forms them.  One CTA per row, one
+// thread per 16-value block; the norm weights are read before the wait on the
+// previous kernel.
+__global__ void __launch_bounds__(1024) xq_kernel(const float *__restrict__ x, int ld_x, int K,
+                                                  __half *nh, __half *nl, int ld_o, int *xe,
+                                                  const float *__restrict__ norm_w, float norm_eps,
+                                                  int seq_norm, float *xn, uint8_t *qc, uint8_t *qs,
+                                                  int *qe) {
+  const int row = blockIdx.x, blk = threadIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nb = K / 16, nw = (int)(blockDim.x >> 5);
+  const bool mine = blk < nb;
+  __shared__ float red[2][32];  // term maxima, double-buffered by term parity
+  __shared__ float red_a[32];   // sum of squares, then the split's maximum
+  __shared__ float s_inv;
+  float wv[16];
+  if (norm_w) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float4 f = mine ? __ldg(reinterpret_cast<const float4 *>(norm_w + 16 * blk) + u)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+      wv[4 * u] = f.x; wv[4 * u + 1] = f.y; wv[4 * u + 2] = f.z; wv[4 * u + 3] = f.w;
+    }
+  }
+  pdl_enter();
+  const float *xr = x + (size_t)row * ld_x;
+  float v[16];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const float4 f = mine ? __ldg(reinterpret_cast<const float4 *>(xr + 16 * blk) + u)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+    v[4 * u] = f.x; v[4 * u + 1] = f.y; v[4 * u + 2] = f.z; v[4 * u + 3] = f.w;
+  }
+  if (norm_w) {
+    if (seq_norm) {
+      if (threadIdx.x == 0) {
+        float ss = 0.f;
+        for (int c = 0; c < K; ++c) ss = __fadd_rn(ss, __fmul_rn(xr[c], xr[c]));
+        s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), norm_eps)));
+      }
+    } else {
+      float ss = 0.f;
+#pragma unroll
+      for (int u = 0; u < 16; ++u) ss = fmaf(v[u], v[u], ss);
+      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) red_a[wid] = ss;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int w = 0; w < nw; ++w) t += red_a[w];
+        s_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)K), norm_eps)));
+      }
+    }
+    __syncthreads();
+    const float inv = s_inv;
+#pragma unroll
+    for (int u = 0; u < 16; ++u) v[u] = __fmul_rn(__fmul_rn(v[u], inv), wv[u]);
+    if (xn && mine) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        reinterpret_cast<float4 *>(xn + (size_t)row * K + 16 * blk)[u] =
+            make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+    }
+  }
+  // the tensor router's f16 hi/lo split
+  {
+    float am = 0.f;
+#pragma unroll
+    for (int u = 0; u < 16; ++u) am = fmaxf(am, fabsf(v[u]));
+    for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    __syncthreads();  // (red_a's sums were read before the barrier above)
+    if (lane == 0) red_a[wid] = am;
+    __syncthreads();
+    float m = lane < nw ? red_a[lane] : 0.f;
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    int e = 0;
+    if (m > 0.f && isfinite(m)) {
+      int ex;
+      frexpf(m, &ex);  // m = f 2^ex, f in [0.5, 1)
+      e = max(-100, min(100, ex - 15));
+    }
+    if (threadIdx.x == 0) xe[row] = e;
+    if (mine) {
+      const float sc = pow2f(-e);
+      uint32_t wh[8], wl[8];  // f16 pairs, even column in the low half
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        __half h0, l0, h1, l1;
+        split_f16(v[2 * u] * sc, h0, l0);
+        split_f16(v[2 * u + 1] * sc, h1, l1);
+        wh[u] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+        wl[u] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+      }
+      uint4 *dh = reinterpret_cast<uint4 *>(nh + (size_t)row * ld_o + 16 * blk);
+      uint4 *dl = reinterpret_cast<uint4 *>(nl + (size_t)row * ld_o + 16 * blk);
+      dh[0] = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+      dh[1] = make_uint4(wh[4], wh[5], wh[6], wh[7]);
+      dl[0] = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+      dl[1] = make_uint4(wl[4], wl[5], wl[6], wl[7]);
+    }
+  }
+  q4_terms(v, mine, row, K, red, qc, qs, qe);  // the four NVFP4 terms, as q4_kernel forms them
+}
+
 }  // namespace f4
+
+int launch_xprep_q4(const float *x, int ld_x, int rows, int K, __half *nh, __half *nl, int ld_o, int *xe,
+                    const float *norm_w, float norm_eps, int seq_norm, float *xn, uint8_t *qc,
+                    uint8_t *qs, int *qe, cudaStream_t st) {
+  if (rows <= 0) return 0;
+  if (K % 256 || K > 16384 || ld_x % 4 || ld_o % 8 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (reinterpret_cast<uintptr_t>(norm_w) & 15) || (reinterpret_cast<uintptr_t>(xn) & 15) ||
+      ((reinterpret_cast<uintptr_t>(nh) | reinterpret_cast<uintptr_t>(nl)) & 15))
+    return fail(FFN_B200_EUNSUP, "xprep_q4: K must be a multiple of 256 up to 16384, rows 16-byte aligned");
+  const int threads = (K / 16 + 31) / 32 * 32;
+  FFN_LAUNCH_PDL(FFN_B200_K_XPREP, st, "xq_kernel", f4::xq_kernel, rows, threads, 0, x, ld_x, K, nh, nl, ld_o, xe,
+                 norm_w, norm_eps, seq_norm, xn, qc, qs, qe);
+  return 0;
+}
 
 int launch_q4(const float *x, int ld_x, int rows, int K, uint8_t *qc, uint8_t *qs, int *qe, cudaStream_t st) {
   if (rows <= 0) return 0;
@@ -533,8 +667,8 @@ int launch_fp4_moe(const Fp4Args &g, cudaStream_t st) {
   const Chunk *chunks = g.slices;
   const int *n_chunks = g.n_slices;
   FFN_CUDA_TRY(cudaMemsetAsync(g.err, 0, sizeof(int), st));
-  int rc = launch_q4(g.x, H, T, H, g.xq, g.xs, g.xqe, st);
-  if (rc) return rc;
+  int rc = 0;
+  if (g.x && (rc = launch_q4(g.x, H, T, H, g.xq, g.xs, g.xqe, st))) return rc;  // else quantised already
   const int sms = sm_count_of(dev);
   const long long max_chunks = (long long)P / f4::kNTok + e_loc;
   GemmArgs p{};

@@ -44,6 +44,7 @@ EXPORTS = [
     "ffn_b200_st_find", "ffn_b200_st_expert_bytes", "ffn_b200_st_load_expert",
     "ffn_b200_compress_ws_bytes", "ffn_b200_compress_ternary_b64",
     "ffn_b200_quantize_nvfp4x4", "ffn_b200_ep_moe_layer", "ffn_b200_set_host_cache_budget",
+    "ffn_b200_topk",
 ]
 
 # Kernel kinds of ffn_b200_profile_read (FFN_B200_K_*).
@@ -115,6 +116,7 @@ def lib() -> C.CDLL:
         L.ffn_b200_ternary_matvec.argtypes = [sz, sz, sz, C.POINTER(TnMat), vp, vp, vp, sz, vp]
         L.ffn_b200_mxfp4_matvec.argtypes = [sz, sz, sz, C.POINTER(NvMat), vp, vp, vp, sz, vp]
         L.ffn_b200_quantize_nvfp4x4.argtypes = [sz, sz, vp, sz, vp, vp, vp, vp]
+        L.ffn_b200_topk.argtypes = [sz, sz, sz, C.c_int32, vp, sz, vp, vp, vp, vp]
         L.gx10_rust_mxfp4_matvec.argtypes = [sz, sz, vp, vp, vp, vp]
         L.gx10_rust_mxfp4_matvec.restype = C.c_bool
         L.gx10_rust_mxfp4_mlp_accum.argtypes = [sz, sz, vp, vp, vp, vp, vp, vp, vp, vp, f32,
@@ -649,6 +651,23 @@ def gen_normal(k: int, n: int, stdev: float = 1.0, device="cuda", stream=None):
     check(lib().ffn_b200_gen_normal(k, n, float(stdev), _ptr(out), _stream(stream)),
           "gen_normal")
     return out
+
+
+def topk(logits, top_k, score_fn=SCORE_SIGMOID, bias=None, stream=None):
+    """The MoE layer's top-k step on device logits, [n_tok, n_exp] or partial
+    planes [n_part, n_tok, n_exp] (added in plane order): (idx int32, wt f32),
+    each [n_tok, top_k] (ffn_b200_topk)."""
+    torch = _torch()
+    lg = logits if logits.dim() == 3 else logits.unsqueeze(0)
+    lg = lg.contiguous()
+    n_part, n_tok, n_exp = lg.shape
+    idx = torch.empty(n_tok, top_k, dtype=torch.int32, device=lg.device)
+    wt = torch.empty(n_tok, top_k, dtype=torch.float32, device=lg.device)
+    b = None if bias is None else bias.contiguous()
+    check(lib().ffn_b200_topk(n_tok, n_exp, top_k, int(score_fn), _ptr(lg), n_part,
+                              None if b is None else _ptr(b), _ptr(idx), _ptr(wt), _stream(stream)),
+          "topk")
+    return idx, wt
 
 
 def expert_table(experts, device="cuda"):

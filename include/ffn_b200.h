@@ -228,6 +228,19 @@ FFN_B200_EXPORT int ffn_b200_quantize_nvfp4x4(size_t rows, size_t K, const float
                                               uint8_t *codes, uint8_t *scales, int32_t *exps,
                                               void *stream);
 
+/* The layer's top-k step on precomputed logits (flash1017.rs:7280-7376): per
+ * token, logit = sum of the n_part (1..3) partial planes in plane order
+ * (logits [n_part][n_tok][n_exp], DEVICE), score = score_fn(logit), biased =
+ * score + bias (bias DEVICE [n_exp] or NULL); the top_k by biased score
+ * (desc, lower expert index first on ties; NaN never selected; a round with no
+ * candidate yields index 0x7fffffff, weight 0) in selection order, weights =
+ * score * (1.5 for REF_SQRTSOFTPLUS, 1 for SIGMOID) / (sum of the selected
+ * scores in selection order), 0 when that sum <= 1e-12.  idx, wt DEVICE
+ * [n_tok][top_k]; top_k <= 16. */
+FFN_B200_EXPORT int ffn_b200_topk(size_t n_tok, size_t n_exp, size_t top_k, int32_t score_fn,
+                                  const float *logits, size_t n_part, const float *bias,
+                                  int32_t *idx, float *wt, void *stream);
+
 FFN_B200_EXPORT size_t ffn_b200_moe_ws_bytes(const ffn_b200_moe_desc *d, size_t max_tokens);
 /* x [n_tok, hidden] f32; out [n_tok, hidden] = residual + moe(xn) when
  * residual != NULL, else moe(xn), with xn = x or its RMSNorm (norm_w); residual

@@ -152,6 +152,36 @@ def test_fp4_layer_vs_oracle(oracle, ffn, cuda, E, H, I, T, K):
     oracle.assert_close(out - xs, ref, what=f"fp4 layer E{E} H{H} I{I} T{T}")
 
 
+@pytest.mark.parametrize("mode", ["exact", "tensor"])
+def test_fp4_layer_with_ffn_norm(oracle, ffn, cuda, mode):
+    """The reference's ffn_norm before routing (RMSNorm, flash1017.rs:7637): on
+    the FP4 path the norm, the router's f16 split and the experts' four NVFP4
+    terms come from one kernel (xq_kernel).  With the exact router the norm's
+    sum runs in the reference's order, so the top-6 sets match the oracle's
+    exactly; the tensor router may differ only at near-ties."""
+    import torch
+    E, H, I, T, K = 32, 1024, 512, 16, 6
+    experts, wr, _ = _layer(ffn, E, H, I, 95, ffn.PATH_FP4)
+    nw = (1.0 + 0.1 * ffn.gen_normal(ffn.path_key(95, 0, 1, ffn.TAG_X), H)).contiguous()
+    x = (3.0 * ffn.gen_normal(ffn.path_key(95, 0, 0, ffn.TAG_X), T * H)).view(T, H)
+    rm = ffn.ROUTER_EXACT if mode == "exact" else ffn.ROUTER_TENSOR
+    layer = ffn.MoeLayer(experts, wr, H, I, top_k=K, path=ffn.PATH_FP4, router_mode=rm, norm_w=nw,
+                         norm_eps=1e-20)
+    idx = torch.empty(T, K, dtype=torch.int32, device=cuda)
+    out = host(layer.forward(x, topk_idx=idx, residual=x))
+    oe = [oracle_nvfp4_expert(oracle, e) for e in experts]
+    xs = host(x)
+    ref, ridx, _ = oracle.moe_layer(oe, host(wr), xs, top_k=K, norm_w=host(nw), norm_eps=1e-20)
+    if mode == "exact":
+        assert np.array_equal(host(idx), ridx)
+    else:
+        xn = xs / np.sqrt((xs.astype(np.float64) ** 2).mean(axis=1, keepdims=True)) * host(nw)
+        bs = oracle.biased_sorted(oracle.router_logits(host(wr), xn.astype(np.float32)), K)
+        assert oracle.topk_agrees(host(idx), ridx, bs).all()
+    same = (host(idx) == ridx).all(axis=1)
+    oracle.assert_close((out - xs)[same], ref[same], what=f"fp4 layer with ffn_norm ({mode} router)")
+
+
 def test_fp4_matches_gemv_path_and_is_deterministic(oracle, ffn, cuda):
     E, H, I, T, K = 24, 1024, 512, 48, 6
     experts, wr, make = _layer(ffn, E, H, I, 91, ffn.PATH_FP4)

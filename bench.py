@@ -218,9 +218,10 @@ class CpuSample:
         return 1.0 / (self.a.layers * dt / n), dt, n
 
     def describe(self, dt, n):
-        return (f"oracle C restatement of the reference CPU path, {self.threads} threads: "
-                f"{n} token-layers ({self.N_TOK} tokens x {self.n_lay} layers, repeated) in "
-                f"{dt:.1f} s, scaled to the {self.a.layers}-layer stack")
+        return (f"oracle C restatement of the reference CPU path, {self.threads} threads, per-token "
+                f"decode order (flash1017.rs:7259-7567): {n} token-layers ({self.N_TOK} tokens x "
+                f"{self.n_lay} layers, repeated) in {dt:.1f} s, extrapolated to the {self.a.layers}-layer "
+                f"stack from that sample")
 
 
 def run_reference(a):
@@ -346,7 +347,9 @@ def run_ours(a):
         torch.cuda.empty_cache()
     free, _ = torch.cuda.mem_get_info(dev)
     reserve = 4 << 30
-    resident = max(1, min(L, (free - reserve - L * E * H * 4) // (layer_bytes + 512 * e_loc)))
+    # NVFP4 layers also hold their stage images (the FP4 path's copy of the same bytes)
+    per_layer = (2 if not tern else 1) * layer_bytes + 512 * e_loc
+    resident = max(1, min(L, (free - reserve - L * E * H * 4) // per_layer))
     if a.max_resident:
         resident = min(resident, a.max_resident)
     if world > 1:  # every rank streams the same layer schedule
@@ -359,9 +362,15 @@ def run_ours(a):
     tables = []
     buffers = []
     gen = torch.Generator(device=dev)
+    gu_b = F.lib().ffn_b200_fp4_pack_bytes(I, H, 0)
+    dn_b = F.lib().ffn_b200_fp4_pack_bytes(I, H, 1)
     for lay in range(resident):
         buf = torch.empty(layer_bytes + 512 * e_loc, dtype=torch.uint8, device=dev)
         buffers.append(buf)
+        # the layer's stage images, one buffer carved per expert
+        img = None if tern else torch.empty(e_loc * (gu_b + dn_b), dtype=torch.uint8, device=dev)
+        if img is not None:
+            buffers.append(img)
         experts = [None] * E
         off = 0
 
@@ -400,6 +409,9 @@ def run_ours(a):
                                        generator=gen))
                 mats.append(F.TernaryMatrix(p, rs, r, c, core=(ca, cas, cb, cbs), bs=bs))
             experts[e] = F.SwigluExpert(F.FMT_TERNARY if tern else F.FMT_NVFP4, mats, I, H)
+            if not tern:
+                o = j * (gu_b + dn_b)
+                experts[e].pack_fp4(img.narrow(0, o, gu_b), img.narrow(0, o + gu_b, dn_b))
         tables.append((experts, F.expert_table(experts, dev)))
     routers = [F.gen_normal(F.path_key(a.seed, lay, 0, F.TAG_ROUTER), E * H, 0.02).view(E, H)
                for lay in range(L)]
@@ -574,7 +586,7 @@ def run_ours(a):
         if rank == 0:
             cur = x0
             for lay in range(2):
-                full = [F.SwigluExpert.generate(F.FMT_NVFP4, a.seed, lay, e, I, H) for e in range(E)]
+                full = [F.SwigluExpert.generate(F.FMT_NVFP4, a.seed, lay, e, I, H).pack_fp4() for e in range(E)]
                 lf = F.MoeLayer(full, routers[lay], H, I, top_k=K, score_fn=F.SCORE_SIGMOID, norm_w=norm_w,
                                 norm_eps=1e-20, router_mode=F.ROUTER_TENSOR, path=path)
                 cur = lf.forward(cur, residual=cur)
@@ -1109,6 +1121,8 @@ def _sub_layer(a, F, dev, cfg, cpu_s):
     H, I, E, K = a.hidden, a.inter, a.experts, a.top_k
     T, seed = (64, 2) if cfg == 2 else (8192, 3)
     experts = [F.SwigluExpert.generate(F.FMT_NVFP4, seed, 0, e, I, H) for e in range(E)]
+    if cfg == 2:  # the decode layer runs on the FP4 path's stage images
+        experts = [e.pack_fp4() for e in experts]
     wr = F.gen_normal(F.path_key(seed, 0, 0, F.TAG_ROUTER), E * H, 0.02).view(E, H)
     layer = F.MoeLayer(experts, wr, H, I, top_k=K, score_fn=F.SCORE_SIGMOID, router_mode=F.ROUTER_TENSOR)
     x = F.gen_normal(F.path_key(seed, 0, 0, F.TAG_X), T * H).view(T, H)

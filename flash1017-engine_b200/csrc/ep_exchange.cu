@@ -65,6 +65,9 @@ struct PushArgs {
   EpCombine comb;                 // the MoE layer's expert outputs (fused)
   int fused;
   float *inbox[kEpMax];           // every rank's inbox: [sender][rows_per][hidden]
+  unsigned long long *flags[kEpMax];  // every rank's row flags: [sender][rows_per], = tag when sent
+  const unsigned long long *flags_local;
+  unsigned long long tag;         // this call's number (flags of earlier calls hold smaller ones)
   float *slot[kEpMax];            // every rank's output slot of this call
   unsigned long long *cnt1[kEpMax], *cnt2[kEpMax];
   const unsigned long long *cnt1_local, *cnt2_local;
@@ -145,6 +148,16 @@ __global__ void __launch_bounds__(kEpThreads) ep_push_kernel(const PushArgs a) {
       }
       __syncthreads();
     }
+    // a token none of whose experts is on this rank has a zero partial: it is
+    // not sent (its flag stays old), and the owner adds zero in its place
+    bool present = !a.fused || moe_bad || s_bad;
+    if (!present)
+      for (int k = 0; k < a.comb.top_k; ++k) present |= pk[k] >= 0;
+    if (!present) continue;
+    if (threadIdx.x == 0 && u % a.chunks == 0) {
+      const int s = t / a.rows_per, j = t - s * a.rows_per;
+      a.flags[s][a.rank * a.rows_per + j] = a.tag;
+    }
     if (c4 < H4) {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       if (!a.fused) {
@@ -186,7 +199,9 @@ __global__ void __launch_bounds__(kEpThreads) ep_push_kernel(const PushArgs a) {
     float4 v[W];
 #pragma unroll
     for (int src = 0; src < W; ++src)
-      v[src] = __ldcg(reinterpret_cast<const float4 *>(inbox + ((size_t)src * a.rows_per + j) * a.hidden) + c4);
+      v[src] = __ldcg(a.flags_local + src * a.rows_per + j) == a.tag
+                   ? __ldcg(reinterpret_cast<const float4 *>(inbox + ((size_t)src * a.rows_per + j) * a.hidden) + c4)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int src = 0; src < W; ++src) {
@@ -248,6 +263,10 @@ struct ffn_b200_ep {
 
 static size_t round256(size_t n) { return (n + 255) & ~(size_t)255; }
 static size_t rows_max(size_t max_tokens, int world) { return (max_tokens + world - 1) / world; }
+// the row flags sit after the inbox rows, inside the inbox area
+static size_t flags_off(const ffn_b200_ep &ep) {
+  return round256((size_t)ep.world * rows_max(ep.max_tokens, ep.world) * ep.hidden * sizeof(float));
+}
 static size_t ep_alloc_bytes(const ffn_b200_ep &ep) {
   return sizeof(EpShared) + ep.part_bytes + ep.inbox_bytes + 2 * ep.part_bytes;
 }
@@ -283,14 +302,17 @@ int ep_exchange(ffn_b200_ep *ep, size_t n_tok, const EpCombine *comb, const floa
   }
   const size_t inbox_off = sizeof(EpShared) + ep->part_bytes;
   const size_t slot_off = inbox_off + ep->inbox_bytes + (ep->epoch & 1) * ep->part_bytes;
+  a.tag = ep->epoch;
   for (int r = 0; r < ep->world; ++r) {
     EpShared *h = reinterpret_cast<EpShared *>(ep->peer[r]);
     a.inbox[r] = reinterpret_cast<float *>(ep->peer[r] + inbox_off);
+    a.flags[r] = reinterpret_cast<unsigned long long *>(ep->peer[r] + inbox_off + flags_off(*ep));
     a.slot[r] = reinterpret_cast<float *>(ep->peer[r] + slot_off);
     a.cnt1[r] = &h->cnt1;
     a.cnt2[r] = &h->cnt2;
   }
   EpShared *mine = reinterpret_cast<EpShared *>(ep->base);
+  a.flags_local = a.flags[ep->rank];
   a.cnt1_local = &mine->cnt1;
   a.cnt2_local = &mine->cnt2;
   a.err = &mine->err;
@@ -326,10 +348,14 @@ int ffn_b200_ep_create(int rank, int world, size_t max_tokens, size_t hidden, vo
   ep->max_tokens = max_tokens;
   ep->hidden = hidden;
   ep->part_bytes = round256(max_tokens * hidden * sizeof(float));
-  ep->inbox_bytes = round256((size_t)world * rows_max(max_tokens, world) * hidden * sizeof(float));
+  ep->inbox_bytes = round256((size_t)world * rows_max(max_tokens, world) * hidden * sizeof(float)) +
+                    round256((size_t)world * rows_max(max_tokens, world) * sizeof(unsigned long long));
   cudaError_t e = cudaGetDevice(&ep->device);
   if (e == cudaSuccess) e = cudaMalloc(&ep->base, ep_alloc_bytes(*ep));
   if (e == cudaSuccess) e = cudaMemset(ep->base, 0, sizeof(EpShared));
+  if (e == cudaSuccess)  // the row flags: 0 = no call has sent the row
+    e = cudaMemset(ep->base + sizeof(EpShared) + ep->part_bytes + flags_off(*ep), 0,
+                   ep->inbox_bytes - flags_off(*ep));
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t *>(my_handle), ep->base);
   int sms = 0;
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ep->device);

@@ -174,7 +174,7 @@ static int check_nvfp4(const ffn_b200_nvfp4_mat &m, const char *what) {
   return 0;
 }
 
-static_assert(sizeof(ffn_b200_expert) == 248, "ffn_b200_expert is part of the extension ABI");
+static_assert(sizeof(ffn_b200_expert) == 264, "ffn_b200_expert is part of the extension ABI");
 
 static int check_ternary(const ffn_b200_ternary_mat &m, const char *what) {
   if (!m.p || !m.rs) return fail(FFN_B200_EINVAL, std::string(what) + ": null ternary pointer");
@@ -604,11 +604,11 @@ struct MoeWs {
   float *hf;
 };
 
-// The block-scaled FP4 path can run the layer: NVFP4 experts only, shapes
-// in whole 256-column stages and quantiser rows.
+// The block-scaled FP4 path can run the layer: NVFP4 experts only, packed
+// (stage images), shapes in whole 256-column stages and quantiser rows.
 static bool fp4_path_ok(const ffn_b200_moe_desc &d) {
-  return d.has_nvfp4 && !d.has_ternary && !d.has_mxfp4 && d.hidden % 256 == 0 && d.inter % 256 == 0 &&
-         d.hidden <= 16384 && d.inter <= 16384;
+  return d.fp4_packed && d.has_nvfp4 && !d.has_ternary && !d.has_mxfp4 && d.hidden % 256 == 0 &&
+         d.inter % 256 == 0 && d.hidden <= 16384 && d.inter <= 16384;
 }
 
 static MoeWs carve_moe(Carve &c, const ffn_b200_moe_desc &d, size_t T) {
@@ -637,13 +637,13 @@ static MoeWs carve_moe(Carve &c, const ffn_b200_moe_desc &d, size_t T) {
   w.part = c.take<float>(kListSplitBytes / sizeof(float));
   w.cnt = c.take<int>(4 * (size_t)kSplitItems);
   if (fp4_path_ok(d)) {
-    w.xq = c.take<uint8_t>(T * 4 * H / 2);
-    w.xs = c.take<uint8_t>(T * 4 * H / 16);
-    w.xqe = c.take<int>(T * 4);
+    w.xq = c.take<uint8_t>(T * kFp4Terms * H / 2);
+    w.xs = c.take<uint8_t>(T * kFp4Terms * H / 16);
+    w.xqe = c.take<int>(T * kFp4Terms);
     w.hf = c.take<float>(P * I);
-    w.hq = c.take<uint8_t>(P * 4 * I / 2);
-    w.hs = c.take<uint8_t>(P * 4 * I / 16);
-    w.hqe = c.take<int>(P * 4);
+    w.hq = c.take<uint8_t>(P * kFp4Terms * I / 2);
+    w.hs = c.take<uint8_t>(P * kFp4Terms * I / 16);
+    w.hqe = c.take<int>(P * kFp4Terms);
   }
   return w;
 }
@@ -1070,8 +1070,8 @@ static int moe_layer_impl(const ffn_b200_moe_desc *d, size_t n_tok, const float 
   const bool fp4_ok = fp4_path_ok(*d);
   if (d->path == FFN_B200_PATH_FP4 && !fp4_ok)
     return fail(FFN_B200_EUNSUP,
-                "moe_layer: the FP4 path needs NVFP4-only experts and hidden, inter multiples of 256 "
-                "up to 16384");
+                "moe_layer: the FP4 path needs NVFP4-only experts packed by ffn_b200_pack_nvfp4_expert "
+                "(fp4_packed) and hidden, inter multiples of 256 up to 16384");
   const bool grouped_ok = !d->has_ternary && !d->has_mxfp4 && H % 256 == 0 && I % 256 == 0;
   if (d->path == FFN_B200_PATH_GROUPED && !grouped_ok)
     return fail(FFN_B200_EUNSUP,

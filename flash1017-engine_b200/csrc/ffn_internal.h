@@ -57,7 +57,10 @@ struct GroupedArgs {
 size_t gg_chunk_bytes(int n_pairs, int n_local);
 int launch_grouped_moe(const GroupedArgs &g, cudaStream_t st);
 
-// Block-scaled FP4 tensor-core MoE path (NVFP4 experts, decode-sized chunks).
+// Block-scaled FP4 tensor-core MoE path (NVFP4 experts packed by
+// ffn_b200_pack_nvfp4_expert, decode-sized chunks); activations as kFp4Terms
+// NVFP4 terms.
+constexpr int kFp4Terms = 6;
 struct Fp4Args {
   const ffn_b200_expert *experts;
   int e_begin, e_end;
@@ -68,17 +71,18 @@ struct Fp4Args {
   const int32_t *pair_tok;
   const float *x;               // [n_tok][hidden] f32, the layer input the experts see, or
                                 // nullptr when xq/xs/xqe already hold its terms (launch_xprep_q4)
-  uint8_t *xq, *xs;             // x as 4 NVFP4 terms: codes [tok][4][hidden/2], scales [tok][4][hidden/16]
-  int *xqe;                     // [tok][4] exponents
+  uint8_t *xq, *xs;             // x as kFp4Terms NVFP4 terms: codes [tok][t][hidden/2], scales [tok][t][hidden/16]
+  int *xqe;                     // [tok][t] exponents
   float *h;                     // [pair][inter] f32
-  uint8_t *hq, *hs;             // h as 4 NVFP4 terms
+  uint8_t *hq, *hs;             // h as kFp4Terms NVFP4 terms
   int *hqe;
   float *y;                     // [pair][hidden]
-  int *err;                     // device int: 1 timed-out wait, 2 scale outside UE4M3, 3 misaligned
+  int *err;                     // device int: 1 timed-out wait, 3 an expert without stage images
 };
 int launch_fp4_moe(const Fp4Args &g, cudaStream_t st);
-// rows of f32 (K % 256 == 0, K <= 16384, 16-byte aligned rows) -> 4 NVFP4 terms
-int launch_q4(const float *x, int ld_x, int rows, int K, uint8_t *qc, uint8_t *qs, int *qe, cudaStream_t st);
+// rows of f32 (K % 256 == 0, K <= 16384, 16-byte aligned rows) -> `terms` NVFP4 terms
+int launch_q4(const float *x, int ld_x, int rows, int K, int terms, uint8_t *qc, uint8_t *qs, int *qe,
+              cudaStream_t st);
 // launch_xprep's natural-order output (RMSNorm, f16 hi/lo split, exponents;
 // xn only when non-null) and launch_q4 of the normalised rows, in one kernel
 int launch_xprep_q4(const float *x, int ld_x, int rows, int K, __half *nh, __half *nl, int ld_o, int *xe,

@@ -7,44 +7,54 @@
 // (:7537-7547, batched :8285-8324).  The weights enter the tensor core exactly
 // as stored: the E2M1 nibbles are the MMA's A operand and the E4M3 block
 // scales its A scale factors (both are NVFP4 by definition; a scale byte with
-// the sign bit set, or the E4M3 NaN 0x7F, is not a UE4M3 value and is
-// reported through the error word).  No weight is decoded by the SMs.
+// the sign bit set, or the E4M3 NaN 0x7F, is not a UE4M3 value and such an
+// expert cannot be packed).  No weight is decoded by the SMs.
+//
+// Packed weights (ffn_b200_pack_nvfp4_expert): the kernel's pipeline stage is
+// two 128-row blocks x 256 K values -- the W1 and W3 rows of an output block
+// in phase 1, the two halves of a 256-row W2 block in phase 2 -- and packing
+// stores every stage's bytes as the image the stage has in shared memory: the
+// two blocks' codes as 128-byte-swizzled K-major tiles (16 KB each), then
+// their scale-factor atoms (4 K-steps x 512 B each), 36 KB per stage, stages
+// ordered (row block, K step).  One non-multicast bulk copy brings a stage in,
+// and DRAM streams 36 KB contiguous pieces (the reference layout would be read
+// as 128-byte pieces of rows 2 KB apart, which HBM serves markedly slower).
 //
 // Activations: an FP4 MMA multiplies FP4 by FP4, so every activation row x is
-// written as a sum of four NVFP4 rows, x ~= sum_t 2^E_t q_t, each with its own
+// written as a sum of kTerms NVFP4 rows, x ~= sum_t 2^E_t q_t, each with its own
 // UE4M3 scale per 16 values and its own power-of-two exponent E_t (term t
-// quantises what terms 0 .. t-1 left over).  Four terms leave a relative error
-// of about 1e-4 on a dot product (three leave ~1e-3), inside the path's 1e-3
-// bound.  The terms are four MMA columns of one token, so one MMA per K-step
-// and matrix covers all of them; the epilogue adds the columns with their 2^E_t.
+// quantises what terms 0 .. t-1 left over; each term gains about 2.6 bits).
+// Six terms keep a 40-layer stack inside the path's 1e-3 bound (four leave
+// ~2.6e-4 per layer, which compounds through the stack).  The terms are
+// MMA columns of one token, so one MMA per K-step and block covers all of
+// them; the epilogue adds the columns with their 2^E_t.
 //
 // Kernels:
-//   q4_kernel        rows of f32 -> 4 NVFP4 terms (codes [row][t][K/2], scales
+//   q4_kernel        rows of f32 -> NVFP4 terms (codes [row][t][K/2], scales
 //                    [row][t][K/16], exponents [row][t]); one CTA per row, one
 //                    thread per 16-value block.
 //   xq_kernel        the layer input's RMSNorm and router split (xprep's
-//                    output) and its four terms in one pass.
+//                    output) and its terms in one pass.
+//   pack_kernel      reference-layout NVFP4 matrices -> stage images.
 //   fp4_gemm_kernel  PH 1: h[p][r] = SwiGLU(gate, up) for 128 rows of W1 and W3;
 //                    PH 2: y[p][r] for 256 rows of W2 (two 128-row blocks).
 // The gemm is persistent (one CTA per SM walks the (chunk, row block) tiles)
 // and warp-specialised (256 threads):
-//   warps 0, 1  A producers: 128 weight rows each, 256 K values (128 bytes) per
-//               stage by cp.async into the 128-byte-swizzled K-major tile, and
-//               the rows' 16 scale bytes per stage into a staging area; the
-//               copies' completion arrives on the stage's `landed` barrier by
-//               itself, so a producer only ever waits for a free slot.
-//   warp 2      B producer: the chunk's 4 x tokens activation rows and scales;
-//               kLag stages behind, it transposes each landed stage's scales
-//               into the scale-factor atoms and hands the stage over (`full`).
-//   warp 3      TMEM owner; lane 0 copies the stage's scale atoms to TMEM
-//               (tcgen05.cp) and issues the MMAs (M = 128, N = 4 x tokens
+//   warp 0      producer: lane 0 waits for a free slot and issues the stage's
+//               bulk copy (36 KB, completing on a_full).
+//   warp 1      activations: the chunk's kTerms x tokens rows for the stage's
+//               K range, and their scales straight into the scale-factor
+//               atoms (row n at line n % 32, word n / 32), all by cp.async
+//               arriving on b_full when landed: this warp never waits for
+//               data.
+//   warp 2      TMEM owner; lane 0 copies the stage's atoms to TMEM
+//               (tcgen05.cp) and issues the MMAs (M = 128, N = kTerms x tokens
 //               rounded to 8, K = 64), committing to the stage and
 //               accumulator barriers.
 //   warps 4-7   epilogue: thread = TMEM lane = output row of the tile.
-// A stage is handed over by the B warp after its copies landed and its atoms
-// are written (fence.proxy.async, then mbarrier arrive).  All waits are bounded
-// (tcgen05.cuh); a wait that runs out sets the error word, the other roles
-// see it and drain, and the combine kernel writes NaN outputs.
+// All waits are bounded (tcgen05.cuh); a wait that runs out sets the error
+// word, the other roles see it and drain, and the combine kernel writes NaN
+// outputs.
 #include <algorithm>
 
 #include "ffn_internal.h"
@@ -55,39 +65,33 @@ namespace ffn {
 namespace f4 {
 
 constexpr int kThreads = 256;
-constexpr int kStages = 4;
-#ifndef F4_LAG
-#define F4_LAG 2
-#endif
-constexpr int kLag = F4_LAG;       // stages the B warp's issue runs ahead of its hand-overs
-// kLag <= kStages - 2: one stage of slack between the hand-over of stage j and
-// the B warp's wait for slot j + kStages (with kLag = kStages - 1 every stage
-// waits for the MMA commit round trip)
-static_assert(kLag <= kStages - 2, "the B warp hands a stage over one stage before it needs the slot again");
+constexpr int kStages = 5;
 constexpr int kTileM = 128;
-constexpr int kKC = 256;           // K values per stage (128 bytes of a row)
-constexpr int kTerms = 4;
-constexpr int kNTok = 8;           // tokens per chunk
-constexpr int kNMax = kTerms * kNTok;  // MMA columns per chunk (32)
+constexpr int kKC = 256;                  // K values per stage (128 bytes of a row)
+constexpr int kTerms = kFp4Terms;         // activation terms the layer uses
+constexpr int kMaxTerms = 8;              // the quantiser's limit
+constexpr int kNTok = 8;                  // tokens per chunk
+constexpr int kNMax = kTerms * kNTok;     // MMA columns per chunk (48)
+static_assert(kNMax <= 64, "B rows: one or two per lane");
 
-// one pipeline stage in shared memory
-constexpr int OFF_A = 0;                        // 2 blocks x 128 rows x 128 B, swizzled
-constexpr int OFF_B = 2 * kTileM * 128;         // kNMax rows x 128 B, swizzled
-constexpr int OFF_SAS = OFF_B + kNMax * 128;    // A scale staging: 2 x 128 rows x 16 B
-constexpr int OFF_SAA = OFF_SAS + 2 * kTileM * 16;  // A scale atoms: 2 blocks x 4 K-steps x 512 B
-constexpr int OFF_SBS = OFF_SAA + 2 * 4 * 512;  // B scale staging: kNMax rows x 16 B
-constexpr int OFF_SBA = OFF_SBS + kNMax * 16;   // B scale atoms: 4 K-steps x 512 B
+// one stage in shared memory: the packed image (bulk copy), then the B rows
+// and the B scale atoms
+constexpr int kImg = 2 * kTileM * 128 + 2 * 4 * 512;  // 36 KB: codes blk 0, blk 1, atoms blk 0, blk 1
+constexpr int OFF_A = 0;
+constexpr int OFF_SAA = 2 * kTileM * 128;             // A atoms inside the image
+constexpr int OFF_B = kImg;                           // kNMax rows x 128 B, swizzled
+constexpr int OFF_SBA = OFF_B + ((kNMax * 128 + 1023) / 1024) * 1024;  // 4 K-steps x 512 B
 constexpr int STAGE = ((OFF_SBA + 4 * 512) + 1023) / 1024 * 1024;
 constexpr int SMEM = 1024 + kStages * STAGE;
 static_assert(OFF_B % 1024 == 0 && STAGE % 1024 == 0, "swizzled tiles need 1024-byte alignment");
-static_assert(SMEM + 1024 <= 227 * 1024, "shared memory");
+static_assert(SMEM <= 227 * 1024, "shared memory");
 
 // TMEM: two accumulator buffers of 2 blocks x kNMax f32 columns, then two
 // scale-factor slots (SFA: 2 blocks x 4 K-steps x 4 columns; SFB: 4 x 4)
 constexpr int kAccCols = 2 * kNMax;
 constexpr int kSfCols = 2 * 16 + 16;
 constexpr int kSf0 = 2 * kAccCols;
-constexpr int kTmemCols = 256;
+constexpr int kTmemCols = 512;
 static_assert(kSf0 + 2 * kSfCols <= kTmemCols, "TMEM");
 
 // A chunk = the grouping kernel's slice of one expert's routed pairs
@@ -101,13 +105,13 @@ struct GemmArgs {
   const int *n_chunks;
   int K;                    // reduction length
   int rows;                 // output rows
-  const uint8_t *qc;        // activation terms: codes [row][4][K/2]
-  const uint8_t *qs;        //                   scales [row][4][K/16]
-  const int *qe;            //                   exponents [row][4]
+  const uint8_t *qc;        // activation terms: codes [row][kTerms][K/2]
+  const uint8_t *qs;        //                   scales [row][kTerms][K/16]
+  const int *qe;            //                   exponents [row][kTerms]
   const int32_t *pair_tok;  // phase 1: activation row of pair p; phase 2: nullptr (row = pair)
   float *out;               // phase 1: h [pair][rows]; phase 2: y [pair][rows]
   int ld_out;
-  int *err;                 // 1 timed-out wait, 2 scale byte outside UE4M3, 3 misaligned weights
+  int *err;                 // 1 timed-out wait, 3 expert not packed
 };
 
 __device__ __forceinline__ float silu10(float g) { return fminf(g / (1.0f + expf(-g)), 10.0f); }
@@ -121,7 +125,7 @@ template <int PH>
 __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a) {
   pdl_enter();
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t landed[kStages], full[kStages], empty[kStages];
+  __shared__ __align__(8) uint64_t a_full[kStages], b_full[kStages], empty[kStages];
   __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], mma_done;
   __shared__ uint32_t s_tmem;
   uint8_t *smem = smem_raw + ((1024 - (tc::sa(smem_raw) & 1023)) & 1023);
@@ -130,8 +134,8 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
-      tc::bar_init(&landed[s], 96);  // every A and B producer lane's copies (noinc arrivals)
-      tc::bar_init(&full[s], 1);     // the hand-over by the B warp
+      tc::bar_init(&a_full[s], 1);   // the producer's expect_tx; the bulk copy's bytes complete it
+      tc::bar_init(&b_full[s], 32);  // the activation warp's lanes' cp.async (noinc arrivals)
       tc::bar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -141,7 +145,7 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
     tc::bar_init(&mma_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 3) tc::alloc(&s_tmem, kTmemCols);
+  if (warp == 2) tc::alloc(&s_tmem, kTmemCols);
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
@@ -150,27 +154,54 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
   const int rb_count = a.rows / ROWS;
   const int n_tiles = *a.n_chunks * rb_count;
   const int KT = a.K / kKC;
-  const size_t wld = (size_t)a.K / 2, sld = (size_t)a.K / 16;
 
-  if (warp < 2) {
-    // ------------------------------------------------------ A producers
-    // Issue a stage's copies and move on: the copies' completion arrives on
-    // landed[s] by itself (cp.async.mbarrier.arrive.noinc), so a producer waits
-    // only for free slots and every free stage can be in flight.
-    const int mi = warp;
+  if (warp == 0) {
+    // ------------------------------------------------------ producer
+    if (lane == 0) {
+      int it = 0, issued = 0;
+      bool live = true;
+      for (int tile = blockIdx.x; tile < n_tiles && live; tile += gridDim.x) {
+        const Chunk ch = a.chunks[tile / rb_count];
+        const uint8_t *img = PH == 1 ? a.experts[ch.expert].fp4_gu : a.experts[ch.expert].fp4_dn;
+        if (!img || (reinterpret_cast<uintptr_t>(img) & 15)) {
+          atomicExch(a.err, 3);
+          break;
+        }
+        img += (size_t)(tile % rb_count) * KT * kImg;
+        for (int kt = 0; kt < KT; ++kt, ++it) {
+          const int s = it % kStages;
+          if (!tc::bar_wait(&empty[s], ((it / kStages) & 1) ^ 1, a.err)) { live = false; break; }
+          tc::bar_arrive_tx(&a_full[s], (uint32_t)kImg);
+          tc::bulk_g2s(smem + s * STAGE + OFF_A, img + (size_t)kt * kImg, (uint32_t)kImg, &a_full[s]);
+          issued = it + 1;
+        }
+      }
+      // before leaving, the copies this thread issued have landed (bounded:
+      // a copy always completes; this only guards a shared-memory release)
+      for (int j = max(0, issued - kStages); j < issued; ++j)
+        tc::bar_wait_drain(&a_full[j % kStages], (j / kStages) & 1);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------ activations
+    // lane l owns B rows l and l + 32 (when < kNMax): token n / kTerms, term n % kTerms
+    for (int i = lane; i < kStages * 4 * 32; i += 32)  // B atom words 2-3 (rows 64-127) stay zero
+      reinterpret_cast<uint2 *>(smem + (i / 128) * STAGE + OFF_SBA + (i % 128) * 16)[1] = make_uint2(0u, 0u);
+    tc::fence_async_smem();  // (the MMA issuer reads them through the async proxy)
+    const size_t cld = (size_t)a.K / 2, qsld = (size_t)a.K / 16;
     int it = 0;
     bool live = true;
     for (int tile = blockIdx.x; tile < n_tiles && live; tile += gridDim.x) {
       const Chunk ch = a.chunks[tile / rb_count];
-      const int row0 = (tile % rb_count) * ROWS + (PH == 2 ? mi * kTileM : 0);
-      const ffn_b200_nvfp4_mat &M = a.experts[ch.expert].nv[PH == 1 ? mi : 2];
-      const uint8_t *wb = M.w + (size_t)row0 * wld;
-      const uint8_t *sb = M.s + (size_t)row0 * sld;
-      const bool s16 = (reinterpret_cast<uintptr_t>(sb) & 15) == 0;
-      if ((reinterpret_cast<uintptr_t>(wb) & 15) || (reinterpret_cast<uintptr_t>(sb) & 3)) {
-        atomicExch(a.err, 3);
-        live = false;
-        break;
+      const uint8_t *cb[2] = {nullptr, nullptr}, *sbp[2] = {nullptr, nullptr};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int n = lane + 32 * h, i = n / kTerms, t = n - i * kTerms;
+        if (n < kNMax && i < ch.count) {
+          const int xr = a.pair_tok ? __ldg(a.pair_tok + ch.offset + i) : ch.offset + i;
+          cb[h] = a.qc + ((size_t)xr * kTerms + t) * cld;
+          sbp[h] = a.qs + ((size_t)xr * kTerms + t) * qsld;
+        }
       }
       for (int kt = 0; kt < KT; ++kt, ++it) {
         const int s = it % kStages;
@@ -179,115 +210,28 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
           break;
         }
         uint8_t *st = smem + s * STAGE;
-        uint8_t *ta = st + OFF_A + mi * (kTileM * 128);
-        // 8 lanes per row, 16 bytes each: one instruction copies 4 whole rows
-#pragma unroll 8
-        for (int j = 0; j < 32; ++j) {
-          const int rr = 4 * j + (lane >> 3), pc = lane & 7;
-          cp_async16(ta + tc::sw128(rr, pc), wb + (size_t)rr * wld + (size_t)kt * 128 + pc * 16);
-        }
-        uint8_t *stg = st + OFF_SAS + mi * (kTileM * 16);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int rr = lane + 32 * q;
-          const uint8_t *src = sb + (size_t)rr * sld + (size_t)kt * 16;
-          if (s16) {
-            cp_async16(stg + rr * 16, src);
-          } else {
+        for (int h = 0; h < 2; ++h)
+          if (cb[h]) {
+            const uint8_t *src = cb[h] + (size_t)kt * 128;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) cp_async4(stg + rr * 16 + 4 * u, src + 4 * u);
+            for (int c = 0; c < 8; ++c) cp_async16(st + OFF_B + tc::sw128(lane + 32 * h, c), src + c * 16);
           }
-        }
-        tc::cp_async_arrive(&landed[s]);
+        // this K range's 16 scale bytes of row n, 4 per K-step, copied straight
+        // to word n / 32 of line n % 32 of the 4 atoms (no wait in this warp;
+        // the words of absent rows keep stale values, read only into MMA
+        // columns the epilogue never reads)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          if (sbp[h]) {
+            const uint8_t *src = sbp[h] + (size_t)kt * 16;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) cp_async4(st + OFF_SBA + k * 512 + lane * 16 + 4 * h, src + 4 * k);
+          }
+        tc::cp_async_arrive(&b_full[s]);
       }
     }
   } else if (warp == 2) {
-    // ------------------------------------------------------ B producer + hand-over
-    // Issues the chunk's activation rows; kLag stages behind, once a stage's
-    // copies have all landed, transposes its A and B scales into the
-    // scale-factor atoms, fences the async proxy and hands the stage over.
-    int it = 0;
-    bool live = true;
-    auto finish = [&](int j) -> bool {
-      const int sj = j % kStages;
-      if (!__all_sync(0xffffffffu, tc::bar_wait(&landed[sj], (j / kStages) & 1, a.err))) return false;
-      uint8_t *st = smem + sj * STAGE;
-      // a byte with the sign bit set or 0x7F is not a UE4M3 scale: flag the
-      // layer (NaN outputs) and hand the tensor core a zero scale instead
-      uint32_t bad = 0;
-      auto clean = [&](uint32_t w) {
-        const uint32_t off = (w & 0x80808080u) | __vcmpeq4(w & 0x7F7F7F7Fu, 0x7F7F7F7Fu);
-        bad |= off;
-        const uint32_t sel = ((off >> 7) & 0x01010101u) * 0xFFu;  // bytes to clear
-        return w & ~sel;
-      };
-#pragma unroll
-      for (int mi = 0; mi < 2; ++mi) {
-        const uint8_t *stg = st + OFF_SAS + mi * (kTileM * 16);
-        uint4 r[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) r[q] = *reinterpret_cast<const uint4 *>(stg + (lane + 32 * q) * 16);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) r[q] = make_uint4(clean(r[q].x), clean(r[q].y), clean(r[q].z), clean(r[q].w));
-        uint8_t *atoms = st + OFF_SAA + mi * 2048;
-        *reinterpret_cast<uint4 *>(atoms + 0 * 512 + lane * 16) = make_uint4(r[0].x, r[1].x, r[2].x, r[3].x);
-        *reinterpret_cast<uint4 *>(atoms + 1 * 512 + lane * 16) = make_uint4(r[0].y, r[1].y, r[2].y, r[3].y);
-        *reinterpret_cast<uint4 *>(atoms + 2 * 512 + lane * 16) = make_uint4(r[0].z, r[1].z, r[2].z, r[3].z);
-        *reinterpret_cast<uint4 *>(atoms + 3 * 512 + lane * 16) = make_uint4(r[0].w, r[1].w, r[2].w, r[3].w);
-      }
-      if (bad) atomicExch(a.err, 2);
-      const uint4 r = *reinterpret_cast<const uint4 *>(st + OFF_SBS + lane * 16);  // row = lane (kNMax = 32)
-      uint8_t *atoms = st + OFF_SBA;
-      *reinterpret_cast<uint4 *>(atoms + 0 * 512 + lane * 16) = make_uint4(r.x, 0u, 0u, 0u);
-      *reinterpret_cast<uint4 *>(atoms + 1 * 512 + lane * 16) = make_uint4(r.y, 0u, 0u, 0u);
-      *reinterpret_cast<uint4 *>(atoms + 2 * 512 + lane * 16) = make_uint4(r.z, 0u, 0u, 0u);
-      *reinterpret_cast<uint4 *>(atoms + 3 * 512 + lane * 16) = make_uint4(r.w, 0u, 0u, 0u);
-      tc::fence_async_smem();
-      __syncwarp();
-      if (lane == 0) tc::bar_arrive(&full[sj]);
-      return true;
-    };
-    static_assert(kNMax == 32, "one B row per lane");
-    const size_t cld = (size_t)a.K / 2, qsld = (size_t)a.K / 16;
-    for (int tile = blockIdx.x; tile < n_tiles && live; tile += gridDim.x) {
-      const Chunk ch = a.chunks[tile / rb_count];
-      // this lane's B row n = lane: token i = n / 4, term t = n % 4
-      const int i = lane >> 2, t = lane & 3;
-      const bool have = i < ch.count;
-      const uint8_t *cb = nullptr, *sbp = nullptr;
-      if (have) {
-        const int xr = a.pair_tok ? __ldg(a.pair_tok + ch.offset + i) : ch.offset + i;
-        cb = a.qc + ((size_t)xr * kTerms + t) * cld;
-        sbp = a.qs + ((size_t)xr * kTerms + t) * qsld;
-      }
-      const int nrows = kTerms * ch.count;
-      for (int kt = 0; kt < KT; ++kt, ++it) {
-        const int s = it % kStages;
-        if (!__all_sync(0xffffffffu, tc::bar_wait(&empty[s], ((it / kStages) & 1) ^ 1, a.err))) {
-          live = false;
-          break;
-        }
-        uint8_t *st = smem + s * STAGE;
-#pragma unroll
-        for (int j = 0; j < kNMax / 4; ++j) {
-          const int n = 4 * j + (lane >> 3), pc = lane & 7;
-          const uint8_t *rowp = reinterpret_cast<const uint8_t *>(
-              __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(cb), n));
-          if (n < nrows) cp_async16(st + OFF_B + tc::sw128(n, pc), rowp + (size_t)kt * 128 + pc * 16);
-        }
-        if (have) cp_async16(st + OFF_SBS + lane * 16, sbp + (size_t)kt * 16);
-        else *reinterpret_cast<uint4 *>(st + OFF_SBS + lane * 16) = make_uint4(0u, 0u, 0u, 0u);
-        tc::cp_async_arrive(&landed[s]);
-        if (it >= kLag && !finish(it - kLag)) {
-          live = false;
-          break;
-        }
-      }
-    }
-    if (live)
-      for (int j = max(0, it - kLag); j < it; ++j)
-        if (!finish(j)) break;
-  } else if (warp == 3) {
     // ------------------------------------------------------ MMA issuer
     if (lane == 0) {
       int it = 0, tcount = 0;
@@ -302,8 +246,12 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
         const uint32_t acc = tmem + b * kAccCols;
         for (int kt = 0; kt < KT; ++kt, ++it) {
           const int s = it % kStages;
-          if (!tc::bar_wait(&full[s], (it / kStages) & 1, a.err)) { live = false; break; }
-          tc::fence_async_smem();  // the producers' cp.async data, for the tensor core's reads
+          if (!tc::bar_wait(&a_full[s], (it / kStages) & 1, a.err) ||
+              !tc::bar_wait(&b_full[s], (it / kStages) & 1, a.err)) {
+            live = false;
+            break;
+          }
+          tc::fence_async_smem();  // the activations' cp.async data, for the tensor core's reads
           tc::fence_after();
           const uint8_t *st = smem + s * STAGE;
           const uint32_t sf = tmem + kSf0 + (it & 1) * kSfCols;
@@ -332,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
       tc::bar_wait_drain(&mma_done, 0);
     }
     __syncwarp();
-  } else {
+  } else if (warp >= 4) {
     // ------------------------------------------------------ epilogue (warps 4-7)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int tcount = 0;
@@ -340,21 +288,25 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
       const Chunk ch = a.chunks[tile / rb_count];
       const int row0 = (tile % rb_count) * ROWS;
       const int b = tcount & 1, use = tcount >> 1;
-      // lane n: 2^E of MMA column n = (token n / 4, term n % 4); 0 when absent
-      float csl = 0.f;
-      {
-        const int i = lane >> 2, t = lane & 3;
-        if (i < ch.count) {
+      // lane l: 2^E of MMA columns l and l + 32 (token n / kTerms, term n % kTerms); 0 when absent
+      float csl[2] = {0.f, 0.f};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int n = lane + 32 * h, i = n / kTerms, t = n - i * kTerms;
+        if (n < kNMax && i < ch.count) {
           const int xr = a.pair_tok ? __ldg(a.pair_tok + ch.offset + i) : ch.offset + i;
-          csl = pow2f(__ldg(a.qe + (size_t)xr * kTerms + t));
+          csl[h] = pow2f(__ldg(a.qe + (size_t)xr * kTerms + t));
         }
       }
       if (!__all_sync(0xffffffffu, tc::bar_wait(&acc_full[b], use & 1, a.err))) break;
       tc::fence_after();
-      uint32_t v0[32], v1[32];
+      uint32_t v0[kNMax], v1[kNMax];
       const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16) + b * kAccCols;
-      tc::ld32(tl, v0);
-      tc::ld32(tl + kNMax, v1);
+      static_assert(kNMax == 48, "the epilogue reads 32 + 16 columns per block");
+      tc::ld32(tl, *reinterpret_cast<uint32_t(*)[32]>(v0));
+      tc::ld16(tl + 32, v0 + 32);
+      tc::ld32(tl + kNMax, *reinterpret_cast<uint32_t(*)[32]>(v1));
+      tc::ld16(tl + kNMax + 32, v1 + 32);
       tc::wait_ld();
       const ffn_b200_expert &E = a.experts[ch.expert];
       const float gs0 = E.nv[PH == 1 ? 0 : 2].gs, gs1 = E.nv[PH == 1 ? 1 : 2].gs;
@@ -365,9 +317,10 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
         float d0 = 0.f, d1 = 0.f;
 #pragma unroll
         for (int t = kTerms - 1; t >= 0; --t) {  // smallest term first
-          const float c = __shfl_sync(0xffffffffu, csl, kTerms * i + t);
-          d0 += __uint_as_float(v0[kTerms * i + t]) * c;
-          d1 += __uint_as_float(v1[kTerms * i + t]) * c;
+          const int n = kTerms * i + t;
+          const float c = __shfl_sync(0xffffffffu, csl[n >> 5], n & 31);
+          d0 += __uint_as_float(v0[n]) * c;
+          d1 += __uint_as_float(v1[n]) * c;
         }
         float *o = a.out + (size_t)(ch.offset + i) * a.ld_out + row0 + r;
         if (PH == 1) {
@@ -385,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
   asm volatile("cp.async.wait_all;" ::: "memory");
   tc::fence_before();
   __syncthreads();
-  if (warp == 3) {
+  if (warp == 2) {
     tc::fence_after();
     tc::dealloc(tmem, kTmemCols);
   }
@@ -466,16 +419,16 @@ __device__ __forceinline__ int term_exp(float m) {
   return max(-110, min(110, ex - 1 - 8));
 }
 
-// The four terms of one row, thread = 16-value block `threadIdx.x` holding
+// The `terms` terms of one row, thread = 16-value block `threadIdx.x` holding
 // v (its values; the remainder afterwards).  Term t: one CTA-wide maximum
 // (warp shuffles, then the warps' maxima through red[t & 1]), the exponent,
 // and one block quantisation per thread.  Every thread of the CTA calls it.
-__device__ __forceinline__ void q4_terms(float (&v)[16], bool mine, int row, int K, float (*red)[32],
+__device__ __forceinline__ void q4_terms(float (&v)[16], bool mine, int row, int K, int terms, float (*red)[32],
                                          uint8_t *qc, uint8_t *qs, int *qe) {
   const int blk = threadIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int nw = (int)(blockDim.x >> 5);
 #pragma unroll 1
-  for (int t = 0; t < kTerms; ++t) {
+  for (int t = 0; t < terms; ++t) {
     float am = 0.f;
 #pragma unroll
     for (int u = 0; u < 16; ++u) am = fmaxf(am, fabsf(v[u]));
@@ -485,24 +438,24 @@ __device__ __forceinline__ void q4_terms(float (&v)[16], bool mine, int row, int
     float m = lane < nw ? red[t & 1][lane] : 0.f;
     for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     const int e = term_exp(m);
-    if (threadIdx.x == 0) qe[(size_t)row * kTerms + t] = e;
+    if (threadIdx.x == 0) qe[(size_t)row * terms + t] = e;
     if (mine) {
       uint2 cw;
       const uint32_t code = quant_block(v, pow2f(-e), pow2f(e), cw);
-      *reinterpret_cast<uint2 *>(qc + ((size_t)row * kTerms + t) * (K / 2) + 8 * blk) = cw;
-      qs[((size_t)row * kTerms + t) * (K / 16) + blk] = (uint8_t)code;
+      *reinterpret_cast<uint2 *>(qc + ((size_t)row * terms + t) * (K / 2) + 8 * blk) = cw;
+      qs[((size_t)row * terms + t) * (K / 16) + blk] = (uint8_t)code;
     }
   }
 }
 
-// x row (f32, K values) -> 4 NVFP4 terms.  Term t: E_t = floor(log2 max|r_t|)
+// x row (f32, K values) -> `terms` NVFP4 terms.  Term t: E_t = floor(log2 max|r_t|)
 // - 8 over the row's remainder r_t, then every 16-value block quantised by
 // quant_block.  A zero remainder gives E_t = 0 and zero codes.
 // One CTA per row and one thread per 16-value block (blockDim = K / 16 rounded
 // up to a warp): each term costs one CTA-wide maximum (warp shuffles, then
 // the warps' maxima through shared memory) and one block quantisation per
-// thread, so a row's four terms are four short dependent steps.
-__global__ void __launch_bounds__(1024) q4_kernel(const float *__restrict__ x, int ld_x, int K,
+// thread, so a row's terms are short dependent steps.
+__global__ void __launch_bounds__(1024) q4_kernel(const float *__restrict__ x, int ld_x, int K, int terms,
                                                   uint8_t *qc, uint8_t *qs, int *qe) {
   pdl_enter();
   const int row = blockIdx.x, blk = threadIdx.x;
@@ -515,7 +468,7 @@ __global__ void __launch_bounds__(1024) q4_kernel(const float *__restrict__ x, i
                           : make_float4(0.f, 0.f, 0.f, 0.f);
     v[4 * u] = f.x; v[4 * u + 1] = f.y; v[4 * u + 2] = f.z; v[4 * u + 3] = f.w;
   }
-  q4_terms(v, mine, row, K, red, qc, qs, qe);
+  q4_terms(v, mine, row, K, terms, red, qc, qs, qe);
 }
 
 // The layer input's preparation and its quantisation in one pass (the FP4
@@ -623,7 +576,52 @@ __global__ void __launch_bounds__(1024) xq_kernel(const float *__restrict__ x, i
       dl[1] = make_uint4(wl[4], wl[5], wl[6], wl[7]);
     }
   }
-  q4_terms(v, mine, row, K, red, qc, qs, qe);  // the four NVFP4 terms, as q4_kernel forms them
+  q4_terms(v, mine, row, K, kTerms, red, qc, qs, qe);  // the layer's terms, as q4_kernel forms them
+}
+
+// Bytes of a scale word that are not UE4M3 (sign bit set, or 0x7F: its low
+// seven bits plus one carry into bit 7), as 0x80 in each such byte.
+__device__ __forceinline__ uint32_t not_ue4m3(uint32_t w) {
+  return (w | ((w & 0x7F7F7F7Fu) + 0x01010101u)) & 0x80808080u;
+}
+
+// Reference-layout NVFP4 matrices -> stage images (the layout is described at
+// the top of this file).  One CTA per image (row block rb, K step kt): the two
+// blocks' codes (2 x 128 rows x 8 pieces of 16 bytes, moved to their swizzled
+// places), then the two blocks' scale atoms (2 x 4 K-steps x 32 lines of 16
+// bytes: line l = the 4 scale bytes of rows l, l + 32, l + 64, l + 96).  A
+// scale byte that is not UE4M3 is counted in *bad.
+struct PackArgs {
+  const uint8_t *w0, *w1;  // codes of the matrices holding block 0 and block 1
+  const uint8_t *s0, *s1;  // their E4M3 scales
+  int row_off1;            // block 1's first row, relative to block 0's
+  int rows_per_rb;         // rows between consecutive row blocks
+  int K, KT;
+  uint8_t *out;
+  int *bad;
+};
+__global__ void __launch_bounds__(256) pack_kernel(const PackArgs a) {
+  const int img = blockIdx.x, rb = img / a.KT, kt = img - rb * a.KT;
+  uint8_t *o = a.out + (size_t)img * kImg;
+  const size_t wld = (size_t)a.K / 2, sld = (size_t)a.K / 16;
+  for (int p = threadIdx.x; p < 2 * kTileM * 8; p += blockDim.x) {
+    const int blk = p / (kTileM * 8), r = (p / 8) % kTileM, c = p % 8;
+    const size_t row = (size_t)rb * a.rows_per_rb + (blk ? a.row_off1 : 0) + r;
+    const uint4 v = *reinterpret_cast<const uint4 *>((blk ? a.w1 : a.w0) + row * wld + (size_t)kt * 128 + c * 16);
+    *reinterpret_cast<uint4 *>(o + blk * (kTileM * 128) + tc::sw128(r, c)) = v;
+  }
+  for (int p = threadIdx.x; p < 2 * 4 * 32; p += blockDim.x) {
+    const int blk = p / 128, k = (p / 32) % 4, l = p % 32;
+    uint32_t w[4], off = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const size_t row = (size_t)rb * a.rows_per_rb + (blk ? a.row_off1 : 0) + l + 32 * q;
+      w[q] = *reinterpret_cast<const uint32_t *>((blk ? a.s1 : a.s0) + row * sld + (size_t)kt * 16 + 4 * k);
+      off |= not_ue4m3(w[q]);
+    }
+    *reinterpret_cast<uint4 *>(o + OFF_SAA + blk * 2048 + k * 512 + l * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    if (off) atomicAdd(a.bad, 1);
+  }
 }
 
 }  // namespace f4
@@ -642,12 +640,14 @@ int launch_xprep_q4(const float *x, int ld_x, int rows, int K, __half *nh, __hal
   return 0;
 }
 
-int launch_q4(const float *x, int ld_x, int rows, int K, uint8_t *qc, uint8_t *qs, int *qe, cudaStream_t st) {
+int launch_q4(const float *x, int ld_x, int rows, int K, int terms, uint8_t *qc, uint8_t *qs, int *qe,
+              cudaStream_t st) {
   if (rows <= 0) return 0;
   if (K % 256 || K > 16384 || ld_x % 4 || (reinterpret_cast<uintptr_t>(x) & 15))
     return fail(FFN_B200_EUNSUP, "q4: K must be a multiple of 256 up to 16384, rows 16-byte aligned");
+  if (terms < 1 || terms > f4::kMaxTerms) return fail(FFN_B200_EINVAL, "q4: terms must be 1..8");
   const int threads = (K / 16 + 31) / 32 * 32;  // one thread per 16-value block
-  FFN_LAUNCH_PDL(FFN_B200_K_QUANT, st, "q4_kernel", f4::q4_kernel, rows, threads, 0, x, ld_x, K, qc, qs, qe);
+  FFN_LAUNCH_PDL(FFN_B200_K_QUANT, st, "q4_kernel", f4::q4_kernel, rows, threads, 0, x, ld_x, K, terms, qc, qs, qe);
   return 0;
 }
 
@@ -668,7 +668,7 @@ int launch_fp4_moe(const Fp4Args &g, cudaStream_t st) {
   const int *n_chunks = g.n_slices;
   FFN_CUDA_TRY(cudaMemsetAsync(g.err, 0, sizeof(int), st));
   int rc = 0;
-  if (g.x && (rc = launch_q4(g.x, H, T, H, g.xq, g.xs, g.xqe, st))) return rc;  // else quantised already
+  if (g.x && (rc = launch_q4(g.x, H, T, H, kTerms, g.xq, g.xs, g.xqe, st))) return rc;  // else quantised already
   const int sms = sm_count_of(dev);
   const long long max_chunks = (long long)P / f4::kNTok + e_loc;
   GemmArgs p{};
@@ -686,7 +686,7 @@ int launch_fp4_moe(const Fp4Args &g, cudaStream_t st) {
   p.err = g.err;
   int grid = (int)std::max(1LL, std::min<long long>(sms, max_chunks * (I / kTileM)));
   FFN_LAUNCH_PDL(FFN_B200_K_FP4_GATEUP, st, "fp4_gemm_kernel<1>", (fp4_gemm_kernel<1>), grid, f4::kThreads, SMEM, p);
-  if ((rc = launch_q4(g.h, I, P, I, g.hq, g.hs, g.hqe, st))) return rc;
+  if ((rc = launch_q4(g.h, I, P, I, kTerms, g.hq, g.hs, g.hqe, st))) return rc;
   GemmArgs q = p;
   q.K = I;
   q.rows = H;
@@ -705,13 +705,64 @@ int launch_fp4_moe(const Fp4Args &g, cudaStream_t st) {
 
 extern "C" {
 
+int ffn_b200_quantize_nvfp4_terms(size_t rows, size_t K, size_t terms, const float *x, size_t ld_x,
+                                  uint8_t *codes, uint8_t *scales, int32_t *exps, void *stream) {
+  if (rows == 0) return 0;
+  if (!x || !codes || !scales || !exps) return ffn::fail(FFN_B200_EINVAL, "quantize_nvfp4: null pointer");
+  if (rows > (1u << 24) || ld_x < K || ld_x > (1u << 30))
+    return ffn::fail(FFN_B200_EINVAL, "quantize_nvfp4: bad rows / ld_x");
+  if (terms < 1 || terms > (size_t)ffn::f4::kMaxTerms) return ffn::fail(FFN_B200_EINVAL, "quantize_nvfp4: terms must be 1..8");
+  return ffn::launch_q4(x, (int)ld_x, (int)rows, (int)K, (int)terms, codes, scales, exps, (cudaStream_t)stream);
+}
+
+size_t ffn_b200_fp4_pack_bytes(size_t inter, size_t hidden, int which) {
+  if (inter % 256 || hidden % 256) return 0;
+  return which == 0 ? (inter / 128) * (hidden / 256) * (size_t)ffn::f4::kImg
+                    : (hidden / 256) * (inter / 256) * (size_t)ffn::f4::kImg;
+}
+
+int ffn_b200_pack_nvfp4_expert(size_t inter, size_t hidden, const ffn_b200_expert *e, uint8_t *gu, uint8_t *dn,
+                               void *stream) {
+  using namespace ffn;
+  if (!e) return fail(FFN_B200_EINVAL, "pack_nvfp4_expert: null expert");
+  if (e->format != FFN_B200_FMT_NVFP4) return fail(FFN_B200_EINVAL, "pack_nvfp4_expert: not an NVFP4 expert");
+  if (inter % 256 || hidden % 256 || inter == 0 || hidden == 0 || inter > 16384 || hidden > 16384)
+    return fail(FFN_B200_EUNSUP, "pack_nvfp4_expert: inter and hidden must be multiples of 256 up to 16384");
+  for (int m = 0; m < 3; ++m)
+    if (!e->nv[m].w || !e->nv[m].s || (reinterpret_cast<uintptr_t>(e->nv[m].w) & 15) ||
+        (reinterpret_cast<uintptr_t>(e->nv[m].s) & 3))
+      return fail(FFN_B200_EINVAL, "pack_nvfp4_expert: codes must be 16-byte and scales 4-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(gu) | reinterpret_cast<uintptr_t>(dn)) & 15)
+    return fail(FFN_B200_EINVAL, "pack_nvfp4_expert: images must be 16-byte aligned");
+  cudaStream_t st = (cudaStream_t)stream;
+  int dev = 0;
+  FFN_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(FFN_B200_EUNSUP, "pack_nvfp4_expert: device index >= 64");
+  static int *bad_dev[64] = {nullptr};  // one counter per device (packing is a load-time step)
+  if (!bad_dev[dev]) FFN_CUDA_TRY(cudaMalloc(&bad_dev[dev], sizeof(int)));
+  FFN_CUDA_TRY(cudaMemsetAsync(bad_dev[dev], 0, sizeof(int), st));
+  const int H = (int)hidden, I = (int)inter;
+  if (gu) {
+    f4::PackArgs p{e->nv[0].w, e->nv[1].w, e->nv[0].s, e->nv[1].s, 0, f4::kTileM, H, H / 256, gu, bad_dev[dev]};
+    FFN_LAUNCH(FFN_B200_K_OTHER, st, "pack_kernel", (f4::pack_kernel<<<(I / 128) * (H / 256), 256, 0, st>>>(p)));
+  }
+  if (dn) {
+    f4::PackArgs p{e->nv[2].w, e->nv[2].w, e->nv[2].s, e->nv[2].s, f4::kTileM, 2 * f4::kTileM, I, I / 256, dn,
+                   bad_dev[dev]};
+    FFN_LAUNCH(FFN_B200_K_OTHER, st, "pack_kernel", (f4::pack_kernel<<<(H / 256) * (I / 256), 256, 0, st>>>(p)));
+  }
+  int bad = 0;
+  FFN_CUDA_TRY(cudaMemcpyAsync(&bad, bad_dev[dev], sizeof(int), cudaMemcpyDeviceToHost, st));
+  FFN_CUDA_TRY(cudaStreamSynchronize(st));
+  if (bad)
+    return fail(FFN_B200_EINVAL, "pack_nvfp4_expert: a scale byte is not UE4M3 (sign bit set or 0x7F); "
+                                 "the FP4 path cannot take this expert");
+  return 0;
+}
+
 int ffn_b200_quantize_nvfp4x4(size_t rows, size_t K, const float *x, size_t ld_x, uint8_t *codes,
                               uint8_t *scales, int32_t *exps, void *stream) {
-  if (rows == 0) return 0;
-  if (!x || !codes || !scales || !exps) return ffn::fail(FFN_B200_EINVAL, "quantize_nvfp4x4: null pointer");
-  if (rows > (1u << 24) || ld_x < K || ld_x > (1u << 30))
-    return ffn::fail(FFN_B200_EINVAL, "quantize_nvfp4x4: bad rows / ld_x");
-  return ffn::launch_q4(x, (int)ld_x, (int)rows, (int)K, codes, scales, exps, (cudaStream_t)stream);
+  return ffn_b200_quantize_nvfp4_terms(rows, K, 4, x, ld_x, codes, scales, exps, stream);
 }
 
 }  // extern "C"

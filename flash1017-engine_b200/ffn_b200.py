@@ -44,7 +44,8 @@ EXPORTS = [
     "ffn_b200_st_find", "ffn_b200_st_expert_bytes", "ffn_b200_st_load_expert",
     "ffn_b200_compress_ws_bytes", "ffn_b200_compress_ternary_b64",
     "ffn_b200_quantize_nvfp4x4", "ffn_b200_ep_moe_layer", "ffn_b200_set_host_cache_budget",
-    "ffn_b200_topk",
+    "ffn_b200_topk", "ffn_b200_quantize_nvfp4_terms", "ffn_b200_fp4_pack_bytes",
+    "ffn_b200_pack_nvfp4_expert",
 ]
 
 # Kernel kinds of ffn_b200_profile_read (FFN_B200_K_*).
@@ -79,7 +80,7 @@ class TnMat(C.Structure):
 
 class Expert(C.Structure):
     _fields_ = [("format", C.c_int32), ("proj_scale", C.c_float), ("nv", NvMat * 3),
-                ("tn", TnMat * 3)]
+                ("tn", TnMat * 3), ("fp4_gu", C.c_void_p), ("fp4_dn", C.c_void_p)]
 
 
 class MoeDesc(C.Structure):
@@ -89,10 +90,10 @@ class MoeDesc(C.Structure):
                 ("router_mode", C.c_int32), ("expert_begin", C.c_int32),
                 ("expert_end", C.c_int32), ("has_nvfp4", C.c_int32),
                 ("has_ternary", C.c_int32), ("norm_w", C.c_void_p), ("norm_eps", C.c_float),
-                ("path", C.c_int32), ("has_mxfp4", C.c_int32)]
+                ("path", C.c_int32), ("has_mxfp4", C.c_int32), ("fp4_packed", C.c_int32)]
 
 
-assert C.sizeof(Expert) == 248, C.sizeof(Expert)
+assert C.sizeof(Expert) == 264, C.sizeof(Expert)
 
 _lib = None
 
@@ -117,6 +118,10 @@ def lib() -> C.CDLL:
         L.ffn_b200_mxfp4_matvec.argtypes = [sz, sz, sz, C.POINTER(NvMat), vp, vp, vp, sz, vp]
         L.ffn_b200_quantize_nvfp4x4.argtypes = [sz, sz, vp, sz, vp, vp, vp, vp]
         L.ffn_b200_topk.argtypes = [sz, sz, sz, C.c_int32, vp, sz, vp, vp, vp, vp]
+        L.ffn_b200_quantize_nvfp4_terms.argtypes = [sz, sz, sz, vp, sz, vp, vp, vp, vp]
+        L.ffn_b200_fp4_pack_bytes.restype = sz
+        L.ffn_b200_fp4_pack_bytes.argtypes = [sz, sz, C.c_int]
+        L.ffn_b200_pack_nvfp4_expert.argtypes = [sz, sz, C.POINTER(Expert), vp, vp, vp]
         L.gx10_rust_mxfp4_matvec.argtypes = [sz, sz, vp, vp, vp, vp]
         L.gx10_rust_mxfp4_matvec.restype = C.c_bool
         L.gx10_rust_mxfp4_mlp_accum.argtypes = [sz, sz, vp, vp, vp, vp, vp, vp, vp, vp, f32,
@@ -526,6 +531,7 @@ class SwigluExpert:
     def __init__(self, fmt, mats, inter, hidden, proj_scale=1.0):
         self.fmt, self.mats, self.inter, self.hidden = fmt, mats, inter, hidden
         self.proj_scale = float(proj_scale)
+        self.fp4 = None  # (gate/up, down) stage images of the FP4 path
 
     def cstruct(self) -> Expert:
         e = Expert()
@@ -536,7 +542,29 @@ class SwigluExpert:
                 e.tn[i] = m.cstruct()
             else:  # NVFP4 and MXFP4 use nv[]
                 e.nv[i] = m.cstruct()
+        if self.fp4 is not None:
+            e.fp4_gu, e.fp4_dn = _ptr(self.fp4[0]), _ptr(self.fp4[1])
         return e
+
+    def pack_fp4(self, gu=None, dn=None, stream=None):
+        """The FP4 path's stage images of this NVFP4 expert
+        (ffn_b200_pack_nvfp4_expert), into gu / dn (uint8 device tensors of
+        ffn_b200_fp4_pack_bytes, e.g. views of one larger buffer) or new
+        tensors; raises FfnError when a scale byte is not UE4M3.  Returns self."""
+        torch = _torch()
+        dev = self.mats[0].w.device
+        nb = [lib().ffn_b200_fp4_pack_bytes(self.inter, self.hidden, w) for w in (0, 1)]
+        if gu is None:
+            gu = torch.empty(nb[0], dtype=torch.uint8, device=dev)
+        if dn is None:
+            dn = torch.empty(nb[1], dtype=torch.uint8, device=dev)
+        if gu.numel() < nb[0] or dn.numel() < nb[1]:
+            raise FfnError("pack_fp4: image buffers too small")
+        e = self.cstruct()
+        check(lib().ffn_b200_pack_nvfp4_expert(self.inter, self.hidden, C.byref(e), _ptr(gu), _ptr(dn),
+                                               _stream(stream)), "pack_nvfp4_expert")
+        self.fp4 = (gu, dn)
+        return self
 
     @classmethod
     def generate(cls, fmt, seed, layer, expert, inter, hidden, gs=1.0, with_core=True,
@@ -702,11 +730,15 @@ class MoeLayer:
         else:  # a shared (table, formats) pair
             self.table, fmts = table
         lo, hi = expert_range if expert_range else (0, n)
+        # the FP4 path reads stage images: every local expert must carry them
+        # (the table must have been built after pack_fp4)
+        packed = all(experts[e] is not None and getattr(experts[e], "fp4", None) is not None
+                     for e in range(lo, hi))
         self.desc = MoeDesc(hidden, inter, n, top_k, _ptr(self.table), _ptr(router_w),
                             _ptr(router_bias), score_fn, router_mode, lo, hi,
                             int(FMT_NVFP4 in fmts or FMT_MXFP4 in fmts or not fmts),
                             int(FMT_TERNARY in fmts), _ptr(norm_w), float(norm_eps), int(path),
-                            int(FMT_MXFP4 in fmts))
+                            int(FMT_MXFP4 in fmts), int(packed))
         self.ws = ws if ws is not None else Workspace(device)
 
     def ws_bytes(self, n_tok: int) -> int:

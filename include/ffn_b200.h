@@ -22,6 +22,8 @@
  *           byte j; 0->-1, 1->0, 2->+1, 3->0), rs [rows] f32 row scales;
  *           optional rank-16 Q8 core a [16, cols] i8 (= V^T), a_sc [16],
  *           b [rows, 16] i8 (= U), b_sc [16]  (flash1017.rs:2393-2672).
+ * The FP4 path reads a derived copy of NVFP4 experts, its stage images
+ * (ffn_b200_pack_nvfp4_expert), written from those layouts.
  */
 #ifndef FFN_B200_H
 #define FFN_B200_H
@@ -107,6 +109,10 @@ typedef struct ffn_b200_expert {
     float proj_scale;   /* ternary tier_b_proj_scale (flash1017.rs:7551-7561); 1 for NVFP4 */
     ffn_b200_nvfp4_mat nv[3];
     ffn_b200_ternary_mat tn[3];
+    /* NVFP4 experts packed for the FP4 tensor-core path
+     * (ffn_b200_pack_nvfp4_expert; DEVICE, 16-byte aligned), or NULL */
+    const uint8_t *fp4_gu;  /* W1 and W3 stage images */
+    const uint8_t *fp4_dn;  /* W2 stage images */
 } ffn_b200_expert;
 
 /* ---------------------------------------------------------------- library */
@@ -204,21 +210,26 @@ typedef struct ffn_b200_moe_desc {
     /* MXFP4 experts occur in experts[] (they count as has_nvfp4 too: same
      * kernel family; the grouped GEMM is NVFP4-only). */
     int32_t has_mxfp4;
+    /* every expert in [expert_begin, expert_end) carries fp4_gu and fp4_dn
+     * (the FP4 path needs them) */
+    int32_t fp4_packed;
 } ffn_b200_moe_desc;
 
 #define FFN_B200_PATH_AUTO 0
 #define FFN_B200_PATH_GEMV 1    /* slices of <= 8 tokens, f16 hi/lo activations (~fp32) */
 #define FFN_B200_PATH_GROUPED 2 /* tcgen05 grouped GEMM, f16 activations (rel. err ~2e-4) */
 /* tcgen05 kind::mxf4nvf4: the NVFP4 weights and their E4M3 block scales enter
- * the tensor core as stored (scale bytes must be UE4M3: sign bit clear, not
- * 0x7F; otherwise the layer's outputs are NaN), activations as four NVFP4
- * residual terms (rel. err ~2e-4); chunks of <= 8 tokens per expert */
+ * the tensor core unchanged, from the stage images ffn_b200_pack_nvfp4_expert
+ * writes (fp4_packed; scale bytes must be UE4M3: sign bit clear, not 0x7F),
+ * activations as six NVFP4 residual terms (rel. err ~1e-5 per layer); chunks
+ * of <= 8 tokens per expert.  AUTO takes it for NVFP4-only packed layers
+ * below FFN_B200_GROUPED_MIN_PAIRS pairs per expert. */
 #define FFN_B200_PATH_FP4 3
 #define FFN_B200_GROUPED_MIN_PAIRS 48
 
 /* The FP4 path's activation format (no reference counterpart: the reference
  * multiplies f32 activations).  Each row x of K values (K % 256 == 0, K <=
- * 16384; rows 16-byte aligned, ld_x % 4 == 0) becomes four NVFP4 terms,
+ * 16384; rows 16-byte aligned, ld_x % 4 == 0) becomes NVFP4 terms (four here),
  * x ~= sum_t 2^exps[t] * q_t: codes [rows][4][K/2] (E2M1 pairs, low nibble =
  * even column), scales [rows][4][K/16] (UE4M3 per 16 values), exps [rows][4].
  * Term t quantises what terms < t left: E_t = floor(log2 max|r_t|) - 8, block
@@ -227,6 +238,30 @@ typedef struct ffn_b200_moe_desc {
 FFN_B200_EXPORT int ffn_b200_quantize_nvfp4x4(size_t rows, size_t K, const float *x, size_t ld_x,
                                               uint8_t *codes, uint8_t *scales, int32_t *exps,
                                               void *stream);
+/* The same with `terms` (1..8) terms: codes [rows][terms][K/2], scales
+ * [rows][terms][K/16], exps [rows][terms].  The FP4 path uses six. */
+FFN_B200_EXPORT int ffn_b200_quantize_nvfp4_terms(size_t rows, size_t K, size_t terms, const float *x,
+                                                  size_t ld_x, uint8_t *codes, uint8_t *scales,
+                                                  int32_t *exps, void *stream);
+
+/* The FP4 path's weight format (no reference counterpart; the reference keeps
+ * the row-major NVFP4 layout, which stays the input here).  A pipeline stage
+ * of the FP4 kernels covers two 128-row blocks x 256 K values -- the W1 and W3
+ * rows of an output block (gate/up), or the two halves of a 256-row W2 block
+ * (down) -- and its image holds, in order: each block's codes as a K-major
+ * 128-byte-swizzled tile (16 B piece c of row r at r/8*1024 + r%8*128 +
+ * (c ^ r%8)*16; 16 KB per block), then each block's scale atoms (4 K-steps x
+ * 512 B; line l = the 4 E4M3 scale bytes of rows l, l+32, l+64, l+96).  Images
+ * follow in (row block, K step) order, 36,864 bytes each: gate/up
+ * inter/128 x hidden/256 images, down hidden/256 x inter/256 -- the same bytes
+ * as the reference layout.  which: 0 gate/up, 1 down; 0 when inter or hidden
+ * is not a multiple of 256. */
+FFN_B200_EXPORT size_t ffn_b200_fp4_pack_bytes(size_t inter, size_t hidden, int which);
+/* Writes e's images (e: host struct, DEVICE pointers; w 16-byte, s 4-byte
+ * aligned) into gu and/or dn (DEVICE, 16-byte aligned; either may be NULL).
+ * Synchronises the stream.  FFN_B200_EINVAL when a scale byte is not UE4M3. */
+FFN_B200_EXPORT int ffn_b200_pack_nvfp4_expert(size_t inter, size_t hidden, const ffn_b200_expert *e,
+                                               uint8_t *gu, uint8_t *dn, void *stream);
 
 /* The layer's top-k step on precomputed logits (flash1017.rs:7280-7376): per
  * token, logit = sum of the n_part (1..3) partial planes in plane order

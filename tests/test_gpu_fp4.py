@@ -1,11 +1,13 @@
 """The MoE layer's block-scaled FP4 tensor-core path (FFN_B200_PATH_FP4,
 tcgen05 kind::mxf4nvf4) against the CPU oracle, through the C-ABI.
 
-The weights enter the tensor core exactly as stored (E2M1 codes, E4M3 block
-scales); the activations enter as four NVFP4 residual terms
-(ffn_b200_quantize_nvfp4x4).  The quantiser is checked bit for bit against a
-numpy restatement of its rule, the layer against the oracle at the path's
-tolerance (max|y-ref|/max|ref| <= 1e-3, cosine >= 0.99999)."""
+The weights enter the tensor core unchanged, from the stage images
+ffn_b200_pack_nvfp4_expert writes (E2M1 codes, E4M3 block scales; checked
+byte for byte against a numpy restatement of the layout); the activations
+enter as six NVFP4 residual terms (ffn_b200_quantize_nvfp4_terms).  The
+quantiser is checked bit for bit against a numpy restatement of its rule, the
+layer against the oracle at the path's tolerance (max|y-ref|/max|ref| <= 1e-3,
+cosine >= 0.99999)."""
 import ctypes as C
 
 import numpy as np
@@ -50,13 +52,13 @@ def _e2m1_rne(v):
     return np.where(np.signbit(v), c | 8, c).astype(np.uint8)  # a negative value keeps its sign at 0
 
 
-def quantize_ref(x):
+def quantize_ref(x, terms=4):
     rows, K = x.shape
-    codes = np.zeros((rows, 4, K // 2), np.uint8)
-    scales = np.zeros((rows, 4, K // 16), np.uint8)
-    exps = np.zeros((rows, 4), np.int32)
+    codes = np.zeros((rows, terms, K // 2), np.uint8)
+    scales = np.zeros((rows, terms, K // 16), np.uint8)
+    exps = np.zeros((rows, terms), np.int32)
     r = x.astype(np.float32).copy()
-    for t in range(4):
+    for t in range(terms):
         am = np.abs(r).max(1)
         for i in range(rows):
             e = 0
@@ -82,39 +84,43 @@ def quantize_ref(x):
 
 
 def dequant_terms(codes, scales, exps):
-    rows, _, half = codes.shape
+    rows, terms, half = codes.shape
     K = 2 * half
     lo, hi = codes & 15, codes >> 4
-    c = np.stack([lo, hi], -1).reshape(rows, 4, K)
+    c = np.stack([lo, hi], -1).reshape(rows, terms, K)
     val = np.where(c & 8, -_E2M1[c & 7], _E2M1[c & 7]).astype(np.float64)
     s = _ue4m3_value(scales).astype(np.float64).repeat(16, axis=2)
     return (val * s * np.exp2(exps[..., None].astype(np.float64))).sum(1)
 
 
-def gpu_quantize(ffn, cuda, x):
+def gpu_quantize(ffn, cuda, x, terms=4):
     import torch
     rows, K = x.shape
     xd = torch.from_numpy(x).to(cuda)
-    codes = torch.empty(rows, 4, K // 2, dtype=torch.uint8, device=cuda)
-    scales = torch.empty(rows, 4, K // 16, dtype=torch.uint8, device=cuda)
-    exps = torch.empty(rows, 4, dtype=torch.int32, device=cuda)
+    codes = torch.empty(rows, terms, K // 2, dtype=torch.uint8, device=cuda)
+    scales = torch.empty(rows, terms, K // 16, dtype=torch.uint8, device=cuda)
+    exps = torch.empty(rows, terms, dtype=torch.int32, device=cuda)
     p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
-    ffn.check(ffn.lib().ffn_b200_quantize_nvfp4x4(rows, K, p(xd), K, p(codes), p(scales), p(exps), None),
-              "quantize_nvfp4x4")
+    if terms == 4:
+        rc = ffn.lib().ffn_b200_quantize_nvfp4x4(rows, K, p(xd), K, p(codes), p(scales), p(exps), None)
+    else:
+        rc = ffn.lib().ffn_b200_quantize_nvfp4_terms(rows, K, terms, p(xd), K, p(codes), p(scales), p(exps),
+                                                     None)
+    ffn.check(rc, "quantize_nvfp4")
     torch.cuda.synchronize()
     return host(codes), host(scales), host(exps)
 
 
-@pytest.mark.parametrize("K", [256, 2048, 4096, 7168])
-def test_quantizer_bit_exact_and_accurate(ffn, cuda, K):
+@pytest.mark.parametrize("K,terms", [(256, 4), (2048, 4), (4096, 4), (7168, 4), (2048, 6), (4096, 6)])
+def test_quantizer_bit_exact_and_accurate(ffn, cuda, K, terms):
     rng = np.random.default_rng(K)
     rows = [rng.standard_normal(K), rng.standard_normal(K) * 1e-6, np.zeros(K),
             rng.standard_normal(K) * np.exp(rng.uniform(-12, 12, K)),  # wide dynamic range
             np.where(rng.random(K) < 0.9, 0.0, rng.standard_normal(K) * 50),  # mostly zero
             np.full(K, 3.0), rng.uniform(-100, 100, K)]
     x = np.stack(rows).astype(np.float32)
-    got = gpu_quantize(ffn, cuda, x)
-    want = quantize_ref(x)
+    got = gpu_quantize(ffn, cuda, x, terms)
+    want = quantize_ref(x, terms)
     for g, w, name in zip(got, want, ("codes", "scales", "exponents")):
         assert np.array_equal(g, w), f"{name} differ at {np.argwhere(g != w)[:5]}"
     back = dequant_terms(*got)
@@ -123,13 +129,13 @@ def test_quantizer_bit_exact_and_accurate(ffn, cuda, K):
         if den == 0:
             assert np.all(back[i] == 0)
             continue
-        # element-wise: a single value can keep up to ~max/6^4; dot products average it out
-        assert np.abs(back[i] - x[i]).max() / den < 1e-3, f"row {i}"
+        # element-wise: a single value can keep up to ~max/6^terms; dot products average it out
+        assert np.abs(back[i] - x[i]).max() / den < (1e-3 if terms == 4 else 1e-4), f"row {i}"
 
 
 # ------------------------------------------------------------- the layer
 def _layer(ffn, E, H, I, seed, path, score_fn=None):
-    experts = [ffn.SwigluExpert.generate(ffn.FMT_NVFP4, seed, 0, e, I, H) for e in range(E)]
+    experts = [ffn.SwigluExpert.generate(ffn.FMT_NVFP4, seed, 0, e, I, H).pack_fp4() for e in range(E)]
     wr = ffn.gen_normal(ffn.path_key(seed, 0, 0, ffn.TAG_ROUTER), E * H, 0.02).view(E, H)
     kw = {} if score_fn is None else {"score_fn": score_fn}
     return experts, wr, lambda top_k, p=path: ffn.MoeLayer(experts, wr, H, I, top_k=top_k, path=p, **kw)
@@ -155,8 +161,8 @@ def test_fp4_layer_vs_oracle(oracle, ffn, cuda, E, H, I, T, K):
 @pytest.mark.parametrize("mode", ["exact", "tensor"])
 def test_fp4_layer_with_ffn_norm(oracle, ffn, cuda, mode):
     """The reference's ffn_norm before routing (RMSNorm, flash1017.rs:7637): on
-    the FP4 path the norm, the router's f16 split and the experts' four NVFP4
-    terms come from one kernel (xq_kernel).  With the exact router the norm's
+    the FP4 path the norm, the router's f16 split and the experts' NVFP4 terms
+    come from one kernel (xq_kernel).  With the exact router the norm's
     sum runs in the reference's order, so the top-6 sets match the oracle's
     exactly; the tensor router may differ only at near-ties."""
     import torch
@@ -194,22 +200,69 @@ def test_fp4_matches_gemv_path_and_is_deterministic(oracle, ffn, cuda):
 
 
 def test_fp4_rejects_scales_outside_ue4m3(oracle, ffn, cuda):
-    """A scale byte with the sign bit set is not a UE4M3 value: the layer's
-    outputs are NaN (the failure is visible), and the next call is clean."""
+    """A scale byte with the sign bit set (or the E4M3 NaN 0x7F) is not a UE4M3
+    value: packing refuses the expert, so the FP4 path never sees it, and the
+    layer of unpacked experts runs on the GEMV slices (which decode E4M3)."""
+    import torch
     E, H, I, T, K = 8, 512, 256, 6, 6
-    experts, wr, make = _layer(ffn, E, H, I, 93, ffn.PATH_FP4)
+    experts = [ffn.SwigluExpert.generate(ffn.FMT_NVFP4, 93, 0, e, I, H) for e in range(E)]
+    for bad in (0xB8, 0x7F):  # -1.0 in E4M3, NaN
+        s = experts[3].mats[0].s
+        keep = s[5].clone()
+        s[5] = bad
+        with pytest.raises(ffn.FfnError, match="UE4M3"):
+            experts[3].pack_fp4()
+        s[5] = keep
+    assert experts[3].fp4 is None
+    wr = ffn.gen_normal(ffn.path_key(93, 0, 0, ffn.TAG_ROUTER), E * H, 0.02).view(E, H)
     x = ffn.gen_normal(ffn.path_key(93, 0, 0, ffn.TAG_X), T * H).view(T, H)
-    layer = make(K)
-    good = host(layer.forward(x))
-    assert np.isfinite(good).all()
-    s = experts[3].mats[0].s
-    keep = s[5].clone()
-    s[5] = 0xB8  # -1.0 in E4M3
-    bad = host(make(K).forward(x))
-    s[5] = keep
-    assert np.isnan(bad).all()
-    again = host(make(K).forward(x))
-    assert np.array_equal(again, good)
+    with pytest.raises(ffn.FfnError, match="packed"):
+        ffn.MoeLayer(experts, wr, H, I, top_k=K, path=ffn.PATH_FP4).forward(x)
+    ffn.profile_enable(True)
+    out = host(ffn.MoeLayer(experts, wr, H, I, top_k=K).forward(x))
+    torch.cuda.synchronize()
+    prof = ffn.profile_read()
+    ffn.profile_enable(False)
+    assert "gateup_nvfp4" in prof and "fp4_gateup" not in prof and np.isfinite(out).all()
+
+
+def test_fp4_stage_images(oracle, ffn, cuda):
+    """ffn_b200_pack_nvfp4_expert against a numpy restatement of the layout:
+    stage (row block, K step) = both blocks' 128-byte-swizzled code tiles, then
+    their scale atoms (line l = rows l, l+32, l+64, l+96)."""
+    H, I = 512, 768
+    ex = ffn.SwigluExpert.generate(ffn.FMT_NVFP4, 97, 0, 0, I, H).pack_fp4()
+    gu, dn = host(ex.fp4[0]), host(ex.fp4[1])
+    assert gu.size == ffn.lib().ffn_b200_fp4_pack_bytes(I, H, 0) == 2 * I * (H // 2 + H // 16)
+    assert dn.size == ffn.lib().ffn_b200_fp4_pack_bytes(I, H, 1) == H * (I // 2 + I // 16)
+    w = [host(m.w).reshape(m.rows, m.cols // 2) for m in ex.mats]
+    s = [host(m.s).reshape(m.rows, m.cols // 16) for m in ex.mats]
+
+    def image(wa, sa, ra, wb, sb, rb_, kt):
+        img = np.zeros(36864, dtype=np.uint8)
+        for blk, (ww, ss, r0) in enumerate(((wa, sa, ra), (wb, sb, rb_))):
+            for r in range(128):
+                for c in range(8):
+                    off = blk * 16384 + (r // 8) * 1024 + (r % 8) * 128 + ((c ^ (r % 8)) * 16)
+                    img[off:off + 16] = ww[r0 + r, kt * 128 + c * 16: kt * 128 + c * 16 + 16]
+            for k in range(4):
+                for l in range(32):
+                    off = 32768 + blk * 2048 + k * 512 + l * 16
+                    for q in range(4):
+                        img[off + 4 * q: off + 4 * q + 4] = ss[r0 + l + 32 * q, kt * 16 + 4 * k: kt * 16 + 4 * k + 4]
+        return img
+
+    kt_h, kt_i = H // 256, I // 256
+    for rb in (0, I // 128 - 1):
+        for kt in (0, kt_h - 1):
+            want = image(w[0], s[0], rb * 128, w[1], s[1], rb * 128, kt)
+            got = gu[(rb * kt_h + kt) * 36864:(rb * kt_h + kt + 1) * 36864]
+            np.testing.assert_array_equal(got, want)
+    for rb in (0, H // 256 - 1):
+        for kt in (0, kt_i - 1):
+            want = image(w[2], s[2], rb * 256, w[2], s[2], rb * 256 + 128, kt)
+            got = dn[(rb * kt_i + kt) * 36864:(rb * kt_i + kt + 1) * 36864]
+            np.testing.assert_array_equal(got, want)
 
 
 def test_fp4_config2_all_tokens(oracle, ffn, cuda):

@@ -10,9 +10,11 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-def _layer(F, E, H, I, seed, path, expert_range=None, top_k=6):
+def _layer(F, E, H, I, seed, path, expert_range=None, top_k=6, pack=False):
     import torch
     experts = [F.SwigluExpert.generate(F.FMT_NVFP4, seed, 0, e, I, H) for e in range(E)]
+    if pack:
+        experts = [e.pack_fp4() for e in experts]
     wr = F.gen_normal(F.path_key(seed, 0, 0, F.TAG_ROUTER), E * H, 0.02).view(E, H)
     nw = torch.ones(H, device="cuda")
     return experts, wr, F.MoeLayer(experts, wr, H, I, top_k=top_k, router_mode=F.ROUTER_TENSOR,
@@ -69,12 +71,21 @@ def test_grouped_matches_gemv_path(ffn, oracle, cuda, E, T, rng):
 
 def test_grouped_auto_selection(ffn, cuda):
     """AUTO picks the grouped path only at >= GROUPED_MIN_PAIRS pairs per expert
-    (below: the block-scaled FP4 path for this NVFP4 layer); a ternary layer or
-    odd dims are refused by PATH_GROUPED."""
+    (below: the block-scaled FP4 path for this packed NVFP4 layer, the GEMV
+    slices when it is not packed); a ternary layer or odd dims are refused by
+    PATH_GROUPED."""
     import torch
     F = ffn
     E, H, I = 8, 512, 256
-    experts, wr, lay = _layer(F, E, H, I, 35, F.PATH_AUTO)
+    experts, wr, lay = _layer(F, E, H, I, 35, F.PATH_AUTO, pack=True)
+    _, _, plain = _layer(F, E, H, I, 35, F.PATH_AUTO)
+    x = F.gen_normal(F.path_key(35, 0, 0, F.TAG_X), 8 * H).view(8, H)
+    F.profile_enable(True)
+    plain.forward(x)
+    torch.cuda.synchronize()
+    prof = F.profile_read()
+    F.profile_enable(False)
+    assert "gateup_nvfp4" in prof and "fp4_gateup" not in prof
     te = [F.SwigluExpert.generate(F.FMT_TERNARY, 35, 0, e, I, H) for e in range(E)]
     lt = F.MoeLayer(te, wr, H, I, top_k=6, router_mode=F.ROUTER_TENSOR, path=F.PATH_GROUPED)
     x = F.gen_normal(F.path_key(35, 0, 0, F.TAG_X), 64 * H).view(64, H)

@@ -347,8 +347,11 @@ def run_ours(a):
         torch.cuda.empty_cache()
     free, _ = torch.cuda.mem_get_info(dev)
     reserve = 4 << 30
-    # NVFP4 layers also hold their stage images (the FP4 path's copy of the same bytes)
-    per_layer = (2 if not tern else 1) * layer_bytes + 512 * e_loc
+    # NVFP4 layers on the FP4 path hold only their stage images (the same bytes;
+    # the reference layout is generated into a scratch expert and packed); the
+    # GEMV path keeps the reference layout
+    images = not tern and path != F.PATH_GEMV
+    per_layer = layer_bytes + 512 * e_loc
     resident = max(1, min(L, (free - reserve - L * E * H * 4) // per_layer))
     if a.max_resident:
         resident = min(resident, a.max_resident)
@@ -364,13 +367,12 @@ def run_ours(a):
     gen = torch.Generator(device=dev)
     gu_b = F.lib().ffn_b200_fp4_pack_bytes(I, H, 0)
     dn_b = F.lib().ffn_b200_fp4_pack_bytes(I, H, 1)
+    scratch = torch.empty(3 * (n1 + n1s), dtype=torch.uint8, device=dev) if images else None
     for lay in range(resident):
-        buf = torch.empty(layer_bytes + 512 * e_loc, dtype=torch.uint8, device=dev)
+        # the layer's stage images, one buffer carved per expert; or the reference layout
+        buf = torch.empty(e_loc * (gu_b + dn_b) if images else layer_bytes + 512 * e_loc,
+                          dtype=torch.uint8, device=dev)
         buffers.append(buf)
-        # the layer's stage images, one buffer carved per expert
-        img = None if tern else torch.empty(e_loc * (gu_b + dn_b), dtype=torch.uint8, device=dev)
-        if img is not None:
-            buffers.append(img)
         experts = [None] * E
         off = 0
 
@@ -383,6 +385,11 @@ def run_ours(a):
 
         for j in range(e_loc):
             e = e_lo + j
+            if images:
+                experts[e] = packed_expert(F, a.seed, lay, e, I, H, scratch,
+                                           buf.narrow(0, j * (gu_b + dn_b), gu_b),
+                                           buf.narrow(0, j * (gu_b + dn_b) + gu_b, dn_b))
+                continue
             mats = []
             for tag, (r, c) in zip((F.TAG_W1, F.TAG_W3, F.TAG_W2), ((I, H), (I, H), (H, I))):
                 k = F.path_key(a.seed, lay, e, tag)
@@ -409,9 +416,6 @@ def run_ours(a):
                                        generator=gen))
                 mats.append(F.TernaryMatrix(p, rs, r, c, core=(ca, cas, cb, cbs), bs=bs))
             experts[e] = F.SwigluExpert(F.FMT_TERNARY if tern else F.FMT_NVFP4, mats, I, H)
-            if not tern:
-                o = j * (gu_b + dn_b)
-                experts[e].pack_fp4(img.narrow(0, o, gu_b), img.narrow(0, o + gu_b, dn_b))
         tables.append((experts, F.expert_table(experts, dev)))
     routers = [F.gen_normal(F.path_key(a.seed, lay, 0, F.TAG_ROUTER), E * H, 0.02).view(E, H)
                for lay in range(L)]
@@ -586,7 +590,8 @@ def run_ours(a):
         if rank == 0:
             cur = x0
             for lay in range(2):
-                full = [F.SwigluExpert.generate(F.FMT_NVFP4, a.seed, lay, e, I, H).pack_fp4() for e in range(E)]
+                sc = torch.empty(3 * (n1 + n1s), dtype=torch.uint8, device=dev)
+                full = [packed_expert(F, a.seed, lay, e, I, H, sc) for e in range(E)]
                 lf = F.MoeLayer(full, routers[lay], H, I, top_k=K, score_fn=F.SCORE_SIGMOID, norm_w=norm_w,
                                 norm_eps=1e-20, router_mode=F.ROUTER_TENSOR, path=path)
                 cur = lf.forward(cur, residual=cur)
@@ -848,6 +853,27 @@ def _traffic_per_launch(kind, alg_bytes_per_launch):
         return alg_bytes_per_launch * float(d["traffic_over_algorithmic"])
     except (OSError, KeyError, ValueError):
         return None
+
+
+def packed_expert(F, seed, layer, expert, I, H, scratch, gu=None, dn=None):
+    """An NVFP4 expert of the stack as the FP4 path holds it: the seeded
+    reference layout generated into `scratch` (reused), packed into stage
+    images (gu / dn, or new tensors); the expert keeps only the images and its
+    global scales (its reference-layout pointers are NULL, so a layer of such
+    experts runs only the FP4 path)."""
+    n1, n1s = I * H // 2, I * H // 16
+    mats = []
+    off = 0
+    for tag, (r, c) in zip((F.TAG_W1, F.TAG_W3, F.TAG_W2), ((I, H), (I, H), (H, I))):
+        w, s = scratch.narrow(0, off, n1), scratch.narrow(0, off + n1, n1s)
+        off += n1 + n1s
+        F.check(F.lib().ffn_b200_gen_nvfp4(F.path_key(seed, layer, expert, tag), r, c, w.data_ptr(),
+                                           s.data_ptr(), F._stream()), "gen_nvfp4")
+        mats.append(F.Nvfp4Matrix(w, s, 1.0, r, c))
+    ex = F.SwigluExpert(F.FMT_NVFP4, mats, I, H).pack_fp4(gu, dn)
+    for m in ex.mats:
+        m.w = m.s = None
+    return ex
 
 
 def _path_code(a):

@@ -729,6 +729,13 @@ class MoeLayer:
             self.table, fmts = expert_table(experts, device)
         else:  # a shared (table, formats) pair
             self.table, fmts = table
+        # experts kept only as stage images (reference-layout pointers NULL) can
+        # run nowhere but the FP4 path
+        if any(e is not None and e.mats is not None and any(getattr(m, "w", 0) is None for m in e.mats)
+               for e in experts):
+            if path not in (PATH_AUTO, PATH_FP4):
+                raise FfnError("experts held only as FP4 stage images run only on PATH_FP4")
+            path = PATH_FP4
         lo, hi = expert_range if expert_range else (0, n)
         # the FP4 path reads stage images: every local expert must carry them
         # (the table must have been built after pack_fp4)

@@ -631,7 +631,7 @@ def run_ours(a):
     if rank == 0:
         cfg = base_config(a, world, resident)
         cfg["exchange"] = exch_used
-        cfg["expert_path"] = ("tcgen05 block-scaled FP4 (kind::mxf4nvf4), activations as 4 NVFP4 terms"
+        cfg["expert_path"] = ("tcgen05 block-scaled FP4 (kind::mxf4nvf4), activations as 6 NVFP4 terms"
                               if fp4 else "warp GEMV slices, f16x2 activations")
         cfg["experts_hit_per_layer_rank0"] = u_loc
         cfg["weight_bytes_per_step_rank0"] = weight_bytes_step
@@ -641,7 +641,7 @@ def run_ours(a):
             "scaling": "strong", "vs_baseline": None,
             "dtype": ("ternary (block-64 U8 scales, rank-16 Q8 core) weights x f16x2 split "
                       "activations, f32 accumulate" if tern else
-                      "nvfp4 weights x 4-term nvfp4 activations (tcgen05 block-scaled FP4 MMA), f32 "
+                      "nvfp4 weights x 6-term nvfp4 activations (tcgen05 block-scaled FP4 MMA), f32 "
                       "accumulate" if fp4 else
                       "nvfp4 weights x f16x2 split activations, f32 accumulate"),
             "data": "synthetic (seeded random-init weights and N(0,1) hidden states)",

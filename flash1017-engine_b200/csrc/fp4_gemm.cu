@@ -87,11 +87,14 @@ static_assert(OFF_B % 1024 == 0 && STAGE % 1024 == 0, "swizzled tiles need 1024-
 static_assert(SMEM <= 227 * 1024, "shared memory");
 
 // TMEM: two accumulator buffers of 2 blocks x kNMax f32 columns, then two
-// scale-factor slots (SFA: 2 blocks x 4 K-steps x 4 columns; SFB: 4 x 4)
-constexpr int kAccCols = 2 * kNMax;
-constexpr int kSfCols = 2 * 16 + 16;
+// scale-factor slots (SFA: 2 blocks x 4 K-steps x 4 columns; SFB: 4 x 4);
+// every accumulator and slot starts on a 64-column boundary
+constexpr int kAccStride = 64;            // columns per block accumulator (kNMax used)
+constexpr int kAccCols = 2 * kAccStride;
+constexpr int kSfCols = 64;               // slot stride (48 used)
 constexpr int kSf0 = 2 * kAccCols;
 constexpr int kTmemCols = 512;
+static_assert(kNMax <= kAccStride && 2 * 16 + 16 <= kSfCols, "TMEM layout");
 static_assert(kSf0 + 2 * kSfCols <= kTmemCols, "TMEM");
 
 // A chunk = the grouping kernel's slice of one expert's routed pairs
@@ -266,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
           for (int k = 0; k < 4; ++k)
 #pragma unroll
             for (int mi = 0; mi < 2; ++mi)
-              tc::mma_nvf4(acc + mi * kNMax, tc::desc_sw128(ab + mi * (kTileM * 128) + 32 * k),
+              tc::mma_nvf4(acc + mi * kAccStride, tc::desc_sw128(ab + mi * (kTileM * 128) + 32 * k),
                            tc::desc_sw128(bb + 32 * k), id, sf + 16 * mi + 4 * k, sf + 32 + 4 * k,
                            (kt > 0 || k > 0) ? 1u : 0u);
           tc::commit(&empty[s]);
@@ -305,8 +308,8 @@ __global__ void __launch_bounds__(kThreads, 1) fp4_gemm_kernel(const GemmArgs a)
       static_assert(kNMax == 48, "the epilogue reads 32 + 16 columns per block");
       tc::ld32(tl, *reinterpret_cast<uint32_t(*)[32]>(v0));
       tc::ld16(tl + 32, v0 + 32);
-      tc::ld32(tl + kNMax, *reinterpret_cast<uint32_t(*)[32]>(v1));
-      tc::ld16(tl + kNMax + 32, v1 + 32);
+      tc::ld32(tl + kAccStride, *reinterpret_cast<uint32_t(*)[32]>(v1));
+      tc::ld16(tl + kAccStride + 32, v1 + 32);
       tc::wait_ld();
       const ffn_b200_expert &E = a.experts[ch.expert];
       const float gs0 = E.nv[PH == 1 ? 0 : 2].gs, gs1 = E.nv[PH == 1 ? 1 : 2].gs;

@@ -170,11 +170,15 @@ FFN_B200_EXPORT int ffn_b200_expert_forward(size_t inter, size_t hidden, size_t 
  * point has no counterpart in the reference.  It uses a fixed 1 MiB scratch
  * array that the library keeps on every GPU that loads it until the process
  * exits, and calls no allocator.  Shapes that need more scratch than 1 MiB
- * (ffn_b200_expert_ws_bytes) are rejected with FFN_B200_EINVAL.  The first
- * call on a device looks up the array's device address, so make that first
- * call before any stream capture.  All calls share the one array: calls whose
- * work overlaps on the GPU (different streams, or different host threads)
- * race on it and must be serialised by the caller. */
+ * (ffn_b200_expert_ws_bytes) are rejected with FFN_B200_EINVAL.  Before any
+ * stream capture, make one call per device and per weight format the captured
+ * code will use (NVFP4, MXFP4, ternary, MXFP8): the first call on a device looks
+ * up the array's device address, and the first call of a format sets its
+ * kernels' shared-memory attribute; neither may run under capture.  The
+ * address is cached per device index for the process, so it assumes one CUDA
+ * context per device (no cudaDeviceReset between calls).  All calls share the
+ * one array: calls whose work overlaps on the GPU (different streams, or
+ * different host threads) race on it and must be serialised by the caller. */
 FFN_B200_EXPORT int ffn_b200_expert_forward_noalloc(size_t inter, size_t hidden, size_t seq,
                                                     const ffn_b200_expert *e, const float *x,
                                                     float *out, float accum_weight,
@@ -421,7 +425,12 @@ FFN_B200_EXPORT int ffn_b200_st_load_expert(const ffn_b200_st *st, const char *p
  * core_b [rows, 16] / core_b_sc [16] / core_a [16, cols] / core_a_sc [16] of
  * the residual (seed: the reference's subspace-iteration seed).  The outputs
  * are exactly the tensors ffn_b200_ternary_mat reads.  Device pointers, caller
- * workspace, enqueued on `stream`. */
+ * workspace, enqueued on `stream`.  The reference function also returns the
+ * squared Frobenius norms of the matrix, of its ternary error and of the error
+ * left after the core (its shard writer reports their ratio,
+ * flash1017.rs:10747-10768); this entry point does not: a caller that wants
+ * them decodes both forms (ffn_b200_dequant_nvfp4, ffn_b200_ternary_matvec on
+ * unit vectors or the dequantised ternary) and sums the squares itself. */
 FFN_B200_EXPORT size_t ffn_b200_compress_ws_bytes(size_t rows, size_t cols);
 FFN_B200_EXPORT int ffn_b200_compress_ternary_b64(size_t rows, size_t cols, const uint8_t *w,
                                                   const uint8_t *s, float gs, uint64_t seed,

@@ -1363,6 +1363,129 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t *__restrict__
   if (tid == 0) { n_vexp[0] = s_tot[0]; n_vexp[1] = s_tot[1]; }
 }
 
+// The same groups from per-expert token bitmaps, for up to 32 x 32 tokens:
+// bit t of expert e's words = token t routed to e.  A token picks an expert at
+// most once, so a pair's position is its expert's offset plus the number of
+// the expert's tokens before its own: the pair order of the linear scan.  (A
+// token listed twice for one expert by a caller would get one row for both
+// pairs, whose outputs are equal, so the weighted sum is unchanged.)
+constexpr int kGroupBitsMaxWords = 32;
+__global__ void __launch_bounds__(1024) group_bits_kernel(const int32_t *__restrict__ idx, int n_tok,
+                                                          int top_k, int n_exp, int e_begin, int e_end,
+                                                          const ffn_b200_expert *__restrict__ experts,
+                                                          int *counts, int *offsets, int *vbase,
+                                                          int32_t *pair_tok, int32_t *inv, VExp *vexp_nv,
+                                                          VExp *vexp_tn, int *n_vexp) {
+  extern __shared__ uint32_t gb_smem[];
+  const int W = (n_tok + 31) >> 5;
+  uint32_t *bm = gb_smem;                               // [n_exp][W]
+  int *s_counts = reinterpret_cast<int *>(bm + (size_t)n_exp * W);
+  int *s_off = s_counts + n_exp;
+  int *s_nv = s_off + n_exp;
+  int *s_vb = s_nv + n_exp;
+  __shared__ int s_tot[2];
+  __shared__ int ws_p[32], ws_n[32], ws_t[32];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  // nothing here depends on the previous kernel: runs while it finishes
+  for (int i = tid; i < n_exp * W; i += blockDim.x) bm[i] = 0u;
+  for (int e = tid; e < n_exp; e += blockDim.x) s_nv[e] = experts[e].format != FFN_B200_FMT_TERNARY;
+  pdl_enter();
+  __syncthreads();
+  const int n_pairs = n_tok * top_k;
+  for (int q = tid; q < n_pairs; q += blockDim.x) {
+    const int e = idx[q];
+    if (e >= e_begin && e < e_end) {
+      const int t = q / top_k;
+      atomicOr(&bm[e * W + (t >> 5)], 1u << (t & 31));
+    }
+  }
+  __syncthreads();
+  for (int e = tid; e < n_exp; e += blockDim.x) {
+    int c = 0;
+    for (int w = 0; w < W; ++w) c += __popc(bm[e * W + w]);
+    s_counts[e] = c;
+  }
+  __syncthreads();
+  // each thread owns a contiguous run of `per` experts; block-wide exclusive
+  // scans of the pairs and of the two slice lists
+  const int per = (n_exp + blockDim.x - 1) / blockDim.x;
+  int loc_pairs = 0, loc_nv = 0, loc_tn = 0;
+  for (int i = 0; i < per; ++i) {
+    const int e = tid * per + i;
+    if (e < n_exp) {
+      const int c = s_counts[e], sl = (c + kNTok - 1) / kNTok;
+      loc_pairs += c;
+      if (s_nv[e]) loc_nv += sl; else loc_tn += sl;
+    }
+  }
+  int inc_p = loc_pairs, inc_n = loc_nv, inc_t = loc_tn;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int x1 = __shfl_up_sync(0xffffffffu, inc_p, o);
+    const int x2 = __shfl_up_sync(0xffffffffu, inc_n, o);
+    const int x3 = __shfl_up_sync(0xffffffffu, inc_t, o);
+    if (lane >= o) { inc_p += x1; inc_n += x2; inc_t += x3; }
+  }
+  if (lane == 31) { ws_p[wid] = inc_p; ws_n[wid] = inc_n; ws_t[wid] = inc_t; }
+  __syncthreads();
+  if (wid == 0) {
+    const int nw = blockDim.x >> 5;
+    int x1 = lane < nw ? ws_p[lane] : 0, x2 = lane < nw ? ws_n[lane] : 0, x3 = lane < nw ? ws_t[lane] : 0;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y1 = __shfl_up_sync(0xffffffffu, x1, o);
+      const int y2 = __shfl_up_sync(0xffffffffu, x2, o);
+      const int y3 = __shfl_up_sync(0xffffffffu, x3, o);
+      if (lane >= o) { x1 += y1; x2 += y2; x3 += y3; }
+    }
+    ws_p[lane] = x1; ws_n[lane] = x2; ws_t[lane] = x3;
+    if (lane == 31) { s_tot[0] = x2; s_tot[1] = x3; }
+  }
+  __syncthreads();
+  int base_p = (wid ? ws_p[wid - 1] : 0) + inc_p - loc_pairs;
+  int base_n = (wid ? ws_n[wid - 1] : 0) + inc_n - loc_nv;
+  int base_t = (wid ? ws_t[wid - 1] : 0) + inc_t - loc_tn;
+  for (int i = 0; i < per; ++i) {
+    const int e = tid * per + i;
+    if (e < n_exp) {
+      const int c = s_counts[e], sl = (c + kNTok - 1) / kNTok;
+      counts[e] = c;
+      offsets[e] = base_p;
+      s_off[e] = base_p;
+      base_p += c;
+      const int vb = s_nv[e] ? base_n : base_t;
+      vbase[e] = vb;
+      s_vb[e] = vb;
+      if (s_nv[e]) base_n += sl; else base_t += sl;
+    }
+  }
+  __syncthreads();
+  for (int q = tid; q < n_pairs; q += blockDim.x) {
+    const int e = idx[q];
+    if (e >= e_begin && e < e_end) {
+      const int t = q / top_k, w = t >> 5;
+      const uint32_t *row = bm + e * W;
+      int pos = s_off[e] + __popc(row[w] & ((1u << (t & 31)) - 1u));
+      for (int w2 = 0; w2 < w; ++w2) pos += __popc(row[w2]);
+      pair_tok[pos] = t;
+      inv[q] = pos;
+    } else {
+      inv[q] = -1;
+    }
+  }
+  for (int e = tid; e < n_exp; e += blockDim.x) {
+    const int c = s_counts[e];
+    VExp *dst = s_nv[e] ? vexp_nv : vexp_tn;  // NVFP4, MXFP4 | ternary
+    for (int j = 0; j * kNTok < c; ++j) {
+      VExp v;
+      v.expert = e;
+      v.offset = s_off[e] + j * kNTok;
+      v.count = min(kNTok, c - j * kNTok);
+      v.pad = 0;
+      dst[s_vb[e] + j] = v;
+    }
+  }
+  if (tid == 0) { n_vexp[0] = s_tot[0]; n_vexp[1] = s_tot[1]; }
+}
+
 int launch_group(const int32_t *idx, int n_tok, int top_k, int n_exp, int e_begin, int e_end,
                  const ffn_b200_expert *experts, int *ws_int, int32_t *pair_tok, int32_t *inv,
                  VExp *vexp_nv, VExp *vexp_tn, int *n_vexp, cudaStream_t st) {
@@ -1375,6 +1498,17 @@ int launch_group(const int32_t *idx, int n_tok, int top_k, int n_exp, int e_begi
   if (!attr_set[dev]) {
     FFN_CUDA_TRY(cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     attr_set[dev] = true;
+  }
+  const int words = (n_tok + 31) / 32;
+  const size_t smem_bits = ((size_t)n_exp * words + 4 * (size_t)n_exp) * sizeof(int);
+  if (words <= kGroupBitsMaxWords && smem_bits <= 200 * 1024) {
+    static bool bits_attr[64] = {false};
+    if (!bits_attr[dev]) {
+      FFN_CUDA_TRY(cudaFuncSetAttribute(group_bits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+      bits_attr[dev] = true;
+    }
+    FFN_LAUNCH_PDL(FFN_B200_K_GROUP, st, "group_bits_kernel", group_bits_kernel, 1, 1024, smem_bits, idx, n_tok, top_k, n_exp, e_begin, e_end, experts, ws_int, ws_int + n_exp, ws_int + 3 * n_exp, pair_tok, inv, vexp_nv, vexp_tn, n_vexp);
+    return 0;
   }
   FFN_LAUNCH_PDL(FFN_B200_K_GROUP, st, "group_kernel", group_kernel, 1, 1024, smem, idx, n_tok * top_k, top_k, n_exp, e_begin, e_end, experts, ws_int, ws_int + n_exp, ws_int + 2 * n_exp, ws_int + 3 * n_exp, pair_tok, inv, vexp_nv, vexp_tn, n_vexp);
   return 0;

@@ -961,8 +961,12 @@ def run_expert(a):
     t1.record()
     torch.cuda.synchronize()
     launches = F.launch_count() - n0
+    ms_eager = t0.elapsed_time(t1)
+    # the same pass captured once in a CUDA graph and replayed: the library's
+    # launches back to back, without the Python call overhead between them
+    gms = _graph_ms(step, a.steps, a.warmup)
     clk = clocks.stop()
-    ms = t0.elapsed_time(t1)
+    ms = gms * a.steps if gms is not None else ms_eager
     fwd = P * a.steps
     value = fwd / (ms * 1e-3)
     us_fwd = ms * 1e3 / fwd
@@ -1022,12 +1026,17 @@ def run_expert(a):
         "metric": metric_of(a), "value": value, "unit": "expert forwards/s", "n_gpus": 1,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None,
-        "dtype": f"{fmt} weights x f16x2 split activations, f32 accumulate",
+        "dtype": (f"{fmt} weights x f32 activations, f32 accumulate (CUDA-core decode kernels)"
+                  if fmt in ("nvfp4", "mxfp4") and T <= 8 else
+                  f"{fmt} weights x f16x2 split activations, f32 accumulate"),
         "data": "synthetic (seeded random-init weights and N(0,1) hidden states)",
         "config": {"workload": f"one SwiGLU expert ({fmt}), {T} token(s), pool of {P} experts "
                                f"({P * ebytes / 1e9:.2f} GB > 126 MB L2)",
                    "hidden": H, "inter": I, "tokens": T, "pool": P, "seed": a.seed,
-                   "l2": "no flush: the pool exceeds L2, every forward reads its weights from HBM"},
+                   "l2": "no flush: the pool exceeds L2, every forward reads its weights from HBM",
+                   "timing": ("CUDA graph of one pass over the pool, replayed; eager calls: "
+                              f"{ms_eager * 1e3 / fwd:.2f} us per forward") if gms is not None
+                             else "eager calls"},
         "e2e": {"value": e2e, "unit": "expert forwards/s", "h2d_bytes_per_step": T * H * 4,
                 "d2h_bytes_per_step": T * H * 4},
         "gpu_launches": launches,
@@ -1063,6 +1072,29 @@ def _event_ms(step, steps, warmup):
     t1.record()
     torch.cuda.synchronize()
     return t0.elapsed_time(t1) / steps
+
+
+def _graph_ms(step, steps, warmup):
+    """Device ms per step with step() captured once in a CUDA graph and replayed
+    (the library's own launches, without the Python call overhead between
+    them); None when the capture fails."""
+    import torch
+    try:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        ms = _event_ms(g.replay, steps, warmup)
+        del g
+        return ms
+    except Exception:  # noqa: BLE001 -- capture unsupported: eager timing stands
+        torch.cuda.synchronize()
+        return None
 
 
 def _cpu_rate(fn, seconds):
@@ -1104,14 +1136,18 @@ def _sub_expert(a, F, dev, fmt, seed, cpu_s):
         for ex in experts:
             ex.forward(x, out=out, weight=1.0, accumulate=True)
 
-    ms = _event_ms(step, 20, 3)
-    us = ms * 1e3 / pool
+    us_eager = _event_ms(step, 20, 3) * 1e3 / pool
+    gms = _graph_ms(step, 20, 3)
+    us = gms * 1e3 / pool if gms is not None else us_eager
     ebytes = sum(_expert_mat_bytes(fmt, r, c) for r, c in ((I, H), (I, H), (H, I)))
     peak, src = _peaks()
     gbs = ebytes / (us * 1e-6) / 1e9
     rec = {"workload": f"config{1 if tern else 0}: one {'ternary + rank-16 Q8 core' if tern else 'NVFP4'} "
                        f"SwiGLU expert, batch-1 decode, H {H}, I {I}, seed {seed}, pool of {pool} experts",
            "metric": "expert forwards/s", "value": 1e6 / us, "us_per_forward": us,
+           "timing": ("CUDA graph of one pass over the pool (64 ffn_b200_expert_forward calls), replayed"
+                      if gms is not None else "eager calls"),
+           "us_per_forward_eager": us_eager,
            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                         "peak_source": src, "algorithmic_bytes_per_forward": ebytes}}
     y = _host(experts[0].forward(x))[0]

@@ -492,6 +492,17 @@ static int check_expert(const ffn_b200_expert &e, size_t inter, size_t hidden, c
   return 0;
 }
 
+// The two-launch decode kernels for NVFP4 / MXFP4 experts over <= 8 tokens;
+// FFN_B200_EXPERT_DECODE=0 in the environment keeps such calls on the GEMV
+// phase kernels (read once per process).
+static bool expert_decode_enabled() {
+  static const bool on = [] {
+    const char *v = getenv("FFN_B200_EXPERT_DECODE");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 int ffn_b200_expert_forward(size_t inter, size_t hidden, size_t seq, const ffn_b200_expert *e,
                             const float *x, float *out, float accum_weight, int accumulate,
                             void *ws, size_t ws_bytes, void *stream) {
@@ -504,6 +515,10 @@ int ffn_b200_expert_forward(size_t inter, size_t hidden, size_t seq, const ffn_b
   if (!ws || ws_bytes < ffn_b200_expert_ws_bytes(inter, hidden, seq))
     return fail(FFN_B200_ENOSPC, "expert_forward: workspace too small (see ffn_b200_expert_ws_bytes)");
   cudaStream_t st = (cudaStream_t)stream;
+  if (expert_decode_enabled() && expert_decode_fits(*e, inter, hidden, seq) &&
+      ws_bytes >= expert_decode_ws_bytes(inter, seq) && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(out) & 15) == 0 && (reinterpret_cast<uintptr_t>(ws) & 15) == 0)
+    return launch_expert_decode(*e, inter, hidden, seq, x, out, accum_weight, accumulate, ws, st);
   const int fmt = kfam(e->format);  // kernel family
   const bool tern = fmt == FFN_B200_FMT_TERNARY;
   Carve c(ws);

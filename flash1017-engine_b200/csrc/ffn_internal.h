@@ -80,6 +80,14 @@ struct Fp4Args {
   int *err;                     // device int: 1 timed-out wait, 3 an expert without stage images
 };
 int launch_fp4_moe(const Fp4Args &g, cudaStream_t st);
+
+// One NVFP4 / MXFP4 SwiGLU expert over 1..8 tokens in two launches
+// (expert_decode.cu).  fits: the format, shapes, alignment and shared-memory
+// budget the kernels take; ws holds h [seq][inter] f32 (16-byte aligned).
+bool expert_decode_fits(const ffn_b200_expert &e, size_t inter, size_t hidden, size_t seq);
+size_t expert_decode_ws_bytes(size_t inter, size_t seq);
+int launch_expert_decode(const ffn_b200_expert &e, size_t inter, size_t hidden, size_t seq, const float *x,
+                         float *out, float accum_weight, int accumulate, void *ws, cudaStream_t st);
 // rows of f32 (K % 256 == 0, K <= 16384, 16-byte aligned rows) -> `terms` NVFP4 terms
 int launch_q4(const float *x, int ld_x, int rows, int K, int terms, uint8_t *qc, uint8_t *qs, int *qe,
               cudaStream_t st);

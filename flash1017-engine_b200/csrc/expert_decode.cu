@@ -51,20 +51,6 @@ static_assert(kMaxBatches * 8 <= 128, "the batch barriers fit the first 128 byte
 constexpr int kMaxTok = 8;
 constexpr size_t kSmemCap = 110 * 1024;  // per CTA: both phases side by side on one SM
 
-struct DecArgs {
-  const uint8_t *w[2];  // codes [rows][K/2]
-  const uint8_t *s[2];  // scales: NVFP4 E4M3 [rows][K/16], MXFP4 E8M0 [rows][K/32]
-  float gs[2];          // NVFP4 matrix scales (MXFP4: unused, the E8M0 scale is exact in f32)
-  int rows, K, T;
-  const float *x;       // [T][ld_x] activations (x; h for phase 2)
-  int ld_x;
-  float *h;             // phase 1 output [T][ld_h]
-  int ld_h;
-  float *y;             // phase 2 output [T][ld_y]
-  int ld_y;
-  float out_w;
-  int accumulate;
-};
 
 __device__ __forceinline__ float e8m0_f32(uint32_t b) {  // flash1017.rs:1049-1057
   return b == 0xFFu ? __int_as_float(0x7FC00000) : (b == 0u ? __int_as_float(0x00400000) : __int_as_float(b << 23));
@@ -88,11 +74,11 @@ struct Layout {
   int nr, sb;              // rows of this CTA, scale bytes per row
   size_t codes[2], scales[2], red, total;
 };
-__host__ __device__ inline Layout layout(int nmat, int nr, int K, int T, bool mx) {
+__host__ __device__ inline Layout layout(int nmat, int nr, int K, int T, bool mx, size_t base = 128) {
   Layout l;
   l.nr = nr;
   l.sb = mx ? K / 32 : K / 16;
-  size_t o = 128;  // barriers
+  size_t o = base;  // after the barriers
   for (int m = 0; m < nmat; ++m) {
     l.codes[m] = o;
     o += (size_t)nr * (K / 2);
@@ -124,54 +110,51 @@ __device__ __forceinline__ float reduce8(float (&v)[8], int lane) {
   return r;
 }
 
-// PHASE 1: gate (matrix 0) and up (matrix 1) -> h.  PHASE 2: down -> y.
-// A warp task = one column chunk (512 columns: a 16-column group per lane) of
-// RB = 8 / TQ rows of one matrix, for TQ tokens whose activations stay in
-// registers; the 8 sums (RB rows x TQ tokens) leave through one halving
-// reduction.  Tokens beyond TQ take further passes over the codes.
-template <int PHASE, bool MX, int TQ>
-__global__ void __launch_bounds__(kThreads, 2) decode_kernel(const DecArgs a) {
-  constexpr int NMAT = PHASE == 1 ? 2 : 1;
-  constexpr int RB = 8 / TQ;
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t *bar = reinterpret_cast<uint64_t *>(smem);
-  __shared__ int s_err;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int r0 = (int)((long long)blockIdx.x * a.rows / gridDim.x);
-  const int r1 = (int)((long long)(blockIdx.x + 1) * a.rows / gridDim.x);
-  const int nr = r1 - r0, K = a.K, T = a.T;
-  const Layout L = layout(NMAT, nr, K, T, MX);
-  const int nb = (nr + kBatchRows - 1) / kBatchRows;
-  const size_t cb = (size_t)K / 2;  // code bytes per row
+// One phase's matrices: gate and up (NMAT 2) or down (NMAT 1).
+struct Phase {
+  const uint8_t *w[2];
+  const uint8_t *s[2];
+  float gs[2];
+  int rows, K;
+};
 
-  if (tid == 0) {
-    s_err = 0;
-    for (int b = 0; b < nb; ++b) tc::bar_init(&bar[b], 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    for (int b = 0; b < nb; ++b) {
-      const int i0 = b * kBatchRows, n = min(kBatchRows, nr - i0);
-      tc::bar_arrive_tx(&bar[b], (uint32_t)(NMAT * n * (cb + L.sb)));
+// Thread 0: arm this CTA's batch barriers of one phase and issue the bulk
+// copies of its rows [r0, r0 + nr) (barriers initialised and fenced already).
+template <int NMAT>
+__device__ __forceinline__ void issue_rows(const Phase &p, uint8_t *smem, const Layout &L, uint64_t *bar, int r0,
+                                           int nr) {
+  const size_t cb = (size_t)p.K / 2;
+  const int nb = (nr + kBatchRows - 1) / kBatchRows;
+  for (int b = 0; b < nb; ++b) {
+    const int i0 = b * kBatchRows, n = min(kBatchRows, nr - i0);
+    tc::bar_arrive_tx(&bar[b], (uint32_t)(NMAT * n * (cb + L.sb)));
 #pragma unroll
-      for (int m = 0; m < NMAT; ++m) {
-        tc::bulk_g2s(smem + L.codes[m] + i0 * cb, a.w[m] + (size_t)(r0 + i0) * cb, (uint32_t)(n * cb), &bar[b]);
-        tc::bulk_g2s(smem + L.scales[m] + (size_t)i0 * L.sb, a.s[m] + (size_t)(r0 + i0) * L.sb,
-                     (uint32_t)(n * L.sb), &bar[b]);
-      }
+    for (int m = 0; m < NMAT; ++m) {
+      tc::bulk_g2s(smem + L.codes[m] + i0 * cb, p.w[m] + (size_t)(r0 + i0) * cb, (uint32_t)(n * cb), &bar[b]);
+      tc::bulk_g2s(smem + L.scales[m] + (size_t)i0 * L.sb, p.s[m] + (size_t)(r0 + i0) * L.sb, (uint32_t)(n * L.sb),
+                   &bar[b]);
     }
   }
-  // the next kernel may now be scheduled; it waits for this grid's completion
-  // before it reads what this grid writes
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  __syncthreads();
-  // activations (and, for phase 2, h) come from the previous kernels
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
 
-  const int C = K / 512;  // column chunks of 32 groups of 16
+// All warps: the partial sums of this CTA's rows of one phase into the
+// reduction slots.  A warp task = one column chunk (512 columns: a 16-column
+// group per lane) of RB = 8 / TQ rows of one matrix, for TQ tokens whose
+// activations stay in registers; its 8 sums (RB rows x TQ tokens) leave
+// through one halving reduction.  Tokens beyond TQ take further passes.
+// Returns false when a batch of rows did not land in time.
+template <int NMAT, bool MX, int TQ>
+__device__ __forceinline__ bool compute_rows(const Phase &p, const uint8_t *smem, const Layout &L, uint64_t *bar,
+                                             int nr, int T, const float *x, int ld_x, int *s_err) {
+  constexpr int RB = 8 / TQ;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const size_t cb = (size_t)p.K / 2;
+  const int C = p.K / 512;  // column chunks of 32 groups of 16
   const int c = warp % C, slot = warp / C, nslots = kWarps / C;
   const int g = c * 32 + lane;  // this lane's 16-column group
   const int nrb = (nr + RB - 1) / RB;
   const int ntask = nrb * NMAT;
-  float *red = reinterpret_cast<float *>(smem + L.red);
+  float *red = reinterpret_cast<float *>(const_cast<uint8_t *>(smem) + L.red);
   const int vi = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);  // reduce8's value
   bool ok = true;
   for (int tp = 0; tp < T; tp += TQ) {
@@ -179,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const DecArgs a) {
 #pragma unroll
     for (int t = 0; t < TQ; ++t) {
       const bool have = tp + t < T;
-      const float4 *src = reinterpret_cast<const float4 *>(a.x + (size_t)(have ? tp + t : 0) * a.ld_x + 16 * g);
+      const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)(have ? tp + t : 0) * ld_x + 16 * g);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const float4 f = have ? __ldcg(src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -189,7 +172,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const DecArgs a) {
     for (int task = slot; task < ntask; task += nslots) {
       const int rb = task / NMAT, m = task - rb * NMAT;
       const int i0 = rb * RB;
-      ok = tc::bar_wait(&bar[i0 / kBatchRows], 0u, &s_err) && ok;  // returns at once after the first time
+      ok = tc::bar_wait(&bar[i0 / kBatchRows], 0u, s_err) && ok;  // returns at once after the first time
       const uint8_t *cbase = smem + (m ? L.codes[NMAT - 1] : L.codes[0]) + (size_t)i0 * cb + 8 * g;
       const uint8_t *sbase = smem + (m ? L.scales[NMAT - 1] : L.scales[0]) + (size_t)i0 * L.sb + (MX ? g >> 1 : g);
       float v[8];
@@ -204,11 +187,11 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const DecArgs a) {
           const float sc = MX ? e8m0_f32(sbyte) : e4m3_f32(sbyte);
 #pragma unroll
           for (int hw = 0; hw < 2; ++hw) {
-            uint32_t p[4];
-            e2m1x8_to_f16x2(hw ? cw.y : cw.x, p);
+            uint32_t q4[4];
+            e2m1x8_to_f16x2(hw ? cw.y : cw.x, q4);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const float2 w2 = __half22float2(*reinterpret_cast<const __half2 *>(&p[j]));
+              const float2 w2 = __half22float2(*reinterpret_cast<const __half2 *>(&q4[j]));
               const int k = 8 * hw + 2 * j;
 #pragma unroll
               for (int t = 0; t < TQ; ++t) acc[t] = fmaf(w2.y, xr[t][k + 1], fmaf(w2.x, xr[t][k], acc[t]));
@@ -226,9 +209,19 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const DecArgs a) {
         red[((size_t)((i0 + r) * NMAT + m) * T + tp + t) * C + c] = sum;
     }
   }
-  __syncthreads();
-  const bool bad = s_err != 0 || !ok;
-  for (int idx = tid; idx < nr * T; idx += kThreads) {
+  return ok;
+}
+
+// After a __syncthreads: each (row, token) sums its chunks in order, times the
+// matrix scale; phase 1 writes h = min(silu(g), 10) * clamp(u, -10, 10),
+// phase 2 out (+)= out_w * y.  NaN where `bad`.
+template <int NMAT, bool MX>
+__device__ __forceinline__ void finish_rows(const Phase &p, const uint8_t *smem, const Layout &L, int r0, int nr,
+                                            int T, bool bad, float *h, int ld_h, float *y, int ld_y, float out_w,
+                                            int accumulate) {
+  const int C = p.K / 512;
+  const float *red = reinterpret_cast<const float *>(smem + L.red);
+  for (int idx = threadIdx.x; idx < nr * T; idx += kThreads) {
     const int i = idx / T, t = idx - i * T;
     float v[NMAT];
 #pragma unroll
@@ -236,18 +229,66 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const DecArgs a) {
       const float *rr = red + ((size_t)(i * NMAT + m) * T + t) * C;
       float s = 0.f;
       for (int k = 0; k < C; ++k) s += rr[k];
-      v[m] = MX ? s : s * a.gs[m];
+      v[m] = MX ? s : s * p.gs[m];
     }
-    if (PHASE == 1) {
-      a.h[(size_t)t * a.ld_h + r0 + i] = bad ? __int_as_float(0x7FC00000) : silu10(v[0]) * clamp10(v[NMAT - 1]);
+    if (NMAT == 2) {
+      h[(size_t)t * ld_h + r0 + i] = bad ? __int_as_float(0x7FC00000) : silu10(v[0]) * clamp10(v[NMAT - 1]);
     } else {
-      float *dst = a.y + (size_t)t * a.ld_y + r0 + i;
-      const float wy = a.out_w * v[0];  // flash1017.rs:4900-4905 (dst += scale * src)
-      *dst = bad ? __int_as_float(0x7FC00000) : (a.accumulate ? *dst + wy : wy);
+      float *dst = y + (size_t)t * ld_y + r0 + i;
+      const float wy = out_w * v[0];  // flash1017.rs:4900-4905 (dst += scale * src)
+      *dst = bad ? __int_as_float(0x7FC00000) : (accumulate ? *dst + wy : wy);
     }
   }
+}
+
+__device__ __forceinline__ void rows_of(int rows, int &r0, int &nr) {
+  r0 = (int)((long long)blockIdx.x * rows / gridDim.x);
+  nr = (int)((long long)(blockIdx.x + 1) * rows / gridDim.x) - r0;
+}
+
+struct DecArgs {
+  Phase p;
+  int T;
+  const float *x;  // [T][ld_x] activations (x; h for phase 2)
+  int ld_x;
+  float *h;        // phase 1 output [T][ld_h]
+  int ld_h;
+  float *y;        // phase 2 output [T][ld_y]
+  int ld_y;
+  float out_w;
+  int accumulate;
+};
+
+// One phase per launch: PHASE 1 gate (matrix 0) and up (matrix 1) -> h,
+// PHASE 2 down -> y.
+template <int PHASE, bool MX, int TQ>
+__global__ void __launch_bounds__(kThreads, 2) decode_kernel(const DecArgs a) {
+  constexpr int NMAT = PHASE == 1 ? 2 : 1;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smem);
+  __shared__ int s_err;
+  int r0, nr;
+  rows_of(a.p.rows, r0, nr);
+  const Layout L = layout(NMAT, nr, a.p.K, a.T, MX);
+  const int nb = (nr + kBatchRows - 1) / kBatchRows;
+  if (threadIdx.x == 0) {
+    s_err = 0;
+    for (int b = 0; b < nb; ++b) tc::bar_init(&bar[b], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    issue_rows<NMAT>(a.p, smem, L, bar, r0, nr);
+  }
+  // the next kernel may now be scheduled; it waits for this grid's completion
+  // before it reads what this grid writes
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  __syncthreads();
+  // activations (and, for phase 2, h) come from the previous kernels
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const bool ok = compute_rows<NMAT, MX, TQ>(a.p, smem, L, bar, nr, a.T, a.x, a.ld_x, &s_err);
+  __syncthreads();
+  finish_rows<NMAT, MX>(a.p, smem, L, r0, nr, a.T, s_err != 0 || !ok, a.h, a.ld_h, a.y, a.ld_y, a.out_w,
+                        a.accumulate);
   // no bulk copy may still be landing when the CTA's shared memory is released
-  if (tid == 0)
+  if (threadIdx.x == 0)
     for (int b = 0; b < nb; ++b) tc::bar_wait_drain(&bar[b], 0u);
 }
 
@@ -267,6 +308,7 @@ static int sm_count() {
 }
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 
 bool expert_decode_fits(const ffn_b200_expert &e, size_t inter, size_t hidden, size_t seq) {
   if (e.format != FFN_B200_FMT_NVFP4 && e.format != FFN_B200_FMT_MXFP4) return false;
@@ -310,26 +352,43 @@ template <bool MX>
 static int run_decode(const ffn_b200_expert &e, int inter, int hidden, int seq, const float *x, float *out,
                       float w, int accumulate, float *h, cudaStream_t st) {
   const int sms = sm_count();
+  dec::Phase p1{}, p2{};
+  for (int m = 0; m < 2; ++m) {
+    p1.w[m] = e.nv[m].w;
+    p1.s[m] = e.nv[m].s;
+    p1.gs[m] = e.nv[m].gs;
+  }
+  p1.rows = inter;
+  p1.K = hidden;
+  p2.w[0] = e.nv[2].w;
+  p2.s[0] = e.nv[2].s;
+  p2.gs[0] = e.nv[2].gs;
+  p2.rows = hidden;
+  p2.K = inter;
   const int g1 = min(sms, inter), g2 = min(sms, hidden);
-  dec::DecArgs p{};
-  p.w[0] = e.nv[0].w; p.s[0] = e.nv[0].s; p.gs[0] = e.nv[0].gs;
-  p.w[1] = e.nv[1].w; p.s[1] = e.nv[1].s; p.gs[1] = e.nv[1].gs;
-  p.rows = inter; p.K = hidden; p.T = seq;
-  p.x = x; p.ld_x = hidden;
-  p.h = h; p.ld_h = inter;
+  dec::DecArgs a{};
+  a.p = p1;
+  a.T = seq;
+  a.x = x;
+  a.ld_x = hidden;
+  a.h = h;
+  a.ld_h = inter;
   const size_t sm1 = dec::layout(2, (inter + g1 - 1) / g1, hidden, seq, MX).total;
-  int rc = seq == 1 ? launch_dec<1, MX, 1>(p, g1, sm1, st, FFN_B200_K_GATEUP_NVFP4, "decode_kernel<1>")
-                    : launch_dec<1, MX, 2>(p, g1, sm1, st, FFN_B200_K_GATEUP_NVFP4, "decode_kernel<1>");
+  int rc = seq == 1 ? launch_dec<1, MX, 1>(a, g1, sm1, st, FFN_B200_K_GATEUP_NVFP4, "decode_kernel<1>")
+                    : launch_dec<1, MX, 2>(a, g1, sm1, st, FFN_B200_K_GATEUP_NVFP4, "decode_kernel<1>");
   if (rc) return rc;
-  dec::DecArgs q{};
-  q.w[0] = e.nv[2].w; q.s[0] = e.nv[2].s; q.gs[0] = e.nv[2].gs;
-  q.rows = hidden; q.K = inter; q.T = seq;
-  q.x = h; q.ld_x = inter;
-  q.y = out; q.ld_y = hidden;
-  q.out_w = w; q.accumulate = accumulate;
+  dec::DecArgs b{};
+  b.p = p2;
+  b.T = seq;
+  b.x = h;
+  b.ld_x = inter;
+  b.y = out;
+  b.ld_y = hidden;
+  b.out_w = w;
+  b.accumulate = accumulate;
   const size_t sm2 = dec::layout(1, (hidden + g2 - 1) / g2, inter, seq, MX).total;
-  return seq == 1 ? launch_dec<2, MX, 1>(q, g2, sm2, st, FFN_B200_K_DOWN_NVFP4, "decode_kernel<2>")
-                  : launch_dec<2, MX, 2>(q, g2, sm2, st, FFN_B200_K_DOWN_NVFP4, "decode_kernel<2>");
+  return seq == 1 ? launch_dec<2, MX, 1>(b, g2, sm2, st, FFN_B200_K_DOWN_NVFP4, "decode_kernel<2>")
+                  : launch_dec<2, MX, 2>(b, g2, sm2, st, FFN_B200_K_DOWN_NVFP4, "decode_kernel<2>");
 }
 
 int launch_expert_decode(const ffn_b200_expert &e, size_t inter, size_t hidden, size_t seq, const float *x,

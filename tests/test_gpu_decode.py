@@ -1,11 +1,11 @@
-"""The two-launch expert decode kernels (csrc/expert_decode.cu): one NVFP4 or
-MXFP4 SwiGLU expert over 1..8 tokens, as ffn_b200_expert_forward runs it for
-those formats and batch sizes, against the oracle's expert
-(flash1017.rs:7537-7547 over CachedNvfp4Mat / CachedMxfp4Mat rows,
-flash1017.rs:2331-2357, 2717-2744) and the output update out (+)= w * y
-(flash1017.rs:4900-4905).  Tolerance: max|y - ref| / max|ref| <= 1e-3 and
-cosine >= 0.99999.  Each case also checks that the call issued exactly the
-two decode launches (the GEMV chain issues at least three)."""
+"""The expert decode kernels (csrc/expert_decode.cu): one NVFP4 or MXFP4
+SwiGLU expert over 1..8 tokens, as ffn_b200_expert_forward runs it for those
+formats and batch sizes, against the oracle's expert (flash1017.rs:7537-7547
+over CachedNvfp4Mat / CachedMxfp4Mat rows, flash1017.rs:2331-2357, 2717-2744)
+and the output update out (+)= w * y (flash1017.rs:4900-4905).  Tolerance:
+max|y - ref| / max|ref| <= 1e-3 and cosine >= 0.99999.  Each case also checks
+that the call issued exactly the two decode launches (the GEMV chain issues at
+least three)."""
 import numpy as np
 import pytest
 
@@ -23,6 +23,9 @@ def _nvfp4(ffn, oracle, seed, inter, hidden):
     return e, oe
 
 
+LAUNCHES = 2
+
+
 def _run(ffn, e, x, out=None, weight=1.0, accumulate=False):
     n0 = ffn.launch_count()
     y = e.forward(x, out=out, weight=weight, accumulate=accumulate)
@@ -35,7 +38,7 @@ def test_decode_nvfp4_config0(oracle, ffn, cuda, seq):
     e, oe = _nvfp4(ffn, oracle, 0, I, H)
     x = ffn.gen_normal(ffn.path_key(0, 0, seq, ffn.TAG_X), seq * H).view(seq, H)
     y, launches = _run(ffn, e, x)
-    assert launches == 2
+    assert launches == LAUNCHES
     xs = host(x)
     ref = np.stack([oe.forward(np.ascontiguousarray(xs[t])) for t in range(seq)])
     oracle.assert_close(y, ref, what=f"decode nvfp4 seq {seq}")
@@ -52,7 +55,7 @@ def test_decode_accumulate(oracle, ffn, cuda, seq):
     w = 0.37
     out = base.clone()
     _, launches = _run(ffn, e, x, out=out, weight=w, accumulate=True)
-    assert launches == 2
+    assert launches == LAUNCHES
     y2 = host(e.forward(x, out=out, weight=w, accumulate=True))
     xs, b = host(x), host(base)
     ref = np.stack([oe.forward(np.ascontiguousarray(xs[t])) for t in range(seq)])
@@ -71,7 +74,7 @@ def test_decode_shapes(oracle, ffn, cuda, inter, hidden):
     e, oe = _nvfp4(ffn, oracle, 11, inter, hidden)
     x = ffn.gen_normal(ffn.path_key(11, inter, hidden, ffn.TAG_X), seq * hidden).view(seq, hidden)
     y, launches = _run(ffn, e, x)
-    assert launches == 2
+    assert launches == LAUNCHES
     xs = host(x)
     ref = np.stack([oe.forward(np.ascontiguousarray(xs[t])) for t in range(seq)])
     oracle.assert_close(y, ref, what=f"decode nvfp4 {inter}x{hidden}")
@@ -97,7 +100,7 @@ def test_decode_mxfp4(oracle, ffn, cuda, seq):
     e, oe = mx_expert(ffn, oracle, 90, I, H, cuda)
     x = ffn.gen_normal(ffn.path_key(90, 0, seq, ffn.TAG_X), seq * H).view(seq, H)
     y, launches = _run(ffn, e, x)
-    assert launches == 2
+    assert launches == LAUNCHES
     xs = host(x)
     ref = np.stack([oe.forward(np.ascontiguousarray(xs[t])) for t in range(seq)])
     oracle.assert_close(y, ref, what=f"decode mxfp4 seq {seq}")
@@ -118,3 +121,4 @@ def test_decode_back_to_back(oracle, ffn, cuda):
     for k, (_, oe) in enumerate(pairs):
         ref = ref + np.float32(0.125 * (k + 1)) * oe.forward(np.ascontiguousarray(xs))
     oracle.assert_close(host(out)[0], ref, what="eight experts back to back")
+

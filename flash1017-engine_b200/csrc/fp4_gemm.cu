@@ -382,21 +382,12 @@ __device__ __forceinline__ uint32_t e2m1x8(const float *f) {
   return r;
 }
 
-// value of an E2M1 code: magnitudes 0, .5, 1, 1.5, 2, 3, 4, 6, bit 3 = sign
-__device__ __forceinline__ float e2m1_value(uint32_t c) {
-  const uint32_t m = c & 7u;
-  const float a = m < 4u ? 0.5f * (float)m : (m == 7u ? 6.0f : (float)(m - 2u));
-  return (c & 8u) ? -a : a;
-}
-
 // Quantise one 16-value block v of the remainder for term scale 2^e (inv =
 // 2^-e, sc = 2^e): block scale = UE4M3 ceiling of max|v| 2^-e / 6, codes =
 // E2M1(v 2^-e * (1/s)) with the correctly rounded reciprocal; v becomes the
 // new remainder v - 2^e s q.  Writes the 8 code bytes and returns the scale.
-__device__ __forceinline__ uint32_t quant_block(float (&v)[16], float inv, float sc, uint2 &codes) {
-  float bm = 0.f;
-#pragma unroll
-  for (int u = 0; u < 16; ++u) bm = fmaxf(bm, fabsf(v[u]));
+// bm = max|v| over the block (the caller has it already).
+__device__ __forceinline__ uint32_t quant_block(float (&v)[16], float bm, float inv, float sc, uint2 &codes) {
   const uint32_t code = ue4m3_ceil(__fdiv_rn(bm * inv, 6.0f));
   codes = make_uint2(0u, 0u);
   if (!code) return 0u;
@@ -406,10 +397,18 @@ __device__ __forceinline__ uint32_t quant_block(float (&v)[16], float inv, float
   for (int u = 0; u < 16; ++u) qv[u] = __fmul_rn(__fmul_rn(v[u], inv), rcp);
   codes.x = e2m1x8(qv);
   codes.y = e2m1x8(qv + 8);
-  // remainder: the codes' values (exact, from the code words' nibbles) times s 2^e
+  // remainder: the codes' values (exact, from the code words' nibbles) times
+  // s 2^e.  (The hardware E2M1 -> f16x2 decode of these freshly converted code
+  // words left the remainder unchanged in a test build; the arithmetic decode
+  // below is what the bit-exact tests pin.)
   const float ss = sv * sc;
 #pragma unroll
-  for (int u = 0; u < 16; ++u) v[u] -= e2m1_value(((u < 8 ? codes.x : codes.y) >> (4 * (u & 7))) & 15u) * ss;
+  for (int u = 0; u < 16; ++u) {
+    const uint32_t c = ((u < 8 ? codes.x : codes.y) >> (4 * (u & 7))) & 15u;
+    const uint32_t m = c & 7u;  // magnitudes 0, .5, 1, 1.5, 2, 3, 4, 6; bit 3 = sign
+    const float a = m < 4u ? 0.5f * (float)m : (m == 7u ? 6.0f : (float)(m - 2u));
+    v[u] -= ((c & 8u) ? -a : a) * ss;
+  }
   return code;
 }
 
@@ -432,9 +431,10 @@ __device__ __forceinline__ void q4_terms(float (&v)[16], bool mine, int row, int
   const int nw = (int)(blockDim.x >> 5);
 #pragma unroll 1
   for (int t = 0; t < terms; ++t) {
-    float am = 0.f;
+    float bm = 0.f;  // this thread's block maximum
 #pragma unroll
-    for (int u = 0; u < 16; ++u) am = fmaxf(am, fabsf(v[u]));
+    for (int u = 0; u < 16; ++u) bm = fmaxf(bm, fabsf(v[u]));
+    float am = bm;
     for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
     if (lane == 0) red[t & 1][wid] = am;
     __syncthreads();  // (the other buffer was last read before the previous term's barrier)
@@ -444,7 +444,7 @@ __device__ __forceinline__ void q4_terms(float (&v)[16], bool mine, int row, int
     if (threadIdx.x == 0) qe[(size_t)row * terms + t] = e;
     if (mine) {
       uint2 cw;
-      const uint32_t code = quant_block(v, pow2f(-e), pow2f(e), cw);
+      const uint32_t code = quant_block(v, bm, pow2f(-e), pow2f(e), cw);
       *reinterpret_cast<uint2 *>(qc + ((size_t)row * terms + t) * (K / 2) + 8 * blk) = cw;
       qs[((size_t)row * terms + t) * (K / 16) + blk] = (uint8_t)code;
     }

@@ -68,20 +68,31 @@ __device__ __forceinline__ float clamp10(float u) {  // Rust f32::clamp(-10, 10)
   return u;
 }
 
+// Weight formats of the decode kernels.
+constexpr int kNv = 0;    // NVFP4: E2M1 pairs, E4M3 scale per 16 columns, matrix scale
+constexpr int kMx = 1;    // MXFP4: E2M1 pairs, E8M0 scale per 32 columns
+constexpr int kTern = 2;  // ternary: 2-bit codes, row scale, optional U8 scale per 64 columns, rank-16 core
+
+__host__ __device__ constexpr int code_bytes(int F, int K) { return F == kTern ? K / 4 : K / 2; }
+__host__ __device__ constexpr int scale_bytes(int F, int K, bool bs) {
+  return F == kNv ? K / 16 : (F == kMx ? K / 32 : (bs ? K / 64 : 0));
+}
+
 // Shared memory: batch barriers, then per matrix the rows' codes and scales,
 // then the reduction slots red[(row * NMAT + m) * T + t][chunk].
 struct Layout {
-  int nr, sb;              // rows of this CTA, scale bytes per row
+  int nr, cb, sb;  // rows of this CTA, code and scale bytes per row
   size_t codes[2], scales[2], red, total;
 };
-__host__ __device__ inline Layout layout(int nmat, int nr, int K, int T, bool mx, size_t base = 128) {
+__host__ __device__ inline Layout layout(int F, bool bs, int nmat, int nr, int K, int T, size_t base = 128) {
   Layout l;
   l.nr = nr;
-  l.sb = mx ? K / 32 : K / 16;
+  l.cb = code_bytes(F, K);
+  l.sb = scale_bytes(F, K, bs);
   size_t o = base;  // after the barriers
   for (int m = 0; m < nmat; ++m) {
     l.codes[m] = o;
-    o += (size_t)nr * (K / 2);
+    o += (size_t)nr * l.cb;
     l.scales[m] = o;
     o += (size_t)nr * l.sb;
   }
@@ -112,9 +123,18 @@ __device__ __forceinline__ float reduce8(float (&v)[8], int lane) {
 
 // One phase's matrices: gate and up (NMAT 2) or down (NMAT 1).
 struct Phase {
-  const uint8_t *w[2];
-  const uint8_t *s[2];
-  float gs[2];
+  const uint8_t *w[2];      // codes [rows][code_bytes]
+  const uint8_t *s[2];      // scales [rows][scale_bytes] (ternary: U8 block scales or null)
+  float gs[2];              // NVFP4 matrix scales
+  const float *rs[2];       // ternary row scales [rows]
+  const int8_t *core_b[2];  // ternary rank-16 core B [rows][16], or null
+  const float *z;           // ternary gate/up: z [token][3][16] (core A x, times a_sc b_sc)
+  const int8_t *core_a;     // ternary down core A [16][inter], or null: phase 1 writes partial
+                            // sums of A h over its rows, phase 2 adds them up
+  const float *a_sc, *b_sc; // ... and its scales [16] (phase 2)
+  float *zpart;             // [phase-1 CTA][token][16]
+  int zparts;               // phase-1 CTAs (phase 2)
+  float proj;               // ternary gate/up pre-scale (tier_b_proj_scale), else 1
   int rows, K;
 };
 
@@ -123,7 +143,7 @@ struct Phase {
 template <int NMAT>
 __device__ __forceinline__ void issue_rows(const Phase &p, uint8_t *smem, const Layout &L, uint64_t *bar, int r0,
                                            int nr) {
-  const size_t cb = (size_t)p.K / 2;
+  const size_t cb = (size_t)L.cb;
   const int nb = (nr + kBatchRows - 1) / kBatchRows;
   for (int b = 0; b < nb; ++b) {
     const int i0 = b * kBatchRows, n = min(kBatchRows, nr - i0);
@@ -131,10 +151,50 @@ __device__ __forceinline__ void issue_rows(const Phase &p, uint8_t *smem, const 
 #pragma unroll
     for (int m = 0; m < NMAT; ++m) {
       tc::bulk_g2s(smem + L.codes[m] + i0 * cb, p.w[m] + (size_t)(r0 + i0) * cb, (uint32_t)(n * cb), &bar[b]);
-      tc::bulk_g2s(smem + L.scales[m] + (size_t)i0 * L.sb, p.s[m] + (size_t)(r0 + i0) * L.sb, (uint32_t)(n * L.sb),
-                   &bar[b]);
+      if (L.sb)
+        tc::bulk_g2s(smem + L.scales[m] + (size_t)i0 * L.sb, p.s[m] + (size_t)(r0 + i0) * L.sb,
+                     (uint32_t)(n * L.sb), &bar[b]);
     }
   }
+}
+
+// Sum over a lane's 16 columns of L(code) x for one row (per token), times
+// the group's scale: E2M1 via the hardware f16x2 decode; ternary codes
+// (0 -> -1, 1 -> 0, 2 -> +1, 3 -> 0, flash1017.rs:2566) by sign flips and masks.
+template <int F, int TQ>
+__device__ __forceinline__ void row_group(const uint8_t *cptr, float sc, const float (&xr)[TQ][16],
+                                          float (&acc)[TQ]) {
+#pragma unroll
+  for (int t = 0; t < TQ; ++t) acc[t] = 0.f;
+  if (F == kTern) {
+    const uint32_t w = *reinterpret_cast<const uint32_t *>(cptr);
+    const uint32_t neg = ~w & ~(w >> 1) & 0x55555555u;  // bit 2i: code i == 0
+    const uint32_t pos = (w >> 1) & ~w & 0x55555555u;   // bit 2i: code i == 2
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t keep = 0u - (((neg | pos) >> (2 * i)) & 1u);  // all ones for +-1
+      const uint32_t flip = ((neg >> (2 * i)) & 1u) << 31;
+#pragma unroll
+      for (int t = 0; t < TQ; ++t)
+        acc[t] += __uint_as_float((__float_as_uint(xr[t][i]) ^ flip) & keep);
+    }
+  } else {
+    const uint2 cw = *reinterpret_cast<const uint2 *>(cptr);
+#pragma unroll
+    for (int hw = 0; hw < 2; ++hw) {
+      uint32_t q4[4];
+      e2m1x8_to_f16x2(hw ? cw.y : cw.x, q4);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 w2 = __half22float2(*reinterpret_cast<const __half2 *>(&q4[j]));
+        const int k = 8 * hw + 2 * j;
+#pragma unroll
+        for (int t = 0; t < TQ; ++t) acc[t] = fmaf(w2.y, xr[t][k + 1], fmaf(w2.x, xr[t][k], acc[t]));
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < TQ; ++t) acc[t] *= sc;
 }
 
 // All warps: the partial sums of this CTA's rows of one phase into the
@@ -143,12 +203,11 @@ __device__ __forceinline__ void issue_rows(const Phase &p, uint8_t *smem, const 
 // activations stay in registers; its 8 sums (RB rows x TQ tokens) leave
 // through one halving reduction.  Tokens beyond TQ take further passes.
 // Returns false when a batch of rows did not land in time.
-template <int NMAT, bool MX, int TQ>
+template <int NMAT, int F, int TQ>
 __device__ __forceinline__ bool compute_rows(const Phase &p, const uint8_t *smem, const Layout &L, uint64_t *bar,
                                              int nr, int T, const float *x, int ld_x, int *s_err) {
   constexpr int RB = 8 / TQ;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const size_t cb = (size_t)p.K / 2;
   const int C = p.K / 512;  // column chunks of 32 groups of 16
   const int c = warp % C, slot = warp / C, nslots = kWarps / C;
   const int g = c * 32 + lane;  // this lane's 16-column group
@@ -156,6 +215,8 @@ __device__ __forceinline__ bool compute_rows(const Phase &p, const uint8_t *smem
   const int ntask = nrb * NMAT;
   float *red = reinterpret_cast<float *>(const_cast<uint8_t *>(smem) + L.red);
   const int vi = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);  // reduce8's value
+  const int cg = F == kTern ? 4 * g : 8 * g;                                          // code byte of the group
+  const int sg = F == kNv ? g : (F == kMx ? g >> 1 : g >> 2);                         // scale byte of the group
   bool ok = true;
   for (int tp = 0; tp < T; tp += TQ) {
     float xr[TQ][16];
@@ -173,32 +234,21 @@ __device__ __forceinline__ bool compute_rows(const Phase &p, const uint8_t *smem
       const int rb = task / NMAT, m = task - rb * NMAT;
       const int i0 = rb * RB;
       ok = tc::bar_wait(&bar[i0 / kBatchRows], 0u, s_err) && ok;  // returns at once after the first time
-      const uint8_t *cbase = smem + (m ? L.codes[NMAT - 1] : L.codes[0]) + (size_t)i0 * cb + 8 * g;
-      const uint8_t *sbase = smem + (m ? L.scales[NMAT - 1] : L.scales[0]) + (size_t)i0 * L.sb + (MX ? g >> 1 : g);
+      const uint8_t *cbase = smem + (m ? L.codes[NMAT - 1] : L.codes[0]) + (size_t)i0 * L.cb + cg;
+      const uint8_t *sbase = smem + (m ? L.scales[NMAT - 1] : L.scales[0]) + (size_t)i0 * L.sb + sg;
       float v[8];
 #pragma unroll
       for (int r = 0; r < RB; ++r) {
         float acc[TQ];
-#pragma unroll
-        for (int t = 0; t < TQ; ++t) acc[t] = 0.f;
         if (i0 + r < nr) {
-          const uint2 cw = *reinterpret_cast<const uint2 *>(cbase + r * cb);
-          const uint32_t sbyte = sbase[r * L.sb];
-          const float sc = MX ? e8m0_f32(sbyte) : e4m3_f32(sbyte);
+          float sc = 1.0f;
+          if (F == kNv) sc = e4m3_f32(sbase[r * L.sb]);
+          else if (F == kMx) sc = e8m0_f32(sbase[r * L.sb]);
+          else if (L.sb) sc = (float)sbase[r * L.sb];
+          row_group<F, TQ>(cbase + r * L.cb, sc, xr, acc);
+        } else {
 #pragma unroll
-          for (int hw = 0; hw < 2; ++hw) {
-            uint32_t q4[4];
-            e2m1x8_to_f16x2(hw ? cw.y : cw.x, q4);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 w2 = __half22float2(*reinterpret_cast<const __half2 *>(&q4[j]));
-              const int k = 8 * hw + 2 * j;
-#pragma unroll
-              for (int t = 0; t < TQ; ++t) acc[t] = fmaf(w2.y, xr[t][k + 1], fmaf(w2.x, xr[t][k], acc[t]));
-            }
-          }
-#pragma unroll
-          for (int t = 0; t < TQ; ++t) acc[t] *= sc;
+          for (int t = 0; t < TQ; ++t) acc[t] = 0.f;
         }
 #pragma unroll
         for (int t = 0; t < TQ; ++t) v[t * RB + r] = acc[t];
@@ -212,13 +262,51 @@ __device__ __forceinline__ bool compute_rows(const Phase &p, const uint8_t *smem
   return ok;
 }
 
-// After a __syncthreads: each (row, token) sums its chunks in order, times the
-// matrix scale; phase 1 writes h = min(silu(g), 10) * clamp(u, -10, 10),
-// phase 2 out (+)= out_w * y.  NaN where `bad`.
-template <int NMAT, bool MX>
+// The rank-16 core's term of a row (flash1017.rs:2465-2472 in the oracle's
+// order): sum_r B[row][r] z[r], z already times a_sc b_sc.
+__device__ __forceinline__ float core_row(const int8_t *b, int row, const float *z) {
+  const int4 v = __ldg(reinterpret_cast<const int4 *>(b + (size_t)row * 16));
+  const int8_t *bb = reinterpret_cast<const int8_t *>(&v);
+  float acc = 0.f;
+#pragma unroll
+  for (int r = 0; r < 16; ++r) acc += (float)bb[r] * z[r];
+  return acc;
+}
+
+// Ternary down core, z[t][r] = (sum_c A[r][c] h[t][c]) a_sc[r] b_sc[r]
+// (flash1017.rs:2452-2463), split over the phases: a phase-1 CTA owns h's
+// columns [r0, r0 + nr), so it writes the partial sums over them
+// (core_partial, from h in shared memory); phase 2 adds the CTAs' partials in
+// CTA order (core_sum).
+__device__ __forceinline__ void core_partial(const Phase &p, int r0, int nr, int T, const float *s_h) {
+  for (int q = threadIdx.x; q < T * 16; q += kThreads) {
+    const int t = q >> 4, r = q & 15;
+    const int8_t *arow = p.core_a + (size_t)r * p.rows + r0;
+    float acc = 0.f;
+    for (int i = 0; i < nr; ++i) acc = fmaf((float)__ldg(arow + i), s_h[t * kMaxRows + i], acc);
+    p.zpart[((size_t)blockIdx.x * T + t) * 16 + r] = acc;
+  }
+}
+__device__ __forceinline__ void core_sum(const Phase &p, int T, float *s_z) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int item = warp; item < T * 16; item += kWarps) {
+    const int t = item >> 4, r = item & 15;
+    float acc = 0.f;
+    for (int b = lane; b < p.zparts; b += 32) acc += __ldcg(p.zpart + ((size_t)b * T + t) * 16 + r);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) s_z[t * 16 + r] = acc * __ldg(p.a_sc + r) * __ldg(p.b_sc + r);
+  }
+}
+
+// After a __syncthreads: each (row, token) sums its chunks in order and
+// scales (NVFP4: the matrix scale; ternary: the row scale, then + the core
+// term); phase 1 writes h = min(silu(g), 10) * clamp(u, -10, 10) (ternary:
+// g, u times proj first), phase 2 out (+)= out_w * y.  NaN where `bad`.
+template <int NMAT, int F>
 __device__ __forceinline__ void finish_rows(const Phase &p, const uint8_t *smem, const Layout &L, int r0, int nr,
-                                            int T, bool bad, float *h, int ld_h, float *y, int ld_y, float out_w,
-                                            int accumulate) {
+                                            int T, bool bad, const float *s_z, float *s_h, float *h, int ld_h,
+                                            float *y, int ld_y, float out_w, int accumulate) {
   const int C = p.K / 512;
   const float *red = reinterpret_cast<const float *>(smem + L.red);
   for (int idx = threadIdx.x; idx < nr * T; idx += kThreads) {
@@ -229,10 +317,19 @@ __device__ __forceinline__ void finish_rows(const Phase &p, const uint8_t *smem,
       const float *rr = red + ((size_t)(i * NMAT + m) * T + t) * C;
       float s = 0.f;
       for (int k = 0; k < C; ++k) s += rr[k];
-      v[m] = MX ? s : s * p.gs[m];
+      if (F == kNv) s *= p.gs[m];
+      if (F == kTern) {
+        s *= __ldg(p.rs[m] + r0 + i);
+        if (p.core_b[m]) s += core_row(p.core_b[m], r0 + i, s_z + (t * NMAT + m) * 16);
+      }
+      v[m] = s;
     }
     if (NMAT == 2) {
-      h[(size_t)t * ld_h + r0 + i] = bad ? __int_as_float(0x7FC00000) : silu10(v[0]) * clamp10(v[NMAT - 1]);
+      float gv = v[0], uv = v[NMAT - 1];
+      if (F == kTern) { gv *= p.proj; uv *= p.proj; }
+      const float hv = bad ? __int_as_float(0x7FC00000) : silu10(gv) * clamp10(uv);
+      h[(size_t)t * ld_h + r0 + i] = hv;
+      if (s_h) s_h[t * kMaxRows + i] = hv;
     } else {
       float *dst = y + (size_t)t * ld_y + r0 + i;
       const float wy = out_w * v[0];  // flash1017.rs:4900-4905 (dst += scale * src)
@@ -261,7 +358,7 @@ struct DecArgs {
 
 // One phase per launch: PHASE 1 gate (matrix 0) and up (matrix 1) -> h,
 // PHASE 2 down -> y.
-template <int PHASE, bool MX, int TQ>
+template <int PHASE, int F, int TQ>
 __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const DecArgs a) {
   constexpr int NMAT = PHASE == 1 ? 2 : 1;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -269,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const DecArgs a) {
   __shared__ int s_err;
   int r0, nr;
   rows_of(a.p.rows, r0, nr);
-  const Layout L = layout(NMAT, nr, a.p.K, a.T, MX);
+  const Layout L = layout(F, a.p.s[0] != nullptr, NMAT, nr, a.p.K, a.T);
   const int nb = (nr + kBatchRows - 1) / kBatchRows;
   if (threadIdx.x == 0) {
     s_err = 0;
@@ -281,12 +378,28 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const DecArgs a) {
   // before it reads what this grid writes
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __syncthreads();
-  // activations (and, for phase 2, h) come from the previous kernels
+  // activations (and, for phase 2, h; ternary: z) come from the previous kernels
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const bool ok = compute_rows<NMAT, MX, TQ>(a.p, smem, L, bar, nr, a.T, a.x, a.ld_x, &s_err);
+  __shared__ float s_z[kMaxTok * 2 * 16];  // ternary cores' z [token][matrix][16]
+  if (F == kTern) {
+    if (PHASE == 1 && (a.p.core_b[0] || a.p.core_b[1])) {
+      for (int q = threadIdx.x; q < a.T * 2 * 16; q += kThreads) {
+        const int t = q >> 5, m = (q >> 4) & 1, r = q & 15;
+        s_z[q] = __ldcg(a.p.z + ((size_t)t * 3 + m) * 16 + r);
+      }
+    }
+    if (PHASE == 2 && a.p.core_a) core_sum(a.p, a.T, s_z);
+  }
+  const bool ok = compute_rows<NMAT, F, TQ>(a.p, smem, L, bar, nr, a.T, a.x, a.ld_x, &s_err);
   __syncthreads();
-  finish_rows<NMAT, MX>(a.p, smem, L, r0, nr, a.T, s_err != 0 || !ok, a.h, a.ld_h, a.y, a.ld_y, a.out_w,
-                        a.accumulate);
+  __shared__ float s_h[F == kTern && PHASE == 1 ? kMaxTok * kMaxRows : 1];  // this CTA's h for the down core
+  const bool partial = F == kTern && PHASE == 1 && a.p.core_a != nullptr;
+  finish_rows<NMAT, F>(a.p, smem, L, r0, nr, a.T, s_err != 0 || !ok, s_z, partial ? s_h : nullptr, a.h, a.ld_h,
+                       a.y, a.ld_y, a.out_w, a.accumulate);
+  if (partial) {
+    __syncthreads();
+    core_partial(a.p, r0, nr, a.T, s_h);
+  }
   // no bulk copy may still be landing when the CTA's shared memory is released
   if (threadIdx.x == 0)
     for (int b = 0; b < nb; ++b) tc::bar_wait_drain(&bar[b], 0u);
@@ -310,62 +423,131 @@ static int sm_count() {
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 
-bool expert_decode_fits(const ffn_b200_expert &e, size_t inter, size_t hidden, size_t seq) {
-  if (e.format != FFN_B200_FMT_NVFP4 && e.format != FFN_B200_FMT_MXFP4) return false;
-  if (seq < 1 || seq > (size_t)dec::kMaxTok) return false;
-  if (inter % 512 || hidden % 512 || inter > 8192 || hidden > 8192) return false;
-  if (16 % (inter / 512) || 16 % (hidden / 512)) return false;  // column chunks split the 16 warps evenly
+// Which decode format an expert takes, or -1: NVFP4 / MXFP4 / ternary with
+// the shapes, alignment and shared-memory budget of the kernels.
+static int decode_format(const ffn_b200_expert &e, size_t inter, size_t hidden, size_t seq) {
+  using namespace dec;
+  const int F = e.format == FFN_B200_FMT_NVFP4 ? kNv
+                : e.format == FFN_B200_FMT_MXFP4 ? kMx
+                : e.format == FFN_B200_FMT_TERNARY ? kTern : -1;
+  if (F < 0 || seq < 1 || seq > (size_t)kMaxTok) return -1;
+  // ternary: the sign-and-mask decode costs about twice the E2M1 one per
+  // value and is repeated per token pass; from 2 tokens on the GEMV engine's
+  // tensor-core decode is as fast (config-1 shapes: 52 us at 2 tokens here)
+  if (F == kTern && seq > 1) return -1;
+  if (inter % 512 || hidden % 512 || inter > 8192 || hidden > 8192) return -1;
+  if (16 % (inter / 512) || 16 % (hidden / 512)) return -1;  // column chunks split the 16 warps evenly
   const int sms = sm_count();
-  if (sms <= 0) return false;
-  const bool mx = e.format == FFN_B200_FMT_MXFP4;
-  for (int m = 0; m < 3; ++m)
-    if (!e.nv[m].w || !e.nv[m].s || !aligned16(e.nv[m].w) || !aligned16(e.nv[m].s)) return false;
+  if (sms <= 0) return -1;
+  bool bs1 = false, bs2 = false;
+  if (F == kTern) {
+    for (int m = 0; m < 3; ++m) {
+      const ffn_b200_ternary_mat &t = e.tn[m];
+      if (!t.p || !t.rs || !aligned16(t.p)) return -1;
+      if ((t.core_a == nullptr) != (t.core_b == nullptr)) return -1;
+      if (t.core_a && (!t.core_a_sc || !t.core_b_sc || !aligned16(t.core_a) || !aligned16(t.core_b))) return -1;
+      if (t.bs && !aligned16(t.bs)) return -1;
+    }
+    if ((e.tn[0].bs == nullptr) != (e.tn[1].bs == nullptr)) return -1;  // gate and up alike
+    bs1 = e.tn[0].bs != nullptr;
+    bs2 = e.tn[2].bs != nullptr;
+    if ((bs1 && hidden % 1024) || (bs2 && inter % 1024)) return -1;  // 16-byte rows of block scales
+  } else {
+    for (int m = 0; m < 3; ++m)
+      if (!e.nv[m].w || !e.nv[m].s || !aligned16(e.nv[m].w) || !aligned16(e.nv[m].s)) return -1;
+  }
   const int nr1 = (int)((inter + sms - 1) / sms), nr2 = (int)((hidden + sms - 1) / sms);
-  if (nr1 > dec::kMaxRows || nr2 > dec::kMaxRows) return false;
-  const size_t s1 = dec::layout(2, nr1, (int)hidden, (int)seq, mx).total;
-  const size_t s2 = dec::layout(1, nr2, (int)inter, (int)seq, mx).total;
-  return s1 <= dec::kSmemCap && s2 <= dec::kSmemCap && s1 + s2 <= 200 * 1024;
+  if (nr1 > kMaxRows || nr2 > kMaxRows) return -1;
+  const size_t s1 = layout(F, bs1, 2, nr1, (int)hidden, (int)seq).total;
+  const size_t s2 = layout(F, bs2, 1, nr2, (int)inter, (int)seq).total;
+  return s1 <= kSmemCap && s2 <= kSmemCap && s1 + s2 <= 200 * 1024 ? F : -1;
 }
 
-size_t expert_decode_ws_bytes(size_t inter, size_t seq) { return seq * inter * sizeof(float); }
+bool expert_decode_fits(const ffn_b200_expert &e, size_t inter, size_t hidden, size_t seq) {
+  return decode_format(e, inter, hidden, seq) >= 0;
+}
 
-template <int PHASE, bool MX, int TQ>
+// h [seq][inter] f32, then (ternary cores) z [seq][3][16] f32 and the down
+// core's partial sums [phase-1 CTAs <= 1024][seq][16] f32
+static size_t h_bytes(size_t inter, size_t seq) { return (seq * inter * sizeof(float) + 15) & ~(size_t)15; }
+size_t expert_decode_ws_bytes(size_t inter, size_t seq) {
+  return h_bytes(inter, seq) + seq * 48 * sizeof(float) + (size_t)1024 * seq * 16 * sizeof(float);
+}
+
+template <int PHASE, int F, int TQ>
 static int launch_dec(const dec::DecArgs &a, int grid, size_t smem, cudaStream_t st, int kind, const char *name) {
   static bool attr[64] = {false};
   int dev = 0;
   FFN_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return fail(FFN_B200_EUNSUP, "expert decode: device index >= 64");
   if (!attr[dev]) {
-    FFN_CUDA_TRY(cudaFuncSetAttribute(dec::decode_kernel<PHASE, MX, TQ>,
+    FFN_CUDA_TRY(cudaFuncSetAttribute(dec::decode_kernel<PHASE, F, TQ>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dec::kSmemCap));
     // the largest shared-memory carve-out for both phases, so that a phase-2
     // CTA finds room next to a running phase-1 CTA without a reconfiguration
-    FFN_CUDA_TRY(cudaFuncSetAttribute(dec::decode_kernel<PHASE, MX, TQ>,
+    FFN_CUDA_TRY(cudaFuncSetAttribute(dec::decode_kernel<PHASE, F, TQ>,
                                       cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     attr[dev] = true;
   }
-  FFN_LAUNCH_PDL(kind, st, name, (dec::decode_kernel<PHASE, MX, TQ>), grid, dec::kThreads, smem, a);
+  FFN_LAUNCH_PDL(kind, st, name, (dec::decode_kernel<PHASE, F, TQ>), grid, dec::kThreads, smem, a);
   return 0;
 }
 
-template <bool MX>
+template <int F>
 static int run_decode(const ffn_b200_expert &e, int inter, int hidden, int seq, const float *x, float *out,
-                      float w, int accumulate, float *h, cudaStream_t st) {
+                      float w, int accumulate, float *h, float *z, float *zpart, cudaStream_t st) {
+  using dec::kTern;
   const int sms = sm_count();
   dec::Phase p1{}, p2{};
-  for (int m = 0; m < 2; ++m) {
-    p1.w[m] = e.nv[m].w;
-    p1.s[m] = e.nv[m].s;
-    p1.gs[m] = e.nv[m].gs;
-  }
   p1.rows = inter;
   p1.K = hidden;
-  p2.w[0] = e.nv[2].w;
-  p2.s[0] = e.nv[2].s;
-  p2.gs[0] = e.nv[2].gs;
+  p1.proj = 1.0f;
   p2.rows = hidden;
   p2.K = inter;
+  p2.proj = 1.0f;
+  if (F == kTern) {
+    for (int m = 0; m < 2; ++m) {
+      p1.w[m] = e.tn[m].p;
+      p1.s[m] = e.tn[m].bs;
+      p1.rs[m] = e.tn[m].rs;
+      p1.core_b[m] = e.tn[m].core_b;
+    }
+    p1.z = z;
+    p1.proj = e.proj_scale;
+    p2.w[0] = e.tn[2].p;
+    p2.s[0] = e.tn[2].bs;
+    p2.rs[0] = e.tn[2].rs;
+    p2.core_b[0] = e.tn[2].core_b;
+    p1.core_a = p2.core_a = e.tn[2].core_a;
+    p2.a_sc = e.tn[2].core_a_sc;
+    p2.b_sc = e.tn[2].core_b_sc;
+    p1.zpart = p2.zpart = zpart;
+    p2.zparts = min(sms, inter);  // phase 1's grid
+    if (e.tn[0].core_a || e.tn[1].core_a) {  // gate/up cores' z from their own kernel
+      CoreZArgs c{};
+      c.direct = e;
+      c.n_tok_direct = seq;
+      c.K = hidden;
+      c.mat0 = 0;
+      c.nmat = 2;
+      c.xf = x;
+      c.ld_xf = hidden;
+      c.z = z;
+      if (int rc = launch_corez(c, (seq + kNTok - 1) / kNTok, st)) return rc;
+    }
+  } else {
+    for (int m = 0; m < 2; ++m) {
+      p1.w[m] = e.nv[m].w;
+      p1.s[m] = e.nv[m].s;
+      p1.gs[m] = e.nv[m].gs;
+    }
+    p2.w[0] = e.nv[2].w;
+    p2.s[0] = e.nv[2].s;
+    p2.gs[0] = e.nv[2].gs;
+  }
   const int g1 = min(sms, inter), g2 = min(sms, hidden);
+  const int k1 = F == kTern ? FFN_B200_K_GATEUP_TERNARY : FFN_B200_K_GATEUP_NVFP4;
+  const int k2 = F == kTern ? FFN_B200_K_DOWN_TERNARY : FFN_B200_K_DOWN_NVFP4;
   dec::DecArgs a{};
   a.p = p1;
   a.T = seq;
@@ -373,9 +555,9 @@ static int run_decode(const ffn_b200_expert &e, int inter, int hidden, int seq, 
   a.ld_x = hidden;
   a.h = h;
   a.ld_h = inter;
-  const size_t sm1 = dec::layout(2, (inter + g1 - 1) / g1, hidden, seq, MX).total;
-  int rc = seq == 1 ? launch_dec<1, MX, 1>(a, g1, sm1, st, FFN_B200_K_GATEUP_NVFP4, "decode_kernel<1>")
-                    : launch_dec<1, MX, 2>(a, g1, sm1, st, FFN_B200_K_GATEUP_NVFP4, "decode_kernel<1>");
+  const size_t sm1 = dec::layout(F, p1.s[0] != nullptr, 2, (inter + g1 - 1) / g1, hidden, seq).total;
+  int rc = seq == 1 ? launch_dec<1, F, 1>(a, g1, sm1, st, k1, "decode_kernel<1>")
+                    : launch_dec<1, F, 2>(a, g1, sm1, st, k1, "decode_kernel<1>");
   if (rc) return rc;
   dec::DecArgs b{};
   b.p = p2;
@@ -386,19 +568,27 @@ static int run_decode(const ffn_b200_expert &e, int inter, int hidden, int seq, 
   b.ld_y = hidden;
   b.out_w = w;
   b.accumulate = accumulate;
-  const size_t sm2 = dec::layout(1, (hidden + g2 - 1) / g2, inter, seq, MX).total;
-  return seq == 1 ? launch_dec<2, MX, 1>(b, g2, sm2, st, FFN_B200_K_DOWN_NVFP4, "decode_kernel<2>")
-                  : launch_dec<2, MX, 2>(b, g2, sm2, st, FFN_B200_K_DOWN_NVFP4, "decode_kernel<2>");
+  const size_t sm2 = dec::layout(F, p2.s[0] != nullptr, 1, (hidden + g2 - 1) / g2, inter, seq).total;
+  return seq == 1 ? launch_dec<2, F, 1>(b, g2, sm2, st, k2, "decode_kernel<2>")
+                  : launch_dec<2, F, 2>(b, g2, sm2, st, k2, "decode_kernel<2>");
 }
 
 int launch_expert_decode(const ffn_b200_expert &e, size_t inter, size_t hidden, size_t seq, const float *x,
                          float *out, float accum_weight, int accumulate, void *ws, cudaStream_t st) {
   float *h = static_cast<float *>(ws);
+  float *z = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + h_bytes(inter, seq));
+  float *zpart = z + seq * 48;
+  if (sm_count() > 1024) return fail(FFN_B200_EUNSUP, "expert decode: more than 1024 SMs");
   if (!aligned16(ws) || !aligned16(x) || !aligned16(out) || (hidden % 4))
     return fail(FFN_B200_EUNSUP, "expert decode: x, out and ws must be 16-byte aligned");
-  return e.format == FFN_B200_FMT_MXFP4
-             ? run_decode<true>(e, (int)inter, (int)hidden, (int)seq, x, out, accum_weight, accumulate, h, st)
-             : run_decode<false>(e, (int)inter, (int)hidden, (int)seq, x, out, accum_weight, accumulate, h, st);
+  const int I = (int)inter, H = (int)hidden, T = (int)seq;
+  switch (decode_format(e, inter, hidden, seq)) {
+    case dec::kNv: return run_decode<dec::kNv>(e, I, H, T, x, out, accum_weight, accumulate, h, z, zpart, st);
+    case dec::kMx: return run_decode<dec::kMx>(e, I, H, T, x, out, accum_weight, accumulate, h, z, zpart, st);
+    case dec::kTern:
+      return run_decode<dec::kTern>(e, I, H, T, x, out, accum_weight, accumulate, h, z, zpart, st);
+    default: return fail(FFN_B200_EUNSUP, "expert decode: expert or shape not supported");
+  }
 }
 
 }  // namespace ffn

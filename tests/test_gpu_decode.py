@@ -1,11 +1,14 @@
-"""The expert decode kernels (csrc/expert_decode.cu): one NVFP4 or MXFP4
-SwiGLU expert over 1..8 tokens, as ffn_b200_expert_forward runs it for those
-formats and batch sizes, against the oracle's expert (flash1017.rs:7537-7547
-over CachedNvfp4Mat / CachedMxfp4Mat rows, flash1017.rs:2331-2357, 2717-2744)
-and the output update out (+)= w * y (flash1017.rs:4900-4905).  Tolerance:
+"""The expert decode kernels (csrc/expert_decode.cu): one NVFP4, MXFP4 or
+ternary SwiGLU expert over 1..8 tokens, as ffn_b200_expert_forward runs it
+for those formats and batch sizes, against the oracle's expert
+(flash1017.rs:7537-7561 over CachedNvfp4Mat / CachedMxfp4Mat /
+CachedTernary158Mat rows with their rank-16 cores, flash1017.rs:2331-2357,
+2717-2744, 2538-2627, 2396-2473) and the output update out (+)= w * y
+(flash1017.rs:4900-4905).  Tolerance:
 max|y - ref| / max|ref| <= 1e-3 and cosine >= 0.99999.  Each case also checks
-that the call issued exactly the two decode launches (the GEMV chain issues at
-least three)."""
+that the call issued exactly the two decode launches (ternary experts with
+gate/up cores: three, the cores' z kernel first; the GEMV chain issues at
+least three, four with cores)."""
 import numpy as np
 import pytest
 
@@ -122,3 +125,46 @@ def test_decode_back_to_back(oracle, ffn, cuda):
         ref = ref + np.float32(0.125 * (k + 1)) * oe.forward(np.ascontiguousarray(xs))
     oracle.assert_close(host(out)[0], ref, what="eight experts back to back")
 
+
+
+def _ternary(ffn, oracle, seed, inter, hidden, cuda, core, bs, proj):
+    from test_gpu_parity import oracle_ternary_expert, with_block_scales
+    e = ffn.SwigluExpert.generate(ffn.FMT_TERNARY, seed, 0, 0, inter, hidden, with_core=core, proj_scale=proj)
+    if bs:
+        e = with_block_scales(e, seed * 10, cuda)
+    return e, oracle_ternary_expert(oracle, e)
+
+
+@pytest.mark.parametrize("seq", [1, 2])
+@pytest.mark.parametrize("core,bs,proj", [(True, False, 1.0), (False, False, 1.0), (True, True, 1.0),
+                                          (True, False, 2.5)])
+def test_decode_ternary_config1(oracle, ffn, cuda, seq, core, bs, proj):
+    """Config 1 shapes: ternary + rank-16 Q8 cores (gate/up z from the core
+    kernel; the down core's sums split between the phases), the 106 GB
+    format's U8 block scales, and tier_b_proj_scale on gate/up.  Two tokens
+    and more run on the GEMV engine."""
+    H, I = 4096, 2048
+    e, oe = _ternary(ffn, oracle, 31, I, H, cuda, core, bs, proj)
+    x = ffn.gen_normal(ffn.path_key(31, seq, int(core), ffn.TAG_X), seq * H).view(seq, H)
+    y, launches = _run(ffn, e, x)
+    if seq == 1:
+        assert launches == (3 if core else 2)
+    else:
+        assert launches >= (5 if core else 3)
+    xs = host(x)
+    ref = np.stack([oe.forward(np.ascontiguousarray(xs[t])) for t in range(seq)])
+    oracle.assert_close(y, ref, what=f"decode ternary seq {seq} core {core} bs {bs} proj {proj}")
+
+
+def test_decode_ternary_accumulate(oracle, ffn, cuda):
+    import torch
+    H, I, seq = 4096, 2048, 1
+    e, oe = _ternary(ffn, oracle, 32, I, H, cuda, True, False, 1.0)
+    x = ffn.gen_normal(ffn.path_key(32, 0, 0, ffn.TAG_X), seq * H).view(seq, H)
+    base = ffn.gen_normal(ffn.path_key(32, 1, 0, ffn.TAG_X), seq * H).view(seq, H)
+    out = base.clone()
+    e.forward(x, out=out, weight=-0.6, accumulate=True)
+    xs, b = host(x), host(base)
+    ref = np.stack([oe.forward(np.ascontiguousarray(xs[t])) for t in range(seq)])
+    oracle.assert_close(host(out) - b, np.float32(-0.6) * ref, what="decode ternary accumulate")
+    assert torch.isfinite(out).all()

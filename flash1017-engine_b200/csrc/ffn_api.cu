@@ -471,7 +471,7 @@ size_t ffn_b200_expert_ws_bytes(size_t inter, size_t hidden, size_t seq) {
     carve_expert(c, fmt, inter, hidden, seq, nullptr, nullptr, nullptr, nullptr);
     need = std::max(need, c.off + 256);
   }
-  return need;
+  return std::max(need, expert_decode_ws_bytes(inter, seq) + 256);
 }
 
 static int check_expert(const ffn_b200_expert &e, size_t inter, size_t hidden, const char *what) {

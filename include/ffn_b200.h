@@ -157,7 +157,16 @@ FFN_B200_EXPORT int ffn_b200_ternary_matvec(size_t rows, size_t cols, size_t seq
  * plus the rank-16 cores the reference's fused path lacks (the reference
  * recomputes such experts on its CPU, flash1017.rs:7483-7486).  For ternary
  * experts the caller passes accum_weight = weight * proj_scale, as the
- * reference does.  `e` is a host struct holding device pointers. */
+ * reference does.  `e` is a host struct holding device pointers.
+ * NVFP4 and MXFP4 experts over 1..8 tokens and ternary experts over one token
+ * (inter and hidden multiples of 512 whose 512-column chunks divide 16, up to
+ * 8192; 16-byte aligned codes, scales, x, out and ws) run as two launches of
+ * the decode kernels (a ternary expert with gate/up cores adds the cores'
+ * z kernel first); their weights and scales are read before the wait on the
+ * previous kernel in the stream, so they must not be written by a kernel the
+ * caller queued just before that lets later work start early (programmatic
+ * dependent launch).  FFN_B200_EXPERT_DECODE=0 in the environment (read once)
+ * keeps every call on the GEMV kernels. */
 FFN_B200_EXPORT size_t ffn_b200_expert_ws_bytes(size_t inter, size_t hidden, size_t seq);
 FFN_B200_EXPORT int ffn_b200_expert_forward(size_t inter, size_t hidden, size_t seq,
                                             const ffn_b200_expert *e, const float *x,
@@ -332,7 +341,7 @@ FFN_B200_EXPORT int ffn_b200_dequant_ternary(size_t rows, size_t cols, const uin
 #define FFN_B200_K_OTHER 11
 #define FFN_B200_K_GEMM_GATEUP 12 /* grouped tensor-core path */
 #define FFN_B200_K_GEMM_DOWN 13
-#define FFN_B200_K_QUANT 14       /* activation rows -> four NVFP4 terms (FP4 path) */
+#define FFN_B200_K_QUANT 14       /* activation rows -> six NVFP4 terms (FP4 path) */
 #define FFN_B200_K_FP4_GATEUP 15  /* block-scaled FP4 tensor-core path */
 #define FFN_B200_K_FP4_DOWN 16
 #define FFN_B200_K_COUNT 17

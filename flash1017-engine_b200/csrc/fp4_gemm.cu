@@ -399,15 +399,20 @@ __device__ __forceinline__ uint32_t quant_block(float (&v)[16], float bm, float 
   codes.y = e2m1x8(qv + 8);
   // remainder: the codes' values (exact, from the code words' nibbles) times
   // s 2^e.  (The hardware E2M1 -> f16x2 decode of these freshly converted code
-  // words left the remainder unchanged in a test build; the arithmetic decode
-  // below is what the bit-exact tests pin.)
+  // words left the remainder unchanged in a test build; the bit decode below
+  // is what the bit-exact tests pin.)
+  // A code c = (sign, m) placed as f32 bits (sign << 31) | (m << 22) is
+  // exactly its E2M1 value times 2^-126 (m = 1 lands on the subnormal 2^-127),
+  // so the decode is shifts and masks and one exact multiply by 2^126.
   const float ss = sv * sc;
 #pragma unroll
   for (int u = 0; u < 16; ++u) {
-    const uint32_t c = ((u < 8 ? codes.x : codes.y) >> (4 * (u & 7))) & 15u;
-    const uint32_t m = c & 7u;  // magnitudes 0, .5, 1, 1.5, 2, 3, 4, 6; bit 3 = sign
-    const float a = m < 4u ? 0.5f * (float)m : (m == 7u ? 6.0f : (float)(m - 2u));
-    v[u] -= ((c & 8u) ? -a : a) * ss;
+    const uint32_t w = u < 8 ? codes.x : codes.y;
+    const int k = 4 * (u & 7);  // the nibble's first bit
+    const uint32_t mag = (k <= 22 ? w << (22 - k) : w >> (k - 22)) & 0x01C00000u;
+    const uint32_t sgn = (w << (28 - k)) & 0x80000000u;
+    const float a = __uint_as_float(mag | sgn) * 0x1p126f;
+    v[u] -= a * ss;
   }
   return code;
 }

@@ -433,7 +433,7 @@ static int decode_format(const ffn_b200_expert &e, size_t inter, size_t hidden, 
   if (F < 0 || seq < 1 || seq > (size_t)kMaxTok) return -1;
   // ternary: the sign-and-mask decode costs about twice the E2M1 one per
   // value and is repeated per token pass; from 2 tokens on the GEMV engine's
-  // tensor-core decode is as fast (config-1 shapes: 52 us at 2 tokens here)
+  // tensor-core decode is as fast
   if (F == kTern && seq > 1) return -1;
   if (inter % 512 || hidden % 512 || inter > 8192 || hidden > 8192) return -1;
   if (16 % (inter / 512) || 16 % (hidden / 512)) return -1;  // column chunks split the 16 warps evenly

@@ -115,8 +115,9 @@ def metric_of(a):
 def base_config(a, world, resident):
     if a.workload == "config3":
         return {
-            "workload": "config3: one NVFP4 MoE layer, prefill of 8192 tokens, top-6 of 384, "
-                        "tensor-core grouped GEMM",
+            "workload": "config3: one NVFP4 MoE layer, prefill of 8192 tokens, top-6 of 384, " + (
+                "block-scaled FP4 decode engine (six activation terms)" if getattr(a, "path", "auto") == "fp4"
+                else "tensor-core grouped GEMM"),
             "hidden": a.hidden, "inter": a.inter, "experts": a.experts, "top_k": a.top_k,
             "tokens": a.tokens, "seed": a.seed,
             "router": "fp32 weights, tensor-core split-f16, sigmoid top-k; bf16-valued inputs",
@@ -683,18 +684,34 @@ def run_prefill(a):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     H, I, E, K, T = a.hidden, a.inter, a.experts, a.top_k, a.tokens
     e_lo, e_hi = expert_range(rank, world, E)
+    fp4 = a.path == "fp4"  # the block-scaled FP4 decode engine instead of the grouped GEMM
     experts = [None] * E
     for e in range(e_lo, e_hi):
         experts[e] = F.SwigluExpert.generate(F.FMT_NVFP4, a.seed, 0, e, I, H)
+        if fp4:
+            experts[e].pack_fp4()
     wr = F.gen_normal(F.path_key(a.seed, 0, 0, F.TAG_ROUTER), E * H, 0.02).view(E, H)
     layer = F.MoeLayer(experts, wr, H, I, top_k=K, score_fn=F.SCORE_SIGMOID,
-                       router_mode=F.ROUTER_TENSOR, expert_range=(e_lo, e_hi))
+                       router_mode=F.ROUTER_TENSOR, expert_range=(e_lo, e_hi), path=_path_code(a))
     x0 = F.gen_normal(F.path_key(a.seed, 0, 0, F.TAG_X), T * H).view(T, H)
     x0 = x0.to(torch.bfloat16).to(torch.float32)  # config 3: bf16 hidden states
     out = torch.empty_like(x0)
     idx = torch.empty(T, K, dtype=torch.int32, device=dev)
     layer.forward(x0, out=out, topk_idx=idx)
     torch.cuda.synchronize()
+    checks = None
+    if fp4 and world == 1:
+        # untimed: the FP4 path's layer output against the grouped GEMM's (whose
+        # config-3 outputs the GPU tests pin to the oracle), all tokens
+        ref_layer = F.MoeLayer(experts, wr, H, I, top_k=K, score_fn=F.SCORE_SIGMOID,
+                               router_mode=F.ROUTER_TENSOR, expert_range=(e_lo, e_hi), path=F.PATH_GROUPED)
+        ref = torch.empty_like(x0)
+        ref_layer.forward(x0, out=ref, topk_idx=idx)
+        torch.cuda.synchronize()
+        err = float((out - ref).abs().max() / ref.abs().max())
+        cos = float(torch.nn.functional.cosine_similarity(out.double().flatten(), ref.double().flatten(), dim=0))
+        checks = {"fp4_vs_grouped": {"tokens": T, "max_rel_err": err, "cosine": cos}}
+        del ref_layer, ref
     ids, cnt = torch.unique(idx, return_counts=True)
     local_pairs = int(cnt[(ids >= e_lo) & (ids < e_hi)].sum().item())
 
@@ -762,22 +779,30 @@ def run_prefill(a):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e = T * a.steps / (float(te.item()) * 1e-3)
 
-    # roofline: gate/up grouped GEMM, algorithmic FLOPs of this rank's pairs
-    gu_ms, gu_n = prof.get("gemm_gateup", (0.0, 0))
+    # roofline: gate/up GEMM, algorithmic FLOPs of this rank's pairs
+    gu_ms, gu_n = prof.get("fp4_gateup" if fp4 else "gemm_gateup", (0.0, 0))
     gu_flop = 2.0 * local_pairs * 2 * H * I
     peak, src = _tensor_peak()
+    if fp4:
+        peak, src = 9000.0, "nominal dense FP4 (9 PFLOP/s; no measured FP4 peak on this pool)"
     achieved = gu_flop * gu_n / (gu_ms * 1e-3) / 1e12 if gu_ms else None
-    dn_ms, dn_n = prof.get("gemm_down", (0.0, 0))
+    dn_ms, dn_n = prof.get("fp4_down" if fp4 else "gemm_down", (0.0, 0))
     dn_tf = 2.0 * local_pairs * H * I * dn_n / (dn_ms * 1e-3) / 1e12 if dn_ms else None
-    roof = {"bound": "tensor", "kernel": "grouped gemm_kernel<1> (gate+up, tcgen05 kind::f16)",
+    roof = {"bound": "tensor",
+            "kernel": ("fp4_gemm_kernel<1> (gate+up, tcgen05 kind::mxf4nvf4, six activation terms, "
+                       "chunks of <= 8 tokens)" if fp4 else "grouped gemm_kernel<1> (gate+up, tcgen05 kind::f16)"),
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
             "frac": achieved / peak if achieved else None, "traffic": None, "peak_source": src,
             "algorithmic_flop_per_launch": gu_flop, "launches": gu_n,
             "avg_launch_us": gu_ms * 1e3 / gu_n if gu_n else None,
             "down_tflops": dn_tf,
             "fp4_dense_nominal_tflops": 9000.0,
-            "note": "f16 operands (weights dequantised exactly in smem); FP4 block-scaled MMA "
-                    "would need FP4 activations, outside the 1e-3 tolerance"}
+            "note": ("FP4 x FP4 MMAs with the activations as six NVFP4 residual terms: the tensor "
+                     "cores do six times the algorithmic FLOPs, and every <= 8-token chunk of an "
+                     "expert streams the expert's weights again" if fp4 else
+                     "f16 operands (weights dequantised exactly in TMEM); FP4 block-scaled MMA "
+                     "needs FP4 activations: one term is outside the 1e-3 tolerance, six terms "
+                     "cost six times the tensor work (--path fp4 measures that engine here)")}
     kernels = {k: {"ms": round(v[0], 3), "launches": v[1]} for k, v in prof.items()}
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
@@ -793,7 +818,8 @@ def run_prefill(a):
             "metric": METRIC3, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None,
-            "dtype": "nvfp4 weights dequantised to f16 x f16 activations, f32 accumulate",
+            "dtype": ("nvfp4 weights x 6-term nvfp4 activations (tcgen05 block-scaled FP4 MMA), f32 accumulate"
+                      if fp4 else "nvfp4 weights dequantised to f16 x f16 activations, f32 accumulate"),
             "data": "synthetic (seeded random-init weights, bf16-valued N(0,1) hidden states)",
             "config": cfg,
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": T * H * 4,
@@ -802,6 +828,8 @@ def run_prefill(a):
             "kernels": kernels,
             "tflops_layer": 2.0 * T * K * 3 * H * I / (ms_step * 1e-3) / 1e12,
         }
+        if checks:
+            line["checks"] = checks
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -80,24 +80,34 @@ __host__ __device__ constexpr int scale_bytes(int F, int K, bool bs) {
 
 // Shared memory: batch barriers, then per matrix the rows' codes and scales,
 // then the reduction slots red[(row * NMAT + m) * T + t][chunk].
+// On the tensor-core path (compute_rows_mma) the code rows sit 16 bytes apart
+// beyond their length, so the 8 rows of an MMA fragment fall in different
+// banks, and each of the 16 warps leaves one partial per row and token.  The
+// CUDA-core path keeps dense rows and one partial per 512-column chunk.
 struct Layout {
-  int nr, cb, sb;  // rows of this CTA, code and scale bytes per row
+  int nr, cb, cs, sb, nch;  // rows of this CTA; code bytes per row, code row stride; scale bytes; partials
   size_t codes[2], scales[2], red, total;
 };
+// NVFP4 takes the tensor cores from kMmaTok tokens on: they cost a fixed
+// amount per 8 tokens, while the CUDA-core sums grow with every token.
+constexpr int kMmaTok = 4;
+__host__ __device__ constexpr bool use_mma(int F, int T) { return F == kNv && T >= kMmaTok; }
 __host__ __device__ inline Layout layout(int F, bool bs, int nmat, int nr, int K, int T, size_t base = 128) {
   Layout l;
   l.nr = nr;
   l.cb = code_bytes(F, K);
+  l.cs = use_mma(F, T) ? l.cb + 16 : l.cb;
   l.sb = scale_bytes(F, K, bs);
+  l.nch = use_mma(F, T) ? kWarps : K / 512;
   size_t o = base;  // after the barriers
   for (int m = 0; m < nmat; ++m) {
     l.codes[m] = o;
-    o += (size_t)nr * l.cb;
+    o += (size_t)nr * l.cs;
     l.scales[m] = o;
     o += (size_t)nr * l.sb;
   }
   l.red = (o + 15) & ~(size_t)15;
-  l.total = l.red + (size_t)nr * nmat * T * (K / 512) * sizeof(float);
+  l.total = l.red + (size_t)nr * nmat * T * l.nch * sizeof(float);
   return l;
 }
 
@@ -150,7 +160,12 @@ __device__ __forceinline__ void issue_rows(const Phase &p, uint8_t *smem, const 
     tc::bar_arrive_tx(&bar[b], (uint32_t)(NMAT * n * (cb + L.sb)));
 #pragma unroll
     for (int m = 0; m < NMAT; ++m) {
-      tc::bulk_g2s(smem + L.codes[m] + i0 * cb, p.w[m] + (size_t)(r0 + i0) * cb, (uint32_t)(n * cb), &bar[b]);
+      if (L.cs == L.cb) {
+        tc::bulk_g2s(smem + L.codes[m] + i0 * cb, p.w[m] + (size_t)(r0 + i0) * cb, (uint32_t)(n * cb), &bar[b]);
+      } else {
+        for (int i = i0; i < i0 + n; ++i)  // one copy per row into its padded slot
+          tc::bulk_g2s(smem + L.codes[m] + (size_t)i * L.cs, p.w[m] + (size_t)(r0 + i) * cb, (uint32_t)cb, &bar[b]);
+      }
       if (L.sb)
         tc::bulk_g2s(smem + L.scales[m] + (size_t)i0 * L.sb, p.s[m] + (size_t)(r0 + i0) * L.sb,
                      (uint32_t)(n * L.sb), &bar[b]);
@@ -197,6 +212,145 @@ __device__ __forceinline__ void row_group(const uint8_t *cptr, float sc, const f
   for (int t = 0; t < TQ; ++t) acc[t] *= sc;
 }
 
+// NVFP4 on the tensor cores (mma.sync m16n8k16, f16 in, f32 accumulate): the
+// A operand is 16 weight rows, E2M1 codes times their E4M3 block scale in f16
+// (exact: at most 6 significant bits, 2^-10 .. 2688); the B operand is the
+// tokens (up to 8, one per MMA column) as two f16 terms hi + lo of x 2^-e,
+// e per token and warp from the maximum over the warp's columns, so the MMAs
+// reproduce f32 products to ~2^-22.  Warp w takes the 128-column blocks
+// w, w + 16, ...; in a block, lane (g, q) = (lane / 4, lane % 4) holds the
+// 32 columns 32q .. 32q + 31 of rows g and g + 8 and feeds them to the eight
+// k16 tiles as columns 32q + 4j .. 4j + 3 of tile j (the k order inside a
+// tile is free as long as A and B agree).  Each warp leaves one partial per
+// row and token, times its 2^e, for finish_rows to add in warp order.
+template <int NMAT>
+__device__ __forceinline__ bool compute_rows_mma(const Phase &p, const uint8_t *smem, const Layout &L,
+                                                 uint64_t *bar, int nr, int T, const float *x, int ld_x,
+                                                 int *s_err) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, q = lane & 3;
+  const int nblk = p.K / 128, ntile = (nr + 15) / 16, nitem = NMAT * ntile;
+  float *red = reinterpret_cast<float *>(const_cast<uint8_t *>(smem) + L.red);
+  bool ok = true;
+  const int nb = (nr + kBatchRows - 1) / kBatchRows;
+  for (int b = 0; b < nb; ++b) ok = tc::bar_wait(&bar[b], 0u, s_err) && ok;
+  // the token's scale exponent over this warp's columns (lanes of token g)
+  const bool have = g < T;
+  const float *xrow = x + (size_t)(have ? g : 0) * ld_x + 32 * q;
+  float xm = 0.f;
+  if (have)
+    for (int blk = warp; blk < nblk; blk += kWarps) {
+      const float4 *src = reinterpret_cast<const float4 *>(xrow + 128 * blk);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float4 f = __ldcg(src + u);
+        xm = fmaxf(xm, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
+      }
+    }
+  xm = fmaxf(xm, __shfl_xor_sync(0xffffffffu, xm, 1));
+  xm = fmaxf(xm, __shfl_xor_sync(0xffffffffu, xm, 2));
+  int e = 0;
+  if (xm > 0.f && isfinite(xm)) {
+    int ex;
+    frexpf(xm, &ex);  // xm < 2^ex: |x 2^-e| < 2^15 with e = ex - 15
+    e = max(-100, min(100, ex - 15));
+  }
+  const float xs = pow2f(-e);
+  // the exponents of this lane's two accumulator columns (tokens 2q, 2q + 1)
+  const float c0s = pow2f(__shfl_sync(0xffffffffu, e, 8 * q)), c1s = pow2f(__shfl_sync(0xffffffffu, e, 8 * q + 4));
+  for (int it0 = 0; it0 < nitem; it0 += 2) {
+    float acc[2][4];
+#pragma unroll
+    for (int ii = 0; ii < 2; ++ii)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[ii][k] = 0.f;
+    for (int blk = warp; blk < nblk; blk += kWarps) {
+      // block scales of rows g and g + 8 (groups 8 blk + 2q and + 1) per item, as f16 pairs
+      uint32_t sc[2][2][2];  // [item][row g | g + 8][group 2q | 2q + 1]: scale in both halves
+#pragma unroll
+      for (int ii = 0; ii < 2; ++ii) {
+        const int it = it0 + ii, m = it % NMAT, tile = it / NMAT;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int row = tile * 16 + g + 8 * h;
+          uint16_t two = 0;
+          if (it < nitem && row < nr)
+            two = *reinterpret_cast<const uint16_t *>(smem + (m ? L.scales[NMAT - 1] : L.scales[0]) +
+                                                      (size_t)row * L.sb + 8 * blk + 2 * q);
+          const uint32_t pr = e4m3x2_to_f16x2(two);
+          sc[ii][h][0] = (pr & 0xFFFFu) * 0x10001u;
+          sc[ii][h][1] = (pr >> 16) * 0x10001u;
+        }
+      }
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        // B: x of token g, columns 32q + 8w .. + 7 (tiles 2w and 2w + 1), hi and lo
+        uint32_t bh[4], bl[4];
+        {
+          float v[8];
+          if (have) {
+            const float4 *src = reinterpret_cast<const float4 *>(xrow + 128 * blk + 8 * w);
+            const float4 f0 = __ldcg(src), f1 = __ldcg(src + 1);
+            v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w; v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+          } else {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = 0.f;
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            __half h0, l0, h1, l1;
+            split_f16(v[2 * u] * xs, h0, l0);
+            split_f16(v[2 * u + 1] * xs, h1, l1);
+            bh[u] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+            bl[u] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+          }
+        }
+#pragma unroll
+        for (int ii = 0; ii < 2; ++ii) {
+          const int it = it0 + ii;
+          if (it >= nitem) break;  // warp-uniform
+          const int m = it % NMAT, tile = it / NMAT;
+          const uint8_t *cbase = smem + (m ? L.codes[NMAT - 1] : L.codes[0]) + 64 * blk + 16 * q + 4 * w;
+          const int ra = tile * 16 + g, rb = ra + 8;
+          const uint32_t wa = ra < nr ? *reinterpret_cast<const uint32_t *>(cbase + (size_t)ra * L.cs) : 0u;
+          const uint32_t wb = rb < nr ? *reinterpret_cast<const uint32_t *>(cbase + (size_t)rb * L.cs) : 0u;
+          uint32_t qa[4], qb[4];
+          e2m1x8_to_f16x2(wa, qa);
+          e2m1x8_to_f16x2(wb, qb);
+          const int grp = w >> 1;  // columns 32q + 8w .. + 7: group 2q for w < 2, else 2q + 1
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            __half2 ha = __hmul2(*reinterpret_cast<const __half2 *>(&qa[k]),
+                                 *reinterpret_cast<const __half2 *>(&sc[ii][0][grp]));
+            __half2 hb = __hmul2(*reinterpret_cast<const __half2 *>(&qb[k]),
+                                 *reinterpret_cast<const __half2 *>(&sc[ii][1][grp]));
+            qa[k] = *reinterpret_cast<uint32_t *>(&ha);
+            qb[k] = *reinterpret_cast<uint32_t *>(&hb);
+          }
+          // tile 2w: bytes 0 (k slots 2q, 2q+1) and 1 (2q+8, 2q+9); tile 2w + 1: bytes 2 and 3
+          mma_f16(acc[ii], qa[0], qb[0], qa[1], qb[1], bh[0], bh[1]);
+          mma_f16(acc[ii], qa[0], qb[0], qa[1], qb[1], bl[0], bl[1]);
+          mma_f16(acc[ii], qa[2], qb[2], qa[3], qb[3], bh[2], bh[3]);
+          mma_f16(acc[ii], qa[2], qb[2], qa[3], qb[3], bl[2], bl[3]);
+        }
+      }
+    }
+#pragma unroll
+    for (int ii = 0; ii < 2; ++ii) {
+      const int it = it0 + ii;
+      if (it >= nitem) break;
+      const int m = it % NMAT, tile = it / NMAT;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int row = tile * 16 + g + 8 * (k >> 1), t = 2 * q + (k & 1);
+        if (row < nr && t < T)
+          red[((size_t)(row * NMAT + m) * T + t) * kWarps + warp] = acc[ii][k] * ((k & 1) ? c1s : c0s);
+      }
+    }
+  }
+  return ok;
+}
+
 // All warps: the partial sums of this CTA's rows of one phase into the
 // reduction slots.  A warp task = one column chunk (512 columns: a 16-column
 // group per lane) of RB = 8 / TQ rows of one matrix, for TQ tokens whose
@@ -206,6 +360,7 @@ __device__ __forceinline__ void row_group(const uint8_t *cptr, float sc, const f
 template <int NMAT, int F, int TQ>
 __device__ __forceinline__ bool compute_rows(const Phase &p, const uint8_t *smem, const Layout &L, uint64_t *bar,
                                              int nr, int T, const float *x, int ld_x, int *s_err) {
+  if (use_mma(F, T)) return compute_rows_mma<NMAT>(p, smem, L, bar, nr, T, x, ld_x, s_err);
   constexpr int RB = 8 / TQ;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int C = p.K / 512;  // column chunks of 32 groups of 16
@@ -307,7 +462,7 @@ template <int NMAT, int F>
 __device__ __forceinline__ void finish_rows(const Phase &p, const uint8_t *smem, const Layout &L, int r0, int nr,
                                             int T, bool bad, const float *s_z, float *s_h, float *h, int ld_h,
                                             float *y, int ld_y, float out_w, int accumulate) {
-  const int C = p.K / 512;
+  const int C = L.nch;
   const float *red = reinterpret_cast<const float *>(smem + L.red);
   for (int idx = threadIdx.x; idx < nr * T; idx += kThreads) {
     const int i = idx / T, t = idx - i * T;

@@ -1,5 +1,6 @@
 """The expert decode kernels (csrc/expert_decode.cu): one NVFP4, MXFP4 or
-ternary SwiGLU expert over 1..8 tokens, as ffn_b200_expert_forward runs it
+ternary SwiGLU expert over 1..8 tokens (NVFP4 from 4 tokens on the tensor
+cores), as ffn_b200_expert_forward runs it
 for those formats and batch sizes, against the oracle's expert
 (flash1017.rs:7537-7561 over CachedNvfp4Mat / CachedMxfp4Mat /
 CachedTernary158Mat rows with their rank-16 cores, flash1017.rs:2331-2357,
@@ -70,10 +71,12 @@ def test_decode_accumulate(oracle, ffn, cuda, seq):
     assert torch.equal(again, out)
 
 
+@pytest.mark.parametrize("seq", [2, 4])
 @pytest.mark.parametrize("inter,hidden", [(512, 1024), (1024, 512), (1024, 8192), (4096, 2048)])
-def test_decode_shapes(oracle, ffn, cuda, inter, hidden):
-    """Rows per CTA from 3 up to 56, one to sixteen column chunks."""
-    seq = 2
+def test_decode_shapes(oracle, ffn, cuda, inter, hidden, seq):
+    """Rows per CTA from 3 up to 56, one to sixteen column chunks; 2 tokens on
+    the CUDA cores, 4 on the tensor cores (4 to 64 column blocks over 16
+    warps)."""
     e, oe = _nvfp4(ffn, oracle, 11, inter, hidden)
     x = ffn.gen_normal(ffn.path_key(11, inter, hidden, ffn.TAG_X), seq * hidden).view(seq, hidden)
     y, launches = _run(ffn, e, x)

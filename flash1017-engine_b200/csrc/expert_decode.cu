@@ -85,12 +85,13 @@ __host__ __device__ constexpr int scale_bytes(int F, int K, bool bs) {
 // banks, and each of the 16 warps leaves one partial per row and token.  The
 // CUDA-core path keeps dense rows and one partial per 512-column chunk.
 struct Layout {
-  int nr, cb, cs, sb, nch;  // rows of this CTA; code bytes per row, code row stride; scale bytes; partials
+  int nr, cb, cs, sb, ss, nch;  // rows of this CTA; code bytes per row and row stride; the same for
+                                // the scales; partials per row and token
   size_t codes[2], scales[2], red, total;
 };
 // NVFP4 takes the tensor cores from kMmaTok tokens on: they cost a fixed
 // amount per 8 tokens, while the CUDA-core sums grow with every token.
-constexpr int kMmaTok = 4;
+constexpr int kMmaTok = 3;
 __host__ __device__ constexpr bool use_mma(int F, int T) { return F == kNv && T >= kMmaTok; }
 __host__ __device__ inline Layout layout(int F, bool bs, int nmat, int nr, int K, int T, size_t base = 128) {
   Layout l;
@@ -98,13 +99,14 @@ __host__ __device__ inline Layout layout(int F, bool bs, int nmat, int nr, int K
   l.cb = code_bytes(F, K);
   l.cs = use_mma(F, T) ? l.cb + 16 : l.cb;
   l.sb = scale_bytes(F, K, bs);
+  l.ss = use_mma(F, T) ? l.sb + 16 : l.sb;
   l.nch = use_mma(F, T) ? kWarps : K / 512;
   size_t o = base;  // after the barriers
   for (int m = 0; m < nmat; ++m) {
     l.codes[m] = o;
     o += (size_t)nr * l.cs;
     l.scales[m] = o;
-    o += (size_t)nr * l.sb;
+    o += (size_t)nr * l.ss;
   }
   l.red = (o + 15) & ~(size_t)15;
   l.total = l.red + (size_t)nr * nmat * T * l.nch * sizeof(float);
@@ -166,9 +168,14 @@ __device__ __forceinline__ void issue_rows(const Phase &p, uint8_t *smem, const 
         for (int i = i0; i < i0 + n; ++i)  // one copy per row into its padded slot
           tc::bulk_g2s(smem + L.codes[m] + (size_t)i * L.cs, p.w[m] + (size_t)(r0 + i) * cb, (uint32_t)cb, &bar[b]);
       }
-      if (L.sb)
+      if (L.sb && L.ss == L.sb) {
         tc::bulk_g2s(smem + L.scales[m] + (size_t)i0 * L.sb, p.s[m] + (size_t)(r0 + i0) * L.sb,
                      (uint32_t)(n * L.sb), &bar[b]);
+      } else if (L.sb) {
+        for (int i = i0; i < i0 + n; ++i)
+          tc::bulk_g2s(smem + L.scales[m] + (size_t)i * L.ss, p.s[m] + (size_t)(r0 + i) * L.sb, (uint32_t)L.sb,
+                       &bar[b]);
+      }
     }
   }
 }
@@ -218,11 +225,13 @@ __device__ __forceinline__ void row_group(const uint8_t *cptr, float sc, const f
 // tokens (up to 8, one per MMA column) as two f16 terms hi + lo of x 2^-e,
 // e per token and warp from the maximum over the warp's columns, so the MMAs
 // reproduce f32 products to ~2^-22.  Warp w takes the 128-column blocks
-// w, w + 16, ...; in a block, lane (g, q) = (lane / 4, lane % 4) holds the
-// 32 columns 32q .. 32q + 31 of rows g and g + 8 and feeds them to the eight
-// k16 tiles as columns 32q + 4j .. 4j + 3 of tile j (the k order inside a
-// tile is free as long as A and B agree).  Each warp leaves one partial per
-// row and token, times its 2^e, for finish_rows to add in warp order.
+// w, w + 16, ...; in a block, lane (g, q) = (lane / 4, lane % 4) reads the
+// 32-bit code word 4v + q (v = 0..3: columns 32v + 8q .. + 7) of rows g and
+// g + 8 and feeds them to k16 tiles 2v and 2v + 1 as their columns
+// 32v + 8q .. + 3 and + 4 .. + 7 (the k order inside a tile is free as long as
+// A and B agree).  Code rows 16 bytes apart beyond their length put the 32
+// lanes' words in 32 banks; scale rows likewise.  Each warp leaves one partial
+// per row and token, times its 2^e, for finish_rows to add in warp order.
 template <int NMAT>
 __device__ __forceinline__ bool compute_rows_mma(const Phase &p, const uint8_t *smem, const Layout &L,
                                                  uint64_t *bar, int nr, int T, const float *x, int ld_x,
@@ -236,15 +245,18 @@ __device__ __forceinline__ bool compute_rows_mma(const Phase &p, const uint8_t *
   for (int b = 0; b < nb; ++b) ok = tc::bar_wait(&bar[b], 0u, s_err) && ok;
   // the token's scale exponent over this warp's columns (lanes of token g)
   const bool have = g < T;
-  const float *xrow = x + (size_t)(have ? g : 0) * ld_x + 32 * q;
+  const float *xrow = x + (size_t)(have ? g : 0) * ld_x + 8 * q;
   float xm = 0.f;
   if (have)
     for (int blk = warp; blk < nblk; blk += kWarps) {
-      const float4 *src = reinterpret_cast<const float4 *>(xrow + 128 * blk);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float4 f = __ldcg(src + u);
-        xm = fmaxf(xm, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
+      for (int v = 0; v < 4; ++v) {
+        const float4 *src = reinterpret_cast<const float4 *>(xrow + 128 * blk + 32 * v);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const float4 f = __ldcg(src + u);
+          xm = fmaxf(xm, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
+        }
       }
     }
   xm = fmaxf(xm, __shfl_xor_sync(0xffffffffu, xm, 1));
@@ -265,42 +277,26 @@ __device__ __forceinline__ bool compute_rows_mma(const Phase &p, const uint8_t *
 #pragma unroll
       for (int k = 0; k < 4; ++k) acc[ii][k] = 0.f;
     for (int blk = warp; blk < nblk; blk += kWarps) {
-      // block scales of rows g and g + 8 (groups 8 blk + 2q and + 1) per item, as f16 pairs
-      uint32_t sc[2][2][2];  // [item][row g | g + 8][group 2q | 2q + 1]: scale in both halves
 #pragma unroll
-      for (int ii = 0; ii < 2; ++ii) {
-        const int it = it0 + ii, m = it % NMAT, tile = it / NMAT;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int row = tile * 16 + g + 8 * h;
-          uint16_t two = 0;
-          if (it < nitem && row < nr)
-            two = *reinterpret_cast<const uint16_t *>(smem + (m ? L.scales[NMAT - 1] : L.scales[0]) +
-                                                      (size_t)row * L.sb + 8 * blk + 2 * q);
-          const uint32_t pr = e4m3x2_to_f16x2(two);
-          sc[ii][h][0] = (pr & 0xFFFFu) * 0x10001u;
-          sc[ii][h][1] = (pr >> 16) * 0x10001u;
-        }
-      }
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        // B: x of token g, columns 32q + 8w .. + 7 (tiles 2w and 2w + 1), hi and lo
+      for (int v = 0; v < 4; ++v) {
+        // B: x of token g, columns 32v + 8q .. + 7 (tiles 2v and 2v + 1), hi and lo
         uint32_t bh[4], bl[4];
         {
-          float v[8];
+          float xv[8];
           if (have) {
-            const float4 *src = reinterpret_cast<const float4 *>(xrow + 128 * blk + 8 * w);
+            const float4 *src = reinterpret_cast<const float4 *>(xrow + 128 * blk + 32 * v);
             const float4 f0 = __ldcg(src), f1 = __ldcg(src + 1);
-            v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w; v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+            xv[0] = f0.x; xv[1] = f0.y; xv[2] = f0.z; xv[3] = f0.w;
+            xv[4] = f1.x; xv[5] = f1.y; xv[6] = f1.z; xv[7] = f1.w;
           } else {
 #pragma unroll
-            for (int u = 0; u < 8; ++u) v[u] = 0.f;
+            for (int u = 0; u < 8; ++u) xv[u] = 0.f;
           }
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             __half h0, l0, h1, l1;
-            split_f16(v[2 * u] * xs, h0, l0);
-            split_f16(v[2 * u + 1] * xs, h1, l1);
+            split_f16(xv[2 * u] * xs, h0, l0);
+            split_f16(xv[2 * u + 1] * xs, h1, l1);
             bh[u] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
             bl[u] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
           }
@@ -310,24 +306,26 @@ __device__ __forceinline__ bool compute_rows_mma(const Phase &p, const uint8_t *
           const int it = it0 + ii;
           if (it >= nitem) break;  // warp-uniform
           const int m = it % NMAT, tile = it / NMAT;
-          const uint8_t *cbase = smem + (m ? L.codes[NMAT - 1] : L.codes[0]) + 64 * blk + 16 * q + 4 * w;
+          const uint8_t *cbase = smem + (m ? L.codes[NMAT - 1] : L.codes[0]) + 64 * blk + 4 * (4 * v + q);
+          const uint8_t *sbase = smem + (m ? L.scales[NMAT - 1] : L.scales[0]) + 8 * blk + 2 * v + (q >> 1);
           const int ra = tile * 16 + g, rb = ra + 8;
           const uint32_t wa = ra < nr ? *reinterpret_cast<const uint32_t *>(cbase + (size_t)ra * L.cs) : 0u;
           const uint32_t wb = rb < nr ? *reinterpret_cast<const uint32_t *>(cbase + (size_t)rb * L.cs) : 0u;
+          // the word's 16-column group scale of each row, in both f16 halves
+          const uint32_t pa = e4m3x2_to_f16x2(ra < nr ? sbase[(size_t)ra * L.ss] : 0);
+          const uint32_t pb = e4m3x2_to_f16x2(rb < nr ? sbase[(size_t)rb * L.ss] : 0);
+          const uint32_t sa = (pa & 0xFFFFu) * 0x10001u, sb = (pb & 0xFFFFu) * 0x10001u;
           uint32_t qa[4], qb[4];
           e2m1x8_to_f16x2(wa, qa);
           e2m1x8_to_f16x2(wb, qb);
-          const int grp = w >> 1;  // columns 32q + 8w .. + 7: group 2q for w < 2, else 2q + 1
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            __half2 ha = __hmul2(*reinterpret_cast<const __half2 *>(&qa[k]),
-                                 *reinterpret_cast<const __half2 *>(&sc[ii][0][grp]));
-            __half2 hb = __hmul2(*reinterpret_cast<const __half2 *>(&qb[k]),
-                                 *reinterpret_cast<const __half2 *>(&sc[ii][1][grp]));
+            __half2 ha = __hmul2(*reinterpret_cast<const __half2 *>(&qa[k]), *reinterpret_cast<const __half2 *>(&sa));
+            __half2 hb = __hmul2(*reinterpret_cast<const __half2 *>(&qb[k]), *reinterpret_cast<const __half2 *>(&sb));
             qa[k] = *reinterpret_cast<uint32_t *>(&ha);
             qb[k] = *reinterpret_cast<uint32_t *>(&hb);
           }
-          // tile 2w: bytes 0 (k slots 2q, 2q+1) and 1 (2q+8, 2q+9); tile 2w + 1: bytes 2 and 3
+          // tile 2v: bytes 0 (k slots 2q, 2q+1) and 1 (2q+8, 2q+9); tile 2v + 1: bytes 2 and 3
           mma_f16(acc[ii], qa[0], qb[0], qa[1], qb[1], bh[0], bh[1]);
           mma_f16(acc[ii], qa[0], qb[0], qa[1], qb[1], bl[0], bl[1]);
           mma_f16(acc[ii], qa[2], qb[2], qa[3], qb[3], bh[2], bh[3]);
@@ -390,16 +388,16 @@ __device__ __forceinline__ bool compute_rows(const Phase &p, const uint8_t *smem
       const int i0 = rb * RB;
       ok = tc::bar_wait(&bar[i0 / kBatchRows], 0u, s_err) && ok;  // returns at once after the first time
       const uint8_t *cbase = smem + (m ? L.codes[NMAT - 1] : L.codes[0]) + (size_t)i0 * L.cb + cg;
-      const uint8_t *sbase = smem + (m ? L.scales[NMAT - 1] : L.scales[0]) + (size_t)i0 * L.sb + sg;
+      const uint8_t *sbase = smem + (m ? L.scales[NMAT - 1] : L.scales[0]) + (size_t)i0 * L.ss + sg;
       float v[8];
 #pragma unroll
       for (int r = 0; r < RB; ++r) {
         float acc[TQ];
         if (i0 + r < nr) {
           float sc = 1.0f;
-          if (F == kNv) sc = e4m3_f32(sbase[r * L.sb]);
-          else if (F == kMx) sc = e8m0_f32(sbase[r * L.sb]);
-          else if (L.sb) sc = (float)sbase[r * L.sb];
+          if (F == kNv) sc = e4m3_f32(sbase[r * L.ss]);
+          else if (F == kMx) sc = e8m0_f32(sbase[r * L.ss]);
+          else if (L.sb) sc = (float)sbase[r * L.ss];
           row_group<F, TQ>(cbase + r * L.cb, sc, xr, acc);
         } else {
 #pragma unroll

@@ -1,5 +1,5 @@
 """The expert decode kernels (csrc/expert_decode.cu): one NVFP4, MXFP4 or
-ternary SwiGLU expert over 1..8 tokens (NVFP4 from 4 tokens on the tensor
+ternary SwiGLU expert over 1..8 tokens (NVFP4 from 3 tokens on the tensor
 cores), as ffn_b200_expert_forward runs it
 for those formats and batch sizes, against the oracle's expert
 (flash1017.rs:7537-7561 over CachedNvfp4Mat / CachedMxfp4Mat /

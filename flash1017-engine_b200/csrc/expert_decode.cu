@@ -241,9 +241,8 @@ __device__ __forceinline__ bool compute_rows_mma(const Phase &p, const uint8_t *
   const int nblk = p.K / 128, ntile = (nr + 15) / 16, nitem = NMAT * ntile;
   float *red = reinterpret_cast<float *>(const_cast<uint8_t *>(smem) + L.red);
   bool ok = true;
-  const int nb = (nr + kBatchRows - 1) / kBatchRows;
-  for (int b = 0; b < nb; ++b) ok = tc::bar_wait(&bar[b], 0u, s_err) && ok;
-  // the token's scale exponent over this warp's columns (lanes of token g)
+  // the token's scale exponent over this warp's columns (lanes of token g),
+  // while the rows' copies are still landing
   const bool have = g < T;
   const float *xrow = x + (size_t)(have ? g : 0) * ld_x + 8 * q;
   float xm = 0.f;
@@ -270,6 +269,8 @@ __device__ __forceinline__ bool compute_rows_mma(const Phase &p, const uint8_t *
   const float xs = pow2f(-e);
   // the exponents of this lane's two accumulator columns (tokens 2q, 2q + 1)
   const float c0s = pow2f(__shfl_sync(0xffffffffu, e, 8 * q)), c1s = pow2f(__shfl_sync(0xffffffffu, e, 8 * q + 4));
+  const int nb = (nr + kBatchRows - 1) / kBatchRows;
+  for (int b = 0; b < nb; ++b) ok = tc::bar_wait(&bar[b], 0u, s_err) && ok;
   for (int it0 = 0; it0 < nitem; it0 += 2) {
     float acc[2][4];
 #pragma unroll

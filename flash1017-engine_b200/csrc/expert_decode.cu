@@ -1,5 +1,6 @@
-// Batch decode of one NVFP4 (or MXFP4) SwiGLU expert for 1..8 tokens in two
-// launches and no other device work.
+// Batch decode of one NVFP4 or MXFP4 SwiGLU expert for 1..8 tokens, or one
+// ternary expert (rank-16 cores, block scales) for 1 token, in two launches
+// (a ternary expert with gate/up cores: the cores' z kernel first).
 //
 //   phase 1  h[t][i] = min(silu(g), 10) * clamp(u, -10, 10),
 //            g = (W1 x_t)_i, u = (W3 x_t)_i          (flash1017.rs:7537-7547)
@@ -22,13 +23,15 @@
 //   activations.  The two phases fit on one SM together (<= 64 registers x 512
 //   threads each, about 100 KB of shared memory between them), so the down
 //   weights stream while gate/up computes;
-// * arithmetic is f32 on the CUDA cores: a lane owns one 16-column scale
-//   group of a row, decodes its 16 E2M1 codes exactly (cvt.rn.f16x2.e2m1x2),
-//   keeps its 16 activations per token in registers across the rows it visits,
-//   sums code x activation, times the group's scale (flash1017.rs:2331-2357
-//   sums each group, times its scale, over the row, times the matrix scale);
-//   lanes and column-chunk warps reduce through shuffles and shared memory in
-//   a fixed order, so results are deterministic.
+// * for 1-2 tokens (any format) the arithmetic is f32 on the CUDA cores: a
+//   lane owns one 16-column scale group of a row, decodes its 16 codes exactly
+//   (cvt.rn.f16x2.e2m1x2; ternary by sign flips and masks), keeps its 16
+//   activations per token in registers across the rows it visits, sums code x
+//   activation, times the group's scale (flash1017.rs:2331-2357 sums each
+//   group, times its scale, over the row, times the matrix scale); NVFP4 from
+//   3 tokens runs mma.sync on the tensor cores (compute_rows_mma), whose work
+//   does not grow with the tokens; warps reduce through shuffles and shared
+//   memory in a fixed order, so results are deterministic.
 //
 // Weights and scales are read before the wait on the previous kernel: they
 // must not be written by a kernel of the same stream that lets this one start

@@ -613,7 +613,7 @@ struct MoeWs {
   int *err;        // grouped path: timed-out wait flag
   float *part;     // GEMV path: K-split partial sums (kListSplitBytes)
   int *cnt;        // GEMV path: split arrival counters, kSplitItems per phase launch (4)
-  // FP4 path: x and h as four NVFP4 terms, h in f32, the chunk list
+  // FP4 path: x and h as six NVFP4 terms, h in f32, the chunk list
   uint8_t *xq, *xs, *hq, *hs;
   int *xqe, *hqe;
   float *hf;
@@ -1113,7 +1113,7 @@ static int moe_layer_impl(const ffn_b200_moe_desc *d, size_t n_tok, const float 
                     (d->path == FFN_B200_PATH_AUTO && (reinterpret_cast<uintptr_t>(xin) & 15) == 0));
   const bool fused_q = fp4 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(d->norm_w)) & 15) == 0;
   if (fused_q) {
-    // one pass: RMSNorm, the router's f16 split and the experts' four NVFP4
+    // one pass: RMSNorm, the router's f16 split and the experts' six NVFP4
     // terms (xn reaches global memory only for the exact router)
     if ((rc = launch_xprep_q4(x, (int)H, T, (int)H, w.xh, w.xl, (int)H, w.xe, d->norm_w, d->norm_eps,
                               exact ? 1 : 0, exact && d->norm_w ? w.xn : nullptr, w.xq, w.xs, w.xqe, st)))
